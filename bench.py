@@ -1,0 +1,433 @@
+"""Cached batched decode benchmark (env-steps/s) on B200.
+
+Workload (one step = every env appends one transition token and the model
+picks its next action): Qwen3-0.6B architecture truncated to 2 layers
+(hidden 1024, 16 q / 8 kv heads, head_dim 128, q/k RMSNorm, RoPE theta 1e6,
+intermediate 3072), random init, bf16. 256 envs per GPU whose cached context
+lengths start uniform in [64, 4096]; paged KV with 128-token pages; policy
+start_cache 1024 / max_cache 8192 (grow-then-rebuild, checked every step).
+Each token embeds one transition id ((obs*4 + action)*2 + reward)*2 + done
+(obs in [0,63], action in [0,3], reward in {0,1}, done ~ Bernoulli(0.02)):
+a single discrete modality of vocab 1024. A 4-way DiscreteActionValueHead
+(fp32 RMSNorm -> SwiGLU -> linear) takes the argmax.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Multi-GPU: one process per GPU (torchrun); each rank decodes its own 256 envs
+(weak scaling, no collective on the decode path); value = all ranks' env-steps
+/ max-over-ranks device time.
+
+`value` times K steps with inputs resident in HBM; `e2e` times the same steps
+through the public API with the token ids in pinned host memory (H2D copy
+each step) and the actions read back to the host (D2H copy + sync each step).
+`--impl reference` times the reference algorithm's CPU restatement (the
+oracle; the reference itself is pure Python and is not installed on the GPU
+box) on the host cores for the same metric.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+HIDDEN, LAYERS, HEADS, KV_HEADS, HEAD_DIM, INTER = 1024, 2, 16, 8, 128, 3072
+ROPE_THETA = 1e6
+ENVS = 256
+PAGE = 128
+START_CACHE, MAX_CACHE = 1024, 8192
+VOCAB = 1024
+LEN_LO, LEN_HI = 64, 4096
+
+
+def transition_ids(rng, actions, n):
+    obs = rng.integers(0, 64, size=n)
+    reward = rng.integers(0, 2, size=n)
+    done = (rng.random(n) < 0.02).astype(np.int64)
+    return (((obs * 4 + actions) * 2 + reward) * 2 + done).astype(np.int32)
+
+
+def workload_config(n_gpus):
+    return {"workload": "cached batched decode, Qwen3-0.6B arch truncated to 2 layers, 256 envs/GPU, "
+                        "context lengths U[64,4096], 128-token pages, start_cache 1024 / max_cache 8192",
+            "envs_per_gpu": ENVS, "global_envs": ENVS * n_gpus, "layers": LAYERS, "hidden": HIDDEN,
+            "q_heads": HEADS, "kv_heads": KV_HEADS, "head_dim": HEAD_DIM, "page_size": PAGE,
+            "context_len": [LEN_LO, LEN_HI], "parallelism": f"env-sharded x{n_gpus} (no collective)",
+            "l2": "inputs larger than L2: each step reads ~4.4 GB of KV per GPU"}
+
+
+# ---------------------------------------------------------------- GPU arm
+def build_model(seed, device):
+    import torch
+
+    from mouse_core_b200.backbone import Qwen3Backbone
+
+    torch.manual_seed(seed)
+    bb = Qwen3Backbone(hidden_dim=HIDDEN, num_layers=LAYERS, num_heads=HEADS, num_key_value_heads=KV_HEADS,
+                       head_dim=HEAD_DIM, intermediate_size=INTER,
+                       rope_parameters={"rope_type": "default", "rope_theta": ROPE_THETA})
+    return bb.to(device=device, dtype=torch.bfloat16).eval()
+
+
+class ActionHead:
+    """fp32 DiscreteActionValueHead(out=4, hidden=1024, num_layers=2): RMSNorm
+    (eps 1e-5) -> SwiGLU(1024 -> 1024) -> Linear(1024 -> 4) (reference
+    models/heads/dqn.py:11-47, swiglu.py:13-74)."""
+
+    def __init__(self, device, seed):
+        import torch
+
+        g = torch.Generator().manual_seed(seed)
+        self.norm_w = torch.ones(HIDDEN, device=device)
+        self.w1 = (torch.randn(2 * HIDDEN, HIDDEN, generator=g) / HIDDEN ** 0.5).to(device)
+        self.b1 = torch.zeros(2 * HIDDEN, device=device)
+        self.w2 = (torch.randn(4, HIDDEN, generator=g) / HIDDEN ** 0.5).to(device)
+        self.b2 = torch.zeros(4, device=device)
+
+    def __call__(self, h):
+        import torch
+        import torch.nn.functional as F
+
+        x = F.rms_norm(h.float(), (HIDDEN,), self.norm_w, 1e-5)
+        a, b = F.linear(x, self.w1, self.b1).chunk(2, dim=-1)
+        return F.linear(F.silu(a) * b, self.w2, self.b2)
+
+
+class Clocks:
+    """nvidia-smi sampling of SM clocks / throttle reasons during a region."""
+
+    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.proc = None
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(gpu_index), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+            out, _ = self.proc.communicate()
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in out.strip().splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 8:
+                continue
+            try:
+                sm.append(float(parts[0]))
+                mx.append(float(parts[1]))
+            except ValueError:
+                continue
+            for name, val in zip(names, parts[4:8]):
+                if val.lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def prefill(sess, table, ctx_ids, lengths, chunk=512):
+    """Feed every env's context through the session in ragged chunks."""
+    import torch
+
+    B = len(lengths)
+    done = np.zeros(B, dtype=np.int64)
+    while (done < lengths).any():
+        n = np.minimum(lengths - done, chunk)
+        S = int(n.max())
+        ids = np.zeros((B, S), dtype=np.int64)
+        for b in range(B):
+            if n[b]:
+                ids[b, S - n[b]:] = ctx_ids[b][done[b]:done[b] + n[b]]
+        emb = table[torch.from_numpy(ids).to(table.device)]
+        sess.forward(embeds=emb, lengths=n.tolist())
+        done += n
+
+
+def roofline_traffic_per_launch():
+    """Per-launch DRAM bytes of the split decode kernel from the committed ncu
+    summary (profiles/decode_attention_cfg2.json), or None."""
+    path = os.path.join(ROOT, "profiles", "decode_attention_cfg2.json")
+    try:
+        with open(path) as f:
+            rec = json.load(f)
+        return rec.get("dram_bytes_per_launch_scaled")
+    except (OSError, ValueError):
+        return None
+
+
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+
+    from mouse_core_b200 import _lib
+    from mouse_core_b200 import kernels as K
+    from mouse_core_b200.kv_policy import cache_needs_rebuild, resolve_cache_bounds
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    max_cache, start_cache = resolve_cache_bounds(MAX_CACHE, START_CACHE)
+    model = build_model(0, dev)
+    head = ActionHead(dev, 1)
+    g = torch.Generator().manual_seed(2)
+    table = (torch.randn(VOCAB, HIDDEN, generator=g)).to(device=dev, dtype=torch.bfloat16)
+
+    rng = np.random.default_rng(1000 + rank)
+    lengths = rng.integers(LEN_LO, LEN_HI + 1, size=ENVS).astype(np.int64)
+    ctx_ids = [transition_ids(rng, rng.integers(0, 4, size=L), L) for L in lengths]
+    sess = model.decode_session(batch_size=ENVS, capacity=max_cache, page_size=PAGE)
+    prefill(sess, table, ctx_ids, lengths)
+    torch.cuda.synchronize()
+    cached_starts = np.zeros(ENVS, dtype=np.int64)
+    ends = lengths.copy()
+    cached_ends = ends.copy()
+    ctx_start = np.zeros(ENVS, dtype=np.int64)
+
+    K_steps, W = args.steps, args.warmup
+    total = K_steps + W
+    # ---------------- device-resident loop (`value`)
+    actions = rng.integers(0, 4, size=ENVS)
+    ids_dev = torch.from_numpy(np.stack([transition_ids(rng, actions, ENVS) for _ in range(2 * total)])).to(dev)
+    ones = [1] * ENVS
+
+    def device_step(i):
+        emb = table[ids_dev[i].long()].view(ENVS, 1, HIDDEN)
+        h = sess.forward(embeds=emb, lengths=ones)
+        return head(h[:, -1]).argmax(-1)
+
+    bytes_per_layer = []
+
+    for i in range(W):
+        device_step(i)
+    torch.cuda.synchronize()
+    barrier()
+    torch.cuda.synchronize()
+    clocks = Clocks(local)
+    sess.attn_events = []
+    launches0 = K.launch_count[0]
+    kv_sum = 0
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for i in range(W, total):
+        kv_sum += int(sess._len.sum()) + ENVS  # kv_len after this step's append
+        device_step(i)
+    e1.record()
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    launches = K.launch_count[0] - launches0
+    ms = e0.elapsed_time(e1)
+    attn_ms = [a.elapsed_time(b) for a, b in sess.attn_events]
+    sess.attn_events = None
+    barrier()
+    ms_t = torch.tensor([ms], device=dev)
+    if world > 1:
+        dist.all_reduce(ms_t, op=dist.ReduceOp.MAX)
+    ms_max = float(ms_t.item())
+    ends = ends + total
+    cached_ends = ends.copy()
+
+    # ---------------- end-to-end loop through the public API (`e2e`)
+    h_ids = torch.empty(ENVS, dtype=torch.int32, pin_memory=True)
+    h_act = torch.empty(ENVS, dtype=torch.int64, pin_memory=True)
+    d_ids = torch.empty(ENVS, dtype=torch.int32, device=dev)
+    act = rng.integers(0, 4, size=ENVS)
+
+    def e2e_step():
+        nonlocal act, ends, cached_ends, sess
+        ends = ends + 1
+        if cache_needs_rebuild(has_cache=True, cached_starts=cached_starts, cached_ends=cached_ends, ends=ends,
+                               context_start=ctx_start, max_cache=max_cache, batch_complete=True):
+            raise RuntimeError("rebuild inside the timed horizon (lengths are chosen so it cannot happen)")
+        h_ids.numpy()[:] = transition_ids(rng, act, ENVS)
+        d_ids.copy_(h_ids, non_blocking=True)
+        emb = table[d_ids.long()].view(ENVS, 1, HIDDEN)
+        h = sess.forward(embeds=emb, lengths=ones)
+        h_act.copy_(head(h[:, -1]).argmax(-1), non_blocking=True)
+        torch.cuda.current_stream().synchronize()
+        act = h_act.numpy().copy()
+        cached_ends = ends.copy()
+
+    for _ in range(W):
+        e2e_step()
+    torch.cuda.synchronize()
+    barrier()
+    torch.cuda.synchronize()
+    f0 = torch.cuda.Event(enable_timing=True)
+    f1 = torch.cuda.Event(enable_timing=True)
+    f0.record()
+    for _ in range(K_steps):
+        e2e_step()
+    f1.record()
+    torch.cuda.synchronize()
+    e2e_ms = f0.elapsed_time(f1)
+    et = torch.tensor([e2e_ms], device=dev)
+    if world > 1:
+        dist.all_reduce(et, op=dist.ReduceOp.MAX)
+    e2e_max = float(et.item())
+    status = _lib.device_status()
+
+    # Algorithmic bytes of one attention launch: K+V of every cached slot of
+    # every row and kv-head (2 * Hkv * hd * 2 B per token) + q/out.
+    mean_kv = kv_sum / K_steps
+    attn_bytes = mean_kv * 2 * KV_HEADS * HEAD_DIM * 2 + 2 * ENVS * HEADS * HEAD_DIM * 2
+    attn_avg_ms = statistics.mean(attn_ms) if attn_ms else float("nan")
+    achieved = attn_bytes / (attn_avg_ms * 1e-3) / 1e9
+    peaks = {}
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            peaks = json.load(f)
+    except (OSError, ValueError):
+        pass
+    peak = float(peaks.get("hbm_gbs", 6650.0))
+    peak_src = "measured" if "hbm_gbs" in peaks else "fallback"
+
+    out = None
+    if rank == 0:
+        value = ENVS * world * K_steps / (ms_max * 1e-3)
+        out = {
+            "metric": "env-steps/s in cached batched decode",
+            "value": round(value, 1),
+            "unit": "env-steps/s",
+            "n_gpus": world,
+            "steps": K_steps,
+            "warmup": W,
+            "ms_per_step": round(ms_max / K_steps, 4),
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": "bf16",
+            "data": "synthetic (seeded transition tokens; random-init weights)",
+            "config": workload_config(world),
+            "e2e": {"value": round(ENVS * world * K_steps / (e2e_max * 1e-3), 1), "unit": "env-steps/s",
+                    "h2d_bytes_per_step": int(ENVS * 4 * world), "d2h_bytes_per_step": int(ENVS * 8 * world),
+                    "ms_per_step": round(e2e_max / K_steps, 4)},
+            "roofline": {"kernel": "split_decode_kernel (K1)", "bound": "hbm", "achieved": round(achieved, 1),
+                         "peak": peak, "peak_source": peak_src, "unit": "GB/s", "frac": round(achieved / peak, 4),
+                         "traffic": roofline_traffic_per_launch(), "algorithmic_bytes_per_launch": int(attn_bytes),
+                         "avg_launch_ms": round(attn_avg_ms, 5), "launches_timed": len(attn_ms)},
+            "gpu_launches": int(launches),
+            "clocks": clk,
+            "device_status": status,
+        }
+    if rank == 0 and not args.no_cpu_baseline:
+        out["cpu_baseline"] = cpu_baseline(args.cpu_seconds)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return out
+
+
+# ---------------------------------------------------------------- CPU arm
+def _oracle_decoder(seed):
+    """The bench model's architecture as a float64 oracle decoder (weights
+    drawn from the same seed on the CPU)."""
+    import torch
+
+    from mouse_core_b200.backbone import Qwen3Backbone
+    from oracle import decoder as odec
+
+    torch.manual_seed(seed)
+    bb = Qwen3Backbone(hidden_dim=HIDDEN, num_layers=LAYERS, num_heads=HEADS, num_key_value_heads=KV_HEADS,
+                       head_dim=HEAD_DIM, intermediate_size=INTER,
+                       rope_parameters={"rope_type": "default", "rope_theta": ROPE_THETA})
+    sd = {k: v.detach().float().numpy() for k, v in bb.model.state_dict().items() if "rotary" not in k}
+    cfg = odec.config_from_hf(bb.model.config, bb.model.rotary_emb.inv_freq.numpy())
+    return odec.DecoderOracle(sd, cfg)
+
+
+def cpu_baseline(seconds=15.0, sample_envs=16):
+    """Oracle port of the reference decode step on the host cores: one S=1
+    step of ``sample_envs`` envs whose caches hold U[64,4096] random slots,
+    repeated for about ``seconds``."""
+    import torch
+
+    from oracle import decoder as odec
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    dec = _oracle_decoder(0)
+    rng = np.random.default_rng(7)
+    lens = rng.integers(LEN_LO, LEN_HI + 1, size=sample_envs)
+    sess = odec.DecodeSessionOracle(dec, sample_envs)
+    for li in range(LAYERS):
+        sess.k[li] = [rng.standard_normal((L, KV_HEADS, HEAD_DIM)) for L in lens]
+        sess.v[li] = [rng.standard_normal((L, KV_HEADS, HEAD_DIM)) for L in lens]
+    sess.lengths = lens.astype(np.int64)
+    emb = rng.standard_normal((sample_envs, 1, HIDDEN))
+    steps, t0 = 0, time.perf_counter()
+    while True:
+        sess.forward(emb, [1] * sample_envs)
+        steps += 1
+        el = time.perf_counter() - t0
+        if el >= seconds:
+            break
+    return {"value": round(sample_envs * steps / el, 3), "unit": "env-steps/s", "cores": os.cpu_count() or 1,
+            "kind": "port",
+            "sample": f"{steps} decode steps of {sample_envs} envs (2 layers, float64 numpy oracle restating "
+                      f"FlexDecodeSession.forward), cache lengths U[64,4096], {el:.1f} s"}
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if rank != 0:
+        return None
+    per_step = max(args.cpu_seconds / max(args.steps + args.warmup, 1), 1.0)
+    base = cpu_baseline(seconds=per_step * args.steps)
+    return {"impl": "reference", "metric": "env-steps/s in cached batched decode", "value": base["value"],
+            "unit": "env-steps/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f64",
+            "data": "synthetic", "config": workload_config(world), "cpu_baseline": base,
+            "e2e": {"value": base["value"], "unit": "env-steps/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=30)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--cpu-seconds", type=float, default=15.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    out = run_reference(args) if args.impl == "reference" else run_ours(args)
+    if out is not None:
+        print(json.dumps(out), flush=True)
+
+
+if __name__ == "__main__":
+    main()

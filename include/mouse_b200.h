@@ -1,0 +1,129 @@
+/*
+ * mouse_b200.h — C ABI of the B200 (sm_100a) attention hot path of mouse-core.
+ *
+ * Plain pointers, sizes and a CUDA stream; no framework types. Every entry
+ * point returns an mb_status (0 = MB_OK) and never throws; the text of the
+ * last error on the calling thread is available from mb_last_error(). Device
+ * buffers are owned by the caller; the library allocates nothing, frees
+ * nothing and starts no host threads. All kernels are enqueued on `stream`.
+ *
+ * The reference (micahr234/mouse-core v0.4.0) is pure Python; each entry
+ * point below names the reference call site it replaces (file:line, paths
+ * relative to the reference's src/mouse_core/).
+ *
+ * Layouts (bf16 unless stated):
+ *   q / out        [batch, q_len, q_heads, head_dim]   (== the reference's
+ *                  q.transpose(1, 2) of flex_decode.py:218 before the kernel)
+ *   k_pool/v_pool  [num_pages, kv_heads, page_size, head_dim], one layer
+ *   block_table    int32 [batch, max_pages]: logical page i of row b
+ *   q_pos          int32 [batch, q_len]: query (b, s) attends slots 0..q_pos
+ *   kv_len         int32 [batch]: slots written for row b (after this call's
+ *                  append)
+ */
+#ifndef MOUSE_B200_H
+#define MOUSE_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st* mb_stream_t; /* a cudaStream_t; NULL = default stream */
+
+enum mb_status {
+  MB_OK = 0,
+  MB_ERR_INVALID_ARG = 1, /* bad shape, pointer, alignment or size */
+  MB_ERR_UNSUPPORTED = 2, /* a shape the kernels are not built for */
+  MB_ERR_WORKSPACE = 3,   /* workspace missing or too small */
+  MB_ERR_CUDA = 4         /* a CUDA runtime/driver call failed */
+};
+
+/* Text of the last error raised on this thread ("" if none). */
+const char* mb_last_error(void);
+
+/* ABI version of this library (major * 100 + minor). */
+int mb_version(void);
+
+/* Read (and optionally clear) the device status word the kernels report
+ * bounded-wait timeouts and out-of-pool page ids through. Synchronizes the
+ * device. 0 = healthy. */
+int mb_device_status(int* status_out, int clear);
+
+/* ---------------------------------------------------------------------
+ * Cached decode attention (K1).
+ * Replaces models/backbone/flex_decode.py:226-229
+ *   self._flex(q, k_cache[li], v_cache[li], block_mask=..., scale=..., enable_gqa=True)
+ * with the mask of flex_decode.py:129-134 (kv_idx <= q_pos[b, q]) and the
+ * per-call BlockMask build of flex_decode.py:198-202. Slots of row b at or
+ * beyond kv_len[b] read as zero, as the reference's zero-filled cache does.
+ * ------------------------------------------------------------------- */
+
+/* Bytes of workspace mb_decode_attention needs when q_rows = (q_heads /
+ * kv_heads) * q_len <= 16 (split mode); 0 otherwise. max_kv_len bounds
+ * kv_len[b] over the batch. */
+size_t mb_decode_workspace_bytes(int batch, int kv_heads, int q_rows, int head_dim, int max_kv_len);
+
+/* Build the split-mode work list (row, chunk) from kv_len into `workspace`.
+ * It depends only on kv_len, so one plan serves every layer of a step. */
+int mb_decode_plan(const int32_t* kv_len, int batch, int kv_heads, int q_rows, int head_dim, int max_kv_len,
+                   void* workspace, size_t workspace_bytes, mb_stream_t stream);
+
+/* out = softmax(scale * q k^T, masked to slots <= q_pos) v, per row and
+ * q-head (q-head h reads kv-head h / (q_heads / kv_heads)). head_dim 64 or
+ * 128; page_size a multiple of 64. plan_ready = 1 reuses the plan already
+ * in `workspace` (built by mb_decode_plan for the same kv_len); 0 builds it. */
+int mb_decode_attention(const void* q, const void* k_pool, const void* v_pool, int num_pages,
+                        const int32_t* block_table, int max_pages, const int32_t* q_pos, const int32_t* kv_len,
+                        int batch, int q_len, int q_heads, int kv_heads, int head_dim, int page_size, float scale,
+                        int max_kv_len, int plan_ready, void* out, void* workspace, size_t workspace_bytes,
+                        mb_stream_t stream);
+
+/* ---------------------------------------------------------------------
+ * Fused q/k RMSNorm + RoPE + paged K/V append (K2).
+ * Replaces models/backbone/flex_decode.py:212-224 (q/k projections' norm,
+ * apply_rotary_pos_emb with cos/sin from rotary_emb at :204, and the cache
+ * scatter k_cache[li][real_rows, :, cache_slots] = ...), and the same norm +
+ * RoPE of models/backbone/flex_train.py:137-146.
+ *   qkv      [tokens, qkv_stride] = q (q_heads*hd) | k (kv_heads*hd) | v
+ *   pos      int32 [tokens] RoPE position; slot int32 [tokens] =
+ *            page * page_size + offset, or -1 for tokens not cached
+ *   q_norm_w / k_norm_w  [head_dim] or NULL (Llama); inv_freq f32 [hd/2]
+ *   q_out    [tokens, q_heads, hd]; k_out / v_out [tokens, kv_heads, hd]
+ *            or NULL; k_pool / v_pool one layer's pool or NULL
+ * ------------------------------------------------------------------- */
+int mb_kv_append(const void* qkv, int tokens, int qkv_stride, const int32_t* pos, const int32_t* slot,
+                 const void* q_norm_w, const void* k_norm_w, float eps, const float* inv_freq,
+                 float attention_scaling, int q_heads, int kv_heads, int head_dim, int page_size,
+                 long long num_pages, void* q_out, void* k_out, void* v_out, void* k_pool, void* v_pool,
+                 mb_stream_t stream);
+
+/* ---------------------------------------------------------------------
+ * Page copy (K3): dst_pool[dst_pages[i]] = src_pool[src_pages[i]] for one
+ * layer's pool, page_elems = kv_heads * page_size * head_dim elements.
+ * Replaces the whole-cache copy of FlexDecodeSession._grow
+ * (models/backbone/flex_decode.py:140-149) for the cases paging still needs
+ * a copy: copy-on-write of a shared partial page and rebuild-from-cache.
+ * ------------------------------------------------------------------- */
+int mb_page_copy(const void* src_pool, void* dst_pool, const int32_t* src_pages, const int32_t* dst_pages, int n,
+                 long long page_elems, mb_stream_t stream);
+
+/* ---------------------------------------------------------------------
+ * Decoder-layer glue.
+ * mb_rmsnorm: sum_out = x + residual (bf16), norm_out = RMSNorm(sum) * w;
+ *   with residual == NULL it normalises x (sum_out unused). Replaces the
+ *   residual adds and input/post_attention_layernorm calls of
+ *   flex_decode.py:210, 231-232.
+ * mb_silu_mul: out[r, :] = silu(gate_up[r, :I]) * gate_up[r, I:]. Replaces
+ *   the activation product inside layer.mlp (flex_decode.py:232).
+ * ------------------------------------------------------------------- */
+int mb_rmsnorm(const void* x, const void* residual, const void* weight, float eps, int rows, int dim, void* sum_out,
+               void* norm_out, mb_stream_t stream);
+int mb_silu_mul(const void* gate_up, int rows, int inter, void* out, mb_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MOUSE_B200_H */

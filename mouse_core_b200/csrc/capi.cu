@@ -1,0 +1,248 @@
+// extern "C" entry points declared in include/mouse_b200.h: argument
+// validation, TMA descriptor encoding and kernel launches. No exceptions cross
+// the ABI; every failure returns a status and records a message.
+#include <string>
+
+#include "../../include/mouse_b200.h"
+#include "common.cuh"
+#include "kernels.h"
+
+namespace {
+
+thread_local std::string g_err;
+
+int fail(int code, const std::string& msg) {
+  g_err = msg;
+  return code;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+  return fail(MB_ERR_CUDA, std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  if (!fn) {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(ptr);
+  }
+  return fn;
+}
+
+// 2-D view [rows, head_dim] of one layer's pool, 64x64 boxes, 128B swizzle.
+int encode_pool_map(CUtensorMap* map, const void* pool, long long rows, int head_dim) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return fail(MB_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
+  cuuint64_t dims[2] = {(cuuint64_t)head_dim, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)head_dim * 2};
+  cuuint32_t box[2] = {64, 64};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(pool), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(MB_ERR_CUDA, "cuTensorMapEncodeTiled failed (" + std::to_string((int)r) + ")");
+  return MB_OK;
+}
+
+int check_decode_shape(int batch, int q_len, int q_heads, int kv_heads, int head_dim, int page_size) {
+  if (batch < 0 || q_len < 0 || q_heads <= 0 || kv_heads <= 0)
+    return fail(MB_ERR_INVALID_ARG, "batch/q_len must be >= 0 and head counts > 0");
+  if (q_heads % kv_heads != 0) return fail(MB_ERR_INVALID_ARG, "q_heads must be a multiple of kv_heads");
+  if (head_dim != 64 && head_dim != 128) return fail(MB_ERR_UNSUPPORTED, "head_dim must be 64 or 128");
+  if (page_size <= 0 || page_size % 64 != 0) return fail(MB_ERR_UNSUPPORTED, "page_size must be a multiple of 64");
+  return MB_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* mb_last_error(void) { return g_err.c_str(); }
+
+int mb_version(void) { return 100; }
+
+int mb_device_status(int* status_out, int clear) {
+  if (!status_out) return fail(MB_ERR_INVALID_ARG, "status_out is NULL");
+  cudaError_t e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceSynchronize");
+  e = cudaMemcpyFromSymbol(status_out, mb::g_device_status, sizeof(int));
+  if (e != cudaSuccess) return cuda_fail(e, "read device status");
+  if (clear) {
+    const int zero = 0;
+    e = cudaMemcpyToSymbol(mb::g_device_status, &zero, sizeof(int));
+    if (e != cudaSuccess) return cuda_fail(e, "clear device status");
+  }
+  return MB_OK;
+}
+
+size_t mb_decode_workspace_bytes(int batch, int kv_heads, int q_rows, int head_dim, int max_kv_len) {
+  if (batch <= 0 || kv_heads <= 0 || q_rows <= 0 || q_rows > 16) return 0;
+  if (head_dim != 64 && head_dim != 128) return 0;
+  mb::WorkspaceLayout lay;
+  return mb::decode_workspace_layout(batch, kv_heads, q_rows, head_dim, max_kv_len, &lay);
+}
+
+int mb_decode_plan(const int32_t* kv_len, int batch, int kv_heads, int q_rows, int head_dim, int max_kv_len,
+                   void* workspace, size_t workspace_bytes, mb_stream_t stream) {
+  if (batch <= 0) return MB_OK;
+  if (!kv_len) return fail(MB_ERR_INVALID_ARG, "kv_len is NULL");
+  if (q_rows <= 0 || q_rows > 16) return fail(MB_ERR_INVALID_ARG, "a plan exists only for 1..16 query rows");
+  if (head_dim != 64 && head_dim != 128) return fail(MB_ERR_UNSUPPORTED, "head_dim must be 64 or 128");
+  mb::WorkspaceLayout lay;
+  const size_t need = mb::decode_workspace_layout(batch, kv_heads, q_rows, head_dim, max_kv_len, &lay);
+  if (!workspace || workspace_bytes < need || !aligned(workspace, 256))
+    return fail(MB_ERR_WORKSPACE, "workspace needs " + std::to_string(need) + " bytes, 256-byte aligned");
+  cudaError_t e = mb::launch_decode_plan(kv_len, batch, kv_heads, head_dim, lay,
+                                         static_cast<uint8_t*>(workspace), (cudaStream_t)stream);
+  return e == cudaSuccess ? MB_OK : cuda_fail(e, "decode plan launch");
+}
+
+int mb_decode_attention(const void* q, const void* k_pool, const void* v_pool, int num_pages,
+                        const int32_t* block_table, int max_pages, const int32_t* q_pos, const int32_t* kv_len,
+                        int batch, int q_len, int q_heads, int kv_heads, int head_dim, int page_size, float scale,
+                        int max_kv_len, int plan_ready, void* out, void* workspace, size_t workspace_bytes,
+                        mb_stream_t stream) {
+  int rc = check_decode_shape(batch, q_len, q_heads, kv_heads, head_dim, page_size);
+  if (rc) return rc;
+  if (batch == 0 || q_len == 0) return MB_OK;
+  if (!q || !k_pool || !v_pool || !block_table || !q_pos || !kv_len || !out)
+    return fail(MB_ERR_INVALID_ARG, "a required pointer is NULL");
+  if (num_pages <= 0 || max_pages <= 0) return fail(MB_ERR_INVALID_ARG, "num_pages and max_pages must be > 0");
+  if (!aligned(k_pool, 16) || !aligned(v_pool, 16) || !aligned(q, 4) || !aligned(out, 4))
+    return fail(MB_ERR_INVALID_ARG, "pools must be 16-byte aligned, q/out 4-byte aligned");
+  if (max_kv_len < 0 || (long long)max_kv_len > (long long)max_pages * page_size)
+    return fail(MB_ERR_INVALID_ARG, "max_kv_len exceeds max_pages * page_size");
+  const long long rows = (long long)num_pages * kv_heads * page_size;
+  if (rows >= (1ll << 31)) return fail(MB_ERR_UNSUPPORTED, "pool too large for one layer (>= 2^31 rows)");
+
+  const int G = q_heads / kv_heads;
+  const int R = G * q_len;
+  const bool split = R <= 16;
+
+  CUtensorMap km, vm;
+  if ((rc = encode_pool_map(&km, k_pool, rows, head_dim))) return rc;
+  if ((rc = encode_pool_map(&vm, v_pool, rows, head_dim))) return rc;
+
+  mb::AttnParams p{};
+  p.q = static_cast<const __nv_bfloat16*>(q);
+  p.out = static_cast<__nv_bfloat16*>(out);
+  p.block_table = block_table;
+  p.q_pos = q_pos;
+  p.kv_len = kv_len;
+  p.B = batch;
+  p.S = q_len;
+  p.Hq = q_heads;
+  p.Hkv = kv_heads;
+  p.G = G;
+  p.R = R;
+  p.head_dim = head_dim;
+  p.max_pages = max_pages;
+  p.page_size = page_size;
+  p.num_pages = num_pages;
+  p.scale_log2 = scale * 1.4426950408889634f;
+
+  mb::WorkspaceLayout lay{};
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  if (split) {
+    const size_t need = mb::decode_workspace_layout(batch, kv_heads, R, head_dim, max_kv_len, &lay);
+    if (!workspace || workspace_bytes < need || !aligned(workspace, 256))
+      return fail(MB_ERR_WORKSPACE, "workspace needs " + std::to_string(need) + " bytes, 256-byte aligned");
+    if (!plan_ready) {
+      cudaError_t e = mb::launch_decode_plan(kv_len, batch, kv_heads, head_dim, lay, ws, (cudaStream_t)stream);
+      if (e != cudaSuccess) return cuda_fail(e, "decode plan launch");
+    }
+  }
+  cudaError_t e = mb::launch_decode_attention(km, vm, p, lay, ws, split, (cudaStream_t)stream);
+  return e == cudaSuccess ? MB_OK : cuda_fail(e, "decode attention launch");
+}
+
+int mb_kv_append(const void* qkv, int tokens, int qkv_stride, const int32_t* pos, const int32_t* slot,
+                 const void* q_norm_w, const void* k_norm_w, float eps, const float* inv_freq,
+                 float attention_scaling, int q_heads, int kv_heads, int head_dim, int page_size,
+                 long long num_pages, void* q_out, void* k_out, void* v_out, void* k_pool, void* v_pool,
+                 mb_stream_t stream) {
+  if (tokens < 0) return fail(MB_ERR_INVALID_ARG, "tokens must be >= 0");
+  if (tokens == 0) return MB_OK;
+  if (head_dim != 64 && head_dim != 128) return fail(MB_ERR_UNSUPPORTED, "head_dim must be 64 or 128");
+  if (q_heads <= 0 || kv_heads <= 0) return fail(MB_ERR_INVALID_ARG, "head counts must be > 0");
+  if (!qkv || !pos || !inv_freq || !q_out) return fail(MB_ERR_INVALID_ARG, "a required pointer is NULL");
+  if (qkv_stride < (q_heads + 2 * kv_heads) * head_dim)
+    return fail(MB_ERR_INVALID_ARG, "qkv_stride smaller than (q_heads + 2 * kv_heads) * head_dim");
+  if (qkv_stride % 2 || !aligned(qkv, 4) || !aligned(q_out, 4))
+    return fail(MB_ERR_INVALID_ARG, "qkv/q_out must be 4-byte aligned with an even stride");
+  if ((k_pool == nullptr) != (v_pool == nullptr)) return fail(MB_ERR_INVALID_ARG, "pass both pools or neither");
+  if (k_pool && (!slot || page_size <= 0 || num_pages <= 0))
+    return fail(MB_ERR_INVALID_ARG, "paged append needs slot, page_size and num_pages");
+  mb::AppendParams p{};
+  p.qkv = static_cast<const __nv_bfloat16*>(qkv);
+  p.T = tokens;
+  p.qkv_stride = qkv_stride;
+  p.pos = pos;
+  p.slot = slot;
+  p.q_norm_w = static_cast<const __nv_bfloat16*>(q_norm_w);
+  p.k_norm_w = static_cast<const __nv_bfloat16*>(k_norm_w);
+  p.eps = eps;
+  p.inv_freq = inv_freq;
+  p.attn_scaling = attention_scaling;
+  p.Hq = q_heads;
+  p.Hkv = kv_heads;
+  p.head_dim = head_dim;
+  p.page_size = page_size > 0 ? page_size : 1;
+  p.q_out = static_cast<__nv_bfloat16*>(q_out);
+  p.k_out = static_cast<__nv_bfloat16*>(k_out);
+  p.v_out = static_cast<__nv_bfloat16*>(v_out);
+  p.k_pool = static_cast<__nv_bfloat16*>(k_pool);
+  p.v_pool = static_cast<__nv_bfloat16*>(v_pool);
+  p.num_slots = k_pool ? num_pages * (long long)page_size : 0;
+  cudaError_t e = mb::launch_append(p, (cudaStream_t)stream);
+  return e == cudaSuccess ? MB_OK : cuda_fail(e, "kv append launch");
+}
+
+int mb_page_copy(const void* src_pool, void* dst_pool, const int32_t* src_pages, const int32_t* dst_pages, int n,
+                 long long page_elems, mb_stream_t stream) {
+  if (n < 0) return fail(MB_ERR_INVALID_ARG, "n must be >= 0");
+  if (n == 0) return MB_OK;
+  if (!src_pool || !dst_pool || !src_pages || !dst_pages) return fail(MB_ERR_INVALID_ARG, "NULL pointer");
+  if (page_elems <= 0 || page_elems % 8 || !aligned(src_pool, 16) || !aligned(dst_pool, 16))
+    return fail(MB_ERR_INVALID_ARG, "page_elems must be a positive multiple of 8 and pools 16-byte aligned");
+  cudaError_t e = mb::launch_page_copy(static_cast<const __nv_bfloat16*>(src_pool),
+                                       static_cast<__nv_bfloat16*>(dst_pool), src_pages, dst_pages, n, page_elems,
+                                       (cudaStream_t)stream);
+  return e == cudaSuccess ? MB_OK : cuda_fail(e, "page copy launch");
+}
+
+int mb_rmsnorm(const void* x, const void* residual, const void* weight, float eps, int rows, int dim, void* sum_out,
+               void* norm_out, mb_stream_t stream) {
+  if (rows < 0 || dim <= 0 || dim % 2) return fail(MB_ERR_INVALID_ARG, "rows >= 0 and an even dim > 0 required");
+  if (rows == 0) return MB_OK;
+  if (!x || !weight || !norm_out) return fail(MB_ERR_INVALID_ARG, "NULL pointer");
+  if (residual && !sum_out) return fail(MB_ERR_INVALID_ARG, "residual needs sum_out");
+  if (!aligned(x, 4) || !aligned(norm_out, 4) || (residual && (!aligned(residual, 4) || !aligned(sum_out, 4))))
+    return fail(MB_ERR_INVALID_ARG, "buffers must be 4-byte aligned");
+  cudaError_t e = mb::launch_rmsnorm(static_cast<const __nv_bfloat16*>(x), static_cast<const __nv_bfloat16*>(residual),
+                                     static_cast<const __nv_bfloat16*>(weight), eps, rows, dim,
+                                     static_cast<__nv_bfloat16*>(sum_out), static_cast<__nv_bfloat16*>(norm_out),
+                                     (cudaStream_t)stream);
+  return e == cudaSuccess ? MB_OK : cuda_fail(e, "rmsnorm launch");
+}
+
+int mb_silu_mul(const void* gate_up, int rows, int inter, void* out, mb_stream_t stream) {
+  if (rows < 0 || inter <= 0 || inter % 2) return fail(MB_ERR_INVALID_ARG, "rows >= 0 and an even inter required");
+  if (rows == 0) return MB_OK;
+  if (!gate_up || !out || !aligned(gate_up, 4) || !aligned(out, 4))
+    return fail(MB_ERR_INVALID_ARG, "NULL or misaligned pointer");
+  cudaError_t e = mb::launch_silu_mul(static_cast<const __nv_bfloat16*>(gate_up), rows, inter,
+                                      static_cast<__nv_bfloat16*>(out), (cudaStream_t)stream);
+  return e == cudaSuccess ? MB_OK : cuda_fail(e, "silu_mul launch");
+}
+
+}  // extern "C"

@@ -1,0 +1,78 @@
+// Internal declarations shared by the kernel files and the C-ABI layer.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+#include <algorithm>
+
+namespace mb {
+
+struct AttnParams {
+  const __nv_bfloat16* q;      // [B, S, Hq, HD]
+  __nv_bfloat16* out;          // [B, S, Hq, HD]
+  const int32_t* block_table;  // [B, max_pages]
+  const int32_t* q_pos;        // [B, S]
+  const int32_t* kv_len;       // [B]
+  int B, S, Hq, Hkv, G, R, head_dim;
+  int max_pages, page_size, num_pages;
+  int chunk_tokens;
+  float scale_log2;
+  // split-mode work list (inside the caller's workspace)
+  const int2* entries;
+  const int* n_entries;
+  const int* row_start;
+  const int* row_chunks;
+  int* counters;
+  float* part_lse;
+  float* part_o;
+};
+
+struct WorkspaceLayout {
+  size_t max_entries;
+  size_t entries, n_entries, row_start, row_chunks, counters, part_lse, part_o;
+  size_t total;
+};
+
+size_t decode_chunk_tokens(int head_dim);
+size_t decode_workspace_layout(int B, int Hkv, int R, int head_dim, int max_kv_len, WorkspaceLayout* lay);
+cudaError_t launch_decode_plan(const int32_t* kv_len, int B, int Hkv, int head_dim, const WorkspaceLayout& lay,
+                               uint8_t* ws, cudaStream_t stream);
+cudaError_t launch_decode_attention(const CUtensorMap& km, const CUtensorMap& vm, AttnParams p,
+                                    const WorkspaceLayout& lay, uint8_t* ws, bool split, cudaStream_t stream);
+
+struct AppendParams {
+  const __nv_bfloat16* qkv;  // [T, qkv_stride]: q | k | v
+  int T, qkv_stride;
+  const int32_t* pos;        // [T] RoPE position
+  const int32_t* slot;       // [T] page * page_size + offset, or -1 (not cached)
+  const __nv_bfloat16* q_norm_w;  // [HD] or null
+  const __nv_bfloat16* k_norm_w;  // [HD] or null
+  float eps;
+  const float* inv_freq;     // [HD/2]
+  float attn_scaling;
+  int Hq, Hkv, head_dim, page_size;
+  __nv_bfloat16* q_out;      // [T, Hq, HD]
+  __nv_bfloat16* k_out;      // [T, Hkv, HD] or null (contiguous copy of the new keys)
+  __nv_bfloat16* v_out;      // [T, Hkv, HD] or null
+  __nv_bfloat16* k_pool;     // [P, Hkv, page, HD] or null
+  __nv_bfloat16* v_pool;
+  long long num_slots;       // P * page_size (slot bound check)
+};
+cudaError_t launch_append(const AppendParams& p, cudaStream_t stream);
+
+cudaError_t launch_page_copy(const __nv_bfloat16* src_pool, __nv_bfloat16* dst_pool, const int32_t* src_pages,
+                             const int32_t* dst_pages, int n, long long page_elems, cudaStream_t stream);
+
+cudaError_t launch_rmsnorm(const __nv_bfloat16* x, const __nv_bfloat16* residual, const __nv_bfloat16* w,
+                           float eps, int rows, int D, __nv_bfloat16* sum_out, __nv_bfloat16* norm_out,
+                           cudaStream_t stream);
+cudaError_t launch_silu_mul(const __nv_bfloat16* gate_up, int rows, int I, __nv_bfloat16* out, cudaStream_t stream);
+
+cudaError_t launch_segment_meta(const int64_t* seq, int L, int tile, int64_t* pos_out, int32_t* seg_start,
+                                int32_t* tile_kv_lo, cudaStream_t stream);
+
+}  // namespace mb

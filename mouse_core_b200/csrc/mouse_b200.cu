@@ -1,0 +1,6 @@
+// Single translation unit of libmouse_b200.so: the kernels share the device
+// status word without relocatable device code.
+#include "decode_attention.cu"
+#include "kv_append.cu"
+#include "elementwise.cu"
+#include "capi.cu"

@@ -1,0 +1,314 @@
+"""Paged cached decoding — drop-in for mouse-core's ``FlexDecodeSession``.
+
+Reference: ``FlexDecodeSession`` (src/mouse_core/models/backbone/flex_decode.py:
+75-240). Same constructor ``(model, batch_size, capacity)``, same
+``forward(*, embeds, lengths, output_hidden_states=False)`` contract, same
+``B``/``lengths`` attributes and errors; every row decodes exactly as it
+would alone with a private cache.
+
+What changes is the machinery, built for B200:
+
+* KV lives in pages of ``page_size`` tokens drawn from one pool per layer
+  (``[num_pages, kv_heads, page, head_dim]`` bf16) and addressed through a
+  block table, so a row that outgrows its space gets a new page instead of the
+  reference's whole-cache doubling copy (flex_decode.py:140-149).
+* Per layer, the decoder loop (flex_decode.py:208-234) runs five kernels of
+  ``libmouse_b200`` around three cuBLAS GEMMs: fused residual-add + RMSNorm;
+  QKV GEMM; K2 (q/k RMSNorm + RoPE + page append); K1 (paged split-KV GQA
+  attention, replacing the FlexAttention call and the per-call BlockMask
+  build); o_proj GEMM; residual-add + RMSNorm; gate/up GEMM; SiLU product;
+  down GEMM.
+* Per call, positions, cache slots and the changed block table are computed
+  on the host (where the lengths already are) and shipped in ONE host-to-device
+  copy; the split-KV work list is built once on the device and reused by every
+  layer. The reference's host syncs (``.max()`` at flex_decode.py:180,
+  ``nonzero`` at :195) are gone.
+
+The session requires a CUDA bf16 model with head_dim 64 or 128; anything else
+raises — there is no CPU or eager fallback.
+"""
+
+from __future__ import annotations
+
+from typing import Any, cast
+
+import numpy as np
+import torch
+import torch.nn.functional as F
+
+from mouse_core_b200 import kernels as K
+from mouse_core_b200.pages import PageTable
+
+DEFAULT_PAGE_SIZE = 128
+
+
+def _round_up(value: int, multiple: int) -> int:
+    return -(-value // multiple) * multiple
+
+
+class _LayerWeights:
+    """Per-layer weights; QKV and gate/up are concatenated once per weight
+    version so each runs as one GEMM."""
+
+    def __init__(self, layer, n_heads, n_kv_heads, head_dim):
+        self.layer = layer
+        self.version = None
+        self.refresh()
+
+    def _sources(self):
+        a = self.layer.self_attn
+        m = self.layer.mlp
+        return (a.q_proj.weight, a.k_proj.weight, a.v_proj.weight, m.gate_proj.weight, m.up_proj.weight)
+
+    def refresh(self) -> None:
+        ver = tuple((t.data_ptr(), t._version) for t in self._sources())
+        if ver == self.version:
+            return
+        a = self.layer.self_attn
+        m = self.layer.mlp
+        with torch.no_grad():
+            self.wqkv = torch.cat([a.q_proj.weight, a.k_proj.weight, a.v_proj.weight], 0).contiguous()
+            bq = a.q_proj.bias
+            self.bqkv = torch.cat([a.q_proj.bias, a.k_proj.bias, a.v_proj.bias]) if bq is not None else None
+            self.wgu = torch.cat([m.gate_proj.weight, m.up_proj.weight], 0).contiguous()
+            bg = getattr(m.gate_proj, "bias", None)
+            self.bgu = torch.cat([m.gate_proj.bias, m.up_proj.bias]) if bg is not None else None
+        self.version = ver
+        self.in_w = self.layer.input_layernorm.weight
+        self.in_eps = float(self.layer.input_layernorm.variance_epsilon)
+        self.post_w = self.layer.post_attention_layernorm.weight
+        self.post_eps = float(self.layer.post_attention_layernorm.variance_epsilon)
+        qn = getattr(a, "q_norm", None)
+        self.q_norm_w = qn.weight if qn is not None else None
+        self.k_norm_w = a.k_norm.weight if qn is not None else None
+        self.qk_eps = float(qn.variance_epsilon) if qn is not None else 1e-6
+        self.o_proj = a.o_proj
+        self.down = m.down_proj
+        self.scale = float(a.scaling)
+
+
+class PagedDecodeSession:
+    """Incremental decoder over ``batch_size`` independently-growing sequences.
+
+    Args:
+        model: A transformers decoder stack (``Qwen3Model`` / ``LlamaModel``)
+            with ``layers``, ``rotary_emb`` and ``norm``; used in place. Must
+            be bf16 on a CUDA device.
+        batch_size: Number of sequences decoded by this session.
+        capacity: Initial per-row KV slots used to size the page pool (the
+            pool grows when it runs out; rows never need a copy).
+        page_size: Tokens per KV page (a multiple of 64).
+        num_pages: Pool size in pages (default: enough for ``capacity`` slots
+            in every row).
+    """
+
+    def __init__(self, model: torch.nn.Module, batch_size: int, capacity: int = DEFAULT_PAGE_SIZE, *,
+                 page_size: int = DEFAULT_PAGE_SIZE, num_pages: int | None = None) -> None:
+        hf = cast(Any, model)
+        if getattr(hf.config, "use_sliding_window", False):
+            raise ValueError("FlexDecodeSession does not support sliding-window attention.")
+        self.model = hf
+        cfg = hf.config
+        self.B = int(batch_size)
+        self.n_heads = int(cfg.num_attention_heads)
+        self.n_kv_heads = int(cfg.num_key_value_heads)
+        self.head_dim = int(getattr(cfg, "head_dim", None) or cfg.hidden_size // cfg.num_attention_heads)
+        param = next(hf.parameters())
+        self.device, self.dtype = param.device, param.dtype
+        if self.device.type != "cuda":
+            raise RuntimeError("mouse_core_b200 decoding runs on a CUDA device (B200, sm_100a) only; "
+                               f"the model is on {self.device}")
+        if self.dtype != torch.bfloat16:
+            raise TypeError("mouse_core_b200 kernels compute in bfloat16; move the backbone to "
+                            f"torch.bfloat16 (got {self.dtype})")
+        if self.head_dim not in (64, 128):
+            raise ValueError(f"head_dim must be 64 or 128 for the sm_100a kernels, got {self.head_dim}")
+        if page_size <= 0 or page_size % 64:
+            raise ValueError("page_size must be a positive multiple of 64")
+        self.page_size = int(page_size)
+        self.n_layers = len(hf.layers)
+        cap = _round_up(max(int(capacity), 1), self.page_size)
+        pages_per_row = cap // self.page_size
+        P = int(num_pages) if num_pages is not None else max(self.B * pages_per_row, 1)
+        shape = (self.n_layers, P, self.n_kv_heads, self.page_size, self.head_dim)
+        # Zero-filled like the reference's cache: slots never written read as 0.
+        self.k_pool = torch.zeros(shape, device=self.device, dtype=self.dtype)
+        self.v_pool = torch.zeros_like(self.k_pool)
+        self.pages = PageTable(self.B, P, self.page_size, pages_per_row)
+        self._len = np.zeros(self.B, dtype=np.int64)
+        self._bt_dev = torch.full((self.B, self.pages.max_pages), -1, dtype=torch.int32, device=self.device)
+        self._workspace = torch.empty(0, dtype=torch.uint8, device=self.device)
+        self._staging = [None, None]
+        self._staging_ev = [None, None]
+        self._turn = 0
+        self._layers = [_LayerWeights(layer, self.n_heads, self.n_kv_heads, self.head_dim) for layer in hf.layers]
+        self.inv_freq = hf.rotary_emb.inv_freq.to(device=self.device, dtype=torch.float32)
+        self.attention_scaling = float(getattr(hf.rotary_emb, "attention_scaling", 1.0))
+        # When a list, each attention launch appends its (start, end) CUDA
+        # events recorded on the launching stream (used for roofline timing).
+        self.attn_events: list | None = None
+
+    # ------------------------------------------------------------------ state
+    @property
+    def lengths(self) -> torch.Tensor:
+        """Tokens cached per row, ``[B]`` long on the session device."""
+        return torch.from_numpy(self._len.copy()).to(self.device)
+
+    @property
+    def cap(self) -> int:
+        """Slots addressable per row without widening the block table."""
+        return self.pages.max_pages * self.page_size
+
+    @property
+    def block_table(self) -> torch.Tensor:
+        return self._bt_dev
+
+    def reset_rows(self, rows) -> None:
+        """Empty ``rows`` (their pages return to the pool); the next call
+        decodes them from position 0, as a fresh session would."""
+        self.pages.release_rows(rows)
+        self._len[np.atleast_1d(np.asarray(rows, dtype=np.int64))] = 0
+
+    # ------------------------------------------------------------------ pool
+    def _grow_pool(self, need_free: int) -> None:
+        old = self.pages.num_pages
+        new = max(2 * old, old + need_free - self.pages.free_pages)
+        shape = (self.n_layers, new, self.n_kv_heads, self.page_size, self.head_dim)
+        for name in ("k_pool", "v_pool"):
+            src = getattr(self, name)
+            dst = torch.zeros(shape, device=self.device, dtype=self.dtype)
+            dst[:, :old] = src
+            setattr(self, name, dst)
+        self.pages.grow_pool(new)
+
+    def _stage(self, n_int32: int) -> torch.Tensor:
+        """A pinned int32 staging buffer that no in-flight copy still reads."""
+        i = self._turn
+        self._turn ^= 1
+        buf = self._staging[i]
+        ev = self._staging_ev[i]
+        if ev is not None:
+            ev.synchronize()
+        if buf is None or buf.numel() < n_int32:
+            buf = torch.empty(max(n_int32, 1024), dtype=torch.int32, pin_memory=True)
+            self._staging[i] = buf
+        return buf, i
+
+    # --------------------------------------------------------------- forward
+    def prepare(self, lengths, S: int):
+        """Host bookkeeping of one call: allocate pages and upload positions,
+        slots, lengths and (if changed) the block table in one copy.
+        Returns the device views ``(q_pos [B,S], kv_len [B], slot [B*S], max_kv)``."""
+        B = self.B
+        n = np.asarray(lengths, dtype=np.int64).reshape(-1)
+        if n.shape[0] != B:
+            raise ValueError(f"lengths has {n.shape[0]} entries, session batch_size={B}.")
+        if (n < 0).any() or (n > S).any():
+            raise ValueError(f"lengths must satisfy 0 <= lengths[b] <= S={S}.")
+        new_len = self._len + n
+        add = self.pages.pages_needed(new_len)
+        total = int(add.sum())
+        if total > self.pages.free_pages:
+            self._grow_pool(total)
+        self.pages.allocate(add)
+
+        col = np.arange(S, dtype=np.int64)[None, :]
+        pad = (S - n)[:, None]
+        pos = self._len[:, None] + col - pad
+        q_pos = np.maximum(pos, 0)
+        real = col >= pad
+        rows = np.broadcast_to(np.arange(B)[:, None], (B, S))
+        slot = np.full((B, S), -1, dtype=np.int64)
+        if real.any():
+            slot[real] = self.pages.slots(rows[real], pos[real])
+
+        bt_changed = self.pages.dirty
+        width = self.pages.max_pages
+        n_meta = 2 * B * S + B + (B * width if bt_changed else 0)
+        buf, i = self._stage(n_meta)
+        host = buf.numpy()
+        o = 0
+        host[o:o + B * S] = q_pos.reshape(-1)
+        o += B * S
+        host[o:o + B] = new_len
+        o += B
+        host[o:o + B * S] = slot.reshape(-1)
+        o += B * S
+        if bt_changed:
+            host[o:o + B * width] = self.pages.table.reshape(-1)
+        dev = buf[:n_meta].to(self.device, non_blocking=True)
+        ev = torch.cuda.Event()
+        ev.record()
+        self._staging_ev[i] = ev
+        q_pos_d = dev[:B * S].view(B, S)
+        kv_len_d = dev[B * S:B * S + B]
+        slot_d = dev[B * S + B:2 * B * S + B]
+        if bt_changed:
+            if self._bt_dev.shape[1] != width:
+                self._bt_dev = torch.empty((B, width), dtype=torch.int32, device=self.device)
+            self._bt_dev.copy_(dev[2 * B * S + B:].view(B, width))
+            self.pages.dirty = False
+        self._len = new_len
+        return q_pos_d, kv_len_d, slot_d, int(new_len.max()) if B else 0
+
+    @torch.no_grad()
+    def forward(self, *, embeds: torch.Tensor, lengths, output_hidden_states: bool = False):
+        """Decode one chunk per sequence (left-padded ``embeds [B, S, D]``,
+        ``lengths[b]`` real trailing tokens per row). Returns hidden states
+        ``[B, S, D]`` (pad positions meaningless) and, with
+        ``output_hidden_states=True``, the tuple of per-layer hidden states."""
+        B, S, D = embeds.shape
+        if B != self.B:
+            raise ValueError(f"Session was created for batch_size={self.B}, got {B}.")
+        x = embeds.to(self.device, self.dtype).reshape(B * S, D).contiguous()
+        q_pos, kv_len, slot, max_kv = self.prepare(lengths, S)
+        if B == 0 or S == 0:
+            h = x.view(B, S, D)
+            return (h, tuple(h for _ in range(self.n_layers))) if output_hidden_states else h
+
+        Hq, Hkv, hd = self.n_heads, self.n_kv_heads, self.head_dim
+        R = (Hq // Hkv) * S
+        split = R <= 16
+        if split:
+            need = K.decode_workspace_bytes(B, Hkv, R, hd, self.cap)
+            if self._workspace.numel() < need:
+                self._workspace = torch.empty(need, dtype=torch.uint8, device=self.device)
+            K.decode_plan(kv_len, Hkv, R, hd, self.cap, self._workspace)
+        q_pos_flat = q_pos.reshape(-1)
+
+        resid, delta = x, None
+        hiddens = []
+        for li, lw in enumerate(self._layers):
+            lw.refresh()
+            if delta is None:
+                _, hn = K.rmsnorm(resid, lw.in_w, lw.in_eps)
+            else:
+                resid, hn = K.rmsnorm(delta, lw.in_w, lw.in_eps, residual=resid)
+            qkv = F.linear(hn, lw.wqkv, lw.bqkv)
+            q = K.kv_append(qkv, q_pos_flat, Hq, Hkv, hd, self.inv_freq, self.attention_scaling,
+                            lw.q_norm_w, lw.k_norm_w, lw.qk_eps, slot=slot,
+                            k_pool=self.k_pool[li], v_pool=self.v_pool[li])
+            if self.attn_events is not None:
+                ev0 = torch.cuda.Event(enable_timing=True)
+                ev0.record()
+            o = K.decode_attention(q.view(B, S, Hq, hd), self.k_pool[li], self.v_pool[li], self._bt_dev, q_pos,
+                                   kv_len, lw.scale, self.cap, workspace=self._workspace if split else None,
+                                   plan_ready=split)
+            if self.attn_events is not None:
+                ev1 = torch.cuda.Event(enable_timing=True)
+                ev1.record()
+                self.attn_events.append((ev0, ev1))
+            a = lw.o_proj(o.view(B * S, Hq * hd))
+            resid, hn2 = K.rmsnorm(a, lw.post_w, lw.post_eps, residual=resid)
+            delta = lw.down(K.silu_mul(F.linear(hn2, lw.wgu, lw.bgu)))
+            if output_hidden_states:
+                hiddens.append((resid + delta).view(B, S, D))
+        h = hiddens[-1] if output_hidden_states else (resid + delta).view(B, S, D)
+        h = self.model.norm(h)
+        if output_hidden_states:
+            return h, tuple(hiddens)
+        return h
+
+
+# The reference's name, so callers and tests written against it keep working.
+FlexDecodeSession = PagedDecodeSession

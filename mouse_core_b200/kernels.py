@@ -1,0 +1,174 @@
+"""Torch-facing wrappers of the C ABI: check devices, dtypes and layouts, then
+pass raw pointers and torch's current CUDA stream to ``libmouse_b200.so``.
+
+Every function raises ``TypeError``/``ValueError`` on bad arguments and
+``mouse_core_b200._lib.KernelError`` if the library reports an error. Nothing
+here computes on the CPU.
+"""
+
+from __future__ import annotations
+
+import torch
+
+from mouse_core_b200 import _lib
+
+BF16 = torch.bfloat16
+
+# Kernels of libmouse_b200 launched through this module (read by the bench).
+launch_count = [0]
+
+
+def _count(n: int = 1) -> None:
+    launch_count[0] += n
+
+
+def _need(t: torch.Tensor, name: str, dtype=None, contiguous=True) -> None:
+    if not isinstance(t, torch.Tensor):
+        raise TypeError(f"{name} must be a torch.Tensor")
+    if t.device.type != "cuda":
+        raise ValueError(f"{name} must be on a CUDA device, got {t.device}")
+    if dtype is not None and t.dtype != dtype:
+        raise TypeError(f"{name} must be {dtype}, got {t.dtype}")
+    if contiguous and not t.is_contiguous():
+        raise ValueError(f"{name} must be contiguous")
+
+
+def _p(t):
+    return None if t is None else t.data_ptr()
+
+
+def _stream(t: torch.Tensor):
+    return torch.cuda.current_stream(t.device).cuda_stream
+
+
+def decode_workspace_bytes(batch: int, kv_heads: int, q_rows: int, head_dim: int, max_kv_len: int) -> int:
+    return int(_lib.load().mb_decode_workspace_bytes(batch, kv_heads, q_rows, head_dim, max_kv_len))
+
+
+def decode_plan(kv_len: torch.Tensor, kv_heads: int, q_rows: int, head_dim: int, max_kv_len: int,
+                workspace: torch.Tensor) -> None:
+    _need(kv_len, "kv_len", torch.int32)
+    _need(workspace, "workspace", torch.uint8)
+    _lib.call("mb_decode_plan", _p(kv_len), kv_len.numel(), kv_heads, q_rows, head_dim, max_kv_len,
+              _p(workspace), workspace.numel(), _stream(kv_len))
+    _count()
+
+
+def decode_attention(q: torch.Tensor, k_pool: torch.Tensor, v_pool: torch.Tensor, block_table: torch.Tensor,
+                     q_pos: torch.Tensor, kv_len: torch.Tensor, scale: float, max_kv_len: int,
+                     out: torch.Tensor | None = None, workspace: torch.Tensor | None = None,
+                     plan_ready: bool = False) -> torch.Tensor:
+    """Paged GQA attention (K1).
+
+    q ``[B, S, Hq, hd]`` bf16; pools ``[P, Hkv, page, hd]`` bf16 (one layer);
+    block_table ``[B, max_pages]`` int32; q_pos ``[B, S]`` int32; kv_len
+    ``[B]`` int32. Returns ``out [B, S, Hq, hd]``.
+    """
+    _need(q, "q", BF16)
+    _need(k_pool, "k_pool", BF16)
+    _need(v_pool, "v_pool", BF16)
+    _need(block_table, "block_table", torch.int32)
+    _need(q_pos, "q_pos", torch.int32)
+    _need(kv_len, "kv_len", torch.int32)
+    if q.ndim != 4 or k_pool.ndim != 4 or k_pool.shape != v_pool.shape:
+        raise ValueError("q must be [B, S, Hq, hd] and the pools [P, Hkv, page, hd] of equal shape")
+    B, S, Hq, hd = q.shape
+    P, Hkv, page, hd2 = k_pool.shape
+    if hd2 != hd:
+        raise ValueError(f"head_dim mismatch: q {hd}, pool {hd2}")
+    if block_table.ndim != 2 or block_table.shape[0] != B or tuple(q_pos.shape) != (B, S) or kv_len.numel() != B:
+        raise ValueError("block_table [B, max_pages], q_pos [B, S] and kv_len [B] must match q")
+    if out is None:
+        out = torch.empty_like(q)
+    else:
+        _need(out, "out", BF16)
+    G = Hq // Hkv
+    ws_ptr, ws_n = None, 0
+    if G * S <= 16:
+        need = decode_workspace_bytes(B, Hkv, G * S, hd, max_kv_len)
+        if workspace is None or workspace.numel() < need:
+            workspace = torch.empty(need, dtype=torch.uint8, device=q.device)
+        _need(workspace, "workspace", torch.uint8)
+        ws_ptr, ws_n = _p(workspace), workspace.numel()
+    _lib.call("mb_decode_attention", _p(q), _p(k_pool), _p(v_pool), P, _p(block_table), block_table.shape[1],
+              _p(q_pos), _p(kv_len), B, S, Hq, Hkv, hd, page, float(scale), int(max_kv_len), int(plan_ready),
+              _p(out), ws_ptr, ws_n, _stream(q))
+    _count(2 if (ws_ptr is not None and not plan_ready) else 1)
+    return out
+
+
+def kv_append(qkv: torch.Tensor, pos: torch.Tensor, q_heads: int, kv_heads: int, head_dim: int,
+              inv_freq: torch.Tensor, attention_scaling: float = 1.0, q_norm_w: torch.Tensor | None = None,
+              k_norm_w: torch.Tensor | None = None, eps: float = 1e-6, slot: torch.Tensor | None = None,
+              k_pool: torch.Tensor | None = None, v_pool: torch.Tensor | None = None,
+              q_out: torch.Tensor | None = None, k_out: torch.Tensor | None = None,
+              v_out: torch.Tensor | None = None) -> torch.Tensor:
+    """Fused q/k RMSNorm + RoPE + paged append (K2). ``qkv [T, >=(Hq+2Hkv)hd]``
+    bf16 with unit inner stride; returns ``q_out [T, Hq, hd]``."""
+    _need(qkv, "qkv", BF16, contiguous=False)
+    if qkv.ndim != 2 or qkv.stride(1) != 1:
+        raise ValueError("qkv must be 2-D with unit inner stride")
+    _need(pos, "pos", torch.int32)
+    _need(inv_freq, "inv_freq", torch.float32)
+    T = qkv.shape[0]
+    if pos.numel() != T:
+        raise ValueError("pos must have one entry per token")
+    if q_out is None:
+        q_out = torch.empty(T, q_heads, head_dim, dtype=BF16, device=qkv.device)
+    for name, t in (("q_norm_w", q_norm_w), ("k_norm_w", k_norm_w)):
+        if t is not None:
+            _need(t, name, BF16)
+    page_size, num_pages = 0, 0
+    if k_pool is not None:
+        _need(k_pool, "k_pool", BF16)
+        _need(v_pool, "v_pool", BF16)
+        _need(slot, "slot", torch.int32)
+        num_pages, _, page_size, _ = k_pool.shape
+    for name, t in (("k_out", k_out), ("v_out", v_out)):
+        if t is not None:
+            _need(t, name, BF16)
+    _lib.call("mb_kv_append", _p(qkv), T, qkv.stride(0), _p(pos), _p(slot), _p(q_norm_w), _p(k_norm_w),
+              float(eps), _p(inv_freq), float(attention_scaling), q_heads, kv_heads, head_dim, page_size,
+              num_pages, _p(q_out), _p(k_out), _p(v_out), _p(k_pool), _p(v_pool), _stream(qkv))
+    _count()
+    return q_out
+
+
+def page_copy(src_pool: torch.Tensor, dst_pool: torch.Tensor, src_pages: torch.Tensor,
+              dst_pages: torch.Tensor) -> None:
+    """``dst_pool[dst_pages[i]] = src_pool[src_pages[i]]`` (K3), one layer."""
+    _need(src_pool, "src_pool", BF16)
+    _need(dst_pool, "dst_pool", BF16)
+    _need(src_pages, "src_pages", torch.int32)
+    _need(dst_pages, "dst_pages", torch.int32)
+    page_elems = src_pool[0].numel()
+    _lib.call("mb_page_copy", _p(src_pool), _p(dst_pool), _p(src_pages), _p(dst_pages), src_pages.numel(),
+              page_elems, _stream(src_pool))
+    _count()
+
+
+def rmsnorm(x: torch.Tensor, weight: torch.Tensor, eps: float, residual: torch.Tensor | None = None):
+    """Returns ``(sum, norm)``: ``sum = x + residual`` (or ``x``), ``norm = RMSNorm(sum) * weight``."""
+    _need(x, "x", BF16)
+    _need(weight, "weight", BF16)
+    D = x.shape[-1]
+    rows = x.numel() // D
+    norm = torch.empty_like(x)
+    s = None
+    if residual is not None:
+        _need(residual, "residual", BF16)
+        s = torch.empty_like(x)
+    _lib.call("mb_rmsnorm", _p(x), _p(residual), _p(weight), float(eps), rows, D, _p(s), _p(norm), _stream(x))
+    _count()
+    return (s if s is not None else x), norm
+
+
+def silu_mul(gate_up: torch.Tensor) -> torch.Tensor:
+    """``silu(gate) * up`` for ``gate_up [..., 2I]``; returns ``[..., I]``."""
+    _need(gate_up, "gate_up", BF16)
+    I2 = gate_up.shape[-1]
+    rows = gate_up.numel() // I2
+    out = torch.empty(*gate_up.shape[:-1], I2 // 2, dtype=BF16, device=gate_up.device)
+    _lib.call("mb_silu_mul", _p(gate_up), rows, I2 // 2, _p(out), _stream(gate_up))
+    _count()
+    return out

@@ -1,0 +1,111 @@
+"""Decode-layout and segment index maps of the packed/cached paths.
+
+Same functions and results as the reference (bit-exact; checked against
+fixtures it produced), written as whole-tensor gathers instead of the
+reference's per-row Python loops with ``.item()`` host syncs:
+
+* ``left_align_content``             embedding/packing.py:8-28
+* ``flat_to_batched_left_pad``       models/base.py:1163-1201
+* ``flat_sequence_position_ids``     models/base.py:1226-1236
+* ``flat_sequence_causal_mask``      models/base.py:1204-1223
+
+They run on whatever device their inputs are on (they are index plumbing,
+not kernels); the CUDA training path computes position ids with the K7
+segment kernel instead (``mouse_core_b200.packed``).
+"""
+
+from __future__ import annotations
+
+import torch
+
+
+def left_align_content(embeds: torch.Tensor, prediction_indices: torch.Tensor):
+    """Shift right-padded rows so content sits in the trailing columns.
+
+    Row ``b`` has ``prediction_indices[b, -1] + 1`` content columns; rows with
+    content move it to columns ``L - row_len ..`` and shift their indices by
+    ``L - row_len``. Returns ``(aligned_embeds, aligned_indices)``.
+    """
+    B, L = embeds.shape[0], embeds.shape[1]
+    row_len = prediction_indices[:, -1] + 1
+    has = row_len > 0
+    offset = torch.where(has, L - row_len, torch.zeros_like(row_len))
+    col = torch.arange(L, device=embeds.device)[None, :]
+    src = col - offset[:, None]
+    keep = (src >= 0) & has[:, None]
+    gathered = torch.gather(embeds, 1, src.clamp_min(0)[..., None].expand(B, L, embeds.shape[2]))
+    aligned = torch.where(keep[..., None], gathered, torch.zeros((), dtype=embeds.dtype, device=embeds.device))
+    return aligned, prediction_indices + offset[:, None]
+
+
+def _rank_within_id(sequence_ids: torch.Tensor) -> torch.Tensor:
+    """Index of each token among the tokens sharing its id (stable order)."""
+    L = sequence_ids.shape[0]
+    if L == 0:
+        return torch.zeros(0, dtype=torch.long, device=sequence_ids.device)
+    order = torch.sort(sequence_ids, stable=True).indices
+    sid = sequence_ids[order]
+    first = torch.ones(L, dtype=torch.bool, device=sequence_ids.device)
+    first[1:] = sid[1:] != sid[:-1]
+    idx = torch.arange(L, device=sequence_ids.device)
+    group_start = torch.cummax(torch.where(first, idx, torch.zeros_like(idx)), 0).values
+    rank = torch.empty(L, dtype=torch.long, device=sequence_ids.device)
+    rank[order] = idx - group_start
+    return rank
+
+
+def flat_to_batched_left_pad(embeds: torch.Tensor, sequence_ids: torch.Tensor, prediction_indices: torch.Tensor,
+                             B: int, S: int, step_counts):
+    """Scatter flat ``[L, D]`` embeds into right-padded ``[B, Lmax, D]`` rows.
+
+    Returns ``(out, token_lengths, local_indices)``: ``token_lengths[b]`` is
+    the number of tokens with id ``b`` (a Python list, as in the reference),
+    and ``local_indices[b, S - n + s]`` the in-row index of row ``b``'s
+    ``s``-th prediction token (``n = step_counts[b]``).
+    """
+    L, D = embeds.shape
+    dev = embeds.device
+    seq = sequence_ids.to(dev).long()
+    counts = torch.bincount(seq[(seq >= 0) & (seq < B)], minlength=B)[:B] if L else torch.zeros(B, dtype=torch.long)
+    token_lengths = [int(c) for c in counts.tolist()]
+    lmax = max(token_lengths) if token_lengths else 0
+    sel = (seq >= 0) & (seq < B)
+    # tokens of rows outside 0..B-1 have no in-row index (-1, as in the reference)
+    rank = torch.where(sel, _rank_within_id(seq), torch.full_like(seq, -1))
+    out = embeds.new_zeros(B, lmax, D)
+    out[seq[sel], rank[sel]] = embeds[sel]
+    steps = [int(step_counts[b]) if b < len(step_counts) else S for b in range(B)]
+    local = torch.zeros(B, S, dtype=torch.long, device=dev)
+    total = sum(steps)
+    if total:
+        n = torch.tensor(steps, dtype=torch.long, device=dev)
+        rows = torch.repeat_interleave(torch.arange(B, device=dev), n)
+        within = torch.arange(total, device=dev) - torch.repeat_interleave(torch.cumsum(n, 0) - n, n)
+        cols = S - n[rows] + within
+        local[rows, cols] = rank[prediction_indices[:total].to(dev).long()]
+    return out, token_lengths, local
+
+
+def flat_sequence_position_ids(sequence_ids: torch.Tensor) -> torch.Tensor:
+    """RoPE positions ``[1, L]`` restarting at 0 at every run boundary
+    (``sequence_ids[i] != sequence_ids[i-1]``)."""
+    L = sequence_ids.shape[0]
+    dev = sequence_ids.device
+    if L == 0:
+        return torch.zeros(1, 0, dtype=torch.long, device=dev)
+    idx = torch.arange(L, device=dev)
+    boundary = torch.ones(L, dtype=torch.bool, device=dev)
+    boundary[1:] = sequence_ids[1:] != sequence_ids[:-1]
+    run_start = torch.cummax(torch.where(boundary, idx, torch.zeros_like(idx)), 0).values
+    return (idx - run_start).unsqueeze(0)
+
+
+def flat_sequence_causal_mask(*, sequence_ids: torch.Tensor, dtype: torch.dtype) -> torch.Tensor:
+    """Additive ``[1, 1, L, L]`` mask: 0 where ``kv <= q`` and ids match,
+    ``finfo(dtype).min`` elsewhere (the CPU SDPA path's dense mask)."""
+    L = sequence_ids.shape[0]
+    idx = torch.arange(L, device=sequence_ids.device)
+    allow = (idx[None, :] <= idx[:, None]) & (sequence_ids[:, None] == sequence_ids[None, :])
+    out = torch.full((L, L), torch.finfo(dtype).min, dtype=dtype, device=sequence_ids.device)
+    out.masked_fill_(allow, 0.0)
+    return out.view(1, 1, L, L)

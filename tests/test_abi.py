@@ -1,0 +1,69 @@
+"""The C-ABI library builds for sm_100a, loads, and exports exactly what
+include/mouse_b200.h declares (no GPU needed: only argument-validation paths
+that return before any CUDA call are exercised)."""
+
+from __future__ import annotations
+
+import ctypes
+import os
+import re
+
+import pytest
+
+from mouse_core_b200 import _lib, build
+
+HEADER = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "include", "mouse_b200.h")
+
+
+def declared_functions():
+    text = open(HEADER).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(mb_[a-z0-9_]+)\s*\(", text)))
+
+
+@pytest.fixture(scope="module")
+def lib():
+    build.build()
+    return _lib.load()
+
+
+def test_header_declares_entry_points():
+    names = declared_functions()
+    assert "mb_decode_attention" in names and "mb_kv_append" in names
+    assert set(names) == set(_lib.PROTOTYPES), "ctypes prototypes and header disagree"
+
+
+def test_library_exports_every_declared_symbol(lib):
+    raw = ctypes.CDLL(build.LIB)
+    for name in declared_functions():
+        assert hasattr(raw, name), f"{name} declared in mouse_b200.h but not exported"
+
+
+def test_version_and_error_text(lib):
+    assert lib.mb_version() == 100
+    # head_dim 96 is rejected before any CUDA call
+    rc = lib.mb_decode_attention(None, None, None, 1, None, 1, None, None, 1, 1, 2, 1, 96, 64, 1.0, 1, 0,
+                                 None, None, 0, None)
+    assert rc == 2  # MB_ERR_UNSUPPORTED
+    assert b"head_dim" in lib.mb_last_error()
+    rc = lib.mb_decode_attention(None, None, None, 1, None, 1, None, None, 1, 1, 3, 2, 64, 64, 1.0, 1, 0,
+                                 None, None, 0, None)
+    assert rc == 1 and b"multiple" in lib.mb_last_error()
+    rc = lib.mb_kv_append(None, 4, 8, None, None, None, None, 1e-6, None, 1.0, 1, 1, 64, 0, 0, None, None, None,
+                          None, None, None)
+    assert rc == 1
+
+
+def test_workspace_size_rules(lib):
+    small = lib.mb_decode_workspace_bytes(256, 8, 2, 128, 4096)
+    big = lib.mb_decode_workspace_bytes(256, 8, 2, 128, 8192)
+    assert 0 < small < big
+    assert lib.mb_decode_workspace_bytes(256, 8, 17, 128, 4096) == 0  # block mode needs none
+    assert lib.mb_decode_workspace_bytes(256, 8, 2, 96, 4096) == 0
+
+
+def test_zero_sized_calls_are_noops(lib):
+    assert lib.mb_kv_append(None, 0, 0, None, None, None, None, 0.0, None, 1.0, 1, 1, 64, 0, 0, None, None, None,
+                            None, None, None) == 0
+    assert lib.mb_page_copy(None, None, None, None, 0, 8, None) == 0
+    assert lib.mb_rmsnorm(None, None, None, 1e-6, 0, 8, None, None, None) == 0

@@ -1,0 +1,302 @@
+"""GPU parity of the cached-decode path (K1 paged attention, K2 append, glue
+kernels, the paged session) against the CPU oracle, which is itself pinned to
+the reference by tests/test_oracle_golden.py.
+
+Tolerances: kernels compute in bf16 with fp32 accumulation; attention and
+append outputs must be within 2e-2 max-abs of the float64 oracle on the same
+bf16 inputs; whole-model hidden states within atol 2e-2 + rtol 1e-2 (the bf16
+residual stream itself is rounded to 2^-8 relative)."""
+
+from __future__ import annotations
+
+import gc
+import math
+import weakref
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import attention as oatt
+from oracle import decoder as odec
+from oracle import policy as opol
+from tests.golden_io import decoder_from_fixture, load
+
+pytestmark = pytest.mark.gpu
+
+ATOL = 2e-2
+
+
+def _dev():
+    if not torch.cuda.is_available():
+        pytest.skip("needs a CUDA device")
+    from mouse_core_b200 import build
+
+    build.build()
+    return torch.device("cuda")
+
+
+def _paged_case(B, Hq, Hkv, hd, page, S, lens_after, n_new, seed):
+    """Random q and per-row logical K/V scattered into a shuffled page pool."""
+    g = torch.Generator().manual_seed(seed)
+    q = torch.randn(B, S, Hq, hd, generator=g).bfloat16()
+    k_rows = [torch.randn(L, Hkv, hd, generator=g).bfloat16() for L in lens_after]
+    v_rows = [torch.randn(L, Hkv, hd, generator=g).bfloat16() for L in lens_after]
+    npg = [math.ceil(L / page) for L in lens_after]
+    P = sum(npg) + 3
+    perm = np.random.default_rng(seed).permutation(P).astype(np.int32)
+    maxp = max(max(npg), 1)
+    bt = np.full((B, maxp), -1, dtype=np.int32)
+    kp = torch.zeros(P, Hkv, page, hd, dtype=torch.bfloat16)
+    vp = torch.zeros_like(kp)
+    nxt = 0
+    for b, L in enumerate(lens_after):
+        for i in range(npg[b]):
+            pg = int(perm[nxt])
+            nxt += 1
+            bt[b, i] = pg
+            lo, hi = i * page, min(L, (i + 1) * page)
+            kp[pg, :, : hi - lo] = k_rows[b][lo:hi].transpose(0, 1)
+            vp[pg, :, : hi - lo] = v_rows[b][lo:hi].transpose(0, 1)
+    lens_before = np.array(lens_after) - np.array(n_new)
+    q_pos, _ = opol.decode_positions(lens_before, n_new, S)
+    return q, kp, vp, bt, q_pos.astype(np.int32), k_rows, v_rows
+
+
+CASES = [
+    # B, Hq, Hkv, hd, page, S, seed
+    (7, 16, 8, 128, 128, 1, 0),     # decode, split mode, G=2
+    (5, 32, 8, 64, 64, 1, 1),       # G=4, hd 64, page 64
+    (4, 32, 8, 64, 64, 4, 2),       # R = 16: largest split-mode row count
+    (4, 32, 8, 64, 128, 5, 3),      # R = 20: block mode
+    (3, 16, 8, 128, 128, 40, 4),    # ragged prefill chunk, 2 query blocks
+    (3, 4, 4, 128, 64, 3, 5),       # no GQA sharing
+    (2, 8, 2, 64, 64, 70, 6),       # G=4 prefill, 280 rows
+]
+
+
+@pytest.mark.parametrize("B,Hq,Hkv,hd,page,S,seed", CASES)
+def test_decode_attention_matches_oracle(B, Hq, Hkv, hd, page, S, seed):
+    dev = _dev()
+    from mouse_core_b200 import kernels as K
+
+    rng = np.random.default_rng(100 + seed)
+    n_new = rng.integers(0, S + 1, size=B)
+    n_new[0] = S
+    before = rng.integers(0, 1500, size=B)
+    before[-1] = 0 if B > 2 else before[-1]          # an empty history
+    if B > 3:
+        before[1] = 512 - n_new[1]                     # a chunk boundary
+        before[2] = 1024 + 1 - n_new[2]
+    lens_after = (before + n_new).tolist()
+    q, kp, vp, bt, q_pos, k_rows, v_rows = _paged_case(B, Hq, Hkv, hd, page, S, lens_after, n_new, seed)
+    scale = hd ** -0.5
+    out = K.decode_attention(q.to(dev), kp.to(dev), vp.to(dev), torch.from_numpy(bt).to(dev),
+                             torch.from_numpy(q_pos).to(dev), torch.tensor(lens_after, dtype=torch.int32, device=dev),
+                             scale, max(lens_after))
+    torch.cuda.synchronize()
+    ref = oatt.cached_decode_attention(q.float().numpy(), [k.float().numpy() for k in k_rows],
+                                       [v.float().numpy() for v in v_rows], q_pos, scale)
+    got = out.float().cpu().numpy()
+    assert np.isfinite(got).all()
+    err = np.abs(got - ref).max()
+    assert err < ATOL, f"max abs err {err}"
+    from mouse_core_b200 import _lib
+
+    assert _lib.device_status() == 0
+
+
+def test_decode_attention_long_rows_split_combine():
+    """Rows spanning many split chunks (the cross-CTA merge) at decode shape."""
+    dev = _dev()
+    from mouse_core_b200 import kernels as K
+
+    B, Hq, Hkv, hd, page, S = 6, 16, 8, 128, 128, 1
+    lens_after = [4096, 3001, 1, 5000, 2048, 777]
+    n_new = [1] * B
+    q, kp, vp, bt, q_pos, k_rows, v_rows = _paged_case(B, Hq, Hkv, hd, page, S, lens_after, n_new, 9)
+    out = K.decode_attention(q.to(dev), kp.to(dev), vp.to(dev), torch.from_numpy(bt).to(dev),
+                             torch.from_numpy(q_pos).to(dev), torch.tensor(lens_after, dtype=torch.int32, device=dev),
+                             hd ** -0.5, max(lens_after))
+    ref = oatt.cached_decode_attention(q.float().numpy(), [k.float().numpy() for k in k_rows],
+                                       [v.float().numpy() for v in v_rows], q_pos, hd ** -0.5)
+    assert np.abs(out.float().cpu().numpy() - ref).max() < ATOL
+
+
+@pytest.mark.parametrize("hd,qk_norm", [(128, True), (64, False), (64, True)])
+def test_kv_append_matches_oracle(hd, qk_norm):
+    dev = _dev()
+    from mouse_core_b200 import kernels as K
+
+    T, Hq, Hkv, page, P = 37, 8, 2, 64, 9
+    g = torch.Generator().manual_seed(hd)
+    qkv = torch.randn(T, (Hq + 2 * Hkv) * hd + 8, generator=g).bfloat16()[:, : (Hq + 2 * Hkv) * hd]
+    pos = torch.randint(0, 20000, (T,), generator=g, dtype=torch.int32)
+    slots = torch.randperm(P * page, generator=g)[:T].to(torch.int32)
+    slots[5] = -1  # a pad token: not cached
+    qw = (1 + 0.3 * torch.randn(hd, generator=g)).bfloat16() if qk_norm else None
+    kw = (1 + 0.3 * torch.randn(hd, generator=g)).bfloat16() if qk_norm else None
+    theta = 1e6 if hd == 128 else 5e5
+    inv_freq = 1.0 / (theta ** (torch.arange(0, hd, 2, dtype=torch.float32) / hd))
+    kp = torch.zeros(P, Hkv, page, hd, dtype=torch.bfloat16, device=dev)
+    vp = torch.zeros_like(kp)
+    qkv_d = torch.zeros(T, (Hq + 2 * Hkv) * hd + 8, dtype=torch.bfloat16, device=dev)
+    qkv_d[:, : (Hq + 2 * Hkv) * hd] = qkv.to(dev)
+    q_out = K.kv_append(qkv_d[:, : (Hq + 2 * Hkv) * hd], pos.to(dev), Hq, Hkv, hd, inv_freq.to(dev), 1.0,
+                        None if qw is None else qw.to(dev), None if kw is None else kw.to(dev), 1e-6,
+                        slot=slots.to(dev), k_pool=kp, v_pool=vp)
+    x = qkv.float().numpy().astype(np.float64)
+    qx = x[:, : Hq * hd].reshape(T, Hq, hd)
+    kx = x[:, Hq * hd:(Hq + Hkv) * hd].reshape(T, Hkv, hd)
+    vx = x[:, (Hq + Hkv) * hd:].reshape(T, Hkv, hd)
+    if qk_norm:
+        qx = odec.rms_norm(qx, qw.float().numpy(), 1e-6)
+        kx = odec.rms_norm(kx, kw.float().numpy(), 1e-6)
+    p = pos.numpy()
+    qr = odec.rope(qx, p, inv_freq.numpy())
+    kr = odec.rope(kx, p, inv_freq.numpy())
+    assert np.abs(q_out.float().cpu().numpy() - qr).max() < ATOL
+    kpc, vpc = kp.float().cpu().numpy(), vp.float().cpu().numpy()
+    written = np.zeros((P, page), dtype=bool)
+    for t in range(T):
+        s = int(slots[t])
+        if s < 0:
+            continue
+        pg, off = divmod(s, page)
+        written[pg, off] = True
+        assert np.abs(kpc[pg, :, off] - kr[t]).max() < ATOL
+        assert np.abs(vpc[pg, :, off] - vx[t]).max() < 1e-2
+    assert (kpc.transpose(0, 2, 1, 3)[~written] == 0).all(), "append wrote outside its slots"
+
+
+def test_rmsnorm_and_silu_mul_match_fp32():
+    dev = _dev()
+    from mouse_core_b200 import kernels as K
+
+    g = torch.Generator().manual_seed(0)
+    x = torch.randn(33, 1024, generator=g).bfloat16().to(dev)
+    r = torch.randn(33, 1024, generator=g).bfloat16().to(dev)
+    w = (1 + 0.1 * torch.randn(1024, generator=g)).bfloat16().to(dev)
+    s, n = K.rmsnorm(x, w, 1e-6, residual=r)
+    s_ref = (x.float() + r.float()).bfloat16().float()
+    assert torch.equal(s.float(), s_ref)
+    n_ref = s_ref * torch.rsqrt(s_ref.pow(2).mean(-1, keepdim=True) + 1e-6) * w.float()
+    assert (n.float() - n_ref).abs().max().item() < 3e-2
+    gu = torch.randn(9, 2 * 3072, generator=g).bfloat16().to(dev)
+    o = K.silu_mul(gu)
+    ref = torch.nn.functional.silu(gu[:, :3072].float()) * gu[:, 3072:].float()
+    assert (o.float() - ref).abs().max().item() < 3e-2
+
+
+def _backbone_from_fixture(rec, arch, dev):
+    from mouse_core_b200.backbone import LlamaBackbone, Qwen3Backbone
+
+    if arch == "qwen3":
+        bb = Qwen3Backbone(hidden_dim=64, num_layers=2, num_heads=2, num_key_value_heads=1, head_dim=64)
+    else:
+        bb = LlamaBackbone(hidden_dim=128, num_layers=2, num_heads=2, num_key_value_heads=1)
+    sd = {k[2:]: torch.from_numpy(v.astype(np.float32)) for k, v in rec.items() if k.startswith("w:")}
+    missing, unexpected = bb.model.load_state_dict(sd, strict=False)
+    assert not unexpected and all("rotary" in m for m in missing)
+    bb.model.rotary_emb.inv_freq.copy_(torch.from_numpy(rec["inv_freq"]))
+    return bb.to(device=dev, dtype=torch.bfloat16).eval()
+
+
+@pytest.mark.parametrize("arch", ["qwen3", "llama"])
+def test_session_matches_reference_golden(arch):
+    """Ragged schedule incl. empty first chunks, zero-length rows and a pool
+    that must grow: real columns match the reference's FlexDecodeSession."""
+    dev = _dev()
+    rec = load(f"decode_{arch}.npz")
+    bb = _backbone_from_fixture(rec, arch, dev)
+    sess = bb.decode_session(batch_size=3, capacity=4, num_pages=1)  # must grow
+    # The oracle with the same bf16-rounded weights and inputs isolates kernel error.
+    rec16 = {k: (v.astype(np.float32) if k.startswith("w:") else v) for k, v in rec.items()}
+    for k in list(rec16):
+        if k.startswith("w:"):
+            rec16[k] = torch.from_numpy(rec16[k]).bfloat16().float().numpy()
+    dec16, _ = decoder_from_fixture(rec16)
+    osess = odec.DecodeSessionOracle(dec16, 3)
+    for ci, lens in enumerate(rec["schedule"].tolist()):
+        emb = torch.from_numpy(rec[f"c{ci}_emb"])
+        h, layers = sess.forward(embeds=emb.to(dev), lengths=lens, output_hidden_states=True)
+        h = h.float().cpu().numpy()
+        assert np.isfinite(h).all(), "NaN/inf leaked from padding"
+        S = h.shape[1]
+        ref = rec[f"c{ci}_out"]
+        o16 = osess.forward(emb.bfloat16().float().numpy(), lens)
+        for b, n in enumerate(lens):
+            if n:
+                np.testing.assert_allclose(h[b, S - n:], o16[b, S - n:], atol=ATOL, rtol=1e-2)
+                np.testing.assert_allclose(h[b, S - n:], ref[b, S - n:], atol=5e-2, rtol=2e-2)
+    assert sess.lengths.cpu().tolist() == rec["final_lengths"].tolist()
+    assert sess.pages.num_pages >= 3, "the pool should have grown"
+
+
+def test_session_random_schedule_fuzz():
+    """Randomised ragged schedules on a Qwen3-shaped model (hd 128, GQA 2):
+    every real step equals the oracle session."""
+    dev = _dev()
+    from mouse_core_b200.backbone import Qwen3Backbone
+
+    torch.manual_seed(7)
+    bb = Qwen3Backbone(hidden_dim=256, num_layers=2, num_heads=4, num_key_value_heads=2, head_dim=128)
+    with torch.no_grad():
+        for n_, p in bb.model.named_parameters():
+            if "norm" in n_:
+                p.copy_(1 + 0.2 * torch.randn_like(p))
+            else:
+                p.mul_(3.0)  # make attention non-trivial
+        for p in bb.model.parameters():
+            p.copy_(p.bfloat16().float())
+    sd = {k: v.detach().numpy() for k, v in bb.model.state_dict().items() if "rotary" not in k}
+    cfg = odec.config_from_hf(bb.model.config, bb.model.rotary_emb.inv_freq.numpy())
+    dec = odec.DecoderOracle(sd, cfg)
+    bb = bb.to(device=dev, dtype=torch.bfloat16).eval()
+    rng = np.random.default_rng(3)
+    B = 5
+    sess = bb.decode_session(batch_size=B, capacity=16)
+    osess = odec.DecodeSessionOracle(dec, B)
+    for call in range(6):
+        lens = rng.integers(0, 9, size=B)
+        if call == 0:
+            lens[1] = 300  # a long prefill row: block mode for S > 8
+        S = max(int(lens.max()), 1)
+        emb = torch.randn(B, S, 256).bfloat16()
+        h = sess.forward(embeds=emb.to(dev), lengths=lens.tolist()).float().cpu().numpy()
+        o = osess.forward(emb.float().numpy(), lens)
+        for b, n in enumerate(lens):
+            if n:
+                np.testing.assert_allclose(h[b, S - n:], o[b, S - n:], atol=3 * ATOL, rtol=2e-2)
+
+
+def test_session_freed_by_refcount_alone():
+    dev = _dev()
+    from mouse_core_b200.backbone import Qwen3Backbone
+
+    bb = Qwen3Backbone(hidden_dim=128, num_layers=1, num_heads=2, num_key_value_heads=1, head_dim=64)
+    bb = bb.to(device=dev, dtype=torch.bfloat16)
+    sess = bb.decode_session(batch_size=2, capacity=64)
+    sess.forward(embeds=torch.randn(2, 3, 128, device=dev), lengths=[3, 1])
+    wr = weakref.ref(sess)
+    gc.disable()
+    try:
+        del sess
+        assert wr() is None, "session stayed alive without cyclic GC"
+    finally:
+        gc.enable()
+
+
+def test_session_rejects_bad_inputs():
+    dev = _dev()
+    from mouse_core_b200.backbone import Qwen3Backbone
+
+    bb = Qwen3Backbone(hidden_dim=128, num_layers=1, num_heads=2, num_key_value_heads=1, head_dim=64)
+    with pytest.raises(TypeError):
+        bb.to(dev).decode_session(batch_size=2, capacity=8)  # fp32 model
+    bb = bb.to(device=dev, dtype=torch.bfloat16)
+    sess = bb.decode_session(batch_size=2, capacity=8)
+    with pytest.raises(ValueError, match="batch_size"):
+        sess.forward(embeds=torch.randn(3, 1, 128, device=dev), lengths=[1, 1, 1])
+    with pytest.raises(ValueError):
+        sess.forward(embeds=torch.randn(2, 1, 128, device=dev), lengths=[2, 1])

@@ -1,0 +1,94 @@
+"""Host-side logic of mouse_core_b200 on CPU: the kv_policy and packing maps
+must equal the reference's outputs bit for bit (fixtures made by the
+reference itself), and the page table must behave as a refcounted pool."""
+
+from __future__ import annotations
+
+import numpy as np
+import torch
+
+import mouse_core_b200 as mb
+from mouse_core_b200.pages import PageTable
+from tests.golden_io import load
+
+
+def test_kv_policy_bit_exact_with_reference():
+    g = load("kv_policy.json")
+    for mx, st, expect in g["bounds"]:
+        assert list(mb.resolve_cache_bounds(mx, st)) == expect
+    for ends, ctx, st, mx, expect in g["starts"]:
+        got = mb.rebuild_starts(ends=np.array(ends), context_start=ctx if isinstance(ctx, int) else np.array(ctx),
+                                start_cache=st, max_cache=mx)
+        assert got.dtype == np.int64 and got.tolist() == expect
+    for has, cs, ce, ends, ctx, mx, comp, expect in g["rebuild"]:
+        got = mb.cache_needs_rebuild(has_cache=has, cached_starts=np.array(cs), cached_ends=np.array(ce),
+                                     ends=np.array(ends), context_start=np.array(ctx), max_cache=mx,
+                                     batch_complete=comp)
+        assert got is expect
+
+
+def test_rows_needing_rebuild_agrees_with_batch_rule():
+    g = load("kv_policy.json")
+    for has, cs, ce, ends, ctx, mx, comp, expect in g["rebuild"]:
+        if not has or not comp or len(ends) != len(cs):
+            continue
+        rows = mb.rows_needing_rebuild(cached_starts=np.array(cs), cached_ends=np.array(ce), ends=np.array(ends),
+                                       context_start=np.array(ctx), max_cache=mx)
+        assert bool(rows.any()) == expect
+
+
+def test_position_ids_and_mask_bit_exact():
+    g = load("index_maps.npz")
+    names = sorted({k[4:-3] for k in g if k.startswith("pos_") and k.endswith("_in")})
+    for name in names:
+        seq = torch.tensor(g[f"pos_{name}_in"], dtype=torch.long)
+        got = mb.flat_sequence_position_ids(seq)
+        assert torch.equal(got, torch.tensor(g[f"pos_{name}_out"]).view(1, -1)), name
+        if f"mask_{name}_allow" in g:
+            m = mb.flat_sequence_causal_mask(sequence_ids=seq, dtype=torch.float32)
+            assert torch.equal(m[0, 0] == 0, torch.tensor(g[f"mask_{name}_allow"]))
+
+
+def test_packing_maps_bit_exact():
+    g = load("index_maps.npz")
+    for c in range(4):
+        a, ai = mb.left_align_content(torch.tensor(g[f"la{c}_emb"]), torch.tensor(g[f"la{c}_idx"]))
+        assert torch.equal(ai, torch.tensor(g[f"la{c}_outidx"]))
+        assert torch.equal(a, torch.tensor(g[f"la{c}_out"]))
+        steps = g[f"fb{c}_steps"]
+        B, S = steps.shape[0], int(steps.max())
+        o, tl, li = mb.flat_to_batched_left_pad(torch.tensor(g[f"fb{c}_emb"]), torch.tensor(g[f"fb{c}_seq"]),
+                                                torch.tensor(g[f"fb{c}_pidx"]), B, S, steps.tolist())
+        assert torch.equal(o, torch.tensor(g[f"fb{c}_out"]))
+        assert tl == g[f"fb{c}_tl"].tolist()
+        assert torch.equal(li, torch.tensor(g[f"fb{c}_local"]))
+
+
+def test_page_table_allocate_release_share():
+    pt = PageTable(batch_size=3, num_pages=8, page_size=64, max_pages=1)
+    add = pt.pages_needed(np.array([1, 130, 0]))
+    assert add.tolist() == [1, 3, 0]
+    pt.allocate(add)
+    assert pt.free_pages == 4 and pt.max_pages >= 3
+    used = set(pt.table[0, :1].tolist()) | set(pt.table[1, :3].tolist())
+    assert len(used) == 4 and all(0 <= p < 8 for p in used)
+    # slots land in the right pages
+    s = pt.slots(np.array([1, 1]), np.array([0, 129]))
+    assert s[0] == pt.table[1, 0] * 64 and s[1] == pt.table[1, 2] * 64 + 1
+    # copy-free sharing keeps pages alive until every holder lets go
+    pt.share(2, 1, 2)
+    assert (pt.table[2, :2] == pt.table[1, :2]).all() and pt.free_pages == 4
+    pt.release_rows([1])
+    assert pt.free_pages == 5  # only the unshared third page came back
+    pt.release_rows([2, 0])
+    assert pt.free_pages == 8
+    # growth registers new pages
+    pt.grow_pool(12)
+    pt.allocate(np.array([12, 0, 0]) // 1)
+    assert pt.free_pages == 0
+    try:
+        pt.allocate(np.array([1, 0, 0]))
+    except RuntimeError as e:
+        assert "exhausted" in str(e)
+    else:
+        raise AssertionError("allocation beyond the pool must raise")
