@@ -421,9 +421,12 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--envs", type=int, default=ENVS, help="envs per GPU (256 is the benchmark workload; "
+                    "smaller values only for profiling captures)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
+    globals()["ENVS"] = args.envs
     out = run_reference(args) if args.impl == "reference" else run_ours(args)
     if out is not None:
         print(json.dumps(out), flush=True)

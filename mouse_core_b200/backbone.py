@@ -119,14 +119,16 @@ class Qwen3BackboneConfig:
 
 @dataclass
 class LlamaBackboneConfig:
+    # Defaults follow the reference's Llama adapter (llama.py:52-58), which
+    # differ from its Qwen3 adapter's.
     num_layers: int
     num_heads: int
     num_key_value_heads: int | None = None
-    max_position_embeddings: int = 32768
-    expand: int = 3
+    max_position_embeddings: int = 4096
+    expand: int = 4
     intermediate_size: int | None = None
     rope_parameters: dict | None = None
-    rms_norm_eps: float = 1e-6
+    rms_norm_eps: float = 1e-5
     attention_bias: bool = False
 
     def __post_init__(self) -> None:

@@ -4,8 +4,10 @@ the reference by tests/test_oracle_golden.py.
 
 Tolerances: kernels compute in bf16 with fp32 accumulation; attention and
 append outputs must be within 2e-2 max-abs of the float64 oracle on the same
-bf16 inputs; whole-model hidden states within atol 2e-2 + rtol 1e-2 (the bf16
-residual stream itself is rounded to 2^-8 relative)."""
+bf16 inputs. Whole-model hidden states carry the bf16 residual stream
+(rounded to 2^-8 relative at every add), so they must be within atol 2e-2 +
+rtol 1e-2 of the oracle on the golden fixtures and within 2e-2 x the row's
+largest magnitude on the randomised schedules."""
 
 from __future__ import annotations
 
@@ -267,7 +269,9 @@ def test_session_random_schedule_fuzz():
         o = osess.forward(emb.float().numpy(), lens)
         for b, n in enumerate(lens):
             if n:
-                np.testing.assert_allclose(h[b, S - n:], o[b, S - n:], atol=3 * ATOL, rtol=2e-2)
+                # bf16 residual stream: error bound scales with the row's magnitude
+                scale = max(1.0, float(np.abs(o[b, S - n:]).max()))
+                assert np.abs(h[b, S - n:] - o[b, S - n:]).max() <= ATOL * scale, (call, b)
 
 
 def test_session_freed_by_refcount_alone():
