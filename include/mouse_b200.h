@@ -122,6 +122,19 @@ int mb_rmsnorm(const void* x, const void* residual, const void* weight, float ep
                void* norm_out, mb_stream_t stream);
 int mb_silu_mul(const void* gate_up, int rows, int inter, void* out, mb_stream_t stream);
 
+/* ---------------------------------------------------------------------
+ * Segment metadata of a packed stream (K7).
+ * Replaces the position ids of models/backbone/flex_train.py:84-92 (and
+ * models/base.py:1226-1236) and the BlockMask build of flex_train.py:116-125.
+ *   sequence_ids int64 [L] -> position int64 [L] (restarts at 0 where
+ *   sequence_ids[i] != sequence_ids[i-1]), run_start int32 [L],
+ *   tile_lo int32 [ceil(L / tile)] = run_start of each tile's first token,
+ *   flags int32 [1]: flags[0] = 1 if the ids are not sorted (an id may then
+ *   own several runs; the caller reorders tokens so each id is one run).
+ * ------------------------------------------------------------------- */
+int mb_segment_meta(const int64_t* sequence_ids, int L, int tile, int64_t* position, int32_t* run_start,
+                    int32_t* tile_lo, int32_t* flags, mb_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

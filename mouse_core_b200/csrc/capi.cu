@@ -245,4 +245,15 @@ int mb_silu_mul(const void* gate_up, int rows, int inter, void* out, mb_stream_t
   return e == cudaSuccess ? MB_OK : cuda_fail(e, "silu_mul launch");
 }
 
+int mb_segment_meta(const int64_t* sequence_ids, int L, int tile, int64_t* position, int32_t* run_start,
+                    int32_t* tile_lo, int32_t* flags, mb_stream_t stream) {
+  if (L < 0 || tile <= 0) return fail(MB_ERR_INVALID_ARG, "L must be >= 0 and tile > 0");
+  if (L == 0) return MB_OK;
+  if (!sequence_ids || !position || !run_start || !tile_lo || !flags)
+    return fail(MB_ERR_INVALID_ARG, "a required pointer is NULL");
+  cudaError_t e = mb::launch_segment_meta(sequence_ids, L, tile, position, run_start, tile_lo, flags,
+                                          (cudaStream_t)stream);
+  return e == cudaSuccess ? MB_OK : cuda_fail(e, "segment meta launch");
+}
+
 }  // extern "C"

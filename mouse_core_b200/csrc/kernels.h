@@ -72,7 +72,7 @@ cudaError_t launch_rmsnorm(const __nv_bfloat16* x, const __nv_bfloat16* residual
                            cudaStream_t stream);
 cudaError_t launch_silu_mul(const __nv_bfloat16* gate_up, int rows, int I, __nv_bfloat16* out, cudaStream_t stream);
 
-cudaError_t launch_segment_meta(const int64_t* seq, int L, int tile, int64_t* pos_out, int32_t* seg_start,
-                                int32_t* tile_kv_lo, cudaStream_t stream);
+cudaError_t launch_segment_meta(const int64_t* seq, int L, int tile, int64_t* pos_out, int32_t* run_start,
+                                int32_t* tile_lo, int32_t* flags, cudaStream_t stream);
 
 }  // namespace mb

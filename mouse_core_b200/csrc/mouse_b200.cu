@@ -3,4 +3,5 @@
 #include "decode_attention.cu"
 #include "kv_append.cu"
 #include "elementwise.cu"
+#include "segment_meta.cu"
 #include "capi.cu"

@@ -163,6 +163,22 @@ def rmsnorm(x: torch.Tensor, weight: torch.Tensor, eps: float, residual: torch.T
     return (s if s is not None else x), norm
 
 
+def segment_meta(sequence_ids: torch.Tensor, tile: int = 128):
+    """K7: ``(position int64 [L], run_start int32 [L], tile_lo int32 [ceil(L/tile)],
+    unsorted flag int32 [1])`` of a packed stream."""
+    _need(sequence_ids, "sequence_ids", torch.int64)
+    L = sequence_ids.numel()
+    dev = sequence_ids.device
+    pos = torch.empty(L, dtype=torch.int64, device=dev)
+    rs = torch.empty(L, dtype=torch.int32, device=dev)
+    tl = torch.empty((L + tile - 1) // tile, dtype=torch.int32, device=dev)
+    flags = torch.zeros(1, dtype=torch.int32, device=dev)
+    _lib.call("mb_segment_meta", _p(sequence_ids), L, tile, _p(pos), _p(rs), _p(tl), _p(flags),
+              _stream(sequence_ids))
+    _count()
+    return pos, rs, tl, flags
+
+
 def silu_mul(gate_up: torch.Tensor) -> torch.Tensor:
     """``silu(gate) * up`` for ``gate_up [..., 2I]``; returns ``[..., I]``."""
     _need(gate_up, "gate_up", BF16)
