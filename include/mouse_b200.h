@@ -80,6 +80,29 @@ int mb_decode_attention(const void* q, const void* k_pool, const void* v_pool, i
                         int max_kv_len, int plan_ready, void* out, void* workspace, size_t workspace_bytes,
                         mb_stream_t stream);
 
+/* Scratch size built into the library for mb_decode_attention_noalloc. */
+#define MB_NOALLOC_SCRATCH_BYTES (32u * 1024u * 1024u)
+
+/* The same attention as mb_decode_attention, for callers that cannot
+ * allocate device memory and so cannot pass a workspace: for example an FFI
+ * caller (ctypes, cgo, JNI) that only holds the pointers its framework gave
+ * it, or a process whose device memory belongs to another framework's
+ * allocator. It has no counterpart in the reference (the reference is Python
+ * and its FlexAttention call allocates through torch).
+ * Its scratch is an array of MB_NOALLOC_SCRATCH_BYTES compiled into the
+ * library, held by every GPU that loads it until the process exits; a shape
+ * whose workspace (mb_decode_workspace_bytes) exceeds that is rejected with
+ * MB_ERR_WORKSPACE. It calls no allocator. The first call on a device looks
+ * up the array's device address (cudaGetSymbolAddress) with that device
+ * current; make it before capturing any stream. Every call shares the one
+ * array and rebuilds its work list and merge counters from scratch, so calls
+ * that overlap on the GPU (several streams or host threads at once) race and
+ * must be serialised by the caller. */
+int mb_decode_attention_noalloc(const void* q, const void* k_pool, const void* v_pool, int num_pages,
+                                const int32_t* block_table, int max_pages, const int32_t* q_pos,
+                                const int32_t* kv_len, int batch, int q_len, int q_heads, int kv_heads, int head_dim,
+                                int page_size, float scale, int max_kv_len, void* out, mb_stream_t stream);
+
 /* ---------------------------------------------------------------------
  * Fused q/k RMSNorm + RoPE + paged K/V append (K2).
  * Replaces models/backbone/flex_decode.py:212-224 (q/k projections' norm,

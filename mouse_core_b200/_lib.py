@@ -23,6 +23,8 @@ PROTOTYPES = {
     "mb_decode_plan": (_c_int, [_vp, _c_int, _c_int, _c_int, _c_int, _c_int, _vp, _c_size, _vp]),
     "mb_decode_attention": (_c_int, [_vp, _vp, _vp, _c_int, _vp, _c_int, _vp, _vp, _c_int, _c_int, _c_int,
                                      _c_int, _c_int, _c_int, _c_float, _c_int, _c_int, _vp, _vp, _c_size, _vp]),
+    "mb_decode_attention_noalloc": (_c_int, [_vp, _vp, _vp, _c_int, _vp, _c_int, _vp, _vp, _c_int, _c_int,
+                                             _c_int, _c_int, _c_int, _c_int, _c_float, _c_int, _vp, _vp]),
     "mb_kv_append": (_c_int, [_vp, _c_int, _c_int, _vp, _vp, _vp, _vp, _c_float, _vp, _c_float, _c_int, _c_int,
                               _c_int, _c_int, _c_ll, _vp, _vp, _vp, _vp, _vp, _vp]),
     "mb_page_copy": (_c_int, [_vp, _vp, _vp, _vp, _c_int, _c_ll, _vp]),

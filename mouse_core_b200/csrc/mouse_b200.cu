@@ -5,3 +5,4 @@
 #include "elementwise.cu"
 #include "segment_meta.cu"
 #include "capi.cu"
+#include "decode_noalloc.cu"
