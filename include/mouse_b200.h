@@ -146,6 +146,21 @@ int mb_rmsnorm(const void* x, const void* residual, const void* weight, float ep
 int mb_silu_mul(const void* gate_up, int rows, int inter, void* out, mb_stream_t stream);
 
 /* ---------------------------------------------------------------------
+ * Packed varlen segment-causal attention forward (K5, tcgen05).
+ * Replaces models/backbone/flex_train.py:147 (flex_attention with the mask of
+ * flex_train.py:98-102, built at :116-125): out[i, h] = softmax over keys j
+ * with run_start[i] <= j <= i of scale * q[i, h] . k[j, h / G], times v.
+ *   q [L, q_heads, hd], k/v [L, kv_heads, hd] bf16 (16-byte aligned);
+ *   run_start int32 [L] and tile_lo int32 [ceil(L / 128)] from
+ *   mb_segment_meta(tile = 128) on ids that are sorted;
+ *   out [L, q_heads, hd] bf16; lse f32 [q_heads, L] = log2 of the softmax
+ *   denominator of the log2-scaled scores (saved for the backward).
+ * ------------------------------------------------------------------- */
+int mb_varlen_attention_fwd(const void* q, const void* k, const void* v, int L, int q_heads, int kv_heads,
+                            int head_dim, const int32_t* run_start, const int32_t* tile_lo, float scale, void* out,
+                            float* lse, mb_stream_t stream);
+
+/* ---------------------------------------------------------------------
  * Segment metadata of a packed stream (K7).
  * Replaces the position ids of models/backbone/flex_train.py:84-92 (and
  * models/base.py:1226-1236) and the BlockMask build of flex_train.py:116-125.

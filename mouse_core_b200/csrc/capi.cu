@@ -53,6 +53,22 @@ int encode_pool_map(CUtensorMap* map, const void* pool, long long rows, int head
   return MB_OK;
 }
 
+// 3-D view {head_dim, heads, tokens} of a token-major [L, heads, head_dim]
+// tensor: 64-element x 1-head x 128-token boxes, 128B swizzle.
+int encode_token_map(CUtensorMap* map, const void* base, int L, int heads, int head_dim) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return fail(MB_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
+  cuuint64_t dims[3] = {(cuuint64_t)head_dim, (cuuint64_t)heads, (cuuint64_t)L};
+  cuuint64_t strides[2] = {(cuuint64_t)head_dim * 2, (cuuint64_t)heads * head_dim * 2};
+  cuuint32_t box[3] = {64, 1, 128};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(MB_ERR_CUDA, "cuTensorMapEncodeTiled failed (" + std::to_string((int)r) + ")");
+  return MB_OK;
+}
+
 int check_decode_shape(int batch, int q_len, int q_heads, int kv_heads, int head_dim, int page_size) {
   if (batch < 0 || q_len < 0 || q_heads <= 0 || kv_heads <= 0)
     return fail(MB_ERR_INVALID_ARG, "batch/q_len must be >= 0 and head counts > 0");
@@ -243,6 +259,38 @@ int mb_silu_mul(const void* gate_up, int rows, int inter, void* out, mb_stream_t
   cudaError_t e = mb::launch_silu_mul(static_cast<const __nv_bfloat16*>(gate_up), rows, inter,
                                       static_cast<__nv_bfloat16*>(out), (cudaStream_t)stream);
   return e == cudaSuccess ? MB_OK : cuda_fail(e, "silu_mul launch");
+}
+
+int mb_varlen_attention_fwd(const void* q, const void* k, const void* v, int L, int q_heads, int kv_heads,
+                            int head_dim, const int32_t* run_start, const int32_t* tile_lo, float scale, void* out,
+                            float* lse, mb_stream_t stream) {
+  if (L < 0 || q_heads <= 0 || kv_heads <= 0) return fail(MB_ERR_INVALID_ARG, "L >= 0 and head counts > 0 required");
+  if (q_heads % kv_heads) return fail(MB_ERR_INVALID_ARG, "q_heads must be a multiple of kv_heads");
+  if (head_dim != 64 && head_dim != 128) return fail(MB_ERR_UNSUPPORTED, "head_dim must be 64 or 128");
+  if (L == 0) return MB_OK;
+  if (!q || !k || !v || !run_start || !tile_lo || !out || !lse)
+    return fail(MB_ERR_INVALID_ARG, "a required pointer is NULL");
+  if (!aligned(q, 16) || !aligned(k, 16) || !aligned(v, 16) || !aligned(out, 16))
+    return fail(MB_ERR_INVALID_ARG, "q, k, v and out must be 16-byte aligned");
+  CUtensorMap qm, km, vm;
+  int rc;
+  if ((rc = encode_token_map(&qm, q, L, q_heads, head_dim))) return rc;
+  if ((rc = encode_token_map(&km, k, L, kv_heads, head_dim))) return rc;
+  if ((rc = encode_token_map(&vm, v, L, kv_heads, head_dim))) return rc;
+  mb::VarlenParams p{};
+  p.L = L;
+  p.Hq = q_heads;
+  p.Hkv = kv_heads;
+  p.G = q_heads / kv_heads;
+  p.heads_per_cta = (p.G % 2 == 0) ? 2 : 1;
+  p.head_dim = head_dim;
+  p.run_start = run_start;
+  p.tile_lo = tile_lo;
+  p.scale_log2 = scale * 1.4426950408889634f;
+  p.out = static_cast<__nv_bfloat16*>(out);
+  p.lse = lse;
+  cudaError_t e = mb::launch_varlen_fwd(qm, km, vm, p, (cudaStream_t)stream);
+  return e == cudaSuccess ? MB_OK : cuda_fail(e, "varlen attention forward launch");
 }
 
 int mb_segment_meta(const int64_t* sequence_ids, int L, int tile, int64_t* position, int32_t* run_start,

@@ -72,6 +72,17 @@ cudaError_t launch_rmsnorm(const __nv_bfloat16* x, const __nv_bfloat16* residual
                            cudaStream_t stream);
 cudaError_t launch_silu_mul(const __nv_bfloat16* gate_up, int rows, int I, __nv_bfloat16* out, cudaStream_t stream);
 
+struct VarlenParams {
+  int L, Hq, Hkv, G, heads_per_cta, head_dim;
+  const int32_t* run_start;  // [L]
+  const int32_t* tile_lo;    // [ceil(L / 128)]
+  float scale_log2;
+  __nv_bfloat16* out;        // [L, Hq, HD]
+  float* lse;                // [Hq, L], log2 units
+};
+cudaError_t launch_varlen_fwd(const CUtensorMap& qm, const CUtensorMap& km, const CUtensorMap& vm,
+                              const VarlenParams& p, cudaStream_t stream);
+
 cudaError_t launch_segment_meta(const int64_t* seq, int L, int tile, int64_t* pos_out, int32_t* run_start,
                                 int32_t* tile_lo, int32_t* flags, cudaStream_t stream);
 

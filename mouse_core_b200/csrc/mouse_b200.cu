@@ -4,5 +4,6 @@
 #include "kv_append.cu"
 #include "elementwise.cu"
 #include "segment_meta.cu"
+#include "varlen_attention.cu"
 #include "capi.cu"
 #include "decode_noalloc.cu"

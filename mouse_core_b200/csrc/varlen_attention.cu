@@ -1,0 +1,316 @@
+// K5: packed varlen segment-causal GQA attention forward on tcgen05.
+//
+// Replaces the FlexAttention call of flex_packed_forward
+// (src/mouse_core/models/backbone/flex_train.py:147) with its mask
+// (flex_train.py:98-102): query i attends key j iff j <= i and both lie in the
+// same segment. Segments are runs of sequence_ids; K7 turns them into
+// run_start[i] (the smallest j token i may see) and tile_lo[t] (run_start of
+// query tile t's first token), so the mask is run_start[i] <= j <= i and no
+// BlockMask is needed: a query tile only visits key tiles from
+// tile_lo[t] / 128 to its diagonal.
+//
+// One CTA = one 128-token query tile x one pair of q-heads sharing a kv-head
+// (a single q-head when the GQA group is odd). Warp roles (320 threads):
+//   warp 0      TMA producer: Q once, then K/V tiles through a 2-3 stage ring
+//   warp 1      TMEM allocator; lane 0 issues every tcgen05.mma
+//   warps 2-5   softmax of head 0 (thread = query row = TMEM lane)
+//   warps 6-9   softmax of head 1
+// Tensor memory (512 columns): S_h = Q_h K^T at columns 128h, O_h at 256 + HD h.
+// Softmax reads S, writes P (bf16 pairs) back over the first 64 columns of
+// S_h, and the MMA O_h += P V takes P straight from TMEM. The two heads
+// ping-pong: while one head's softmax runs, the tensor core works on the
+// other head. O is rescaled only when a row maximum grows by more than 2^8
+// (exact: the final normalisation uses the same stale maximum).
+// Outputs: out [L, Hq, HD] bf16 and lse [Hq, L] f32 in log2 units of the
+// scaled scores (log2 sum 2^(s * scale * log2 e)).
+#include "common.cuh"
+#include "kernels.h"
+#include "tcgen05.cuh"
+
+namespace mb {
+
+template <int HD>
+struct FwdTile {
+  static constexpr int BM = 128, BN = 128;
+  static constexpr int NCB = HD / 64;                 // 64-element column blocks
+  static constexpr int BOX = 128 * 128;               // bytes of a 64 x 128-row box
+  static constexpr int QTILE = NCB * BOX;             // one head's Q tile
+  static constexpr int KVTILE = NCB * BOX;            // one K (or V) tile
+  static constexpr int STAGES = HD == 128 ? 2 : 3;
+  static constexpr int RING = 2 * STAGES * KVTILE;
+  static constexpr int SMEM = 1024 + 2 * QTILE + RING + 256;
+  static constexpr uint32_t TMEM_COLS = 512;
+};
+
+struct FwdBarriers {
+  uint64_t q_full;
+  uint64_t k_full[3], v_full[3], kv_empty[3];
+  uint64_t s_full[2], p_full[2];
+  uint64_t o_full;
+  uint32_t tmem_base;
+};
+
+template <int HD>
+__global__ void __launch_bounds__(320, 1) varlen_fwd_kernel(const __grid_constant__ CUtensorMap qmap,
+                                                           const __grid_constant__ CUtensorMap kmap,
+                                                           const __grid_constant__ CUtensorMap vmap,
+                                                           const VarlenParams p) {
+  using C = FwdTile<HD>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* qs = smem;                         // [2][QTILE]
+  uint8_t* ks = smem + 2 * C::QTILE;          // [STAGES][KVTILE]
+  uint8_t* vs = ks + C::STAGES * C::KVTILE;   // [STAGES][KVTILE]
+  FwdBarriers* bars = reinterpret_cast<FwdBarriers*>(vs + C::STAGES * C::KVTILE);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n_qt = (p.L + C::BM - 1) / C::BM;
+  const int qt = n_qt - 1 - (int)blockIdx.x;  // longest-history tiles of a stream first
+  const int q0 = qt * C::BM;
+  const int h0 = blockIdx.y * p.heads_per_cta;
+  const int hpc = p.heads_per_cta;
+  const int kvh = h0 / p.G;
+  const int t_lo = p.tile_lo[qt] / C::BN;
+  const int t_hi = min(q0 + C::BM - 1, p.L - 1) / C::BN;
+  const int n_tiles = t_hi - t_lo + 1;
+
+  if (threadIdx.x == 0) {
+    mbar_init(&bars->q_full, 1);
+    for (int s = 0; s < C::STAGES; ++s) {
+      mbar_init(&bars->k_full[s], 1);
+      mbar_init(&bars->v_full[s], 1);
+      mbar_init(&bars->kv_empty[s], 1);
+    }
+    for (int h = 0; h < 2; ++h) {
+      mbar_init(&bars->s_full[h], 1);
+      mbar_init(&bars->p_full[h], 4);
+    }
+    mbar_init(&bars->o_full, 1);
+    fence_barrier_init();
+  }
+  if (warp == 1) tmem_alloc(&bars->tmem_base, C::TMEM_COLS);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tbase = bars->tmem_base;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      prefetch_tensormap(&qmap);
+      prefetch_tensormap(&kmap);
+      prefetch_tensormap(&vmap);
+      mbar_arrive_expect_tx(&bars->q_full, hpc * C::QTILE);
+      for (int hh = 0; hh < hpc; ++hh)
+        for (int cb = 0; cb < C::NCB; ++cb)
+          tma_load_3d(qs + hh * C::QTILE + cb * C::BOX, &qmap, &bars->q_full, cb * 64, h0 + hh, q0);
+      for (int j = 0; j < n_tiles; ++j) {
+        const int st = j % C::STAGES;
+        if (!mbar_wait(&bars->kv_empty[st], ((j / C::STAGES) & 1) ^ 1, kDevTimeoutEmpty)) break;
+        const int kv0 = (t_lo + j) * C::BN;
+        mbar_arrive_expect_tx(&bars->k_full[st], C::KVTILE);
+        for (int cb = 0; cb < C::NCB; ++cb)
+          tma_load_3d(ks + st * C::KVTILE + cb * C::BOX, &kmap, &bars->k_full[st], cb * 64, kvh, kv0);
+        mbar_arrive_expect_tx(&bars->v_full[st], C::KVTILE);
+        for (int cb = 0; cb < C::NCB; ++cb)
+          tma_load_3d(vs + st * C::KVTILE + cb * C::BOX, &vmap, &bars->v_full[st], cb * 64, kvh, kv0);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issue
+    if (lane == 0) {
+      constexpr uint32_t ID_QK = umma_idesc_bf16(128, 128, 0, 0);
+      constexpr uint32_t ID_PV = umma_idesc_bf16(128, HD, 0, 1);
+      bool ok = mbar_wait(&bars->q_full, 0, kDevTimeoutFull);
+      tc_fence_after();
+      auto issue_qk = [&](int hh, int st) {
+        const uint32_t qa = smem_u32(qs + hh * C::QTILE);
+        const uint32_t kb = smem_u32(ks + st * C::KVTILE);
+#pragma unroll
+        for (int kk = 0; kk < HD / 16; ++kk) {
+          const uint32_t off = (kk >> 2) * C::BOX + (kk & 3) * 32;
+          umma_ss(tbase + 128 * hh, umma_desc_sw128(qa + off, 16, 1024), umma_desc_sw128(kb + off, 16, 1024), ID_QK,
+                  kk > 0);
+        }
+        umma_commit(&bars->s_full[hh]);
+      };
+      if (ok) ok = mbar_wait(&bars->k_full[0], 0, kDevTimeoutFull);
+      if (ok) {
+        tc_fence_after();
+        for (int hh = 0; hh < hpc; ++hh) issue_qk(hh, 0);
+      }
+      for (int j = 0; ok && j < n_tiles; ++j) {
+        const int st = j % C::STAGES;
+        const uint32_t ph = (j / C::STAGES) & 1;
+        if (!mbar_wait(&bars->v_full[st], ph, kDevTimeoutFull)) break;
+        const bool more = j + 1 < n_tiles;
+        const int st1 = (j + 1) % C::STAGES;
+        bool k_next = false;
+        for (int hh = 0; hh < hpc; ++hh) {
+          if (!mbar_wait(&bars->p_full[hh], j & 1, kDevTimeoutFull)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t vb = smem_u32(vs + st * C::KVTILE);
+#pragma unroll
+          for (int kk = 0; kk < C::BN / 16; ++kk)
+            umma_ts(tbase + 256 + HD * hh, tbase + 128 * hh + 8 * kk, umma_desc_sw128(vb + kk * 2048, C::BOX, 1024),
+                    ID_PV, (j > 0 || kk > 0) ? 1u : 0u);
+          if (more) {
+            if (!k_next) {
+              if (!mbar_wait(&bars->k_full[st1], ((j + 1) / C::STAGES) & 1, kDevTimeoutFull)) {
+                ok = false;
+                break;
+              }
+              tc_fence_after();
+              k_next = true;
+            }
+            issue_qk(hh, st1);
+          }
+        }
+        umma_commit(&bars->kv_empty[st]);
+      }
+      umma_commit(&bars->o_full);
+    }
+  } else {
+    // ------------------------------------------------------------ softmax
+    const int hh = (warp - 2) >> 2;
+    const int sub = warp & 3;  // TMEM lane quarter this warp may access
+    const int r = sub * 32 + lane;
+    const int q_tok = q0 + r;
+    const bool row_ok = q_tok < p.L;
+    const int lo = row_ok ? p.run_start[q_tok] : 0x7fffffff;
+    const int hi = q_tok;
+    const uint32_t lane_bits = (uint32_t)(sub * 32) << 16;
+    const uint32_t t_s = tbase + 128 * hh + lane_bits;
+    const uint32_t t_o = tbase + 256 + HD * hh + lane_bits;
+    const bool active = hh < hpc;
+    float m_used = -INFINITY, l = 0.f;
+    bool ok = true;
+    for (int j = 0; active && j < n_tiles; ++j) {
+      const int kv0 = (t_lo + j) * C::BN;
+      if (ok) ok = mbar_wait_warp(&bars->s_full[hh], j & 1, kDevTimeoutFull);
+      tc_fence_after();
+      float alpha = 1.f;
+      bool rescale = false;
+      if (ok) {
+        const bool full = row_ok && kv0 >= lo && kv0 + C::BN - 1 <= hi;
+        float mx = -INFINITY;
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          uint32_t v[32];
+          tmem_ld32(t_s + 32 * c, v);
+          tmem_wait_ld();
+#pragma unroll
+          for (int e = 0; e < 32; ++e) {
+            float x = __uint_as_float(v[e]) * p.scale_log2;
+            if (!full) {
+              const int kv = kv0 + 32 * c + e;
+              if (!row_ok || kv < lo || kv > hi) x = -INFINITY;
+            }
+            mx = fmaxf(mx, x);
+          }
+        }
+        const float m_new = fmaxf(m_used, mx);
+        if (m_new > m_used + 8.f) {
+          rescale = true;
+          alpha = exp2f(m_used - m_new);
+          m_used = m_new;
+        }
+        const float mu = (m_used == -INFINITY) ? 0.f : m_used;
+        float lt = 0.f;
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          uint32_t v[32];
+          tmem_ld32(t_s + 32 * c, v);
+          tmem_wait_ld();
+          uint32_t pk[16];
+#pragma unroll
+          for (int e = 0; e < 32; e += 2) {
+            float x0 = __uint_as_float(v[e]) * p.scale_log2;
+            float x1 = __uint_as_float(v[e + 1]) * p.scale_log2;
+            float p0 = exp2f(x0 - mu), p1 = exp2f(x1 - mu);
+            if (!full) {
+              const int kv = kv0 + 32 * c + e;
+              if (!row_ok || kv < lo || kv > hi) p0 = 0.f;
+              if (!row_ok || kv + 1 < lo || kv + 1 > hi) p1 = 0.f;
+            }
+            lt += p0 + p1;
+            pk[e >> 1] = pack_bf16x2(p0, p1);
+          }
+          tmem_st16(t_s + 16 * c, pk);
+        }
+        l = l * alpha + lt;
+        if (__any_sync(0xffffffffu, rescale && j > 0)) {
+          const float a = (rescale && j > 0) ? alpha : 1.f;
+#pragma unroll
+          for (int c = 0; c < HD / 32; ++c) {
+            uint32_t v[32];
+            tmem_ld32(t_o + 32 * c, v);
+            tmem_wait_ld();
+#pragma unroll
+            for (int e = 0; e < 32; ++e) v[e] = __float_as_uint(__uint_as_float(v[e]) * a);
+            tmem_st32(t_o + 32 * c, v);
+          }
+        }
+        tmem_wait_st();
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bars->p_full[hh]);
+    }
+    if (active) {
+      if (ok) ok = mbar_wait_warp(&bars->o_full, 0, kDevTimeoutFull);
+      tc_fence_after();
+      if (ok) {
+        const int h = h0 + hh;
+        const float inv = (l > 0.f) ? 1.f / l : 0.f;
+        __nv_bfloat16* dst = p.out + ((size_t)q_tok * p.Hq + h) * HD;
+#pragma unroll
+        for (int c = 0; c < HD / 32; ++c) {
+          uint32_t v[32];
+          tmem_ld32(t_o + 32 * c, v);
+          tmem_wait_ld();
+          if (row_ok) {
+            uint4* d4 = reinterpret_cast<uint4*>(dst + 32 * c);
+#pragma unroll
+            for (int q4 = 0; q4 < 4; ++q4) {
+              uint4 w;
+              w.x = pack_bf16x2(__uint_as_float(v[8 * q4 + 0]) * inv, __uint_as_float(v[8 * q4 + 1]) * inv);
+              w.y = pack_bf16x2(__uint_as_float(v[8 * q4 + 2]) * inv, __uint_as_float(v[8 * q4 + 3]) * inv);
+              w.z = pack_bf16x2(__uint_as_float(v[8 * q4 + 4]) * inv, __uint_as_float(v[8 * q4 + 5]) * inv);
+              w.w = pack_bf16x2(__uint_as_float(v[8 * q4 + 6]) * inv, __uint_as_float(v[8 * q4 + 7]) * inv);
+              d4[q4] = w;
+            }
+          }
+        }
+        if (row_ok) p.lse[(size_t)h * p.L + q_tok] = (l > 0.f) ? m_used + log2f(l) : -INFINITY;
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc(tbase, C::TMEM_COLS);
+}
+
+cudaError_t launch_varlen_fwd(const CUtensorMap& qm, const CUtensorMap& km, const CUtensorMap& vm,
+                              const VarlenParams& p, cudaStream_t stream) {
+  const int n_qt = (p.L + 127) / 128;
+  dim3 grid(n_qt, p.Hq / p.heads_per_cta);
+  if (p.head_dim == 128) {
+    const int smem = FwdTile<128>::SMEM;
+    cudaError_t e = cudaFuncSetAttribute(varlen_fwd_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return e;
+    varlen_fwd_kernel<128><<<grid, 320, smem, stream>>>(qm, km, vm, p);
+  } else {
+    const int smem = FwdTile<64>::SMEM;
+    cudaError_t e = cudaFuncSetAttribute(varlen_fwd_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return e;
+    varlen_fwd_kernel<64><<<grid, 320, smem, stream>>>(qm, km, vm, p);
+  }
+  return cudaGetLastError();
+}
+
+}  // namespace mb

@@ -179,6 +179,26 @@ def segment_meta(sequence_ids: torch.Tensor, tile: int = 128):
     return pos, rs, tl, flags
 
 
+def varlen_attention_fwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, run_start: torch.Tensor,
+                        tile_lo: torch.Tensor, scale: float):
+    """K5: segment-causal GQA attention over a packed stream. q ``[L, Hq, hd]``,
+    k/v ``[L, Hkv, hd]`` bf16; returns ``(out [L, Hq, hd], lse [Hq, L] f32, log2 units)``."""
+    for name, t in (("q", q), ("k", k), ("v", v)):
+        _need(t, name, BF16)
+    _need(run_start, "run_start", torch.int32)
+    _need(tile_lo, "tile_lo", torch.int32)
+    L, Hq, hd = q.shape
+    Hkv = k.shape[1]
+    if k.shape != (L, Hkv, hd) or v.shape != k.shape:
+        raise ValueError("k and v must be [L, Hkv, hd] matching q")
+    out = torch.empty_like(q)
+    lse = torch.empty(Hq, L, dtype=torch.float32, device=q.device)
+    _lib.call("mb_varlen_attention_fwd", _p(q), _p(k), _p(v), L, Hq, Hkv, hd, _p(run_start), _p(tile_lo),
+              float(scale), _p(out), _p(lse), _stream(q))
+    _count()
+    return out, lse
+
+
 def silu_mul(gate_up: torch.Tensor) -> torch.Tensor:
     """``silu(gate) * up`` for ``gate_up [..., 2I]``; returns ``[..., I]``."""
     _need(gate_up, "gate_up", BF16)
