@@ -341,12 +341,72 @@ def run_ours(args):
             "clocks": clk,
             "device_status": status,
         }
+    if rank == 0 and not args.no_packed:
+        out["packed_attention"] = packed_attention_metric(dev)
     if rank == 0 and not args.no_cpu_baseline:
         out["cpu_baseline"] = cpu_baseline(args.cpu_seconds)
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
     return out
+
+
+def packed_segments(seed, rows=8, row_len=16384, lo=256, hi=4096):
+    """Segment lengths of the packed-training workload: per row, lengths
+    U[lo, hi] until the row is full, the last one truncated."""
+    rng = np.random.default_rng(seed)
+    segs = []
+    for _ in range(rows):
+        total = 0
+        while total < row_len:
+            s = min(int(rng.integers(lo, hi + 1)), row_len - total)
+            segs.append(s)
+            total += s
+    return segs
+
+
+def packed_attention_metric(device, reps=10, rows=8):
+    """Forward TFLOP/s of the K5 segment-causal attention on the packed
+    training workload's attention shape: 8 rows x 16384 tokens (one stream of
+    131072), segments U[256,4096], 16 q / 8 kv heads, hd 128, bf16. Algorithmic
+    FLOPs = 4 * Hq * hd * sum_s s(s+1)/2 (only unmasked pairs)."""
+    import torch
+
+    from mouse_core_b200 import kernels as K
+
+    segs = packed_segments(0, rows=rows)
+    seq = np.concatenate([np.full(n, i, dtype=np.int64) for i, n in enumerate(segs)])
+    L, Hq, Hkv, hd = seq.shape[0], 16, 8, 128
+    g = torch.Generator(device=device).manual_seed(0)
+    q = torch.randn(L, Hq, hd, generator=g, device=device).bfloat16()
+    k = torch.randn(L, Hkv, hd, generator=g, device=device).bfloat16()
+    v = torch.randn(L, Hkv, hd, generator=g, device=device).bfloat16()
+    _, rs, tl, _ = K.segment_meta(torch.from_numpy(seq).to(device), tile=128)
+    flops = 4 * Hq * hd * sum(s * (s + 1) // 2 for s in segs)
+    for _ in range(3):
+        K.varlen_attention_fwd(q, k, v, rs, tl, hd ** -0.5)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        K.varlen_attention_fwd(q, k, v, rs, tl, hd ** -0.5)
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / reps
+    peaks = {}
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            peaks = json.load(f)
+    except (OSError, ValueError):
+        pass
+    peak = float(peaks.get("bf16_tflops", 1590.0))
+    tf = flops / (ms * 1e-3) / 1e12
+    return {"metric": "packed varlen segment-causal attention forward TFLOP/s",
+            "workload": f"{L} tokens ({rows} x 16384), {len(segs)} segments U[256,4096], 16/8 heads, hd 128, bf16",
+            "value": round(tf, 1), "unit": "TFLOP/s", "ms": round(ms, 4), "algorithmic_flops": flops,
+            "roofline": {"bound": "tensor", "achieved": round(tf, 1), "peak": peak,
+                         "peak_source": "measured" if "bf16_tflops" in peaks else "fallback",
+                         "unit": "TFLOP/s", "frac": round(tf / peak, 4)}}
 
 
 # ---------------------------------------------------------------- CPU arm
@@ -421,13 +481,22 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-packed", action="store_true", help="skip the packed-attention secondary metric")
+    ap.add_argument("--packed-only", action="store_true", help="only time the packed-attention kernels")
+    ap.add_argument("--packed-rows", type=int, default=8, help="16384-token rows in the packed stream")
     ap.add_argument("--envs", type=int, default=ENVS, help="envs per GPU (256 is the benchmark workload; "
                     "smaller values only for profiling captures)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
     globals()["ENVS"] = args.envs
-    out = run_reference(args) if args.impl == "reference" else run_ours(args)
+    if args.packed_only:
+        import torch
+
+        out = packed_attention_metric(torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0"))),
+                                      reps=args.steps, rows=args.packed_rows)
+    else:
+        out = run_reference(args) if args.impl == "reference" else run_ours(args)
     if out is not None:
         print(json.dumps(out), flush=True)
 
