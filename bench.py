@@ -401,7 +401,10 @@ def packed_attention_metric(device, reps=10, rows=8):
         pass
     peak = float(peaks.get("bf16_tflops", 1590.0))
     tf = flops / (ms * 1e-3) / 1e12
-    return {"metric": "packed varlen segment-causal attention forward TFLOP/s",
+    from mouse_core_b200 import _lib
+
+    status = _lib.device_status()
+    return {"device_status": status,"metric": "packed varlen segment-causal attention forward TFLOP/s",
             "workload": f"{L} tokens ({rows} x 16384), {len(segs)} segments U[256,4096], 16/8 heads, hd 128, bf16",
             "value": round(tf, 1), "unit": "TFLOP/s", "ms": round(ms, 4), "algorithmic_flops": flops,
             "roofline": {"bound": "tensor", "achieved": round(tf, 1), "peak": peak,

@@ -114,6 +114,13 @@ __device__ __forceinline__ void tma_load_3d(void* smem_dst, const CUtensorMap* m
       : "memory");
 }
 
+// 2^x on the SFU (ex2.approx: about 2 ulp, flushes denormals; x = -inf gives 0).
+__device__ __forceinline__ float fast_exp2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 // Warp-uniform bounded wait: false (in every lane) if any lane timed out.
 __device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity, int code) {
   const bool ok = mbar_wait(bar, parity, code);

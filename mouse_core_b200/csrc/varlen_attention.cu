@@ -196,46 +196,38 @@ __global__ void __launch_bounds__(320, 1) varlen_fwd_kernel(const __grid_constan
       bool rescale = false;
       if (ok) {
         const bool full = row_ok && kv0 >= lo && kv0 + C::BN - 1 <= hi;
-        float mx = -INFINITY;
+        // One TMEM read of the whole 128-column score row into registers.
+        uint32_t v[128];
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          uint32_t v[32];
-          tmem_ld32(t_s + 32 * c, v);
-          tmem_wait_ld();
+        for (int c = 0; c < 4; ++c) tmem_ld32(t_s + 32 * c, *reinterpret_cast<uint32_t(*)[32]>(v + 32 * c));
+        tmem_wait_ld();
+        if (!full) {
 #pragma unroll
-          for (int e = 0; e < 32; ++e) {
-            float x = __uint_as_float(v[e]) * p.scale_log2;
-            if (!full) {
-              const int kv = kv0 + 32 * c + e;
-              if (!row_ok || kv < lo || kv > hi) x = -INFINITY;
-            }
-            mx = fmaxf(mx, x);
+          for (int e = 0; e < 128; ++e) {
+            const int kv = kv0 + e;
+            if (!row_ok || kv < lo || kv > hi) v[e] = 0xff800000u;  // -inf
           }
         }
-        const float m_new = fmaxf(m_used, mx);
+        float mx = -INFINITY;
+#pragma unroll
+        for (int e = 0; e < 128; ++e) mx = fmaxf(mx, __uint_as_float(v[e]));
+        // The scale is positive, so the max of raw scores gives the max of scaled ones.
+        const float m_tile = mx * p.scale_log2;
+        const float m_new = fmaxf(m_used, m_tile);
         if (m_new > m_used + 8.f) {
           rescale = true;
           alpha = exp2f(m_used - m_new);
           m_used = m_new;
         }
-        const float mu = (m_used == -INFINITY) ? 0.f : m_used;
+        const float neg_mu = (m_used == -INFINITY) ? 0.f : -m_used;
         float lt = 0.f;
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
-          uint32_t v[32];
-          tmem_ld32(t_s + 32 * c, v);
-          tmem_wait_ld();
           uint32_t pk[16];
 #pragma unroll
           for (int e = 0; e < 32; e += 2) {
-            float x0 = __uint_as_float(v[e]) * p.scale_log2;
-            float x1 = __uint_as_float(v[e + 1]) * p.scale_log2;
-            float p0 = exp2f(x0 - mu), p1 = exp2f(x1 - mu);
-            if (!full) {
-              const int kv = kv0 + 32 * c + e;
-              if (!row_ok || kv < lo || kv > hi) p0 = 0.f;
-              if (!row_ok || kv + 1 < lo || kv + 1 > hi) p1 = 0.f;
-            }
+            const float p0 = fast_exp2(fmaf(__uint_as_float(v[32 * c + e]), p.scale_log2, neg_mu));
+            const float p1 = fast_exp2(fmaf(__uint_as_float(v[32 * c + e + 1]), p.scale_log2, neg_mu));
             lt += p0 + p1;
             pk[e >> 1] = pack_bf16x2(p0, p1);
           }
@@ -246,12 +238,12 @@ __global__ void __launch_bounds__(320, 1) varlen_fwd_kernel(const __grid_constan
           const float a = (rescale && j > 0) ? alpha : 1.f;
 #pragma unroll
           for (int c = 0; c < HD / 32; ++c) {
-            uint32_t v[32];
-            tmem_ld32(t_o + 32 * c, v);
+            uint32_t o[32];
+            tmem_ld32(t_o + 32 * c, o);
             tmem_wait_ld();
 #pragma unroll
-            for (int e = 0; e < 32; ++e) v[e] = __float_as_uint(__uint_as_float(v[e]) * a);
-            tmem_st32(t_o + 32 * c, v);
+            for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * a);
+            tmem_st32(t_o + 32 * c, o);
           }
         }
         tmem_wait_st();
