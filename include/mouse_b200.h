@@ -161,17 +161,32 @@ int mb_varlen_attention_fwd(const void* q, const void* k, const void* v, int L, 
                             float* lse, mb_stream_t stream);
 
 /* ---------------------------------------------------------------------
+ * Packed varlen segment-causal attention backward (K6, tcgen05).
+ * The gradient the reference obtains by autograd through flex_attention
+ * (models/backbone/flex_train.py:147): given the forward's q, k, v, out, lse
+ * and the upstream dout [L, q_heads, hd], writes dq [L, q_heads, hd] and
+ * dk, dv [L, kv_heads, hd] (bf16; dk/dv summed over each GQA group).
+ * run_start / run_end come from mb_segment_meta. delta is caller scratch of
+ * q_heads * L floats. Deterministic (no atomics).
+ * ------------------------------------------------------------------- */
+int mb_varlen_attention_bwd(const void* q, const void* k, const void* v, const void* out, const void* dout,
+                            const float* lse, int L, int q_heads, int kv_heads, int head_dim,
+                            const int32_t* run_start, const int32_t* run_end, float scale, void* dq, void* dk,
+                            void* dv, float* delta, mb_stream_t stream);
+
+/* ---------------------------------------------------------------------
  * Segment metadata of a packed stream (K7).
  * Replaces the position ids of models/backbone/flex_train.py:84-92 (and
  * models/base.py:1226-1236) and the BlockMask build of flex_train.py:116-125.
  *   sequence_ids int64 [L] -> position int64 [L] (restarts at 0 where
  *   sequence_ids[i] != sequence_ids[i-1]), run_start int32 [L],
+ *   run_end int32 [L] or NULL (one past the end of i's run),
  *   tile_lo int32 [ceil(L / tile)] = run_start of each tile's first token,
  *   flags int32 [1]: flags[0] = 1 if the ids are not sorted (an id may then
  *   own several runs; the caller reorders tokens so each id is one run).
  * ------------------------------------------------------------------- */
 int mb_segment_meta(const int64_t* sequence_ids, int L, int tile, int64_t* position, int32_t* run_start,
-                    int32_t* tile_lo, int32_t* flags, mb_stream_t stream);
+                    int32_t* run_end, int32_t* tile_lo, int32_t* flags, mb_stream_t stream);
 
 #ifdef __cplusplus
 }

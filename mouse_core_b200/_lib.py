@@ -32,7 +32,9 @@ PROTOTYPES = {
     "mb_silu_mul": (_c_int, [_vp, _c_int, _c_int, _vp, _vp]),
     "mb_varlen_attention_fwd": (_c_int, [_vp, _vp, _vp, _c_int, _c_int, _c_int, _c_int, _vp, _vp, _c_float, _vp,
                                          _vp, _vp]),
-    "mb_segment_meta": (_c_int, [_vp, _c_int, _c_int, _vp, _vp, _vp, _vp, _vp]),
+    "mb_varlen_attention_bwd": (_c_int, [_vp, _vp, _vp, _vp, _vp, _vp, _c_int, _c_int, _c_int, _c_int, _vp, _vp,
+                                         _c_float, _vp, _vp, _vp, _vp, _vp]),
+    "mb_segment_meta": (_c_int, [_vp, _c_int, _c_int, _vp, _vp, _vp, _vp, _vp, _vp]),
 }
 
 _LIB = None

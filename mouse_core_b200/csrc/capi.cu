@@ -293,13 +293,52 @@ int mb_varlen_attention_fwd(const void* q, const void* k, const void* v, int L, 
   return e == cudaSuccess ? MB_OK : cuda_fail(e, "varlen attention forward launch");
 }
 
+int mb_varlen_attention_bwd(const void* q, const void* k, const void* v, const void* out, const void* dout,
+                            const float* lse, int L, int q_heads, int kv_heads, int head_dim,
+                            const int32_t* run_start, const int32_t* run_end, float scale, void* dq, void* dk,
+                            void* dv, float* delta, mb_stream_t stream) {
+  if (L < 0 || q_heads <= 0 || kv_heads <= 0) return fail(MB_ERR_INVALID_ARG, "L >= 0 and head counts > 0 required");
+  if (q_heads % kv_heads) return fail(MB_ERR_INVALID_ARG, "q_heads must be a multiple of kv_heads");
+  if (head_dim != 64 && head_dim != 128) return fail(MB_ERR_UNSUPPORTED, "head_dim must be 64 or 128");
+  if (L == 0) return MB_OK;
+  if (!q || !k || !v || !out || !dout || !lse || !run_start || !run_end || !dq || !dk || !dv || !delta)
+    return fail(MB_ERR_INVALID_ARG, "a required pointer is NULL");
+  if (!aligned(q, 16) || !aligned(k, 16) || !aligned(v, 16) || !aligned(dout, 16) || !aligned(dq, 16) ||
+      !aligned(dk, 16) || !aligned(dv, 16) || !aligned(out, 4))
+    return fail(MB_ERR_INVALID_ARG, "q, k, v, dout, dq, dk, dv must be 16-byte aligned");
+  CUtensorMap qm, km, vm, dm;
+  int rc;
+  if ((rc = encode_token_map(&qm, q, L, q_heads, head_dim))) return rc;
+  if ((rc = encode_token_map(&km, k, L, kv_heads, head_dim))) return rc;
+  if ((rc = encode_token_map(&vm, v, L, kv_heads, head_dim))) return rc;
+  if ((rc = encode_token_map(&dm, dout, L, q_heads, head_dim))) return rc;
+  mb::VarlenBwdParams p{};
+  p.L = L;
+  p.Hq = q_heads;
+  p.Hkv = kv_heads;
+  p.G = q_heads / kv_heads;
+  p.head_dim = head_dim;
+  p.run_start = run_start;
+  p.run_end = run_end;
+  p.lse = lse;
+  p.delta = delta;
+  p.scale = scale;
+  p.scale_log2 = scale * 1.4426950408889634f;
+  p.dq = static_cast<__nv_bfloat16*>(dq);
+  p.dk = static_cast<__nv_bfloat16*>(dk);
+  p.dv = static_cast<__nv_bfloat16*>(dv);
+  cudaError_t e = mb::launch_varlen_bwd(qm, km, vm, dm, static_cast<const __nv_bfloat16*>(out),
+                                        static_cast<const __nv_bfloat16*>(dout), p, (cudaStream_t)stream);
+  return e == cudaSuccess ? MB_OK : cuda_fail(e, "varlen attention backward launch");
+}
+
 int mb_segment_meta(const int64_t* sequence_ids, int L, int tile, int64_t* position, int32_t* run_start,
-                    int32_t* tile_lo, int32_t* flags, mb_stream_t stream) {
+                    int32_t* run_end, int32_t* tile_lo, int32_t* flags, mb_stream_t stream) {
   if (L < 0 || tile <= 0) return fail(MB_ERR_INVALID_ARG, "L must be >= 0 and tile > 0");
   if (L == 0) return MB_OK;
   if (!sequence_ids || !position || !run_start || !tile_lo || !flags)
     return fail(MB_ERR_INVALID_ARG, "a required pointer is NULL");
-  cudaError_t e = mb::launch_segment_meta(sequence_ids, L, tile, position, run_start, tile_lo, flags,
+  cudaError_t e = mb::launch_segment_meta(sequence_ids, L, tile, position, run_start, run_end, tile_lo, flags,
                                           (cudaStream_t)stream);
   return e == cudaSuccess ? MB_OK : cuda_fail(e, "segment meta launch");
 }

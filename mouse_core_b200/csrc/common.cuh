@@ -127,6 +127,10 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   return *reinterpret_cast<uint32_t*>(&v);
 }
 
+__device__ __forceinline__ float2 unpack_bf16x2(uint32_t v) {
+  return __bfloat1622float2(*reinterpret_cast<__nv_bfloat162*>(&v));
+}
+
 // Byte offset of 16-byte chunk `chunk` (0..7) of row `row` inside a TMA box
 // written with CU_TENSOR_MAP_SWIZZLE_128B (128-byte rows, 1024-byte aligned).
 __device__ __forceinline__ uint32_t swz128(uint32_t row, uint32_t chunk) {

@@ -83,7 +83,22 @@ struct VarlenParams {
 cudaError_t launch_varlen_fwd(const CUtensorMap& qm, const CUtensorMap& km, const CUtensorMap& vm,
                               const VarlenParams& p, cudaStream_t stream);
 
+struct VarlenBwdParams {
+  int L, Hq, Hkv, G, head_dim;
+  const int32_t* run_start;  // [L]
+  const int32_t* run_end;    // [L]
+  const float* lse;          // [Hq, L] log2 units (from the forward)
+  float* delta;              // [Hq, L] scratch: rowsum(dO * O)
+  float scale, scale_log2;
+  __nv_bfloat16* dq;         // [L, Hq, HD]
+  __nv_bfloat16* dk;         // [L, Hkv, HD]
+  __nv_bfloat16* dv;         // [L, Hkv, HD]
+};
+cudaError_t launch_varlen_bwd(const CUtensorMap& qm, const CUtensorMap& km, const CUtensorMap& vm,
+                              const CUtensorMap& dom, const __nv_bfloat16* out, const __nv_bfloat16* dout,
+                              VarlenBwdParams p, cudaStream_t stream);
+
 cudaError_t launch_segment_meta(const int64_t* seq, int L, int tile, int64_t* pos_out, int32_t* run_start,
-                                int32_t* tile_lo, int32_t* flags, cudaStream_t stream);
+                                int32_t* run_end, int32_t* tile_lo, int32_t* flags, cudaStream_t stream);
 
 }  // namespace mb

@@ -5,5 +5,6 @@
 #include "elementwise.cu"
 #include "segment_meta.cu"
 #include "varlen_attention.cu"
+#include "varlen_backward.cu"
 #include "capi.cu"
 #include "decode_noalloc.cu"

@@ -121,6 +121,18 @@ __device__ __forceinline__ float fast_exp2(float x) {
   return y;
 }
 
+// Warpgroup register re-balancing (all four warps of a warpgroup execute it).
+// The block's register budget is fixed at launch; a kernel's decreases and
+// increases must sum to no more than that budget.
+template <uint32_t N>
+__device__ __forceinline__ void regs_dec() {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
+}
+template <uint32_t N>
+__device__ __forceinline__ void regs_inc() {
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
+}
+
 // Warp-uniform bounded wait: false (in every lane) if any lane timed out.
 __device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity, int code) {
   const bool ok = mbar_wait(bar, parity, code);

@@ -284,7 +284,10 @@ __global__ void __launch_bounds__(320, 1) varlen_fwd_kernel(const __grid_constan
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  if (warp == 1) tmem_dealloc(tbase, C::TMEM_COLS);
+  if (warp == 1) {
+    __syncwarp();
+    tmem_dealloc(tbase, C::TMEM_COLS);
+  }
 }
 
 cudaError_t launch_varlen_fwd(const CUtensorMap& qm, const CUtensorMap& km, const CUtensorMap& vm,

@@ -163,9 +163,10 @@ def rmsnorm(x: torch.Tensor, weight: torch.Tensor, eps: float, residual: torch.T
     return (s if s is not None else x), norm
 
 
-def segment_meta(sequence_ids: torch.Tensor, tile: int = 128):
+def segment_meta(sequence_ids: torch.Tensor, tile: int = 128, with_run_end: bool = False):
     """K7: ``(position int64 [L], run_start int32 [L], tile_lo int32 [ceil(L/tile)],
-    unsorted flag int32 [1])`` of a packed stream."""
+    unsorted flag int32 [1])`` of a packed stream, plus ``run_end int32 [L]``
+    (one past the end of each token's run) last when ``with_run_end``."""
     _need(sequence_ids, "sequence_ids", torch.int64)
     L = sequence_ids.numel()
     dev = sequence_ids.device
@@ -173,9 +174,12 @@ def segment_meta(sequence_ids: torch.Tensor, tile: int = 128):
     rs = torch.empty(L, dtype=torch.int32, device=dev)
     tl = torch.empty((L + tile - 1) // tile, dtype=torch.int32, device=dev)
     flags = torch.zeros(1, dtype=torch.int32, device=dev)
-    _lib.call("mb_segment_meta", _p(sequence_ids), L, tile, _p(pos), _p(rs), _p(tl), _p(flags),
+    re = torch.empty(L, dtype=torch.int32, device=dev) if with_run_end else None
+    _lib.call("mb_segment_meta", _p(sequence_ids), L, tile, _p(pos), _p(rs), _p(re), _p(tl), _p(flags),
               _stream(sequence_ids))
     _count()
+    if with_run_end:
+        return pos, rs, tl, flags, re
     return pos, rs, tl, flags
 
 
@@ -197,6 +201,25 @@ def varlen_attention_fwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, run_
               float(scale), _p(out), _p(lse), _stream(q))
     _count()
     return out, lse
+
+
+def varlen_attention_bwd(q, k, v, out, dout, lse, run_start, run_end, scale):
+    """K6: ``(dq, dk, dv)`` of ``varlen_attention_fwd`` for upstream ``dout``."""
+    for name, t in (("q", q), ("k", k), ("v", v), ("out", out), ("dout", dout)):
+        _need(t, name, BF16)
+    _need(lse, "lse", torch.float32)
+    _need(run_start, "run_start", torch.int32)
+    _need(run_end, "run_end", torch.int32)
+    L, Hq, hd = q.shape
+    Hkv = k.shape[1]
+    dq = torch.empty_like(q)
+    dk = torch.empty_like(k)
+    dv = torch.empty_like(v)
+    delta = torch.empty(Hq, L, dtype=torch.float32, device=q.device)
+    _lib.call("mb_varlen_attention_bwd", _p(q), _p(k), _p(v), _p(out), _p(dout), _p(lse), L, Hq, Hkv, hd,
+              _p(run_start), _p(run_end), float(scale), _p(dq), _p(dk), _p(dv), _p(delta), _stream(q))
+    _count(3)
+    return dq, dk, dv
 
 
 def silu_mul(gate_up: torch.Tensor) -> torch.Tensor:

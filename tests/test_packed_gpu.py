@@ -50,9 +50,19 @@ def test_segment_meta_bit_exact(case):
         seq = np.zeros(9000, dtype=np.int64)
     else:
         seq = np.array([7], dtype=np.int64)
-    pos, rs, tl, flags = K.segment_meta(torch.from_numpy(seq).to(dev), tile=128)
+    pos, rs, tl, flags, re = K.segment_meta(torch.from_numpy(seq).to(dev), tile=128, with_run_end=True)
     torch.cuda.synchronize()
     ref = opol.position_ids(seq)
+    L = seq.shape[0]
+    boundary = np.ones(L + 1, dtype=bool)
+    boundary[1:L] = seq[1:] != seq[:-1]
+    nxt = np.empty(L, dtype=np.int64)
+    cur = L
+    for i in range(L - 1, -1, -1):
+        nxt[i] = cur
+        if boundary[i]:
+            cur = i
+    assert np.array_equal(re.cpu().numpy(), nxt)
     assert np.array_equal(pos.cpu().numpy(), ref)
     assert np.array_equal(rs.cpu().numpy(), np.arange(seq.shape[0]) - ref)
     assert np.array_equal(tl.cpu().numpy(), (np.arange(seq.shape[0]) - ref)[::128])
@@ -111,3 +121,57 @@ def test_varlen_fwd_packed_2048_against_reference_samples():
     flat = out.reshape(-1)
     err = np.abs(flat[g["out_idx"]] - g["out_val"]).max()
     assert err < ATOL, f"max abs err vs reference samples {err}"
+
+
+def _run_bwd(seq, q, k, v, do, dev):
+    from mouse_core_b200 import kernels as K
+
+    st = torch.from_numpy(seq).to(dev)
+    _, rs, tl, flags, re = K.segment_meta(st, tile=128, with_run_end=True)
+    qd, kd, vd, dod = q.to(dev), k.to(dev), v.to(dev), do.to(dev)
+    scale = q.shape[-1] ** -0.5
+    out, lse = K.varlen_attention_fwd(qd, kd, vd, rs, tl, scale)
+    dq, dk, dv = K.varlen_attention_bwd(qd, kd, vd, out, dod, lse, rs, re, scale)
+    torch.cuda.synchronize()
+    return [t.float().cpu().numpy() for t in (dq, dk, dv)]
+
+
+BWD_CASES = FWD_CASES + [("g2_hd128_many", 4, 2, 128, [5, 300, 1, 1, 1, 64, 129, 600])]
+
+
+@pytest.mark.parametrize("name,Hq,Hkv,hd,lens", BWD_CASES)
+def test_varlen_bwd_matches_oracle(name, Hq, Hkv, hd, lens):
+    """dq, dk, dv (bf16, fp32 accumulation) vs the float64 analytic gradient on
+    the same bf16 inputs: max-abs error within 2e-2 of each gradient's scale
+    (its largest magnitude, at least 1)."""
+    dev = _dev()
+    seq = _seq_from_lengths(lens)
+    L = seq.shape[0]
+    q, k, v, do = cfg1_inputs(13, L, Hq, Hkv, hd)
+    q, k, v, do = q.bfloat16(), k.bfloat16(), v.bfloat16(), do.bfloat16()
+    got = _run_bwd(seq, q, k, v, do, dev)
+    ref = oatt.packed_attention_bwd(q.float().numpy(), k.float().numpy(), v.float().numpy(), seq, hd ** -0.5,
+                                    do.float().numpy())
+    for gname, g, r in zip(("dq", "dk", "dv"), got, ref):
+        assert np.isfinite(g).all(), gname
+        scale = max(1.0, float(np.abs(r).max()))
+        err = np.abs(g - r).max()
+        assert err <= ATOL * scale, f"{name} {gname}: max abs err {err} (scale {scale})"
+    from mouse_core_b200 import _lib
+
+    assert _lib.device_status() == 0
+
+
+def test_varlen_bwd_packed_2048_against_reference_samples():
+    """Gradients of the 2048-token packed workload vs the reference's fp32
+    SDPA-mask autograd (sampled entries)."""
+    dev = _dev()
+    g = load("packed_attn_cfg1.npz")
+    seq = _seq_from_lengths(cfg1_segments(0))
+    q, k, v, do = cfg1_inputs(0, 2048, 4, 2, 64)
+    got = _run_bwd(seq, q.bfloat16(), k.bfloat16(), v.bfloat16(), do.bfloat16(), dev)
+    for gname, arr in zip(("dq", "dk", "dv"), got):
+        ref = g[f"{gname}_val"]
+        scale = max(1.0, float(np.abs(ref).max()))
+        err = np.abs(arr.reshape(-1)[g[f"{gname}_idx"]] - ref).max()
+        assert err <= ATOL * scale, f"{gname}: max abs err vs reference samples {err}"
