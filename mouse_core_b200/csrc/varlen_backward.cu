@@ -85,13 +85,17 @@ __device__ __forceinline__ void init_bwd_bars(BwdBars* b, int ring_full_count) {
   fence_barrier_init();
 }
 
-// A += sum over 8 K-steps; A K-major in smem (rows x HD), B K-major in smem.
+// D = A B^T over HD; A and B K-major in smem (128 rows x HD). The start
+// address is the descriptor's low field, so K-steps add (offset >> 4) to the
+// 64-bit descriptor (shared-memory addresses stay below 2^18, no carry).
+// Issue loops stay rolled to keep the issuing warp's registers few.
 template <int HD>
 __device__ __forceinline__ void mma_kmajor_ss(uint32_t d, uint32_t a_base, uint32_t b_base, uint32_t idesc) {
-#pragma unroll
+  const uint64_t da = umma_desc_sw128(a_base, 16, 1024), db = umma_desc_sw128(b_base, 16, 1024);
+#pragma unroll 1
   for (int kk = 0; kk < HD / 16; ++kk) {
-    const uint32_t off = (kk >> 2) * BwdTile<HD>::BOX + (kk & 3) * 32;
-    umma_ss(d, umma_desc_sw128(a_base + off, 16, 1024), umma_desc_sw128(b_base + off, 16, 1024), idesc, kk > 0);
+    const uint32_t off = ((kk >> 2) * BwdTile<HD>::BOX + (kk & 3) * 32) >> 4;
+    umma_ss(d, da + off, db + off, idesc, kk > 0);
   }
 }
 
@@ -99,10 +103,10 @@ __device__ __forceinline__ void mma_kmajor_ss(uint32_t d, uint32_t a_base, uint3
 template <int HD>
 __device__ __forceinline__ void mma_tmem_a(uint32_t d, uint32_t a_tmem, uint32_t b_base, uint32_t idesc,
                                            bool accumulate) {
-#pragma unroll
+  const uint64_t db = umma_desc_sw128(b_base, BwdTile<HD>::BOX, 1024);
+#pragma unroll 1
   for (int kk = 0; kk < 8; ++kk)
-    umma_ts(d, a_tmem + 8 * kk, umma_desc_sw128(b_base + kk * 2048, BwdTile<HD>::BOX, 1024), idesc,
-            (accumulate || kk > 0) ? 1u : 0u);
+    umma_ts(d, a_tmem + 8 * kk, db + (uint64_t)((kk * 2048) >> 4), idesc, (accumulate || kk > 0) ? 1u : 0u);
 }
 
 // ---------------------------------------------------------------- dq kernel
@@ -211,32 +215,37 @@ __global__ void __launch_bounds__(320, 1) varlen_bwd_dq_kernel(const __grid_cons
     const float dlt = row_ok ? p.delta[(size_t)h * p.L + q_tok] : 0.f;
     const uint32_t lane_bits = (uint32_t)(sub * 32) << 16;
     const uint32_t t_x = tbase + 128 * grp + lane_bits;
+    const uint32_t t_p = tbase + 384 + 64 * grp + lane_bits;
     bool ok = true;
     for (int j = grp; j < n; j += 2) {
       const int kv0 = (t_lo + j) * 128;
       const uint32_t par = (j >> 1) & 1;
       if (ok) ok = mbar_wait_warp(&bars->s_full[grp], par, kDevTimeoutFull);
       tc_fence_after();
-      uint32_t pr[64];  // P as bf16 pairs, kept across the dP MMA
       if (ok) {
         const bool full = row_ok && kv0 >= lo && kv0 + 127 <= q_tok;
+        uint32_t v[128];
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          uint32_t v[32];
-          tmem_ld32(t_x + 32 * c, v);
-          tmem_wait_ld();
+        for (int c = 0; c < 4; ++c) tmem_ld32(t_x + 32 * c, *reinterpret_cast<uint32_t(*)[32]>(v + 32 * c));
+        tmem_wait_ld();
 #pragma unroll
-          for (int e = 0; e < 32; e += 2) {
-            float x0 = fast_exp2(fmaf(__uint_as_float(v[e]), p.scale_log2, neg_lse));
-            float x1 = fast_exp2(fmaf(__uint_as_float(v[e + 1]), p.scale_log2, neg_lse));
+        for (int c = 0; c < 8; ++c) {
+          uint32_t pk[8];
+#pragma unroll
+          for (int e = 0; e < 16; e += 2) {
+            const int col = 16 * c + e;
+            float x0 = fast_exp2(fmaf(__uint_as_float(v[col]), p.scale_log2, neg_lse));
+            float x1 = fast_exp2(fmaf(__uint_as_float(v[col + 1]), p.scale_log2, neg_lse));
             if (!full) {
-              const int kv = kv0 + 32 * c + e;
+              const int kv = kv0 + col;
               if (!row_ok || kv < lo || kv > q_tok) x0 = 0.f;
               if (!row_ok || kv + 1 < lo || kv + 1 > q_tok) x1 = 0.f;
             }
-            pr[16 * c + (e >> 1)] = pack_bf16x2(x0, x1);
+            pk[e >> 1] = pack_bf16x2(x0, x1);
           }
+          tmem_st8(t_p + 8 * c, pk);  // P parked in spare TMEM across the dP MMA
         }
+        tmem_wait_st();
       }
       tc_fence_before();
       __syncwarp();
@@ -245,19 +254,24 @@ __global__ void __launch_bounds__(320, 1) varlen_bwd_dq_kernel(const __grid_cons
       tc_fence_after();
       if (ok) {
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          uint32_t v[32];
-          tmem_ld32(t_x + 32 * c, v);
+        for (int hf = 0; hf < 2; ++hf) {
+          uint32_t v[64], pp[32];
+          tmem_ld32(t_x + 64 * hf, *reinterpret_cast<uint32_t(*)[32]>(v));
+          tmem_ld32(t_x + 64 * hf + 32, *reinterpret_cast<uint32_t(*)[32]>(v + 32));
+          tmem_ld32(t_p + 32 * hf, pp);
           tmem_wait_ld();
-          uint32_t pk[16];
 #pragma unroll
-          for (int e = 0; e < 32; e += 2) {
-            const float2 pp = unpack_bf16x2(pr[(32 * c + e) >> 1]);
-            const float d0 = pp.x * (__uint_as_float(v[e]) - dlt);
-            const float d1 = pp.y * (__uint_as_float(v[e + 1]) - dlt);
-            pk[e >> 1] = pack_bf16x2(d0, d1);
+          for (int c = 0; c < 4; ++c) {
+            uint32_t pk[8];
+#pragma unroll
+            for (int e = 0; e < 16; e += 2) {
+              const int col = 16 * c + e;
+              const float2 pf = unpack_bf16x2(pp[col >> 1]);
+              pk[e >> 1] = pack_bf16x2(pf.x * (__uint_as_float(v[col]) - dlt),
+                                       pf.y * (__uint_as_float(v[col + 1]) - dlt));
+            }
+            tmem_st8(t_x + 32 * hf + 8 * c, pk);  // dS over dP columns already read
           }
-          tmem_st16(t_x + 16 * c, pk);
         }
         tmem_wait_st();
       }
@@ -434,20 +448,21 @@ __global__ void __launch_bounds__(320, 1) varlen_bwd_dkdv_kernel(const __grid_co
       if (ok) {
         const bool full = k_ok && q0 >= k_tok && q0 + 127 < q_end;
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          uint32_t v[32];
-          tmem_ld32(t_x + 32 * c, v);
+        for (int c = 0; c < 8; ++c) {
+          uint32_t v[16];
+          tmem_ld16(t_x + 16 * c, v);
           tmem_wait_ld();
 #pragma unroll
-          for (int e = 0; e < 32; e += 2) {
-            const int q = q0 + 32 * c + e;
-            float x0 = fast_exp2(fmaf(__uint_as_float(v[e]), p.scale_log2, -lse_s[32 * c + e]));
-            float x1 = fast_exp2(fmaf(__uint_as_float(v[e + 1]), p.scale_log2, -lse_s[32 * c + e + 1]));
+          for (int e = 0; e < 16; e += 2) {
+            const int col = 16 * c + e;
+            float x0 = fast_exp2(fmaf(__uint_as_float(v[e]), p.scale_log2, -lse_s[col]));
+            float x1 = fast_exp2(fmaf(__uint_as_float(v[e + 1]), p.scale_log2, -lse_s[col + 1]));
             if (!full) {
+              const int q = q0 + col;
               if (q < k_tok || q >= q_end) x0 = 0.f;
               if (q + 1 < k_tok || q + 1 >= q_end) x1 = 0.f;
             }
-            pr[16 * c + (e >> 1)] = pack_bf16x2(x0, x1);
+            pr[col >> 1] = pack_bf16x2(x0, x1);
           }
         }
       }
@@ -458,19 +473,19 @@ __global__ void __launch_bounds__(320, 1) varlen_bwd_dkdv_kernel(const __grid_co
       tc_fence_after();
       if (ok) {
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          uint32_t v[32];
-          tmem_ld32(t_x + 32 * c, v);
+        for (int c = 0; c < 8; ++c) {
+          uint32_t v[16];
+          tmem_ld16(t_x + 16 * c, v);
           tmem_wait_ld();
-          uint32_t pk[16];
+          uint32_t pk[8];
 #pragma unroll
-          for (int e = 0; e < 32; e += 2) {
-            const float2 pp = unpack_bf16x2(pr[(32 * c + e) >> 1]);
-            const float d0 = pp.x * (__uint_as_float(v[e]) - lse_s[128 + 32 * c + e]);
-            const float d1 = pp.y * (__uint_as_float(v[e + 1]) - lse_s[128 + 32 * c + e + 1]);
-            pk[e >> 1] = pack_bf16x2(d0, d1);
+          for (int e = 0; e < 16; e += 2) {
+            const int col = 16 * c + e;
+            const float2 pf = unpack_bf16x2(pr[col >> 1]);
+            pk[e >> 1] = pack_bf16x2(pf.x * (__uint_as_float(v[e]) - lse_s[128 + col]),
+                                     pf.y * (__uint_as_float(v[e + 1]) - lse_s[128 + col + 1]));
           }
-          tmem_st16(t_x + 16 * c, pk);  // dS^T over the dP^T columns already read
+          tmem_st8(t_x + 8 * c, pk);  // dS^T over dP^T columns already read
         }
 #pragma unroll
         for (int c = 0; c < 4; ++c) tmem_st16(t_x + 64 + 16 * c, *reinterpret_cast<uint32_t(*)[16]>(pr + 16 * c));
