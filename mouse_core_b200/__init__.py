@@ -4,6 +4,8 @@ Drop-in pieces for ``mouse_core.models``:
 
 * ``PagedDecodeSession`` (alias ``FlexDecodeSession``) — cached batched
   decode over ragged env batches with a paged KV cache.
+* ``flex_packed_forward`` — packed segment-causal training forward whose
+  attention (and its backward) run on tcgen05 kernels.
 * ``Qwen3Backbone`` / ``LlamaBackbone`` / ``IdentityBackbone`` /
   ``Backbone.decode_session`` — adapters whose decode sessions are paged.
 * ``resolve_cache_bounds`` / ``rebuild_starts`` / ``cache_needs_rebuild`` —
@@ -32,6 +34,7 @@ from mouse_core_b200.packing import (
 __all__ = [
     "PagedDecodeSession",
     "FlexDecodeSession",
+    "flex_packed_forward",
     "Backbone",
     "Qwen3Backbone",
     "LlamaBackbone",
@@ -54,6 +57,10 @@ def __getattr__(name):
         from mouse_core_b200 import decode
 
         return getattr(decode, name)
+    if name == "flex_packed_forward":
+        from mouse_core_b200.packed import flex_packed_forward
+
+        return flex_packed_forward
     if name in ("Backbone", "Qwen3Backbone", "LlamaBackbone", "IdentityBackbone"):
         from mouse_core_b200 import backbone
 

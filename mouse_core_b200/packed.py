@@ -1,0 +1,153 @@
+"""Packed segment-causal forward — drop-in for mouse-core's ``flex_packed_forward``.
+
+Reference: ``flex_packed_forward`` (src/mouse_core/models/backbone/
+flex_train.py:51-157). Same keyword signature, same ``ValueError``s, same
+result: a decoder pass over one flat stream ``embeds [L, D]`` where token ``i``
+attends token ``j`` iff ``j <= i`` and ``sequence_ids[i] == sequence_ids[j]``,
+with RoPE positions restarting at every run of ``sequence_ids``; autograd
+reaches ``embeds`` and every weight.
+
+B200 machinery instead of the reference's BlockMask + compiled
+FlexAttention:
+
+* K7 (``mb_segment_meta``) computes the position ids (bit-exact with the
+  reference's cummax formula), each token's run start/end and each 128-token
+  query tile's first visible key, in one pass; no ``[L, L]`` mask exists.
+* The attention core is the tcgen05 kernel pair K5 (forward, saves the log2
+  softmax denominator) / K6 (backward: deterministic dK/dV and dQ kernels)
+  behind ``torch.autograd.Function``.
+* Projections, RMSNorms, RoPE and the MLP run through the model's own
+  transformers modules (cuBLAS GEMMs, torch autograd).
+
+Ids that are not sorted (one id owning several runs) are made contiguous by a
+stable sort before the attention call and scattered back after it, which
+keeps the reference's id-equality mask; positions still restart per run.
+"""
+
+from __future__ import annotations
+
+from typing import Any, cast
+
+import torch
+
+from mouse_core_b200 import kernels as K
+
+
+class _SegmentAttention(torch.autograd.Function):
+    """out = segment-causal GQA attention of ``q [L,Hq,hd]`` over ``k, v [L,Hkv,hd]``."""
+
+    @staticmethod
+    def forward(ctx, q, k, v, run_start, run_end, tile_lo, scale):
+        q, k, v = q.contiguous(), k.contiguous(), v.contiguous()
+        out, lse = K.varlen_attention_fwd(q, k, v, run_start, tile_lo, scale)
+        ctx.save_for_backward(q, k, v, out, lse, run_start, run_end)
+        ctx.scale = scale
+        return out
+
+    @staticmethod
+    def backward(ctx, dout):
+        q, k, v, out, lse, run_start, run_end = ctx.saved_tensors
+        dq, dk, dv = K.varlen_attention_bwd(q, k, v, out, dout.contiguous(), lse, run_start, run_end, ctx.scale)
+        return dq, dk, dv, None, None, None, None
+
+
+def segment_attention(q, k, v, run_start, run_end, tile_lo, scale):
+    """Autograd-aware K5/K6 attention (``q [L,Hq,hd]``, ``k, v [L,Hkv,hd]``, bf16)."""
+    return _SegmentAttention.apply(q, k, v, run_start, run_end, tile_lo, scale)
+
+
+class SegmentLayout:
+    """Per-stream metadata shared by every layer of one packed forward."""
+
+    def __init__(self, sequence_ids: torch.Tensor, device: torch.device):
+        seq = sequence_ids.to(device=device, dtype=torch.long).contiguous()
+        self.L = seq.shape[0]
+        pos, rs, tl, flags, re = K.segment_meta(seq, tile=128, with_run_end=True)
+        self.position_ids = pos
+        if sequence_ids.device.type == "cpu":
+            unsorted = bool((sequence_ids[1:] < sequence_ids[:-1]).any()) if self.L > 1 else False
+        else:
+            unsorted = bool(flags.item())
+        self.perm = None
+        self.inv = None
+        if unsorted:
+            # Make every id one run: stable sort keeps each id's token order.
+            self.perm = torch.sort(seq, stable=True).indices
+            self.inv = torch.empty_like(self.perm)
+            self.inv[self.perm] = torch.arange(self.L, device=device)
+            _, rs, tl, _, re = K.segment_meta(seq[self.perm].contiguous(), tile=128, with_run_end=True)
+        self.run_start, self.run_end, self.tile_lo = rs, re, tl
+
+    def attend(self, q, k, v, scale):
+        if self.perm is None:
+            return segment_attention(q, k, v, self.run_start, self.run_end, self.tile_lo, scale)
+        o = segment_attention(q[self.perm], k[self.perm], v[self.perm], self.run_start, self.run_end,
+                              self.tile_lo, scale)
+        return o[self.inv]
+
+
+def _rotate_half(x):
+    half = x.shape[-1] // 2
+    return torch.cat((-x[..., half:], x[..., :half]), dim=-1)
+
+
+def flex_packed_forward(*, model: torch.nn.Module, embeds: torch.Tensor, sequence_ids: torch.Tensor,
+                        output_hidden_states: bool = False):
+    """Full pass over a flat packed sequence ``embeds [L, D]``.
+
+    Attention is causal within positions that share ``sequence_ids``; RoPE
+    positions restart at each new run of ``sequence_ids``. Returns ``[L, D]``
+    (and the tuple of per-layer hidden states when ``output_hidden_states``).
+    """
+    if embeds.ndim != 2:
+        raise ValueError(f"embeds must be [L, D], got shape {tuple(embeds.shape)}")
+    L, _D = embeds.shape
+    if sequence_ids.shape != (L,):
+        raise ValueError("sequence_ids must have shape [L]")
+    hf = cast(Any, model)
+    param = next(hf.parameters())
+    device, dtype = param.device, param.dtype
+    if device.type != "cuda":
+        raise RuntimeError(f"mouse_core_b200 packed attention runs on a CUDA device (B200) only; model is on {device}")
+    if dtype != torch.bfloat16:
+        raise TypeError("mouse_core_b200 kernels compute in bfloat16; move the backbone to torch.bfloat16 "
+                        f"(got {dtype})")
+    cfg = hf.config
+    n_heads = int(cfg.num_attention_heads)
+    n_kv = int(cfg.num_key_value_heads)
+    hd = int(getattr(cfg, "head_dim", None) or cfg.hidden_size // n_heads)
+    if hd not in (64, 128):
+        raise ValueError(f"head_dim must be 64 or 128 for the sm_100a kernels, got {hd}")
+
+    x = embeds.to(device=device, dtype=dtype)
+    if L == 0:
+        h = hf.norm(x)
+        return (h, tuple(x for _ in hf.layers)) if output_hidden_states else h
+    layout = SegmentLayout(sequence_ids, device)
+    cos, sin = hf.rotary_emb(x.unsqueeze(0), layout.position_ids.unsqueeze(0))
+    cos, sin = cos[0].unsqueeze(1), sin[0].unsqueeze(1)  # [L, 1, hd]
+
+    h = x
+    hiddens = []
+    for layer in hf.layers:
+        residual = h
+        hn = layer.input_layernorm(h)
+        attn = layer.self_attn
+        q = attn.q_proj(hn).view(L, n_heads, hd)
+        k = attn.k_proj(hn).view(L, n_kv, hd)
+        q_norm = getattr(attn, "q_norm", None)
+        if q_norm is not None:
+            q = q_norm(q)
+            k = attn.k_norm(k)
+        v = attn.v_proj(hn).view(L, n_kv, hd)
+        q = q * cos + _rotate_half(q) * sin
+        k = k * cos + _rotate_half(k) * sin
+        o = layout.attend(q, k, v, float(attn.scaling))
+        h = residual + attn.o_proj(o.reshape(L, n_heads * hd))
+        h = h + layer.mlp(layer.post_attention_layernorm(h))
+        if output_hidden_states:
+            hiddens.append(h)
+    h = hf.norm(h)
+    if output_hidden_states:
+        return h, tuple(hiddens)
+    return h

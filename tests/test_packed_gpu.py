@@ -175,3 +175,133 @@ def test_varlen_bwd_packed_2048_against_reference_samples():
         scale = max(1.0, float(np.abs(ref).max()))
         err = np.abs(arr.reshape(-1)[g[f"{gname}_idx"]] - ref).max()
         assert err <= ATOL * scale, f"{gname}: max abs err vs reference samples {err}"
+
+
+# ---------------------------------------------------------------- flex_packed_forward
+
+
+def _qwen3_fixture_model(rec, dev):
+    from mouse_core_b200.backbone import Qwen3Backbone
+
+    bb = Qwen3Backbone(hidden_dim=64, num_layers=2, num_heads=2, num_key_value_heads=1, head_dim=64)
+    sd = {k[2:]: torch.from_numpy(v.astype(np.float32)) for k, v in rec.items() if k.startswith("w:")}
+    bb.model.load_state_dict(sd, strict=False)
+    bb.model.rotary_emb.inv_freq.copy_(torch.from_numpy(rec["inv_freq"]))
+    return bb.to(device=dev, dtype=torch.bfloat16)
+
+
+def test_flex_packed_forward_matches_reference_golden():
+    dev = _dev()
+    from mouse_core_b200 import flex_packed_forward
+    from oracle import decoder as odec
+    from tests.golden_io import decoder_from_fixture
+
+    rec = dict(load("packed_fwd_qwen3.npz"))
+    bb = _qwen3_fixture_model(rec, dev)
+    emb = torch.from_numpy(rec["emb"])
+    seq = torch.from_numpy(rec["seq"])
+    with torch.no_grad():
+        h, layers = flex_packed_forward(model=bb.model, embeds=emb.to(dev), sequence_ids=seq.to(dev),
+                                        output_hidden_states=True)
+    h = h.float().cpu().numpy()
+    assert h.shape == rec["out"].shape and len(layers) == 2
+    rec16 = dict(rec)
+    for key in list(rec16):
+        if key.startswith("w:"):
+            rec16[key] = torch.from_numpy(rec16[key].astype(np.float32)).bfloat16().float().numpy()
+    rec16.update(num_layers=np.array(2), n_heads=np.array(2), n_kv_heads=np.array(1), head_dim=np.array(64),
+                 qk_norm=np.array(True))
+    dec16, _ = decoder_from_fixture(rec16)
+    o16 = odec.packed_forward(dec16, emb.bfloat16().float().numpy(), rec["seq"])
+    np.testing.assert_allclose(h, o16, atol=ATOL, rtol=1e-2)
+    np.testing.assert_allclose(h, rec["out"], atol=5e-2, rtol=2e-2)
+
+
+def _train_model(dev, hd, seed=0):
+    from mouse_core_b200.backbone import Qwen3Backbone
+
+    torch.manual_seed(seed)
+    bb = Qwen3Backbone(hidden_dim=256, num_layers=2, num_heads=4, num_key_value_heads=2, head_dim=hd)
+    with torch.no_grad():
+        for name, prm in bb.model.named_parameters():
+            if "norm" not in name:
+                prm.mul_(4.0)  # non-trivial attention at init
+            prm.copy_(prm.bfloat16().float())
+    return bb
+
+
+@pytest.mark.parametrize("hd,ids", [(64, "sorted"), (128, "sorted"), (64, "unsorted")])
+def test_flex_packed_gradients_match_fp32_torch(hd, ids):
+    """Loss gradients w.r.t. embeds and weights: bf16 tcgen05 path vs the
+    reference's dense-mask SDPA path run in fp32 (plain PyTorch) on the GPU."""
+    dev = _dev()
+    import copy
+
+    from mouse_core_b200 import flex_packed_forward
+    from mouse_core_b200.packing import flat_sequence_causal_mask, flat_sequence_position_ids
+
+    bb = _train_model(dev, hd)
+    ref_bb = copy.deepcopy(bb).to(device=dev, dtype=torch.float32)
+    ours = bb.to(device=dev, dtype=torch.bfloat16)
+    if ids == "sorted":
+        seq = torch.from_numpy(_seq_from_lengths([100, 1, 300, 17, 200]))
+    else:
+        seq = torch.tensor(([0] * 40 + [1] * 25 + [0] * 60 + [2] * 90 + [1] * 30) * 2, dtype=torch.long)
+    L = seq.shape[0]
+    g = torch.Generator().manual_seed(1)
+    emb = torch.randn(L, 256, generator=g).bfloat16().float()
+    w = torch.randn(L, 256, generator=g)
+
+    e1 = emb.to(dev).requires_grad_(True)
+    h1 = flex_packed_forward(model=ours.model, embeds=e1, sequence_ids=seq.to(dev))
+    (h1.float() * w.to(dev)).sum().backward()
+
+    e2 = emb.to(dev).requires_grad_(True)
+    sd = seq.to(dev)
+    mask = flat_sequence_causal_mask(sequence_ids=sd, dtype=torch.float32)
+    pos = flat_sequence_position_ids(sd)
+    h2 = ref_bb(e2[None], attention_mask=mask, position_ids=pos)[0]
+    (h2 * w.to(dev)).sum().backward()
+
+    def rel(a, b):
+        return float((a.float() - b.float()).norm() / (b.float().norm() + 1e-12))
+
+    assert rel(h1, h2) < 2e-2
+    assert rel(e1.grad, e2.grad) < 3e-2
+    p1 = dict(ours.model.named_parameters())
+    for name, p2 in ref_bb.model.named_parameters():
+        if p2.grad is None:
+            continue
+        assert rel(p1[name].grad, p2.grad) < 3e-2, name
+
+
+def test_flex_packed_forward_isolates_sequences():
+    """Changing one segment's embeddings leaves every other segment's outputs
+    bitwise unchanged (segments never attend across ids)."""
+    dev = _dev()
+    from mouse_core_b200 import flex_packed_forward
+
+    bb = _train_model(dev, 128).to(device=dev, dtype=torch.bfloat16)
+    seq = torch.from_numpy(_seq_from_lengths([130, 70, 260])).to(dev)
+    g = torch.Generator().manual_seed(2)
+    emb = torch.randn(460, 256, generator=g).to(dev)
+    emb2 = emb.clone()
+    emb2[130:200] = torch.randn(70, 256, generator=g).to(dev)
+    with torch.no_grad():
+        a = flex_packed_forward(model=bb.model, embeds=emb, sequence_ids=seq)
+        b = flex_packed_forward(model=bb.model, embeds=emb2, sequence_ids=seq)
+    assert torch.equal(a[:130], b[:130]) and torch.equal(a[200:], b[200:])
+    assert not torch.equal(a[130:200], b[130:200])
+
+
+def test_flex_packed_forward_rejects_bad_shapes():
+    dev = _dev()
+    from mouse_core_b200 import flex_packed_forward
+
+    bb = _train_model(dev, 64).to(device=dev, dtype=torch.bfloat16)
+    with pytest.raises(ValueError, match=r"\[L, D\]"):
+        flex_packed_forward(model=bb.model, embeds=torch.zeros(1, 4, 256, device=dev),
+                            sequence_ids=torch.zeros(4, dtype=torch.long, device=dev))
+    with pytest.raises(ValueError, match="sequence_ids"):
+        flex_packed_forward(model=bb.model, embeds=torch.zeros(4, 256, device=dev),
+                            sequence_ids=torch.zeros(3, dtype=torch.long, device=dev))
