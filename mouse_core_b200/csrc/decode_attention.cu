@@ -13,10 +13,12 @@
 //
 // Two schedules share one TMA producer:
 //  * split mode (G*S <= 16 query rows per (row, kv-head)): persistent CTAs
-//    walk a device-built work list of (row, chunk) entries x kv-heads. Each
-//    item streams its chunk's K/V tiles through a 3-stage TMA ring; four
-//    consumer warps split the tile's tokens, run QK^T and PV on the tensor
-//    pipe (m16n8k16) with an online softmax, then merge across warps in shared
+//    walk a device-built work list of (row, chunk) entries x kv-heads. A
+//    producer warp stages each item's metadata and Q rows in a 2-slot
+//    shared-memory ring and streams its K/V tiles through a 3-stage TMA ring,
+//    so the consumers never wait on dependent global loads; four consumer
+//    warps split each tile's tokens, run QK^T and PV on the tensor pipe
+//    (m16n8k16) with an online softmax, then merge across warps in shared
 //    memory. Rows with several chunks write (O, lse) partials and the last
 //    CTA of a (row, kv-head) — found with an atomic ticket — merges them.
 //  * block mode (more rows): one CTA per (64-row query block, kv-head, row);
@@ -192,36 +194,54 @@ __device__ __forceinline__ void online_softmax(float (&s)[NJ][4], float (&o)[HD 
 template <int HD>
 struct SplitSmem {
   static constexpr int RING = 2 * AttnTile<HD>::STAGES * AttnTile<HD>::TILE_BYTES;
-  // after the ring: comb_o [4][R][HD] f32, comb_m [4][R], comb_l [4][R], bars, flag
+  // Item slots staged by the producer: 16 Q rows (padded against bank
+  // conflicts) + metadata ints.
+  static constexpr int QROW = HD * 2 + 16;
+  static constexpr int META = 32;  // ints
+  static constexpr int SLOT = 16 * QROW + META * 4;
+  static constexpr int NSLOT = 2;
+  // after the ring and slots: comb_o [4][R][HD] f32, comb_m [4][R], comb_l [4][R], bars, flag
   static size_t bytes(int R) {
-    return 1024 + RING + (size_t)4 * R * HD * 4 + (size_t)8 * R * 4 + 2 * AttnTile<HD>::STAGES * 8 + 16;
+    return 1024 + RING + NSLOT * SLOT + (size_t)4 * R * HD * 4 + (size_t)8 * R * 4 +
+           (2 * AttnTile<HD>::STAGES + 2 * NSLOT) * 8 + 16;
   }
 };
 
+// Item metadata slot layout (ints after the Q rows).
+enum : int { kMetaB = 0, kMetaH, kMetaBegin, kMetaEnd, kMetaChunks, kMetaKvEnd = 8 };
+
 template <int HD>
-__global__ void __launch_bounds__(160) split_decode_kernel(const __grid_constant__ CUtensorMap kmap,
+__global__ void __launch_bounds__(160, 2) split_decode_kernel(const __grid_constant__ CUtensorMap kmap,
                                                            const __grid_constant__ CUtensorMap vmap,
                                                            const AttnParams p) {
   using C = AttnTile<HD>;
+  using SM = SplitSmem<HD>;
   constexpr int TW = C::T / 4;   // tokens per warp per tile
   constexpr int NJ = TW / 8;     // n-tiles per warp
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* kring = smem;
   uint8_t* vring = smem + C::STAGES * C::TILE_BYTES;
+  uint8_t* slots = smem + SM::RING;
   const int R = p.R;
-  float* comb_o = reinterpret_cast<float*>(smem + SplitSmem<HD>::RING);
+  float* comb_o = reinterpret_cast<float*>(slots + SM::NSLOT * SM::SLOT);
   float* comb_m = comb_o + 4 * R * HD;
   float* comb_l = comb_m + 4 * R;
   uint64_t* full = reinterpret_cast<uint64_t*>(comb_l + 4 * R);
   uint64_t* empty = full + C::STAGES;
-  int* flag = reinterpret_cast<int*>(empty + C::STAGES);
+  uint64_t* item_full = empty + C::STAGES;
+  uint64_t* item_empty = item_full + SM::NSLOT;
+  int* flag = reinterpret_cast<int*>(item_empty + SM::NSLOT);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::STAGES; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 4);
+    }
+    for (int s = 0; s < SM::NSLOT; ++s) {
+      mbar_init(&item_full[s], 1);
+      mbar_init(&item_empty[s], 1);
     }
     fence_barrier_init();
   }
@@ -230,23 +250,63 @@ __global__ void __launch_bounds__(160) split_decode_kernel(const __grid_constant
   const int n_items = *p.n_entries * p.Hkv;
 
   if (warp == 4) {
-    // ---------------------------------------------------------- producer
+    // ---------------------------------------------------------- producer warp
+    // Per item: stage its metadata and Q rows in a slot (all lanes), then
+    // lane 0 streams the item's K/V tiles into the TMA ring.
     if (lane == 0) {
       prefetch_tensormap(&kmap);
       prefetch_tensormap(&vmap);
-      uint32_t it = 0;
-      for (int item = blockIdx.x; item < n_items; item += gridDim.x) {
-        const int2 ent = p.entries[item / p.Hkv];
-        const int h = item % p.Hkv, b = ent.x;
-        const int len = p.kv_len[b];
-        const int t_end = min(ent.y * p.chunk_tokens + p.chunk_tokens, len);
-        for (int t0 = ent.y * p.chunk_tokens; t0 < t_end; t0 += C::T, ++it) {
+    }
+    uint32_t it = 0;
+    int k = 0;
+    for (int item = blockIdx.x; item < n_items; item += gridDim.x, ++k) {
+      const int slot = k & 1;
+      bool ok = true;
+      if (lane == 0) ok = mbar_wait(&item_empty[slot], ((k >> 1) & 1) ^ 1, kDevTimeoutEmpty);
+      if (!__shfl_sync(0xffffffffu, ok, 0)) break;
+      const int2 ent = p.entries[item / p.Hkv];
+      const int h = item % p.Hkv, b = ent.x;
+      const int len = p.kv_len[b];
+      const int t_begin = ent.y * p.chunk_tokens;
+      const int t_end = min(t_begin + p.chunk_tokens, len);
+      uint8_t* sq = slots + slot * SM::SLOT;
+      int* meta = reinterpret_cast<int*>(sq + 16 * SM::QROW);
+      if (lane < 16) {
+        int ke = len;
+        if (lane < R) ke = min(p.q_pos[(size_t)b * p.S + lane / p.G] + 1, len);
+        meta[kMetaKvEnd + lane] = ke;
+      }
+      if (lane == 0) {
+        meta[kMetaB] = b;
+        meta[kMetaH] = h;
+        meta[kMetaBegin] = t_begin;
+        meta[kMetaEnd] = t_end;
+        meta[kMetaChunks] = p.row_chunks[b];
+      }
+      for (int c = lane; c < 16 * (HD / 8); c += 32) {
+        const int r = c / (HD / 8), ch = c % (HD / 8);
+        uint4 val = make_uint4(0, 0, 0, 0);
+        if (r < R) {
+          const int s_ = r / p.G, g = r % p.G;
+          val = *reinterpret_cast<const uint4*>(p.q + (((size_t)b * p.S + s_) * p.Hq + (size_t)h * p.G + g) * HD +
+                                                ch * 8);
+        }
+        *reinterpret_cast<uint4*>(sq + r * SM::QROW + ch * 16) = val;
+      }
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(&item_full[slot]);
+        for (int t0 = t_begin; t0 < t_end; t0 += C::T, ++it) {
           const int st = it % C::STAGES;
-          if (!mbar_wait(&empty[st], ((it / C::STAGES) & 1) ^ 1, kDevTimeoutEmpty)) return;
-          issue_tile<HD>(&kmap, &vmap, kring + st * C::TILE_BYTES, vring + st * C::TILE_BYTES, &full[st], p, b, h,
-                         t0, len);
+          if (!mbar_wait(&empty[st], ((it / C::STAGES) & 1) ^ 1, kDevTimeoutEmpty)) {
+            ok = false;
+            break;
+          }
+          issue_tile<HD>(&kmap, &vmap, kring + st * C::TILE_BYTES, vring + st * C::TILE_BYTES, &full[st], p, b,
+                         h, t0, len);
         }
       }
+      if (!__shfl_sync(0xffffffffu, ok, 0)) break;
     }
     return;
   }
@@ -256,24 +316,26 @@ __global__ void __launch_bounds__(160) split_decode_kernel(const __grid_constant
   const int gid = lane >> 2, tig = lane & 3;
   uint32_t it = 0;
   bool alive = true;
-  for (int item = blockIdx.x; item < n_items; item += gridDim.x) {
-    const int e_idx = item / p.Hkv;
-    const int2 ent = p.entries[e_idx];
-    const int h = item % p.Hkv, b = ent.x;
-    const int len = p.kv_len[b];
-    const int t_begin = ent.y * p.chunk_tokens;
-    const int t_end = min(t_begin + p.chunk_tokens, len);
-    const int nchunks = p.row_chunks[b];
-
-    int kv_end[2];
-#pragma unroll
-    for (int half = 0; half < 2; ++half) {
-      const int r = gid + 8 * half;
-      kv_end[half] = len;
-      if (r < R) kv_end[half] = min(p.q_pos[(size_t)b * p.S + r / p.G] + 1, len);
-    }
+  int k = 0;
+  for (int item = blockIdx.x; item < n_items; item += gridDim.x, ++k) {
+    const int slot = k & 1;
+    if (alive && !mbar_wait(&item_full[slot], (k >> 1) & 1, kDevTimeoutFull)) alive = false;
+    const uint8_t* sq = slots + slot * SM::SLOT;
+    const int* meta = reinterpret_cast<const int*>(sq + 16 * SM::QROW);
+    const int b = meta[kMetaB], h = meta[kMetaH];
+    const int t_begin = meta[kMetaBegin], t_end = alive ? meta[kMetaEnd] : meta[kMetaBegin];
+    const int nchunks = meta[kMetaChunks];
+    const int kv_end[2] = {meta[kMetaKvEnd + gid], meta[kMetaKvEnd + gid + 8]};
     uint32_t qa[HD / 16][4];
-    load_q_frags<HD>(qa, p, b, h, 0, R, lane);
+#pragma unroll
+    for (int kk = 0; kk < HD / 16; ++kk) {
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+        const uint8_t* row = sq + (gid + 8 * half) * SM::QROW;
+        qa[kk][half] = *reinterpret_cast<const uint32_t*>(row + (kk * 16 + tig * 2) * 2);
+        qa[kk][2 + half] = *reinterpret_cast<const uint32_t*>(row + (kk * 16 + 8 + tig * 2) * 2);
+      }
+    }
 
     float o[HD / 8][4];
 #pragma unroll
@@ -332,23 +394,25 @@ __global__ void __launch_bounds__(160) split_decode_kernel(const __grid_constant
       }
       const float val = (L > 0.f) ? O / L : 0.f;
       if (nchunks == 1) {
-        const int s = r / p.G, g = r % p.G;
-        p.out[(((size_t)b * p.S + s) * p.Hq + (size_t)h * p.G + g) * HD + col] = __float2bfloat16_rn(val);
+        const int s_ = r / p.G, g = r % p.G;
+        p.out[(((size_t)b * p.S + s_) * p.Hq + (size_t)h * p.G + g) * HD + col] = __float2bfloat16_rn(val);
       } else {
         p.part_o[((size_t)item * R + r) * HD + col] = val;
         if (col == 0) p.part_lse[(size_t)item * R + r] = (L > 0.f) ? M + log2f(L) : -INFINITY;
       }
     }
     if (nchunks > 1) {
-      __threadfence();
+      // Release this CTA's partials, take a ticket; the last CTA of the
+      // (row, kv-head) acquires every partial and merges them.
       named_barrier(1, 128);
       if (tid == 0) {
+        __threadfence();
         const int ticket = atomicAdd(&p.counters[b * p.Hkv + h], 1);
         *flag = (ticket == nchunks - 1);
+        if (*flag) __threadfence();
       }
       named_barrier(1, 128);
       if (*flag) {
-        __threadfence();
         const int first = p.row_start[b];
         for (int idx = tid; idx < R * HD; idx += 128) {
           const int r = idx / HD, col = idx % HD;
@@ -363,14 +427,15 @@ __global__ void __launch_bounds__(160) split_decode_kernel(const __grid_constant
             den += f;
             num += f * __ldcg(&p.part_o[(pit * R + r) * HD + col]);
           }
-          const int s = r / p.G, g = r % p.G;
-          p.out[(((size_t)b * p.S + s) * p.Hq + (size_t)h * p.G + g) * HD + col] =
+          const int s_ = r / p.G, g = r % p.G;
+          p.out[(((size_t)b * p.S + s_) * p.Hq + (size_t)h * p.G + g) * HD + col] =
               __float2bfloat16_rn(den > 0.f ? num / den : 0.f);
         }
         if (tid == 0) p.counters[b * p.Hkv + h] = 0;
       }
     }
     named_barrier(1, 128);
+    if (tid == 0) mbar_arrive(&item_empty[slot]);
   }
 }
 
@@ -534,7 +599,7 @@ __global__ void __launch_bounds__(160) block_decode_kernel(const __grid_constant
 
 // ------------------------------------------------------------------ host side
 
-size_t decode_chunk_tokens(int head_dim) { return head_dim == 128 ? 512 : 1024; }
+size_t decode_chunk_tokens(int head_dim) { return head_dim == 128 ? 1024 : 2048; }
 
 size_t decode_workspace_layout(int B, int Hkv, int R, int head_dim, int max_kv_len, WorkspaceLayout* lay) {
   const size_t chunk = decode_chunk_tokens(head_dim);
