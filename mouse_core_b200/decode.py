@@ -138,6 +138,13 @@ class PagedDecodeSession:
         self._len = np.zeros(self.B, dtype=np.int64)
         self._bt_dev = torch.full((self.B, self.pages.max_pages), -1, dtype=torch.int32, device=self.device)
         self._workspace = torch.empty(0, dtype=torch.uint8, device=self.device)
+        self._meta_dev = torch.empty(0, dtype=torch.int32, device=self.device)
+        # Single-token steps (S = 1, the steady state of env stepping) replay a
+        # CUDA graph of the whole layer stack after one eager warm-up call.
+        self.use_graphs = True
+        self._graph = None
+        self._graph_key = None
+        self._graph_warm = False
         self._staging = [None, None]
         self._staging_ev = [None, None]
         self._turn = 0
@@ -236,7 +243,12 @@ class PagedDecodeSession:
         o += B * S
         if bt_changed:
             host[o:o + B * width] = self.pages.table.reshape(-1)
-        dev = buf[:n_meta].to(self.device, non_blocking=True)
+        if self._meta_dev.numel() < n_meta:
+            self._meta_dev = torch.empty(max(n_meta, 2 * self._meta_dev.numel()), dtype=torch.int32,
+                                         device=self.device)
+            self._graph = None  # its captured views point at the old buffer
+        dev = self._meta_dev
+        dev[:n_meta].copy_(buf[:n_meta], non_blocking=True)
         ev = torch.cuda.Event()
         ev.record()
         self._staging_ev[i] = ev
@@ -246,7 +258,7 @@ class PagedDecodeSession:
         if bt_changed:
             if self._bt_dev.shape[1] != width:
                 self._bt_dev = torch.empty((B, width), dtype=torch.int32, device=self.device)
-            self._bt_dev.copy_(dev[2 * B * S + B:].view(B, width))
+            self._bt_dev.copy_(dev[2 * B * S + B:n_meta].view(B, width))
             self.pages.dirty = False
         self._len = new_len
         return q_pos_d, kv_len_d, slot_d, int(new_len.max()) if B else 0
@@ -265,7 +277,44 @@ class PagedDecodeSession:
         if B == 0 or S == 0:
             h = x.view(B, S, D)
             return (h, tuple(h for _ in range(self.n_layers))) if output_hidden_states else h
+        graphable = (S == 1 and self.use_graphs and not output_hidden_states and self.attn_events is None
+                     and not torch.cuda.is_current_stream_capturing())
+        if not graphable:
+            out = self._body(x, q_pos, kv_len, slot, S, output_hidden_states)
+            if output_hidden_states:
+                h, hiddens = out
+                return self.model.norm(h.view(B, S, D)), tuple(t.view(B, S, D) for t in hiddens)
+            return self.model.norm(out.view(B, S, D))
+        for lw in self._layers:
+            lw.refresh()
+        key = (self.k_pool.data_ptr(), self._bt_dev.data_ptr(), self._meta_dev.data_ptr(), self.cap,
+               tuple(lw.version for lw in self._layers))
+        if self._graph is None or self._graph_key != key:
+            if not self._graph_warm:
+                # Eager warm-up: allocates the workspace and initialises cuBLAS.
+                self._graph_warm = True
+                return self.model.norm(self._body(x, q_pos, kv_len, slot, 1, False).view(B, S, D))
+            self._graph = None
+            self._graph_x = torch.empty_like(x)
+            self._graph_x.copy_(x)
+            graph = torch.cuda.CUDAGraph()
+            n0 = K.launch_count[0]
+            with torch.cuda.graph(graph):
+                self._graph_out = self._body(self._graph_x, q_pos, kv_len, slot, 1, False)
+            self._graph_launches = K.launch_count[0] - n0
+            K.launch_count[0] = n0
+            self._graph, self._graph_key = graph, key
+        else:
+            self._graph_x.copy_(x)
+        self._graph.replay()
+        K._count(self._graph_launches)
+        return self.model.norm(self._graph_out.view(B, S, D).clone())
 
+    def _body(self, x, q_pos, kv_len, slot, S, output_hidden_states):
+        """The layer stack for flattened ``x [B*S, D]``; returns the last hidden
+        state (before the final norm) and, if asked, every layer's."""
+        B = self.B
+        D = x.shape[-1]
         Hq, Hkv, hd = self.n_heads, self.n_kv_heads, self.head_dim
         R = (Hq // Hkv) * S
         split = R <= 16
@@ -273,6 +322,7 @@ class PagedDecodeSession:
             need = K.decode_workspace_bytes(B, Hkv, R, hd, self.cap)
             if self._workspace.numel() < need:
                 self._workspace = torch.empty(need, dtype=torch.uint8, device=self.device)
+                self._graph = None
             K.decode_plan(kv_len, Hkv, R, hd, self.cap, self._workspace)
         q_pos_flat = q_pos.reshape(-1)
 
@@ -302,11 +352,10 @@ class PagedDecodeSession:
             resid, hn2 = K.rmsnorm(a, lw.post_w, lw.post_eps, residual=resid)
             delta = lw.down(K.silu_mul(F.linear(hn2, lw.wgu, lw.bgu)))
             if output_hidden_states:
-                hiddens.append((resid + delta).view(B, S, D))
-        h = hiddens[-1] if output_hidden_states else (resid + delta).view(B, S, D)
-        h = self.model.norm(h)
+                hiddens.append(resid + delta)
+        h = hiddens[-1] if output_hidden_states else resid + delta
         if output_hidden_states:
-            return h, tuple(hiddens)
+            return h, hiddens
         return h
 
 

@@ -304,3 +304,32 @@ def test_session_rejects_bad_inputs():
         sess.forward(embeds=torch.randn(3, 1, 128, device=dev), lengths=[1, 1, 1])
     with pytest.raises(ValueError):
         sess.forward(embeds=torch.randn(2, 1, 128, device=dev), lengths=[2, 1])
+
+
+def test_session_graph_replay_matches_eager():
+    """Single-token steps replay a captured CUDA graph; they must equal the
+    eager path step for step, across page boundaries and a block-table
+    widening (which forces a re-capture)."""
+    dev = _dev()
+    from mouse_core_b200.backbone import Qwen3Backbone
+
+    torch.manual_seed(9)
+    bb = Qwen3Backbone(hidden_dim=256, num_layers=2, num_heads=4, num_key_value_heads=2, head_dim=128)
+    bb = bb.to(device=dev, dtype=torch.bfloat16).eval()
+    B = 4
+    graph_sess = bb.decode_session(batch_size=B, capacity=64, page_size=64)
+    eager_sess = bb.decode_session(batch_size=B, capacity=64, page_size=64)
+    eager_sess.use_graphs = False
+    g = torch.Generator().manual_seed(4)
+    pre = torch.randn(B, 60, 256, generator=g).bfloat16().to(dev)
+    lens = [60, 3, 0, 59]
+    a = graph_sess.forward(embeds=pre, lengths=lens)
+    b = eager_sess.forward(embeds=pre, lengths=lens)
+    assert torch.equal(a, b)
+    for step in range(80):  # crosses the 64-token page and widens the table past 64 slots
+        x = torch.randn(B, 1, 256, generator=g).bfloat16().to(dev)
+        a = graph_sess.forward(embeds=x, lengths=[1] * B)
+        b = eager_sess.forward(embeds=x, lengths=[1] * B)
+        assert (a.float() - b.float()).abs().max().item() <= 1e-3, step
+    assert graph_sess._graph is not None
+    assert graph_sess.lengths.tolist() == eager_sess.lengths.tolist()
