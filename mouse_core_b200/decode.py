@@ -176,6 +176,53 @@ class PagedDecodeSession:
         self.pages.release_rows(rows)
         self._len[np.atleast_1d(np.asarray(rows, dtype=np.int64))] = 0
 
+    def fork(self, src_rows, dst_rows, prefix_lengths=None) -> None:
+        """Start rows ``dst_rows`` as branches of ``src_rows``: branch ``i``
+        holds the first ``prefix_lengths[i]`` cached tokens of its source row
+        (default: all of them) and continues decoding from there.
+
+        The prefix's full pages are shared by reference (no copy; pages are
+        refcounted and return to the pool when the last holder lets go); only
+        a partially filled last page is copied (K3) so the branch can append
+        to it. Destination rows are emptied first. This has no counterpart in
+        the reference, whose GRPO rollouts re-run every branch uncached."""
+        src = np.atleast_1d(np.asarray(src_rows, dtype=np.int64))
+        dst = np.atleast_1d(np.asarray(dst_rows, dtype=np.int64))
+        if src.shape != dst.shape:
+            raise ValueError("src_rows and dst_rows must have the same length")
+        plen = self._len[src].copy() if prefix_lengths is None else np.atleast_1d(
+            np.asarray(prefix_lengths, dtype=np.int64))
+        if plen.shape != src.shape or (plen < 0).any() or (plen > self._len[src]).any():
+            raise ValueError("prefix_lengths must satisfy 0 <= prefix <= the source row's length")
+        if len(set(dst.tolist())) != dst.size or set(dst.tolist()) & set(src.tolist()):
+            raise ValueError("dst_rows must be distinct and disjoint from src_rows")
+        self.pages.release_rows(dst)
+        self._len[dst] = 0
+        page = self.page_size
+        full = plen // page
+        partial = plen % page
+        n_copy = int((partial > 0).sum())
+        if n_copy > self.pages.free_pages:
+            self._grow_pool(n_copy)
+        copy_src, copy_dst = [], []
+        for s_row, d_row, nf, part in zip(src, dst, full, partial):
+            self.pages.share(int(d_row), int(s_row), int(nf))
+            if part:
+                new = int(self.pages.take_free(1)[0])
+                self.pages.ensure_width(int(nf) + 1)
+                self.pages.table[d_row, nf] = new
+                self.pages.npages[d_row] = nf + 1
+                self.pages.dirty = True
+                copy_src.append(int(self.pages.table[s_row, nf]))
+                copy_dst.append(new)
+        if copy_src:
+            cs = torch.tensor(copy_src, dtype=torch.int32, device=self.device)
+            cd = torch.tensor(copy_dst, dtype=torch.int32, device=self.device)
+            for li in range(self.n_layers):
+                K.page_copy(self.k_pool[li], self.k_pool[li], cs, cd)
+                K.page_copy(self.v_pool[li], self.v_pool[li], cs, cd)
+        self._len[dst] = plen
+
     # ------------------------------------------------------------------ pool
     def _grow_pool(self, need_free: int) -> None:
         old = self.pages.num_pages

@@ -333,3 +333,59 @@ def test_session_graph_replay_matches_eager():
         assert (a.float() - b.float()).abs().max().item() <= 1e-3, step
     assert graph_sess._graph is not None
     assert graph_sess.lengths.tolist() == eager_sess.lengths.tolist()
+
+
+def test_fork_shares_prefix_pages_and_matches_independent_rows():
+    """Branches forked at arbitrary points share the root's full pages, copy
+    only the partial last page, and decode exactly like rows that computed
+    the same prefix themselves."""
+    dev = _dev()
+    from mouse_core_b200.backbone import Qwen3Backbone
+
+    torch.manual_seed(3)
+    bb = Qwen3Backbone(hidden_dim=256, num_layers=2, num_heads=4, num_key_value_heads=2, head_dim=128)
+    bb = bb.to(device=dev, dtype=torch.bfloat16).eval()
+    page, R, G = 64, 2, 3          # 2 roots, 3 branches each
+    B = R + R * G
+    g = torch.Generator().manual_seed(8)
+    root_len = [200, 131]
+    ctx = [torch.randn(L, 256, generator=g).bfloat16() for L in root_len]
+    forks = [[200, 64, 1], [131, 128, 70]]  # fork points (full-page, page-aligned, partial cases)
+
+    shared = bb.decode_session(batch_size=B, capacity=256, page_size=page)
+    S = max(root_len)
+    emb = torch.zeros(B, S, 256, dtype=torch.bfloat16)
+    for r in range(R):
+        emb[r, S - root_len[r]:] = ctx[r]
+    shared.forward(embeds=emb.to(dev), lengths=root_len + [0] * (R * G))
+    free_before = shared.pages.free_pages
+    src, dst, plen = [], [], []
+    for r in range(R):
+        for j in range(G):
+            src.append(r)
+            dst.append(R + r * G + j)
+            plen.append(forks[r][j])
+    shared.fork(src, dst, plen)
+    n_partial = sum(1 for p_ in plen if p_ % page)
+    assert shared.pages.free_pages == free_before - n_partial  # only partial pages were copied
+    assert shared.lengths.cpu().tolist()[R:] == plen
+
+    # Independent reference: every branch row prefills its own prefix.
+    indep = bb.decode_session(batch_size=B, capacity=256, page_size=page)
+    emb2 = torch.zeros(B, S, 256, dtype=torch.bfloat16)
+    lens2 = list(root_len) + plen
+    for r in range(R):
+        emb2[r, S - root_len[r]:] = ctx[r]
+    for i, (s_, p_) in enumerate(zip(src, plen)):
+        if p_:
+            emb2[R + i, S - p_:] = ctx[s_][:p_]
+    indep.forward(embeds=emb2.to(dev), lengths=lens2)
+
+    for step in range(5):
+        x = torch.randn(B, 1, 256, generator=g).bfloat16().to(dev)
+        a = shared.forward(embeds=x, lengths=[1] * B)
+        b = indep.forward(embeds=x, lengths=[1] * B)
+        assert (a.float() - b.float()).abs().max().item() <= 2e-2, step
+    # Releasing the branches returns their private pages; shared pages stay with the roots.
+    shared.reset_rows(dst)
+    assert shared.pages.npages[:R].tolist() == [int(np.ceil((L + 5) / page)) for L in root_len]
