@@ -476,6 +476,181 @@ def packed_attention_metric(device, reps=10, rows=8):
                          "unit": "TFLOP/s", "frac": round(tf_all / peak, 4)}}
 
 
+# ------------------------------------------------------- packed training
+TRAIN_LAYERS, TRAIN_ROWS, TRAIN_ROW_LEN = 28, 8, 16384
+
+
+def train_config(n_gpus, rows=TRAIN_ROWS):
+    return {"workload": f"packed DQN training step, Qwen3-0.6B arch (28 layers), {rows} rows x 16384 tokens, "
+                        "segments U[256,4096] (last truncated per row), synthetic transition tokens, "
+                        "Q targets U[0,1]^4 in place of the target head, AdamW",
+            "rows": rows, "row_len": TRAIN_ROW_LEN, "layers": TRAIN_LAYERS, "hidden": HIDDEN, "q_heads": HEADS,
+            "kv_heads": KV_HEADS, "head_dim": HEAD_DIM, "intermediate": INTER,
+            "parallelism": f"dp{n_gpus} (rows split across ranks; one fp32 gradient all-reduce per step)",
+            "l2": "inputs larger than L2: each layer's activations of one row are ~1 GB"}
+
+
+def train_row_segments(seed=0, rows=TRAIN_ROWS, row_len=TRAIN_ROW_LEN, lo=256, hi=4096):
+    """Per-row segment lengths: U[lo, hi] until the row is full, the last truncated."""
+    rng = np.random.default_rng(seed)
+    out = []
+    for _ in range(rows):
+        segs, total = [], 0
+        while total < row_len:
+            s = min(int(rng.integers(lo, hi + 1)), row_len - total)
+            segs.append(s)
+            total += s
+        out.append(segs)
+    return out
+
+
+def train_row_host(seed, segs):
+    """One packed row in host memory: transition token ids and the fields the
+    TD loss reads (action, reward, done code), sequence ids, U[0,1]^4 targets."""
+    rng = np.random.default_rng(seed)
+    n = int(sum(segs))
+    obs = rng.integers(0, 64, size=n)
+    action = rng.integers(0, 4, size=n)
+    reward = rng.integers(0, 2, size=n)
+    done = (rng.random(n) < 0.02).astype(np.int64)
+    ids = (((obs * 4 + action) * 2 + reward) * 2 + done).astype(np.int64)
+    seq = np.concatenate([np.full(s, i, dtype=np.int64) for i, s in enumerate(segs)])
+    return {"token_ids": ids, "sequence_ids": seq, "action": action.astype(np.int64),
+            "reward": reward.astype(np.float32), "done": done, "q_target": rng.random((n, 4), dtype=np.float32)}
+
+
+def train_flops(segs_per_row, n_params):
+    """Algorithmic FLOPs of one training step over the given rows: 6 * params
+    * tokens for the linear layers + 3.5x the segment-causal attention
+    forward (4 * Hq * hd * sum s(s+1)/2 per layer)."""
+    tokens = sum(sum(s) for s in segs_per_row)
+    attn_fwd = 4 * HEADS * HEAD_DIM * TRAIN_LAYERS * sum(x * (x + 1) // 2 for s in segs_per_row for x in s)
+    return 6 * n_params * tokens + 3.5 * attn_fwd, attn_fwd
+
+
+def run_train(args):
+    import torch
+    import torch.distributed as dist
+
+    from mouse_core_b200 import _lib
+    from mouse_core_b200 import kernels as K
+    from mouse_core_b200.backbone import Qwen3Backbone
+    from mouse_core_b200.train import ActionValueHead, PackedDQNTrainer, PackedRow
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    rows_total = args.train_rows
+    torch.manual_seed(0)
+    bb = Qwen3Backbone(hidden_dim=HIDDEN, num_layers=TRAIN_LAYERS, num_heads=HEADS, num_key_value_heads=KV_HEADS,
+                       head_dim=HEAD_DIM, intermediate_size=INTER,
+                       rope_parameters={"rope_type": "default", "rope_theta": ROPE_THETA})
+    bb = bb.to(device=dev, dtype=torch.bfloat16).train()
+    emb = torch.nn.Embedding(VOCAB, HIDDEN).to(device=dev, dtype=torch.bfloat16)
+    head = ActionValueHead(HIDDEN, 4).to(dev)
+    params = list(emb.parameters()) + list(bb.model.parameters()) + list(head.parameters())
+    opt = torch.optim.AdamW(params, lr=1e-5, fused=True)
+    trainer = PackedDQNTrainer(emb, bb.model, head, opt)
+    n_backbone = sum(p.numel() for n, p in bb.model.named_parameters() if "embed_tokens" not in n)
+
+    segs = train_row_segments(0, rows=rows_total)
+    mine = list(range(rank, rows_total, world))
+    host = [train_row_host(100 + i, segs[i]) for i in mine]
+
+    def to_dev(r, pinned=None):
+        src = pinned if pinned is not None else {k: torch.from_numpy(v) for k, v in r.items()}
+        return PackedRow(**{k: t.to(dev, non_blocking=True) for k, t in src.items()})
+
+    resident = [to_dev(r) for r in host]
+    pinned = [{k: torch.from_numpy(v).pin_memory() for k, v in r.items()} for r in host]
+    h2d_bytes = sum(t.numel() * t.element_size() for p in pinned for t in p.values()) * world
+
+    W, K_steps = args.warmup, args.steps
+    for _ in range(W):
+        trainer.step(resident, rows_total)
+    torch.cuda.synchronize()
+    barrier()
+    torch.cuda.synchronize()
+    clocks = Clocks(local)
+    launches0 = K.launch_count[0]
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(K_steps):
+        loss = trainer.step(resident, rows_total)
+    e1.record()
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    launches = K.launch_count[0] - launches0
+    ms = e0.elapsed_time(e1)
+    ms_t = torch.tensor([ms], device=dev)
+    if world > 1:
+        dist.all_reduce(ms_t, op=dist.ReduceOp.MAX)
+    ms_max = float(ms_t.item())
+
+    # End to end: every step copies its rows from pinned host memory and
+    # reads the loss back.
+    h_loss = torch.empty((), dtype=torch.float32, pin_memory=True)
+    barrier()
+    torch.cuda.synchronize()
+    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    f0.record()
+    for _ in range(K_steps):
+        rows = [to_dev(None, p) for p in pinned]
+        h_loss.copy_(trainer.step(rows, rows_total), non_blocking=True)
+        torch.cuda.current_stream().synchronize()
+    f1.record()
+    torch.cuda.synchronize()
+    et = torch.tensor([f0.elapsed_time(f1)], device=dev)
+    if world > 1:
+        dist.all_reduce(et, op=dist.ReduceOp.MAX)
+    e2e_max = float(et.item())
+    status = _lib.device_status()
+
+    flops, attn_fwd = train_flops(segs, n_backbone)
+    peaks = {}
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            peaks = json.load(f)
+    except (OSError, ValueError):
+        pass
+    peak = float(peaks.get("bf16_tflops_sustained", peaks.get("bf16_tflops", 1400.0)))
+    out = None
+    if rank == 0:
+        tokens = rows_total * TRAIN_ROW_LEN
+        achieved = flops * K_steps / (ms_max * 1e-3) / 1e12
+        out = {"metric": "tokens/s in packed DQN training (fwd+bwd+AdamW)",
+               "value": round(tokens * K_steps / (ms_max * 1e-3), 1), "unit": "tokens/s", "n_gpus": world,
+               "steps": K_steps, "warmup": W, "ms_per_step": round(ms_max / K_steps, 3), "higher_is_better": True,
+               "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+               "data": "synthetic (seeded transition tokens and U[0,1]^4 Q targets; random-init weights)",
+               "config": train_config(world, rows_total),
+               "e2e": {"value": round(tokens * K_steps / (e2e_max * 1e-3), 1), "unit": "tokens/s",
+                       "h2d_bytes_per_step": int(h2d_bytes), "d2h_bytes_per_step": 4 * world,
+                       "ms_per_step": round(e2e_max / K_steps, 3)},
+               "roofline": {"kernel": "whole step (cuBLAS GEMMs + K5/K6 attention)", "bound": "tensor",
+                            "achieved": round(achieved, 1), "peak": peak,
+                            "peak_source": "measured (sustained)" if "bf16_tflops_sustained" in peaks else "fallback",
+                            "unit": "TFLOP/s", "frac": round(achieved / peak, 4), "traffic": None,
+                            "flops_note": "6 * 440.4M params * tokens + 3.5 x algorithmic attention forward"},
+               "attention_fwd_flops_per_step": attn_fwd, "loss": float(loss.item()),
+               "gpu_launches": int(launches), "clocks": clk, "device_status": status}
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return out
+
+
 # ---------------------------------------------------------------- CPU arm
 def _oracle_decoder(seed):
     """The bench model's architecture as a float64 oracle decoder (weights
@@ -525,11 +700,59 @@ def cpu_baseline(seconds=15.0, sample_envs=16):
                       f"FlexDecodeSession.forward), cache lengths U[64,4096], {el:.1f} s"}
 
 
+def train_cpu_baseline(seconds=15.0, row_len=2048, layers=1):
+    """The reference's CPU training path (dense additive segment-causal mask +
+    restarting position ids through the transformers stack, models/base.py:
+    962-969, 1204-1236), fp32, forward + backward of the TD loss, on a reduced
+    instance: ``layers`` of the 28-layer Qwen3-0.6B stack and one row of
+    ``row_len`` tokens. tokens/s is scaled by layers/28 to a full-depth
+    figure (marked as extrapolated)."""
+    import torch
+
+    from mouse_core_b200.backbone import Qwen3Backbone
+    from mouse_core_b200.packing import flat_sequence_causal_mask, flat_sequence_position_ids
+    from mouse_core_b200.train import ActionValueHead, td_loss
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    torch.manual_seed(0)
+    bb = Qwen3Backbone(hidden_dim=HIDDEN, num_layers=layers, num_heads=HEADS, num_key_value_heads=KV_HEADS,
+                       head_dim=HEAD_DIM, intermediate_size=INTER,
+                       rope_parameters={"rope_type": "default", "rope_theta": ROPE_THETA}).float()
+    emb = torch.nn.Embedding(VOCAB, HIDDEN)
+    head = ActionValueHead(HIDDEN, 4)
+    segs = train_row_segments(0, rows=1, row_len=row_len)[0]
+    r = {k: torch.from_numpy(v) for k, v in train_row_host(100, segs).items()}
+    steps, t0 = 0, time.perf_counter()
+    while True:
+        mask = flat_sequence_causal_mask(sequence_ids=r["sequence_ids"], dtype=torch.float32)
+        pos = flat_sequence_position_ids(r["sequence_ids"])
+        h = bb(emb(r["token_ids"])[None], attention_mask=mask, position_ids=pos)[0]
+        loss = td_loss(head(h), r["q_target"], r["action"], r["reward"], r["done"], r["sequence_ids"])
+        loss.backward()
+        steps += 1
+        el = time.perf_counter() - t0
+        if el >= seconds:
+            break
+    per_layer = row_len * steps / el * layers
+    return {"value": round(per_layer / TRAIN_LAYERS, 3), "unit": "tokens/s", "cores": os.cpu_count() or 1,
+            "kind": "port", "per_layer_tokens_per_s": round(per_layer, 1),
+            "sample": f"{steps} fwd+bwd passes of one {row_len}-token row (segments {segs}) through {layers} "
+                      f"layer(s), fp32 dense-mask SDPA path, {el:.1f} s; value extrapolated to 28 layers"}
+
+
 def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     if rank != 0:
         return None
+    if args.train:
+        base = train_cpu_baseline(seconds=max(args.cpu_seconds, 5.0))
+        return {"impl": "reference", "metric": "tokens/s in packed DQN training (fwd+bwd+AdamW)",
+                "value": base["value"], "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+                "dtype": "f32", "data": "synthetic", "config": train_config(world, args.train_rows),
+                "cpu_baseline": base, "e2e": {"value": base["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                                              "d2h_bytes_per_step": 0}}
     per_step = max(args.cpu_seconds / max(args.steps + args.warmup, 1), 1.0)
     base = cpu_baseline(seconds=per_step * args.steps)
     return {"impl": "reference", "metric": "env-steps/s in cached batched decode", "value": base["value"],
@@ -553,11 +776,15 @@ def main():
     ap.add_argument("--packed-rows", type=int, default=8, help="16384-token rows in the packed stream")
     ap.add_argument("--envs", type=int, default=ENVS, help="envs per GPU (256 is the benchmark workload; "
                     "smaller values only for profiling captures)")
+    ap.add_argument("--train", action="store_true", help="time the packed DQN training step instead of decode")
+    ap.add_argument("--train-rows", type=int, default=TRAIN_ROWS, help="16384-token rows per training step")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
     globals()["ENVS"] = args.envs
-    if args.packed_only:
+    if args.train and args.impl == "ours":
+        out = run_train(args)
+    elif args.packed_only:
         import torch
 
         out = packed_attention_metric(torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0"))),
