@@ -23,6 +23,7 @@ enum DeviceStatus : int {
   kDevTimeoutFull = 1,   // consumer gave up waiting for a TMA stage
   kDevTimeoutEmpty = 2,  // producer gave up waiting for a free stage
   kDevBadPage = 3,       // block-table entry outside the page pool
+  kDevBadSmem = 4,       // dynamic shared memory base not 1024-byte aligned
 };
 
 // The library is one translation unit (mouse_b200.cu), so the status word is

@@ -9,23 +9,28 @@
 //
 // Three kernels, no atomics (deterministic):
 //  * delta:  D[h, i] (fp32) from dO and O.
-//  * dkdv:   one CTA per (128-key tile, kv-head). It walks every (q-head of the
-//            group, 128-query tile) pair whose queries may see its keys (from
-//            its own tile to the end of its last key's run). Per pair, with
-//            keys on the TMEM lanes: S^T = K Q^T, P^T, dP^T = V dO^T,
-//            dS^T = P^T o (dP^T - D), then dV += P^T dO and dK += dS^T Q with
-//            P^T / dS^T taken from TMEM. dV, dK accumulate in TMEM across the
-//            whole walk.
-//  * dq:     one CTA per (128-query tile, q-head), walking the same key tiles
-//            as the forward: S = Q K^T, P, dP = dO V^T, dS, dQ += dS K.
+//  * dkdv:   one CTA per (128-key tile, kv-head), walking every (q-head of the
+//            group, 128-query tile) item whose queries may see its keys. Keys
+//            sit on the TMEM lanes: S^T = K Q^T and dP^T = V dO^T land in two
+//            128-column regions; the element-wise warps turn them into P^T and
+//            dS^T (bf16, written back over the dP^T columns they read) and
+//            dV += P^T dO, dK += dS^T Q accumulate in TMEM over the walk.
+//  * dq:     one CTA per (128-query tile, q-head), walking the key tiles the
+//            forward visits: S = Q K^T (double-buffered in TMEM), dP = dO V^T,
+//            dS (bf16, over the S columns it came from), dQ += dS K.
+//
+// Pipelining (one item stream per CTA, every MMA 128 x 128 or 128 x HD wide):
+//  * The element-wise warps read S early and signal once it is in registers,
+//    so the next item's S MMA overlaps this item's exponentials; they signal
+//    the dP read the same way (dq) and hand the bf16 operands over in four
+//    32-column chunks, each releasing two K-steps of the dV/dK (dQ) MMAs.
+//  * The operand needed first (Q in dkdv, K in dq) has a 3-slot TMA ring, the
+//    other (dO, V) a 2-slot ring, so loads run an item or more ahead.
+//  * tcgen05.mma operations of one CTA execute in issue order, so an MMA may
+//    overwrite TMEM columns that an earlier MMA reads as its A operand.
 // Warp roles (320 threads): warp 0 TMA producer, warp 1 TMEM allocator and
-// MMA issuer, warps 2-5 and 6-9 the element-wise work of the two streams
-// (thread = TMEM lane = one key / query row). Both walks alternate
-// two streams (even / odd pairs) so one stream's element-wise work overlaps
-// the other's MMAs. Each stream has one 128-column
-// TMEM scratch that holds S, then dP, then the bf16 dS (and P) operands;
-// P stays in registers (as bf16 pairs, the precision the MMAs take it in)
-// across the dP MMA.
+// MMA issuer, warps 2-9 element-wise (warp w owns TMEM lanes 32*(w%4) and
+// column half (w-2)/4 of each 128-column tile).
 #include "common.cuh"
 #include "kernels.h"
 #include "tcgen05.cuh"
@@ -61,30 +66,6 @@ __global__ void bwd_delta_kernel(const __nv_bfloat16* __restrict__ out, const __
 }
 
 // ---------------------------------------------------------------- shared pieces
-struct BwdBars {
-  uint64_t fixed_full;          // K,V (dkdv) or Q,dO (dq)
-  uint64_t ring_full[2], ring_empty[2];
-  uint64_t ring_v_full[2];      // dq only: V half of a ring slot
-  uint64_t s_full[2], ew1[2], dp_full[2], ew2[2];
-  uint64_t acc_full;
-  uint32_t tmem_base;
-};
-
-__device__ __forceinline__ void init_bwd_bars(BwdBars* b, int ring_full_count) {
-  mbar_init(&b->fixed_full, 1);
-  for (int s = 0; s < 2; ++s) {
-    mbar_init(&b->ring_full[s], ring_full_count);
-    mbar_init(&b->ring_empty[s], 1);
-    mbar_init(&b->ring_v_full[s], 1);
-    mbar_init(&b->s_full[s], 1);
-    mbar_init(&b->ew1[s], 4);
-    mbar_init(&b->dp_full[s], 1);
-    mbar_init(&b->ew2[s], 4);
-  }
-  mbar_init(&b->acc_full, 1);
-  fence_barrier_init();
-}
-
 // D = A B^T over HD; A and B K-major in smem (128 rows x HD). The start
 // address is the descriptor's low field, so K-steps add (offset >> 4) to the
 // 64-bit descriptor (shared-memory addresses stay below 2^18, no carry).
@@ -99,17 +80,37 @@ __device__ __forceinline__ void mma_kmajor_ss(uint32_t d, uint32_t a_base, uint3
   }
 }
 
-// D (+)= A_tmem[128 x 128 (bf16, 64 cols)] * B[128 x HD] with B MN-major in smem.
-template <int HD>
-__device__ __forceinline__ void mma_tmem_a(uint32_t d, uint32_t a_tmem, uint32_t b_base, uint32_t idesc,
-                                           bool accumulate) {
-  const uint64_t db = umma_desc_sw128(b_base, BwdTile<HD>::BOX, 1024);
-#pragma unroll 1
-  for (int kk = 0; kk < 8; ++kk)
-    umma_ts(d, a_tmem + 8 * kk, db + (uint64_t)((kk * 2048) >> 4), idesc, (accumulate || kk > 0) ? 1u : 0u);
-}
+// TMEM column (relative to a 128-column region) of the bf16 A operand for
+// K-step kk (16 tokens): element-wise warp half h = kk / 4 writes its 64
+// tokens packed into columns [64h, 64h + 32) of the region.
+__device__ __forceinline__ uint32_t a_col(int kk) { return (uint32_t)(64 * (kk >> 2) + 8 * (kk & 3)); }
+
+// dkdv: TMEM column of the bf16 P^T for K-step kk (dS^T sits 16 columns
+// further): chunk c = kk / 2 of 32 queries is written over the 32 dP^T columns
+// [32c, 32c + 32) it came from, P^T in the first 16, dS^T in the last 16.
+__device__ __forceinline__ uint32_t pt_col(int kk) { return (uint32_t)(32 * (kk >> 1) + 8 * (kk & 1)); }
+
+// Order in which the MMA warp consumes the four 32-token chunks: the two
+// column halves are produced concurrently, so alternate between them.
+__device__ __forceinline__ int chunk_order(int i) { return ((i & 1) << 1) | (i >> 1); }
+
+// Dynamic shared memory is used from its base without padding (the kernels
+// need nearly all 227 KB); the 128-byte-swizzled TMA boxes need the base
+// 1024-byte aligned, which is checked before anything else runs.
+__device__ __forceinline__ bool smem_base_aligned(const void* p) { return (smem_u32(p) & 1023u) == 0; }
 
 // ---------------------------------------------------------------- dq kernel
+struct DqBars {
+  uint64_t fixed_full;  // Q, dO
+  uint64_t k_full[3], k_empty[3], v_full[2], v_empty[2];
+  uint64_t s_full[2];   // S(j) in TMEM region j & 1
+  uint64_t dp_full;     // dP(j)
+  uint64_t dp_loaded;   // element-wise warps hold dP(j) in registers
+  uint64_t chunk[2][4]; // bf16 dS chunk c of item j ready (set j & 1)
+  uint64_t acc_full;
+  uint32_t tmem_base;
+};
+
 template <int HD>
 __global__ void __launch_bounds__(320, 1) varlen_bwd_dq_kernel(const __grid_constant__ CUtensorMap qmap,
                                                               const __grid_constant__ CUtensorMap kmap,
@@ -117,13 +118,16 @@ __global__ void __launch_bounds__(320, 1) varlen_bwd_dq_kernel(const __grid_cons
                                                               const __grid_constant__ CUtensorMap dom,
                                                               const VarlenBwdParams p) {
   using C = BwdTile<HD>;
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  extern __shared__ __align__(1024) uint8_t smem[];
+  if (!smem_base_aligned(smem)) {
+    if (threadIdx.x == 0) report(kDevBadSmem);
+    return;
+  }
   uint8_t* qs = smem;
   uint8_t* dos = smem + C::TILE;
-  uint8_t* ks = smem + 2 * C::TILE;   // [2][TILE]
-  uint8_t* vs = smem + 4 * C::TILE;   // [2][TILE]
-  BwdBars* bars = reinterpret_cast<BwdBars*>(smem + 6 * C::TILE);
+  uint8_t* kring = smem + 2 * C::TILE;  // [3][TILE]
+  uint8_t* vring = smem + 5 * C::TILE;  // [2][TILE]
+  DqBars* bars = reinterpret_cast<DqBars*>(smem + 7 * C::TILE);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n_qt = (p.L + 127) / 128;
@@ -135,13 +139,29 @@ __global__ void __launch_bounds__(320, 1) varlen_bwd_dq_kernel(const __grid_cons
   const int t_hi = min(q0 + 127, p.L - 1) / 128;
   const int n = t_hi - t_lo + 1;
 
-  if (threadIdx.x == 0) init_bwd_bars(bars, 1);
+  if (threadIdx.x == 0) {
+    mbar_init(&bars->fixed_full, 1);
+    for (int s = 0; s < 3; ++s) {
+      mbar_init(&bars->k_full[s], 1);
+      mbar_init(&bars->k_empty[s], 1);
+    }
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&bars->v_full[s], 1);
+      mbar_init(&bars->v_empty[s], 1);
+      mbar_init(&bars->s_full[s], 1);
+      for (int c = 0; c < 4; ++c) mbar_init(&bars->chunk[s][c], 4);
+    }
+    mbar_init(&bars->dp_full, 1);
+    mbar_init(&bars->dp_loaded, 8);
+    mbar_init(&bars->acc_full, 1);
+    fence_barrier_init();
+  }
   if (warp == 1) tmem_alloc(&bars->tmem_base, 512);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tbase = bars->tmem_base;
-  const uint32_t t_dq = tbase + 256;
+  const uint32_t t_p = tbase + 256, t_dq = tbase + 384;
 
   if (warp == 0) {
     if (lane == 0) {
@@ -155,15 +175,16 @@ __global__ void __launch_bounds__(320, 1) varlen_bwd_dq_kernel(const __grid_cons
         tma_load_3d(dos + cb * C::BOX, &dom, &bars->fixed_full, cb * 64, h, q0);
       }
       for (int j = 0; j < n; ++j) {
-        const int s = j & 1;
-        if (!mbar_wait(&bars->ring_empty[s], ((j >> 1) & 1) ^ 1, kDevTimeoutEmpty)) break;
+        const int ks = j % 3, vsl = j & 1;
         const int kv0 = (t_lo + j) * 128;
-        mbar_arrive_expect_tx(&bars->ring_full[s], C::TILE);
+        if (!mbar_wait(&bars->k_empty[ks], ((j / 3) & 1) ^ 1, kDevTimeoutEmpty)) break;
+        mbar_arrive_expect_tx(&bars->k_full[ks], C::TILE);
         for (int cb = 0; cb < C::NCB; ++cb)
-          tma_load_3d(ks + s * C::TILE + cb * C::BOX, &kmap, &bars->ring_full[s], cb * 64, kvh, kv0);
-        mbar_arrive_expect_tx(&bars->ring_v_full[s], C::TILE);
+          tma_load_3d(kring + ks * C::TILE + cb * C::BOX, &kmap, &bars->k_full[ks], cb * 64, kvh, kv0);
+        if (!mbar_wait(&bars->v_empty[vsl], ((j >> 1) & 1) ^ 1, kDevTimeoutEmpty)) break;
+        mbar_arrive_expect_tx(&bars->v_full[vsl], C::TILE);
         for (int cb = 0; cb < C::NCB; ++cb)
-          tma_load_3d(vs + s * C::TILE + cb * C::BOX, &vmap, &bars->ring_v_full[s], cb * 64, kvh, kv0);
+          tma_load_3d(vring + vsl * C::TILE + cb * C::BOX, &vmap, &bars->v_full[vsl], cb * 64, kvh, kv0);
       }
     }
   } else if (warp == 1) {
@@ -172,41 +193,51 @@ __global__ void __launch_bounds__(320, 1) varlen_bwd_dq_kernel(const __grid_cons
       constexpr uint32_t ID_DQ = umma_idesc_bf16(128, HD, 0, 1);
       bool ok = mbar_wait(&bars->fixed_full, 0, kDevTimeoutFull);
       const uint32_t qa = smem_u32(qs), da = smem_u32(dos);
-      auto issue_s = [&](int j) {
-        const int s = j & 1;
-        if (!mbar_wait(&bars->ring_full[s], (j >> 1) & 1, kDevTimeoutFull)) return false;
+      auto issue_s = [&](int j) {  // S(j) = Q K_j^T into region j & 1
+        const int ks = j % 3;
+        if (!mbar_wait(&bars->k_full[ks], (j / 3) & 1, kDevTimeoutFull)) return false;
         tc_fence_after();
-        mma_kmajor_ss<HD>(tbase + 128 * s, qa, smem_u32(ks + s * C::TILE), ID_S);
-        umma_commit(&bars->s_full[s]);
+        mma_kmajor_ss<HD>(tbase + 128 * (j & 1), qa, smem_u32(kring + ks * C::TILE), ID_S);
+        umma_commit(&bars->s_full[j & 1]);
+        return true;
+      };
+      auto issue_dp = [&](int j) {  // dP(j) = dO V_j^T; V_j is free once it completes
+        const int vsl = j & 1;
+        if (!mbar_wait(&bars->v_full[vsl], (j >> 1) & 1, kDevTimeoutFull)) return false;
+        tc_fence_after();
+        mma_kmajor_ss<HD>(t_p, da, smem_u32(vring + vsl * C::TILE), ID_S);
+        umma_commit(&bars->dp_full);
+        umma_commit(&bars->v_empty[vsl]);
         return true;
       };
       tc_fence_after();
       if (ok) ok = issue_s(0);
       if (ok && n > 1) ok = issue_s(1);
-      for (int j0 = 0; ok && j0 < n; j0 += 2) {
-        for (int j = j0; ok && j < min(j0 + 2, n); ++j) {
-          const int s = j & 1;
-          ok = mbar_wait(&bars->ew1[s], (j >> 1) & 1, kDevTimeoutFull) &&
-               mbar_wait(&bars->ring_v_full[s], (j >> 1) & 1, kDevTimeoutFull);
-          if (!ok) break;
+      if (ok) ok = issue_dp(0);
+      for (int j = 0; ok && j < n; ++j) {
+        if (!(ok = mbar_wait(&bars->dp_loaded, j & 1, kDevTimeoutFull))) break;
+        tc_fence_after();
+        if (j + 1 < n && !(ok = issue_dp(j + 1))) break;
+        const uint32_t ts = tbase + 128 * (j & 1);
+        const uint64_t kdesc = umma_desc_sw128(smem_u32(kring + (j % 3) * C::TILE), C::BOX, 1024);
+        for (int i = 0; ok && i < 4; ++i) {
+          const int ci = chunk_order(i);
+          if (!(ok = mbar_wait(&bars->chunk[j & 1][ci], (j >> 1) & 1, kDevTimeoutFull))) break;
           tc_fence_after();
-          mma_kmajor_ss<HD>(tbase + 128 * s, da, smem_u32(vs + s * C::TILE), ID_S);  // dP = dO V^T
-          umma_commit(&bars->dp_full[s]);
+#pragma unroll 1
+          for (int kk = 2 * ci; kk < 2 * ci + 2; ++kk)  // dQ += dS K over keys [16kk, 16kk + 16)
+            umma_ts(t_dq, ts + a_col(kk), kdesc + (uint64_t)((kk * 2048) >> 4), ID_DQ,
+                    (j > 0 || kk > 0) ? 1u : 0u);
         }
-        for (int j = j0; ok && j < min(j0 + 2, n); ++j) {
-          const int s = j & 1;
-          if (!(ok = mbar_wait(&bars->ew2[s], (j >> 1) & 1, kDevTimeoutFull))) break;
-          tc_fence_after();
-          mma_tmem_a<HD>(t_dq, tbase + 128 * s, smem_u32(ks + s * C::TILE), ID_DQ, j > 0);  // dQ += dS K
-          umma_commit(&bars->ring_empty[s]);
-          if (j + 2 < n) ok = issue_s(j + 2);
-        }
+        if (!ok) break;
+        umma_commit(&bars->k_empty[j % 3]);
+        if (j + 2 < n) ok = issue_s(j + 2);
       }
       umma_commit(&bars->acc_full);
     }
   } else {
-    const int grp = (warp - 2) >> 2;  // stream: even / odd key tiles
-    const int sub = warp & 3;
+    const int hf = (warp - 2) >> 2;  // column half of every 128-column tile
+    const int sub = warp & 3;         // TMEM lane quarter
     const int r = sub * 32 + lane;
     const int q_tok = q0 + r;
     const bool row_ok = q_tok < p.L;
@@ -214,79 +245,62 @@ __global__ void __launch_bounds__(320, 1) varlen_bwd_dq_kernel(const __grid_cons
     const float neg_lse = row_ok ? -p.lse[(size_t)h * p.L + q_tok] : 0.f;
     const float dlt = row_ok ? p.delta[(size_t)h * p.L + q_tok] : 0.f;
     const uint32_t lane_bits = (uint32_t)(sub * 32) << 16;
-    const uint32_t t_x = tbase + 128 * grp + lane_bits;
-    const uint32_t t_p = tbase + 384 + 64 * grp + lane_bits;
     bool ok = true;
-    for (int j = grp; j < n; j += 2) {
-      const int kv0 = (t_lo + j) * 128;
-      const uint32_t par = (j >> 1) & 1;
-      if (ok) ok = mbar_wait_warp(&bars->s_full[grp], par, kDevTimeoutFull);
+    for (int j = 0; j < n; ++j) {
+      const int kc0 = (t_lo + j) * 128 + 64 * hf;  // first key of this warp's 64 columns
+      const uint32_t ts = tbase + 128 * (j & 1) + lane_bits + 64 * hf;
+      float pf[64];
+      if (ok) ok = mbar_wait_warp(&bars->s_full[j & 1], (j >> 1) & 1, kDevTimeoutFull);
       tc_fence_after();
       if (ok) {
-        const bool full = row_ok && kv0 >= lo && kv0 + 127 <= q_tok;
-        uint32_t v[128];
-#pragma unroll
-        for (int c = 0; c < 4; ++c) tmem_ld32(t_x + 32 * c, *reinterpret_cast<uint32_t(*)[32]>(v + 32 * c));
+        uint32_t sv[64];
+        tmem_ld32(ts, *reinterpret_cast<uint32_t(*)[32]>(sv));
+        tmem_ld32(ts + 32, *reinterpret_cast<uint32_t(*)[32]>(sv + 32));
         tmem_wait_ld();
 #pragma unroll
-        for (int c = 0; c < 8; ++c) {
-          uint32_t pk[8];
+        for (int c = 0; c < 64; ++c) pf[c] = fast_exp2(fmaf(__uint_as_float(sv[c]), p.scale_log2, neg_lse));
+        if (!(row_ok && kc0 >= lo && kc0 + 63 <= q_tok)) {
 #pragma unroll
-          for (int e = 0; e < 16; e += 2) {
-            const int col = 16 * c + e;
-            float x0 = fast_exp2(fmaf(__uint_as_float(v[col]), p.scale_log2, neg_lse));
-            float x1 = fast_exp2(fmaf(__uint_as_float(v[col + 1]), p.scale_log2, neg_lse));
-            if (!full) {
-              const int kv = kv0 + col;
-              if (!row_ok || kv < lo || kv > q_tok) x0 = 0.f;
-              if (!row_ok || kv + 1 < lo || kv + 1 > q_tok) x1 = 0.f;
-            }
-            pk[e >> 1] = pack_bf16x2(x0, x1);
-          }
-          tmem_st8(t_p + 8 * c, pk);  // P parked in spare TMEM across the dP MMA
+          for (int c = 0; c < 64; ++c)
+            if (!row_ok || kc0 + c < lo || kc0 + c > q_tok) pf[c] = 0.f;
         }
-        tmem_wait_st();
       }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&bars->ew1[grp]);
-      if (ok) ok = mbar_wait_warp(&bars->dp_full[grp], par, kDevTimeoutFull);
+      if (ok) ok = mbar_wait_warp(&bars->dp_full, j & 1, kDevTimeoutFull);
       tc_fence_after();
+      uint32_t dv[64];
       if (ok) {
-#pragma unroll
-        for (int hf = 0; hf < 2; ++hf) {
-          uint32_t v[64], pp[32];
-          tmem_ld32(t_x + 64 * hf, *reinterpret_cast<uint32_t(*)[32]>(v));
-          tmem_ld32(t_x + 64 * hf + 32, *reinterpret_cast<uint32_t(*)[32]>(v + 32));
-          tmem_ld32(t_p + 32 * hf, pp);
-          tmem_wait_ld();
-#pragma unroll
-          for (int c = 0; c < 4; ++c) {
-            uint32_t pk[8];
-#pragma unroll
-            for (int e = 0; e < 16; e += 2) {
-              const int col = 16 * c + e;
-              const float2 pf = unpack_bf16x2(pp[col >> 1]);
-              pk[e >> 1] = pack_bf16x2(pf.x * (__uint_as_float(v[col]) - dlt),
-                                       pf.y * (__uint_as_float(v[col + 1]) - dlt));
-            }
-            tmem_st8(t_x + 32 * hf + 8 * c, pk);  // dS over dP columns already read
-          }
-        }
-        tmem_wait_st();
+        tmem_ld32(t_p + lane_bits + 64 * hf, *reinterpret_cast<uint32_t(*)[32]>(dv));
+        tmem_ld32(t_p + lane_bits + 64 * hf + 32, *reinterpret_cast<uint32_t(*)[32]>(dv + 32));
+        tmem_wait_ld();
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&bars->ew2[grp]);
+      if (lane == 0) mbar_arrive(&bars->dp_loaded);
+#pragma unroll
+      for (int c2 = 0; c2 < 2; ++c2) {
+        if (ok) {
+          uint32_t ds[16];
+#pragma unroll
+          for (int e = 0; e < 16; ++e) {
+            const int c = 32 * c2 + 2 * e;
+            ds[e] = pack_bf16x2(pf[c] * (__uint_as_float(dv[c]) - dlt), pf[c + 1] * (__uint_as_float(dv[c + 1]) - dlt));
+          }
+          tmem_st16(ts + 16 * c2, ds);  // over S columns this warp already read
+          tmem_wait_st();
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bars->chunk[j & 1][2 * hf + c2]);
+      }
     }
-    // Epilogue: stream 0 writes dQ columns [0, HD/2), stream 1 [HD/2, HD).
+    // Epilogue: half 0 writes dQ columns [0, HD/2), half 1 [HD/2, HD).
     if (ok) ok = mbar_wait_warp(&bars->acc_full, 0, kDevTimeoutFull);
     tc_fence_after();
     if (ok) {
       __nv_bfloat16* dst = p.dq + ((size_t)q_tok * p.Hq + h) * HD;
 #pragma unroll
       for (int c = 0; c < HD / 64; ++c) {
-        const int col = grp * (HD / 2) + 32 * c;
+        const int col = hf * (HD / 2) + 32 * c;
         uint32_t v[32];
         tmem_ld32(t_dq + lane_bits + col, v);
         tmem_wait_ld();
@@ -315,6 +329,16 @@ __global__ void __launch_bounds__(320, 1) varlen_bwd_dq_kernel(const __grid_cons
 }
 
 // ---------------------------------------------------------------- dkdv kernel
+struct DkdvBars {
+  uint64_t fixed_full;  // K, V
+  uint64_t q_full[3], q_empty[3], d_full[2], d_empty[2];
+  uint64_t s_full, dp_full;  // S^T(t), dP^T(t)
+  uint64_t s_loaded;         // element-wise warps hold S^T(t) in registers
+  uint64_t chunk[4];         // bf16 P^T / dS^T chunk c of the current item ready
+  uint64_t acc_full;
+  uint32_t tmem_base;
+};
+
 template <int HD>
 __global__ void __launch_bounds__(320, 1) varlen_bwd_dkdv_kernel(const __grid_constant__ CUtensorMap qmap,
                                                                 const __grid_constant__ CUtensorMap kmap,
@@ -322,18 +346,20 @@ __global__ void __launch_bounds__(320, 1) varlen_bwd_dkdv_kernel(const __grid_co
                                                                 const __grid_constant__ CUtensorMap dom,
                                                                 const VarlenBwdParams p) {
   using C = BwdTile<HD>;
-  constexpr int VEC = 2 * 128 * 4;  // lse + delta of one query tile (f32)
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  extern __shared__ __align__(1024) uint8_t smem[];
+  if (!smem_base_aligned(smem)) {
+    if (threadIdx.x == 0) report(kDevBadSmem);
+    return;
+  }
   uint8_t* ks = smem;
   uint8_t* vs = smem + C::TILE;
-  uint8_t* qring = smem + 2 * C::TILE;     // [2][TILE]
-  uint8_t* dring = smem + 4 * C::TILE;     // [2][TILE]
-  float* vecs = reinterpret_cast<float*>(smem + 6 * C::TILE);  // [2][2][128]
-  BwdBars* bars = reinterpret_cast<BwdBars*>(smem + 6 * C::TILE + 2 * VEC);
+  uint8_t* qring = smem + 2 * C::TILE;  // [3][TILE]
+  uint8_t* dring = smem + 5 * C::TILE;  // [2][TILE]
+  float* lse_ring = reinterpret_cast<float*>(smem + 7 * C::TILE);  // [3][128], with the Q slot
+  float* dlt_ring = lse_ring + 3 * 128;                             // [2][128], with the dO slot
+  DkdvBars* bars = reinterpret_cast<DkdvBars*>(dlt_ring + 2 * 128);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int n_kt = (p.L + 127) / 128;
   const int kt = (int)blockIdx.x;
   const int kv0 = kt * 128;
   const int kvh = blockIdx.y;
@@ -341,16 +367,31 @@ __global__ void __launch_bounds__(320, 1) varlen_bwd_dkdv_kernel(const __grid_co
   const int i_lo = kt;
   const int i_hi = (p.run_end[last] - 1) / 128;
   const int nqi = i_hi - i_lo + 1;
-  const int n = p.G * nqi;  // (q-head, query tile) pairs
-  (void)n_kt;
+  const int n = p.G * nqi;  // (q-head, query tile) items
 
-  if (threadIdx.x == 0) init_bwd_bars(bars, 2);
+  if (threadIdx.x == 0) {
+    mbar_init(&bars->fixed_full, 1);
+    for (int s = 0; s < 3; ++s) {
+      mbar_init(&bars->q_full[s], 2);  // TMA bytes + the lse staging arrive
+      mbar_init(&bars->q_empty[s], 1);
+    }
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&bars->d_full[s], 2);  // TMA bytes + the delta staging arrive
+      mbar_init(&bars->d_empty[s], 1);
+    }
+    mbar_init(&bars->s_full, 1);
+    mbar_init(&bars->dp_full, 1);
+    mbar_init(&bars->s_loaded, 8);
+    for (int c = 0; c < 4; ++c) mbar_init(&bars->chunk[c], 4);
+    mbar_init(&bars->acc_full, 1);
+    fence_barrier_init();
+  }
   if (warp == 1) tmem_alloc(&bars->tmem_base, 512);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tbase = bars->tmem_base;
-  const uint32_t t_dv = tbase + 256, t_dk = tbase + 256 + HD;
+  const uint32_t t_s = tbase, t_x = tbase + 128, t_dv = tbase + 256, t_dk = tbase + 256 + HD;
 
   if (warp == 0) {
     // Producer warp: lane 0 issues TMA; all lanes stage lse / delta.
@@ -367,27 +408,37 @@ __global__ void __launch_bounds__(320, 1) varlen_bwd_dkdv_kernel(const __grid_co
     }
     bool ok = true;
     for (int t = 0; t < n; ++t) {
-      const int s = t & 1;
+      const int qs = t % 3, dsl = t & 1;
       const int hq = kvh * p.G + t / nqi;
       const int q0 = (i_lo + t % nqi) * 128;
-      if (lane == 0) ok = ok && mbar_wait(&bars->ring_empty[s], ((t >> 1) & 1) ^ 1, kDevTimeoutEmpty);
+      if (lane == 0) ok = ok && mbar_wait(&bars->q_empty[qs], ((t / 3) & 1) ^ 1, kDevTimeoutEmpty);
       ok = __shfl_sync(0xffffffffu, ok, 0);
       if (!ok) break;
       if (lane == 0) {
-        mbar_arrive_expect_tx(&bars->ring_full[s], 2 * C::TILE);
-        for (int cb = 0; cb < C::NCB; ++cb) {
-          tma_load_3d(qring + s * C::TILE + cb * C::BOX, &qmap, &bars->ring_full[s], cb * 64, hq, q0);
-          tma_load_3d(dring + s * C::TILE + cb * C::BOX, &dom, &bars->ring_full[s], cb * 64, hq, q0);
-        }
+        mbar_arrive_expect_tx(&bars->q_full[qs], C::TILE);
+        for (int cb = 0; cb < C::NCB; ++cb)
+          tma_load_3d(qring + qs * C::TILE + cb * C::BOX, &qmap, &bars->q_full[qs], cb * 64, hq, q0);
       }
-      float* lse_s = vecs + s * 256;
       for (int c = lane; c < 128; c += 32) {
         const int q = q0 + c;
-        lse_s[c] = (q < p.L) ? p.lse[(size_t)hq * p.L + q] : INFINITY;
-        lse_s[128 + c] = (q < p.L) ? p.delta[(size_t)hq * p.L + q] : 0.f;
+        lse_ring[qs * 128 + c] = (q < p.L) ? p.lse[(size_t)hq * p.L + q] : INFINITY;
       }
       __syncwarp();
-      if (lane == 0) mbar_arrive(&bars->ring_full[s]);
+      if (lane == 0) mbar_arrive(&bars->q_full[qs]);
+      if (lane == 0) ok = mbar_wait(&bars->d_empty[dsl], ((t >> 1) & 1) ^ 1, kDevTimeoutEmpty);
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      if (!ok) break;
+      if (lane == 0) {
+        mbar_arrive_expect_tx(&bars->d_full[dsl], C::TILE);
+        for (int cb = 0; cb < C::NCB; ++cb)
+          tma_load_3d(dring + dsl * C::TILE + cb * C::BOX, &dom, &bars->d_full[dsl], cb * 64, hq, q0);
+      }
+      for (int c = lane; c < 128; c += 32) {
+        const int q = q0 + c;
+        dlt_ring[dsl * 128 + c] = (q < p.L) ? p.delta[(size_t)hq * p.L + q] : 0.f;
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bars->d_full[dsl]);
     }
   } else if (warp == 1) {
     if (lane == 0) {
@@ -395,113 +446,136 @@ __global__ void __launch_bounds__(320, 1) varlen_bwd_dkdv_kernel(const __grid_co
       constexpr uint32_t ID_G = umma_idesc_bf16(128, HD, 0, 1);
       bool ok = mbar_wait(&bars->fixed_full, 0, kDevTimeoutFull);
       const uint32_t ka = smem_u32(ks), va = smem_u32(vs);
-      auto issue_s = [&](int t) {
-        const int s = t & 1;
-        if (!mbar_wait(&bars->ring_full[s], (t >> 1) & 1, kDevTimeoutFull)) return false;
+      auto issue_s = [&](int t) {  // S^T(t) = K Q_t^T
+        const int qs = t % 3;
+        if (!mbar_wait(&bars->q_full[qs], (t / 3) & 1, kDevTimeoutFull)) return false;
         tc_fence_after();
-        mma_kmajor_ss<HD>(tbase + 128 * s, ka, smem_u32(qring + s * C::TILE), ID_S);  // S^T = K Q^T
-        umma_commit(&bars->s_full[s]);
+        mma_kmajor_ss<HD>(t_s, ka, smem_u32(qring + qs * C::TILE), ID_S);
+        umma_commit(&bars->s_full);
+        return true;
+      };
+      auto issue_dp = [&](int t) {  // dP^T(t) = V dO_t^T
+        const int dsl = t & 1;
+        if (!mbar_wait(&bars->d_full[dsl], (t >> 1) & 1, kDevTimeoutFull)) return false;
+        tc_fence_after();
+        mma_kmajor_ss<HD>(t_x, va, smem_u32(dring + dsl * C::TILE), ID_S);
+        umma_commit(&bars->dp_full);
         return true;
       };
       tc_fence_after();
       if (ok) ok = issue_s(0);
-      if (ok && n > 1) ok = issue_s(1);
-      for (int t0 = 0; ok && t0 < n; t0 += 2) {
-        for (int t = t0; ok && t < min(t0 + 2, n); ++t) {
-          const int s = t & 1;
-          if (!(ok = mbar_wait(&bars->ew1[s], (t >> 1) & 1, kDevTimeoutFull))) break;
+      if (ok) ok = issue_dp(0);
+      for (int t = 0; ok && t < n; ++t) {
+        if (!(ok = mbar_wait(&bars->s_loaded, t & 1, kDevTimeoutFull))) break;
+        tc_fence_after();
+        if (t + 1 < n && !(ok = issue_s(t + 1))) break;
+        const uint64_t ddesc = umma_desc_sw128(smem_u32(dring + (t & 1) * C::TILE), C::BOX, 1024);
+        const uint64_t qdesc = umma_desc_sw128(smem_u32(qring + (t % 3) * C::TILE), C::BOX, 1024);
+        for (int i = 0; ok && i < 4; ++i) {
+          const int ci = chunk_order(i);
+          if (!(ok = mbar_wait(&bars->chunk[ci], t & 1, kDevTimeoutFull))) break;
           tc_fence_after();
-          mma_kmajor_ss<HD>(tbase + 128 * s, va, smem_u32(dring + s * C::TILE), ID_S);  // dP^T = V dO^T
-          umma_commit(&bars->dp_full[s]);
+#pragma unroll 1
+          for (int kk = 2 * ci; kk < 2 * ci + 2; ++kk) {  // queries [16kk, 16kk + 16)
+            const uint32_t acc = (t > 0 || kk > 0) ? 1u : 0u;
+            const uint64_t boff = (uint64_t)((kk * 2048) >> 4);
+            umma_ts(t_dv, t_x + pt_col(kk), ddesc + boff, ID_G, acc);       // dV += P^T dO
+            umma_ts(t_dk, t_x + pt_col(kk) + 16, qdesc + boff, ID_G, acc);  // dK += dS^T Q
+          }
         }
-        for (int t = t0; ok && t < min(t0 + 2, n); ++t) {
-          const int s = t & 1;
-          if (!(ok = mbar_wait(&bars->ew2[s], (t >> 1) & 1, kDevTimeoutFull))) break;
-          tc_fence_after();
-          mma_tmem_a<HD>(t_dv, tbase + 128 * s + 64, smem_u32(dring + s * C::TILE), ID_G, t > 0);  // dV += P^T dO
-          mma_tmem_a<HD>(t_dk, tbase + 128 * s, smem_u32(qring + s * C::TILE), ID_G, t > 0);       // dK += dS^T Q
-          umma_commit(&bars->ring_empty[s]);
-          if (t + 2 < n) ok = issue_s(t + 2);
-        }
+        if (!ok) break;
+        umma_commit(&bars->q_empty[t % 3]);
+        umma_commit(&bars->d_empty[t & 1]);
+        if (t + 1 < n) ok = issue_dp(t + 1);
       }
       umma_commit(&bars->acc_full);
     }
   } else {
-    const int grp = (warp - 2) >> 2;
-    const int sub = warp & 3;
+    const int hf = (warp - 2) >> 2;  // column half of every 128-column tile
+    const int sub = warp & 3;         // TMEM lane quarter
     const int r = sub * 32 + lane;
     const int k_tok = kv0 + r;
     const bool k_ok = k_tok < p.L;
     const int q_end = k_ok ? p.run_end[k_tok] : 0;  // queries k_tok <= q < q_end see this key
     const uint32_t lane_bits = (uint32_t)(sub * 32) << 16;
-    const uint32_t t_x = tbase + 128 * grp + lane_bits;
+    const uint32_t ts = t_s + lane_bits + 64 * hf, tx = t_x + lane_bits + 64 * hf;
     bool ok = true;
-    for (int t = grp; t < n; t += 2) {
-      const int s = t & 1;
-      const int q0 = (i_lo + t % nqi) * 128;
-      const uint32_t par = (t >> 1) & 1;
-      if (ok) ok = mbar_wait_warp(&bars->ring_full[s], par, kDevTimeoutFull);
-      if (ok) ok = mbar_wait_warp(&bars->s_full[s], par, kDevTimeoutFull);
+    for (int t = 0; t < n; ++t) {
+      const int qc0 = (i_lo + t % nqi) * 128 + 64 * hf;  // first query of this warp's 64 columns
+      uint32_t pk[32];  // P^T as bf16 pairs (the precision the dV MMA takes it in)
+      if (ok) ok = mbar_wait_warp(&bars->q_full[t % 3], (t / 3) & 1, kDevTimeoutFull);
+      if (ok) ok = mbar_wait_warp(&bars->s_full, t & 1, kDevTimeoutFull);
       tc_fence_after();
-      const float* lse_s = vecs + s * 256;
-      uint32_t pr[64];  // P^T as bf16 pairs, kept across the dP^T MMA
+      uint32_t sv[64];
       if (ok) {
-        const bool full = k_ok && q0 >= k_tok && q0 + 127 < q_end;
+        tmem_ld32(ts, *reinterpret_cast<uint32_t(*)[32]>(sv));
+        tmem_ld32(ts + 32, *reinterpret_cast<uint32_t(*)[32]>(sv + 32));
+        tmem_wait_ld();
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bars->s_loaded);
+      if (ok) {
+        const float4* l4 = reinterpret_cast<const float4*>(lse_ring + (t % 3) * 128 + 64 * hf);
+        const bool full = k_ok && qc0 >= k_tok && qc0 + 63 < q_end;
 #pragma unroll
-        for (int c = 0; c < 8; ++c) {
-          uint32_t v[16];
-          tmem_ld16(t_x + 16 * c, v);
-          tmem_wait_ld();
+        for (int c4 = 0; c4 < 16; ++c4) {
+          const float4 l = l4[c4];
+          float x[4];
+          x[0] = fast_exp2(fmaf(__uint_as_float(sv[4 * c4 + 0]), p.scale_log2, -l.x));
+          x[1] = fast_exp2(fmaf(__uint_as_float(sv[4 * c4 + 1]), p.scale_log2, -l.y));
+          x[2] = fast_exp2(fmaf(__uint_as_float(sv[4 * c4 + 2]), p.scale_log2, -l.z));
+          x[3] = fast_exp2(fmaf(__uint_as_float(sv[4 * c4 + 3]), p.scale_log2, -l.w));
+          if (!full) {
 #pragma unroll
-          for (int e = 0; e < 16; e += 2) {
-            const int col = 16 * c + e;
-            float x0 = fast_exp2(fmaf(__uint_as_float(v[e]), p.scale_log2, -lse_s[col]));
-            float x1 = fast_exp2(fmaf(__uint_as_float(v[e + 1]), p.scale_log2, -lse_s[col + 1]));
-            if (!full) {
-              const int q = q0 + col;
-              if (q < k_tok || q >= q_end) x0 = 0.f;
-              if (q + 1 < k_tok || q + 1 >= q_end) x1 = 0.f;
+            for (int e = 0; e < 4; ++e) {
+              const int q = qc0 + 4 * c4 + e;
+              if (q < k_tok || q >= q_end) x[e] = 0.f;
             }
-            pr[col >> 1] = pack_bf16x2(x0, x1);
           }
+          pk[2 * c4] = pack_bf16x2(x[0], x[1]);
+          pk[2 * c4 + 1] = pack_bf16x2(x[2], x[3]);
         }
       }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&bars->ew1[s]);
-      if (ok) ok = mbar_wait_warp(&bars->dp_full[s], par, kDevTimeoutFull);
+      if (ok) ok = mbar_wait_warp(&bars->d_full[t & 1], (t >> 1) & 1, kDevTimeoutFull);
+      if (ok) ok = mbar_wait_warp(&bars->dp_full, t & 1, kDevTimeoutFull);
       tc_fence_after();
-      if (ok) {
 #pragma unroll
-        for (int c = 0; c < 8; ++c) {
-          uint32_t v[16];
-          tmem_ld16(t_x + 16 * c, v);
+      for (int c2 = 0; c2 < 2; ++c2) {
+        if (ok) {
+          uint32_t dv[32];
+          tmem_ld32(tx + 32 * c2, dv);
           tmem_wait_ld();
-          uint32_t pk[8];
+          const float4* d4 = reinterpret_cast<const float4*>(dlt_ring + (t & 1) * 128 + 64 * hf + 32 * c2);
+          uint32_t pp[16], ds[16];
 #pragma unroll
-          for (int e = 0; e < 16; e += 2) {
-            const int col = 16 * c + e;
-            const float2 pf = unpack_bf16x2(pr[col >> 1]);
-            pk[e >> 1] = pack_bf16x2(pf.x * (__uint_as_float(v[e]) - lse_s[128 + col]),
-                                     pf.y * (__uint_as_float(v[e + 1]) - lse_s[128 + col + 1]));
+          for (int e4 = 0; e4 < 8; ++e4) {
+            const float4 d = d4[e4];
+            pp[2 * e4] = pk[16 * c2 + 2 * e4];
+            pp[2 * e4 + 1] = pk[16 * c2 + 2 * e4 + 1];
+            const float2 p01 = unpack_bf16x2(pp[2 * e4]), p23 = unpack_bf16x2(pp[2 * e4 + 1]);
+            ds[2 * e4] = pack_bf16x2(p01.x * (__uint_as_float(dv[4 * e4]) - d.x),
+                                     p01.y * (__uint_as_float(dv[4 * e4 + 1]) - d.y));
+            ds[2 * e4 + 1] = pack_bf16x2(p23.x * (__uint_as_float(dv[4 * e4 + 2]) - d.z),
+                                         p23.y * (__uint_as_float(dv[4 * e4 + 3]) - d.w));
           }
-          tmem_st8(t_x + 8 * c, pk);  // dS^T over dP^T columns already read
+          // Over the 32 dP^T columns just read: P^T at [0, 16), dS^T at [16, 32).
+          tmem_st16(tx + 32 * c2, pp);
+          tmem_st16(tx + 32 * c2 + 16, ds);
+          tmem_wait_st();
         }
-#pragma unroll
-        for (int c = 0; c < 4; ++c) tmem_st16(t_x + 64 + 16 * c, *reinterpret_cast<uint32_t(*)[16]>(pr + 16 * c));
-        tmem_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bars->chunk[2 * hf + c2]);
       }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&bars->ew2[s]);
     }
-    // Epilogue: stream 0 writes dV, stream 1 writes dK (scaled).
+    // Epilogue: half 0 writes dV, half 1 writes dK (scaled).
     if (ok) ok = mbar_wait_warp(&bars->acc_full, 0, kDevTimeoutFull);
     tc_fence_after();
     if (ok) {
-      const uint32_t src = (grp == 0 ? t_dv : t_dk) + lane_bits;
-      const float mul = (grp == 0) ? 1.f : p.scale;
-      __nv_bfloat16* dst = (grp == 0 ? p.dv : p.dk) + ((size_t)k_tok * p.Hkv + kvh) * HD;
+      const uint32_t src = (hf == 0 ? t_dv : t_dk) + lane_bits;
+      const float mul = (hf == 0) ? 1.f : p.scale;
+      __nv_bfloat16* dst = (hf == 0 ? p.dv : p.dk) + ((size_t)k_tok * p.Hkv + kvh) * HD;
 #pragma unroll
       for (int c = 0; c < HD / 32; ++c) {
         uint32_t v[32];
@@ -536,8 +610,8 @@ static cudaError_t launch_bwd_hd(const CUtensorMap& qm, const CUtensorMap& km, c
                                  const CUtensorMap& dom, const VarlenBwdParams& p, cudaStream_t stream) {
   using C = BwdTile<HD>;
   const int n_t = (p.L + 127) / 128;
-  const int smem_dq = 1024 + 6 * C::TILE + (int)sizeof(BwdBars) + 64;
-  const int smem_kv = 1024 + 6 * C::TILE + 2 * 2 * 128 * 4 + (int)sizeof(BwdBars) + 64;
+  const int smem_dq = 7 * C::TILE + (int)sizeof(DqBars);
+  const int smem_kv = 7 * C::TILE + 5 * 128 * 4 + (int)sizeof(DkdvBars);
   cudaError_t e = cudaFuncSetAttribute(varlen_bwd_dkdv_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        smem_kv);
   if (e != cudaSuccess) return e;
