@@ -50,6 +50,88 @@ __device__ __forceinline__ void umma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64
       "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate));
 }
 
+// Warp-wide forms: all 32 lanes execute them (converged) and elect.sync picks
+// the one lane that issues. Running the MMA warp's whole control flow with all
+// lanes keeps descriptors and TMEM addresses warp-uniform, which issues
+// markedly faster than a loop confined to `if (lane == 0)`.
+__device__ __forceinline__ void umma_ss_warp(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                             uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p, e;\n\telect.sync _|e, 0xffffffff;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate));
+}
+
+__device__ __forceinline__ void umma_ts_warp(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                             uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p, e;\n\telect.sync _|e, 0xffffffff;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate));
+}
+
+// One warp-wide asm block per group of MMAs: a single elect.sync, then the
+// K-steps with their descriptor offsets as immediates, so the issuing warp
+// spends a few instructions per MMA (its SM sub-partition is shared with
+// element-wise warps, and a long issue sequence starves the tensor pipe).
+//
+// D = A B^T over 128 (HD = 128: K-steps at 32-byte offsets inside each of two
+// 64-element boxes 16 KB apart) or 64 (one box) elements; A and B K-major
+// SW128 descriptors; the first K-step overwrites D.
+__device__ __forceinline__ void umma_ss_k128_warp(uint32_t d, uint64_t da, uint64_t db, uint32_t idesc) {
+  asm volatile(
+      "{\n\t.reg .pred e, t, f;\n\t.reg .b64 a, b;\n\t"
+      "elect.sync _|e, 0xffffffff;\n\tsetp.eq.b32 t, %3, %3;\n\tsetp.ne.b32 f, %3, %3;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, f;\n\t"
+      "add.s64 a, %1, 2;\n\tadd.s64 b, %2, 2;\n\t@e tcgen05.mma.cta_group::1.kind::f16 [%0], a, b, %3, t;\n\t"
+      "add.s64 a, %1, 4;\n\tadd.s64 b, %2, 4;\n\t@e tcgen05.mma.cta_group::1.kind::f16 [%0], a, b, %3, t;\n\t"
+      "add.s64 a, %1, 6;\n\tadd.s64 b, %2, 6;\n\t@e tcgen05.mma.cta_group::1.kind::f16 [%0], a, b, %3, t;\n\t"
+      "add.s64 a, %1, 1024;\n\tadd.s64 b, %2, 1024;\n\t@e tcgen05.mma.cta_group::1.kind::f16 [%0], a, b, %3, t;\n\t"
+      "add.s64 a, %1, 1026;\n\tadd.s64 b, %2, 1026;\n\t@e tcgen05.mma.cta_group::1.kind::f16 [%0], a, b, %3, t;\n\t"
+      "add.s64 a, %1, 1028;\n\tadd.s64 b, %2, 1028;\n\t@e tcgen05.mma.cta_group::1.kind::f16 [%0], a, b, %3, t;\n\t"
+      "add.s64 a, %1, 1030;\n\tadd.s64 b, %2, 1030;\n\t@e tcgen05.mma.cta_group::1.kind::f16 [%0], a, b, %3, t;\n\t}"
+      ::"r"(d), "l"(da), "l"(db), "r"(idesc));
+}
+
+__device__ __forceinline__ void umma_ss_k64_warp(uint32_t d, uint64_t da, uint64_t db, uint32_t idesc) {
+  asm volatile(
+      "{\n\t.reg .pred e, t, f;\n\t.reg .b64 a, b;\n\t"
+      "elect.sync _|e, 0xffffffff;\n\tsetp.eq.b32 t, %3, %3;\n\tsetp.ne.b32 f, %3, %3;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, f;\n\t"
+      "add.s64 a, %1, 2;\n\tadd.s64 b, %2, 2;\n\t@e tcgen05.mma.cta_group::1.kind::f16 [%0], a, b, %3, t;\n\t"
+      "add.s64 a, %1, 4;\n\tadd.s64 b, %2, 4;\n\t@e tcgen05.mma.cta_group::1.kind::f16 [%0], a, b, %3, t;\n\t"
+      "add.s64 a, %1, 6;\n\tadd.s64 b, %2, 6;\n\t@e tcgen05.mma.cta_group::1.kind::f16 [%0], a, b, %3, t;\n\t}"
+      ::"r"(d), "l"(da), "l"(db), "r"(idesc));
+}
+
+// D (+)= A B over 128 tokens: A bf16 in TMEM, 16 tokens per K-step packed in
+// 8 columns, the K-steps of token block kk at column 64 * (kk / 4) + 8 * (kk % 4)
+// (two 64-token halves, each packed into its first 32 columns); B MN-major
+// SW128 (16 token rows = 2048 bytes per K-step). `accumulate` applies to the
+// first K-step only.
+__device__ __forceinline__ void umma_ts_t128_warp(uint32_t d, uint32_t a, uint64_t db, uint32_t idesc,
+                                                  uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred e, t, p;\n\t.reg .b32 ta;\n\t.reg .b64 b;\n\t"
+      "elect.sync _|e, 0xffffffff;\n\tsetp.eq.b32 t, %3, %3;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t"
+      "add.u32 ta, %1, 8;\n\tadd.s64 b, %2, 128;\n\t@e tcgen05.mma.cta_group::1.kind::f16 [%0], [ta], b, %3, t;\n\t"
+      "add.u32 ta, %1, 16;\n\tadd.s64 b, %2, 256;\n\t@e tcgen05.mma.cta_group::1.kind::f16 [%0], [ta], b, %3, t;\n\t"
+      "add.u32 ta, %1, 24;\n\tadd.s64 b, %2, 384;\n\t@e tcgen05.mma.cta_group::1.kind::f16 [%0], [ta], b, %3, t;\n\t"
+      "add.u32 ta, %1, 64;\n\tadd.s64 b, %2, 512;\n\t@e tcgen05.mma.cta_group::1.kind::f16 [%0], [ta], b, %3, t;\n\t"
+      "add.u32 ta, %1, 72;\n\tadd.s64 b, %2, 640;\n\t@e tcgen05.mma.cta_group::1.kind::f16 [%0], [ta], b, %3, t;\n\t"
+      "add.u32 ta, %1, 80;\n\tadd.s64 b, %2, 768;\n\t@e tcgen05.mma.cta_group::1.kind::f16 [%0], [ta], b, %3, t;\n\t"
+      "add.u32 ta, %1, 88;\n\tadd.s64 b, %2, 896;\n\t@e tcgen05.mma.cta_group::1.kind::f16 [%0], [ta], b, %3, t;\n\t}"
+      ::"r"(d), "r"(a), "l"(db), "r"(idesc), "r"(accumulate));
+}
+
+__device__ __forceinline__ void umma_commit_warp(uint64_t* bar) {
+  asm volatile(
+      "{\n\t.reg .pred e;\n\telect.sync _|e, 0xffffffff;\n\t"
+      "@e tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n\t}" ::"r"(smem_u32(bar))
+      : "memory");
+}
+
 // Arrive on `bar` once every tcgen05 operation this thread issued so far is done.
 __device__ __forceinline__ void umma_commit(uint64_t* bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))

@@ -12,18 +12,24 @@
 //  * dkdv:   one CTA per (128-key tile, kv-head), walking every (q-head of the
 //            group, 128-query tile) item whose queries may see its keys. Keys
 //            sit on the TMEM lanes: S^T = K Q^T and dP^T = V dO^T land in two
-//            128-column regions; the element-wise warps turn them into P^T and
-//            dS^T (bf16, written back over the dP^T columns they read) and
-//            dV += P^T dO, dK += dS^T Q accumulate in TMEM over the walk.
+//            128-column regions; the element-wise warps write P^T (bf16) over
+//            the S^T columns they read and dS^T over the dP^T columns, and
+//            dV += P^T dO, dK += dS^T Q accumulate in TMEM over the walk. The
+//            MMA order per item is dV(t), S^T(t+1), dK(t), dP^T(t+1), so the
+//            P phase of one item overlaps the dK and dP^T MMAs and its dS
+//            phase the dV and S^T MMAs.
 //  * dq:     one CTA per (128-query tile, q-head), walking the key tiles the
 //            forward visits: S = Q K^T (double-buffered in TMEM), dP = dO V^T,
 //            dS (bf16, over the S columns it came from), dQ += dS K.
 //
 // Pipelining (one item stream per CTA, every MMA 128 x 128 or 128 x HD wide):
-//  * The element-wise warps read S early and signal once it is in registers,
-//    so the next item's S MMA overlaps this item's exponentials; they signal
-//    the dP read the same way (dq) and hand the bf16 operands over in four
-//    32-column chunks, each releasing two K-steps of the dV/dK (dQ) MMAs.
+//  * The element-wise warps signal once per phase (one mbarrier arrive per
+//    warp); in dq they also signal once dP is in registers so the next item's
+//    dP MMA can start.
+//  * The MMA warp runs its loop with all 32 lanes and issues through
+//    elect.sync, and it waits on a barrier only after queuing a full group of
+//    8 MMAs: each wait costs the issuing warp a few hundred cycles, which the
+//    queued MMAs cover.
 //  * The operand needed first (Q in dkdv, K in dq) has a 3-slot TMA ring, the
 //    other (dO, V) a 2-slot ring, so loads run an item or more ahead.
 //  * tcgen05.mma operations of one CTA execute in issue order, so an MMA may
@@ -66,33 +72,28 @@ __global__ void bwd_delta_kernel(const __nv_bfloat16* __restrict__ out, const __
 }
 
 // ---------------------------------------------------------------- shared pieces
-// D = A B^T over HD; A and B K-major in smem (128 rows x HD). The start
-// address is the descriptor's low field, so K-steps add (offset >> 4) to the
-// 64-bit descriptor (shared-memory addresses stay below 2^18, no carry).
-// Issue loops stay rolled to keep the issuing warp's registers few.
+// D = A B^T over HD; A and B K-major in smem (128 rows x HD); issued by the
+// whole MMA warp as one straight-line group.
 template <int HD>
 __device__ __forceinline__ void mma_kmajor_ss(uint32_t d, uint32_t a_base, uint32_t b_base, uint32_t idesc) {
   const uint64_t da = umma_desc_sw128(a_base, 16, 1024), db = umma_desc_sw128(b_base, 16, 1024);
-#pragma unroll 1
-  for (int kk = 0; kk < HD / 16; ++kk) {
-    const uint32_t off = ((kk >> 2) * BwdTile<HD>::BOX + (kk & 3) * 32) >> 4;
-    umma_ss(d, da + off, db + off, idesc, kk > 0);
-  }
+  if constexpr (HD == 128)
+    umma_ss_k128_warp(d, da, db, idesc);
+  else
+    umma_ss_k64_warp(d, da, db, idesc);
 }
 
-// TMEM column (relative to a 128-column region) of the bf16 A operand for
-// K-step kk (16 tokens): element-wise warp half h = kk / 4 writes its 64
-// tokens packed into columns [64h, 64h + 32) of the region.
-__device__ __forceinline__ uint32_t a_col(int kk) { return (uint32_t)(64 * (kk >> 2) + 8 * (kk & 3)); }
+// D (+)= A_tmem[128 x 128 tokens (bf16)] * B[128 tokens x HD], B MN-major in
+// smem; whole MMA warp.
+template <int HD>
+__device__ __forceinline__ void mma_tmem_a(uint32_t d, uint32_t a_tmem, uint32_t b_base, uint32_t idesc,
+                                           bool accumulate) {
+  umma_ts_t128_warp(d, a_tmem, umma_desc_sw128(b_base, BwdTile<HD>::BOX, 1024), idesc, accumulate ? 1u : 0u);
+}
 
-// dkdv: TMEM column of the bf16 P^T for K-step kk (dS^T sits 16 columns
-// further): chunk c = kk / 2 of 32 queries is written over the 32 dP^T columns
-// [32c, 32c + 32) it came from, P^T in the first 16, dS^T in the last 16.
-__device__ __forceinline__ uint32_t pt_col(int kk) { return (uint32_t)(32 * (kk >> 1) + 8 * (kk & 1)); }
-
-// Order in which the MMA warp consumes the four 32-token chunks: the two
-// column halves are produced concurrently, so alternate between them.
-__device__ __forceinline__ int chunk_order(int i) { return ((i & 1) << 1) | (i >> 1); }
+// bf16 A operands in TMEM: element-wise warp half h packs its 64 tokens into
+// columns [64h, 64h + 32) of the 128-column region it read them from, the
+// layout umma_ts_t128_warp consumes.
 
 // Dynamic shared memory is used from its base without padding (the kernels
 // need nearly all 227 KB); the 128-byte-swizzled TMA boxes need the base
@@ -106,7 +107,7 @@ struct DqBars {
   uint64_t s_full[2];   // S(j) in TMEM region j & 1
   uint64_t dp_full;     // dP(j)
   uint64_t dp_loaded;   // element-wise warps hold dP(j) in registers
-  uint64_t chunk[2][4]; // bf16 dS chunk c of item j ready (set j & 1)
+  uint64_t ds_done[2];  // bf16 dS of item j in TMEM (set j & 1)
   uint64_t acc_full;
   uint32_t tmem_base;
 };
@@ -149,7 +150,7 @@ __global__ void __launch_bounds__(320, 1) varlen_bwd_dq_kernel(const __grid_cons
       mbar_init(&bars->v_full[s], 1);
       mbar_init(&bars->v_empty[s], 1);
       mbar_init(&bars->s_full[s], 1);
-      for (int c = 0; c < 4; ++c) mbar_init(&bars->chunk[s][c], 4);
+      mbar_init(&bars->ds_done[s], 8);
     }
     mbar_init(&bars->dp_full, 1);
     mbar_init(&bars->dp_loaded, 8);
@@ -188,53 +189,38 @@ __global__ void __launch_bounds__(320, 1) varlen_bwd_dq_kernel(const __grid_cons
       }
     }
   } else if (warp == 1) {
-    if (lane == 0) {
-      constexpr uint32_t ID_S = umma_idesc_bf16(128, 128, 0, 0);
-      constexpr uint32_t ID_DQ = umma_idesc_bf16(128, HD, 0, 1);
-      bool ok = mbar_wait(&bars->fixed_full, 0, kDevTimeoutFull);
-      const uint32_t qa = smem_u32(qs), da = smem_u32(dos);
-      auto issue_s = [&](int j) {  // S(j) = Q K_j^T into region j & 1
-        const int ks = j % 3;
-        if (!mbar_wait(&bars->k_full[ks], (j / 3) & 1, kDevTimeoutFull)) return false;
-        tc_fence_after();
-        mma_kmajor_ss<HD>(tbase + 128 * (j & 1), qa, smem_u32(kring + ks * C::TILE), ID_S);
-        umma_commit(&bars->s_full[j & 1]);
-        return true;
-      };
-      auto issue_dp = [&](int j) {  // dP(j) = dO V_j^T; V_j is free once it completes
-        const int vsl = j & 1;
-        if (!mbar_wait(&bars->v_full[vsl], (j >> 1) & 1, kDevTimeoutFull)) return false;
-        tc_fence_after();
-        mma_kmajor_ss<HD>(t_p, da, smem_u32(vring + vsl * C::TILE), ID_S);
-        umma_commit(&bars->dp_full);
-        umma_commit(&bars->v_empty[vsl]);
-        return true;
-      };
-      tc_fence_after();
-      if (ok) ok = issue_s(0);
-      if (ok && n > 1) ok = issue_s(1);
-      if (ok) ok = issue_dp(0);
-      for (int j = 0; ok && j < n; ++j) {
-        if (!(ok = mbar_wait(&bars->dp_loaded, j & 1, kDevTimeoutFull))) break;
-        tc_fence_after();
-        if (j + 1 < n && !(ok = issue_dp(j + 1))) break;
-        const uint32_t ts = tbase + 128 * (j & 1);
-        const uint64_t kdesc = umma_desc_sw128(smem_u32(kring + (j % 3) * C::TILE), C::BOX, 1024);
-        for (int i = 0; ok && i < 4; ++i) {
-          const int ci = chunk_order(i);
-          if (!(ok = mbar_wait(&bars->chunk[j & 1][ci], (j >> 1) & 1, kDevTimeoutFull))) break;
-          tc_fence_after();
-#pragma unroll 1
-          for (int kk = 2 * ci; kk < 2 * ci + 2; ++kk)  // dQ += dS K over keys [16kk, 16kk + 16)
-            umma_ts(t_dq, ts + a_col(kk), kdesc + (uint64_t)((kk * 2048) >> 4), ID_DQ,
-                    (j > 0 || kk > 0) ? 1u : 0u);
-        }
-        if (!ok) break;
-        umma_commit(&bars->k_empty[j % 3]);
-        if (j + 2 < n) ok = issue_s(j + 2);
-      }
-      umma_commit(&bars->acc_full);
+    constexpr uint32_t ID_S = umma_idesc_bf16(128, 128, 0, 0);
+    constexpr uint32_t ID_DQ = umma_idesc_bf16(128, HD, 0, 1);
+    bool ok = mbar_wait_warp(&bars->fixed_full, 0, kDevTimeoutFull);
+    const uint32_t qa = smem_u32(qs), da = smem_u32(dos);
+    auto issue_s = [&](int j) {  // S(j) = Q K_j^T into region j & 1
+      const int ks = j % 3;
+      if (!mbar_wait_warp(&bars->k_full[ks], (j / 3) & 1, kDevTimeoutFull)) return false;
+      mma_kmajor_ss<HD>(tbase + 128 * (j & 1), qa, smem_u32(kring + ks * C::TILE), ID_S);
+      umma_commit_warp(&bars->s_full[j & 1]);
+      return true;
+    };
+    auto issue_dp = [&](int j) {  // dP(j) = dO V_j^T; V_j is free once it completes
+      const int vsl = j & 1;
+      if (!mbar_wait_warp(&bars->v_full[vsl], (j >> 1) & 1, kDevTimeoutFull)) return false;
+      mma_kmajor_ss<HD>(t_p, da, smem_u32(vring + vsl * C::TILE), ID_S);
+      umma_commit_warp(&bars->dp_full);
+      umma_commit_warp(&bars->v_empty[vsl]);
+      return true;
+    };
+    if (ok) ok = issue_s(0);
+    if (ok && n > 1) ok = issue_s(1);
+    if (ok) ok = issue_dp(0);
+    for (int j = 0; ok && j < n; ++j) {
+      if (!(ok = mbar_wait_warp(&bars->dp_loaded, j & 1, kDevTimeoutFull))) break;
+      if (j + 1 < n && !(ok = issue_dp(j + 1))) break;
+      if (!(ok = mbar_wait_warp(&bars->ds_done[j & 1], (j >> 1) & 1, kDevTimeoutFull))) break;
+      // dQ += dS K over the 128 keys of item j.
+      mma_tmem_a<HD>(t_dq, tbase + 128 * (j & 1), smem_u32(kring + (j % 3) * C::TILE), ID_DQ, j > 0);
+      umma_commit_warp(&bars->k_empty[j % 3]);
+      if (j + 2 < n) ok = issue_s(j + 2);
     }
+    umma_commit_warp(&bars->acc_full);
   } else {
     const int hf = (warp - 2) >> 2;  // column half of every 128-column tile
     const int sub = warp & 3;         // TMEM lane quarter
@@ -276,9 +262,9 @@ __global__ void __launch_bounds__(320, 1) varlen_bwd_dq_kernel(const __grid_cons
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&bars->dp_loaded);
+      if (ok) {
 #pragma unroll
-      for (int c2 = 0; c2 < 2; ++c2) {
-        if (ok) {
+        for (int c2 = 0; c2 < 2; ++c2) {
           uint32_t ds[16];
 #pragma unroll
           for (int e = 0; e < 16; ++e) {
@@ -286,12 +272,12 @@ __global__ void __launch_bounds__(320, 1) varlen_bwd_dq_kernel(const __grid_cons
             ds[e] = pack_bf16x2(pf[c] * (__uint_as_float(dv[c]) - dlt), pf[c + 1] * (__uint_as_float(dv[c + 1]) - dlt));
           }
           tmem_st16(ts + 16 * c2, ds);  // over S columns this warp already read
-          tmem_wait_st();
         }
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&bars->chunk[j & 1][2 * hf + c2]);
+        tmem_wait_st();
       }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bars->ds_done[j & 1]);
     }
     // Epilogue: half 0 writes dQ columns [0, HD/2), half 1 [HD/2, HD).
     if (ok) ok = mbar_wait_warp(&bars->acc_full, 0, kDevTimeoutFull);
@@ -333,8 +319,8 @@ struct DkdvBars {
   uint64_t fixed_full;  // K, V
   uint64_t q_full[3], q_empty[3], d_full[2], d_empty[2];
   uint64_t s_full, dp_full;  // S^T(t), dP^T(t)
-  uint64_t s_loaded;         // element-wise warps hold S^T(t) in registers
-  uint64_t chunk[4];         // bf16 P^T / dS^T chunk c of the current item ready
+  uint64_t p_done;           // bf16 P^T of the current item in TMEM
+  uint64_t ds_done;          // bf16 dS^T of the current item in TMEM
   uint64_t acc_full;
   uint32_t tmem_base;
 };
@@ -381,8 +367,8 @@ __global__ void __launch_bounds__(320, 1) varlen_bwd_dkdv_kernel(const __grid_co
     }
     mbar_init(&bars->s_full, 1);
     mbar_init(&bars->dp_full, 1);
-    mbar_init(&bars->s_loaded, 8);
-    for (int c = 0; c < 4; ++c) mbar_init(&bars->chunk[c], 4);
+    mbar_init(&bars->p_done, 8);
+    mbar_init(&bars->ds_done, 8);
     mbar_init(&bars->acc_full, 1);
     fence_barrier_init();
   }
@@ -441,55 +427,42 @@ __global__ void __launch_bounds__(320, 1) varlen_bwd_dkdv_kernel(const __grid_co
       if (lane == 0) mbar_arrive(&bars->d_full[dsl]);
     }
   } else if (warp == 1) {
-    if (lane == 0) {
-      constexpr uint32_t ID_S = umma_idesc_bf16(128, 128, 0, 0);
-      constexpr uint32_t ID_G = umma_idesc_bf16(128, HD, 0, 1);
-      bool ok = mbar_wait(&bars->fixed_full, 0, kDevTimeoutFull);
-      const uint32_t ka = smem_u32(ks), va = smem_u32(vs);
-      auto issue_s = [&](int t) {  // S^T(t) = K Q_t^T
-        const int qs = t % 3;
-        if (!mbar_wait(&bars->q_full[qs], (t / 3) & 1, kDevTimeoutFull)) return false;
-        tc_fence_after();
-        mma_kmajor_ss<HD>(t_s, ka, smem_u32(qring + qs * C::TILE), ID_S);
-        umma_commit(&bars->s_full);
-        return true;
-      };
-      auto issue_dp = [&](int t) {  // dP^T(t) = V dO_t^T
-        const int dsl = t & 1;
-        if (!mbar_wait(&bars->d_full[dsl], (t >> 1) & 1, kDevTimeoutFull)) return false;
-        tc_fence_after();
-        mma_kmajor_ss<HD>(t_x, va, smem_u32(dring + dsl * C::TILE), ID_S);
-        umma_commit(&bars->dp_full);
-        return true;
-      };
-      tc_fence_after();
-      if (ok) ok = issue_s(0);
-      if (ok) ok = issue_dp(0);
-      for (int t = 0; ok && t < n; ++t) {
-        if (!(ok = mbar_wait(&bars->s_loaded, t & 1, kDevTimeoutFull))) break;
-        tc_fence_after();
-        if (t + 1 < n && !(ok = issue_s(t + 1))) break;
-        const uint64_t ddesc = umma_desc_sw128(smem_u32(dring + (t & 1) * C::TILE), C::BOX, 1024);
-        const uint64_t qdesc = umma_desc_sw128(smem_u32(qring + (t % 3) * C::TILE), C::BOX, 1024);
-        for (int i = 0; ok && i < 4; ++i) {
-          const int ci = chunk_order(i);
-          if (!(ok = mbar_wait(&bars->chunk[ci], t & 1, kDevTimeoutFull))) break;
-          tc_fence_after();
-#pragma unroll 1
-          for (int kk = 2 * ci; kk < 2 * ci + 2; ++kk) {  // queries [16kk, 16kk + 16)
-            const uint32_t acc = (t > 0 || kk > 0) ? 1u : 0u;
-            const uint64_t boff = (uint64_t)((kk * 2048) >> 4);
-            umma_ts(t_dv, t_x + pt_col(kk), ddesc + boff, ID_G, acc);       // dV += P^T dO
-            umma_ts(t_dk, t_x + pt_col(kk) + 16, qdesc + boff, ID_G, acc);  // dK += dS^T Q
-          }
-        }
-        if (!ok) break;
-        umma_commit(&bars->q_empty[t % 3]);
-        umma_commit(&bars->d_empty[t & 1]);
-        if (t + 1 < n) ok = issue_dp(t + 1);
-      }
-      umma_commit(&bars->acc_full);
+    constexpr uint32_t ID_S = umma_idesc_bf16(128, 128, 0, 0);
+    constexpr uint32_t ID_G = umma_idesc_bf16(128, HD, 0, 1);
+    bool ok = mbar_wait_warp(&bars->fixed_full, 0, kDevTimeoutFull);
+    const uint32_t ka = smem_u32(ks), va = smem_u32(vs);
+    auto issue_s = [&](int t) {  // S^T(t) = K Q_t^T
+      const int qs = t % 3;
+      if (!mbar_wait_warp(&bars->q_full[qs], (t / 3) & 1, kDevTimeoutFull)) return false;
+      mma_kmajor_ss<HD>(t_s, ka, smem_u32(qring + qs * C::TILE), ID_S);
+      umma_commit_warp(&bars->s_full);
+      return true;
+    };
+    auto issue_dp = [&](int t) {  // dP^T(t) = V dO_t^T
+      const int dsl = t & 1;
+      if (!mbar_wait_warp(&bars->d_full[dsl], (t >> 1) & 1, kDevTimeoutFull)) return false;
+      mma_kmajor_ss<HD>(t_x, va, smem_u32(dring + dsl * C::TILE), ID_S);
+      umma_commit_warp(&bars->dp_full);
+      return true;
+    };
+    // One item: dV(t) once P^T is in TMEM, then S^T(t+1) over the P^T columns
+    // dV has read, dK(t) once dS^T is in TMEM, then dP^T(t+1) over the dS^T
+    // columns dK has read.
+    if (ok) ok = issue_s(0);
+    if (ok) ok = issue_dp(0);
+    for (int t = 0; ok && t < n; ++t) {
+      if (!(ok = mbar_wait_warp(&bars->p_done, t & 1, kDevTimeoutFull))) break;
+      mma_tmem_a<HD>(t_dv, t_s, smem_u32(dring + (t & 1) * C::TILE), ID_G, t > 0);  // dV += P^T dO
+      if (t + 1 < n && !(ok = issue_s(t + 1))) break;
+      if (!(ok = mbar_wait_warp(&bars->ds_done, t & 1, kDevTimeoutFull))) break;
+      mma_tmem_a<HD>(t_dk, t_x, smem_u32(qring + (t % 3) * C::TILE), ID_G, t > 0);  // dK += dS^T Q
+      // Both slots (and their staged lse / delta, read until the dS^T phase
+      // ends) are free once dK(t) completes.
+      umma_commit_warp(&bars->q_empty[t % 3]);
+      umma_commit_warp(&bars->d_empty[t & 1]);
+      if (t + 1 < n) ok = issue_dp(t + 1);
     }
+    umma_commit_warp(&bars->acc_full);
   } else {
     const int hf = (warp - 2) >> 2;  // column half of every 128-column tile
     const int sub = warp & 3;         // TMEM lane quarter
@@ -503,40 +476,45 @@ __global__ void __launch_bounds__(320, 1) varlen_bwd_dkdv_kernel(const __grid_co
     for (int t = 0; t < n; ++t) {
       const int qc0 = (i_lo + t % nqi) * 128 + 64 * hf;  // first query of this warp's 64 columns
       uint32_t pk[32];  // P^T as bf16 pairs (the precision the dV MMA takes it in)
+      // P phase: S^T -> P^T, written packed over the S^T columns just read.
       if (ok) ok = mbar_wait_warp(&bars->q_full[t % 3], (t / 3) & 1, kDevTimeoutFull);
       if (ok) ok = mbar_wait_warp(&bars->s_full, t & 1, kDevTimeoutFull);
       tc_fence_after();
-      uint32_t sv[64];
-      if (ok) {
-        tmem_ld32(ts, *reinterpret_cast<uint32_t(*)[32]>(sv));
-        tmem_ld32(ts + 32, *reinterpret_cast<uint32_t(*)[32]>(sv + 32));
-        tmem_wait_ld();
-      }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&bars->s_loaded);
-      if (ok) {
-        const float4* l4 = reinterpret_cast<const float4*>(lse_ring + (t % 3) * 128 + 64 * hf);
-        const bool full = k_ok && qc0 >= k_tok && qc0 + 63 < q_end;
+      const bool full = k_ok && qc0 >= k_tok && qc0 + 63 < q_end;
 #pragma unroll
-        for (int c4 = 0; c4 < 16; ++c4) {
-          const float4 l = l4[c4];
-          float x[4];
-          x[0] = fast_exp2(fmaf(__uint_as_float(sv[4 * c4 + 0]), p.scale_log2, -l.x));
-          x[1] = fast_exp2(fmaf(__uint_as_float(sv[4 * c4 + 1]), p.scale_log2, -l.y));
-          x[2] = fast_exp2(fmaf(__uint_as_float(sv[4 * c4 + 2]), p.scale_log2, -l.z));
-          x[3] = fast_exp2(fmaf(__uint_as_float(sv[4 * c4 + 3]), p.scale_log2, -l.w));
-          if (!full) {
+      for (int c2 = 0; c2 < 2; ++c2) {
+        if (ok) {
+          uint32_t sv[32];
+          tmem_ld32(ts + 32 * c2, sv);
+          tmem_wait_ld();
+          const float4* l4 = reinterpret_cast<const float4*>(lse_ring + (t % 3) * 128 + 64 * hf + 32 * c2);
 #pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              const int q = qc0 + 4 * c4 + e;
-              if (q < k_tok || q >= q_end) x[e] = 0.f;
+          for (int c4 = 0; c4 < 8; ++c4) {
+            const float4 l = l4[c4];
+            const int c = 32 * c2 + 4 * c4;
+            float x[4];
+            x[0] = fast_exp2(fmaf(__uint_as_float(sv[4 * c4 + 0]), p.scale_log2, -l.x));
+            x[1] = fast_exp2(fmaf(__uint_as_float(sv[4 * c4 + 1]), p.scale_log2, -l.y));
+            x[2] = fast_exp2(fmaf(__uint_as_float(sv[4 * c4 + 2]), p.scale_log2, -l.z));
+            x[3] = fast_exp2(fmaf(__uint_as_float(sv[4 * c4 + 3]), p.scale_log2, -l.w));
+            if (!full) {
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                const int q = qc0 + c + e;
+                if (q < k_tok || q >= q_end) x[e] = 0.f;
+              }
             }
+            pk[16 * c2 + 2 * c4] = pack_bf16x2(x[0], x[1]);
+            pk[16 * c2 + 2 * c4 + 1] = pack_bf16x2(x[2], x[3]);
           }
-          pk[2 * c4] = pack_bf16x2(x[0], x[1]);
-          pk[2 * c4 + 1] = pack_bf16x2(x[2], x[3]);
+          tmem_st16(ts + 16 * c2, *reinterpret_cast<uint32_t(*)[16]>(pk + 16 * c2));
         }
       }
+      if (ok) tmem_wait_st();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bars->p_done);
+      // dS phase: dP^T -> dS^T = P^T o (dP^T - D), packed over the dP^T columns.
       if (ok) ok = mbar_wait_warp(&bars->d_full[t & 1], (t >> 1) & 1, kDevTimeoutFull);
       if (ok) ok = mbar_wait_warp(&bars->dp_full, t & 1, kDevTimeoutFull);
       tc_fence_after();
@@ -547,27 +525,23 @@ __global__ void __launch_bounds__(320, 1) varlen_bwd_dkdv_kernel(const __grid_co
           tmem_ld32(tx + 32 * c2, dv);
           tmem_wait_ld();
           const float4* d4 = reinterpret_cast<const float4*>(dlt_ring + (t & 1) * 128 + 64 * hf + 32 * c2);
-          uint32_t pp[16], ds[16];
+          uint32_t ds[16];
 #pragma unroll
           for (int e4 = 0; e4 < 8; ++e4) {
             const float4 d = d4[e4];
-            pp[2 * e4] = pk[16 * c2 + 2 * e4];
-            pp[2 * e4 + 1] = pk[16 * c2 + 2 * e4 + 1];
-            const float2 p01 = unpack_bf16x2(pp[2 * e4]), p23 = unpack_bf16x2(pp[2 * e4 + 1]);
-            ds[2 * e4] = pack_bf16x2(p01.x * (__uint_as_float(dv[4 * e4]) - d.x),
-                                     p01.y * (__uint_as_float(dv[4 * e4 + 1]) - d.y));
-            ds[2 * e4 + 1] = pack_bf16x2(p23.x * (__uint_as_float(dv[4 * e4 + 2]) - d.z),
-                                         p23.y * (__uint_as_float(dv[4 * e4 + 3]) - d.w));
+            const int c = 4 * e4;
+            const float2 p01 = unpack_bf16x2(pk[16 * c2 + 2 * e4]), p23 = unpack_bf16x2(pk[16 * c2 + 2 * e4 + 1]);
+            ds[2 * e4] = pack_bf16x2(p01.x * (__uint_as_float(dv[c]) - d.x), p01.y * (__uint_as_float(dv[c + 1]) - d.y));
+            ds[2 * e4 + 1] =
+                pack_bf16x2(p23.x * (__uint_as_float(dv[c + 2]) - d.z), p23.y * (__uint_as_float(dv[c + 3]) - d.w));
           }
-          // Over the 32 dP^T columns just read: P^T at [0, 16), dS^T at [16, 32).
-          tmem_st16(tx + 32 * c2, pp);
-          tmem_st16(tx + 32 * c2 + 16, ds);
-          tmem_wait_st();
+          tmem_st16(tx + 16 * c2, ds);
         }
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&bars->chunk[2 * hf + c2]);
       }
+      if (ok) tmem_wait_st();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bars->ds_done);
     }
     // Epilogue: half 0 writes dV, half 1 writes dK (scaled).
     if (ok) ok = mbar_wait_warp(&bars->acc_full, 0, kDevTimeoutFull);
