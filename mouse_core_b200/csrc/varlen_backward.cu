@@ -392,6 +392,20 @@ __global__ void __launch_bounds__(320, 1) varlen_bwd_dkdv_kernel(const __grid_co
         tma_load_3d(vs + cb * C::BOX, &vmap, &bars->fixed_full, cb * 64, kvh, kv0);
       }
     }
+    // lse / delta of the next item are loaded into registers one item ahead,
+    // so their global-memory latency never delays a TMA issue.
+    float lpre[4], dpre[4];
+    auto prefetch = [&](int t) {
+      const int hq = kvh * p.G + t / nqi;
+      const int q0 = (i_lo + t % nqi) * 128;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int q = q0 + lane + 32 * i;
+        lpre[i] = (q < p.L) ? p.lse[(size_t)hq * p.L + q] : INFINITY;
+        dpre[i] = (q < p.L) ? p.delta[(size_t)hq * p.L + q] : 0.f;
+      }
+    };
+    prefetch(0);
     bool ok = true;
     for (int t = 0; t < n; ++t) {
       const int qs = t % 3, dsl = t & 1;
@@ -405,10 +419,8 @@ __global__ void __launch_bounds__(320, 1) varlen_bwd_dkdv_kernel(const __grid_co
         for (int cb = 0; cb < C::NCB; ++cb)
           tma_load_3d(qring + qs * C::TILE + cb * C::BOX, &qmap, &bars->q_full[qs], cb * 64, hq, q0);
       }
-      for (int c = lane; c < 128; c += 32) {
-        const int q = q0 + c;
-        lse_ring[qs * 128 + c] = (q < p.L) ? p.lse[(size_t)hq * p.L + q] : INFINITY;
-      }
+#pragma unroll
+      for (int i = 0; i < 4; ++i) lse_ring[qs * 128 + lane + 32 * i] = lpre[i];
       __syncwarp();
       if (lane == 0) mbar_arrive(&bars->q_full[qs]);
       if (lane == 0) ok = mbar_wait(&bars->d_empty[dsl], ((t >> 1) & 1) ^ 1, kDevTimeoutEmpty);
@@ -419,12 +431,11 @@ __global__ void __launch_bounds__(320, 1) varlen_bwd_dkdv_kernel(const __grid_co
         for (int cb = 0; cb < C::NCB; ++cb)
           tma_load_3d(dring + dsl * C::TILE + cb * C::BOX, &dom, &bars->d_full[dsl], cb * 64, hq, q0);
       }
-      for (int c = lane; c < 128; c += 32) {
-        const int q = q0 + c;
-        dlt_ring[dsl * 128 + c] = (q < p.L) ? p.delta[(size_t)hq * p.L + q] : 0.f;
-      }
+#pragma unroll
+      for (int i = 0; i < 4; ++i) dlt_ring[dsl * 128 + lane + 32 * i] = dpre[i];
       __syncwarp();
       if (lane == 0) mbar_arrive(&bars->d_full[dsl]);
+      if (t + 1 < n) prefetch(t + 1);
     }
   } else if (warp == 1) {
     constexpr uint32_t ID_S = umma_idesc_bf16(128, 128, 0, 0);
