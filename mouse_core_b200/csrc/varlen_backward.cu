@@ -499,25 +499,26 @@ __global__ void __launch_bounds__(320, 1) varlen_bwd_dkdv_kernel(const __grid_co
           tmem_ld32(ts + 32 * c2, sv);
           tmem_wait_ld();
           const float4* l4 = reinterpret_cast<const float4*>(lse_ring + (t % 3) * 128 + 64 * hf + 32 * c2);
+          float x[32];
 #pragma unroll
           for (int c4 = 0; c4 < 8; ++c4) {
             const float4 l = l4[c4];
-            const int c = 32 * c2 + 4 * c4;
-            float x[4];
-            x[0] = fast_exp2(fmaf(__uint_as_float(sv[4 * c4 + 0]), p.scale_log2, -l.x));
-            x[1] = fast_exp2(fmaf(__uint_as_float(sv[4 * c4 + 1]), p.scale_log2, -l.y));
-            x[2] = fast_exp2(fmaf(__uint_as_float(sv[4 * c4 + 2]), p.scale_log2, -l.z));
-            x[3] = fast_exp2(fmaf(__uint_as_float(sv[4 * c4 + 3]), p.scale_log2, -l.w));
-            if (!full) {
-#pragma unroll
-              for (int e = 0; e < 4; ++e) {
-                const int q = qc0 + c + e;
-                if (q < k_tok || q >= q_end) x[e] = 0.f;
-              }
-            }
-            pk[16 * c2 + 2 * c4] = pack_bf16x2(x[0], x[1]);
-            pk[16 * c2 + 2 * c4 + 1] = pack_bf16x2(x[2], x[3]);
+            x[4 * c4 + 0] = fmaf(__uint_as_float(sv[4 * c4 + 0]), p.scale_log2, -l.x);
+            x[4 * c4 + 1] = fmaf(__uint_as_float(sv[4 * c4 + 1]), p.scale_log2, -l.y);
+            x[4 * c4 + 2] = fmaf(__uint_as_float(sv[4 * c4 + 2]), p.scale_log2, -l.z);
+            x[4 * c4 + 3] = fmaf(__uint_as_float(sv[4 * c4 + 3]), p.scale_log2, -l.w);
           }
+#pragma unroll
+          for (int e = 0; e < 32; ++e) x[e] = fast_exp2(x[e]);
+          if (!full) {
+#pragma unroll
+            for (int e = 0; e < 32; ++e) {
+              const int q = qc0 + 32 * c2 + e;
+              if (q < k_tok || q >= q_end) x[e] = 0.f;
+            }
+          }
+#pragma unroll
+          for (int e = 0; e < 16; ++e) pk[16 * c2 + e] = pack_bf16x2(x[2 * e], x[2 * e + 1]);
           tmem_st16(ts + 16 * c2, *reinterpret_cast<uint32_t(*)[16]>(pk + 16 * c2));
         }
       }
