@@ -118,61 +118,48 @@ __global__ void __launch_bounds__(320, 1) varlen_fwd_kernel(const __grid_constan
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issue
-    if (lane == 0) {
-      constexpr uint32_t ID_QK = umma_idesc_bf16(128, 128, 0, 0);
-      constexpr uint32_t ID_PV = umma_idesc_bf16(128, HD, 0, 1);
-      bool ok = mbar_wait(&bars->q_full, 0, kDevTimeoutFull);
-      tc_fence_after();
-      auto issue_qk = [&](int hh, int st) {
-        const uint32_t qa = smem_u32(qs + hh * C::QTILE);
-        const uint32_t kb = smem_u32(ks + st * C::KVTILE);
-#pragma unroll
-        for (int kk = 0; kk < HD / 16; ++kk) {
-          const uint32_t off = (kk >> 2) * C::BOX + (kk & 3) * 32;
-          umma_ss(tbase + 128 * hh, umma_desc_sw128(qa + off, 16, 1024), umma_desc_sw128(kb + off, 16, 1024), ID_QK,
-                  kk > 0);
-        }
-        umma_commit(&bars->s_full[hh]);
-      };
-      if (ok) ok = mbar_wait(&bars->k_full[0], 0, kDevTimeoutFull);
-      if (ok) {
-        tc_fence_after();
-        for (int hh = 0; hh < hpc; ++hh) issue_qk(hh, 0);
-      }
-      for (int j = 0; ok && j < n_tiles; ++j) {
-        const int st = j % C::STAGES;
-        const uint32_t ph = (j / C::STAGES) & 1;
-        if (!mbar_wait(&bars->v_full[st], ph, kDevTimeoutFull)) break;
-        const bool more = j + 1 < n_tiles;
-        const int st1 = (j + 1) % C::STAGES;
-        bool k_next = false;
-        for (int hh = 0; hh < hpc; ++hh) {
-          if (!mbar_wait(&bars->p_full[hh], j & 1, kDevTimeoutFull)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          const uint32_t vb = smem_u32(vs + st * C::KVTILE);
-#pragma unroll
-          for (int kk = 0; kk < C::BN / 16; ++kk)
-            umma_ts(tbase + 256 + HD * hh, tbase + 128 * hh + 8 * kk, umma_desc_sw128(vb + kk * 2048, C::BOX, 1024),
-                    ID_PV, (j > 0 || kk > 0) ? 1u : 0u);
-          if (more) {
-            if (!k_next) {
-              if (!mbar_wait(&bars->k_full[st1], ((j + 1) / C::STAGES) & 1, kDevTimeoutFull)) {
-                ok = false;
-                break;
-              }
-              tc_fence_after();
-              k_next = true;
-            }
-            issue_qk(hh, st1);
-          }
-        }
-        umma_commit(&bars->kv_empty[st]);
-      }
-      umma_commit(&bars->o_full);
+    // The whole warp runs this loop; each group of MMAs is one straight-line
+    // asm block issued by an elected lane.
+    constexpr uint32_t ID_QK = umma_idesc_bf16(128, 128, 0, 0);
+    constexpr uint32_t ID_PV = umma_idesc_bf16(128, HD, 0, 1);
+    bool ok = mbar_wait_warp(&bars->q_full, 0, kDevTimeoutFull);
+    auto issue_qk = [&](int hh, int st) {
+      const uint64_t dq = umma_desc_sw128(smem_u32(qs + hh * C::QTILE), 16, 1024);
+      const uint64_t dk = umma_desc_sw128(smem_u32(ks + st * C::KVTILE), 16, 1024);
+      if constexpr (HD == 128)
+        umma_ss_k128_warp(tbase + 128 * hh, dq, dk, ID_QK);
+      else
+        umma_ss_k64_warp(tbase + 128 * hh, dq, dk, ID_QK);
+      umma_commit_warp(&bars->s_full[hh]);
+    };
+    if (ok) ok = mbar_wait_warp(&bars->k_full[0], 0, kDevTimeoutFull);
+    if (ok) {
+      for (int hh = 0; hh < hpc; ++hh) issue_qk(hh, 0);
     }
+    for (int j = 0; ok && j < n_tiles; ++j) {
+      const int st = j % C::STAGES;
+      const uint32_t ph = (j / C::STAGES) & 1;
+      if (!(ok = mbar_wait_warp(&bars->v_full[st], ph, kDevTimeoutFull))) break;
+      const bool more = j + 1 < n_tiles;
+      const int st1 = (j + 1) % C::STAGES;
+      bool k_next = false;
+      const uint64_t dv = umma_desc_sw128(smem_u32(vs + st * C::KVTILE), C::BOX, 1024);
+      for (int hh = 0; hh < hpc; ++hh) {
+        if (!(ok = mbar_wait_warp(&bars->p_full[hh], j & 1, kDevTimeoutFull))) break;
+        // O_h += P_h V (P bf16 in the first 64 columns of S_h)
+        umma_ts_t128_linear_warp(tbase + 256 + HD * hh, tbase + 128 * hh, dv, ID_PV, j > 0 ? 1u : 0u);
+        if (more) {
+          if (!k_next) {
+            if (!(ok = mbar_wait_warp(&bars->k_full[st1], ((j + 1) / C::STAGES) & 1, kDevTimeoutFull))) break;
+            k_next = true;
+          }
+          issue_qk(hh, st1);
+        }
+      }
+      if (!ok) break;
+      umma_commit_warp(&bars->kv_empty[st]);
+    }
+    umma_commit_warp(&bars->o_full);
   } else {
     // ------------------------------------------------------------ softmax
     const int hh = (warp - 2) >> 2;
