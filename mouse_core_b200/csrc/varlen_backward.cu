@@ -51,23 +51,54 @@ struct BwdTile {
 };
 
 // ---------------------------------------------------------------- delta
-__global__ void bwd_delta_kernel(const __nv_bfloat16* __restrict__ out, const __nv_bfloat16* __restrict__ dout,
-                                 int L, int Hq, int hd, float* __restrict__ delta) {
-  const int warps = (gridDim.x * blockDim.x) >> 5;
-  const int lane = threadIdx.x & 31;
-  for (long long w = (long long)(blockIdx.x * blockDim.x + threadIdx.x) >> 5; w < (long long)L * Hq; w += warps) {
-    const long long i = w / Hq;
-    const int h = (int)(w % Hq);
-    const __nv_bfloat16* o = out + (i * Hq + h) * hd;
-    const __nv_bfloat16* g = dout + (i * Hq + h) * hd;
-    float acc = 0.f;
-    for (int d = lane * 2; d < hd; d += 64) {
-      const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(o + d));
-      const float2 b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(g + d));
-      acc += a.x * b.x + a.y * b.y;
+// D[h, i] = sum_d dO[i, h, d] O[i, h, d]: HBM-bound (2 * hd * 2 bytes read per
+// row). hd / 8 threads share a row, each loading 16 bytes of both tensors, and
+// each thread keeps two rows in flight.
+__device__ __forceinline__ float dot8_bf16(uint4 a, uint4 b) {
+  const uint32_t* x = reinterpret_cast<const uint32_t*>(&a);
+  const uint32_t* y = reinterpret_cast<const uint32_t*>(&b);
+  float acc = 0.f;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 u = unpack_bf16x2(x[i]), v = unpack_bf16x2(y[i]);
+    acc = fmaf(u.x, v.x, fmaf(u.y, v.y, acc));
+  }
+  return acc;
+}
+
+__global__ void __launch_bounds__(256) bwd_delta_kernel(const __nv_bfloat16* __restrict__ out,
+                                                        const __nv_bfloat16* __restrict__ dout, int L, int Hq,
+                                                        int hd, float* __restrict__ delta) {
+  const int tpr = hd >> 3;  // threads per row (16 or 8), a power of two dividing 32
+  const long long rows = (long long)L * Hq;
+  const long long tid = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  const long long stride = ((long long)gridDim.x * blockDim.x) / tpr;
+  const int part = (int)(tid % tpr);
+  // The row groups of one warp advance together (the stride is a multiple of
+  // the groups per warp), so the loop test on the warp's first row keeps the
+  // shuffles below convergent; rows past the end are masked per group.
+  const long long gw = (tid & 31) / tpr;
+  for (long long r0 = tid / tpr; r0 - gw < rows; r0 += 2 * stride) {
+    const long long r1 = r0 + stride;
+    const bool has0 = r0 < rows, has1 = r1 < rows;
+    uint4 a0 = make_uint4(0, 0, 0, 0), b0 = a0, a1 = a0, b1 = a0;
+    if (has0) {
+      a0 = __ldg(reinterpret_cast<const uint4*>(out + r0 * hd) + part);
+      b0 = __ldg(reinterpret_cast<const uint4*>(dout + r0 * hd) + part);
     }
-    acc = warp_sum(acc);
-    if (lane == 0) delta[(long long)h * L + i] = acc;
+    if (has1) {
+      a1 = __ldg(reinterpret_cast<const uint4*>(out + r1 * hd) + part);
+      b1 = __ldg(reinterpret_cast<const uint4*>(dout + r1 * hd) + part);
+    }
+    float s0 = dot8_bf16(a0, b0), s1 = dot8_bf16(a1, b1);
+    for (int o = tpr >> 1; o > 0; o >>= 1) {
+      s0 += __shfl_xor_sync(0xffffffffu, s0, o);
+      s1 += __shfl_xor_sync(0xffffffffu, s1, o);
+    }
+    if (part == 0) {
+      if (has0) delta[(r0 % Hq) * (long long)L + r0 / Hq] = s0;
+      if (has1) delta[(r1 % Hq) * (long long)L + r1 / Hq] = s1;
+    }
   }
 }
 
@@ -613,8 +644,10 @@ static cudaError_t launch_bwd_hd(const CUtensorMap& qm, const CUtensorMap& km, c
 cudaError_t launch_varlen_bwd(const CUtensorMap& qm, const CUtensorMap& km, const CUtensorMap& vm,
                               const CUtensorMap& dom, const __nv_bfloat16* out, const __nv_bfloat16* dout,
                               VarlenBwdParams p, cudaStream_t stream) {
-  const long long warps_needed = (long long)p.L * p.Hq;
-  const int blocks = (int)std::min<long long>((warps_needed + 7) / 8, 148 * 32);
+  // Whole rows per thread group; a grid of 8 blocks per SM keeps enough loads
+  // in flight to saturate HBM.
+  const long long threads_needed = (long long)p.L * p.Hq * (p.head_dim / 8);
+  const int blocks = (int)std::max<long long>(1, std::min<long long>((threads_needed + 255) / 256, 148 * 8));
   bwd_delta_kernel<<<blocks, 256, 0, stream>>>(out, dout, p.L, p.Hq, p.head_dim, p.delta);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
