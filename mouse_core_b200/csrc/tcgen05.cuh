@@ -125,6 +125,25 @@ __device__ __forceinline__ void umma_ts_t128_warp(uint32_t d, uint32_t a, uint64
       ::"r"(d), "r"(a), "l"(db), "r"(idesc), "r"(accumulate));
 }
 
+// As umma_ts_t128_warp, with A written by four 32-token quarters, each packed
+// into the first 16 columns of its own 32: K-step kk at column
+// 32 * (kk / 2) + 8 * (kk % 2).
+__device__ __forceinline__ void umma_ts_t128_quarters_warp(uint32_t d, uint32_t a, uint64_t db, uint32_t idesc,
+                                                           uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred e, t, p;\n\t.reg .b32 ta;\n\t.reg .b64 b;\n\t"
+      "elect.sync _|e, 0xffffffff;\n\tsetp.eq.b32 t, %3, %3;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t"
+      "add.u32 ta, %1, 8;\n\tadd.s64 b, %2, 128;\n\t@e tcgen05.mma.cta_group::1.kind::f16 [%0], [ta], b, %3, t;\n\t"
+      "add.u32 ta, %1, 32;\n\tadd.s64 b, %2, 256;\n\t@e tcgen05.mma.cta_group::1.kind::f16 [%0], [ta], b, %3, t;\n\t"
+      "add.u32 ta, %1, 40;\n\tadd.s64 b, %2, 384;\n\t@e tcgen05.mma.cta_group::1.kind::f16 [%0], [ta], b, %3, t;\n\t"
+      "add.u32 ta, %1, 64;\n\tadd.s64 b, %2, 512;\n\t@e tcgen05.mma.cta_group::1.kind::f16 [%0], [ta], b, %3, t;\n\t"
+      "add.u32 ta, %1, 72;\n\tadd.s64 b, %2, 640;\n\t@e tcgen05.mma.cta_group::1.kind::f16 [%0], [ta], b, %3, t;\n\t"
+      "add.u32 ta, %1, 96;\n\tadd.s64 b, %2, 768;\n\t@e tcgen05.mma.cta_group::1.kind::f16 [%0], [ta], b, %3, t;\n\t"
+      "add.u32 ta, %1, 104;\n\tadd.s64 b, %2, 896;\n\t@e tcgen05.mma.cta_group::1.kind::f16 [%0], [ta], b, %3, t;\n\t}"
+      ::"r"(d), "r"(a), "l"(db), "r"(idesc), "r"(accumulate));
+}
+
 // As umma_ts_t128_warp, with the 128 tokens of A packed contiguously: K-step
 // kk at column 8 * kk.
 __device__ __forceinline__ void umma_ts_t128_linear_warp(uint32_t d, uint32_t a, uint64_t db, uint32_t idesc,
@@ -234,6 +253,23 @@ __device__ __forceinline__ float fast_exp2(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
+}
+
+// 2^x on the FMA pipe, to take part of the exponentials off the SFU when it is
+// the bottleneck. Range reduction: adding 1.5 * 2^23 rounds x to the nearest
+// integer n (kept in the low mantissa bits), f = x - n lies in [-0.5, 0.5];
+// 2^f is a cubic (1 + c1 f + c2 f^2 + c3 f^3, least-squares fit of the
+// relative error, reweighted to near-minimax: max relative error 1.0e-4,
+// below the bf16 rounding the results get), and n is added to the exponent
+// field. x is clamped at -126 (the result is then ~1e-38, not 0).
+__device__ __forceinline__ float exp2_fma(float x) {
+  x = fmaxf(x, -126.f);
+  const float t = x + 12582912.f;
+  const float f = x - (t - 12582912.f);
+  float p = fmaf(0.0550089821f, f, 0.242210975f);
+  p = fmaf(p, f, 0.693282916f);
+  p = fmaf(p, f, 1.f);
+  return __int_as_float(__float_as_int(p) + (__float_as_int(t) << 23));
 }
 
 // Warpgroup register re-balancing (all four warps of a warpgroup execute it).

@@ -34,9 +34,10 @@
 //    other (dO, V) a 2-slot ring, so loads run an item or more ahead.
 //  * tcgen05.mma operations of one CTA execute in issue order, so an MMA may
 //    overwrite TMEM columns that an earlier MMA reads as its A operand.
-// Warp roles (320 threads): warp 0 TMA producer, warp 1 TMEM allocator and
-// MMA issuer, warps 2-9 element-wise (warp w owns TMEM lanes 32*(w%4) and
-// column half (w-2)/4 of each 128-column tile).
+// Warp roles (576 threads): warp 0 TMA producer, warp 1 TMEM allocator and
+// MMA issuer, warps 2-17 element-wise (warp w owns TMEM lanes 32*(w%4) and
+// column quarter (w-2)/4 of each 128-column tile; four warps per lane quarter
+// hide the TMEM and MUFU latencies of the element-wise phases).
 #include "common.cuh"
 #include "kernels.h"
 #include "tcgen05.cuh"
@@ -115,16 +116,21 @@ __device__ __forceinline__ void mma_kmajor_ss(uint32_t d, uint32_t a_base, uint3
 }
 
 // D (+)= A_tmem[128 x 128 tokens (bf16)] * B[128 tokens x HD], B MN-major in
-// smem; whole MMA warp.
+// smem; whole MMA warp. A is written by the element-wise warps: column quarter
+// q packs its 32 tokens into columns [32q, 32q + 16) of the 128-column region
+// it read them from.
 template <int HD>
 __device__ __forceinline__ void mma_tmem_a(uint32_t d, uint32_t a_tmem, uint32_t b_base, uint32_t idesc,
                                            bool accumulate) {
-  umma_ts_t128_warp(d, a_tmem, umma_desc_sw128(b_base, BwdTile<HD>::BOX, 1024), idesc, accumulate ? 1u : 0u);
+  umma_ts_t128_quarters_warp(d, a_tmem, umma_desc_sw128(b_base, BwdTile<HD>::BOX, 1024), idesc,
+                             accumulate ? 1u : 0u);
 }
 
-// bf16 A operands in TMEM: element-wise warp half h packs its 64 tokens into
-// columns [64h, 64h + 32) of the 128-column region it read them from, the
-// layout umma_ts_t128_warp consumes.
+constexpr int kBwdThreads = 576;  // producer + MMA warp + 16 element-wise warps
+constexpr int kEwWarps = 16;
+// Of each warp's 32 exponentials per item, this many run on the FMA pipe
+// (exp2_fma) instead of the SFU, whose throughput bounds the P phase.
+constexpr int kFmaExp = 8;
 
 // Dynamic shared memory is used from its base without padding (the kernels
 // need nearly all 227 KB); the 128-byte-swizzled TMA boxes need the base
@@ -144,7 +150,7 @@ struct DqBars {
 };
 
 template <int HD>
-__global__ void __launch_bounds__(320, 1) varlen_bwd_dq_kernel(const __grid_constant__ CUtensorMap qmap,
+__global__ void __launch_bounds__(kBwdThreads, 1) varlen_bwd_dq_kernel(const __grid_constant__ CUtensorMap qmap,
                                                               const __grid_constant__ CUtensorMap kmap,
                                                               const __grid_constant__ CUtensorMap vmap,
                                                               const __grid_constant__ CUtensorMap dom,
@@ -181,10 +187,10 @@ __global__ void __launch_bounds__(320, 1) varlen_bwd_dq_kernel(const __grid_cons
       mbar_init(&bars->v_full[s], 1);
       mbar_init(&bars->v_empty[s], 1);
       mbar_init(&bars->s_full[s], 1);
-      mbar_init(&bars->ds_done[s], 8);
+      mbar_init(&bars->ds_done[s], kEwWarps);
     }
     mbar_init(&bars->dp_full, 1);
-    mbar_init(&bars->dp_loaded, 8);
+    mbar_init(&bars->dp_loaded, kEwWarps);
     mbar_init(&bars->acc_full, 1);
     fence_barrier_init();
   }
@@ -253,7 +259,7 @@ __global__ void __launch_bounds__(320, 1) varlen_bwd_dq_kernel(const __grid_cons
     }
     umma_commit_warp(&bars->acc_full);
   } else {
-    const int hf = (warp - 2) >> 2;  // column half of every 128-column tile
+    const int cq = (warp - 2) >> 2;  // column quarter of every 128-column tile
     const int sub = warp & 3;         // TMEM lane quarter
     const int r = sub * 32 + lane;
     const int q_tok = q0 + r;
@@ -264,74 +270,71 @@ __global__ void __launch_bounds__(320, 1) varlen_bwd_dq_kernel(const __grid_cons
     const uint32_t lane_bits = (uint32_t)(sub * 32) << 16;
     bool ok = true;
     for (int j = 0; j < n; ++j) {
-      const int kc0 = (t_lo + j) * 128 + 64 * hf;  // first key of this warp's 64 columns
-      const uint32_t ts = tbase + 128 * (j & 1) + lane_bits + 64 * hf;
-      float pf[64];
+      const int kc0 = (t_lo + j) * 128 + 32 * cq;  // first key of this warp's 32 columns
+      const uint32_t ts = tbase + 128 * (j & 1) + lane_bits + 32 * cq;
+      float pf[32];
       if (ok) ok = mbar_wait_warp(&bars->s_full[j & 1], (j >> 1) & 1, kDevTimeoutFull);
       tc_fence_after();
       if (ok) {
-        uint32_t sv[64];
-        tmem_ld32(ts, *reinterpret_cast<uint32_t(*)[32]>(sv));
-        tmem_ld32(ts + 32, *reinterpret_cast<uint32_t(*)[32]>(sv + 32));
+        uint32_t sv[32];
+        tmem_ld32(ts, sv);
         tmem_wait_ld();
 #pragma unroll
-        for (int c = 0; c < 64; ++c) pf[c] = fast_exp2(fmaf(__uint_as_float(sv[c]), p.scale_log2, neg_lse));
-        if (!(row_ok && kc0 >= lo && kc0 + 63 <= q_tok)) {
+        for (int c = 0; c < 32; ++c) {
+          const float xc = fmaf(__uint_as_float(sv[c]), p.scale_log2, neg_lse);
+          pf[c] = c < 32 - kFmaExp ? fast_exp2(xc) : exp2_fma(xc);
+        }
+        if (!(row_ok && kc0 >= lo && kc0 + 31 <= q_tok)) {
 #pragma unroll
-          for (int c = 0; c < 64; ++c)
+          for (int c = 0; c < 32; ++c)
             if (!row_ok || kc0 + c < lo || kc0 + c > q_tok) pf[c] = 0.f;
         }
       }
       if (ok) ok = mbar_wait_warp(&bars->dp_full, j & 1, kDevTimeoutFull);
       tc_fence_after();
-      uint32_t dv[64];
+      uint32_t dv[32];
       if (ok) {
-        tmem_ld32(t_p + lane_bits + 64 * hf, *reinterpret_cast<uint32_t(*)[32]>(dv));
-        tmem_ld32(t_p + lane_bits + 64 * hf + 32, *reinterpret_cast<uint32_t(*)[32]>(dv + 32));
+        tmem_ld32(t_p + lane_bits + 32 * cq, dv);
         tmem_wait_ld();
       }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&bars->dp_loaded);
       if (ok) {
+        uint32_t ds[16];
 #pragma unroll
-        for (int c2 = 0; c2 < 2; ++c2) {
-          uint32_t ds[16];
-#pragma unroll
-          for (int e = 0; e < 16; ++e) {
-            const int c = 32 * c2 + 2 * e;
-            ds[e] = pack_bf16x2(pf[c] * (__uint_as_float(dv[c]) - dlt), pf[c + 1] * (__uint_as_float(dv[c + 1]) - dlt));
-          }
-          tmem_st16(ts + 16 * c2, ds);  // over S columns this warp already read
-        }
+        for (int e = 0; e < 16; ++e)
+          ds[e] = pack_bf16x2(pf[2 * e] * (__uint_as_float(dv[2 * e]) - dlt),
+                              pf[2 * e + 1] * (__uint_as_float(dv[2 * e + 1]) - dlt));
+        tmem_st16(ts, ds);  // over S columns this warp already read
         tmem_wait_st();
       }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&bars->ds_done[j & 1]);
     }
-    // Epilogue: half 0 writes dQ columns [0, HD/2), half 1 [HD/2, HD).
+    // Epilogue: column quarter cq writes dQ columns [cq HD/4, (cq + 1) HD/4).
     if (ok) ok = mbar_wait_warp(&bars->acc_full, 0, kDevTimeoutFull);
     tc_fence_after();
     if (ok) {
-      __nv_bfloat16* dst = p.dq + ((size_t)q_tok * p.Hq + h) * HD;
-#pragma unroll
-      for (int c = 0; c < HD / 64; ++c) {
-        const int col = hf * (HD / 2) + 32 * c;
-        uint32_t v[32];
+      constexpr int W = HD / 4;  // 32 or 16 columns
+      const int col = cq * W;
+      uint32_t v[32];
+      if constexpr (W == 32)
         tmem_ld32(t_dq + lane_bits + col, v);
-        tmem_wait_ld();
-        if (row_ok) {
-          uint4* d4 = reinterpret_cast<uint4*>(dst + col);
+      else
+        tmem_ld16(t_dq + lane_bits + col, *reinterpret_cast<uint32_t(*)[16]>(v));
+      tmem_wait_ld();
+      if (row_ok) {
+        uint4* d4 = reinterpret_cast<uint4*>(p.dq + ((size_t)q_tok * p.Hq + h) * HD + col);
 #pragma unroll
-          for (int q4 = 0; q4 < 4; ++q4) {
-            uint4 w;
-            w.x = pack_bf16x2(__uint_as_float(v[8 * q4 + 0]) * p.scale, __uint_as_float(v[8 * q4 + 1]) * p.scale);
-            w.y = pack_bf16x2(__uint_as_float(v[8 * q4 + 2]) * p.scale, __uint_as_float(v[8 * q4 + 3]) * p.scale);
-            w.z = pack_bf16x2(__uint_as_float(v[8 * q4 + 4]) * p.scale, __uint_as_float(v[8 * q4 + 5]) * p.scale);
-            w.w = pack_bf16x2(__uint_as_float(v[8 * q4 + 6]) * p.scale, __uint_as_float(v[8 * q4 + 7]) * p.scale);
-            d4[q4] = w;
-          }
+        for (int q4 = 0; q4 < W / 8; ++q4) {
+          uint4 w;
+          w.x = pack_bf16x2(__uint_as_float(v[8 * q4 + 0]) * p.scale, __uint_as_float(v[8 * q4 + 1]) * p.scale);
+          w.y = pack_bf16x2(__uint_as_float(v[8 * q4 + 2]) * p.scale, __uint_as_float(v[8 * q4 + 3]) * p.scale);
+          w.z = pack_bf16x2(__uint_as_float(v[8 * q4 + 4]) * p.scale, __uint_as_float(v[8 * q4 + 5]) * p.scale);
+          w.w = pack_bf16x2(__uint_as_float(v[8 * q4 + 6]) * p.scale, __uint_as_float(v[8 * q4 + 7]) * p.scale);
+          d4[q4] = w;
         }
       }
     }
@@ -357,7 +360,7 @@ struct DkdvBars {
 };
 
 template <int HD>
-__global__ void __launch_bounds__(320, 1) varlen_bwd_dkdv_kernel(const __grid_constant__ CUtensorMap qmap,
+__global__ void __launch_bounds__(kBwdThreads, 1) varlen_bwd_dkdv_kernel(const __grid_constant__ CUtensorMap qmap,
                                                                 const __grid_constant__ CUtensorMap kmap,
                                                                 const __grid_constant__ CUtensorMap vmap,
                                                                 const __grid_constant__ CUtensorMap dom,
@@ -398,8 +401,8 @@ __global__ void __launch_bounds__(320, 1) varlen_bwd_dkdv_kernel(const __grid_co
     }
     mbar_init(&bars->s_full, 1);
     mbar_init(&bars->dp_full, 1);
-    mbar_init(&bars->p_done, 8);
-    mbar_init(&bars->ds_done, 8);
+    mbar_init(&bars->p_done, kEwWarps);
+    mbar_init(&bars->ds_done, kEwWarps);
     mbar_init(&bars->acc_full, 1);
     fence_barrier_init();
   }
@@ -506,54 +509,50 @@ __global__ void __launch_bounds__(320, 1) varlen_bwd_dkdv_kernel(const __grid_co
     }
     umma_commit_warp(&bars->acc_full);
   } else {
-    const int hf = (warp - 2) >> 2;  // column half of every 128-column tile
+    const int cq = (warp - 2) >> 2;  // column quarter of every 128-column tile
     const int sub = warp & 3;         // TMEM lane quarter
     const int r = sub * 32 + lane;
     const int k_tok = kv0 + r;
     const bool k_ok = k_tok < p.L;
     const int q_end = k_ok ? p.run_end[k_tok] : 0;  // queries k_tok <= q < q_end see this key
     const uint32_t lane_bits = (uint32_t)(sub * 32) << 16;
-    const uint32_t ts = t_s + lane_bits + 64 * hf, tx = t_x + lane_bits + 64 * hf;
+    const uint32_t ts = t_s + lane_bits + 32 * cq, tx = t_x + lane_bits + 32 * cq;
     bool ok = true;
     for (int t = 0; t < n; ++t) {
-      const int qc0 = (i_lo + t % nqi) * 128 + 64 * hf;  // first query of this warp's 64 columns
-      uint32_t pk[32];  // P^T as bf16 pairs (the precision the dV MMA takes it in)
+      const int qc0 = (i_lo + t % nqi) * 128 + 32 * cq;  // first query of this warp's 32 columns
+      uint32_t pk[16];  // P^T as bf16 pairs (the precision the dV MMA takes it in)
       // P phase: S^T -> P^T, written packed over the S^T columns just read.
       if (ok) ok = mbar_wait_warp(&bars->q_full[t % 3], (t / 3) & 1, kDevTimeoutFull);
       if (ok) ok = mbar_wait_warp(&bars->s_full, t & 1, kDevTimeoutFull);
       tc_fence_after();
-      const bool full = k_ok && qc0 >= k_tok && qc0 + 63 < q_end;
+      if (ok) {
+        uint32_t sv[32];
+        tmem_ld32(ts, sv);
+        tmem_wait_ld();
+        const float4* l4 = reinterpret_cast<const float4*>(lse_ring + (t % 3) * 128 + 32 * cq);
+        float x[32];
 #pragma unroll
-      for (int c2 = 0; c2 < 2; ++c2) {
-        if (ok) {
-          uint32_t sv[32];
-          tmem_ld32(ts + 32 * c2, sv);
-          tmem_wait_ld();
-          const float4* l4 = reinterpret_cast<const float4*>(lse_ring + (t % 3) * 128 + 64 * hf + 32 * c2);
-          float x[32];
-#pragma unroll
-          for (int c4 = 0; c4 < 8; ++c4) {
-            const float4 l = l4[c4];
-            x[4 * c4 + 0] = fmaf(__uint_as_float(sv[4 * c4 + 0]), p.scale_log2, -l.x);
-            x[4 * c4 + 1] = fmaf(__uint_as_float(sv[4 * c4 + 1]), p.scale_log2, -l.y);
-            x[4 * c4 + 2] = fmaf(__uint_as_float(sv[4 * c4 + 2]), p.scale_log2, -l.z);
-            x[4 * c4 + 3] = fmaf(__uint_as_float(sv[4 * c4 + 3]), p.scale_log2, -l.w);
-          }
-#pragma unroll
-          for (int e = 0; e < 32; ++e) x[e] = fast_exp2(x[e]);
-          if (!full) {
-#pragma unroll
-            for (int e = 0; e < 32; ++e) {
-              const int q = qc0 + 32 * c2 + e;
-              if (q < k_tok || q >= q_end) x[e] = 0.f;
-            }
-          }
-#pragma unroll
-          for (int e = 0; e < 16; ++e) pk[16 * c2 + e] = pack_bf16x2(x[2 * e], x[2 * e + 1]);
-          tmem_st16(ts + 16 * c2, *reinterpret_cast<uint32_t(*)[16]>(pk + 16 * c2));
+        for (int c4 = 0; c4 < 8; ++c4) {
+          const float4 l = l4[c4];
+          x[4 * c4 + 0] = fmaf(__uint_as_float(sv[4 * c4 + 0]), p.scale_log2, -l.x);
+          x[4 * c4 + 1] = fmaf(__uint_as_float(sv[4 * c4 + 1]), p.scale_log2, -l.y);
+          x[4 * c4 + 2] = fmaf(__uint_as_float(sv[4 * c4 + 2]), p.scale_log2, -l.z);
+          x[4 * c4 + 3] = fmaf(__uint_as_float(sv[4 * c4 + 3]), p.scale_log2, -l.w);
         }
+#pragma unroll
+        for (int e = 0; e < 32; ++e) x[e] = e < 32 - kFmaExp ? fast_exp2(x[e]) : exp2_fma(x[e]);
+        if (!(k_ok && qc0 >= k_tok && qc0 + 31 < q_end)) {
+#pragma unroll
+          for (int e = 0; e < 32; ++e) {
+            const int q = qc0 + e;
+            if (q < k_tok || q >= q_end) x[e] = 0.f;
+          }
+        }
+#pragma unroll
+        for (int e = 0; e < 16; ++e) pk[e] = pack_bf16x2(x[2 * e], x[2 * e + 1]);
+        tmem_st16(ts, pk);
+        tmem_wait_st();
       }
-      if (ok) tmem_wait_st();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&bars->p_done);
@@ -561,45 +560,45 @@ __global__ void __launch_bounds__(320, 1) varlen_bwd_dkdv_kernel(const __grid_co
       if (ok) ok = mbar_wait_warp(&bars->d_full[t & 1], (t >> 1) & 1, kDevTimeoutFull);
       if (ok) ok = mbar_wait_warp(&bars->dp_full, t & 1, kDevTimeoutFull);
       tc_fence_after();
+      if (ok) {
+        uint32_t dv[32];
+        tmem_ld32(tx, dv);
+        tmem_wait_ld();
+        const float4* d4 = reinterpret_cast<const float4*>(dlt_ring + (t & 1) * 128 + 32 * cq);
+        uint32_t ds[16];
 #pragma unroll
-      for (int c2 = 0; c2 < 2; ++c2) {
-        if (ok) {
-          uint32_t dv[32];
-          tmem_ld32(tx + 32 * c2, dv);
-          tmem_wait_ld();
-          const float4* d4 = reinterpret_cast<const float4*>(dlt_ring + (t & 1) * 128 + 64 * hf + 32 * c2);
-          uint32_t ds[16];
-#pragma unroll
-          for (int e4 = 0; e4 < 8; ++e4) {
-            const float4 d = d4[e4];
-            const int c = 4 * e4;
-            const float2 p01 = unpack_bf16x2(pk[16 * c2 + 2 * e4]), p23 = unpack_bf16x2(pk[16 * c2 + 2 * e4 + 1]);
-            ds[2 * e4] = pack_bf16x2(p01.x * (__uint_as_float(dv[c]) - d.x), p01.y * (__uint_as_float(dv[c + 1]) - d.y));
-            ds[2 * e4 + 1] =
-                pack_bf16x2(p23.x * (__uint_as_float(dv[c + 2]) - d.z), p23.y * (__uint_as_float(dv[c + 3]) - d.w));
-          }
-          tmem_st16(tx + 16 * c2, ds);
+        for (int e4 = 0; e4 < 8; ++e4) {
+          const float4 d = d4[e4];
+          const float2 p01 = unpack_bf16x2(pk[2 * e4]), p23 = unpack_bf16x2(pk[2 * e4 + 1]);
+          ds[2 * e4] = pack_bf16x2(p01.x * (__uint_as_float(dv[4 * e4]) - d.x),
+                                   p01.y * (__uint_as_float(dv[4 * e4 + 1]) - d.y));
+          ds[2 * e4 + 1] = pack_bf16x2(p23.x * (__uint_as_float(dv[4 * e4 + 2]) - d.z),
+                                       p23.y * (__uint_as_float(dv[4 * e4 + 3]) - d.w));
         }
+        tmem_st16(tx, ds);
+        tmem_wait_st();
       }
-      if (ok) tmem_wait_st();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&bars->ds_done);
     }
-    // Epilogue: half 0 writes dV, half 1 writes dK (scaled).
+    // Epilogue: quarters 0-1 write dV, 2-3 write dK (scaled); each covers half
+    // of the HD columns.
     if (ok) ok = mbar_wait_warp(&bars->acc_full, 0, kDevTimeoutFull);
     tc_fence_after();
     if (ok) {
-      const uint32_t src = (hf == 0 ? t_dv : t_dk) + lane_bits;
-      const float mul = (hf == 0) ? 1.f : p.scale;
-      __nv_bfloat16* dst = (hf == 0 ? p.dv : p.dk) + ((size_t)k_tok * p.Hkv + kvh) * HD;
+      const bool is_v = cq < 2;
+      const int col0 = (cq & 1) * (HD / 2);
+      const uint32_t src = (is_v ? t_dv : t_dk) + lane_bits + col0;
+      const float mul = is_v ? 1.f : p.scale;
+      __nv_bfloat16* dst = (is_v ? p.dv : p.dk) + ((size_t)k_tok * p.Hkv + kvh) * HD + col0;
 #pragma unroll
-      for (int c = 0; c < HD / 32; ++c) {
+      for (int c = 0; c < HD / 64; ++c) {
         uint32_t v[32];
         tmem_ld32(src + 32 * c, v);
         tmem_wait_ld();
         if (k_ok) {
-          uint4* d4 = reinterpret_cast<uint4*>(dst + 32 * c);
+          uint4* o4 = reinterpret_cast<uint4*>(dst + 32 * c);
 #pragma unroll
           for (int q4 = 0; q4 < 4; ++q4) {
             uint4 w;
@@ -607,7 +606,7 @@ __global__ void __launch_bounds__(320, 1) varlen_bwd_dkdv_kernel(const __grid_co
             w.y = pack_bf16x2(__uint_as_float(v[8 * q4 + 2]) * mul, __uint_as_float(v[8 * q4 + 3]) * mul);
             w.z = pack_bf16x2(__uint_as_float(v[8 * q4 + 4]) * mul, __uint_as_float(v[8 * q4 + 5]) * mul);
             w.w = pack_bf16x2(__uint_as_float(v[8 * q4 + 6]) * mul, __uint_as_float(v[8 * q4 + 7]) * mul);
-            d4[q4] = w;
+            o4[q4] = w;
           }
         }
       }
@@ -634,10 +633,10 @@ static cudaError_t launch_bwd_hd(const CUtensorMap& qm, const CUtensorMap& km, c
   if (e != cudaSuccess) return e;
   e = cudaFuncSetAttribute(varlen_bwd_dq_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_dq);
   if (e != cudaSuccess) return e;
-  varlen_bwd_dkdv_kernel<HD><<<dim3(n_t, p.Hkv), 320, smem_kv, stream>>>(qm, km, vm, dom, p);
+  varlen_bwd_dkdv_kernel<HD><<<dim3(n_t, p.Hkv), kBwdThreads, smem_kv, stream>>>(qm, km, vm, dom, p);
   e = cudaGetLastError();
   if (e != cudaSuccess) return e;
-  varlen_bwd_dq_kernel<HD><<<dim3(n_t, p.Hq), 320, smem_dq, stream>>>(qm, km, vm, dom, p);
+  varlen_bwd_dq_kernel<HD><<<dim3(n_t, p.Hq), kBwdThreads, smem_dq, stream>>>(qm, km, vm, dom, p);
   return cudaGetLastError();
 }
 
