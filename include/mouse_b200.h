@@ -188,6 +188,42 @@ int mb_varlen_attention_bwd(const void* q, const void* k, const void* v, const v
 int mb_segment_meta(const int64_t* sequence_ids, int L, int tile, int64_t* position, int32_t* run_start,
                     int32_t* run_end, int32_t* tile_lo, int32_t* flags, mb_stream_t stream);
 
+/* ---------------------------------------------------------------------
+ * Packed training layer, element-wise forward and backward (K4).
+ * The decoder layer that models/backbone/flex_train.py:128-150 runs on the
+ * packed stream (transformers' Qwen3DecoderLayer / LlamaDecoderLayer) in
+ * fused passes. All tensors bf16 unless noted; rstd and weight gradients f32.
+ *
+ * mb_rmsnorm_fwd: y = weight * bf16(x * rstd), rstd[r] = 1 / sqrt(mean(x^2) +
+ *   eps) (input_layernorm, post_attention_layernorm and the final norm,
+ *   flex_train.py:145-150). dim a multiple of 256, <= 2048.
+ * mb_rmsnorm_bwd: dx and dweight (= sum over rows of dy * bf16(x * rstd));
+ *   scratch holds mb_rmsnorm_bwd_scratch_floats(rows, dim) floats.
+ * mb_qk_norm_rope_fwd: per (token, head) of x (rows x_row_stride elements
+ *   apart, e.g. the q or k slice of a fused QKV projection): optional
+ *   per-head RMSNorm (q_norm / k_norm; weight NULL skips it), then
+ *   y = n * cos + rotate_half(n) * sin with cos/sin [L, head_dim] per token.
+ *   y is [L, heads, head_dim]; rstd f32 [L * heads] when weight is set.
+ * mb_qk_norm_rope_bwd: dx (written with row stride dx_row_stride, e.g. into
+ *   the fused QKV gradient) and dweight [head_dim] when weight is set;
+ *   scratch holds mb_qk_norm_rope_bwd_scratch_floats(L, heads, head_dim).
+ * mb_silu_mul_bwd: gradient of h = silu(gate) * up over gate_up [rows, 2I]:
+ *   dgate_up[:, :I] = dh * up * silu'(gate), dgate_up[:, I:] = dh * silu(gate).
+ * ------------------------------------------------------------------- */
+int mb_rmsnorm_fwd(const void* x, const void* weight, float eps, int rows, int dim, void* y, float* rstd,
+                   mb_stream_t stream);
+size_t mb_rmsnorm_bwd_scratch_floats(int rows, int dim);
+int mb_rmsnorm_bwd(const void* dy, const void* x, const void* weight, const float* rstd, int rows, int dim, void* dx,
+                   float* dweight, float* scratch, size_t scratch_floats, mb_stream_t stream);
+int mb_qk_norm_rope_fwd(const void* x, long long x_row_stride, const void* weight, float eps, const void* cos,
+                        const void* sin, int L, int heads, int head_dim, void* y, float* rstd, mb_stream_t stream);
+size_t mb_qk_norm_rope_bwd_scratch_floats(int L, int heads, int head_dim);
+int mb_qk_norm_rope_bwd(const void* dy, const void* x, long long x_row_stride, const void* weight, const void* cos,
+                        const void* sin, const float* rstd, int L, int heads, int head_dim, void* dx,
+                        long long dx_row_stride, float* dweight, float* scratch, size_t scratch_floats,
+                        mb_stream_t stream);
+int mb_silu_mul_bwd(const void* gate_up, const void* dh, int rows, int inter, void* dgate_up, mb_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -343,4 +343,112 @@ int mb_segment_meta(const int64_t* sequence_ids, int L, int tile, int64_t* posit
   return e == cudaSuccess ? MB_OK : cuda_fail(e, "segment meta launch");
 }
 
+// ---------------------------------------------------------------- training element-wise (K4)
+
+namespace {
+int check_norm_dim(int rows, int dim) {
+  if (rows < 0) return fail(MB_ERR_INVALID_ARG, "rows must be >= 0");
+  if (dim <= 0 || dim % 256 || dim > 2048) return fail(MB_ERR_UNSUPPORTED, "dim must be a multiple of 256, <= 2048");
+  return MB_OK;
+}
+
+int check_head_shape(int L, int heads, int head_dim) {
+  if (L < 0 || heads <= 0) return fail(MB_ERR_INVALID_ARG, "L >= 0 and heads > 0 required");
+  if (head_dim != 64 && head_dim != 128) return fail(MB_ERR_UNSUPPORTED, "head_dim must be 64 or 128");
+  return MB_OK;
+}
+}  // namespace
+
+int mb_rmsnorm_fwd(const void* x, const void* weight, float eps, int rows, int dim, void* y, float* rstd,
+                   mb_stream_t stream) {
+  if (int rc = check_norm_dim(rows, dim)) return rc;
+  if (rows == 0) return MB_OK;
+  if (!x || !weight || !y || !rstd) return fail(MB_ERR_INVALID_ARG, "a required pointer is NULL");
+  if (!aligned(x, 16) || !aligned(weight, 16) || !aligned(y, 16))
+    return fail(MB_ERR_INVALID_ARG, "x, weight and y must be 16-byte aligned");
+  cudaError_t e = mb::launch_rmsnorm_fwd(static_cast<const __nv_bfloat16*>(x), static_cast<const __nv_bfloat16*>(weight),
+                                         eps, rows, dim, static_cast<__nv_bfloat16*>(y), rstd, (cudaStream_t)stream);
+  return e == cudaSuccess ? MB_OK : cuda_fail(e, "rmsnorm fwd launch");
+}
+
+size_t mb_rmsnorm_bwd_scratch_floats(int rows, int dim) {
+  if (rows <= 0 || dim <= 0) return 0;
+  return (size_t)mb::rmsnorm_bwd_partials(rows) * (size_t)dim;
+}
+
+int mb_rmsnorm_bwd(const void* dy, const void* x, const void* weight, const float* rstd, int rows, int dim, void* dx,
+                   float* dweight, float* scratch, size_t scratch_floats, mb_stream_t stream) {
+  if (int rc = check_norm_dim(rows, dim)) return rc;
+  if (!dweight) return fail(MB_ERR_INVALID_ARG, "dweight is NULL");
+  if (rows > 0) {
+    if (!dy || !x || !weight || !rstd || !dx || !scratch) return fail(MB_ERR_INVALID_ARG, "a required pointer is NULL");
+    if (scratch_floats < mb_rmsnorm_bwd_scratch_floats(rows, dim))
+      return fail(MB_ERR_INVALID_ARG, "scratch is smaller than mb_rmsnorm_bwd_scratch_floats");
+    if (!aligned(dy, 16) || !aligned(x, 16) || !aligned(weight, 16) || !aligned(dx, 16))
+      return fail(MB_ERR_INVALID_ARG, "dy, x, weight and dx must be 16-byte aligned");
+  }
+  cudaError_t e = mb::launch_rmsnorm_bwd(static_cast<const __nv_bfloat16*>(dy), static_cast<const __nv_bfloat16*>(x),
+                                         static_cast<const __nv_bfloat16*>(weight), rstd, rows, dim,
+                                         static_cast<__nv_bfloat16*>(dx), scratch, dweight, (cudaStream_t)stream);
+  return e == cudaSuccess ? MB_OK : cuda_fail(e, "rmsnorm bwd launch");
+}
+
+int mb_qk_norm_rope_fwd(const void* x, long long x_row_stride, const void* weight, float eps, const void* cos,
+                        const void* sin, int L, int heads, int head_dim, void* y, float* rstd, mb_stream_t stream) {
+  if (int rc = check_head_shape(L, heads, head_dim)) return rc;
+  if (L == 0) return MB_OK;
+  if (!x || !cos || !sin || !y || (weight && !rstd)) return fail(MB_ERR_INVALID_ARG, "a required pointer is NULL");
+  if (x_row_stride < (long long)heads * head_dim || x_row_stride % 2)
+    return fail(MB_ERR_INVALID_ARG, "x_row_stride must be even and >= heads * head_dim");
+  if (!aligned(x, 4) || !aligned(cos, 4) || !aligned(sin, 4) || !aligned(y, 4))
+    return fail(MB_ERR_INVALID_ARG, "x, cos, sin and y must be 4-byte aligned");
+  cudaError_t e = mb::launch_qk_norm_rope_fwd(
+      static_cast<const __nv_bfloat16*>(x), x_row_stride, static_cast<const __nv_bfloat16*>(weight), eps,
+      static_cast<const __nv_bfloat16*>(cos), static_cast<const __nv_bfloat16*>(sin), L, heads, head_dim,
+      static_cast<__nv_bfloat16*>(y), rstd, (cudaStream_t)stream);
+  return e == cudaSuccess ? MB_OK : cuda_fail(e, "qk norm rope fwd launch");
+}
+
+size_t mb_qk_norm_rope_bwd_scratch_floats(int L, int heads, int head_dim) {
+  if (L <= 0 || heads <= 0 || head_dim <= 0) return 0;
+  return (size_t)mb::qk_norm_rope_bwd_partials(L, heads) * (size_t)head_dim;
+}
+
+int mb_qk_norm_rope_bwd(const void* dy, const void* x, long long x_row_stride, const void* weight, const void* cos,
+                        const void* sin, const float* rstd, int L, int heads, int head_dim, void* dx,
+                        long long dx_row_stride, float* dweight, float* scratch, size_t scratch_floats,
+                        mb_stream_t stream) {
+  if (int rc = check_head_shape(L, heads, head_dim)) return rc;
+  if (weight && !dweight) return fail(MB_ERR_INVALID_ARG, "a weight needs dweight");
+  if (L > 0) {
+    if (!dy || !cos || !sin || !dx) return fail(MB_ERR_INVALID_ARG, "a required pointer is NULL");
+    if (weight && (!x || !rstd || !scratch)) return fail(MB_ERR_INVALID_ARG, "the norm needs x, rstd and scratch");
+    if (weight && scratch_floats < mb_qk_norm_rope_bwd_scratch_floats(L, heads, head_dim))
+      return fail(MB_ERR_INVALID_ARG, "scratch is smaller than mb_qk_norm_rope_bwd_scratch_floats");
+    const long long need = (long long)heads * head_dim;
+    if (dx_row_stride < need || dx_row_stride % 2 || (weight && (x_row_stride < need || x_row_stride % 2)))
+      return fail(MB_ERR_INVALID_ARG, "row strides must be even and >= heads * head_dim");
+    if (!aligned(dy, 4) || !aligned(cos, 4) || !aligned(sin, 4) || !aligned(dx, 4) || (x && !aligned(x, 4)))
+      return fail(MB_ERR_INVALID_ARG, "dy, x, cos, sin and dx must be 4-byte aligned");
+  }
+  cudaError_t e = mb::launch_qk_norm_rope_bwd(
+      static_cast<const __nv_bfloat16*>(dy), static_cast<const __nv_bfloat16*>(x), x_row_stride,
+      static_cast<const __nv_bfloat16*>(weight), static_cast<const __nv_bfloat16*>(cos),
+      static_cast<const __nv_bfloat16*>(sin), rstd, L, heads, head_dim, static_cast<__nv_bfloat16*>(dx),
+      dx_row_stride, scratch, weight ? dweight : nullptr, (cudaStream_t)stream);
+  return e == cudaSuccess ? MB_OK : cuda_fail(e, "qk norm rope bwd launch");
+}
+
+int mb_silu_mul_bwd(const void* gate_up, const void* dh, int rows, int inter, void* dgate_up, mb_stream_t stream) {
+  if (rows < 0 || inter <= 0 || inter % 2) return fail(MB_ERR_INVALID_ARG, "rows >= 0 and an even inter required");
+  if (rows == 0) return MB_OK;
+  if (!gate_up || !dh || !dgate_up) return fail(MB_ERR_INVALID_ARG, "a required pointer is NULL");
+  if (!aligned(gate_up, 4) || !aligned(dh, 4) || !aligned(dgate_up, 4))
+    return fail(MB_ERR_INVALID_ARG, "buffers must be 4-byte aligned");
+  cudaError_t e = mb::launch_silu_mul_bwd(static_cast<const __nv_bfloat16*>(gate_up),
+                                          static_cast<const __nv_bfloat16*>(dh), rows, inter,
+                                          static_cast<__nv_bfloat16*>(dgate_up), (cudaStream_t)stream);
+  return e == cudaSuccess ? MB_OK : cuda_fail(e, "silu_mul bwd launch");
+}
+
 }  // extern "C"

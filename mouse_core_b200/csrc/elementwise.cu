@@ -65,8 +65,10 @@ __global__ void silu_mul_kernel(const __nv_bfloat16* gu, int I, long long total_
     const long long row = (i * 2) / I, col = (i * 2) % I;
     const float2 g = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(gu + row * 2 * I + col));
     const float2 u = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(gu + row * 2 * I + I + col));
-    const float a = g.x / (1.f + expf(-g.x));
-    const float b = g.y / (1.f + expf(-g.y));
+    // silu(gate) is rounded to bf16 before the product, as the module's bf16
+    // activation output is.
+    const float a = __bfloat162float(__float2bfloat16_rn(g.x / (1.f + expf(-g.x))));
+    const float b = __bfloat162float(__float2bfloat16_rn(g.y / (1.f + expf(-g.y))));
     *reinterpret_cast<__nv_bfloat162*>(out + row * I + col) = __floats2bfloat162_rn(a * u.x, b * u.y);
   }
 }

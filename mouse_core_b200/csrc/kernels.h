@@ -98,6 +98,24 @@ cudaError_t launch_varlen_bwd(const CUtensorMap& qm, const CUtensorMap& km, cons
                               const CUtensorMap& dom, const __nv_bfloat16* out, const __nv_bfloat16* dout,
                               VarlenBwdParams p, cudaStream_t stream);
 
+// Training element-wise kernels (train_elementwise.cu).
+cudaError_t launch_rmsnorm_fwd(const __nv_bfloat16* x, const __nv_bfloat16* w, float eps, int rows, int D,
+                               __nv_bfloat16* y, float* rstd, cudaStream_t stream);
+int rmsnorm_bwd_partials(int rows);
+cudaError_t launch_rmsnorm_bwd(const __nv_bfloat16* dy, const __nv_bfloat16* x, const __nv_bfloat16* w,
+                               const float* rstd, int rows, int D, __nv_bfloat16* dx, float* partial, float* dw,
+                               cudaStream_t stream);
+int qk_norm_rope_bwd_partials(int L, int H);
+cudaError_t launch_qk_norm_rope_fwd(const __nv_bfloat16* x, long long xs, const __nv_bfloat16* w, float eps,
+                                    const __nv_bfloat16* cosv, const __nv_bfloat16* sinv, int L, int H, int HD,
+                                    __nv_bfloat16* y, float* rstd, cudaStream_t stream);
+cudaError_t launch_qk_norm_rope_bwd(const __nv_bfloat16* dy, const __nv_bfloat16* x, long long xs,
+                                    const __nv_bfloat16* w, const __nv_bfloat16* cosv, const __nv_bfloat16* sinv,
+                                    const float* rstd, int L, int H, int HD, __nv_bfloat16* dx, long long dxs,
+                                    float* partial, float* dw, cudaStream_t stream);
+cudaError_t launch_silu_mul_bwd(const __nv_bfloat16* gu, const __nv_bfloat16* dh, int rows, int I,
+                                __nv_bfloat16* dgu, cudaStream_t stream);
+
 cudaError_t launch_segment_meta(const int64_t* seq, int L, int tile, int64_t* pos_out, int32_t* run_start,
                                 int32_t* run_end, int32_t* tile_lo, int32_t* flags, cudaStream_t stream);
 

@@ -3,6 +3,7 @@
 #include "decode_attention.cu"
 #include "kv_append.cu"
 #include "elementwise.cu"
+#include "train_elementwise.cu"
 #include "segment_meta.cu"
 #include "varlen_attention.cu"
 #include "varlen_backward.cu"

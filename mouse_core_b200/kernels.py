@@ -231,3 +231,105 @@ def silu_mul(gate_up: torch.Tensor) -> torch.Tensor:
     _lib.call("mb_silu_mul", _p(gate_up), rows, I2 // 2, _p(out), _stream(gate_up))
     _count()
     return out
+
+
+# ---------------------------------------------------------------- training layer element-wise (K4)
+
+
+def _rows_view(x: torch.Tensor, name: str):
+    """``(rows, row_stride)`` of a 2-D bf16 view whose last dim is contiguous."""
+    if x.dim() != 2 or x.stride(1) != 1:
+        raise ValueError(f"{name} must be 2-D with a contiguous last dimension")
+    return x.shape[0], x.stride(0)
+
+
+def rmsnorm_fwd(x: torch.Tensor, weight: torch.Tensor, eps: float):
+    """``(y, rstd)``: ``y = weight * bf16(x * rstd)`` over the last dim; rstd f32 ``[rows]``."""
+    _need(x, "x", BF16)
+    _need(weight, "weight", BF16)
+    D = x.shape[-1]
+    rows = x.numel() // D
+    y = torch.empty_like(x)
+    rstd = torch.empty(rows, dtype=torch.float32, device=x.device)
+    _lib.call("mb_rmsnorm_fwd", _p(x), _p(weight), float(eps), rows, D, _p(y), _p(rstd), _stream(x))
+    _count()
+    return y, rstd
+
+
+def rmsnorm_bwd(dy: torch.Tensor, x: torch.Tensor, weight: torch.Tensor, rstd: torch.Tensor):
+    """``(dx bf16, dweight f32)`` of ``rmsnorm_fwd``."""
+    for name, t in (("dy", dy), ("x", x), ("weight", weight)):
+        _need(t, name, BF16)
+    _need(rstd, "rstd", torch.float32)
+    D = x.shape[-1]
+    rows = x.numel() // D
+    if dy.shape != x.shape or rstd.numel() != rows:
+        raise ValueError("dy must match x and rstd must hold one value per row")
+    dx = torch.empty_like(x)
+    dw = torch.empty(D, dtype=torch.float32, device=x.device)
+    n = int(_lib.load().mb_rmsnorm_bwd_scratch_floats(rows, D))
+    scratch = torch.empty(max(n, 1), dtype=torch.float32, device=x.device)
+    _lib.call("mb_rmsnorm_bwd", _p(dy), _p(x), _p(weight), _p(rstd), rows, D, _p(dx), _p(dw), _p(scratch), n,
+              _stream(x))
+    _count(2)
+    return dx, dw
+
+
+def qk_norm_rope_fwd(x: torch.Tensor, heads: int, head_dim: int, weight: torch.Tensor | None, eps: float,
+                     cos: torch.Tensor, sin: torch.Tensor):
+    """Per-head RMSNorm (skipped when ``weight`` is None) then rotate-half RoPE.
+    ``x`` is a 2-D ``[L, >= heads * head_dim]`` view (rows may be strided, e.g. the
+    q or k columns of a fused QKV projection); ``cos``/``sin`` ``[L, head_dim]``.
+    Returns ``(y [L, heads, head_dim], rstd f32 [L * heads] or None)``."""
+    _need(x, "x", BF16, contiguous=False)
+    L, xs = _rows_view(x, "x")
+    for name, t in (("cos", cos), ("sin", sin)):
+        _need(t, name, BF16)
+        if t.shape != (L, head_dim):
+            raise ValueError(f"{name} must be [L, head_dim]")
+    if weight is not None:
+        _need(weight, "weight", BF16)
+    y = torch.empty(L, heads, head_dim, dtype=BF16, device=x.device)
+    rstd = torch.empty(L * heads, dtype=torch.float32, device=x.device) if weight is not None else None
+    _lib.call("mb_qk_norm_rope_fwd", _p(x), xs, _p(weight), float(eps), _p(cos), _p(sin), L, heads, head_dim,
+              _p(y), _p(rstd), _stream(x))
+    _count()
+    return y, rstd
+
+
+def qk_norm_rope_bwd(dy: torch.Tensor, x: torch.Tensor, weight: torch.Tensor | None, cos: torch.Tensor,
+                     sin: torch.Tensor, rstd: torch.Tensor | None, dx: torch.Tensor):
+    """Gradient of ``qk_norm_rope_fwd``: writes ``dx`` (a 2-D view with a
+    contiguous last dim, e.g. the q or k columns of the fused QKV gradient) and
+    returns ``dweight`` f32 ``[head_dim]`` (None without a weight)."""
+    _need(dy, "dy", BF16)
+    L, heads, head_dim = dy.shape
+    _need(dx, "dx", BF16, contiguous=False)
+    _, dxs = _rows_view(dx, "dx")
+    xs = 0
+    if weight is not None:
+        _need(weight, "weight", BF16)
+        _need(x, "x", BF16, contiguous=False)
+        _need(rstd, "rstd", torch.float32)
+        _, xs = _rows_view(x, "x")
+    dw = torch.empty(head_dim, dtype=torch.float32, device=dy.device) if weight is not None else None
+    n = int(_lib.load().mb_qk_norm_rope_bwd_scratch_floats(L, heads, head_dim)) if weight is not None else 0
+    scratch = torch.empty(max(n, 1), dtype=torch.float32, device=dy.device) if weight is not None else None
+    _lib.call("mb_qk_norm_rope_bwd", _p(dy), _p(x) if weight is not None else None, xs, _p(weight), _p(cos),
+              _p(sin), _p(rstd), L, heads, head_dim, _p(dx), dxs, _p(dw), _p(scratch), n, _stream(dy))
+    _count(2 if weight is not None else 1)
+    return dw
+
+
+def silu_mul_bwd(gate_up: torch.Tensor, dh: torch.Tensor) -> torch.Tensor:
+    """``dgate_up [..., 2I]`` of ``silu_mul`` for upstream ``dh [..., I]``."""
+    _need(gate_up, "gate_up", BF16)
+    _need(dh, "dh", BF16)
+    I2 = gate_up.shape[-1]
+    rows = gate_up.numel() // I2
+    if dh.numel() != rows * (I2 // 2):
+        raise ValueError("dh must be [..., I] matching gate_up [..., 2I]")
+    dgu = torch.empty_like(gate_up)
+    _lib.call("mb_silu_mul_bwd", _p(gate_up), _p(dh), rows, I2 // 2, _p(dgu), _stream(gate_up))
+    _count()
+    return dgu

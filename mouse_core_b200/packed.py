@@ -16,8 +16,15 @@ FlexAttention:
 * The attention core is the tcgen05 kernel pair K5 (forward, saves the log2
   softmax denominator) / K6 (backward: deterministic dK/dV and dQ kernels)
   behind ``torch.autograd.Function``.
-* Projections, RMSNorms, RoPE and the MLP run through the model's own
-  transformers modules (cuBLAS GEMMs, torch autograd).
+* K4 element-wise kernels replace the layer's eager bf16 glue: RMSNorm
+  forward/backward (input, post-attention and final norms), the per-head
+  q/k RMSNorm + RoPE read straight out of one fused QKV projection (and its
+  gradient written straight back into the fused QKV gradient), and the
+  SiLU-gated product over one fused gate|up projection. The projections are
+  cuBLAS GEMMs over the concatenated weights. A model whose shapes the K4
+  kernels are not built for (hidden size not a multiple of 256 up to 2048,
+  biased projections, an activation other than SiLU) keeps those pieces on
+  its own transformers modules.
 
 Ids that are not sorted (one id owning several runs) are made contiguous by a
 stable sort before the attention call and scattered back after it, which
@@ -91,6 +98,86 @@ def _rotate_half(x):
     return torch.cat((-x[..., half:], x[..., :half]), dim=-1)
 
 
+class _RMSNorm(torch.autograd.Function):
+    """``weight * bf16(x * rsqrt(mean(x^2) + eps))`` over the last dim (K4)."""
+
+    @staticmethod
+    def forward(ctx, x, weight, eps):
+        x = x.contiguous()
+        y, rstd = K.rmsnorm_fwd(x, weight, eps)
+        ctx.save_for_backward(x, weight, rstd)
+        return y
+
+    @staticmethod
+    def backward(ctx, dy):
+        x, weight, rstd = ctx.saved_tensors
+        dx, dw = K.rmsnorm_bwd(dy.contiguous(), x, weight, rstd)
+        return dx, dw.to(weight.dtype), None
+
+
+class _QKVHeads(torch.autograd.Function):
+    """Split a fused QKV projection ``[L, (Hq + 2 Hkv) hd]`` into attention
+    inputs: q and k through the per-head RMSNorm (when the model has one) and
+    rotate-half RoPE, v as is (K4)."""
+
+    @staticmethod
+    def forward(ctx, qkv, q_w, k_w, cos, sin, q_eps, k_eps, Hq, Hkv, hd):
+        nq, nk = Hq * hd, Hkv * hd
+        q, q_rstd = K.qk_norm_rope_fwd(qkv[:, :nq], Hq, hd, q_w, q_eps, cos, sin)
+        k, k_rstd = K.qk_norm_rope_fwd(qkv[:, nq:nq + nk], Hkv, hd, k_w, k_eps, cos, sin)
+        v = qkv[:, nq + nk:].reshape(qkv.shape[0], Hkv, hd).contiguous()
+        ctx.save_for_backward(qkv, q_w, k_w, cos, sin, q_rstd, k_rstd)
+        ctx.shape = (Hq, Hkv, hd)
+        return q, k, v
+
+    @staticmethod
+    def backward(ctx, dq, dk, dv):
+        qkv, q_w, k_w, cos, sin, q_rstd, k_rstd = ctx.saved_tensors
+        Hq, Hkv, hd = ctx.shape
+        nq, nk = Hq * hd, Hkv * hd
+        L = qkv.shape[0]
+        dqkv = torch.empty_like(qkv)
+        dqw = K.qk_norm_rope_bwd(dq.contiguous(), qkv[:, :nq], q_w, cos, sin, q_rstd, dqkv[:, :nq])
+        dkw = K.qk_norm_rope_bwd(dk.contiguous(), qkv[:, nq:nq + nk], k_w, cos, sin, k_rstd, dqkv[:, nq:nq + nk])
+        dqkv[:, nq + nk:].copy_(dv.reshape(L, nk))
+        return (dqkv, None if dqw is None else dqw.to(q_w.dtype), None if dkw is None else dkw.to(k_w.dtype),
+                None, None, None, None, None, None, None)
+
+
+class _SiluMul(torch.autograd.Function):
+    """``bf16(silu(gate)) * up`` over a fused ``gate|up`` projection ``[L, 2I]`` (K4)."""
+
+    @staticmethod
+    def forward(ctx, gate_up):
+        gate_up = gate_up.contiguous()
+        ctx.save_for_backward(gate_up)
+        return K.silu_mul(gate_up)
+
+    @staticmethod
+    def backward(ctx, dh):
+        (gate_up,) = ctx.saved_tensors
+        return K.silu_mul_bwd(gate_up, dh.contiguous())
+
+
+def _norm(module, x):
+    """The model's RMSNorm through K4 when its width is supported (an
+    ``nn.Identity`` final norm, as the backbones install, stays as is)."""
+    D = x.shape[-1]
+    if hasattr(module, "variance_epsilon") and D % 256 == 0 and D <= 2048:
+        return _RMSNorm.apply(x, module.weight, float(module.variance_epsilon))
+    return module(x)
+
+
+def _fused_attention_inputs(attn):
+    """True when the attention block has bias-free q/k/v projections."""
+    return all(getattr(attn, n).bias is None for n in ("q_proj", "k_proj", "v_proj"))
+
+
+def _fused_mlp(mlp, cfg):
+    return (getattr(cfg, "hidden_act", "silu") == "silu" and mlp.gate_proj.bias is None
+            and mlp.up_proj.bias is None)
+
+
 def flex_packed_forward(*, model: torch.nn.Module, embeds: torch.Tensor, sequence_ids: torch.Tensor,
                         output_hidden_states: bool = False):
     """Full pass over a flat packed sequence ``embeds [L, D]``.
@@ -125,29 +212,46 @@ def flex_packed_forward(*, model: torch.nn.Module, embeds: torch.Tensor, sequenc
         return (h, tuple(x for _ in hf.layers)) if output_hidden_states else h
     layout = SegmentLayout(sequence_ids, device)
     cos, sin = hf.rotary_emb(x.unsqueeze(0), layout.position_ids.unsqueeze(0))
-    cos, sin = cos[0].unsqueeze(1), sin[0].unsqueeze(1)  # [L, 1, hd]
+    cos, sin = cos[0].contiguous(), sin[0].contiguous()  # [L, hd]
 
     h = x
     hiddens = []
     for layer in hf.layers:
         residual = h
-        hn = layer.input_layernorm(h)
+        hn = _norm(layer.input_layernorm, h)
         attn = layer.self_attn
-        q = attn.q_proj(hn).view(L, n_heads, hd)
-        k = attn.k_proj(hn).view(L, n_kv, hd)
         q_norm = getattr(attn, "q_norm", None)
-        if q_norm is not None:
-            q = q_norm(q)
-            k = attn.k_norm(k)
-        v = attn.v_proj(hn).view(L, n_kv, hd)
-        q = q * cos + _rotate_half(q) * sin
-        k = k * cos + _rotate_half(k) * sin
+        if _fused_attention_inputs(attn):
+            w_qkv = torch.cat((attn.q_proj.weight, attn.k_proj.weight, attn.v_proj.weight), dim=0)
+            qkv = torch.nn.functional.linear(hn, w_qkv)
+            if q_norm is not None:
+                q, k, v = _QKVHeads.apply(qkv, q_norm.weight, attn.k_norm.weight, cos, sin,
+                                          float(q_norm.variance_epsilon), float(attn.k_norm.variance_epsilon),
+                                          n_heads, n_kv, hd)
+            else:
+                q, k, v = _QKVHeads.apply(qkv, None, None, cos, sin, 0.0, 0.0, n_heads, n_kv, hd)
+        else:
+            q = attn.q_proj(hn).view(L, n_heads, hd)
+            k = attn.k_proj(hn).view(L, n_kv, hd)
+            if q_norm is not None:
+                q = q_norm(q)
+                k = attn.k_norm(k)
+            v = attn.v_proj(hn).view(L, n_kv, hd)
+            c, s_ = cos.unsqueeze(1), sin.unsqueeze(1)
+            q = q * c + _rotate_half(q) * s_
+            k = k * c + _rotate_half(k) * s_
         o = layout.attend(q, k, v, float(attn.scaling))
         h = residual + attn.o_proj(o.reshape(L, n_heads * hd))
-        h = h + layer.mlp(layer.post_attention_layernorm(h))
+        mlp = layer.mlp
+        hn = _norm(layer.post_attention_layernorm, h)
+        if _fused_mlp(mlp, cfg):
+            gate_up = torch.nn.functional.linear(hn, torch.cat((mlp.gate_proj.weight, mlp.up_proj.weight), dim=0))
+            h = h + mlp.down_proj(_SiluMul.apply(gate_up))
+        else:
+            h = h + mlp(hn)
         if output_hidden_states:
             hiddens.append(h)
-    h = hf.norm(h)
+    h = _norm(hf.norm, h)
     if output_hidden_states:
         return h, tuple(hiddens)
     return h

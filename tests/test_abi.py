@@ -67,3 +67,29 @@ def test_zero_sized_calls_are_noops(lib):
                             None, None, None) == 0
     assert lib.mb_page_copy(None, None, None, None, 0, 8, None) == 0
     assert lib.mb_rmsnorm(None, None, None, 1e-6, 0, 8, None, None, None) == 0
+
+
+def test_training_elementwise_argument_rules(lib):
+    # dim must be a multiple of 256 (<= 2048); rejected before any CUDA call
+    assert lib.mb_rmsnorm_fwd(None, None, 1e-6, 4, 1000, None, None, None) == 2
+    assert b"256" in lib.mb_last_error()
+    assert lib.mb_rmsnorm_fwd(None, None, 1e-6, 4, 4096, None, None, None) == 2
+    assert lib.mb_rmsnorm_fwd(None, None, 1e-6, 0, 1024, None, None, None) == 0
+    assert lib.mb_rmsnorm_fwd(None, None, 1e-6, 4, 1024, None, None, None) == 1
+    # scratch sizing: one row of dim floats per reduction block
+    n = lib.mb_rmsnorm_bwd_scratch_floats(32768, 1024)
+    assert n > 0 and n % 1024 == 0
+    assert lib.mb_rmsnorm_bwd_scratch_floats(0, 1024) == 0
+    assert lib.mb_rmsnorm_bwd(None, None, None, None, 8, 1024, None, ctypes.c_void_p(16), ctypes.c_void_p(16),
+                              1, None) == 1
+    assert b"NULL" in lib.mb_last_error()
+    # q/k norm + RoPE: head_dim 64/128 only, strides checked
+    assert lib.mb_qk_norm_rope_fwd(None, 96 * 4, None, 1e-6, None, None, 4, 4, 96, None, None, None) == 2
+    assert lib.mb_qk_norm_rope_fwd(None, 0, None, 1e-6, None, None, 0, 4, 128, None, None, None) == 0
+    assert lib.mb_qk_norm_rope_bwd_scratch_floats(1024, 16, 128) % 128 == 0
+    assert lib.mb_qk_norm_rope_bwd(None, None, 0, ctypes.c_void_p(16), None, None, None, 4, 4, 128, None, 512,
+                                   None, None, 0, None) == 1
+    assert b"dweight" in lib.mb_last_error()
+    # SiLU-gated product backward
+    assert lib.mb_silu_mul_bwd(None, None, 0, 3072, None, None) == 0
+    assert lib.mb_silu_mul_bwd(None, None, 4, 3071, None, None) == 1
