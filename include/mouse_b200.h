@@ -199,14 +199,18 @@ int mb_segment_meta(const int64_t* sequence_ids, int L, int tile, int64_t* posit
  *   flex_train.py:145-150). dim a multiple of 256, <= 2048.
  * mb_rmsnorm_bwd: dx and dweight (= sum over rows of dy * bf16(x * rstd));
  *   scratch holds mb_rmsnorm_bwd_scratch_floats(rows, dim) floats.
- * mb_qk_norm_rope_fwd: per (token, head) of x (rows x_row_stride elements
- *   apart, e.g. the q or k slice of a fused QKV projection): optional
- *   per-head RMSNorm (q_norm / k_norm; weight NULL skips it), then
- *   y = n * cos + rotate_half(n) * sin with cos/sin [L, head_dim] per token.
- *   y is [L, heads, head_dim]; rstd f32 [L * heads] when weight is set.
- * mb_qk_norm_rope_bwd: dx (written with row stride dx_row_stride, e.g. into
- *   the fused QKV gradient) and dweight [head_dim] when weight is set;
- *   scratch holds mb_qk_norm_rope_bwd_scratch_floats(L, heads, head_dim).
+ * mb_qkv_heads_fwd: the attention inputs from one fused projection
+ *   qkv [L, qkv_row_stride] = q (q_heads * hd) | k (kv_heads * hd) | v: q and
+ *   k through the optional per-head RMSNorm (q_norm / k_norm of
+ *   flex_train.py:137-142; both weights or neither) then y = n * cos +
+ *   rotate_half(n) * sin (flex_train.py:143-146, cos/sin [L, head_dim] per
+ *   token), v copied: q [L, q_heads, hd], k / v [L, kv_heads, hd]; q_rstd
+ *   [L * q_heads] and k_rstd [L * kv_heads] f32 with the norm. Row strides
+ *   multiples of 8; tensors 16-byte aligned.
+ * mb_qkv_heads_bwd: gradient of mb_qkv_heads_fwd for dq, dk, dv: writes the
+ *   whole of dqkv (row stride dqkv_row_stride) and, with the norm, the f32
+ *   norm-weight gradients [head_dim]; scratch holds
+ *   mb_qkv_heads_bwd_scratch_floats(L, head_dim) floats.
  * mb_silu_mul_bwd: gradient of h = silu(gate) * up over gate_up [rows, 2I]:
  *   dgate_up[:, :I] = dh * up * silu'(gate), dgate_up[:, I:] = dh * silu(gate).
  * ------------------------------------------------------------------- */
@@ -215,13 +219,15 @@ int mb_rmsnorm_fwd(const void* x, const void* weight, float eps, int rows, int d
 size_t mb_rmsnorm_bwd_scratch_floats(int rows, int dim);
 int mb_rmsnorm_bwd(const void* dy, const void* x, const void* weight, const float* rstd, int rows, int dim, void* dx,
                    float* dweight, float* scratch, size_t scratch_floats, mb_stream_t stream);
-int mb_qk_norm_rope_fwd(const void* x, long long x_row_stride, const void* weight, float eps, const void* cos,
-                        const void* sin, int L, int heads, int head_dim, void* y, float* rstd, mb_stream_t stream);
-size_t mb_qk_norm_rope_bwd_scratch_floats(int L, int heads, int head_dim);
-int mb_qk_norm_rope_bwd(const void* dy, const void* x, long long x_row_stride, const void* weight, const void* cos,
-                        const void* sin, const float* rstd, int L, int heads, int head_dim, void* dx,
-                        long long dx_row_stride, float* dweight, float* scratch, size_t scratch_floats,
-                        mb_stream_t stream);
+int mb_qkv_heads_fwd(const void* qkv, long long qkv_row_stride, int L, int q_heads, int kv_heads, int head_dim,
+                     const void* q_norm_weight, const void* k_norm_weight, float q_eps, float k_eps, const void* cos,
+                     const void* sin, void* q, void* k, void* v, float* q_rstd, float* k_rstd, mb_stream_t stream);
+size_t mb_qkv_heads_bwd_scratch_floats(int L, int head_dim);
+int mb_qkv_heads_bwd(const void* dq, const void* dk, const void* dv, const void* qkv, long long qkv_row_stride,
+                     int L, int q_heads, int kv_heads, int head_dim, const void* q_norm_weight,
+                     const void* k_norm_weight, const void* cos, const void* sin, const float* q_rstd,
+                     const float* k_rstd, void* dqkv, long long dqkv_row_stride, float* dq_norm_weight,
+                     float* dk_norm_weight, float* scratch, size_t scratch_floats, mb_stream_t stream);
 int mb_silu_mul_bwd(const void* gate_up, const void* dh, int rows, int inter, void* dgate_up, mb_stream_t stream);
 
 #ifdef __cplusplus

@@ -355,6 +355,7 @@ int check_norm_dim(int rows, int dim) {
 int check_head_shape(int L, int heads, int head_dim) {
   if (L < 0 || heads <= 0) return fail(MB_ERR_INVALID_ARG, "L >= 0 and heads > 0 required");
   if (head_dim != 64 && head_dim != 128) return fail(MB_ERR_UNSUPPORTED, "head_dim must be 64 or 128");
+  if ((long long)L * heads > 0x7fffffffLL) return fail(MB_ERR_UNSUPPORTED, "L * heads must be below 2^31");
   return MB_OK;
 }
 }  // namespace
@@ -373,7 +374,8 @@ int mb_rmsnorm_fwd(const void* x, const void* weight, float eps, int rows, int d
 
 size_t mb_rmsnorm_bwd_scratch_floats(int rows, int dim) {
   if (rows <= 0 || dim <= 0) return 0;
-  return (size_t)mb::rmsnorm_bwd_partials(rows) * (size_t)dim;
+  if (dim % 256 || dim > 2048) return 0;
+  return (size_t)mb::rmsnorm_bwd_partials(rows, dim) * (size_t)dim;
 }
 
 int mb_rmsnorm_bwd(const void* dy, const void* x, const void* weight, const float* rstd, int rows, int dim, void* dx,
@@ -393,50 +395,65 @@ int mb_rmsnorm_bwd(const void* dy, const void* x, const void* weight, const floa
   return e == cudaSuccess ? MB_OK : cuda_fail(e, "rmsnorm bwd launch");
 }
 
-int mb_qk_norm_rope_fwd(const void* x, long long x_row_stride, const void* weight, float eps, const void* cos,
-                        const void* sin, int L, int heads, int head_dim, void* y, float* rstd, mb_stream_t stream) {
-  if (int rc = check_head_shape(L, heads, head_dim)) return rc;
+int mb_qkv_heads_fwd(const void* qkv, long long qkv_row_stride, int L, int q_heads, int kv_heads, int head_dim,
+                     const void* q_norm_weight, const void* k_norm_weight, float q_eps, float k_eps, const void* cos,
+                     const void* sin, void* q, void* k, void* v, float* q_rstd, float* k_rstd, mb_stream_t stream) {
+  if (int rc = check_head_shape(L, q_heads + 2 * kv_heads, head_dim)) return rc;
+  if (kv_heads <= 0 || q_heads <= 0) return fail(MB_ERR_INVALID_ARG, "head counts must be > 0");
+  if (!q_norm_weight != !k_norm_weight) return fail(MB_ERR_INVALID_ARG, "pass both norm weights or neither");
   if (L == 0) return MB_OK;
-  if (!x || !cos || !sin || !y || (weight && !rstd)) return fail(MB_ERR_INVALID_ARG, "a required pointer is NULL");
-  if (x_row_stride < (long long)heads * head_dim || x_row_stride % 2)
-    return fail(MB_ERR_INVALID_ARG, "x_row_stride must be even and >= heads * head_dim");
-  if (!aligned(x, 4) || !aligned(cos, 4) || !aligned(sin, 4) || !aligned(y, 4))
-    return fail(MB_ERR_INVALID_ARG, "x, cos, sin and y must be 4-byte aligned");
-  cudaError_t e = mb::launch_qk_norm_rope_fwd(
-      static_cast<const __nv_bfloat16*>(x), x_row_stride, static_cast<const __nv_bfloat16*>(weight), eps,
-      static_cast<const __nv_bfloat16*>(cos), static_cast<const __nv_bfloat16*>(sin), L, heads, head_dim,
-      static_cast<__nv_bfloat16*>(y), rstd, (cudaStream_t)stream);
-  return e == cudaSuccess ? MB_OK : cuda_fail(e, "qk norm rope fwd launch");
+  if (!qkv || !cos || !sin || !q || !k || !v) return fail(MB_ERR_INVALID_ARG, "a required pointer is NULL");
+  if (q_norm_weight && (!q_rstd || !k_rstd)) return fail(MB_ERR_INVALID_ARG, "the norm needs q_rstd and k_rstd");
+  if (qkv_row_stride < (long long)(q_heads + 2 * kv_heads) * head_dim || qkv_row_stride % 8)
+    return fail(MB_ERR_INVALID_ARG, "qkv_row_stride must be a multiple of 8 and >= (q_heads + 2 kv_heads) * head_dim");
+  const void* ptrs[] = {qkv, cos, sin, q, k, v, q_norm_weight, k_norm_weight};
+  for (const void* p : ptrs)
+    if (p && !aligned(p, 16)) return fail(MB_ERR_INVALID_ARG, "tensors must be 16-byte aligned");
+  cudaError_t e = mb::launch_qkv_heads_fwd(
+      static_cast<const __nv_bfloat16*>(qkv), qkv_row_stride, L, q_heads, kv_heads, head_dim,
+      static_cast<const __nv_bfloat16*>(q_norm_weight), static_cast<const __nv_bfloat16*>(k_norm_weight), q_eps,
+      k_eps, static_cast<const __nv_bfloat16*>(cos), static_cast<const __nv_bfloat16*>(sin),
+      static_cast<__nv_bfloat16*>(q), static_cast<__nv_bfloat16*>(k), static_cast<__nv_bfloat16*>(v), q_rstd, k_rstd,
+      (cudaStream_t)stream);
+  return e == cudaSuccess ? MB_OK : cuda_fail(e, "qkv heads fwd launch");
 }
 
-size_t mb_qk_norm_rope_bwd_scratch_floats(int L, int heads, int head_dim) {
-  if (L <= 0 || heads <= 0 || head_dim <= 0) return 0;
-  return (size_t)mb::qk_norm_rope_bwd_partials(L, heads) * (size_t)head_dim;
+size_t mb_qkv_heads_bwd_scratch_floats(int L, int head_dim) {
+  if (L <= 0 || (head_dim != 64 && head_dim != 128)) return 0;
+  return (size_t)mb::qkv_heads_bwd_partials(L, head_dim) * 2 * (size_t)head_dim;
 }
 
-int mb_qk_norm_rope_bwd(const void* dy, const void* x, long long x_row_stride, const void* weight, const void* cos,
-                        const void* sin, const float* rstd, int L, int heads, int head_dim, void* dx,
-                        long long dx_row_stride, float* dweight, float* scratch, size_t scratch_floats,
-                        mb_stream_t stream) {
-  if (int rc = check_head_shape(L, heads, head_dim)) return rc;
-  if (weight && !dweight) return fail(MB_ERR_INVALID_ARG, "a weight needs dweight");
+int mb_qkv_heads_bwd(const void* dq, const void* dk, const void* dv, const void* qkv, long long qkv_row_stride,
+                     int L, int q_heads, int kv_heads, int head_dim, const void* q_norm_weight,
+                     const void* k_norm_weight, const void* cos, const void* sin, const float* q_rstd,
+                     const float* k_rstd, void* dqkv, long long dqkv_row_stride, float* dq_norm_weight,
+                     float* dk_norm_weight, float* scratch, size_t scratch_floats, mb_stream_t stream) {
+  if (int rc = check_head_shape(L, q_heads + 2 * kv_heads, head_dim)) return rc;
+  if (kv_heads <= 0 || q_heads <= 0) return fail(MB_ERR_INVALID_ARG, "head counts must be > 0");
+  const bool norm = q_norm_weight != nullptr;
+  if (norm != (k_norm_weight != nullptr)) return fail(MB_ERR_INVALID_ARG, "pass both norm weights or neither");
+  if (norm && (!dq_norm_weight || !dk_norm_weight)) return fail(MB_ERR_INVALID_ARG, "norm weights need dweights");
   if (L > 0) {
-    if (!dy || !cos || !sin || !dx) return fail(MB_ERR_INVALID_ARG, "a required pointer is NULL");
-    if (weight && (!x || !rstd || !scratch)) return fail(MB_ERR_INVALID_ARG, "the norm needs x, rstd and scratch");
-    if (weight && scratch_floats < mb_qk_norm_rope_bwd_scratch_floats(L, heads, head_dim))
-      return fail(MB_ERR_INVALID_ARG, "scratch is smaller than mb_qk_norm_rope_bwd_scratch_floats");
-    const long long need = (long long)heads * head_dim;
-    if (dx_row_stride < need || dx_row_stride % 2 || (weight && (x_row_stride < need || x_row_stride % 2)))
-      return fail(MB_ERR_INVALID_ARG, "row strides must be even and >= heads * head_dim");
-    if (!aligned(dy, 4) || !aligned(cos, 4) || !aligned(sin, 4) || !aligned(dx, 4) || (x && !aligned(x, 4)))
-      return fail(MB_ERR_INVALID_ARG, "dy, x, cos, sin and dx must be 4-byte aligned");
+    if (!dq || !dk || !dv || !cos || !sin || !dqkv) return fail(MB_ERR_INVALID_ARG, "a required pointer is NULL");
+    if (norm && (!qkv || !q_rstd || !k_rstd || !scratch))
+      return fail(MB_ERR_INVALID_ARG, "the norm needs qkv, q_rstd, k_rstd and scratch");
+    if (norm && scratch_floats < mb_qkv_heads_bwd_scratch_floats(L, head_dim))
+      return fail(MB_ERR_INVALID_ARG, "scratch is smaller than mb_qkv_heads_bwd_scratch_floats");
+    const long long need = (long long)(q_heads + 2 * kv_heads) * head_dim;
+    if (dqkv_row_stride < need || dqkv_row_stride % 8 || (norm && (qkv_row_stride < need || qkv_row_stride % 8)))
+      return fail(MB_ERR_INVALID_ARG, "row strides must be multiples of 8 and >= (q_heads + 2 kv_heads) * head_dim");
+    const void* ptrs[] = {dq, dk, dv, qkv, cos, sin, dqkv, q_norm_weight, k_norm_weight};
+    for (const void* p : ptrs)
+      if (p && !aligned(p, 16)) return fail(MB_ERR_INVALID_ARG, "tensors must be 16-byte aligned");
   }
-  cudaError_t e = mb::launch_qk_norm_rope_bwd(
-      static_cast<const __nv_bfloat16*>(dy), static_cast<const __nv_bfloat16*>(x), x_row_stride,
-      static_cast<const __nv_bfloat16*>(weight), static_cast<const __nv_bfloat16*>(cos),
-      static_cast<const __nv_bfloat16*>(sin), rstd, L, heads, head_dim, static_cast<__nv_bfloat16*>(dx),
-      dx_row_stride, scratch, weight ? dweight : nullptr, (cudaStream_t)stream);
-  return e == cudaSuccess ? MB_OK : cuda_fail(e, "qk norm rope bwd launch");
+  cudaError_t e = mb::launch_qkv_heads_bwd(
+      static_cast<const __nv_bfloat16*>(dq), static_cast<const __nv_bfloat16*>(dk),
+      static_cast<const __nv_bfloat16*>(dv), static_cast<const __nv_bfloat16*>(qkv), qkv_row_stride, L, q_heads,
+      kv_heads, head_dim, static_cast<const __nv_bfloat16*>(q_norm_weight),
+      static_cast<const __nv_bfloat16*>(k_norm_weight), static_cast<const __nv_bfloat16*>(cos),
+      static_cast<const __nv_bfloat16*>(sin), q_rstd, k_rstd, static_cast<__nv_bfloat16*>(dqkv), dqkv_row_stride,
+      dq_norm_weight, dk_norm_weight, scratch, (cudaStream_t)stream);
+  return e == cudaSuccess ? MB_OK : cuda_fail(e, "qkv heads bwd launch");
 }
 
 int mb_silu_mul_bwd(const void* gate_up, const void* dh, int rows, int inter, void* dgate_up, mb_stream_t stream) {

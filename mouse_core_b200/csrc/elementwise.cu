@@ -59,25 +59,57 @@ cudaError_t launch_rmsnorm(const __nv_bfloat16* x, const __nv_bfloat16* residual
   return cudaGetLastError();
 }
 
-__global__ void silu_mul_kernel(const __nv_bfloat16* gu, int I, long long total_pairs, __nv_bfloat16* out) {
-  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total_pairs;
-       i += (long long)gridDim.x * blockDim.x) {
-    const long long row = (i * 2) / I, col = (i * 2) % I;
-    const float2 g = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(gu + row * 2 * I + col));
-    const float2 u = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(gu + row * 2 * I + I + col));
-    // silu(gate) is rounded to bf16 before the product, as the module's bf16
-    // activation output is.
-    const float a = __bfloat162float(__float2bfloat16_rn(g.x / (1.f + expf(-g.x))));
-    const float b = __bfloat162float(__float2bfloat16_rn(g.y / (1.f + expf(-g.y))));
-    *reinterpret_cast<__nv_bfloat162*>(out + row * I + col) = __floats2bfloat162_rn(a * u.x, b * u.y);
+// silu(gate) is rounded to bf16 before the product, as the module's bf16
+// activation output is. Vector path: 8 elements (16 bytes) per thread,
+// blockIdx.y strides rows; otherwise pairs of elements.
+__device__ __forceinline__ float silu_bf16(float g) {
+  return __bfloat162float(__float2bfloat16_rn(g / (1.f + expf(-g))));
+}
+
+__global__ void __launch_bounds__(128) silu_mul_vec_kernel(const __nv_bfloat16* __restrict__ gu, int rows, int I,
+                                                           __nv_bfloat16* __restrict__ out) {
+  const int c = blockIdx.x * blockDim.x + threadIdx.x;
+  if (c >= (I >> 3)) return;
+  for (int row = blockIdx.y; row < rows; row += gridDim.y) {
+    const size_t gbase = (size_t)row * 2 * I + (size_t)c * 8;
+    const uint4 gv = *reinterpret_cast<const uint4*>(gu + gbase);
+    const uint4 uv = *reinterpret_cast<const uint4*>(gu + gbase + I);
+    const uint32_t* g2 = reinterpret_cast<const uint32_t*>(&gv);
+    const uint32_t* u2 = reinterpret_cast<const uint32_t*>(&uv);
+    uint4 o;
+    uint32_t* o2 = reinterpret_cast<uint32_t*>(&o);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float2 g = unpack_bf16x2(g2[i]), u = unpack_bf16x2(u2[i]);
+      o2[i] = pack_bf16x2(silu_bf16(g.x) * u.x, silu_bf16(g.y) * u.y);
+    }
+    *reinterpret_cast<uint4*>(out + (size_t)row * I + (size_t)c * 8) = o;
   }
 }
 
+__global__ void silu_mul_kernel(const __nv_bfloat16* __restrict__ gu, int rows, int I,
+                                __nv_bfloat16* __restrict__ out) {
+  for (int row = blockIdx.y; row < rows; row += gridDim.y)
+    for (int c = blockIdx.x * blockDim.x + threadIdx.x; c < (I >> 1); c += gridDim.x * blockDim.x) {
+      const size_t gbase = (size_t)row * 2 * I + (size_t)c * 2;
+      const float2 g = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(gu + gbase));
+      const float2 u = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(gu + gbase + I));
+      *reinterpret_cast<uint32_t*>(out + (size_t)row * I + (size_t)c * 2) =
+          pack_bf16x2(silu_bf16(g.x) * u.x, silu_bf16(g.y) * u.y);
+    }
+}
+
 cudaError_t launch_silu_mul(const __nv_bfloat16* gate_up, int rows, int I, __nv_bfloat16* out, cudaStream_t stream) {
-  const long long pairs = (long long)rows * I / 2;
-  if (pairs <= 0) return cudaSuccess;
-  const int blocks = (int)std::min<long long>((pairs + 255) / 256, 148 * 16);
-  silu_mul_kernel<<<blocks, 256, 0, stream>>>(gate_up, I, pairs, out);
+  if (rows <= 0 || I <= 0) return cudaSuccess;
+  const int by = std::min(rows, 65535);
+  const bool vec = I % 8 == 0 && (reinterpret_cast<uintptr_t>(gate_up) & 15) == 0 &&
+                   (reinterpret_cast<uintptr_t>(out) & 15) == 0;
+  if (vec) {
+    silu_mul_vec_kernel<<<dim3((unsigned)((I / 8 + 127) / 128), (unsigned)by), 128, 0, stream>>>(gate_up, rows, I, out);
+  } else {
+    silu_mul_kernel<<<dim3((unsigned)std::min((I / 2 + 127) / 128, 64), (unsigned)by), 128, 0, stream>>>(gate_up, rows,
+                                                                                                      I, out);
+  }
   return cudaGetLastError();
 }
 

@@ -101,18 +101,22 @@ cudaError_t launch_varlen_bwd(const CUtensorMap& qm, const CUtensorMap& km, cons
 // Training element-wise kernels (train_elementwise.cu).
 cudaError_t launch_rmsnorm_fwd(const __nv_bfloat16* x, const __nv_bfloat16* w, float eps, int rows, int D,
                                __nv_bfloat16* y, float* rstd, cudaStream_t stream);
-int rmsnorm_bwd_partials(int rows);
+int rmsnorm_bwd_partials(int rows, int D);
 cudaError_t launch_rmsnorm_bwd(const __nv_bfloat16* dy, const __nv_bfloat16* x, const __nv_bfloat16* w,
                                const float* rstd, int rows, int D, __nv_bfloat16* dx, float* partial, float* dw,
                                cudaStream_t stream);
-int qk_norm_rope_bwd_partials(int L, int H);
-cudaError_t launch_qk_norm_rope_fwd(const __nv_bfloat16* x, long long xs, const __nv_bfloat16* w, float eps,
-                                    const __nv_bfloat16* cosv, const __nv_bfloat16* sinv, int L, int H, int HD,
-                                    __nv_bfloat16* y, float* rstd, cudaStream_t stream);
-cudaError_t launch_qk_norm_rope_bwd(const __nv_bfloat16* dy, const __nv_bfloat16* x, long long xs,
-                                    const __nv_bfloat16* w, const __nv_bfloat16* cosv, const __nv_bfloat16* sinv,
-                                    const float* rstd, int L, int H, int HD, __nv_bfloat16* dx, long long dxs,
-                                    float* partial, float* dw, cudaStream_t stream);
+int qkv_heads_bwd_partials(int L, int HD);
+cudaError_t launch_qkv_heads_fwd(const __nv_bfloat16* qkv, long long xs, int L, int Hq, int Hkv, int HD,
+                                 const __nv_bfloat16* qw, const __nv_bfloat16* kw, float q_eps, float k_eps,
+                                 const __nv_bfloat16* cosv, const __nv_bfloat16* sinv, __nv_bfloat16* q,
+                                 __nv_bfloat16* k, __nv_bfloat16* v, float* q_rstd, float* k_rstd,
+                                 cudaStream_t stream);
+cudaError_t launch_qkv_heads_bwd(const __nv_bfloat16* dq, const __nv_bfloat16* dk, const __nv_bfloat16* dv,
+                                 const __nv_bfloat16* qkv, long long xs, int L, int Hq, int Hkv, int HD,
+                                 const __nv_bfloat16* qw, const __nv_bfloat16* kw, const __nv_bfloat16* cosv,
+                                 const __nv_bfloat16* sinv, const float* q_rstd, const float* k_rstd,
+                                 __nv_bfloat16* dqkv, long long dxs, float* dqw, float* dkw, float* partial,
+                                 cudaStream_t stream);
 cudaError_t launch_silu_mul_bwd(const __nv_bfloat16* gu, const __nv_bfloat16* dh, int rows, int I,
                                 __nv_bfloat16* dgu, cudaStream_t stream);
 

@@ -275,50 +275,73 @@ def rmsnorm_bwd(dy: torch.Tensor, x: torch.Tensor, weight: torch.Tensor, rstd: t
     return dx, dw
 
 
-def qk_norm_rope_fwd(x: torch.Tensor, heads: int, head_dim: int, weight: torch.Tensor | None, eps: float,
-                     cos: torch.Tensor, sin: torch.Tensor):
-    """Per-head RMSNorm (skipped when ``weight`` is None) then rotate-half RoPE.
-    ``x`` is a 2-D ``[L, >= heads * head_dim]`` view (rows may be strided, e.g. the
-    q or k columns of a fused QKV projection); ``cos``/``sin`` ``[L, head_dim]``.
-    Returns ``(y [L, heads, head_dim], rstd f32 [L * heads] or None)``."""
-    _need(x, "x", BF16, contiguous=False)
-    L, xs = _rows_view(x, "x")
+def qkv_heads_fwd(qkv: torch.Tensor, q_heads: int, kv_heads: int, head_dim: int, cos: torch.Tensor,
+                  sin: torch.Tensor, q_norm_weight: torch.Tensor | None = None,
+                  k_norm_weight: torch.Tensor | None = None, q_eps: float = 1e-6, k_eps: float = 1e-6):
+    """Attention inputs from a fused projection ``qkv [L, >= (Hq + 2 Hkv) hd]``
+    (rows may be strided, last dim contiguous): q and k through the optional
+    per-head RMSNorm and rotate-half RoPE (``cos``/``sin [L, hd]``), v copied.
+    Returns ``(q [L,Hq,hd], k [L,Hkv,hd], v [L,Hkv,hd], q_rstd, k_rstd)``
+    (the rstd tensors are None without the norm)."""
+    _need(qkv, "qkv", BF16, contiguous=False)
+    L, xs = _rows_view(qkv, "qkv")
     for name, t in (("cos", cos), ("sin", sin)):
         _need(t, name, BF16)
         if t.shape != (L, head_dim):
             raise ValueError(f"{name} must be [L, head_dim]")
-    if weight is not None:
-        _need(weight, "weight", BF16)
-    y = torch.empty(L, heads, head_dim, dtype=BF16, device=x.device)
-    rstd = torch.empty(L * heads, dtype=torch.float32, device=x.device) if weight is not None else None
-    _lib.call("mb_qk_norm_rope_fwd", _p(x), xs, _p(weight), float(eps), _p(cos), _p(sin), L, heads, head_dim,
-              _p(y), _p(rstd), _stream(x))
+    norm = q_norm_weight is not None
+    if norm != (k_norm_weight is not None):
+        raise ValueError("pass both norm weights or neither")
+    if norm:
+        _need(q_norm_weight, "q_norm_weight", BF16)
+        _need(k_norm_weight, "k_norm_weight", BF16)
+    dev = qkv.device
+    q = torch.empty(L, q_heads, head_dim, dtype=BF16, device=dev)
+    k = torch.empty(L, kv_heads, head_dim, dtype=BF16, device=dev)
+    v = torch.empty(L, kv_heads, head_dim, dtype=BF16, device=dev)
+    q_rstd = torch.empty(L * q_heads, dtype=torch.float32, device=dev) if norm else None
+    k_rstd = torch.empty(L * kv_heads, dtype=torch.float32, device=dev) if norm else None
+    _lib.call("mb_qkv_heads_fwd", _p(qkv), xs, L, q_heads, kv_heads, head_dim, _p(q_norm_weight),
+              _p(k_norm_weight), float(q_eps), float(k_eps), _p(cos), _p(sin), _p(q), _p(k), _p(v), _p(q_rstd),
+              _p(k_rstd), _stream(qkv))
     _count()
-    return y, rstd
+    return q, k, v, q_rstd, k_rstd
 
 
-def qk_norm_rope_bwd(dy: torch.Tensor, x: torch.Tensor, weight: torch.Tensor | None, cos: torch.Tensor,
-                     sin: torch.Tensor, rstd: torch.Tensor | None, dx: torch.Tensor):
-    """Gradient of ``qk_norm_rope_fwd``: writes ``dx`` (a 2-D view with a
-    contiguous last dim, e.g. the q or k columns of the fused QKV gradient) and
-    returns ``dweight`` f32 ``[head_dim]`` (None without a weight)."""
-    _need(dy, "dy", BF16)
-    L, heads, head_dim = dy.shape
-    _need(dx, "dx", BF16, contiguous=False)
-    _, dxs = _rows_view(dx, "dx")
-    xs = 0
-    if weight is not None:
-        _need(weight, "weight", BF16)
-        _need(x, "x", BF16, contiguous=False)
-        _need(rstd, "rstd", torch.float32)
-        _, xs = _rows_view(x, "x")
-    dw = torch.empty(head_dim, dtype=torch.float32, device=dy.device) if weight is not None else None
-    n = int(_lib.load().mb_qk_norm_rope_bwd_scratch_floats(L, heads, head_dim)) if weight is not None else 0
-    scratch = torch.empty(max(n, 1), dtype=torch.float32, device=dy.device) if weight is not None else None
-    _lib.call("mb_qk_norm_rope_bwd", _p(dy), _p(x) if weight is not None else None, xs, _p(weight), _p(cos),
-              _p(sin), _p(rstd), L, heads, head_dim, _p(dx), dxs, _p(dw), _p(scratch), n, _stream(dy))
-    _count(2 if weight is not None else 1)
-    return dw
+def qkv_heads_bwd(dq: torch.Tensor, dk: torch.Tensor, dv: torch.Tensor, qkv: torch.Tensor, cos: torch.Tensor,
+                  sin: torch.Tensor, q_norm_weight: torch.Tensor | None = None,
+                  k_norm_weight: torch.Tensor | None = None, q_rstd: torch.Tensor | None = None,
+                  k_rstd: torch.Tensor | None = None, dqkv: torch.Tensor | None = None):
+    """Gradient of ``qkv_heads_fwd``: fills ``dqkv`` (allocated like ``qkv``
+    when None) and returns ``(dqkv, dq_norm_weight f32, dk_norm_weight f32)``
+    (the weight gradients are None without the norm)."""
+    for name, t in (("dq", dq), ("dk", dk), ("dv", dv)):
+        _need(t, name, BF16)
+    L, Hq, hd = dq.shape
+    Hkv = dk.shape[1]
+    if dk.shape != (L, Hkv, hd) or dv.shape != dk.shape:
+        raise ValueError("dk and dv must be [L, Hkv, hd] matching dq")
+    _need(qkv, "qkv", BF16, contiguous=False)
+    _, xs = _rows_view(qkv, "qkv")
+    if dqkv is None:
+        dqkv = torch.empty(L, (Hq + 2 * Hkv) * hd, dtype=BF16, device=dq.device)
+    _need(dqkv, "dqkv", BF16, contiguous=False)
+    _, dxs = _rows_view(dqkv, "dqkv")
+    norm = q_norm_weight is not None
+    dqw = dkw = scratch = None
+    n = 0
+    if norm:
+        _need(q_rstd, "q_rstd", torch.float32)
+        _need(k_rstd, "k_rstd", torch.float32)
+        dqw = torch.empty(hd, dtype=torch.float32, device=dq.device)
+        dkw = torch.empty(hd, dtype=torch.float32, device=dq.device)
+        n = int(_lib.load().mb_qkv_heads_bwd_scratch_floats(L, hd))
+        scratch = torch.empty(max(n, 1), dtype=torch.float32, device=dq.device)
+    _lib.call("mb_qkv_heads_bwd", _p(dq), _p(dk), _p(dv), _p(qkv), xs, L, Hq, Hkv, hd, _p(q_norm_weight),
+              _p(k_norm_weight), _p(cos), _p(sin), _p(q_rstd), _p(k_rstd), _p(dqkv), dxs, _p(dqw), _p(dkw),
+              _p(scratch), n, _stream(dq))
+    _count(2 if norm else 1)
+    return dqkv, dqw, dkw
 
 
 def silu_mul_bwd(gate_up: torch.Tensor, dh: torch.Tensor) -> torch.Tensor:

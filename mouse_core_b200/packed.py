@@ -117,29 +117,20 @@ class _RMSNorm(torch.autograd.Function):
 
 class _QKVHeads(torch.autograd.Function):
     """Split a fused QKV projection ``[L, (Hq + 2 Hkv) hd]`` into attention
-    inputs: q and k through the per-head RMSNorm (when the model has one) and
-    rotate-half RoPE, v as is (K4)."""
+    inputs in one pass: q and k through the per-head RMSNorm (when the model
+    has one) and rotate-half RoPE, v as is (K4)."""
 
     @staticmethod
     def forward(ctx, qkv, q_w, k_w, cos, sin, q_eps, k_eps, Hq, Hkv, hd):
-        nq, nk = Hq * hd, Hkv * hd
-        q, q_rstd = K.qk_norm_rope_fwd(qkv[:, :nq], Hq, hd, q_w, q_eps, cos, sin)
-        k, k_rstd = K.qk_norm_rope_fwd(qkv[:, nq:nq + nk], Hkv, hd, k_w, k_eps, cos, sin)
-        v = qkv[:, nq + nk:].reshape(qkv.shape[0], Hkv, hd).contiguous()
+        q, k, v, q_rstd, k_rstd = K.qkv_heads_fwd(qkv, Hq, Hkv, hd, cos, sin, q_w, k_w, q_eps, k_eps)
         ctx.save_for_backward(qkv, q_w, k_w, cos, sin, q_rstd, k_rstd)
-        ctx.shape = (Hq, Hkv, hd)
         return q, k, v
 
     @staticmethod
     def backward(ctx, dq, dk, dv):
         qkv, q_w, k_w, cos, sin, q_rstd, k_rstd = ctx.saved_tensors
-        Hq, Hkv, hd = ctx.shape
-        nq, nk = Hq * hd, Hkv * hd
-        L = qkv.shape[0]
-        dqkv = torch.empty_like(qkv)
-        dqw = K.qk_norm_rope_bwd(dq.contiguous(), qkv[:, :nq], q_w, cos, sin, q_rstd, dqkv[:, :nq])
-        dkw = K.qk_norm_rope_bwd(dk.contiguous(), qkv[:, nq:nq + nk], k_w, cos, sin, k_rstd, dqkv[:, nq:nq + nk])
-        dqkv[:, nq + nk:].copy_(dv.reshape(L, nk))
+        dqkv, dqw, dkw = K.qkv_heads_bwd(dq.contiguous(), dk.contiguous(), dv.contiguous(), qkv, cos, sin, q_w,
+                                         k_w, q_rstd, k_rstd)
         return (dqkv, None if dqw is None else dqw.to(q_w.dtype), None if dkw is None else dkw.to(k_w.dtype),
                 None, None, None, None, None, None, None)
 

@@ -47,18 +47,32 @@ class GradientAllReduce:
 
     Gradients are packed into one persistent fp32 buffer, all-reduced once
     (sum), scaled by ``scale`` and written back. With a single rank it only
-    applies the scale.
+    applies the scale, in place, and never allocates the buffer.
     """
 
     def __init__(self, params, group=None):
         self.params = [p for p in params if p.requires_grad]
         self.group = group
-        n = sum(p.numel() for p in self.params)
-        dev = self.params[0].device if self.params else torch.device("cpu")
-        self.flat = torch.zeros(n, dtype=torch.float32, device=dev)
+        self.device = self.params[0].device if self.params else torch.device("cpu")
+        self._flat = None
+
+    @property
+    def flat(self) -> torch.Tensor:
+        """The fp32 exchange buffer, allocated on first use (multi-rank only)."""
+        if self._flat is None:
+            n = sum(p.numel() for p in self.params)
+            self._flat = torch.zeros(n, dtype=torch.float32, device=self.device)
+        return self._flat
 
     def __call__(self, scale: float = 1.0) -> None:
         world = dist.get_world_size(self.group) if dist.is_available() and dist.is_initialized() else 1
+        if world == 1:
+            # nothing to exchange: scale in place, no round trip through the buffer
+            if scale != 1.0:
+                grads = [p.grad for p in self.params if p.grad is not None]
+                if grads:
+                    torch._foreach_mul_(grads, scale)
+            return
         o = 0
         for p in self.params:
             n = p.numel()
@@ -131,8 +145,8 @@ class PackedDQNTrainer:
     def step(self, rows, total_rows: int) -> torch.Tensor:
         """One optimizer step; returns this rank's summed row losses as a
         device scalar (no host sync)."""
-        self.opt.zero_grad(set_to_none=False)
-        loss_sum = torch.zeros((), device=self.reduce.flat.device)
+        self.opt.zero_grad(set_to_none=True)
+        loss_sum = torch.zeros((), device=self.reduce.device)
         for row in rows:
             emb = self.embedding(row.token_ids)
             h = self._forward(model=self.model, embeds=emb, sequence_ids=row.sequence_ids)

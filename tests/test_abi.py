@@ -83,12 +83,19 @@ def test_training_elementwise_argument_rules(lib):
     assert lib.mb_rmsnorm_bwd(None, None, None, None, 8, 1024, None, ctypes.c_void_p(16), ctypes.c_void_p(16),
                               1, None) == 1
     assert b"NULL" in lib.mb_last_error()
-    # q/k norm + RoPE: head_dim 64/128 only, strides checked
-    assert lib.mb_qk_norm_rope_fwd(None, 96 * 4, None, 1e-6, None, None, 4, 4, 96, None, None, None) == 2
-    assert lib.mb_qk_norm_rope_fwd(None, 0, None, 1e-6, None, None, 0, 4, 128, None, None, None) == 0
-    assert lib.mb_qk_norm_rope_bwd_scratch_floats(1024, 16, 128) % 128 == 0
-    assert lib.mb_qk_norm_rope_bwd(None, None, 0, ctypes.c_void_p(16), None, None, None, 4, 4, 128, None, 512,
-                                   None, None, 0, None) == 1
+    # fused QKV heads: head_dim 64/128 only, norm weights in pairs, strides checked
+    assert lib.mb_qkv_heads_fwd(None, 96 * 8, 4, 4, 2, 96, None, None, 1e-6, 1e-6, None, None, None, None, None,
+                                None, None, None) == 2
+    assert lib.mb_qkv_heads_fwd(None, 1024, 0, 4, 2, 128, None, None, 1e-6, 1e-6, None, None, None, None, None,
+                                None, None, None) == 0
+    assert lib.mb_qkv_heads_fwd(None, 1024, 4, 4, 2, 128, ctypes.c_void_p(16), None, 1e-6, 1e-6, None, None, None,
+                                None, None, None, None, None) == 1
+    assert b"both" in lib.mb_last_error()
+    assert lib.mb_qkv_heads_bwd_scratch_floats(16384, 128) % 256 == 0
+    assert lib.mb_qkv_heads_bwd_scratch_floats(16384, 96) == 0
+    assert lib.mb_qkv_heads_bwd(None, None, None, None, 1024, 4, 4, 2, 128, ctypes.c_void_p(16),
+                                ctypes.c_void_p(16), None, None, None, None, None, 1024, None, None, None, 0,
+                                None) == 1
     assert b"dweight" in lib.mb_last_error()
     # SiLU-gated product backward
     assert lib.mb_silu_mul_bwd(None, None, 0, 3072, None, None) == 0

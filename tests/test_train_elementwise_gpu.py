@@ -84,69 +84,82 @@ def _rope_fp32(x, cos, sin):
     return x * cos + rot * sin
 
 
-@pytest.mark.parametrize("hd,norm", [(128, True), (64, True), (128, False)])
-def test_qk_norm_rope_fwd_bwd_strided(hd, norm):
-    dev = _dev()
-    from mouse_core_b200 import kernels as K
-
-    L, Hq, Hkv = 1000, 4, 2
-    g = torch.Generator(device="cpu").manual_seed(hd)
-    width = (Hq + 2 * Hkv) * hd
-    qkv = (torch.randn(L, width, generator=g) * 2).bfloat16().to(dev)
-    w = (1 + 0.3 * torch.randn(hd, generator=g)).bfloat16().to(dev) if norm else None
-    pos = torch.arange(L) % 333
+def _tables(L, hd, period=333):
+    pos = torch.arange(L) % period
     inv = 1.0 / (1e6 ** (torch.arange(0, hd, 2).float() / hd))
     ang = pos[:, None].float() * inv[None, :]
     ang = torch.cat((ang, ang), dim=-1)
-    cos, sin = ang.cos().bfloat16().to(dev), ang.sin().bfloat16().to(dev)
+    return ang.cos().bfloat16(), ang.sin().bfloat16()
 
-    xk = qkv[:, Hq * hd:(Hq + Hkv) * hd]  # the k columns: strided rows
-    y, rstd = K.qk_norm_rope_fwd(xk, Hkv, hd, w, 1e-6, cos, sin)
-    assert y.shape == (L, Hkv, hd) and (rstd is None) == (not norm)
 
-    xf = xk.float().reshape(L, Hkv, hd).requires_grad_(True)
-    wf = w.float().requires_grad_(True) if norm else None
-    n = _rmsnorm_fp32(xf, wf, 1e-6) if norm else xf
-    yf = _rope_fp32(n, cos.float()[:, None, :], sin.float()[:, None, :])
-    dy = torch.randn(L, Hkv, hd, generator=g).bfloat16().to(dev)
-    (yf * dy.float()).sum().backward()
-    assert _maxabs(y, yf.detach()) < 2e-2
+@pytest.mark.parametrize("hd,Hq,Hkv,norm,pad", [(128, 16, 8, True, 0), (64, 4, 2, True, 0), (128, 4, 2, False, 0),
+                                                (64, 6, 1, True, 64), (128, 3, 1, True, 8)])
+def test_qkv_heads_fwd_bwd(hd, Hq, Hkv, norm, pad):
+    """q/k norm + RoPE and the v copy from one (optionally row-padded) fused
+    projection, and the gradient written back into the whole fused gradient."""
+    dev = _dev()
+    from mouse_core_b200 import kernels as K
 
-    dqkv = torch.zeros_like(qkv)
-    dw = K.qk_norm_rope_bwd(dy, xk, w, cos, sin, rstd, dqkv[:, Hq * hd:(Hq + Hkv) * hd])
-    dx = dqkv[:, Hq * hd:(Hq + Hkv) * hd].reshape(L, Hkv, hd)
-    assert _maxabs(dx, xf.grad) < 2e-2
-    # the kernel writes only its own columns of the fused gradient
-    assert not dqkv[:, :Hq * hd].any() and not dqkv[:, (Hq + Hkv) * hd:].any()
+    L = 1000
+    g = torch.Generator(device="cpu").manual_seed(hd + Hq)
+    width = (Hq + 2 * Hkv) * hd
+    store = (torch.randn(L, width + pad, generator=g) * 2).bfloat16().to(dev)
+    qkv = store[:, :width]  # row stride width + pad
+    qw = (1 + 0.3 * torch.randn(hd, generator=g)).bfloat16().to(dev) if norm else None
+    kw = (1 + 0.3 * torch.randn(hd, generator=g)).bfloat16().to(dev) if norm else None
+    cos, sin = (t.to(dev) for t in _tables(L, hd))
+    q, k, v, q_rstd, k_rstd = K.qkv_heads_fwd(qkv, Hq, Hkv, hd, cos, sin, qw, kw, 1e-6, 1e-5)
+    assert (q_rstd is None) == (not norm)
+    assert torch.equal(v, qkv[:, (Hq + Hkv) * hd:].reshape(L, Hkv, hd))
+
+    xf = qkv.float().requires_grad_(True)
+    xq = xf[:, :Hq * hd].reshape(L, Hq, hd)
+    xk = xf[:, Hq * hd:(Hq + Hkv) * hd].reshape(L, Hkv, hd)
+    xv = xf[:, (Hq + Hkv) * hd:].reshape(L, Hkv, hd)
     if norm:
-        assert _rel(dw, wf.grad) < 1e-2
+        qwf = qw.float().requires_grad_(True)
+        kwf = kw.float().requires_grad_(True)
+        xq, xk = _rmsnorm_fp32(xq, qwf, 1e-6), _rmsnorm_fp32(xk, kwf, 1e-5)
+    c, s_ = cos.float()[:, None, :], sin.float()[:, None, :]
+    qf, kf = _rope_fp32(xq, c, s_), _rope_fp32(xk, c, s_)
+    assert _maxabs(q, qf.detach()) < 2e-2 and _maxabs(k, kf.detach()) < 2e-2
+    dq = torch.randn(L, Hq, hd, generator=g).bfloat16().to(dev)
+    dk = torch.randn(L, Hkv, hd, generator=g).bfloat16().to(dev)
+    dv = torch.randn(L, Hkv, hd, generator=g).bfloat16().to(dev)
+    ((qf * dq.float()).sum() + (kf * dk.float()).sum() + (xv * dv.float()).sum()).backward()
+
+    dstore = torch.zeros(L, width + 16, dtype=torch.bfloat16, device=dev)
+    dqkv, dqw, dkw = K.qkv_heads_bwd(dq, dk, dv, qkv, cos, sin, qw, kw, q_rstd, k_rstd, dqkv=dstore[:, :width])
+    assert _maxabs(dqkv[:, :(Hq + Hkv) * hd], xf.grad[:, :(Hq + Hkv) * hd]) < 2e-2
+    assert torch.equal(dqkv[:, (Hq + Hkv) * hd:], dv.reshape(L, -1))
+    assert not dstore[:, width:].any()  # the row padding is never written
+    if norm:
+        assert _rel(dqw, qwf.grad) < 1e-2 and _rel(dkw, kwf.grad) < 1e-2
     else:
-        assert dw is None
+        assert dqw is None and dkw is None
 
 
-def test_qk_norm_rope_matches_module_rounding():
-    """Forward equals Qwen3's q_norm followed by apply_rotary_pos_emb in bf16
-    to within one bf16 ulp (the same rounding after each op)."""
+def test_qkv_heads_match_module_rounding():
+    """q equals Qwen3's q_norm followed by apply_rotary_pos_emb in bf16 up to
+    rare two-ulp differences (the same rounding after each op)."""
     dev = _dev()
     from mouse_core_b200 import kernels as K
     from transformers.models.qwen3.modeling_qwen3 import Qwen3RMSNorm, apply_rotary_pos_emb
 
-    L, H, hd = 513, 3, 128
+    L, H, Hkv, hd = 513, 4, 2, 128
     g = torch.Generator(device="cpu").manual_seed(9)
-    x = torch.randn(L, H * hd, generator=g).bfloat16().to(dev)
+    qkv = torch.randn(L, (H + 2 * Hkv) * hd, generator=g).bfloat16().to(dev)
     w = (1 + 0.3 * torch.randn(hd, generator=g)).bfloat16().to(dev)
-    ang = torch.arange(L)[:, None].float() * (1.0 / (1e6 ** (torch.arange(0, hd, 2).float() / hd)))[None]
-    ang = torch.cat((ang, ang), dim=-1)
-    cos, sin = ang.cos().bfloat16().to(dev), ang.sin().bfloat16().to(dev)
-    y, _ = K.qk_norm_rope_fwd(x, H, hd, w, 1e-6, cos, sin)
+    cos, sin = (t.to(dev) for t in _tables(L, hd, period=L))
+    q, _, _, _, _ = K.qkv_heads_fwd(qkv, H, Hkv, hd, cos, sin, w, w, 1e-6, 1e-6)
     mod = Qwen3RMSNorm(hd, eps=1e-6).to(dev, torch.bfloat16)
     with torch.no_grad():
         mod.weight.copy_(w)
-        n = mod(x.view(1, L, H, hd)).transpose(1, 2)  # [1, H, L, hd]
+        n = mod(qkv[:, :H * hd].reshape(1, L, H, hd)).transpose(1, 2)  # [1, H, L, hd]
         ref, _ = apply_rotary_pos_emb(n, n, cos[None], sin[None])
     ref = ref[0].transpose(0, 1)
     ulp = ref.float().abs() * 2.0 ** -7 + 2.0 ** -14
-    assert float(((y.float() - ref.float()).abs() > 2 * ulp).float().mean()) < 1e-3
+    assert float(((q.float() - ref.float()).abs() > 2 * ulp).float().mean()) < 1e-3
 
 
 @pytest.mark.parametrize("rows,inter", [(1, 2), (1000, 3072), (257, 1000)])
