@@ -1,6 +1,7 @@
 """Host-side logic of mouse_core_b200 on CPU: the kv_policy and packing maps
 must equal the reference's outputs bit for bit (fixtures made by the
-reference itself), and the page table must behave as a refcounted pool."""
+reference itself), the page table must behave as a refcounted pool, and the
+FMA-pipe exp2 of the attention backward must meet its error bound."""
 
 from __future__ import annotations
 
@@ -92,3 +93,32 @@ def test_page_table_allocate_release_share():
         assert "exhausted" in str(e)
     else:
         raise AssertionError("allocation beyond the pool must raise")
+
+
+def _fma32(a, b, c):
+    """float32 fused multiply-add (the float64 product of two float32s is exact)."""
+    return (a.astype(np.float64) * b + c).astype(np.float32)
+
+
+def test_exp2_fma_error_bound():
+    """The FMA-pipe 2^x of the attention backward (`exp2_fma`, tcgen05.cuh),
+    restated step by step in float32: magic-number rounding to n, a cubic in
+    f = x - n on [-0.5, 0.5], n added to the exponent field. Its relative
+    error stays below 1.1e-4 (under bf16's half-ulp of 2^-9) over the softmax
+    range, and the clamp keeps very negative inputs at ~1e-38."""
+    x = np.linspace(-126.0, 0.0, 2_000_001, dtype=np.float32)
+    x = np.concatenate([x, np.array([0.49999997, -0.5, -0.50000006, 1e-8, -1e-8], dtype=np.float32)])
+    magic = np.float32(12582912.0)
+    t = (x + magic).astype(np.float32)
+    f = (x - (t - magic)).astype(np.float32)
+    assert float(np.abs(f).max()) <= 0.5
+    p = _fma32(np.float32(0.0550089821), f, np.float32(0.242210975))
+    p = _fma32(p, f, np.float32(0.693282916))
+    p = _fma32(p, f, np.float32(1.0))
+    bits = (p.view(np.int32).astype(np.int64) + (t.view(np.int32).astype(np.int64) << 23)) & 0xFFFFFFFF
+    y = bits.astype(np.uint32).view(np.float32).astype(np.float64)
+    ref = np.exp2(x.astype(np.float64))
+    rel = np.abs(y - ref) / ref
+    assert float(rel.max()) < 1.1e-4
+    clamped = np.float32(-126.0)
+    assert 0.0 < float(np.exp2(np.float64(clamped))) < 1e-37
