@@ -144,6 +144,21 @@ __device__ __forceinline__ void umma_ts_t128_quarters_warp(uint32_t d, uint32_t 
       ::"r"(d), "r"(a), "l"(db), "r"(idesc), "r"(accumulate));
 }
 
+// Half of umma_ts_t128_quarters_warp: the four K-steps of two 32-token
+// quarters (A columns 0, 8, 32, 40 from `a`; B rows 0-63 from `db`). The
+// second half is the same call with a + 64, db + 512 and accumulate = 1.
+__device__ __forceinline__ void umma_ts_t64_quarters_warp(uint32_t d, uint32_t a, uint64_t db, uint32_t idesc,
+                                                          uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred e, t, p;\n\t.reg .b32 ta;\n\t.reg .b64 b;\n\t"
+      "elect.sync _|e, 0xffffffff;\n\tsetp.eq.b32 t, %3, %3;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t"
+      "add.u32 ta, %1, 8;\n\tadd.s64 b, %2, 128;\n\t@e tcgen05.mma.cta_group::1.kind::f16 [%0], [ta], b, %3, t;\n\t"
+      "add.u32 ta, %1, 32;\n\tadd.s64 b, %2, 256;\n\t@e tcgen05.mma.cta_group::1.kind::f16 [%0], [ta], b, %3, t;\n\t"
+      "add.u32 ta, %1, 40;\n\tadd.s64 b, %2, 384;\n\t@e tcgen05.mma.cta_group::1.kind::f16 [%0], [ta], b, %3, t;\n\t}"
+      ::"r"(d), "r"(a), "l"(db), "r"(idesc), "r"(accumulate));
+}
+
 // As umma_ts_t128_warp, with the 128 tokens of A packed contiguously: K-step
 // kk at column 8 * kk.
 __device__ __forceinline__ void umma_ts_t128_linear_warp(uint32_t d, uint32_t a, uint64_t db, uint32_t idesc,

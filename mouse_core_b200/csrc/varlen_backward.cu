@@ -15,9 +15,12 @@
 //            128-column regions; the element-wise warps write P^T (bf16) over
 //            the S^T columns they read and dS^T over the dP^T columns, and
 //            dV += P^T dO, dK += dS^T Q accumulate in TMEM over the walk. The
-//            MMA order per item is dV(t), S^T(t+1), dK(t), dP^T(t+1), so the
-//            P phase of one item overlaps the dK and dP^T MMAs and its dS
-//            phase the dV and S^T MMAs.
+//            MMA order per item is dV(t) (by halves: queries 0-63 as soon as
+//            the P warps have written them, 64-127 after), S^T(t+1), dK(t),
+//            dP^T(t+1). Separate P warps and dS warps run the two
+//            element-wise phases, so one item's dS phase runs beside the
+//            next item's P phase; the dS warps read P^T back from TMEM
+//            before S^T(t+1) may overwrite it.
 //  * dq:     one CTA per (128-query tile, q-head), walking the key tiles the
 //            forward visits: S = Q K^T (double-buffered in TMEM), dP = dO V^T,
 //            dS (bf16, over the S columns it came from), dQ += dS K.
@@ -35,9 +38,10 @@
 //  * tcgen05.mma operations of one CTA execute in issue order, so an MMA may
 //    overwrite TMEM columns that an earlier MMA reads as its A operand.
 // Warp roles (576 threads): warp 0 TMA producer, warp 1 TMEM allocator and
-// MMA issuer, warps 2-17 element-wise (warp w owns TMEM lanes 32*(w%4) and
-// column quarter (w-2)/4 of each 128-column tile; four warps per lane quarter
-// hide the TMEM and MUFU latencies of the element-wise phases).
+// MMA issuer, warps 2-17 element-wise; warp w owns TMEM lanes 32*(w%4). In dq
+// warp w takes column quarter (w-2)/4 of each 128-column tile (four warps
+// per lane quarter hide the TMEM and MUFU latencies); in dkdv warps 2-9 are
+// P warps and 10-17 dS warps, each taking a 64-column half.
 #include "common.cuh"
 #include "kernels.h"
 #include "tcgen05.cuh"
@@ -126,8 +130,21 @@ __device__ __forceinline__ void mma_tmem_a(uint32_t d, uint32_t a_tmem, uint32_t
                              accumulate ? 1u : 0u);
 }
 
+// One half (K rows 64 * half .. + 63) of mma_tmem_a.
+template <int HD>
+__device__ __forceinline__ void mma_tmem_a_half(uint32_t d, uint32_t a_tmem, uint32_t b_base, uint32_t idesc,
+                                                bool accumulate, int half) {
+  umma_ts_t64_quarters_warp(d, a_tmem + 64 * half,
+                            umma_desc_sw128(b_base, BwdTile<HD>::BOX, 1024) + 512 * (uint64_t)half, idesc,
+                            (accumulate || half) ? 1u : 0u);
+}
+
 constexpr int kBwdThreads = 576;  // producer + MMA warp + 16 element-wise warps
 constexpr int kEwWarps = 16;
+// The dK/dV kernel splits its element-wise warps by phase: warps 2-9 turn
+// S^T into P^T, warps 10-17 turn dP^T into dS^T, so one item's dS phase runs
+// beside the next item's P phase instead of after it.
+constexpr int kPWarps = 8, kDsWarps = 8;
 // Of each warp's 32 exponentials per item, this many run on the FMA pipe
 // (exp2_fma) instead of the SFU, whose throughput bounds the P phase.
 constexpr int kFmaExp = 8;
@@ -353,7 +370,9 @@ struct DkdvBars {
   uint64_t fixed_full;  // K, V
   uint64_t q_full[3], q_empty[3], d_full[2], d_empty[2];
   uint64_t s_full, dp_full;  // S^T(t), dP^T(t)
+  uint64_t p_half;           // bf16 P^T of query quarters 0-1 in TMEM
   uint64_t p_done;           // bf16 P^T of the current item in TMEM
+  uint64_t p_read;           // the dS warps hold that P^T in registers
   uint64_t ds_done;          // bf16 dS^T of the current item in TMEM
   uint64_t acc_full;
   uint32_t tmem_base;
@@ -401,8 +420,10 @@ __global__ void __launch_bounds__(kBwdThreads, 1) varlen_bwd_dkdv_kernel(const _
     }
     mbar_init(&bars->s_full, 1);
     mbar_init(&bars->dp_full, 1);
-    mbar_init(&bars->p_done, kEwWarps);
-    mbar_init(&bars->ds_done, kEwWarps);
+    mbar_init(&bars->p_half, kPWarps);
+    mbar_init(&bars->p_done, kPWarps);
+    mbar_init(&bars->p_read, kDsWarps);
+    mbar_init(&bars->ds_done, kDsWarps);
     mbar_init(&bars->acc_full, 1);
     fence_barrier_init();
   }
@@ -496,8 +517,13 @@ __global__ void __launch_bounds__(kBwdThreads, 1) varlen_bwd_dkdv_kernel(const _
     if (ok) ok = issue_s(0);
     if (ok) ok = issue_dp(0);
     for (int t = 0; ok && t < n; ++t) {
+      // dV += P^T dO, by halves as the P warps finish query quarters 0-1 and 2-3
+      if (!(ok = mbar_wait_warp(&bars->p_half, t & 1, kDevTimeoutFull))) break;
+      mma_tmem_a_half<HD>(t_dv, t_s, smem_u32(dring + (t & 1) * C::TILE), ID_G, t > 0, 0);
       if (!(ok = mbar_wait_warp(&bars->p_done, t & 1, kDevTimeoutFull))) break;
-      mma_tmem_a<HD>(t_dv, t_s, smem_u32(dring + (t & 1) * C::TILE), ID_G, t > 0);  // dV += P^T dO
+      mma_tmem_a_half<HD>(t_dv, t_s, smem_u32(dring + (t & 1) * C::TILE), ID_G, t > 0, 1);
+      // S^T(t+1) overwrites P^T(t): the dS warps must hold it first.
+      if (!(ok = mbar_wait_warp(&bars->p_read, t & 1, kDevTimeoutFull))) break;
       if (t + 1 < n && !(ok = issue_s(t + 1))) break;
       if (!(ok = mbar_wait_warp(&bars->ds_done, t & 1, kDevTimeoutFull))) break;
       mma_tmem_a<HD>(t_dk, t_x, smem_u32(qring + (t % 3) * C::TILE), ID_G, t > 0);  // dK += dS^T Q
@@ -509,86 +535,122 @@ __global__ void __launch_bounds__(kBwdThreads, 1) varlen_bwd_dkdv_kernel(const _
     }
     umma_commit_warp(&bars->acc_full);
   } else {
-    const int cq = (warp - 2) >> 2;  // column quarter of every 128-column tile
-    const int sub = warp & 3;         // TMEM lane quarter
+    const bool p_warp = warp < 2 + kPWarps;
+    const int ch = (warp - (p_warp ? 2 : 2 + kPWarps)) >> 2;  // column half of every 128-column tile
+    const int sub = warp & 3;                                   // TMEM lane quarter
     const int r = sub * 32 + lane;
     const int k_tok = kv0 + r;
     const bool k_ok = k_tok < p.L;
     const int q_end = k_ok ? p.run_end[k_tok] : 0;  // queries k_tok <= q < q_end see this key
     const uint32_t lane_bits = (uint32_t)(sub * 32) << 16;
-    const uint32_t ts = t_s + lane_bits + 32 * cq, tx = t_x + lane_bits + 32 * cq;
     bool ok = true;
-    for (int t = 0; t < n; ++t) {
-      const int qc0 = (i_lo + t % nqi) * 128 + 32 * cq;  // first query of this warp's 32 columns
-      uint32_t pk[16];  // P^T as bf16 pairs (the precision the dV MMA takes it in)
-      // P phase: S^T -> P^T, written packed over the S^T columns just read.
-      if (ok) ok = mbar_wait_warp(&bars->q_full[t % 3], (t / 3) & 1, kDevTimeoutFull);
-      if (ok) ok = mbar_wait_warp(&bars->s_full, t & 1, kDevTimeoutFull);
-      tc_fence_after();
-      if (ok) {
-        uint32_t sv[32];
-        tmem_ld32(ts, sv);
-        tmem_wait_ld();
-        const float4* l4 = reinterpret_cast<const float4*>(lse_ring + (t % 3) * 128 + 32 * cq);
-        float x[32];
+    if (p_warp) {
+      // P phase, per item: S^T -> P^T for query quarters ch and ch + 2, each
+      // packed to bf16 over the first 16 of its columns; quarters 0-1 are
+      // signalled first so the dV MMAs on them start while 2-3 are computed.
+      for (int t = 0; t < n; ++t) {
+        if (ok) ok = mbar_wait_warp(&bars->q_full[t % 3], (t / 3) & 1, kDevTimeoutFull);
+        if (ok) ok = mbar_wait_warp(&bars->s_full, t & 1, kDevTimeoutFull);
+        tc_fence_after();
+        if (ok) {
+#pragma unroll 1
+          for (int h = 0; h < 2; ++h) {
+            const int cq = ch + 2 * h;
+            const uint32_t ts = t_s + lane_bits + 32 * cq;
+            const int qc0 = (i_lo + t % nqi) * 128 + 32 * cq;  // first query of these 32 columns
+            uint32_t sv[32];
+            tmem_ld32(ts, sv);
+            tmem_wait_ld();
+            const float4* l4 = reinterpret_cast<const float4*>(lse_ring + (t % 3) * 128 + 32 * cq);
+            float x[32];
 #pragma unroll
-        for (int c4 = 0; c4 < 8; ++c4) {
-          const float4 l = l4[c4];
-          x[4 * c4 + 0] = fmaf(__uint_as_float(sv[4 * c4 + 0]), p.scale_log2, -l.x);
-          x[4 * c4 + 1] = fmaf(__uint_as_float(sv[4 * c4 + 1]), p.scale_log2, -l.y);
-          x[4 * c4 + 2] = fmaf(__uint_as_float(sv[4 * c4 + 2]), p.scale_log2, -l.z);
-          x[4 * c4 + 3] = fmaf(__uint_as_float(sv[4 * c4 + 3]), p.scale_log2, -l.w);
-        }
+            for (int c4 = 0; c4 < 8; ++c4) {
+              const float4 l = l4[c4];
+              x[4 * c4 + 0] = fmaf(__uint_as_float(sv[4 * c4 + 0]), p.scale_log2, -l.x);
+              x[4 * c4 + 1] = fmaf(__uint_as_float(sv[4 * c4 + 1]), p.scale_log2, -l.y);
+              x[4 * c4 + 2] = fmaf(__uint_as_float(sv[4 * c4 + 2]), p.scale_log2, -l.z);
+              x[4 * c4 + 3] = fmaf(__uint_as_float(sv[4 * c4 + 3]), p.scale_log2, -l.w);
+            }
 #pragma unroll
-        for (int e = 0; e < 32; ++e) x[e] = e < 32 - kFmaExp ? fast_exp2(x[e]) : exp2_fma(x[e]);
-        if (!(k_ok && qc0 >= k_tok && qc0 + 31 < q_end)) {
+            for (int e = 0; e < 32; ++e) x[e] = e < 32 - kFmaExp ? fast_exp2(x[e]) : exp2_fma(x[e]);
+            if (!(k_ok && qc0 >= k_tok && qc0 + 31 < q_end)) {
 #pragma unroll
-          for (int e = 0; e < 32; ++e) {
-            const int q = qc0 + e;
-            if (q < k_tok || q >= q_end) x[e] = 0.f;
+              for (int e = 0; e < 32; ++e) {
+                const int q = qc0 + e;
+                if (q < k_tok || q >= q_end) x[e] = 0.f;
+              }
+            }
+            uint32_t pk[16];
+#pragma unroll
+            for (int e = 0; e < 16; ++e) pk[e] = pack_bf16x2(x[2 * e], x[2 * e + 1]);
+            tmem_st16(ts, pk);
+            if (h == 0) {
+              tmem_wait_st();
+              tc_fence_before();
+              __syncwarp();
+              if (lane == 0) mbar_arrive(&bars->p_half);
+            }
           }
+          tmem_wait_st();
+        } else if (lane == 0) {
+          mbar_arrive(&bars->p_half);  // keep the phase count when a wait gave up
         }
-#pragma unroll
-        for (int e = 0; e < 16; ++e) pk[e] = pack_bf16x2(x[2 * e], x[2 * e + 1]);
-        tmem_st16(ts, pk);
-        tmem_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bars->p_done);
       }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&bars->p_done);
-      // dS phase: dP^T -> dS^T = P^T o (dP^T - D), packed over the dP^T columns.
-      if (ok) ok = mbar_wait_warp(&bars->d_full[t & 1], (t >> 1) & 1, kDevTimeoutFull);
-      if (ok) ok = mbar_wait_warp(&bars->dp_full, t & 1, kDevTimeoutFull);
-      tc_fence_after();
-      if (ok) {
-        uint32_t dv[32];
-        tmem_ld32(tx, dv);
-        tmem_wait_ld();
-        const float4* d4 = reinterpret_cast<const float4*>(dlt_ring + (t & 1) * 128 + 32 * cq);
-        uint32_t ds[16];
-#pragma unroll
-        for (int e4 = 0; e4 < 8; ++e4) {
-          const float4 d = d4[e4];
-          const float2 p01 = unpack_bf16x2(pk[2 * e4]), p23 = unpack_bf16x2(pk[2 * e4 + 1]);
-          ds[2 * e4] = pack_bf16x2(p01.x * (__uint_as_float(dv[4 * e4]) - d.x),
-                                   p01.y * (__uint_as_float(dv[4 * e4 + 1]) - d.y));
-          ds[2 * e4 + 1] = pack_bf16x2(p23.x * (__uint_as_float(dv[4 * e4 + 2]) - d.z),
-                                       p23.y * (__uint_as_float(dv[4 * e4 + 3]) - d.w));
+    } else {
+      // dS phase, per item: read P^T back (then S^T(t+1) may overwrite it),
+      // dS^T = P^T o (dP^T - D), packed over the dP^T columns.
+      for (int t = 0; t < n; ++t) {
+        uint32_t pk[2][16];
+        if (ok) ok = mbar_wait_warp(&bars->p_done, t & 1, kDevTimeoutFull);
+        tc_fence_after();
+        if (ok) {
+          tmem_ld16(t_s + lane_bits + 64 * ch, pk[0]);
+          tmem_ld16(t_s + lane_bits + 64 * ch + 32, pk[1]);
+          tmem_wait_ld();
         }
-        tmem_st16(tx, ds);
-        tmem_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bars->p_read);
+        if (ok) ok = mbar_wait_warp(&bars->d_full[t & 1], (t >> 1) & 1, kDevTimeoutFull);
+        if (ok) ok = mbar_wait_warp(&bars->dp_full, t & 1, kDevTimeoutFull);
+        tc_fence_after();
+        if (ok) {
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            const int cq = 2 * ch + h;
+            const uint32_t tx = t_x + lane_bits + 32 * cq;
+            uint32_t dv[32];
+            tmem_ld32(tx, dv);
+            tmem_wait_ld();
+            const float4* d4 = reinterpret_cast<const float4*>(dlt_ring + (t & 1) * 128 + 32 * cq);
+#pragma unroll
+            for (int e4 = 0; e4 < 8; ++e4) {
+              const float4 d = d4[e4];
+              const float2 p01 = unpack_bf16x2(pk[h][2 * e4]), p23 = unpack_bf16x2(pk[h][2 * e4 + 1]);
+              pk[h][2 * e4] = pack_bf16x2(p01.x * (__uint_as_float(dv[4 * e4]) - d.x),
+                                          p01.y * (__uint_as_float(dv[4 * e4 + 1]) - d.y));
+              pk[h][2 * e4 + 1] = pack_bf16x2(p23.x * (__uint_as_float(dv[4 * e4 + 2]) - d.z),
+                                              p23.y * (__uint_as_float(dv[4 * e4 + 3]) - d.w));
+            }
+            tmem_st16(tx, pk[h]);
+          }
+          tmem_wait_st();
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bars->ds_done);
       }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&bars->ds_done);
     }
-    // Epilogue: quarters 0-1 write dV, 2-3 write dK (scaled); each covers half
-    // of the HD columns.
+    // Epilogue: the P warps write dV, the dS warps dK (scaled); each warp
+    // covers half of the HD columns of its 32 keys.
     if (ok) ok = mbar_wait_warp(&bars->acc_full, 0, kDevTimeoutFull);
     tc_fence_after();
     if (ok) {
-      const bool is_v = cq < 2;
-      const int col0 = (cq & 1) * (HD / 2);
+      const bool is_v = p_warp;
+      const int col0 = ch * (HD / 2);
       const uint32_t src = (is_v ? t_dv : t_dk) + lane_bits + col0;
       const float mul = is_v ? 1.f : p.scale;
       __nv_bfloat16* dst = (is_v ? p.dv : p.dk) + ((size_t)k_tok * p.Hkv + kvh) * HD + col0;
