@@ -167,8 +167,11 @@ int mb_varlen_attention_fwd(const void* q, const void* k, const void* v, int L, 
  * and the upstream dout [L, q_heads, hd], writes dq [L, q_heads, hd] and
  * dk, dv [L, kv_heads, hd] (bf16; dk/dv summed over each GQA group).
  * run_start / run_end come from mb_segment_meta. delta is caller scratch of
- * q_heads * L floats. Deterministic (no atomics).
+ * MB_VARLEN_BWD_SCRATCH_FLOATS(q_heads, L) floats (the row sums of dO * O,
+ * then the tile counters of the persistent kernels). Deterministic: every
+ * output element is written by one CTA, without atomics on the data.
  * ------------------------------------------------------------------- */
+#define MB_VARLEN_BWD_SCRATCH_FLOATS(q_heads, L) ((size_t)(q_heads) * (size_t)(L) + 4u)
 int mb_varlen_attention_bwd(const void* q, const void* k, const void* v, const void* out, const void* dout,
                             const float* lse, int L, int q_heads, int kv_heads, int head_dim,
                             const int32_t* run_start, const int32_t* run_end, float scale, void* dq, void* dk,

@@ -322,6 +322,7 @@ int mb_varlen_attention_bwd(const void* q, const void* k, const void* v, const v
   p.run_end = run_end;
   p.lse = lse;
   p.delta = delta;
+  p.tile_counter = reinterpret_cast<int*>(delta + (size_t)q_heads * L);
   p.scale = scale;
   p.scale_log2 = scale * 1.4426950408889634f;
   p.dq = static_cast<__nv_bfloat16*>(dq);

@@ -89,6 +89,7 @@ struct VarlenBwdParams {
   const int32_t* run_end;    // [L]
   const float* lse;          // [Hq, L] log2 units (from the forward)
   float* delta;              // [Hq, L] scratch: rowsum(dO * O)
+  int* tile_counter;         // [2] scratch: tile counters of the persistent kernels
   float scale, scale_log2;
   __nv_bfloat16* dq;         // [L, Hq, HD]
   __nv_bfloat16* dk;         // [L, Hkv, HD]

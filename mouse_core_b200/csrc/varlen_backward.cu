@@ -7,7 +7,8 @@
 //   dV = P^T dO,  dS = P o (dO V^T - D),  dQ = scale dS K,  dK = scale dS^T Q,
 // with dK/dV summed over the q-heads sharing a kv-head.
 //
-// Three kernels, no atomics (deterministic):
+// Three kernels, deterministic (every output element is computed by one CTA;
+// the only atomic is the dq kernel's tile counter):
 //  * delta:  D[h, i] (fp32) from dO and O.
 //  * dkdv:   one CTA per (128-key tile, kv-head), walking every (q-head of the
 //            group, 128-query tile) item whose queries may see its keys. Keys
@@ -21,9 +22,11 @@
 //            element-wise phases, so one item's dS phase runs beside the
 //            next item's P phase; the dS warps read P^T back from TMEM
 //            before S^T(t+1) may overwrite it.
-//  * dq:     one CTA per (128-query tile, q-head), walking the key tiles the
+//  * dq:     per (128-query tile, q-head) tile, walking the key tiles the
 //            forward visits: S = Q K^T (double-buffered in TMEM), dP = dO V^T,
-//            dS (bf16, over the S columns it came from), dQ += dS K.
+//            dS (bf16, over the S columns it came from), dQ += dS K. The
+//            kernel is persistent (one CTA per SM, tiles from a counter) so a
+//            tile's epilogue overlaps the next tile's loads and first MMAs.
 //
 // Pipelining (one item stream per CTA, every MMA 128 x 128 or 128 x HD wide):
 //  * The element-wise warps signal once per phase (one mbarrier arrive per
@@ -73,7 +76,11 @@ __device__ __forceinline__ float dot8_bf16(uint4 a, uint4 b) {
 
 __global__ void __launch_bounds__(256) bwd_delta_kernel(const __nv_bfloat16* __restrict__ out,
                                                         const __nv_bfloat16* __restrict__ dout, int L, int Hq,
-                                                        int hd, float* __restrict__ delta) {
+                                                        int hd, float* __restrict__ delta,
+                                                        int* __restrict__ tile_counter) {
+  // The persistent kernels launched after this one on the same stream take
+  // their tiles from these counters.
+  if (blockIdx.x == 0 && threadIdx.x < 2) tile_counter[threadIdx.x] = 0;
   const int tpr = hd >> 3;  // threads per row (16 or 8), a power of two dividing 32
   const long long rows = (long long)L * Hq;
   const long long tid = (long long)blockIdx.x * blockDim.x + threadIdx.x;
@@ -147,7 +154,7 @@ constexpr int kEwWarps = 16;
 constexpr int kPWarps = 8, kDsWarps = 8;
 // Of each warp's 32 exponentials per item, this many run on the FMA pipe
 // (exp2_fma) instead of the SFU, whose throughput bounds the P phase.
-constexpr int kFmaExp = 8;
+constexpr int kFmaExp = 4;
 
 // Dynamic shared memory is used from its base without padding (the kernels
 // need nearly all 227 KB); the 128-byte-swizzled TMA boxes need the base
@@ -155,16 +162,40 @@ constexpr int kFmaExp = 8;
 __device__ __forceinline__ bool smem_base_aligned(const void* p) { return (smem_u32(p) & 1023u) == 0; }
 
 // ---------------------------------------------------------------- dq kernel
+// Persistent: one CTA per SM takes (query tile, q-head) tiles from a global
+// counter, heaviest query tiles first. The producer hands each tile id to
+// the MMA and element-wise warps through a two-slot ring; barrier phases and
+// ring slots follow a running item count across tiles, so the next tile's
+// Q / dO loads and first S / dP MMAs overlap the previous tile's epilogue.
 struct DqBars {
-  uint64_t fixed_full;  // Q, dO
+  uint64_t tile_full[2], tile_empty[2];  // tile-id ring (producer -> MMA + element-wise warps)
+  uint64_t fixed_full, fixed_empty;      // Q, dO of the current tile; free again
   uint64_t k_full[3], k_empty[3], v_full[2], v_empty[2];
   uint64_t s_full[2];   // S(j) in TMEM region j & 1
   uint64_t dp_full;     // dP(j)
   uint64_t dp_loaded;   // element-wise warps hold dP(j) in registers
   uint64_t ds_done[2];  // bf16 dS of item j in TMEM (set j & 1)
-  uint64_t acc_full;
+  uint64_t acc_full;    // dQ of the tile complete in TMEM
+  uint64_t acc_empty;   // the element-wise warps have read it out
   uint32_t tmem_base;
+  int tile[2];
 };
+
+struct DqTile {
+  int q0, h, kvh, t_lo, n;
+};
+
+__device__ __forceinline__ DqTile dq_tile(int tile, const VarlenBwdParams& p) {
+  const int n_qt = (p.L + 127) / 128;
+  DqTile d;
+  const int qt = n_qt - 1 - tile / p.Hq;
+  d.h = tile % p.Hq;
+  d.kvh = d.h / p.G;
+  d.q0 = qt * 128;
+  d.t_lo = p.run_start[d.q0] / 128;
+  d.n = min(d.q0 + 127, p.L - 1) / 128 - d.t_lo + 1;
+  return d;
+}
 
 template <int HD>
 __global__ void __launch_bounds__(kBwdThreads, 1) varlen_bwd_dq_kernel(const __grid_constant__ CUtensorMap qmap,
@@ -185,17 +216,15 @@ __global__ void __launch_bounds__(kBwdThreads, 1) varlen_bwd_dq_kernel(const __g
   DqBars* bars = reinterpret_cast<DqBars*>(smem + 7 * C::TILE);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int n_qt = (p.L + 127) / 128;
-  const int qt = n_qt - 1 - (int)blockIdx.x;
-  const int q0 = qt * 128;
-  const int h = blockIdx.y;
-  const int kvh = h / p.G;
-  const int t_lo = p.run_start[q0] / 128;
-  const int t_hi = min(q0 + 127, p.L - 1) / 128;
-  const int n = t_hi - t_lo + 1;
+  const int n_tiles = ((p.L + 127) / 128) * p.Hq;
 
   if (threadIdx.x == 0) {
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&bars->tile_full[s], 1);
+      mbar_init(&bars->tile_empty[s], 1 + kEwWarps);
+    }
     mbar_init(&bars->fixed_full, 1);
+    mbar_init(&bars->fixed_empty, 1);
     for (int s = 0; s < 3; ++s) {
       mbar_init(&bars->k_full[s], 1);
       mbar_init(&bars->k_empty[s], 1);
@@ -209,6 +238,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1) varlen_bwd_dq_kernel(const __g
     mbar_init(&bars->dp_full, 1);
     mbar_init(&bars->dp_loaded, kEwWarps);
     mbar_init(&bars->acc_full, 1);
+    mbar_init(&bars->acc_empty, kEwWarps);
     fence_barrier_init();
   }
   if (warp == 1) tmem_alloc(&bars->tmem_base, 512);
@@ -218,142 +248,207 @@ __global__ void __launch_bounds__(kBwdThreads, 1) varlen_bwd_dq_kernel(const __g
   const uint32_t tbase = bars->tmem_base;
   const uint32_t t_p = tbase + 256, t_dq = tbase + 384;
 
+  // Tile k of this CTA from the ring (every consumer warp reads each slot once).
+  auto take_tile = [&](int k, bool& ok) {
+    ok = mbar_wait_warp(&bars->tile_full[k & 1], (k >> 1) & 1, kDevTimeoutFull);
+    const int tile = ok ? *reinterpret_cast<volatile int*>(&bars->tile[k & 1]) : -1;
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&bars->tile_empty[k & 1]);
+    return tile;
+  };
+
   if (warp == 0) {
+    bool ok = true;
     if (lane == 0) {
       prefetch_tensormap(&qmap);
       prefetch_tensormap(&kmap);
       prefetch_tensormap(&vmap);
       prefetch_tensormap(&dom);
-      mbar_arrive_expect_tx(&bars->fixed_full, 2 * C::TILE);
-      for (int cb = 0; cb < C::NCB; ++cb) {
-        tma_load_3d(qs + cb * C::BOX, &qmap, &bars->fixed_full, cb * 64, h, q0);
-        tma_load_3d(dos + cb * C::BOX, &dom, &bars->fixed_full, cb * 64, h, q0);
+    }
+    int J = 0;  // items of earlier tiles: ring slots and phases continue across tiles
+    for (int k = 0; ok; ++k) {
+      int tile = -1;
+      if (lane == 0) {
+        tile = k == 0 ? (int)blockIdx.x : (int)gridDim.x + atomicAdd(p.tile_counter, 1);
+        if (tile >= n_tiles) tile = -1;
+        ok = mbar_wait(&bars->tile_empty[k & 1], ((k >> 1) & 1) ^ 1, kDevTimeoutEmpty);
+        if (ok) {
+          *reinterpret_cast<volatile int*>(&bars->tile[k & 1]) = tile;
+          mbar_arrive(&bars->tile_full[k & 1]);
+        }
       }
-      for (int j = 0; j < n; ++j) {
-        const int ks = j % 3, vsl = j & 1;
-        const int kv0 = (t_lo + j) * 128;
-        if (!mbar_wait(&bars->k_empty[ks], ((j / 3) & 1) ^ 1, kDevTimeoutEmpty)) break;
-        mbar_arrive_expect_tx(&bars->k_full[ks], C::TILE);
-        for (int cb = 0; cb < C::NCB; ++cb)
-          tma_load_3d(kring + ks * C::TILE + cb * C::BOX, &kmap, &bars->k_full[ks], cb * 64, kvh, kv0);
-        if (!mbar_wait(&bars->v_empty[vsl], ((j >> 1) & 1) ^ 1, kDevTimeoutEmpty)) break;
-        mbar_arrive_expect_tx(&bars->v_full[vsl], C::TILE);
-        for (int cb = 0; cb < C::NCB; ++cb)
-          tma_load_3d(vring + vsl * C::TILE + cb * C::BOX, &vmap, &bars->v_full[vsl], cb * 64, kvh, kv0);
+      tile = __shfl_sync(0xffffffffu, tile, 0);
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      if (!ok || tile < 0) break;
+      const DqTile d = dq_tile(tile, p);
+      if (lane == 0) {
+        // Q / dO slots are free once the previous tile's MMAs have completed.
+        if (k > 0) ok = mbar_wait(&bars->fixed_empty, (k - 1) & 1, kDevTimeoutEmpty);
+        if (ok) {
+          mbar_arrive_expect_tx(&bars->fixed_full, 2 * C::TILE);
+          for (int cb = 0; cb < C::NCB; ++cb) {
+            tma_load_3d(qs + cb * C::BOX, &qmap, &bars->fixed_full, cb * 64, d.h, d.q0);
+            tma_load_3d(dos + cb * C::BOX, &dom, &bars->fixed_full, cb * 64, d.h, d.q0);
+          }
+        }
+        for (int j = 0; ok && j < d.n; ++j) {
+          const int jj = J + j;
+          const int ks = jj % 3, vsl = jj & 1;
+          const int kv0 = (d.t_lo + j) * 128;
+          if (!(ok = mbar_wait(&bars->k_empty[ks], ((jj / 3) & 1) ^ 1, kDevTimeoutEmpty))) break;
+          mbar_arrive_expect_tx(&bars->k_full[ks], C::TILE);
+          for (int cb = 0; cb < C::NCB; ++cb)
+            tma_load_3d(kring + ks * C::TILE + cb * C::BOX, &kmap, &bars->k_full[ks], cb * 64, d.kvh, kv0);
+          if (!(ok = mbar_wait(&bars->v_empty[vsl], ((jj >> 1) & 1) ^ 1, kDevTimeoutEmpty))) break;
+          mbar_arrive_expect_tx(&bars->v_full[vsl], C::TILE);
+          for (int cb = 0; cb < C::NCB; ++cb)
+            tma_load_3d(vring + vsl * C::TILE + cb * C::BOX, &vmap, &bars->v_full[vsl], cb * 64, d.kvh, kv0);
+        }
       }
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      J += d.n;
     }
   } else if (warp == 1) {
     constexpr uint32_t ID_S = umma_idesc_bf16(128, 128, 0, 0);
     constexpr uint32_t ID_DQ = umma_idesc_bf16(128, HD, 0, 1);
-    bool ok = mbar_wait_warp(&bars->fixed_full, 0, kDevTimeoutFull);
     const uint32_t qa = smem_u32(qs), da = smem_u32(dos);
-    auto issue_s = [&](int j) {  // S(j) = Q K_j^T into region j & 1
-      const int ks = j % 3;
-      if (!mbar_wait_warp(&bars->k_full[ks], (j / 3) & 1, kDevTimeoutFull)) return false;
-      mma_kmajor_ss<HD>(tbase + 128 * (j & 1), qa, smem_u32(kring + ks * C::TILE), ID_S);
-      umma_commit_warp(&bars->s_full[j & 1]);
+    auto issue_s = [&](int jj) {  // S = Q K^T of running item jj into region jj & 1
+      const int ks = jj % 3;
+      if (!mbar_wait_warp(&bars->k_full[ks], (jj / 3) & 1, kDevTimeoutFull)) return false;
+      mma_kmajor_ss<HD>(tbase + 128 * (jj & 1), qa, smem_u32(kring + ks * C::TILE), ID_S);
+      umma_commit_warp(&bars->s_full[jj & 1]);
       return true;
     };
-    auto issue_dp = [&](int j) {  // dP(j) = dO V_j^T; V_j is free once it completes
-      const int vsl = j & 1;
-      if (!mbar_wait_warp(&bars->v_full[vsl], (j >> 1) & 1, kDevTimeoutFull)) return false;
+    auto issue_dp = [&](int jj) {  // dP = dO V^T; V's slot is free once it completes
+      const int vsl = jj & 1;
+      if (!mbar_wait_warp(&bars->v_full[vsl], (jj >> 1) & 1, kDevTimeoutFull)) return false;
       mma_kmajor_ss<HD>(t_p, da, smem_u32(vring + vsl * C::TILE), ID_S);
       umma_commit_warp(&bars->dp_full);
       umma_commit_warp(&bars->v_empty[vsl]);
       return true;
     };
-    if (ok) ok = issue_s(0);
-    if (ok && n > 1) ok = issue_s(1);
-    if (ok) ok = issue_dp(0);
-    for (int j = 0; ok && j < n; ++j) {
-      if (!(ok = mbar_wait_warp(&bars->dp_loaded, j & 1, kDevTimeoutFull))) break;
-      if (j + 1 < n && !(ok = issue_dp(j + 1))) break;
-      if (!(ok = mbar_wait_warp(&bars->ds_done[j & 1], (j >> 1) & 1, kDevTimeoutFull))) break;
-      // dQ += dS K over the 128 keys of item j.
-      mma_tmem_a<HD>(t_dq, tbase + 128 * (j & 1), smem_u32(kring + (j % 3) * C::TILE), ID_DQ, j > 0);
-      umma_commit_warp(&bars->k_empty[j % 3]);
-      if (j + 2 < n) ok = issue_s(j + 2);
+    bool ok = true;
+    int J = 0;
+    for (int k = 0; ok; ++k) {
+      const int tile = take_tile(k, ok);
+      if (!ok || tile < 0) break;
+      const int n = dq_tile(tile, p).n;
+      if (!(ok = mbar_wait_warp(&bars->fixed_full, k & 1, kDevTimeoutFull))) break;
+      if (!(ok = issue_s(J))) break;
+      if (n > 1 && !(ok = issue_s(J + 1))) break;
+      if (!(ok = issue_dp(J))) break;
+      for (int j = 0; ok && j < n; ++j) {
+        const int jj = J + j;
+        if (!(ok = mbar_wait_warp(&bars->dp_loaded, jj & 1, kDevTimeoutFull))) break;
+        if (j + 1 < n && !(ok = issue_dp(jj + 1))) break;
+        if (!(ok = mbar_wait_warp(&bars->ds_done[jj & 1], (jj >> 1) & 1, kDevTimeoutFull))) break;
+        // The first dQ MMA of a tile overwrites the accumulator: the previous
+        // tile's epilogue must have read it out.
+        if (j == 0 && k > 0 && !(ok = mbar_wait_warp(&bars->acc_empty, (k - 1) & 1, kDevTimeoutFull))) break;
+        // dQ += dS K over the 128 keys of item jj.
+        mma_tmem_a<HD>(t_dq, tbase + 128 * (jj & 1), smem_u32(kring + (jj % 3) * C::TILE), ID_DQ, j > 0);
+        umma_commit_warp(&bars->k_empty[jj % 3]);
+        if (j + 2 < n) ok = issue_s(jj + 2);
+      }
+      if (!ok) break;
+      umma_commit_warp(&bars->acc_full);
+      umma_commit_warp(&bars->fixed_empty);
+      J += n;
     }
-    umma_commit_warp(&bars->acc_full);
   } else {
     const int cq = (warp - 2) >> 2;  // column quarter of every 128-column tile
     const int sub = warp & 3;         // TMEM lane quarter
     const int r = sub * 32 + lane;
-    const int q_tok = q0 + r;
-    const bool row_ok = q_tok < p.L;
-    const int lo = row_ok ? p.run_start[q_tok] : 0x7fffffff;
-    const float neg_lse = row_ok ? -p.lse[(size_t)h * p.L + q_tok] : 0.f;
-    const float dlt = row_ok ? p.delta[(size_t)h * p.L + q_tok] : 0.f;
     const uint32_t lane_bits = (uint32_t)(sub * 32) << 16;
     bool ok = true;
-    for (int j = 0; j < n; ++j) {
-      const int kc0 = (t_lo + j) * 128 + 32 * cq;  // first key of this warp's 32 columns
-      const uint32_t ts = tbase + 128 * (j & 1) + lane_bits + 32 * cq;
-      float pf[32];
-      if (ok) ok = mbar_wait_warp(&bars->s_full[j & 1], (j >> 1) & 1, kDevTimeoutFull);
-      tc_fence_after();
-      if (ok) {
-        uint32_t sv[32];
-        tmem_ld32(ts, sv);
-        tmem_wait_ld();
+    int J = 0;
+    for (int k = 0; ok; ++k) {
+      const int tile = take_tile(k, ok);
+      if (!ok || tile < 0) break;
+      const DqTile d = dq_tile(tile, p);
+      const int q_tok = d.q0 + r;
+      const bool row_ok = q_tok < p.L;
+      const int lo = row_ok ? p.run_start[q_tok] : 0x7fffffff;
+      const float neg_lse = row_ok ? -p.lse[(size_t)d.h * p.L + q_tok] : 0.f;
+      const float dlt = row_ok ? p.delta[(size_t)d.h * p.L + q_tok] : 0.f;
+      for (int j = 0; j < d.n; ++j) {
+        const int jj = J + j;
+        const int kc0 = (d.t_lo + j) * 128 + 32 * cq;  // first key of this warp's 32 columns
+        const uint32_t ts = tbase + 128 * (jj & 1) + lane_bits + 32 * cq;
+        uint32_t pk[16];  // P as bf16 pairs, the precision dS is formed from in both kernels
+        if (ok) ok = mbar_wait_warp(&bars->s_full[jj & 1], (jj >> 1) & 1, kDevTimeoutFull);
+        tc_fence_after();
+        if (ok) {
+          uint32_t sv[32];
+          tmem_ld32(ts, sv);
+          tmem_wait_ld();
+          float pf[32];
 #pragma unroll
-        for (int c = 0; c < 32; ++c) {
-          const float xc = fmaf(__uint_as_float(sv[c]), p.scale_log2, neg_lse);
-          pf[c] = c < 32 - kFmaExp ? fast_exp2(xc) : exp2_fma(xc);
+          for (int c = 0; c < 32; ++c) {
+            const float xc = fmaf(__uint_as_float(sv[c]), p.scale_log2, neg_lse);
+            pf[c] = c < 32 - kFmaExp ? fast_exp2(xc) : exp2_fma(xc);
+          }
+          if (!(row_ok && kc0 >= lo && kc0 + 31 <= q_tok)) {
+#pragma unroll
+            for (int c = 0; c < 32; ++c)
+              if (!row_ok || kc0 + c < lo || kc0 + c > q_tok) pf[c] = 0.f;
+          }
+#pragma unroll
+          for (int e = 0; e < 16; ++e) pk[e] = pack_bf16x2(pf[2 * e], pf[2 * e + 1]);
         }
-        if (!(row_ok && kc0 >= lo && kc0 + 31 <= q_tok)) {
-#pragma unroll
-          for (int c = 0; c < 32; ++c)
-            if (!row_ok || kc0 + c < lo || kc0 + c > q_tok) pf[c] = 0.f;
+        if (ok) ok = mbar_wait_warp(&bars->dp_full, jj & 1, kDevTimeoutFull);
+        tc_fence_after();
+        uint32_t dv[32];
+        if (ok) {
+          tmem_ld32(t_p + lane_bits + 32 * cq, dv);
+          tmem_wait_ld();
         }
-      }
-      if (ok) ok = mbar_wait_warp(&bars->dp_full, j & 1, kDevTimeoutFull);
-      tc_fence_after();
-      uint32_t dv[32];
-      if (ok) {
-        tmem_ld32(t_p + lane_bits + 32 * cq, dv);
-        tmem_wait_ld();
-      }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&bars->dp_loaded);
-      if (ok) {
-        uint32_t ds[16];
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bars->dp_loaded);
+        if (ok) {
 #pragma unroll
-        for (int e = 0; e < 16; ++e)
-          ds[e] = pack_bf16x2(pf[2 * e] * (__uint_as_float(dv[2 * e]) - dlt),
-                              pf[2 * e + 1] * (__uint_as_float(dv[2 * e + 1]) - dlt));
-        tmem_st16(ts, ds);  // over S columns this warp already read
-        tmem_wait_st();
+          for (int e = 0; e < 16; ++e) {
+            const float2 pp = unpack_bf16x2(pk[e]);
+            pk[e] = pack_bf16x2(pp.x * (__uint_as_float(dv[2 * e]) - dlt), pp.y * (__uint_as_float(dv[2 * e + 1]) - dlt));
+          }
+          tmem_st16(ts, pk);  // dS over S columns this warp already read
+          tmem_wait_st();
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bars->ds_done[jj & 1]);
       }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&bars->ds_done[j & 1]);
-    }
-    // Epilogue: column quarter cq writes dQ columns [cq HD/4, (cq + 1) HD/4).
-    if (ok) ok = mbar_wait_warp(&bars->acc_full, 0, kDevTimeoutFull);
-    tc_fence_after();
-    if (ok) {
+      if (!ok) break;
+      // Epilogue: column quarter cq writes dQ columns [cq HD/4, (cq + 1) HD/4),
+      // 16 at a time; the accumulator is released as soon as it is in registers.
       constexpr int W = HD / 4;  // 32 or 16 columns
       const int col = cq * W;
-      uint32_t v[32];
-      if constexpr (W == 32)
-        tmem_ld32(t_dq + lane_bits + col, v);
-      else
-        tmem_ld16(t_dq + lane_bits + col, *reinterpret_cast<uint32_t(*)[16]>(v));
-      tmem_wait_ld();
-      if (row_ok) {
-        uint4* d4 = reinterpret_cast<uint4*>(p.dq + ((size_t)q_tok * p.Hq + h) * HD + col);
+      uint32_t v[W / 16][16];
+      if (!(ok = mbar_wait_warp(&bars->acc_full, k & 1, kDevTimeoutFull))) break;
+      tc_fence_after();
 #pragma unroll
-        for (int q4 = 0; q4 < W / 8; ++q4) {
-          uint4 w;
-          w.x = pack_bf16x2(__uint_as_float(v[8 * q4 + 0]) * p.scale, __uint_as_float(v[8 * q4 + 1]) * p.scale);
-          w.y = pack_bf16x2(__uint_as_float(v[8 * q4 + 2]) * p.scale, __uint_as_float(v[8 * q4 + 3]) * p.scale);
-          w.z = pack_bf16x2(__uint_as_float(v[8 * q4 + 4]) * p.scale, __uint_as_float(v[8 * q4 + 5]) * p.scale);
-          w.w = pack_bf16x2(__uint_as_float(v[8 * q4 + 6]) * p.scale, __uint_as_float(v[8 * q4 + 7]) * p.scale);
-          d4[q4] = w;
-        }
+      for (int c = 0; c < W / 16; ++c) tmem_ld16(t_dq + lane_bits + col + 16 * c, v[c]);
+      tmem_wait_ld();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bars->acc_empty);
+      if (row_ok) {
+        uint4* d4 = reinterpret_cast<uint4*>(p.dq + ((size_t)q_tok * p.Hq + d.h) * HD + col);
+#pragma unroll
+        for (int c = 0; c < W / 16; ++c)
+#pragma unroll
+          for (int q4 = 0; q4 < 2; ++q4) {
+            const uint32_t* u = v[c] + 8 * q4;
+            uint4 w;
+            w.x = pack_bf16x2(__uint_as_float(u[0]) * p.scale, __uint_as_float(u[1]) * p.scale);
+            w.y = pack_bf16x2(__uint_as_float(u[2]) * p.scale, __uint_as_float(u[3]) * p.scale);
+            w.z = pack_bf16x2(__uint_as_float(u[4]) * p.scale, __uint_as_float(u[5]) * p.scale);
+            w.w = pack_bf16x2(__uint_as_float(u[6]) * p.scale, __uint_as_float(u[7]) * p.scale);
+            d4[2 * c + q4] = w;
+          }
       }
+      J += d.n;
     }
   }
   tc_fence_before();
@@ -698,7 +793,10 @@ static cudaError_t launch_bwd_hd(const CUtensorMap& qm, const CUtensorMap& km, c
   varlen_bwd_dkdv_kernel<HD><<<dim3(n_t, p.Hkv), kBwdThreads, smem_kv, stream>>>(qm, km, vm, dom, p);
   e = cudaGetLastError();
   if (e != cudaSuccess) return e;
-  varlen_bwd_dq_kernel<HD><<<dim3(n_t, p.Hq), kBwdThreads, smem_dq, stream>>>(qm, km, vm, dom, p);
+  int dev = 0, sms = 148;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int dq_grid = std::max(1, std::min(n_t * p.Hq, sms));  // persistent: one CTA per SM
+  varlen_bwd_dq_kernel<HD><<<dq_grid, kBwdThreads, smem_dq, stream>>>(qm, km, vm, dom, p);
   return cudaGetLastError();
 }
 
@@ -709,7 +807,7 @@ cudaError_t launch_varlen_bwd(const CUtensorMap& qm, const CUtensorMap& km, cons
   // in flight to saturate HBM.
   const long long threads_needed = (long long)p.L * p.Hq * (p.head_dim / 8);
   const int blocks = (int)std::max<long long>(1, std::min<long long>((threads_needed + 255) / 256, 148 * 8));
-  bwd_delta_kernel<<<blocks, 256, 0, stream>>>(out, dout, p.L, p.Hq, p.head_dim, p.delta);
+  bwd_delta_kernel<<<blocks, 256, 0, stream>>>(out, dout, p.L, p.Hq, p.head_dim, p.delta, p.tile_counter);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   return p.head_dim == 128 ? launch_bwd_hd<128>(qm, km, vm, dom, p, stream)

@@ -215,7 +215,7 @@ def varlen_attention_bwd(q, k, v, out, dout, lse, run_start, run_end, scale):
     dq = torch.empty_like(q)
     dk = torch.empty_like(k)
     dv = torch.empty_like(v)
-    delta = torch.empty(Hq, L, dtype=torch.float32, device=q.device)
+    delta = torch.empty(Hq * L + 4, dtype=torch.float32, device=q.device)  # MB_VARLEN_BWD_SCRATCH_FLOATS
     _lib.call("mb_varlen_attention_bwd", _p(q), _p(k), _p(v), _p(out), _p(dout), _p(lse), L, Hq, Hkv, hd,
               _p(run_start), _p(run_end), float(scale), _p(dq), _p(dk), _p(dv), _p(delta), _stream(q))
     _count(3)
