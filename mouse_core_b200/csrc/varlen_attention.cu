@@ -195,9 +195,15 @@ __global__ void __launch_bounds__(320, 1) varlen_fwd_kernel(const __grid_constan
             if (!row_ok || kv < lo || kv > hi) v[e] = 0xff800000u;  // -inf
           }
         }
-        float mx = -INFINITY;
+        // Row max and (below) row sum as 8 independent chains: one long
+        // dependent chain per thread would serialise the softmax warp.
+        float mp[8];
 #pragma unroll
-        for (int e = 0; e < 128; ++e) mx = fmaxf(mx, __uint_as_float(v[e]));
+        for (int k = 0; k < 8; ++k) mp[k] = __uint_as_float(v[k]);
+#pragma unroll
+        for (int e = 8; e < 128; ++e) mp[e & 7] = fmaxf(mp[e & 7], __uint_as_float(v[e]));
+        const float mx = fmaxf(fmaxf(fmaxf(mp[0], mp[1]), fmaxf(mp[2], mp[3])),
+                               fmaxf(fmaxf(mp[4], mp[5]), fmaxf(mp[6], mp[7])));
         // The scale is positive, so the max of raw scores gives the max of scaled ones.
         const float m_tile = mx * p.scale_log2;
         const float m_new = fmaxf(m_used, m_tile);
@@ -207,7 +213,9 @@ __global__ void __launch_bounds__(320, 1) varlen_fwd_kernel(const __grid_constan
           m_used = m_new;
         }
         const float neg_mu = (m_used == -INFINITY) ? 0.f : -m_used;
-        float lt = 0.f;
+        float ls[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) ls[k] = 0.f;
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
           uint32_t pk[16];
@@ -215,11 +223,12 @@ __global__ void __launch_bounds__(320, 1) varlen_fwd_kernel(const __grid_constan
           for (int e = 0; e < 32; e += 2) {
             const float p0 = fast_exp2(fmaf(__uint_as_float(v[32 * c + e]), p.scale_log2, neg_mu));
             const float p1 = fast_exp2(fmaf(__uint_as_float(v[32 * c + e + 1]), p.scale_log2, neg_mu));
-            lt += p0 + p1;
+            ls[(e >> 1) & 7] += p0 + p1;
             pk[e >> 1] = pack_bf16x2(p0, p1);
           }
           tmem_st16(t_s + 16 * c, pk);
         }
+        const float lt = ((ls[0] + ls[1]) + (ls[2] + ls[3])) + ((ls[4] + ls[5]) + (ls[6] + ls[7]));
         l = l * alpha + lt;
         if (__any_sync(0xffffffffu, rescale && j > 0)) {
           const float a = (rescale && j > 0) ? alpha : 1.f;
