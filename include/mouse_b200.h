@@ -154,8 +154,11 @@ int mb_silu_mul(const void* gate_up, int rows, int inter, void* out, mb_stream_t
  *   run_start int32 [L] and tile_lo int32 [ceil(L / 128)] from
  *   mb_segment_meta(tile = 128) on ids that are sorted;
  *   out [L, q_heads, hd] bf16; lse f32 [q_heads, L] = log2 of the softmax
- *   denominator of the log2-scaled scores (saved for the backward).
+ *   denominator of the log2-scaled scores (saved for the backward), in a
+ *   buffer of MB_VARLEN_FWD_LSE_FLOATS(q_heads, L) floats whose last 4 are
+ *   the persistent kernel's scratch.
  * ------------------------------------------------------------------- */
+#define MB_VARLEN_FWD_LSE_FLOATS(q_heads, L) ((size_t)(q_heads) * (size_t)(L) + 4u)
 int mb_varlen_attention_fwd(const void* q, const void* k, const void* v, int L, int q_heads, int kv_heads,
                             int head_dim, const int32_t* run_start, const int32_t* tile_lo, float scale, void* out,
                             float* lse, mb_stream_t stream);

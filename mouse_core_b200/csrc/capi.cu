@@ -289,6 +289,7 @@ int mb_varlen_attention_fwd(const void* q, const void* k, const void* v, int L, 
   p.scale_log2 = scale * 1.4426950408889634f;
   p.out = static_cast<__nv_bfloat16*>(out);
   p.lse = lse;
+  p.tile_counter = reinterpret_cast<int*>(lse + (size_t)q_heads * L);
   cudaError_t e = mb::launch_varlen_fwd(qm, km, vm, p, (cudaStream_t)stream);
   return e == cudaSuccess ? MB_OK : cuda_fail(e, "varlen attention forward launch");
 }

@@ -79,6 +79,7 @@ struct VarlenParams {
   float scale_log2;
   __nv_bfloat16* out;        // [L, Hq, HD]
   float* lse;                // [Hq, L], log2 units
+  int* tile_counter;         // [1] scratch: the persistent kernel's tile counter
 };
 cudaError_t launch_varlen_fwd(const CUtensorMap& qm, const CUtensorMap& km, const CUtensorMap& vm,
                               const VarlenParams& p, cudaStream_t stream);

@@ -9,10 +9,16 @@
 // BlockMask is needed: a query tile only visits key tiles from
 // tile_lo[t] / 128 to its diagonal.
 //
-// One CTA = one 128-token query tile x one pair of q-heads sharing a kv-head
-// (a single q-head when the GQA group is odd). Warp roles (320 threads):
-//   warp 0      TMA producer: Q once, then K/V tiles through a 2-3 stage ring
-//   warp 1      TMEM allocator; lane 0 issues every tcgen05.mma
+// Work tile = one 128-token query tile x one pair of q-heads sharing a
+// kv-head (a single q-head when the GQA group is odd). The kernel is
+// persistent: one CTA per SM takes tiles from a counter, longest-history
+// query tiles first; the producer hands each tile id to the other warps
+// through a two-slot ring, and barrier phases follow a running key-tile count
+// across tiles. Q is released after a tile's last Q K^T MMA, so the next
+// tile's Q loads during the last softmax, P V and epilogue; O is released
+// once the epilogue has read it. Warp roles (320 threads):
+//   warp 0      TMA producer: Q once per tile, K/V tiles through a 2-3 stage ring
+//   warp 1      TMEM allocator; the whole warp issues every tcgen05.mma
 //   warps 2-5   softmax of head 0 (thread = query row = TMEM lane)
 //   warps 6-9   softmax of head 1
 // Tensor memory (512 columns): S_h = Q_h K^T at columns 128h, O_h at 256 + HD h.
@@ -43,12 +49,31 @@ struct FwdTile {
 };
 
 struct FwdBarriers {
-  uint64_t q_full;
+  uint64_t tile_full[2], tile_empty[2];  // tile-id ring (producer -> MMA + softmax warps)
+  uint64_t q_full, q_empty;
   uint64_t k_full[3], v_full[3], kv_empty[3];
   uint64_t s_full[2], p_full[2];
-  uint64_t o_full;
+  uint64_t o_full, o_empty;
   uint32_t tmem_base;
+  int tile[2];
 };
+
+struct FwdWork {
+  int q0, h0, kvh, qt, t_lo, n;
+};
+
+__device__ __forceinline__ FwdWork fwd_work(int tile, const VarlenParams& p) {
+  const int n_qt = (p.L + 127) / 128;
+  const int groups = p.Hq / p.heads_per_cta;
+  FwdWork w;
+  w.qt = n_qt - 1 - tile / groups;  // longest-history tiles of a stream first
+  w.h0 = (tile % groups) * p.heads_per_cta;
+  w.kvh = w.h0 / p.G;
+  w.q0 = w.qt * 128;
+  w.t_lo = p.tile_lo[w.qt] / 128;
+  w.n = min(w.q0 + 127, p.L - 1) / 128 - w.t_lo + 1;
+  return w;
+}
 
 template <int HD>
 __global__ void __launch_bounds__(320, 1) varlen_fwd_kernel(const __grid_constant__ CUtensorMap qmap,
@@ -64,18 +89,16 @@ __global__ void __launch_bounds__(320, 1) varlen_fwd_kernel(const __grid_constan
   FwdBarriers* bars = reinterpret_cast<FwdBarriers*>(vs + C::STAGES * C::KVTILE);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int n_qt = (p.L + C::BM - 1) / C::BM;
-  const int qt = n_qt - 1 - (int)blockIdx.x;  // longest-history tiles of a stream first
-  const int q0 = qt * C::BM;
-  const int h0 = blockIdx.y * p.heads_per_cta;
   const int hpc = p.heads_per_cta;
-  const int kvh = h0 / p.G;
-  const int t_lo = p.tile_lo[qt] / C::BN;
-  const int t_hi = min(q0 + C::BM - 1, p.L - 1) / C::BN;
-  const int n_tiles = t_hi - t_lo + 1;
+  const int n_work = ((p.L + C::BM - 1) / C::BM) * (p.Hq / hpc);
 
   if (threadIdx.x == 0) {
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&bars->tile_full[s], 1);
+      mbar_init(&bars->tile_empty[s], 9);  // MMA warp + 8 softmax warps
+    }
     mbar_init(&bars->q_full, 1);
+    mbar_init(&bars->q_empty, 1);
     for (int s = 0; s < C::STAGES; ++s) {
       mbar_init(&bars->k_full[s], 1);
       mbar_init(&bars->v_full[s], 1);
@@ -86,6 +109,7 @@ __global__ void __launch_bounds__(320, 1) varlen_fwd_kernel(const __grid_constan
       mbar_init(&bars->p_full[h], 4);
     }
     mbar_init(&bars->o_full, 1);
+    mbar_init(&bars->o_empty, 8);
     fence_barrier_init();
   }
   if (warp == 1) tmem_alloc(&bars->tmem_base, C::TMEM_COLS);
@@ -94,27 +118,63 @@ __global__ void __launch_bounds__(320, 1) varlen_fwd_kernel(const __grid_constan
   tc_fence_after();
   const uint32_t tbase = bars->tmem_base;
 
+  // Tile k of this CTA from the ring (each consumer warp reads every slot once).
+  auto take_tile = [&](int k, bool& ok) {
+    ok = mbar_wait_warp(&bars->tile_full[k & 1], (k >> 1) & 1, kDevTimeoutFull);
+    const int tile = ok ? *reinterpret_cast<volatile int*>(&bars->tile[k & 1]) : -1;
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&bars->tile_empty[k & 1]);
+    return tile;
+  };
+
   if (warp == 0) {
     // ------------------------------------------------------------ producer
+    bool ok = true;
     if (lane == 0) {
       prefetch_tensormap(&qmap);
       prefetch_tensormap(&kmap);
       prefetch_tensormap(&vmap);
-      mbar_arrive_expect_tx(&bars->q_full, hpc * C::QTILE);
-      for (int hh = 0; hh < hpc; ++hh)
-        for (int cb = 0; cb < C::NCB; ++cb)
-          tma_load_3d(qs + hh * C::QTILE + cb * C::BOX, &qmap, &bars->q_full, cb * 64, h0 + hh, q0);
-      for (int j = 0; j < n_tiles; ++j) {
-        const int st = j % C::STAGES;
-        if (!mbar_wait(&bars->kv_empty[st], ((j / C::STAGES) & 1) ^ 1, kDevTimeoutEmpty)) break;
-        const int kv0 = (t_lo + j) * C::BN;
-        mbar_arrive_expect_tx(&bars->k_full[st], C::KVTILE);
-        for (int cb = 0; cb < C::NCB; ++cb)
-          tma_load_3d(ks + st * C::KVTILE + cb * C::BOX, &kmap, &bars->k_full[st], cb * 64, kvh, kv0);
-        mbar_arrive_expect_tx(&bars->v_full[st], C::KVTILE);
-        for (int cb = 0; cb < C::NCB; ++cb)
-          tma_load_3d(vs + st * C::KVTILE + cb * C::BOX, &vmap, &bars->v_full[st], cb * 64, kvh, kv0);
+    }
+    int J = 0;  // key tiles of earlier work tiles: ring slots and phases continue
+    for (int k = 0; ok; ++k) {
+      int tile = -1;
+      if (lane == 0) {
+        tile = k == 0 ? (int)blockIdx.x : (int)gridDim.x + atomicAdd(p.tile_counter, 1);
+        if (tile >= n_work) tile = -1;
+        ok = mbar_wait(&bars->tile_empty[k & 1], ((k >> 1) & 1) ^ 1, kDevTimeoutEmpty);
+        if (ok) {
+          *reinterpret_cast<volatile int*>(&bars->tile[k & 1]) = tile;
+          mbar_arrive(&bars->tile_full[k & 1]);
+        }
       }
+      tile = __shfl_sync(0xffffffffu, tile, 0);
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      if (!ok || tile < 0) break;
+      const FwdWork w = fwd_work(tile, p);
+      if (lane == 0) {
+        // The Q slots are free once the previous tile's last Q K^T completed.
+        if (k > 0) ok = mbar_wait(&bars->q_empty, (k - 1) & 1, kDevTimeoutEmpty);
+        if (ok) {
+          mbar_arrive_expect_tx(&bars->q_full, hpc * C::QTILE);
+          for (int hh = 0; hh < hpc; ++hh)
+            for (int cb = 0; cb < C::NCB; ++cb)
+              tma_load_3d(qs + hh * C::QTILE + cb * C::BOX, &qmap, &bars->q_full, cb * 64, w.h0 + hh, w.q0);
+        }
+        for (int j = 0; ok && j < w.n; ++j) {
+          const int jj = J + j;
+          const int st = jj % C::STAGES;
+          if (!(ok = mbar_wait(&bars->kv_empty[st], ((jj / C::STAGES) & 1) ^ 1, kDevTimeoutEmpty))) break;
+          const int kv0 = (w.t_lo + j) * C::BN;
+          mbar_arrive_expect_tx(&bars->k_full[st], C::KVTILE);
+          for (int cb = 0; cb < C::NCB; ++cb)
+            tma_load_3d(ks + st * C::KVTILE + cb * C::BOX, &kmap, &bars->k_full[st], cb * 64, w.kvh, kv0);
+          mbar_arrive_expect_tx(&bars->v_full[st], C::KVTILE);
+          for (int cb = 0; cb < C::NCB; ++cb)
+            tma_load_3d(vs + st * C::KVTILE + cb * C::BOX, &vmap, &bars->v_full[st], cb * 64, w.kvh, kv0);
+        }
+      }
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      J += w.n;
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issue
@@ -122,7 +182,6 @@ __global__ void __launch_bounds__(320, 1) varlen_fwd_kernel(const __grid_constan
     // asm block issued by an elected lane.
     constexpr uint32_t ID_QK = umma_idesc_bf16(128, 128, 0, 0);
     constexpr uint32_t ID_PV = umma_idesc_bf16(128, HD, 0, 1);
-    bool ok = mbar_wait_warp(&bars->q_full, 0, kDevTimeoutFull);
     auto issue_qk = [&](int hh, int st) {
       const uint64_t dq = umma_desc_sw128(smem_u32(qs + hh * C::QTILE), 16, 1024);
       const uint64_t dk = umma_desc_sw128(smem_u32(ks + st * C::KVTILE), 16, 1024);
@@ -132,149 +191,179 @@ __global__ void __launch_bounds__(320, 1) varlen_fwd_kernel(const __grid_constan
         umma_ss_k64_warp(tbase + 128 * hh, dq, dk, ID_QK);
       umma_commit_warp(&bars->s_full[hh]);
     };
-    if (ok) ok = mbar_wait_warp(&bars->k_full[0], 0, kDevTimeoutFull);
-    if (ok) {
-      for (int hh = 0; hh < hpc; ++hh) issue_qk(hh, 0);
-    }
-    for (int j = 0; ok && j < n_tiles; ++j) {
-      const int st = j % C::STAGES;
-      const uint32_t ph = (j / C::STAGES) & 1;
-      if (!(ok = mbar_wait_warp(&bars->v_full[st], ph, kDevTimeoutFull))) break;
-      const bool more = j + 1 < n_tiles;
-      const int st1 = (j + 1) % C::STAGES;
-      bool k_next = false;
-      const uint64_t dv = umma_desc_sw128(smem_u32(vs + st * C::KVTILE), C::BOX, 1024);
-      for (int hh = 0; hh < hpc; ++hh) {
-        if (!(ok = mbar_wait_warp(&bars->p_full[hh], j & 1, kDevTimeoutFull))) break;
-        // O_h += P_h V (P bf16 in the first 64 columns of S_h)
-        umma_ts_t128_linear_warp(tbase + 256 + HD * hh, tbase + 128 * hh, dv, ID_PV, j > 0 ? 1u : 0u);
-        if (more) {
-          if (!k_next) {
-            if (!(ok = mbar_wait_warp(&bars->k_full[st1], ((j + 1) / C::STAGES) & 1, kDevTimeoutFull))) break;
-            k_next = true;
+    bool ok = true;
+    int J = 0;
+    for (int k = 0; ok; ++k) {
+      const int tile = take_tile(k, ok);
+      if (!ok || tile < 0) break;
+      const int n = fwd_work(tile, p).n;
+      if (!(ok = mbar_wait_warp(&bars->q_full, k & 1, kDevTimeoutFull))) break;
+      if (!(ok = mbar_wait_warp(&bars->k_full[J % C::STAGES], (J / C::STAGES) & 1, kDevTimeoutFull))) break;
+      for (int hh = 0; hh < hpc; ++hh) issue_qk(hh, J % C::STAGES);
+      if (n == 1) umma_commit_warp(&bars->q_empty);  // that was the tile's last Q K^T
+      for (int j = 0; ok && j < n; ++j) {
+        const int jj = J + j;
+        const int st = jj % C::STAGES;
+        if (!(ok = mbar_wait_warp(&bars->v_full[st], (jj / C::STAGES) & 1, kDevTimeoutFull))) break;
+        const bool more = j + 1 < n;
+        const int st1 = (jj + 1) % C::STAGES;
+        bool k_next = false;
+        const uint64_t dv = umma_desc_sw128(smem_u32(vs + st * C::KVTILE), C::BOX, 1024);
+        for (int hh = 0; hh < hpc; ++hh) {
+          if (!(ok = mbar_wait_warp(&bars->p_full[hh], jj & 1, kDevTimeoutFull))) break;
+          // The tile's first P V overwrites O: the previous epilogue must hold it.
+          if (j == 0 && hh == 0 && k > 0 && !(ok = mbar_wait_warp(&bars->o_empty, (k - 1) & 1, kDevTimeoutFull)))
+            break;
+          // O_h += P_h V (P bf16 in the first 64 columns of S_h)
+          umma_ts_t128_linear_warp(tbase + 256 + HD * hh, tbase + 128 * hh, dv, ID_PV, j > 0 ? 1u : 0u);
+          if (more) {
+            if (!k_next) {
+              if (!(ok = mbar_wait_warp(&bars->k_full[st1], ((jj + 1) / C::STAGES) & 1, kDevTimeoutFull))) break;
+              k_next = true;
+            }
+            issue_qk(hh, st1);
           }
-          issue_qk(hh, st1);
         }
+        if (!ok) break;
+        if (more && j + 2 == n) umma_commit_warp(&bars->q_empty);  // the tile's last Q K^T is queued
+        umma_commit_warp(&bars->kv_empty[st]);
       }
       if (!ok) break;
-      umma_commit_warp(&bars->kv_empty[st]);
+      umma_commit_warp(&bars->o_full);
+      J += n;
     }
-    umma_commit_warp(&bars->o_full);
   } else {
     // ------------------------------------------------------------ softmax
     const int hh = (warp - 2) >> 2;
     const int sub = warp & 3;  // TMEM lane quarter this warp may access
     const int r = sub * 32 + lane;
-    const int q_tok = q0 + r;
-    const bool row_ok = q_tok < p.L;
-    const int lo = row_ok ? p.run_start[q_tok] : 0x7fffffff;
-    const int hi = q_tok;
     const uint32_t lane_bits = (uint32_t)(sub * 32) << 16;
     const uint32_t t_s = tbase + 128 * hh + lane_bits;
     const uint32_t t_o = tbase + 256 + HD * hh + lane_bits;
     const bool active = hh < hpc;
-    float m_used = -INFINITY, l = 0.f;
     bool ok = true;
-    for (int j = 0; active && j < n_tiles; ++j) {
-      const int kv0 = (t_lo + j) * C::BN;
-      if (ok) ok = mbar_wait_warp(&bars->s_full[hh], j & 1, kDevTimeoutFull);
-      tc_fence_after();
-      float alpha = 1.f;
-      bool rescale = false;
-      if (ok) {
-        const bool full = row_ok && kv0 >= lo && kv0 + C::BN - 1 <= hi;
-        // One TMEM read of the whole 128-column score row into registers.
-        uint32_t v[128];
+    int J = 0;
+    for (int k = 0; ok; ++k) {
+      const int tile = take_tile(k, ok);
+      if (!ok || tile < 0) break;
+      const FwdWork w = fwd_work(tile, p);
+      const int q_tok = w.q0 + r;
+      const bool row_ok = q_tok < p.L;
+      const int lo = row_ok ? p.run_start[q_tok] : 0x7fffffff;
+      const int hi = q_tok;
+      float m_used = -INFINITY, l = 0.f;
+      for (int j = 0; active && j < w.n; ++j) {
+        const int jj = J + j;
+        const int kv0 = (w.t_lo + j) * C::BN;
+        if (ok) ok = mbar_wait_warp(&bars->s_full[hh], jj & 1, kDevTimeoutFull);
+        tc_fence_after();
+        float alpha = 1.f;
+        bool rescale = false;
+        if (ok) {
+          const bool full = row_ok && kv0 >= lo && kv0 + C::BN - 1 <= hi;
+          // One TMEM read of the whole 128-column score row into registers.
+          uint32_t v[128];
 #pragma unroll
-        for (int c = 0; c < 4; ++c) tmem_ld32(t_s + 32 * c, *reinterpret_cast<uint32_t(*)[32]>(v + 32 * c));
-        tmem_wait_ld();
-        if (!full) {
+          for (int c = 0; c < 4; ++c) tmem_ld32(t_s + 32 * c, *reinterpret_cast<uint32_t(*)[32]>(v + 32 * c));
+          tmem_wait_ld();
+          if (!full) {
 #pragma unroll
-          for (int e = 0; e < 128; ++e) {
-            const int kv = kv0 + e;
-            if (!row_ok || kv < lo || kv > hi) v[e] = 0xff800000u;  // -inf
+            for (int e = 0; e < 128; ++e) {
+              const int kv = kv0 + e;
+              if (!row_ok || kv < lo || kv > hi) v[e] = 0xff800000u;  // -inf
+            }
           }
-        }
-        // Row max and (below) row sum as 8 independent chains: one long
-        // dependent chain per thread would serialise the softmax warp.
-        float mp[8];
+          // Row max and (below) row sum as 8 independent chains: one long
+          // dependent chain per thread would serialise the softmax warp.
+          float mp[8];
 #pragma unroll
-        for (int k = 0; k < 8; ++k) mp[k] = __uint_as_float(v[k]);
+          for (int q = 0; q < 8; ++q) mp[q] = __uint_as_float(v[q]);
 #pragma unroll
-        for (int e = 8; e < 128; ++e) mp[e & 7] = fmaxf(mp[e & 7], __uint_as_float(v[e]));
-        const float mx = fmaxf(fmaxf(fmaxf(mp[0], mp[1]), fmaxf(mp[2], mp[3])),
-                               fmaxf(fmaxf(mp[4], mp[5]), fmaxf(mp[6], mp[7])));
-        // The scale is positive, so the max of raw scores gives the max of scaled ones.
-        const float m_tile = mx * p.scale_log2;
-        const float m_new = fmaxf(m_used, m_tile);
-        if (m_new > m_used + 8.f) {
-          rescale = true;
-          alpha = exp2f(m_used - m_new);
-          m_used = m_new;
-        }
-        const float neg_mu = (m_used == -INFINITY) ? 0.f : -m_used;
-        float ls[8];
-#pragma unroll
-        for (int k = 0; k < 8; ++k) ls[k] = 0.f;
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          uint32_t pk[16];
-#pragma unroll
-          for (int e = 0; e < 32; e += 2) {
-            const float p0 = fast_exp2(fmaf(__uint_as_float(v[32 * c + e]), p.scale_log2, neg_mu));
-            const float p1 = fast_exp2(fmaf(__uint_as_float(v[32 * c + e + 1]), p.scale_log2, neg_mu));
-            ls[(e >> 1) & 7] += p0 + p1;
-            pk[e >> 1] = pack_bf16x2(p0, p1);
+          for (int e = 8; e < 128; ++e) mp[e & 7] = fmaxf(mp[e & 7], __uint_as_float(v[e]));
+          const float mx = fmaxf(fmaxf(fmaxf(mp[0], mp[1]), fmaxf(mp[2], mp[3])),
+                                 fmaxf(fmaxf(mp[4], mp[5]), fmaxf(mp[6], mp[7])));
+          // The scale is positive, so the max of raw scores gives the max of scaled ones.
+          const float m_tile = mx * p.scale_log2;
+          const float m_new = fmaxf(m_used, m_tile);
+          if (m_new > m_used + 8.f) {
+            rescale = true;
+            alpha = exp2f(m_used - m_new);
+            m_used = m_new;
           }
-          tmem_st16(t_s + 16 * c, pk);
-        }
-        const float lt = ((ls[0] + ls[1]) + (ls[2] + ls[3])) + ((ls[4] + ls[5]) + (ls[6] + ls[7]));
-        l = l * alpha + lt;
-        if (__any_sync(0xffffffffu, rescale && j > 0)) {
-          const float a = (rescale && j > 0) ? alpha : 1.f;
+          const float neg_mu = (m_used == -INFINITY) ? 0.f : -m_used;
+          float ls[8];
 #pragma unroll
-          for (int c = 0; c < HD / 32; ++c) {
-            uint32_t o[32];
-            tmem_ld32(t_o + 32 * c, o);
-            tmem_wait_ld();
+          for (int q = 0; q < 8; ++q) ls[q] = 0.f;
 #pragma unroll
-            for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * a);
-            tmem_st32(t_o + 32 * c, o);
+          for (int c = 0; c < 4; ++c) {
+            uint32_t pk[16];
+#pragma unroll
+            for (int e = 0; e < 32; e += 2) {
+              const float p0 = fast_exp2(fmaf(__uint_as_float(v[32 * c + e]), p.scale_log2, neg_mu));
+              const float p1 = fast_exp2(fmaf(__uint_as_float(v[32 * c + e + 1]), p.scale_log2, neg_mu));
+              ls[(e >> 1) & 7] += p0 + p1;
+              pk[e >> 1] = pack_bf16x2(p0, p1);
+            }
+            tmem_st16(t_s + 16 * c, pk);
           }
+          const float lt = ((ls[0] + ls[1]) + (ls[2] + ls[3])) + ((ls[4] + ls[5]) + (ls[6] + ls[7]));
+          l = l * alpha + lt;
+          if (__any_sync(0xffffffffu, rescale && j > 0)) {
+            const float a = (rescale && j > 0) ? alpha : 1.f;
+#pragma unroll
+            for (int c = 0; c < HD / 32; ++c) {
+              uint32_t o[32];
+              tmem_ld32(t_o + 32 * c, o);
+              tmem_wait_ld();
+#pragma unroll
+              for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * a);
+              tmem_st32(t_o + 32 * c, o);
+            }
+          }
+          tmem_wait_st();
         }
-        tmem_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bars->p_full[hh]);
       }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&bars->p_full[hh]);
-    }
-    if (active) {
-      if (ok) ok = mbar_wait_warp(&bars->o_full, 0, kDevTimeoutFull);
+      // Epilogue: O out of TMEM in 32-column chunks, normalised and stored
+      // with lse; the accumulator is released after its last chunk. A warp
+      // without a head (odd GQA group) only keeps the o_empty count.
+      if (!(ok = ok && mbar_wait_warp(&bars->o_full, k & 1, kDevTimeoutFull))) break;
       tc_fence_after();
-      if (ok) {
-        const int h = h0 + hh;
+      if (active) {
+        const int h = w.h0 + hh;
         const float inv = (l > 0.f) ? 1.f / l : 0.f;
-        __nv_bfloat16* dst = p.out + ((size_t)q_tok * p.Hq + h) * HD;
+        uint4* d4 = reinterpret_cast<uint4*>(p.out + ((size_t)q_tok * p.Hq + h) * HD);
 #pragma unroll
         for (int c = 0; c < HD / 32; ++c) {
-          uint32_t v[32];
-          tmem_ld32(t_o + 32 * c, v);
+          uint32_t o[32];
+          tmem_ld32(t_o + 32 * c, o);
           tmem_wait_ld();
+          if (c == HD / 32 - 1) {
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&bars->o_empty);
+          }
           if (row_ok) {
-            uint4* d4 = reinterpret_cast<uint4*>(dst + 32 * c);
 #pragma unroll
             for (int q4 = 0; q4 < 4; ++q4) {
-              uint4 w;
-              w.x = pack_bf16x2(__uint_as_float(v[8 * q4 + 0]) * inv, __uint_as_float(v[8 * q4 + 1]) * inv);
-              w.y = pack_bf16x2(__uint_as_float(v[8 * q4 + 2]) * inv, __uint_as_float(v[8 * q4 + 3]) * inv);
-              w.z = pack_bf16x2(__uint_as_float(v[8 * q4 + 4]) * inv, __uint_as_float(v[8 * q4 + 5]) * inv);
-              w.w = pack_bf16x2(__uint_as_float(v[8 * q4 + 6]) * inv, __uint_as_float(v[8 * q4 + 7]) * inv);
-              d4[q4] = w;
+              uint4 u;
+              u.x = pack_bf16x2(__uint_as_float(o[8 * q4 + 0]) * inv, __uint_as_float(o[8 * q4 + 1]) * inv);
+              u.y = pack_bf16x2(__uint_as_float(o[8 * q4 + 2]) * inv, __uint_as_float(o[8 * q4 + 3]) * inv);
+              u.z = pack_bf16x2(__uint_as_float(o[8 * q4 + 4]) * inv, __uint_as_float(o[8 * q4 + 5]) * inv);
+              u.w = pack_bf16x2(__uint_as_float(o[8 * q4 + 6]) * inv, __uint_as_float(o[8 * q4 + 7]) * inv);
+              d4[4 * c + q4] = u;
             }
           }
         }
         if (row_ok) p.lse[(size_t)h * p.L + q_tok] = (l > 0.f) ? m_used + log2f(l) : -INFINITY;
+      } else {
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bars->o_empty);
       }
+      J += w.n;
     }
   }
   tc_fence_before();
@@ -288,16 +377,20 @@ __global__ void __launch_bounds__(320, 1) varlen_fwd_kernel(const __grid_constan
 
 cudaError_t launch_varlen_fwd(const CUtensorMap& qm, const CUtensorMap& km, const CUtensorMap& vm,
                               const VarlenParams& p, cudaStream_t stream) {
-  const int n_qt = (p.L + 127) / 128;
-  dim3 grid(n_qt, p.Hq / p.heads_per_cta);
+  const int n_work = ((p.L + 127) / 128) * (p.Hq / p.heads_per_cta);
+  int dev = 0, sms = 148;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int grid = std::max(1, std::min(n_work, sms));  // persistent: one CTA per SM
+  cudaError_t e = cudaMemsetAsync(p.tile_counter, 0, sizeof(int), stream);
+  if (e != cudaSuccess) return e;
   if (p.head_dim == 128) {
     const int smem = FwdTile<128>::SMEM;
-    cudaError_t e = cudaFuncSetAttribute(varlen_fwd_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    e = cudaFuncSetAttribute(varlen_fwd_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
     varlen_fwd_kernel<128><<<grid, 320, smem, stream>>>(qm, km, vm, p);
   } else {
     const int smem = FwdTile<64>::SMEM;
-    cudaError_t e = cudaFuncSetAttribute(varlen_fwd_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    e = cudaFuncSetAttribute(varlen_fwd_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
     varlen_fwd_kernel<64><<<grid, 320, smem, stream>>>(qm, km, vm, p);
   }

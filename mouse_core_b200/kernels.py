@@ -196,11 +196,11 @@ def varlen_attention_fwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, run_
     if k.shape != (L, Hkv, hd) or v.shape != k.shape:
         raise ValueError("k and v must be [L, Hkv, hd] matching q")
     out = torch.empty_like(q)
-    lse = torch.empty(Hq, L, dtype=torch.float32, device=q.device)
+    lse_buf = torch.empty(Hq * L + 4, dtype=torch.float32, device=q.device)  # MB_VARLEN_FWD_LSE_FLOATS
     _lib.call("mb_varlen_attention_fwd", _p(q), _p(k), _p(v), L, Hq, Hkv, hd, _p(run_start), _p(tile_lo),
-              float(scale), _p(out), _p(lse), _stream(q))
+              float(scale), _p(out), _p(lse_buf), _stream(q))
     _count()
-    return out, lse
+    return out, lse_buf[:Hq * L].view(Hq, L)
 
 
 def varlen_attention_bwd(q, k, v, out, dout, lse, run_start, run_end, scale):
