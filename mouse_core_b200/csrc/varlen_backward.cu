@@ -10,7 +10,7 @@
 // Three kernels, deterministic (every output element is computed by one CTA;
 // the only atomic is the dq kernel's tile counter):
 //  * delta:  D[h, i] (fp32) from dO and O.
-//  * dkdv:   one CTA per (128-key tile, kv-head), walking every (q-head of the
+//  * dkdv:   per (128-key tile, kv-head) tile (persistent, like dq), walking every (q-head of the
 //            group, 128-query tile) item whose queries may see its keys. Keys
 //            sit on the TMEM lanes: S^T = K Q^T and dP^T = V dO^T land in two
 //            128-column regions; the element-wise warps write P^T (bf16) over
@@ -461,17 +461,40 @@ __global__ void __launch_bounds__(kBwdThreads, 1) varlen_bwd_dq_kernel(const __g
 }
 
 // ---------------------------------------------------------------- dkdv kernel
+// Persistent like the dq kernel: one CTA per SM takes (key tile, kv-head)
+// tiles from the second counter; K and V are released after a tile's last
+// S^T / dP^T MMAs, so the next tile's K / V load during its last item and
+// epilogue, and dV / dK are released once the epilogue has read them.
 struct DkdvBars {
-  uint64_t fixed_full;  // K, V
+  uint64_t tile_full[2], tile_empty[2];  // tile-id ring (producer -> MMA + element-wise warps)
+  uint64_t fixed_full, fixed_empty;      // K, V of the current tile; free again
   uint64_t q_full[3], q_empty[3], d_full[2], d_empty[2];
   uint64_t s_full, dp_full;  // S^T(t), dP^T(t)
   uint64_t p_half;           // bf16 P^T of query quarters 0-1 in TMEM
   uint64_t p_done;           // bf16 P^T of the current item in TMEM
   uint64_t p_read;           // the dS warps hold that P^T in registers
   uint64_t ds_done;          // bf16 dS^T of the current item in TMEM
-  uint64_t acc_full;
+  uint64_t acc_full;         // dV, dK of the tile complete in TMEM
+  uint64_t acc_empty;        // the element-wise warps have read them out
   uint32_t tmem_base;
+  int tile[2];
 };
+
+struct DkdvTile {
+  int kv0, kvh, i_lo, nqi, n;
+};
+
+__device__ __forceinline__ DkdvTile dkdv_tile(int tile, const VarlenBwdParams& p) {
+  DkdvTile d;
+  const int kt = tile / p.Hkv;
+  d.kvh = tile % p.Hkv;
+  d.kv0 = kt * 128;
+  const int last = min(d.kv0 + 127, p.L - 1);
+  d.i_lo = kt;
+  d.nqi = (p.run_end[last] - 1) / 128 - d.i_lo + 1;
+  d.n = p.G * d.nqi;  // (q-head, query tile) items
+  return d;
+}
 
 template <int HD>
 __global__ void __launch_bounds__(kBwdThreads, 1) varlen_bwd_dkdv_kernel(const __grid_constant__ CUtensorMap qmap,
@@ -494,17 +517,15 @@ __global__ void __launch_bounds__(kBwdThreads, 1) varlen_bwd_dkdv_kernel(const _
   DkdvBars* bars = reinterpret_cast<DkdvBars*>(dlt_ring + 2 * 128);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int kt = (int)blockIdx.x;
-  const int kv0 = kt * 128;
-  const int kvh = blockIdx.y;
-  const int last = min(kv0 + 127, p.L - 1);
-  const int i_lo = kt;
-  const int i_hi = (p.run_end[last] - 1) / 128;
-  const int nqi = i_hi - i_lo + 1;
-  const int n = p.G * nqi;  // (q-head, query tile) items
+  const int n_tiles = ((p.L + 127) / 128) * p.Hkv;
 
   if (threadIdx.x == 0) {
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&bars->tile_full[s], 1);
+      mbar_init(&bars->tile_empty[s], 1 + kPWarps + kDsWarps);
+    }
     mbar_init(&bars->fixed_full, 1);
+    mbar_init(&bars->fixed_empty, 1);
     for (int s = 0; s < 3; ++s) {
       mbar_init(&bars->q_full[s], 2);  // TMA bytes + the lse staging arrive
       mbar_init(&bars->q_empty[s], 1);
@@ -520,6 +541,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1) varlen_bwd_dkdv_kernel(const _
     mbar_init(&bars->p_read, kDsWarps);
     mbar_init(&bars->ds_done, kDsWarps);
     mbar_init(&bars->acc_full, 1);
+    mbar_init(&bars->acc_empty, kPWarps + kDsWarps);
     fence_barrier_init();
   }
   if (warp == 1) tmem_alloc(&bars->tmem_base, 512);
@@ -529,6 +551,15 @@ __global__ void __launch_bounds__(kBwdThreads, 1) varlen_bwd_dkdv_kernel(const _
   const uint32_t tbase = bars->tmem_base;
   const uint32_t t_s = tbase, t_x = tbase + 128, t_dv = tbase + 256, t_dk = tbase + 256 + HD;
 
+  // Tile k of this CTA from the ring (each consumer warp reads every slot once).
+  auto take_tile = [&](int k, bool& ok) {
+    ok = mbar_wait_warp(&bars->tile_full[k & 1], (k >> 1) & 1, kDevTimeoutFull);
+    const int tile = ok ? *reinterpret_cast<volatile int*>(&bars->tile[k & 1]) : -1;
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&bars->tile_empty[k & 1]);
+    return tile;
+  };
+
   if (warp == 0) {
     // Producer warp: lane 0 issues TMA; all lanes stage lse / delta.
     if (lane == 0) {
@@ -536,72 +567,97 @@ __global__ void __launch_bounds__(kBwdThreads, 1) varlen_bwd_dkdv_kernel(const _
       prefetch_tensormap(&kmap);
       prefetch_tensormap(&vmap);
       prefetch_tensormap(&dom);
-      mbar_arrive_expect_tx(&bars->fixed_full, 2 * C::TILE);
-      for (int cb = 0; cb < C::NCB; ++cb) {
-        tma_load_3d(ks + cb * C::BOX, &kmap, &bars->fixed_full, cb * 64, kvh, kv0);
-        tma_load_3d(vs + cb * C::BOX, &vmap, &bars->fixed_full, cb * 64, kvh, kv0);
-      }
     }
-    // lse / delta of the next item are loaded into registers one item ahead,
-    // so their global-memory latency never delays a TMA issue.
-    float lpre[4], dpre[4];
-    auto prefetch = [&](int t) {
-      const int hq = kvh * p.G + t / nqi;
-      const int q0 = (i_lo + t % nqi) * 128;
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const int q = q0 + lane + 32 * i;
-        lpre[i] = (q < p.L) ? p.lse[(size_t)hq * p.L + q] : INFINITY;
-        dpre[i] = (q < p.L) ? p.delta[(size_t)hq * p.L + q] : 0.f;
-      }
-    };
-    prefetch(0);
     bool ok = true;
-    for (int t = 0; t < n; ++t) {
-      const int qs = t % 3, dsl = t & 1;
-      const int hq = kvh * p.G + t / nqi;
-      const int q0 = (i_lo + t % nqi) * 128;
-      if (lane == 0) ok = ok && mbar_wait(&bars->q_empty[qs], ((t / 3) & 1) ^ 1, kDevTimeoutEmpty);
-      ok = __shfl_sync(0xffffffffu, ok, 0);
-      if (!ok) break;
+    int J = 0;  // items of earlier tiles: ring slots and phases continue across tiles
+    for (int k = 0; ok; ++k) {
+      int tile = -1;
       if (lane == 0) {
-        mbar_arrive_expect_tx(&bars->q_full[qs], C::TILE);
-        for (int cb = 0; cb < C::NCB; ++cb)
-          tma_load_3d(qring + qs * C::TILE + cb * C::BOX, &qmap, &bars->q_full[qs], cb * 64, hq, q0);
+        tile = k == 0 ? (int)blockIdx.x : (int)gridDim.x + atomicAdd(p.tile_counter + 1, 1);
+        if (tile >= n_tiles) tile = -1;
+        ok = mbar_wait(&bars->tile_empty[k & 1], ((k >> 1) & 1) ^ 1, kDevTimeoutEmpty);
+        if (ok) {
+          *reinterpret_cast<volatile int*>(&bars->tile[k & 1]) = tile;
+          mbar_arrive(&bars->tile_full[k & 1]);
+        }
       }
-#pragma unroll
-      for (int i = 0; i < 4; ++i) lse_ring[qs * 128 + lane + 32 * i] = lpre[i];
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&bars->q_full[qs]);
-      if (lane == 0) ok = mbar_wait(&bars->d_empty[dsl], ((t >> 1) & 1) ^ 1, kDevTimeoutEmpty);
+      tile = __shfl_sync(0xffffffffu, tile, 0);
       ok = __shfl_sync(0xffffffffu, ok, 0);
-      if (!ok) break;
+      if (!ok || tile < 0) break;
+      const DkdvTile d = dkdv_tile(tile, p);
       if (lane == 0) {
-        mbar_arrive_expect_tx(&bars->d_full[dsl], C::TILE);
-        for (int cb = 0; cb < C::NCB; ++cb)
-          tma_load_3d(dring + dsl * C::TILE + cb * C::BOX, &dom, &bars->d_full[dsl], cb * 64, hq, q0);
+        // K / V slots are free once the previous tile's last S^T and dP^T completed.
+        if (k > 0) ok = mbar_wait(&bars->fixed_empty, (k - 1) & 1, kDevTimeoutEmpty);
+        if (ok) {
+          mbar_arrive_expect_tx(&bars->fixed_full, 2 * C::TILE);
+          for (int cb = 0; cb < C::NCB; ++cb) {
+            tma_load_3d(ks + cb * C::BOX, &kmap, &bars->fixed_full, cb * 64, d.kvh, d.kv0);
+            tma_load_3d(vs + cb * C::BOX, &vmap, &bars->fixed_full, cb * 64, d.kvh, d.kv0);
+          }
+        }
       }
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      // lse / delta of the next item are loaded into registers one item ahead,
+      // so their global-memory latency never delays a TMA issue.
+      float lpre[4], dpre[4];
+      auto prefetch = [&](int t) {
+        const int hq = d.kvh * p.G + t / d.nqi;
+        const int q0 = (d.i_lo + t % d.nqi) * 128;
 #pragma unroll
-      for (int i = 0; i < 4; ++i) dlt_ring[dsl * 128 + lane + 32 * i] = dpre[i];
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&bars->d_full[dsl]);
-      if (t + 1 < n) prefetch(t + 1);
+        for (int i = 0; i < 4; ++i) {
+          const int q = q0 + lane + 32 * i;
+          lpre[i] = (q < p.L) ? p.lse[(size_t)hq * p.L + q] : INFINITY;
+          dpre[i] = (q < p.L) ? p.delta[(size_t)hq * p.L + q] : 0.f;
+        }
+      };
+      prefetch(0);
+      for (int t = 0; ok && t < d.n; ++t) {
+        const int tt = J + t;
+        const int qs = tt % 3, dsl = tt & 1;
+        const int hq = d.kvh * p.G + t / d.nqi;
+        const int q0 = (d.i_lo + t % d.nqi) * 128;
+        if (lane == 0) ok = mbar_wait(&bars->q_empty[qs], ((tt / 3) & 1) ^ 1, kDevTimeoutEmpty);
+        ok = __shfl_sync(0xffffffffu, ok, 0);
+        if (!ok) break;
+        if (lane == 0) {
+          mbar_arrive_expect_tx(&bars->q_full[qs], C::TILE);
+          for (int cb = 0; cb < C::NCB; ++cb)
+            tma_load_3d(qring + qs * C::TILE + cb * C::BOX, &qmap, &bars->q_full[qs], cb * 64, hq, q0);
+        }
+#pragma unroll
+        for (int i = 0; i < 4; ++i) lse_ring[qs * 128 + lane + 32 * i] = lpre[i];
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bars->q_full[qs]);
+        if (lane == 0) ok = mbar_wait(&bars->d_empty[dsl], ((tt >> 1) & 1) ^ 1, kDevTimeoutEmpty);
+        ok = __shfl_sync(0xffffffffu, ok, 0);
+        if (!ok) break;
+        if (lane == 0) {
+          mbar_arrive_expect_tx(&bars->d_full[dsl], C::TILE);
+          for (int cb = 0; cb < C::NCB; ++cb)
+            tma_load_3d(dring + dsl * C::TILE + cb * C::BOX, &dom, &bars->d_full[dsl], cb * 64, hq, q0);
+        }
+#pragma unroll
+        for (int i = 0; i < 4; ++i) dlt_ring[dsl * 128 + lane + 32 * i] = dpre[i];
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bars->d_full[dsl]);
+        if (t + 1 < d.n) prefetch(t + 1);
+      }
+      J += d.n;
     }
   } else if (warp == 1) {
     constexpr uint32_t ID_S = umma_idesc_bf16(128, 128, 0, 0);
     constexpr uint32_t ID_G = umma_idesc_bf16(128, HD, 0, 1);
-    bool ok = mbar_wait_warp(&bars->fixed_full, 0, kDevTimeoutFull);
     const uint32_t ka = smem_u32(ks), va = smem_u32(vs);
-    auto issue_s = [&](int t) {  // S^T(t) = K Q_t^T
-      const int qs = t % 3;
-      if (!mbar_wait_warp(&bars->q_full[qs], (t / 3) & 1, kDevTimeoutFull)) return false;
+    auto issue_s = [&](int tt) {  // S^T = K Q^T of running item tt
+      const int qs = tt % 3;
+      if (!mbar_wait_warp(&bars->q_full[qs], (tt / 3) & 1, kDevTimeoutFull)) return false;
       mma_kmajor_ss<HD>(t_s, ka, smem_u32(qring + qs * C::TILE), ID_S);
       umma_commit_warp(&bars->s_full);
       return true;
     };
-    auto issue_dp = [&](int t) {  // dP^T(t) = V dO_t^T
-      const int dsl = t & 1;
-      if (!mbar_wait_warp(&bars->d_full[dsl], (t >> 1) & 1, kDevTimeoutFull)) return false;
+    auto issue_dp = [&](int tt) {  // dP^T = V dO^T of running item tt
+      const int dsl = tt & 1;
+      if (!mbar_wait_warp(&bars->d_full[dsl], (tt >> 1) & 1, kDevTimeoutFull)) return false;
       mma_kmajor_ss<HD>(t_x, va, smem_u32(dring + dsl * C::TILE), ID_S);
       umma_commit_warp(&bars->dp_full);
       return true;
@@ -609,151 +665,181 @@ __global__ void __launch_bounds__(kBwdThreads, 1) varlen_bwd_dkdv_kernel(const _
     // One item: dV(t) once P^T is in TMEM, then S^T(t+1) over the P^T columns
     // dV has read, dK(t) once dS^T is in TMEM, then dP^T(t+1) over the dS^T
     // columns dK has read.
-    if (ok) ok = issue_s(0);
-    if (ok) ok = issue_dp(0);
-    for (int t = 0; ok && t < n; ++t) {
-      // dV += P^T dO, by halves as the P warps finish query quarters 0-1 and 2-3
-      if (!(ok = mbar_wait_warp(&bars->p_half, t & 1, kDevTimeoutFull))) break;
-      mma_tmem_a_half<HD>(t_dv, t_s, smem_u32(dring + (t & 1) * C::TILE), ID_G, t > 0, 0);
-      if (!(ok = mbar_wait_warp(&bars->p_done, t & 1, kDevTimeoutFull))) break;
-      mma_tmem_a_half<HD>(t_dv, t_s, smem_u32(dring + (t & 1) * C::TILE), ID_G, t > 0, 1);
-      // S^T(t+1) overwrites P^T(t): the dS warps must hold it first.
-      if (!(ok = mbar_wait_warp(&bars->p_read, t & 1, kDevTimeoutFull))) break;
-      if (t + 1 < n && !(ok = issue_s(t + 1))) break;
-      if (!(ok = mbar_wait_warp(&bars->ds_done, t & 1, kDevTimeoutFull))) break;
-      mma_tmem_a<HD>(t_dk, t_x, smem_u32(qring + (t % 3) * C::TILE), ID_G, t > 0);  // dK += dS^T Q
-      // Both slots (and their staged lse / delta, read until the dS^T phase
-      // ends) are free once dK(t) completes.
-      umma_commit_warp(&bars->q_empty[t % 3]);
-      umma_commit_warp(&bars->d_empty[t & 1]);
-      if (t + 1 < n) ok = issue_dp(t + 1);
+    bool ok = true;
+    int J = 0;
+    for (int k = 0; ok; ++k) {
+      const int tile = take_tile(k, ok);
+      if (!ok || tile < 0) break;
+      const int n = dkdv_tile(tile, p).n;
+      if (!(ok = mbar_wait_warp(&bars->fixed_full, k & 1, kDevTimeoutFull))) break;
+      if (!(ok = issue_s(J))) break;
+      if (!(ok = issue_dp(J))) break;
+      if (n == 1) umma_commit_warp(&bars->fixed_empty);  // K and V have no further reader
+      for (int t = 0; ok && t < n; ++t) {
+        const int tt = J + t;
+        // dV += P^T dO, by halves as the P warps finish query quarters 0-1 and 2-3
+        if (!(ok = mbar_wait_warp(&bars->p_half, tt & 1, kDevTimeoutFull))) break;
+        // The tile's first dV / dK overwrite the accumulators: the previous
+        // tile's epilogue must have read them.
+        if (t == 0 && k > 0 && !(ok = mbar_wait_warp(&bars->acc_empty, (k - 1) & 1, kDevTimeoutFull))) break;
+        mma_tmem_a_half<HD>(t_dv, t_s, smem_u32(dring + (tt & 1) * C::TILE), ID_G, t > 0, 0);
+        if (!(ok = mbar_wait_warp(&bars->p_done, tt & 1, kDevTimeoutFull))) break;
+        mma_tmem_a_half<HD>(t_dv, t_s, smem_u32(dring + (tt & 1) * C::TILE), ID_G, t > 0, 1);
+        // S^T(t+1) overwrites P^T(t): the dS warps must hold it first.
+        if (!(ok = mbar_wait_warp(&bars->p_read, tt & 1, kDevTimeoutFull))) break;
+        if (t + 1 < n && !(ok = issue_s(tt + 1))) break;
+        if (!(ok = mbar_wait_warp(&bars->ds_done, tt & 1, kDevTimeoutFull))) break;
+        mma_tmem_a<HD>(t_dk, t_x, smem_u32(qring + (tt % 3) * C::TILE), ID_G, t > 0);  // dK += dS^T Q
+        // Both slots (and their staged lse / delta, read until the dS^T phase
+        // ends) are free once dK(t) completes.
+        umma_commit_warp(&bars->q_empty[tt % 3]);
+        umma_commit_warp(&bars->d_empty[tt & 1]);
+        if (t + 1 < n) {
+          if (!(ok = issue_dp(tt + 1))) break;
+          if (t + 2 == n) umma_commit_warp(&bars->fixed_empty);  // the tile's last S^T and dP^T are queued
+        }
+      }
+      if (!ok) break;
+      umma_commit_warp(&bars->acc_full);
+      J += n;
     }
-    umma_commit_warp(&bars->acc_full);
   } else {
     const bool p_warp = warp < 2 + kPWarps;
     const int ch = (warp - (p_warp ? 2 : 2 + kPWarps)) >> 2;  // column half of every 128-column tile
     const int sub = warp & 3;                                   // TMEM lane quarter
     const int r = sub * 32 + lane;
-    const int k_tok = kv0 + r;
-    const bool k_ok = k_tok < p.L;
-    const int q_end = k_ok ? p.run_end[k_tok] : 0;  // queries k_tok <= q < q_end see this key
     const uint32_t lane_bits = (uint32_t)(sub * 32) << 16;
     bool ok = true;
-    if (p_warp) {
-      // P phase, per item: S^T -> P^T for query quarters ch and ch + 2, each
-      // packed to bf16 over the first 16 of its columns; quarters 0-1 are
-      // signalled first so the dV MMAs on them start while 2-3 are computed.
-      for (int t = 0; t < n; ++t) {
-        if (ok) ok = mbar_wait_warp(&bars->q_full[t % 3], (t / 3) & 1, kDevTimeoutFull);
-        if (ok) ok = mbar_wait_warp(&bars->s_full, t & 1, kDevTimeoutFull);
-        tc_fence_after();
-        if (ok) {
+    int J = 0;
+    for (int k = 0; ok; ++k) {
+      const int tile = take_tile(k, ok);
+      if (!ok || tile < 0) break;
+      const DkdvTile d = dkdv_tile(tile, p);
+      const int k_tok = d.kv0 + r;
+      const bool k_ok = k_tok < p.L;
+      const int q_end = k_ok ? p.run_end[k_tok] : 0;  // queries k_tok <= q < q_end see this key
+      if (p_warp) {
+        // P phase, per item: S^T -> P^T for query quarters ch and ch + 2, each
+        // packed to bf16 over the first 16 of its columns; quarters 0-1 are
+        // signalled first so the dV MMAs on them start while 2-3 are computed.
+        for (int t = 0; t < d.n; ++t) {
+          const int tt = J + t;
+          if (ok) ok = mbar_wait_warp(&bars->q_full[tt % 3], (tt / 3) & 1, kDevTimeoutFull);
+          if (ok) ok = mbar_wait_warp(&bars->s_full, tt & 1, kDevTimeoutFull);
+          tc_fence_after();
+          if (ok) {
 #pragma unroll 1
-          for (int h = 0; h < 2; ++h) {
-            const int cq = ch + 2 * h;
-            const uint32_t ts = t_s + lane_bits + 32 * cq;
-            const int qc0 = (i_lo + t % nqi) * 128 + 32 * cq;  // first query of these 32 columns
-            uint32_t sv[32];
-            tmem_ld32(ts, sv);
-            tmem_wait_ld();
-            const float4* l4 = reinterpret_cast<const float4*>(lse_ring + (t % 3) * 128 + 32 * cq);
-            float x[32];
+            for (int h = 0; h < 2; ++h) {
+              const int cq = ch + 2 * h;
+              const uint32_t ts = t_s + lane_bits + 32 * cq;
+              const int qc0 = (d.i_lo + t % d.nqi) * 128 + 32 * cq;  // first query of these 32 columns
+              uint32_t sv[32];
+              tmem_ld32(ts, sv);
+              tmem_wait_ld();
+              const float4* l4 = reinterpret_cast<const float4*>(lse_ring + (tt % 3) * 128 + 32 * cq);
+              float x[32];
 #pragma unroll
-            for (int c4 = 0; c4 < 8; ++c4) {
-              const float4 l = l4[c4];
-              x[4 * c4 + 0] = fmaf(__uint_as_float(sv[4 * c4 + 0]), p.scale_log2, -l.x);
-              x[4 * c4 + 1] = fmaf(__uint_as_float(sv[4 * c4 + 1]), p.scale_log2, -l.y);
-              x[4 * c4 + 2] = fmaf(__uint_as_float(sv[4 * c4 + 2]), p.scale_log2, -l.z);
-              x[4 * c4 + 3] = fmaf(__uint_as_float(sv[4 * c4 + 3]), p.scale_log2, -l.w);
-            }
+              for (int c4 = 0; c4 < 8; ++c4) {
+                const float4 l = l4[c4];
+                x[4 * c4 + 0] = fmaf(__uint_as_float(sv[4 * c4 + 0]), p.scale_log2, -l.x);
+                x[4 * c4 + 1] = fmaf(__uint_as_float(sv[4 * c4 + 1]), p.scale_log2, -l.y);
+                x[4 * c4 + 2] = fmaf(__uint_as_float(sv[4 * c4 + 2]), p.scale_log2, -l.z);
+                x[4 * c4 + 3] = fmaf(__uint_as_float(sv[4 * c4 + 3]), p.scale_log2, -l.w);
+              }
 #pragma unroll
-            for (int e = 0; e < 32; ++e) x[e] = e < 32 - kFmaExp ? fast_exp2(x[e]) : exp2_fma(x[e]);
-            if (!(k_ok && qc0 >= k_tok && qc0 + 31 < q_end)) {
+              for (int e = 0; e < 32; ++e) x[e] = e < 32 - kFmaExp ? fast_exp2(x[e]) : exp2_fma(x[e]);
+              if (!(k_ok && qc0 >= k_tok && qc0 + 31 < q_end)) {
 #pragma unroll
-              for (int e = 0; e < 32; ++e) {
-                const int q = qc0 + e;
-                if (q < k_tok || q >= q_end) x[e] = 0.f;
+                for (int e = 0; e < 32; ++e) {
+                  const int q = qc0 + e;
+                  if (q < k_tok || q >= q_end) x[e] = 0.f;
+                }
+              }
+              uint32_t pk[16];
+#pragma unroll
+              for (int e = 0; e < 16; ++e) pk[e] = pack_bf16x2(x[2 * e], x[2 * e + 1]);
+              tmem_st16(ts, pk);
+              if (h == 0) {
+                tmem_wait_st();
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&bars->p_half);
               }
             }
-            uint32_t pk[16];
-#pragma unroll
-            for (int e = 0; e < 16; ++e) pk[e] = pack_bf16x2(x[2 * e], x[2 * e + 1]);
-            tmem_st16(ts, pk);
-            if (h == 0) {
-              tmem_wait_st();
-              tc_fence_before();
-              __syncwarp();
-              if (lane == 0) mbar_arrive(&bars->p_half);
-            }
+            tmem_wait_st();
+          } else if (lane == 0) {
+            mbar_arrive(&bars->p_half);  // keep the phase count when a wait gave up
           }
-          tmem_wait_st();
-        } else if (lane == 0) {
-          mbar_arrive(&bars->p_half);  // keep the phase count when a wait gave up
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&bars->p_done);
         }
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&bars->p_done);
-      }
-    } else {
-      // dS phase, per item: read P^T back (then S^T(t+1) may overwrite it),
-      // dS^T = P^T o (dP^T - D), packed over the dP^T columns.
-      for (int t = 0; t < n; ++t) {
-        uint32_t pk[2][16];
-        if (ok) ok = mbar_wait_warp(&bars->p_done, t & 1, kDevTimeoutFull);
-        tc_fence_after();
-        if (ok) {
-          tmem_ld16(t_s + lane_bits + 64 * ch, pk[0]);
-          tmem_ld16(t_s + lane_bits + 64 * ch + 32, pk[1]);
-          tmem_wait_ld();
-        }
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&bars->p_read);
-        if (ok) ok = mbar_wait_warp(&bars->d_full[t & 1], (t >> 1) & 1, kDevTimeoutFull);
-        if (ok) ok = mbar_wait_warp(&bars->dp_full, t & 1, kDevTimeoutFull);
-        tc_fence_after();
-        if (ok) {
-#pragma unroll
-          for (int h = 0; h < 2; ++h) {
-            const int cq = 2 * ch + h;
-            const uint32_t tx = t_x + lane_bits + 32 * cq;
-            uint32_t dv[32];
-            tmem_ld32(tx, dv);
+      } else {
+        // dS phase, per item: read P^T back (then S^T(t+1) may overwrite it),
+        // dS^T = P^T o (dP^T - D), packed over the dP^T columns.
+        for (int t = 0; t < d.n; ++t) {
+          const int tt = J + t;
+          uint32_t pk[2][16];
+          if (ok) ok = mbar_wait_warp(&bars->p_done, tt & 1, kDevTimeoutFull);
+          tc_fence_after();
+          if (ok) {
+            tmem_ld16(t_s + lane_bits + 64 * ch, pk[0]);
+            tmem_ld16(t_s + lane_bits + 64 * ch + 32, pk[1]);
             tmem_wait_ld();
-            const float4* d4 = reinterpret_cast<const float4*>(dlt_ring + (t & 1) * 128 + 32 * cq);
-#pragma unroll
-            for (int e4 = 0; e4 < 8; ++e4) {
-              const float4 d = d4[e4];
-              const float2 p01 = unpack_bf16x2(pk[h][2 * e4]), p23 = unpack_bf16x2(pk[h][2 * e4 + 1]);
-              pk[h][2 * e4] = pack_bf16x2(p01.x * (__uint_as_float(dv[4 * e4]) - d.x),
-                                          p01.y * (__uint_as_float(dv[4 * e4 + 1]) - d.y));
-              pk[h][2 * e4 + 1] = pack_bf16x2(p23.x * (__uint_as_float(dv[4 * e4 + 2]) - d.z),
-                                              p23.y * (__uint_as_float(dv[4 * e4 + 3]) - d.w));
-            }
-            tmem_st16(tx, pk[h]);
           }
-          tmem_wait_st();
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&bars->p_read);
+          if (ok) ok = mbar_wait_warp(&bars->d_full[tt & 1], (tt >> 1) & 1, kDevTimeoutFull);
+          if (ok) ok = mbar_wait_warp(&bars->dp_full, tt & 1, kDevTimeoutFull);
+          tc_fence_after();
+          if (ok) {
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+              const int cq = 2 * ch + h;
+              const uint32_t tx = t_x + lane_bits + 32 * cq;
+              uint32_t dv[32];
+              tmem_ld32(tx, dv);
+              tmem_wait_ld();
+              const float4* d4 = reinterpret_cast<const float4*>(dlt_ring + (tt & 1) * 128 + 32 * cq);
+#pragma unroll
+              for (int e4 = 0; e4 < 8; ++e4) {
+                const float4 dd = d4[e4];
+                const float2 p01 = unpack_bf16x2(pk[h][2 * e4]), p23 = unpack_bf16x2(pk[h][2 * e4 + 1]);
+                pk[h][2 * e4] = pack_bf16x2(p01.x * (__uint_as_float(dv[4 * e4]) - dd.x),
+                                            p01.y * (__uint_as_float(dv[4 * e4 + 1]) - dd.y));
+                pk[h][2 * e4 + 1] = pack_bf16x2(p23.x * (__uint_as_float(dv[4 * e4 + 2]) - dd.z),
+                                                p23.y * (__uint_as_float(dv[4 * e4 + 3]) - dd.w));
+              }
+              tmem_st16(tx, pk[h]);
+            }
+            tmem_wait_st();
+          }
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&bars->ds_done);
         }
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&bars->ds_done);
       }
-    }
-    // Epilogue: the P warps write dV, the dS warps dK (scaled); each warp
-    // covers half of the HD columns of its 32 keys.
-    if (ok) ok = mbar_wait_warp(&bars->acc_full, 0, kDevTimeoutFull);
-    tc_fence_after();
-    if (ok) {
+      // Epilogue: the P warps write dV, the dS warps dK (scaled); each warp
+      // covers half of the HD columns of its 32 keys; the accumulators are
+      // released after the last chunk is read.
+      if (!(ok = ok && mbar_wait_warp(&bars->acc_full, k & 1, kDevTimeoutFull))) break;
+      tc_fence_after();
       const bool is_v = p_warp;
       const int col0 = ch * (HD / 2);
       const uint32_t src = (is_v ? t_dv : t_dk) + lane_bits + col0;
       const float mul = is_v ? 1.f : p.scale;
-      __nv_bfloat16* dst = (is_v ? p.dv : p.dk) + ((size_t)k_tok * p.Hkv + kvh) * HD + col0;
+      __nv_bfloat16* dst = (is_v ? p.dv : p.dk) + ((size_t)k_tok * p.Hkv + d.kvh) * HD + col0;
 #pragma unroll
       for (int c = 0; c < HD / 64; ++c) {
         uint32_t v[32];
         tmem_ld32(src + 32 * c, v);
         tmem_wait_ld();
+        if (c == HD / 64 - 1) {
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&bars->acc_empty);
+        }
         if (k_ok) {
           uint4* o4 = reinterpret_cast<uint4*>(dst + 32 * c);
 #pragma unroll
@@ -767,6 +853,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1) varlen_bwd_dkdv_kernel(const _
           }
         }
       }
+      J += d.n;
     }
   }
   tc_fence_before();
@@ -790,11 +877,12 @@ static cudaError_t launch_bwd_hd(const CUtensorMap& qm, const CUtensorMap& km, c
   if (e != cudaSuccess) return e;
   e = cudaFuncSetAttribute(varlen_bwd_dq_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_dq);
   if (e != cudaSuccess) return e;
-  varlen_bwd_dkdv_kernel<HD><<<dim3(n_t, p.Hkv), kBwdThreads, smem_kv, stream>>>(qm, km, vm, dom, p);
-  e = cudaGetLastError();
-  if (e != cudaSuccess) return e;
   int dev = 0, sms = 148;
   if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int kv_grid = std::max(1, std::min(n_t * p.Hkv, sms));  // persistent: one CTA per SM
+  varlen_bwd_dkdv_kernel<HD><<<kv_grid, kBwdThreads, smem_kv, stream>>>(qm, km, vm, dom, p);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
   const int dq_grid = std::max(1, std::min(n_t * p.Hq, sms));  // persistent: one CTA per SM
   varlen_bwd_dq_kernel<HD><<<dq_grid, kBwdThreads, smem_dq, stream>>>(qm, km, vm, dom, p);
   return cudaGetLastError();
