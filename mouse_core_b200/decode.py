@@ -266,15 +266,24 @@ class PagedDecodeSession:
             self._grow_pool(total)
         self.pages.allocate(add)
 
-        col = np.arange(S, dtype=np.int64)[None, :]
-        pad = (S - n)[:, None]
-        pos = self._len[:, None] + col - pad
-        q_pos = np.maximum(pos, 0)
-        real = col >= pad
-        rows = np.broadcast_to(np.arange(B)[:, None], (B, S))
-        slot = np.full((B, S), -1, dtype=np.int64)
-        if real.any():
-            slot[real] = self.pages.slots(rows[real], pos[real])
+        if S == 1:
+            # A decode step: one position per row, no [B, S] broadcasting.
+            pos = self._len - 1 + n
+            q_pos = np.maximum(pos, 0)
+            slot = np.full(B, -1, dtype=np.int64)
+            live = np.flatnonzero(n)
+            if live.size:
+                slot[live] = self.pages.slots(live, pos[live])
+        else:
+            col = np.arange(S, dtype=np.int64)[None, :]
+            pad = (S - n)[:, None]
+            pos = self._len[:, None] + col - pad
+            q_pos = np.maximum(pos, 0)
+            real = col >= pad
+            rows = np.broadcast_to(np.arange(B)[:, None], (B, S))
+            slot = np.full((B, S), -1, dtype=np.int64)
+            if real.any():
+                slot[real] = self.pages.slots(rows[real], pos[real])
 
         bt_changed = self.pages.dirty
         width = self.pages.max_pages
@@ -296,9 +305,10 @@ class PagedDecodeSession:
             self._graph = None  # its captured views point at the old buffer
         dev = self._meta_dev
         dev[:n_meta].copy_(buf[:n_meta], non_blocking=True)
-        ev = torch.cuda.Event()
+        ev = self._staging_ev[i]
+        if ev is None:
+            ev = self._staging_ev[i] = torch.cuda.Event()
         ev.record()
-        self._staging_ev[i] = ev
         q_pos_d = dev[:B * S].view(B, S)
         kv_len_d = dev[B * S:B * S + B]
         slot_d = dev[B * S + B:2 * B * S + B]
