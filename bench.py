@@ -401,6 +401,186 @@ def run_ours(args):
     return out
 
 
+# Large-batch decode (the 8-GPU slice of a 4096-env workload): Llama-3.2-1B
+# architecture (16 layers, hidden 2048, 32/8 heads, hd 64, intermediate 8192,
+# RoPE theta 5e5 with rope_type "default"), 512 envs per GPU with context
+# lengths log-uniform in [128, 16384], 64-token pages, and 2% of envs retiring
+# every step and restarting from an empty context.
+LB = {"hidden": 2048, "layers": 16, "heads": 32, "kv_heads": 8, "head_dim": 64, "inter": 8192, "theta": 5e5,
+      "envs": 512, "page": 64, "len": (128, 16384), "retire": 0.02}
+
+
+def large_batch_config(n_gpus, envs):
+    return {"workload": f"large-batch cached decode, Llama-3.2-1B arch (16 layers, hd 64), {envs} envs/GPU "
+                        "(the 8-GPU slice of 4096 envs), context lengths log-uniform [128,16384], 64-token pages, "
+                        "2% of envs retire and restart each step",
+            "envs_per_gpu": envs, "global_envs": envs * n_gpus, "layers": LB["layers"], "hidden": LB["hidden"],
+            "q_heads": LB["heads"], "kv_heads": LB["kv_heads"], "head_dim": LB["head_dim"], "page_size": LB["page"],
+            "parallelism": f"env-sharded x{n_gpus} (no collective)",
+            "l2": "inputs larger than L2: each step reads ~54 GB of KV per GPU"}
+
+
+def run_large_batch(args):
+    import torch
+    import torch.distributed as dist
+    import torch.nn.functional as F
+
+    from mouse_core_b200 import _lib
+    from mouse_core_b200 import kernels as K
+    from mouse_core_b200.backbone import LlamaBackbone
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
+    envs = args.lb_envs
+    D, hd, Hkv, Hq, P = LB["hidden"], LB["head_dim"], LB["kv_heads"], LB["heads"], LB["page"]
+    torch.manual_seed(0)
+    bb = LlamaBackbone(hidden_dim=D, num_layers=LB["layers"], num_heads=Hq, num_key_value_heads=Hkv,
+                       intermediate_size=LB["inter"], max_position_embeddings=32768,
+                       rope_parameters={"rope_type": "default", "rope_theta": LB["theta"]})
+    bb = bb.to(device=dev, dtype=torch.bfloat16).eval()
+    g = torch.Generator().manual_seed(2)
+    table = torch.randn(VOCAB, D, generator=g).to(device=dev, dtype=torch.bfloat16)
+    w1 = (torch.randn(2 * D, D, generator=g) / D ** 0.5).to(dev)
+    w2 = (torch.randn(4, D, generator=g) / D ** 0.5).to(dev)
+
+    def head(h):  # fp32 DiscreteActionValueHead (RMSNorm -> SwiGLU -> Linear)
+        a, b = F.linear(F.rms_norm(h.float(), (D,), None, 1e-5), w1).chunk(2, dim=-1)
+        return F.linear(F.silu(a) * b, w2)
+
+    rng = np.random.default_rng(3000 + rank)
+    lo, hi = LB["len"]
+    lengths = np.exp(rng.uniform(np.log(lo), np.log(hi), size=envs)).astype(np.int64)
+    W, K_steps = args.warmup, args.steps
+    n_step_calls = 2 * W + 3 * K_steps  # alternating device / e2e steps, then the roofline pass
+    # Exactly the pages the contexts and every timed step can need (the pool
+    # never grows): each row's longest possible length plus one page of slack.
+    pages = int(((lengths + n_step_calls + P - 1) // P + 1).sum())
+    sess = bb.decode_session(batch_size=envs, capacity=P, page_size=P, num_pages=pages)
+    ctx_ids = [transition_ids(rng, rng.integers(0, 4, size=L), L) for L in lengths]
+    prefill(sess, table, ctx_ids, lengths)
+    torch.cuda.synchronize()
+    retire = rng.random((n_step_calls, envs)) < LB["retire"]
+    ids_dev = torch.from_numpy(np.stack([transition_ids(rng, rng.integers(0, 4, size=envs), envs)
+                                         for _ in range(n_step_calls)])).to(dev)
+    ones = [1] * envs
+    call = [0]
+
+    def device_step():
+        i = call[0]
+        call[0] += 1
+        gone = np.flatnonzero(retire[i])
+        if gone.size:
+            sess.reset_rows(gone)
+        h = sess.forward(embeds=table[ids_dev[i].long()].view(envs, 1, D), lengths=ones)
+        return head(h[:, -1]).argmax(-1)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    # Retirements shrink the cached contexts step after step, so the
+    # device-resident and end-to-end figures alternate step by step over the
+    # same stretch of the trajectory (each step timed with its own events);
+    # the roofline pass of K1 launches follows.
+    h_ids = torch.empty(envs, dtype=torch.int32, pin_memory=True)
+    h_act = torch.empty(envs, dtype=torch.int64, pin_memory=True)
+    d_ids = torch.empty(envs, dtype=torch.int32, device=dev)
+    act = rng.integers(0, 4, size=envs)
+
+    def e2e_step():  # through the public API: ids from pinned host memory, actions read back
+        nonlocal act
+        i = call[0]
+        call[0] += 1
+        gone = np.flatnonzero(retire[i])
+        if gone.size:
+            sess.reset_rows(gone)
+        h_ids.numpy()[:] = transition_ids(rng, act, envs)
+        d_ids.copy_(h_ids, non_blocking=True)
+        h = sess.forward(embeds=table[d_ids.long()].view(envs, 1, D), lengths=ones)
+        h_act.copy_(head(h[:, -1]).argmax(-1), non_blocking=True)
+        torch.cuda.current_stream().synchronize()
+        act = h_act.numpy().copy()
+
+    for _ in range(W):
+        device_step()
+        e2e_step()
+    torch.cuda.synchronize()
+    barrier()
+    torch.cuda.synchronize()
+    clocks = Clocks(local)
+    launches = 0
+    dev_ev, e2e_ev = [], []
+    for _ in range(K_steps):
+        d0, d1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        n0 = K.launch_count[0]
+        d0.record()
+        device_step()
+        d1.record()
+        launches += K.launch_count[0] - n0  # the device-resident steps' own launches
+        dev_ev.append((d0, d1))
+        f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        f0.record()
+        e2e_step()
+        f1.record()
+        e2e_ev.append((f0, f1))
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    ms = sum(x.elapsed_time(y) for x, y in dev_ev)
+    e2e_ms = sum(x.elapsed_time(y) for x, y in e2e_ev)
+    sess.attn_events = []
+    kv_sum = 0
+    for _ in range(K_steps):
+        kv_sum += int(sess._len.sum()) + envs
+        device_step()
+    torch.cuda.synchronize()
+    attn_ms = [a.elapsed_time(b) for a, b in sess.attn_events]
+    sess.attn_events = None
+    t = torch.tensor([ms, e2e_ms], device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_max, e2e_max = (float(x) for x in t.tolist())
+    status = _lib.device_status()
+    attn_bytes = kv_sum / K_steps * 2 * Hkv * hd * 2 + 2 * envs * Hq * hd * 2
+    attn_avg_ms = statistics.mean(attn_ms) if attn_ms else float("nan")
+    achieved = attn_bytes / (attn_avg_ms * 1e-3) / 1e9
+    peaks = {}
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            peaks = json.load(f)
+    except (OSError, ValueError):
+        pass
+    peak = float(peaks.get("hbm_gbs", 6650.0))
+    out = None
+    if rank == 0:
+        out = {"metric": "env-steps/s in large-batch cached decode", "unit": "env-steps/s",
+               "value": round(envs * world * K_steps / (ms_max * 1e-3), 1), "n_gpus": world, "steps": K_steps,
+               "warmup": W, "ms_per_step": round(ms_max / K_steps, 4), "higher_is_better": True, "scaling": "weak",
+               "vs_baseline": None, "dtype": "bf16",
+               "data": "synthetic (seeded transition tokens; random-init weights)",
+               "config": large_batch_config(world, envs),
+               "e2e": {"value": round(envs * world * K_steps / (e2e_max * 1e-3), 1), "unit": "env-steps/s",
+                       "h2d_bytes_per_step": int(envs * 4 * world), "d2h_bytes_per_step": int(envs * 8 * world),
+                       "ms_per_step": round(e2e_max / K_steps, 4)},
+               "roofline": {"kernel": "split_decode_kernel (K1), hd 64", "bound": "hbm", "achieved": round(achieved, 1),
+                            "peak": peak, "peak_source": "measured" if "hbm_gbs" in peaks else "fallback",
+                            "unit": "GB/s", "frac": round(achieved / peak, 4), "traffic": None,
+                            "algorithmic_bytes_per_launch": int(attn_bytes), "avg_launch_ms": round(attn_avg_ms, 5),
+                            "launches_timed": len(attn_ms)},
+               "kv_pool_gb": round(pages * LB["layers"] * 2 * Hkv * P * hd * 2 / 1e9, 1),
+               "gpu_launches": int(launches), "clocks": clk, "device_status": status}
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return out
+
+
 def packed_segments(seed, rows=8, row_len=16384, lo=256, hi=4096):
     """Segment lengths of the packed-training workload: per row, lengths
     U[lo, hi] until the row is full, the last one truncated."""
@@ -778,11 +958,16 @@ def main():
                     "smaller values only for profiling captures)")
     ap.add_argument("--train", action="store_true", help="time the packed DQN training step instead of decode")
     ap.add_argument("--train-rows", type=int, default=TRAIN_ROWS, help="16384-token rows per training step")
+    ap.add_argument("--large-batch", action="store_true",
+                    help="time large-batch decode (Llama-3.2-1B arch, 512 envs/GPU, hd 64) instead")
+    ap.add_argument("--lb-envs", type=int, default=LB["envs"], help="envs per GPU for --large-batch")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
     globals()["ENVS"] = args.envs
-    if args.train and args.impl == "ours":
+    if args.large_batch and args.impl == "ours":
+        out = run_large_batch(args)
+    elif args.train and args.impl == "ours":
         out = run_train(args)
     elif args.packed_only:
         import torch
