@@ -808,7 +808,7 @@ def run_train(args):
     out = None
     if rank == 0:
         tokens = rows_total * TRAIN_ROW_LEN
-        achieved = flops * K_steps / (ms_max * 1e-3) / 1e12
+        achieved = flops * K_steps / (ms_max * 1e-3) / 1e12 / world  # per GPU, against one GPU's peak
         out = {"metric": "tokens/s in packed DQN training (fwd+bwd+AdamW)",
                "value": round(tokens * K_steps / (ms_max * 1e-3), 1), "unit": "tokens/s", "n_gpus": world,
                "steps": K_steps, "warmup": W, "ms_per_step": round(ms_max / K_steps, 3), "higher_is_better": True,
@@ -822,7 +822,8 @@ def run_train(args):
                             "achieved": round(achieved, 1), "peak": peak,
                             "peak_source": "measured (sustained)" if "bf16_tflops_sustained" in peaks else "fallback",
                             "unit": "TFLOP/s", "frac": round(achieved / peak, 4), "traffic": None,
-                            "flops_note": "6 * 440.4M params * tokens + 3.5 x algorithmic attention forward"},
+                            "flops_note": "per GPU: (6 * 440.4M params * tokens + 3.5 x algorithmic attention "
+                                          "forward) / n_gpus"},
                "attention_fwd_flops_per_step": attn_fwd, "loss": float(loss.item()),
                "gpu_launches": int(launches), "clocks": clk, "device_status": status}
     if world > 1:
