@@ -133,6 +133,20 @@ int mb_page_copy(const void* src_pool, void* dst_pool, const int32_t* src_pages,
                  long long page_elems, mb_stream_t stream);
 
 /* ---------------------------------------------------------------------
+ * One decode step's metadata on the device (every row appends one token).
+ * Replaces the host-side position and slot bookkeeping of
+ * FlexDecodeSession.forward (models/backbone/flex_decode.py:180-195) for the
+ * one-token-per-row step: reads each row's current length from kv_len
+ * [batch] (left there by the previous step), writes q_pos = length, the new
+ * token's cache slot (page * page_size + offset, looked up in block_table
+ * [batch, max_pages]) and kv_len = length + 1. new_page [batch] (or NULL)
+ * holds the id of a page a row's token opens (else -1); it is written into
+ * the block table first. All int32, device memory.
+ * ------------------------------------------------------------------- */
+int mb_decode_step_meta(int batch, int max_pages, int page_size, const int32_t* new_page, int32_t* block_table,
+                        int32_t* q_pos, int32_t* kv_len, int32_t* slot, mb_stream_t stream);
+
+/* ---------------------------------------------------------------------
  * Decoder-layer glue.
  * mb_rmsnorm: sum_out = x + residual (bf16), norm_out = RMSNorm(sum) * w;
  *   with residual == NULL it normalises x (sum_out unused). Replaces the

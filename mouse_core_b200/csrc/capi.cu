@@ -236,6 +236,17 @@ int mb_page_copy(const void* src_pool, void* dst_pool, const int32_t* src_pages,
   return e == cudaSuccess ? MB_OK : cuda_fail(e, "page copy launch");
 }
 
+int mb_decode_step_meta(int batch, int max_pages, int page_size, const int32_t* new_page, int32_t* block_table,
+                        int32_t* q_pos, int32_t* kv_len, int32_t* slot, mb_stream_t stream) {
+  if (batch < 0 || max_pages <= 0 || page_size <= 0)
+    return fail(MB_ERR_INVALID_ARG, "batch >= 0, max_pages > 0 and page_size > 0 required");
+  if (batch == 0) return MB_OK;
+  if (!block_table || !q_pos || !kv_len || !slot) return fail(MB_ERR_INVALID_ARG, "a required pointer is NULL");
+  cudaError_t e = mb::launch_decode_step_meta(batch, max_pages, page_size, new_page, block_table, q_pos, kv_len, slot,
+                                              (cudaStream_t)stream);
+  return e == cudaSuccess ? MB_OK : cuda_fail(e, "decode step meta launch");
+}
+
 int mb_rmsnorm(const void* x, const void* residual, const void* weight, float eps, int rows, int dim, void* sum_out,
                void* norm_out, mb_stream_t stream) {
   if (rows < 0 || dim <= 0 || dim % 2) return fail(MB_ERR_INVALID_ARG, "rows >= 0 and an even dim > 0 required");

@@ -122,6 +122,9 @@ cudaError_t launch_qkv_heads_bwd(const __nv_bfloat16* dq, const __nv_bfloat16* d
 cudaError_t launch_silu_mul_bwd(const __nv_bfloat16* gu, const __nv_bfloat16* dh, int rows, int I,
                                 __nv_bfloat16* dgu, cudaStream_t stream);
 
+cudaError_t launch_decode_step_meta(int B, int width, int page_size, const int32_t* new_page, int32_t* block_table,
+                                    int32_t* q_pos, int32_t* kv_len, int32_t* slot, cudaStream_t stream);
+
 cudaError_t launch_segment_meta(const int64_t* seq, int L, int tile, int64_t* pos_out, int32_t* run_start,
                                 int32_t* run_end, int32_t* tile_lo, int32_t* flags, cudaStream_t stream);
 

@@ -123,4 +123,40 @@ cudaError_t launch_page_copy(const __nv_bfloat16* src_pool, __nv_bfloat16* dst_p
   return cudaGetLastError();
 }
 
+// One decode step's metadata on the device (every row appends one token):
+// the current length L = kv_len[b] (left there by the previous step), the
+// new token's position L, its cache slot from the block table, and the new
+// length L + 1. A row whose token opens a page gets that page's id in
+// new_page[b] (else -1), which is written into the block table first. A
+// column past the table's width is reported (kDevBadPage) and the token is
+// not cached (slot -1).
+__global__ void decode_step_meta_kernel(int B, int width, int page_size, const int32_t* __restrict__ new_page,
+                                        int32_t* __restrict__ block_table, int32_t* __restrict__ q_pos,
+                                        int32_t* __restrict__ kv_len, int32_t* __restrict__ slot) {
+  const int b = blockIdx.x * blockDim.x + threadIdx.x;
+  if (b >= B) return;
+  const int L = kv_len[b];
+  const int col = L / page_size;
+  int s = -1;
+  if (L < 0 || col >= width) {
+    report(kDevBadPage);
+  } else {
+    int32_t* entry = block_table + (size_t)b * width + col;
+    const int np = new_page ? new_page[b] : -1;
+    if (np >= 0) *entry = np;
+    s = (np >= 0 ? np : *entry) * page_size + L % page_size;
+  }
+  q_pos[b] = L;
+  slot[b] = s;
+  kv_len[b] = L + 1;
+}
+
+cudaError_t launch_decode_step_meta(int B, int width, int page_size, const int32_t* new_page, int32_t* block_table,
+                                    int32_t* q_pos, int32_t* kv_len, int32_t* slot, cudaStream_t stream) {
+  if (B <= 0) return cudaSuccess;
+  decode_step_meta_kernel<<<(B + 127) / 128, 128, 0, stream>>>(B, width, page_size, new_page, block_table, q_pos,
+                                                               kv_len, slot);
+  return cudaGetLastError();
+}
+
 }  // namespace mb

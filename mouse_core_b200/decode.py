@@ -142,6 +142,14 @@ class PagedDecodeSession:
         # Single-token steps (S = 1, the steady state of env stepping) replay a
         # CUDA graph of the whole layer stack after one eager warm-up call.
         self.use_graphs = True
+        # One-token steps between replays: positions, slots and lengths are
+        # made on the device from the previous step's lengths (K8,
+        # mb_decode_step_meta), fed only with the pages the step opens; the
+        # host keeps its page table and lengths in step with it.
+        self.use_device_step = True
+        self._device_step_ok = False  # device metadata is the one-token layout of the host's state
+        self._new_page_dev = torch.full((self.B,), -1, dtype=torch.int32, device=self.device)
+        self._step_args: tuple | None = None  # pointers of the captured graph's metadata views
         self._graph = None
         self._graph_key = None
         self._graph_warm = False
@@ -173,6 +181,7 @@ class PagedDecodeSession:
     def reset_rows(self, rows) -> None:
         """Empty ``rows`` (their pages return to the pool); the next call
         decodes them from position 0, as a fresh session would."""
+        self._device_step_ok = False
         self.pages.release_rows(rows)
         self._len[np.atleast_1d(np.asarray(rows, dtype=np.int64))] = 0
 
@@ -190,6 +199,7 @@ class PagedDecodeSession:
         dst = np.atleast_1d(np.asarray(dst_rows, dtype=np.int64))
         if src.shape != dst.shape:
             raise ValueError("src_rows and dst_rows must have the same length")
+        self._device_step_ok = False
         plen = self._len[src].copy() if prefix_lengths is None else np.atleast_1d(
             np.asarray(prefix_lengths, dtype=np.int64))
         if plen.shape != src.shape or (plen < 0).any() or (plen > self._len[src]).any():
@@ -225,6 +235,7 @@ class PagedDecodeSession:
 
     # ------------------------------------------------------------------ pool
     def _grow_pool(self, need_free: int) -> None:
+        self._device_step_ok = False
         old = self.pages.num_pages
         new = max(2 * old, old + need_free - self.pages.free_pages)
         shape = (self.n_layers, new, self.n_kv_heads, self.page_size, self.head_dim)
@@ -318,7 +329,46 @@ class PagedDecodeSession:
             self._bt_dev.copy_(dev[2 * B * S + B:n_meta].view(B, width))
             self.pages.dirty = False
         self._len = new_len
+        self._device_step_ok = S == 1
         return q_pos_d, kv_len_d, slot_d, int(new_len.max()) if B else 0
+
+    def _device_step(self, lengths) -> bool:
+        """A one-token step whose metadata the device makes (K8): the host
+        only opens the pages this step's tokens start and uploads their ids.
+        False (nothing changed) when the host path must run instead: not every
+        row appends one token, the device metadata is stale, or the new pages
+        would not fit the pool or the block table's width."""
+        B, P, pages = self.B, self.page_size, self.pages
+        if not self._device_step_ok or pages.dirty:
+            return False
+        if isinstance(lengths, list):
+            if len(lengths) != B or lengths.count(1) != B:
+                return False
+        else:
+            n = np.asarray(lengths).reshape(-1)
+            if n.shape[0] != B or not bool((n == 1).all()):
+                return False
+        opening = np.flatnonzero(pages.npages * P <= self._len)
+        if opening.size:
+            if opening.size > pages.free_pages or int(pages.npages[opening].max()) >= pages.max_pages:
+                return False
+            ids = pages.open_pages(opening)
+            buf, i = self._stage(B)
+            host = buf.numpy()[:B]
+            host.fill(-1)
+            host[opening] = ids
+            self._new_page_dev.copy_(buf[:B], non_blocking=True)
+            ev = self._staging_ev[i]
+            if ev is None:
+                ev = self._staging_ev[i] = torch.cuda.Event()
+            ev.record()
+        if self._step_args is None:
+            dev = self._meta_dev
+            self._step_args = K.decode_step_meta_args(self._bt_dev, dev[:B], dev[B:2 * B], dev[2 * B:3 * B], P,
+                                                      self._new_page_dev)
+        K.decode_step_meta_launch(self._step_args, opening.size > 0, torch.cuda.current_stream().cuda_stream)
+        self._len = self._len + 1
+        return True
 
     @torch.no_grad()
     def forward(self, *, embeds: torch.Tensor, lengths, output_hidden_states: bool = False):
@@ -330,6 +380,18 @@ class PagedDecodeSession:
         if B != self.B:
             raise ValueError(f"Session was created for batch_size={self.B}, got {B}.")
         x = embeds.to(self.device, self.dtype).reshape(B * S, D).contiguous()
+        if (S == 1 and B > 0 and self.use_graphs and self.use_device_step and self._graph is not None
+                and not output_hidden_states and self.attn_events is None
+                and not torch.cuda.is_current_stream_capturing()):
+            for lw in self._layers:
+                lw.refresh()
+            key = (self.k_pool.data_ptr(), self._bt_dev.data_ptr(), self._meta_dev.data_ptr(), self.cap,
+                   tuple(lw.version for lw in self._layers))
+            if key == self._graph_key and self._device_step(lengths):
+                self._graph_x.copy_(x)
+                self._graph.replay()
+                K._count(self._graph_launches)
+                return self.model.norm(self._graph_out.view(B, S, D).clone())
         q_pos, kv_len, slot, max_kv = self.prepare(lengths, S)
         if B == 0 or S == 0:
             h = x.view(B, S, D)
@@ -361,6 +423,7 @@ class PagedDecodeSession:
             self._graph_launches = K.launch_count[0] - n0
             K.launch_count[0] = n0
             self._graph, self._graph_key = graph, key
+            self._step_args = None
         else:
             self._graph_x.copy_(x)
         self._graph.replay()

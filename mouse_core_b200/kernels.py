@@ -147,6 +147,45 @@ def page_copy(src_pool: torch.Tensor, dst_pool: torch.Tensor, src_pages: torch.T
     _count()
 
 
+def decode_step_meta(block_table: torch.Tensor, q_pos: torch.Tensor, kv_len: torch.Tensor, slot: torch.Tensor,
+                     page_size: int, new_page: torch.Tensor | None = None) -> None:
+    """In place: one decode step's ``q_pos``, ``slot`` and ``kv_len`` (int32
+    ``[B]``) from the current ``kv_len`` and ``block_table [B, max_pages]``,
+    after writing ``new_page[b] >= 0`` (pages the step's tokens open) into
+    the table."""
+    for name, t in (("block_table", block_table), ("q_pos", q_pos), ("kv_len", kv_len), ("slot", slot)):
+        _need(t, name, torch.int32)
+    if new_page is not None:
+        _need(new_page, "new_page", torch.int32)
+    B, width = block_table.shape
+    _lib.call("mb_decode_step_meta", B, width, int(page_size), _p(new_page), _p(block_table), _p(q_pos),
+              _p(kv_len), _p(slot), _stream(kv_len))
+    _count()
+
+
+def decode_step_meta_args(block_table: torch.Tensor, q_pos: torch.Tensor, kv_len: torch.Tensor, slot: torch.Tensor,
+                          page_size: int, new_page: torch.Tensor) -> tuple:
+    """Checked argument tuple of ``decode_step_meta`` for tensors that stay in
+    place across many steps; launch it with ``decode_step_meta_launch``."""
+    for name, t in (("block_table", block_table), ("q_pos", q_pos), ("kv_len", kv_len), ("slot", slot),
+                    ("new_page", new_page)):
+        _need(t, name, torch.int32)
+    B, width = block_table.shape
+    if not (q_pos.numel() == kv_len.numel() == slot.numel() == new_page.numel() == B):
+        raise ValueError("q_pos, kv_len, slot and new_page must have one entry per block-table row")
+    return (B, width, int(page_size), new_page.data_ptr(), block_table.data_ptr(), q_pos.data_ptr(),
+            kv_len.data_ptr(), slot.data_ptr())
+
+
+def decode_step_meta_launch(args: tuple, use_new_page: bool, stream: int) -> None:
+    """``decode_step_meta`` from a ``decode_step_meta_args`` tuple; ``new_page``
+    is read only when ``use_new_page``."""
+    B, width, page_size, new_page, bt, q_pos, kv_len, slot = args
+    _lib.call("mb_decode_step_meta", B, width, page_size, new_page if use_new_page else None, bt, q_pos, kv_len,
+              slot, stream)
+    _count()
+
+
 def rmsnorm(x: torch.Tensor, weight: torch.Tensor, eps: float, residual: torch.Tensor | None = None):
     """Returns ``(sum, norm)``: ``sum = x + residual`` (or ``x``), ``norm = RMSNorm(sum) * weight``."""
     _need(x, "x", BF16)

@@ -46,11 +46,12 @@ class PageTable:
         if new_num_pages <= self.num_pages:
             return
         extra = np.arange(new_num_pages - 1, self.num_pages - 1, -1, dtype=np.int32)
-        free = np.empty(self._nfree + extra.shape[0], dtype=np.int32)
+        # The stack holds every page id: pages in use now come back later.
+        free = np.empty(new_num_pages, dtype=np.int32)
         free[: extra.shape[0]] = extra
-        free[extra.shape[0]:] = self._free[: self._nfree]
+        free[extra.shape[0]: extra.shape[0] + self._nfree] = self._free[: self._nfree]
         self._free = free
-        self._nfree = free.shape[0]
+        self._nfree += extra.shape[0]
         rc = np.zeros(new_num_pages, dtype=np.int32)
         rc[: self.num_pages] = self.refcount
         self.refcount = rc
@@ -87,6 +88,21 @@ class PageTable:
         self.refcount[ids] += 1
         self.npages += add
         self.dirty = True
+
+    def open_pages(self, rows: np.ndarray) -> np.ndarray:
+        """Append one fresh page to each of ``rows`` (distinct, ascending; the
+        table must have a free column for each) and return the ids: the same
+        ids ``allocate`` hands out for one page per row. ``dirty`` is left
+        as it is: the caller writes the new entries into the device table."""
+        k = int(rows.shape[0])
+        if k > self._nfree:
+            raise RuntimeError(f"page pool exhausted: need {k} pages, {self._nfree} free")
+        ids = self._free[self._nfree - k: self._nfree][::-1].copy()
+        self._nfree -= k
+        self.table[rows, self.npages[rows]] = ids
+        self.refcount[ids] += 1
+        self.npages[rows] += 1
+        return ids
 
     def release_rows(self, rows) -> None:
         """Drop every page reference of ``rows`` (pages whose refcount reaches

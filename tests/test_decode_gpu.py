@@ -389,3 +389,56 @@ def test_fork_shares_prefix_pages_and_matches_independent_rows():
     # Releasing the branches returns their private pages; shared pages stay with the roots.
     shared.reset_rows(dst)
     assert shared.pages.npages[:R].tolist() == [int(np.ceil((L + 5) / page)) for L in root_len]
+
+
+def test_device_step_matches_host_step():
+    """One-token steps whose positions, slots and lengths the device derives
+    (K8) equal the host-prepared steps bit for bit, across page openings, a
+    pool growth, a block-table widening, row resets, a fork and multi-token
+    chunks in between; the page tables stay identical on host and device."""
+    dev = _dev()
+    from mouse_core_b200.backbone import Qwen3Backbone
+
+    torch.manual_seed(11)
+    bb = Qwen3Backbone(hidden_dim=256, num_layers=2, num_heads=4, num_key_value_heads=2, head_dim=128)
+    bb = bb.to(device=dev, dtype=torch.bfloat16).eval()
+    B, page = 6, 64
+    fast = bb.decode_session(batch_size=B, capacity=64, page_size=page, num_pages=8)
+    host = bb.decode_session(batch_size=B, capacity=64, page_size=page, num_pages=8)
+    host.use_device_step = False
+    taken = [0]
+    inner = fast._device_step
+
+    def counted(n):
+        ok = inner(n)
+        taken[0] += ok
+        return ok
+
+    fast._device_step = counted
+    g = torch.Generator().manual_seed(5)
+    rng = np.random.default_rng(2)
+
+    def both(S, lens):
+        x = torch.randn(B, S, 256, generator=g).bfloat16().to(dev)
+        a = fast.forward(embeds=x, lengths=lens)
+        b = host.forward(embeds=x, lengths=lens)
+        assert torch.equal(a, b), (S, lens)
+        assert fast._len.tolist() == host._len.tolist()
+        assert np.array_equal(fast.pages.table, host.pages.table)
+        w = fast.pages.max_pages
+        assert np.array_equal(fast._bt_dev[:, :w].cpu().numpy(), fast.pages.table)
+
+    both(60, rng.integers(1, 61, size=B).tolist())
+    for step in range(160):
+        if step == 30:
+            fast.reset_rows([1, 3])
+            host.reset_rows([1, 3])
+            both(9, [0, 9, 0, 4, 0, 0])
+        elif step == 60:
+            fast.fork([0, 2], [4, 5], [17, 64])
+            host.fork([0, 2], [4, 5], [17, 64])
+        elif step == 100:
+            both(1, [1, 0, 1, 1, 0, 1])  # a row sitting out goes through the host path
+        both(1, [1] * B)
+    assert taken[0] >= 140, taken[0]
+    assert fast.pages.num_pages > 8 and fast.pages.max_pages > 2  # grew and widened on the way

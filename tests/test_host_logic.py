@@ -95,6 +95,36 @@ def test_page_table_allocate_release_share():
         raise AssertionError("allocation beyond the pool must raise")
 
 
+def test_page_table_release_after_growth_with_pages_in_use():
+    """Pages held across a pool growth return to the free list when their
+    rows are released, and every page id is handed out exactly once."""
+    pt = PageTable(batch_size=3, num_pages=4, page_size=64, max_pages=1)
+    pt.allocate(np.array([2, 2, 0]))
+    pt.grow_pool(8)
+    pt.allocate(np.array([0, 0, 3]))
+    pt.grow_pool(20)
+    pt.release_rows([0, 1, 2])
+    assert pt.free_pages == 20
+    pt.allocate(np.array([7, 6, 7]))
+    assert sorted(pt.table[pt.table >= 0].tolist()) == list(range(20))
+
+
+def test_open_pages_hands_out_what_allocate_does():
+    a = PageTable(batch_size=5, num_pages=16, page_size=64, max_pages=4)
+    b = PageTable(batch_size=5, num_pages=16, page_size=64, max_pages=4)
+    for pt in (a, b):
+        pt.allocate(np.array([1, 0, 2, 1, 0]))
+        pt.release_rows([3])
+    rows = np.array([0, 1, 3, 4])
+    b.dirty = False
+    ids = b.open_pages(rows)
+    a.allocate(np.isin(np.arange(5), rows).astype(np.int64))
+    assert np.array_equal(a.table, b.table) and np.array_equal(a.npages, b.npages)
+    assert np.array_equal(a.refcount, b.refcount) and a.free_pages == b.free_pages
+    assert ids.tolist() == b.table[rows, b.npages[rows] - 1].tolist()
+    assert not b.dirty
+
+
 def _fma32(a, b, c):
     """float32 fused multiply-add (the float64 product of two float32s is exact)."""
     return (a.astype(np.float64) * b + c).astype(np.float32)
