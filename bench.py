@@ -628,9 +628,17 @@ def packed_attention_metric(device, reps=10, rows=8):
         torch.cuda.synchronize()
         return e0.elapsed_time(e1) / reps
 
+    from mouse_core_b200.packed import pair_count
+
+    pair_off = K.varlen_pair_offsets(tl, L)
+    n_pairs = pair_count(seq)
     out, lse = K.varlen_attention_fwd(q, k, v, rs, tl, scale)
+    ms_recompute = timed(lambda: K.varlen_attention_bwd(q, k, v, out, do, lse, rs, re, scale))
+    clocks = Clocks(device.index or 0)
     ms = timed(lambda: K.varlen_attention_fwd(q, k, v, rs, tl, scale))
-    ms_bwd = timed(lambda: K.varlen_attention_bwd(q, k, v, out, do, lse, rs, re, scale))
+    ms_bwd = timed(lambda: K.varlen_attention_bwd(q, k, v, out, do, lse, rs, re, scale, tile_lo=tl,
+                                                  pair_off=pair_off, n_pairs=n_pairs))
+    clk = clocks.stop()
     peaks = {}
     try:
         with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
@@ -638,8 +646,10 @@ def packed_attention_metric(device, reps=10, rows=8):
     except (OSError, ValueError):
         pass
     peak = float(peaks.get("bf16_tflops", 1590.0))
+    peak_sus = peaks.get("bf16_tflops_sustained")
     tf = flops / (ms * 1e-3) / 1e12
     tf_bwd = 2.5 * flops / (ms_bwd * 1e-3) / 1e12
+    tf_rec = 2.5 * flops / (ms_recompute * 1e-3) / 1e12
     tf_all = 3.5 * flops / ((ms + ms_bwd) * 1e-3) / 1e12
     from mouse_core_b200 import _lib
 
@@ -650,10 +660,15 @@ def packed_attention_metric(device, reps=10, rows=8):
             "value": round(tf_all, 1), "unit": "TFLOP/s", "algorithmic_flops_fwd": flops,
             "flops_note": "algorithmic = 4*Hq*hd*sum s(s+1)/2 (unmasked pairs only); bwd counted as 2.5x fwd",
             "fwd": {"ms": round(ms, 4), "tflops": round(tf, 1), "frac": round(tf / peak, 4)},
-            "bwd": {"ms": round(ms_bwd, 4), "tflops": round(tf_bwd, 1), "frac": round(tf_bwd / peak, 4)},
+            "bwd": {"ms": round(ms_bwd, 4), "tflops": round(tf_bwd, 1), "frac": round(tf_bwd / peak, 4),
+                    "path": f"stored dS ({n_pairs} pairs x {Hq} heads x 32 KB = {Hq * n_pairs * 32768 / 2**30:.2f} GiB)"},
+            "bwd_recompute": {"ms": round(ms_recompute, 4), "tflops": round(tf_rec, 1),
+                              "frac": round(tf_rec / peak, 4)},
+            "clocks": clk,
             "roofline": {"bound": "tensor", "achieved": round(tf_all, 1), "peak": peak,
                          "peak_source": "measured" if "bf16_tflops" in peaks else "fallback",
-                         "unit": "TFLOP/s", "frac": round(tf_all / peak, 4)}}
+                         "unit": "TFLOP/s", "frac": round(tf_all / peak, 4),
+                         "frac_of_sustained": round(tf_all / float(peak_sus), 4) if peak_sus else None}}
 
 
 # ------------------------------------------------------- packed training

@@ -195,6 +195,30 @@ int mb_varlen_attention_bwd(const void* q, const void* k, const void* v, const v
                             void* dv, float* delta, mb_stream_t stream);
 
 /* ---------------------------------------------------------------------
+ * Packed attention backward without the recompute of S and dP for dQ.
+ * Same gradients as mb_varlen_attention_bwd; the dK/dV kernel also stores
+ * every bf16 dS^T block (32 KB per q-head and (query tile, key tile) pair)
+ * in ds_scratch, and dQ = scale dS K is one GEMM over the stored blocks.
+ *   tile_lo: from mb_segment_meta (tile 128).
+ *   pair_off int32 [MB_VARLEN_BWD_PAIR_OFFSETS(L)] from
+ *   mb_varlen_bwd_pair_offsets; n_pairs = pair_off[ceil(L/128)], the number
+ *   of pairs the forward visits (the caller reads it back or computes it
+ *   from the segment lengths: sum over query tiles i of i - tile_lo[i]/128 + 1).
+ *   ds_scratch: >= MB_VARLEN_BWD_DS_BYTES(q_heads, n_pairs) bytes, 16-byte
+ *   aligned.
+ * A pair offset that disagrees with n_pairs sets the device status
+ * (mb_device_status) instead of writing outside the scratch.
+ * ------------------------------------------------------------------- */
+#define MB_VARLEN_BWD_PAIR_OFFSETS(L) (((size_t)(L) + 127u) / 128u + 1u)
+#define MB_VARLEN_BWD_DS_BYTES(q_heads, n_pairs) ((size_t)(q_heads) * (size_t)(n_pairs) * 32768u)
+int mb_varlen_bwd_pair_offsets(const int32_t* tile_lo, int L, int32_t* pair_off, mb_stream_t stream);
+int mb_varlen_attention_bwd_stored(const void* q, const void* k, const void* v, const void* out, const void* dout,
+                                   const float* lse, int L, int q_heads, int kv_heads, int head_dim,
+                                   const int32_t* run_start, const int32_t* run_end, const int32_t* tile_lo,
+                                   const int32_t* pair_off, int n_pairs, float scale, void* dq, void* dk, void* dv,
+                                   float* delta, void* ds_scratch, size_t ds_bytes, mb_stream_t stream);
+
+/* ---------------------------------------------------------------------
  * Segment metadata of a packed stream (K7).
  * Replaces the position ids of models/backbone/flex_train.py:84-92 (and
  * models/base.py:1226-1236) and the BlockMask build of flex_train.py:116-125.

@@ -36,6 +36,10 @@ PROTOTYPES = {
     "mb_varlen_attention_bwd": (_c_int, [_vp, _vp, _vp, _vp, _vp, _vp, _c_int, _c_int, _c_int, _c_int, _vp, _vp,
                                          _c_float, _vp, _vp, _vp, _vp, _vp]),
     "mb_segment_meta": (_c_int, [_vp, _c_int, _c_int, _vp, _vp, _vp, _vp, _vp, _vp]),
+    "mb_varlen_bwd_pair_offsets": (_c_int, [_vp, _c_int, _vp, _vp]),
+    "mb_varlen_attention_bwd_stored": (_c_int, [_vp, _vp, _vp, _vp, _vp, _vp, _c_int, _c_int, _c_int, _c_int, _vp,
+                                                _vp, _vp, _vp, _c_int, _c_float, _vp, _vp, _vp, _vp, _vp, _c_size,
+                                                _vp]),
     "mb_rmsnorm_fwd": (_c_int, [_vp, _vp, _c_float, _c_int, _c_int, _vp, _vp, _vp]),
     "mb_rmsnorm_bwd_scratch_floats": (_c_size, [_c_int, _c_int]),
     "mb_rmsnorm_bwd": (_c_int, [_vp, _vp, _vp, _vp, _c_int, _c_int, _vp, _vp, _vp, _c_size, _vp]),

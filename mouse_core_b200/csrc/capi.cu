@@ -305,10 +305,14 @@ int mb_varlen_attention_fwd(const void* q, const void* k, const void* v, int L, 
   return e == cudaSuccess ? MB_OK : cuda_fail(e, "varlen attention forward launch");
 }
 
-int mb_varlen_attention_bwd(const void* q, const void* k, const void* v, const void* out, const void* dout,
-                            const float* lse, int L, int q_heads, int kv_heads, int head_dim,
-                            const int32_t* run_start, const int32_t* run_end, float scale, void* dq, void* dk,
-                            void* dv, float* delta, mb_stream_t stream) {
+namespace {
+
+// Shared body of the two backward entry points; ds == nullptr selects the
+// recompute path.
+int varlen_bwd(const void* q, const void* k, const void* v, const void* out, const void* dout, const float* lse,
+               int L, int q_heads, int kv_heads, int head_dim, const int32_t* run_start, const int32_t* run_end,
+               const int32_t* tile_lo, const int32_t* pair_off, int n_pairs, float scale, void* dq, void* dk,
+               void* dv, float* delta, void* ds, size_t ds_bytes, mb_stream_t stream) {
   if (L < 0 || q_heads <= 0 || kv_heads <= 0) return fail(MB_ERR_INVALID_ARG, "L >= 0 and head counts > 0 required");
   if (q_heads % kv_heads) return fail(MB_ERR_INVALID_ARG, "q_heads must be a multiple of kv_heads");
   if (head_dim != 64 && head_dim != 128) return fail(MB_ERR_UNSUPPORTED, "head_dim must be 64 or 128");
@@ -320,6 +324,14 @@ int mb_varlen_attention_bwd(const void* q, const void* k, const void* v, const v
     return fail(MB_ERR_INVALID_ARG, "q, k, v, dout, dq, dk, dv must be 16-byte aligned");
   CUtensorMap qm, km, vm, dm;
   int rc;
+  if (ds) {
+    const long long tiles = (L + 127) / 128;
+    if (!tile_lo || !pair_off) return fail(MB_ERR_INVALID_ARG, "the stored-dS path needs tile_lo and pair_off");
+    if (n_pairs < tiles) return fail(MB_ERR_INVALID_ARG, "n_pairs must be at least ceil(L / 128)");
+    if (ds_bytes < MB_VARLEN_BWD_DS_BYTES(q_heads, n_pairs))
+      return fail(MB_ERR_WORKSPACE, "ds scratch smaller than MB_VARLEN_BWD_DS_BYTES(q_heads, n_pairs)");
+    if (!aligned(ds, 16)) return fail(MB_ERR_INVALID_ARG, "ds scratch must be 16-byte aligned");
+  }
   if ((rc = encode_token_map(&qm, q, L, q_heads, head_dim))) return rc;
   if ((rc = encode_token_map(&km, k, L, kv_heads, head_dim))) return rc;
   if ((rc = encode_token_map(&vm, v, L, kv_heads, head_dim))) return rc;
@@ -340,9 +352,40 @@ int mb_varlen_attention_bwd(const void* q, const void* k, const void* v, const v
   p.dq = static_cast<__nv_bfloat16*>(dq);
   p.dk = static_cast<__nv_bfloat16*>(dk);
   p.dv = static_cast<__nv_bfloat16*>(dv);
+  p.tile_lo = tile_lo;
+  p.pair_off = pair_off;
+  p.n_pairs = ds ? n_pairs : 0;
+  p.ds = static_cast<__nv_bfloat16*>(ds);
   cudaError_t e = mb::launch_varlen_bwd(qm, km, vm, dm, static_cast<const __nv_bfloat16*>(out),
                                         static_cast<const __nv_bfloat16*>(dout), p, (cudaStream_t)stream);
   return e == cudaSuccess ? MB_OK : cuda_fail(e, "varlen attention backward launch");
+}
+
+}  // namespace
+
+int mb_varlen_attention_bwd(const void* q, const void* k, const void* v, const void* out, const void* dout,
+                            const float* lse, int L, int q_heads, int kv_heads, int head_dim,
+                            const int32_t* run_start, const int32_t* run_end, float scale, void* dq, void* dk,
+                            void* dv, float* delta, mb_stream_t stream) {
+  return varlen_bwd(q, k, v, out, dout, lse, L, q_heads, kv_heads, head_dim, run_start, run_end, nullptr, nullptr, 0,
+                    scale, dq, dk, dv, delta, nullptr, 0, stream);
+}
+
+int mb_varlen_bwd_pair_offsets(const int32_t* tile_lo, int L, int32_t* pair_off, mb_stream_t stream) {
+  if (L < 0) return fail(MB_ERR_INVALID_ARG, "L must be >= 0");
+  if (!pair_off || (L > 0 && !tile_lo)) return fail(MB_ERR_INVALID_ARG, "a required pointer is NULL");
+  cudaError_t e = mb::launch_varlen_pair_offsets(tile_lo, L, pair_off, (cudaStream_t)stream);
+  return e == cudaSuccess ? MB_OK : cuda_fail(e, "pair offsets launch");
+}
+
+int mb_varlen_attention_bwd_stored(const void* q, const void* k, const void* v, const void* out, const void* dout,
+                                   const float* lse, int L, int q_heads, int kv_heads, int head_dim,
+                                   const int32_t* run_start, const int32_t* run_end, const int32_t* tile_lo,
+                                   const int32_t* pair_off, int n_pairs, float scale, void* dq, void* dk, void* dv,
+                                   float* delta, void* ds_scratch, size_t ds_bytes, mb_stream_t stream) {
+  if (L > 0 && !ds_scratch) return fail(MB_ERR_INVALID_ARG, "ds_scratch is NULL");
+  return varlen_bwd(q, k, v, out, dout, lse, L, q_heads, kv_heads, head_dim, run_start, run_end, tile_lo, pair_off,
+                    n_pairs, scale, dq, dk, dv, delta, ds_scratch, ds_bytes, stream);
 }
 
 int mb_segment_meta(const int64_t* sequence_ids, int L, int tile, int64_t* position, int32_t* run_start,

@@ -24,6 +24,7 @@ enum DeviceStatus : int {
   kDevTimeoutEmpty = 2,  // producer gave up waiting for a free stage
   kDevBadPage = 3,       // block-table entry outside the page pool
   kDevBadSmem = 4,       // dynamic shared memory base not 1024-byte aligned
+  kDevBadPair = 5,       // stored-dS pair index outside the scratch (inconsistent pair offsets)
 };
 
 // The library is one translation unit (mouse_b200.cu), so the status word is
@@ -93,6 +94,16 @@ __device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* m
       "cp.async.bulk.tensor.2d.shared::cta.global.mbarrier::complete_tx::bytes"
       " [%0], [%1, {%3, %4}], [%2];" ::"r"(smem_u32(smem_dst)),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y)
+      : "memory");
+}
+
+// Untiled bulk copy global -> this CTA's shared memory (no multicast), completion
+// counted in bytes on `bar`; both addresses 16-byte aligned, bytes a multiple of 16.
+__device__ __forceinline__ void bulk_load(void* smem_dst, const void* gmem_src, uint32_t bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(gmem_src)), "r"(bytes), "r"(smem_u32(bar))
       : "memory");
 }
 

@@ -95,10 +95,20 @@ struct VarlenBwdParams {
   __nv_bfloat16* dq;         // [L, Hq, HD]
   __nv_bfloat16* dk;         // [L, Hkv, HD]
   __nv_bfloat16* dv;         // [L, Hkv, HD]
+  // Stored-dS path (ds != nullptr): the dK/dV kernel writes each (q-head,
+  // query tile i, key tile j) block of dS^T to
+  // ds + ((h * n_pairs + pair_off[i] + j - tile_lo[i] / 128) * 128 * 128),
+  // element (key r, query c) at (c / 8) * 1024 + r * 8 + c % 8, and dQ is one
+  // GEMM over those blocks.
+  const int32_t* tile_lo;    // [ceil(L/128)] run_start of each query tile's first token
+  const int32_t* pair_off;   // [ceil(L/128) + 1]
+  int n_pairs;
+  __nv_bfloat16* ds;
 };
 cudaError_t launch_varlen_bwd(const CUtensorMap& qm, const CUtensorMap& km, const CUtensorMap& vm,
                               const CUtensorMap& dom, const __nv_bfloat16* out, const __nv_bfloat16* dout,
                               VarlenBwdParams p, cudaStream_t stream);
+cudaError_t launch_varlen_pair_offsets(const int32_t* tile_lo, int L, int32_t* pair_off, cudaStream_t stream);
 
 // Training element-wise kernels (train_elementwise.cu).
 cudaError_t launch_rmsnorm_fwd(const __nv_bfloat16* x, const __nv_bfloat16* w, float eps, int rows, int D,

@@ -125,6 +125,39 @@ __device__ __forceinline__ void umma_ts_t128_warp(uint32_t d, uint32_t a, uint64
       ::"r"(d), "r"(a), "l"(db), "r"(idesc), "r"(accumulate));
 }
 
+// Shared-memory descriptor of a non-swizzled canonical layout: 8 x 16-byte
+// core matrices of 128 contiguous bytes. For an MN-major operand, LBO is the
+// byte distance between core matrices adjacent in K (8 rows further) and SBO
+// between core matrices adjacent in M/N (8 elements further).
+__device__ __forceinline__ uint64_t umma_desc_noswz(uint32_t saddr, uint32_t lbo_bytes, uint32_t sbo_bytes) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr >> 4) & 0x3FFFu);
+  d |= (uint64_t)((lbo_bytes >> 4) & 0x3FFFu) << 16;
+  d |= (uint64_t)((sbo_bytes >> 4) & 0x3FFFu) << 32;
+  d |= (uint64_t)1 << 46;  // descriptor version for sm_100; swizzle field 0 = none
+  return d;
+}
+
+// D (+)= A B over 128 K rows, both operands MN-major in shared memory: A
+// non-swizzled with K-adjacent core matrices 128 bytes apart (a K-step of 16
+// rows advances it by 256 bytes), B SW128 (16 rows = 2048 bytes per K-step).
+// `accumulate` applies to the first K-step only.
+__device__ __forceinline__ void umma_ss_mn_t128_warp(uint32_t d, uint64_t da, uint64_t db, uint32_t idesc,
+                                                     uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred e, t, p;\n\t.reg .b64 a, b;\n\t"
+      "elect.sync _|e, 0xffffffff;\n\tsetp.eq.b32 t, %3, %3;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t"
+      "add.s64 a, %1, 16;\n\tadd.s64 b, %2, 128;\n\t@e tcgen05.mma.cta_group::1.kind::f16 [%0], a, b, %3, t;\n\t"
+      "add.s64 a, %1, 32;\n\tadd.s64 b, %2, 256;\n\t@e tcgen05.mma.cta_group::1.kind::f16 [%0], a, b, %3, t;\n\t"
+      "add.s64 a, %1, 48;\n\tadd.s64 b, %2, 384;\n\t@e tcgen05.mma.cta_group::1.kind::f16 [%0], a, b, %3, t;\n\t"
+      "add.s64 a, %1, 64;\n\tadd.s64 b, %2, 512;\n\t@e tcgen05.mma.cta_group::1.kind::f16 [%0], a, b, %3, t;\n\t"
+      "add.s64 a, %1, 80;\n\tadd.s64 b, %2, 640;\n\t@e tcgen05.mma.cta_group::1.kind::f16 [%0], a, b, %3, t;\n\t"
+      "add.s64 a, %1, 96;\n\tadd.s64 b, %2, 768;\n\t@e tcgen05.mma.cta_group::1.kind::f16 [%0], a, b, %3, t;\n\t"
+      "add.s64 a, %1, 112;\n\tadd.s64 b, %2, 896;\n\t@e tcgen05.mma.cta_group::1.kind::f16 [%0], a, b, %3, t;\n\t}"
+      ::"r"(d), "l"(da), "l"(db), "r"(idesc), "r"(accumulate));
+}
+
 // As umma_ts_t128_warp, with A written by four 32-token quarters, each packed
 // into the first 16 columns of its own 32: K-step kk at column
 // 32 * (kk / 2) + 8 * (kk % 2).

@@ -8,7 +8,7 @@
 // with dK/dV summed over the q-heads sharing a kv-head.
 //
 // Three kernels, deterministic (every output element is computed by one CTA;
-// the only atomic is the dq kernel's tile counter):
+// the only atomics are the persistent kernels' tile counters):
 //  * delta:  D[h, i] (fp32) from dO and O.
 //  * dkdv:   per (128-key tile, kv-head) tile (persistent, like dq), walking every (q-head of the
 //            group, 128-query tile) item whose queries may see its keys. Keys
@@ -27,6 +27,12 @@
 //            dS (bf16, over the S columns it came from), dQ += dS K. The
 //            kernel is persistent (one CTA per SM, tiles from a counter) so a
 //            tile's epilogue overlaps the next tile's loads and first MMAs.
+//  * stored-dS path (when the caller gives a dS scratch): the dkdv kernel
+//            also writes every bf16 dS^T block to global memory (coalesced:
+//            query chunks of 8, 128 key rows x 16 bytes each), and dq_stored
+//            computes dQ = scale dS K as one GEMM per query tile over those
+//            blocks. 5 GEMM-equivalents per tile pair instead of 7, for
+//            32 KB written and read back per pair and q-head.
 //
 // Pipelining (one item stream per CTA, every MMA 128 x 128 or 128 x HD wide):
 //  * The element-wise warps signal once per phase (one mbarrier arrive per
@@ -779,6 +785,21 @@ __global__ void __launch_bounds__(kBwdThreads, 1) varlen_bwd_dkdv_kernel(const _
         // dS^T = P^T o (dP^T - D), packed over the dP^T columns.
         for (int t = 0; t < d.n; ++t) {
           const int tt = J + t;
+          // Stored-dS path: this thread's key row of the item's dS^T block, laid
+          // out as 16 chunks of 8 queries, each chunk 128 key rows x 16 bytes,
+          // so a warp's store of one chunk is 512 contiguous bytes.
+          __nv_bfloat16* ds_row = nullptr;
+          if (p.ds != nullptr) {
+            const int qi = d.i_lo + t % d.nqi;
+            const int lo = p.pair_off[qi], hi = p.pair_off[qi + 1];
+            const int pair = lo + d.kv0 / 128 - p.tile_lo[qi] / 128;
+            if (pair >= lo && pair < hi && hi <= p.n_pairs) {
+              const int hq = d.kvh * p.G + t / d.nqi;
+              ds_row = p.ds + ((size_t)hq * p.n_pairs + pair) * (128 * 128) + 8 * r + 64 * 128 * ch;
+            } else if (lane == 0) {
+              report(kDevBadPair);
+            }
+          }
           uint32_t pk[2][16];
           if (ok) ok = mbar_wait_warp(&bars->p_done, tt & 1, kDevTimeoutFull);
           tc_fence_after();
@@ -812,6 +833,12 @@ __global__ void __launch_bounds__(kBwdThreads, 1) varlen_bwd_dkdv_kernel(const _
                                                 p23.y * (__uint_as_float(dv[4 * e4 + 3]) - dd.w));
               }
               tmem_st16(tx, pk[h]);
+              if (ds_row != nullptr) {
+#pragma unroll
+                for (int m = 0; m < 4; ++m)  // query chunk 8 ch + 4 h + m
+                  *reinterpret_cast<uint4*>(ds_row + (4 * h + m) * (8 * 128)) =
+                      make_uint4(pk[h][4 * m], pk[h][4 * m + 1], pk[h][4 * m + 2], pk[h][4 * m + 3]);
+              }
             }
             tmem_wait_st();
           }
@@ -865,6 +892,241 @@ __global__ void __launch_bounds__(kBwdThreads, 1) varlen_bwd_dkdv_kernel(const _
   }
 }
 
+// ---------------------------------------------------------------- dq kernel, stored dS
+// dQ = scale * dS K as one GEMM per (query tile, q-head) tile over the dS^T
+// blocks the dK/dV kernel stored: A = dS (M = queries, K = keys), whose
+// stored layout (query chunks of 8, each 128 key rows x 16 bytes) is the
+// non-swizzled MN-major canonical layout, so one 32 KB bulk copy per block
+// lands it ready for the MMA; B = K MN-major by TMA; fp32 accumulators in
+// TMEM. Two accumulators, so a tile's epilogue overlaps the next tile's MMAs.
+// Persistent, heaviest query tiles first (first counter).
+// Warp 0 issues TMA, warp 1 the MMAs, warps 2-9 the epilogue (warp w reads
+// TMEM lane quarter w % 4 and half of the HD columns).
+constexpr int kDqsStages = 3;
+constexpr int kDqsEpiWarps = 8;
+constexpr int kDqsThreads = 32 * (2 + kDqsEpiWarps);
+
+struct DqsBars {
+  uint64_t tile_full[2], tile_empty[2];              // tile-id ring
+  uint64_t full[kDqsStages], empty[kDqsStages];      // dS block + K tile per stage
+  uint64_t acc_full[2], acc_empty[2];                // the two dQ accumulators
+  uint32_t tmem_base;
+  int tile[2];
+};
+
+struct DqsTile {
+  int q0, h, kvh, t_lo, n, pair0;
+};
+
+__device__ __forceinline__ DqsTile dqs_tile(int tile, const VarlenBwdParams& p) {
+  const int n_qt = (p.L + 127) / 128;
+  DqsTile d;
+  const int qt = n_qt - 1 - tile / p.Hq;
+  d.h = tile % p.Hq;
+  d.kvh = d.h / p.G;
+  d.q0 = qt * 128;
+  d.t_lo = p.tile_lo[qt] / 128;
+  d.n = qt - d.t_lo + 1;  // key tiles t_lo .. qt, the pairs pair_off[qt] ..
+  d.pair0 = p.pair_off[qt];
+  return d;
+}
+
+template <int HD>
+__global__ void __launch_bounds__(kDqsThreads, 1)
+    varlen_bwd_dq_stored_kernel(const __grid_constant__ CUtensorMap kmap, const VarlenBwdParams p) {
+  using C = BwdTile<HD>;
+  constexpr int A_BYTES = 128 * 128 * 2;    // one dS block
+  constexpr int STAGE = A_BYTES + C::TILE;  // and the K tile
+  extern __shared__ __align__(1024) uint8_t smem[];
+  if (!smem_base_aligned(smem)) {
+    if (threadIdx.x == 0) report(kDevBadSmem);
+    return;
+  }
+  DqsBars* bars = reinterpret_cast<DqsBars*>(smem + kDqsStages * STAGE);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n_tiles = ((p.L + 127) / 128) * p.Hq;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&bars->tile_full[s], 1);
+      mbar_init(&bars->tile_empty[s], 1 + kDqsEpiWarps);
+      mbar_init(&bars->acc_full[s], 1);
+      mbar_init(&bars->acc_empty[s], kDqsEpiWarps);
+    }
+    for (int s = 0; s < kDqsStages; ++s) {
+      mbar_init(&bars->full[s], 1);
+      mbar_init(&bars->empty[s], 1);
+    }
+    fence_barrier_init();
+  }
+  if (warp == 1) tmem_alloc(&bars->tmem_base, 2 * HD);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tbase = bars->tmem_base;
+
+  auto take_tile = [&](int k, bool& ok) {
+    ok = mbar_wait_warp(&bars->tile_full[k & 1], (k >> 1) & 1, kDevTimeoutFull);
+    const int tile = ok ? *reinterpret_cast<volatile int*>(&bars->tile[k & 1]) : -1;
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&bars->tile_empty[k & 1]);
+    return tile;
+  };
+
+  if (warp == 0) {
+    if (lane == 0) prefetch_tensormap(&kmap);
+    bool ok = true;
+    int J = 0;  // items of earlier tiles: stage slots and phases continue across tiles
+    for (int k = 0; ok; ++k) {
+      int tile = -1;
+      if (lane == 0) {
+        tile = k == 0 ? (int)blockIdx.x : (int)gridDim.x + atomicAdd(p.tile_counter, 1);
+        if (tile >= n_tiles) tile = -1;
+        ok = mbar_wait(&bars->tile_empty[k & 1], ((k >> 1) & 1) ^ 1, kDevTimeoutEmpty);
+        if (ok) {
+          *reinterpret_cast<volatile int*>(&bars->tile[k & 1]) = tile;
+          mbar_arrive(&bars->tile_full[k & 1]);
+        }
+      }
+      tile = __shfl_sync(0xffffffffu, tile, 0);
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      if (!ok || tile < 0) break;
+      const DqsTile d = dqs_tile(tile, p);
+      if (lane == 0) {
+        const bool pairs_ok = d.pair0 >= 0 && d.pair0 + d.n <= p.n_pairs;
+        if (!pairs_ok) report(kDevBadPair);  // the blocks are then not read (dQ of the tile is garbage)
+        for (int t = 0; ok && t < d.n; ++t) {
+          const int it = J + t, s = it % kDqsStages;
+          ok = mbar_wait(&bars->empty[s], ((it / kDqsStages) & 1) ^ 1, kDevTimeoutEmpty);
+          if (!ok) break;
+          uint8_t* st = smem + s * STAGE;
+          mbar_arrive_expect_tx(&bars->full[s], pairs_ok ? STAGE : C::TILE);
+          if (pairs_ok)
+            bulk_load(st, p.ds + ((size_t)d.h * p.n_pairs + d.pair0 + t) * (128 * 128), A_BYTES, &bars->full[s]);
+          for (int cb = 0; cb < C::NCB; ++cb)
+            tma_load_3d(st + A_BYTES + cb * C::BOX, &kmap, &bars->full[s], cb * 64, d.kvh, (d.t_lo + t) * 128);
+        }
+      }
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      J += d.n;
+    }
+  } else if (warp == 1) {
+    constexpr uint32_t ID = umma_idesc_bf16(128, HD, 1, 1);
+    bool ok = true;
+    int J = 0;
+    for (int k = 0; ok; ++k) {
+      const int tile = take_tile(k, ok);
+      if (!ok || tile < 0) break;
+      const int n = dqs_tile(tile, p).n;
+      const uint32_t acc = tbase + (k & 1) * HD;
+      // Accumulator k & 1 last held tile k - 2: its epilogue must have read it.
+      if (k >= 2 && !(ok = mbar_wait_warp(&bars->acc_empty[k & 1], ((k >> 1) - 1) & 1, kDevTimeoutFull))) break;
+      tc_fence_after();
+      for (int t = 0; t < n; ++t) {
+        const int it = J + t, s = it % kDqsStages;
+        if (!(ok = mbar_wait_warp(&bars->full[s], (it / kDqsStages) & 1, kDevTimeoutFull))) break;
+        tc_fence_after();
+        const uint32_t st = smem_u32(smem + s * STAGE);
+        umma_ss_mn_t128_warp(acc, umma_desc_noswz(st, 128, 2048), umma_desc_sw128(st + A_BYTES, C::BOX, 1024), ID,
+                             t > 0);
+        umma_commit_warp(&bars->empty[s]);
+      }
+      if (!ok) break;
+      umma_commit_warp(&bars->acc_full[k & 1]);
+      J += n;
+    }
+  } else {
+    const int sub = warp & 3, half = (warp - 2) >> 2;
+    const uint32_t lane_bits = (uint32_t)(sub * 32) << 16;
+    constexpr int W = HD / 2;  // columns per warp
+    bool ok = true;
+    for (int k = 0; ok; ++k) {
+      const int tile = take_tile(k, ok);
+      if (!ok || tile < 0) break;
+      const DqsTile d = dqs_tile(tile, p);
+      if (!(ok = mbar_wait_warp(&bars->acc_full[k & 1], (k >> 1) & 1, kDevTimeoutFull))) break;
+      tc_fence_after();
+      const uint32_t src = tbase + (k & 1) * HD + lane_bits + half * W;
+      uint32_t v[W / 32][32];
+#pragma unroll
+      for (int c = 0; c < W / 32; ++c) tmem_ld32(src + 32 * c, v[c]);
+      tmem_wait_ld();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bars->acc_empty[k & 1]);
+      const int q_tok = d.q0 + sub * 32 + lane;
+      if (q_tok < p.L) {
+        uint4* d4 = reinterpret_cast<uint4*>(p.dq + ((size_t)q_tok * p.Hq + d.h) * HD + half * W);
+#pragma unroll
+        for (int c = 0; c < W / 32; ++c)
+#pragma unroll
+          for (int q4 = 0; q4 < 4; ++q4) {
+            const uint32_t* u = v[c] + 8 * q4;
+            uint4 w;
+            w.x = pack_bf16x2(__uint_as_float(u[0]) * p.scale, __uint_as_float(u[1]) * p.scale);
+            w.y = pack_bf16x2(__uint_as_float(u[2]) * p.scale, __uint_as_float(u[3]) * p.scale);
+            w.z = pack_bf16x2(__uint_as_float(u[4]) * p.scale, __uint_as_float(u[5]) * p.scale);
+            w.w = pack_bf16x2(__uint_as_float(u[6]) * p.scale, __uint_as_float(u[7]) * p.scale);
+            d4[4 * c + q4] = w;
+          }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) {
+    __syncwarp();
+    tmem_dealloc(tbase, 2 * HD);
+  }
+}
+
+// Stored-dS pair offsets: pair_off[i] = number of (query tile, key tile)
+// pairs of query tiles before i, query tile i visiting key tiles
+// tile_lo[i] / 128 .. i; pair_off[T] = all pairs. One block of 1024 threads
+// scans the T = ceil(L / 128) entries in chunks with a carried total.
+__global__ void __launch_bounds__(1024) pair_offsets_kernel(const int32_t* __restrict__ tile_lo, int T,
+                                                            int32_t* __restrict__ pair_off) {
+  __shared__ int warp_sum[32];
+  __shared__ int carry;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) carry = 0;
+  __syncthreads();
+  for (int base = 0; base < T; base += 1024) {
+    const int i = base + threadIdx.x;
+    const int v = i < T ? i - tile_lo[i] / 128 + 1 : 0;
+    int x = v;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, x, o);
+      if (lane >= o) x += y;
+    }
+    if (lane == 31) warp_sum[warp] = x;
+    __syncthreads();
+    if (warp == 0) {
+      int w = warp_sum[lane];
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, w, o);
+        if (lane >= o) w += y;
+      }
+      warp_sum[lane] = w;
+    }
+    __syncthreads();
+    const int excl = carry + (warp > 0 ? warp_sum[warp - 1] : 0) + x - v;
+    if (i < T) pair_off[i] = excl;
+    __syncthreads();
+    if (threadIdx.x == 1023) carry = excl + v;
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) pair_off[T] = carry;
+}
+
+cudaError_t launch_varlen_pair_offsets(const int32_t* tile_lo, int L, int32_t* pair_off, cudaStream_t stream) {
+  pair_offsets_kernel<<<1, 1024, 0, stream>>>(tile_lo, (L + 127) / 128, pair_off);
+  return cudaGetLastError();
+}
+
 template <int HD>
 static cudaError_t launch_bwd_hd(const CUtensorMap& qm, const CUtensorMap& km, const CUtensorMap& vm,
                                  const CUtensorMap& dom, const VarlenBwdParams& p, cudaStream_t stream) {
@@ -884,6 +1146,13 @@ static cudaError_t launch_bwd_hd(const CUtensorMap& qm, const CUtensorMap& km, c
   e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   const int dq_grid = std::max(1, std::min(n_t * p.Hq, sms));  // persistent: one CTA per SM
+  if (p.ds != nullptr) {
+    constexpr int smem_dqs = kDqsStages * (128 * 128 * 2 + C::TILE) + (int)sizeof(DqsBars);
+    e = cudaFuncSetAttribute(varlen_bwd_dq_stored_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_dqs);
+    if (e != cudaSuccess) return e;
+    varlen_bwd_dq_stored_kernel<HD><<<dq_grid, kDqsThreads, smem_dqs, stream>>>(km, p);
+    return cudaGetLastError();
+  }
   varlen_bwd_dq_kernel<HD><<<dq_grid, kBwdThreads, smem_dq, stream>>>(qm, km, vm, dom, p);
   return cudaGetLastError();
 }

@@ -242,8 +242,27 @@ def varlen_attention_fwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, run_
     return out, lse_buf[:Hq * L].view(Hq, L)
 
 
-def varlen_attention_bwd(q, k, v, out, dout, lse, run_start, run_end, scale):
-    """K6: ``(dq, dk, dv)`` of ``varlen_attention_fwd`` for upstream ``dout``."""
+# Largest dS scratch the stored-dS backward takes before falling back to the
+# recompute path (bytes); the scratch is Hq x pairs x 32 KB.
+STORED_DS_MAX_BYTES = 24 << 30
+
+
+def varlen_pair_offsets(tile_lo: torch.Tensor, L: int) -> torch.Tensor:
+    """``pair_off int32 [ceil(L/128) + 1]`` of the stored-dS backward (the
+    last entry is the number of (query tile, key tile) pairs)."""
+    _need(tile_lo, "tile_lo", torch.int32)
+    out = torch.empty((L + 127) // 128 + 1, dtype=torch.int32, device=tile_lo.device)
+    _lib.call("mb_varlen_bwd_pair_offsets", _p(tile_lo), int(L), _p(out), _stream(tile_lo))
+    _count()
+    return out
+
+
+def varlen_attention_bwd(q, k, v, out, dout, lse, run_start, run_end, scale, tile_lo=None, pair_off=None,
+                         n_pairs=None):
+    """K6: ``(dq, dk, dv)`` of ``varlen_attention_fwd`` for upstream ``dout``.
+    With ``tile_lo``, ``pair_off`` and ``n_pairs`` (and a dS scratch within
+    ``STORED_DS_MAX_BYTES``) dQ is one GEMM over the dS blocks the dK/dV kernel
+    stores; otherwise the dQ kernel recomputes S and dP."""
     for name, t in (("q", q), ("k", k), ("v", v), ("out", out), ("dout", dout)):
         _need(t, name, BF16)
     _need(lse, "lse", torch.float32)
@@ -255,8 +274,17 @@ def varlen_attention_bwd(q, k, v, out, dout, lse, run_start, run_end, scale):
     dk = torch.empty_like(k)
     dv = torch.empty_like(v)
     delta = torch.empty(Hq * L + 4, dtype=torch.float32, device=q.device)  # MB_VARLEN_BWD_SCRATCH_FLOATS
-    _lib.call("mb_varlen_attention_bwd", _p(q), _p(k), _p(v), _p(out), _p(dout), _p(lse), L, Hq, Hkv, hd,
-              _p(run_start), _p(run_end), float(scale), _p(dq), _p(dk), _p(dv), _p(delta), _stream(q))
+    ds_bytes = Hq * int(n_pairs) * 32768 if n_pairs is not None else None  # MB_VARLEN_BWD_DS_BYTES
+    if pair_off is not None and L > 0 and ds_bytes <= STORED_DS_MAX_BYTES:
+        _need(tile_lo, "tile_lo", torch.int32)
+        _need(pair_off, "pair_off", torch.int32)
+        ds = torch.empty(ds_bytes, dtype=torch.uint8, device=q.device)
+        _lib.call("mb_varlen_attention_bwd_stored", _p(q), _p(k), _p(v), _p(out), _p(dout), _p(lse), L, Hq, Hkv,
+                  hd, _p(run_start), _p(run_end), _p(tile_lo), _p(pair_off), int(n_pairs), float(scale), _p(dq),
+                  _p(dk), _p(dv), _p(delta), _p(ds), ds_bytes, _stream(q))
+    else:
+        _lib.call("mb_varlen_attention_bwd", _p(q), _p(k), _p(v), _p(out), _p(dout), _p(lse), L, Hq, Hkv, hd,
+                  _p(run_start), _p(run_end), float(scale), _p(dq), _p(dk), _p(dv), _p(delta), _stream(q))
     _count(3)
     return dq, dk, dv
 

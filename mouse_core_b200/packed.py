@@ -35,6 +35,7 @@ from __future__ import annotations
 
 from typing import Any, cast
 
+import numpy as np
 import torch
 
 from mouse_core_b200 import kernels as K
@@ -44,23 +45,42 @@ class _SegmentAttention(torch.autograd.Function):
     """out = segment-causal GQA attention of ``q [L,Hq,hd]`` over ``k, v [L,Hkv,hd]``."""
 
     @staticmethod
-    def forward(ctx, q, k, v, run_start, run_end, tile_lo, scale):
+    def forward(ctx, q, k, v, run_start, run_end, tile_lo, scale, pair_off, n_pairs):
         q, k, v = q.contiguous(), k.contiguous(), v.contiguous()
         out, lse = K.varlen_attention_fwd(q, k, v, run_start, tile_lo, scale)
-        ctx.save_for_backward(q, k, v, out, lse, run_start, run_end)
+        ctx.save_for_backward(q, k, v, out, lse, run_start, run_end, tile_lo)
         ctx.scale = scale
+        ctx.pair_off, ctx.n_pairs = pair_off, n_pairs
         return out
 
     @staticmethod
     def backward(ctx, dout):
-        q, k, v, out, lse, run_start, run_end = ctx.saved_tensors
-        dq, dk, dv = K.varlen_attention_bwd(q, k, v, out, dout.contiguous(), lse, run_start, run_end, ctx.scale)
-        return dq, dk, dv, None, None, None, None
+        q, k, v, out, lse, run_start, run_end, tile_lo = ctx.saved_tensors
+        dq, dk, dv = K.varlen_attention_bwd(q, k, v, out, dout.contiguous(), lse, run_start, run_end, ctx.scale,
+                                            tile_lo=tile_lo, pair_off=ctx.pair_off, n_pairs=ctx.n_pairs)
+        return dq, dk, dv, None, None, None, None, None, None
 
 
-def segment_attention(q, k, v, run_start, run_end, tile_lo, scale):
-    """Autograd-aware K5/K6 attention (``q [L,Hq,hd]``, ``k, v [L,Hkv,hd]``, bf16)."""
-    return _SegmentAttention.apply(q, k, v, run_start, run_end, tile_lo, scale)
+def segment_attention(q, k, v, run_start, run_end, tile_lo, scale, pair_off=None, n_pairs=None):
+    """Autograd-aware K5/K6 attention (``q [L,Hq,hd]``, ``k, v [L,Hkv,hd]``, bf16).
+    With ``pair_off``/``n_pairs`` (``SegmentLayout``) the backward stores dS
+    instead of recomputing it for dQ."""
+    return _SegmentAttention.apply(q, k, v, run_start, run_end, tile_lo, scale, pair_off, n_pairs)
+
+
+def pair_count(sequence_ids: np.ndarray) -> int:
+    """Number of (128-query tile, 128-key tile) pairs the segment-causal
+    attention visits over ``sequence_ids`` whose every id is one contiguous
+    run: query tile ``i`` visits key tiles ``run_start(128 i) // 128 .. i``."""
+    ids = np.asarray(sequence_ids).reshape(-1)
+    L = ids.shape[0]
+    if L == 0:
+        return 0
+    T = (L + 127) // 128
+    starts = np.flatnonzero(np.r_[True, ids[1:] != ids[:-1]])
+    first = np.arange(T, dtype=np.int64) * 128
+    rs = starts[np.searchsorted(starts, first, side="right") - 1]
+    return int((np.arange(T, dtype=np.int64) - rs // 128 + 1).sum())
 
 
 class SegmentLayout:
@@ -84,12 +104,21 @@ class SegmentLayout:
             self.inv[self.perm] = torch.arange(self.L, device=device)
             _, rs, tl, _, re = K.segment_meta(seq[self.perm].contiguous(), tile=128, with_run_end=True)
         self.run_start, self.run_end, self.tile_lo = rs, re, tl
+        # (query tile, key tile) pairs of the stored-dS backward: counted on
+        # the host from host ids, else read back once per layout.
+        self.pair_off = K.varlen_pair_offsets(tl, self.L)
+        if sequence_ids.device.type == "cpu":
+            ids = sequence_ids.numpy()
+            self.n_pairs = pair_count(np.sort(ids, kind="stable") if unsorted else ids)
+        else:
+            self.n_pairs = int(self.pair_off[-1].item())
 
     def attend(self, q, k, v, scale):
         if self.perm is None:
-            return segment_attention(q, k, v, self.run_start, self.run_end, self.tile_lo, scale)
+            return segment_attention(q, k, v, self.run_start, self.run_end, self.tile_lo, scale, self.pair_off,
+                                     self.n_pairs)
         o = segment_attention(q[self.perm], k[self.perm], v[self.perm], self.run_start, self.run_end,
-                              self.tile_lo, scale)
+                              self.tile_lo, scale, self.pair_off, self.n_pairs)
         return o[self.inv]
 
 

@@ -100,3 +100,23 @@ def test_training_elementwise_argument_rules(lib):
     # SiLU-gated product backward
     assert lib.mb_silu_mul_bwd(None, None, 0, 3072, None, None) == 0
     assert lib.mb_silu_mul_bwd(None, None, 4, 3071, None, None) == 1
+
+
+def test_stored_ds_backward_argument_rules(lib):
+    p = ctypes.c_void_p(4096)  # aligned, never dereferenced: every call below returns before any CUDA call
+    args = [p, p, p, p, p, p, 1000, 4, 2, 128, p, p, p, p]
+
+    def call(n_pairs, ds, ds_bytes, L=1000):
+        a = list(args)
+        a[6] = L
+        return lib.mb_varlen_attention_bwd_stored(*a, n_pairs, 0.1, p, p, p, p, ds, ds_bytes, None)
+
+    assert call(8, p, 1 << 30, L=0) == 0
+    assert call(8, None, 1 << 30) == 1 and b"ds_scratch" in lib.mb_last_error()
+    assert call(7, p, 1 << 30) == 1 and b"n_pairs" in lib.mb_last_error()  # fewer pairs than query tiles
+    assert call(36, p, 4 * 36 * 32768 - 1) == 3 and b"MB_VARLEN_BWD_DS_BYTES" in lib.mb_last_error()
+    a = list(args)
+    a[12] = None  # tile_lo
+    assert lib.mb_varlen_attention_bwd_stored(*a, 36, 0.1, p, p, p, p, p, 1 << 30, None) == 1
+    assert lib.mb_varlen_bwd_pair_offsets(None, -1, p, None) == 1
+    assert lib.mb_varlen_bwd_pair_offsets(None, 5, p, None) == 1

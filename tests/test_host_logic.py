@@ -152,3 +152,24 @@ def test_exp2_fma_error_bound():
     assert float(rel.max()) < 1.1e-4
     clamped = np.float32(-126.0)
     assert 0.0 < float(np.exp2(np.float64(clamped))) < 1e-37
+
+
+def test_pair_count_matches_brute_force():
+    """Pairs of (128-query tile, 128-key tile) the segment-causal attention
+    visits: a pair is visited when some query of the tile sees some key of the
+    other tile (same run, key <= query)."""
+    from mouse_core_b200.packed import pair_count
+
+    rng = np.random.default_rng(4)
+    for lens in ([1], [128], [129], [300, 1, 1, 700], list(rng.integers(1, 400, size=20)), [2048, 5]):
+        ids = np.repeat(np.arange(len(lens)), lens)
+        L = ids.shape[0]
+        T = (L + 127) // 128
+        brute = 0
+        for i in range(T):
+            q = np.arange(128 * i, min(128 * i + 128, L))
+            for j in range(i + 1):
+                k = np.arange(128 * j, min(128 * j + 128, L))
+                brute += bool(((ids[q][:, None] == ids[k][None, :]) & (k[None, :] <= q[:, None])).any())
+        assert pair_count(ids) == brute, lens
+    assert pair_count(np.zeros(0, dtype=np.int64)) == 0

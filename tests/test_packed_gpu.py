@@ -123,15 +123,25 @@ def test_varlen_fwd_packed_2048_against_reference_samples():
     assert err < ATOL, f"max abs err vs reference samples {err}"
 
 
-def _run_bwd(seq, q, k, v, do, dev):
+def _run_bwd(seq, q, k, v, do, dev, stored=False):
+    """K6 gradients; ``stored`` takes the path whose dQ is one GEMM over the
+    dS blocks the dK/dV kernel stores (pair count from the host ids, checked
+    against the device offsets)."""
     from mouse_core_b200 import kernels as K
+    from mouse_core_b200.packed import pair_count
 
     st = torch.from_numpy(seq).to(dev)
     _, rs, tl, flags, re = K.segment_meta(st, tile=128, with_run_end=True)
     qd, kd, vd, dod = q.to(dev), k.to(dev), v.to(dev), do.to(dev)
     scale = q.shape[-1] ** -0.5
     out, lse = K.varlen_attention_fwd(qd, kd, vd, rs, tl, scale)
-    dq, dk, dv = K.varlen_attention_bwd(qd, kd, vd, out, dod, lse, rs, re, scale)
+    extra = {}
+    if stored:
+        pair_off = K.varlen_pair_offsets(tl, seq.shape[0])
+        n_pairs = pair_count(seq)
+        assert int(pair_off[-1].item()) == n_pairs
+        extra = dict(tile_lo=tl, pair_off=pair_off, n_pairs=n_pairs)
+    dq, dk, dv = K.varlen_attention_bwd(qd, kd, vd, out, dod, lse, rs, re, scale, **extra)
     torch.cuda.synchronize()
     return [t.float().cpu().numpy() for t in (dq, dk, dv)]
 
@@ -139,17 +149,18 @@ def _run_bwd(seq, q, k, v, do, dev):
 BWD_CASES = FWD_CASES + [("g2_hd128_many", 4, 2, 128, [5, 300, 1, 1, 1, 64, 129, 600])]
 
 
+@pytest.mark.parametrize("stored", [False, True])
 @pytest.mark.parametrize("name,Hq,Hkv,hd,lens", BWD_CASES)
-def test_varlen_bwd_matches_oracle(name, Hq, Hkv, hd, lens):
+def test_varlen_bwd_matches_oracle(name, Hq, Hkv, hd, lens, stored):
     """dq, dk, dv (bf16, fp32 accumulation) vs the float64 analytic gradient on
     the same bf16 inputs: max-abs error within 2e-2 of each gradient's scale
-    (its largest magnitude, at least 1)."""
+    (its largest magnitude, at least 1); both dQ paths."""
     dev = _dev()
     seq = _seq_from_lengths(lens)
     L = seq.shape[0]
     q, k, v, do = cfg1_inputs(13, L, Hq, Hkv, hd)
     q, k, v, do = q.bfloat16(), k.bfloat16(), v.bfloat16(), do.bfloat16()
-    got = _run_bwd(seq, q, k, v, do, dev)
+    got = _run_bwd(seq, q, k, v, do, dev, stored)
     ref = oatt.packed_attention_bwd(q.float().numpy(), k.float().numpy(), v.float().numpy(), seq, hd ** -0.5,
                                     do.float().numpy())
     for gname, g, r in zip(("dq", "dk", "dv"), got, ref):
@@ -162,14 +173,15 @@ def test_varlen_bwd_matches_oracle(name, Hq, Hkv, hd, lens):
     assert _lib.device_status() == 0
 
 
-def test_varlen_bwd_packed_2048_against_reference_samples():
+@pytest.mark.parametrize("stored", [False, True])
+def test_varlen_bwd_packed_2048_against_reference_samples(stored):
     """Gradients of the 2048-token packed workload vs the reference's fp32
-    SDPA-mask autograd (sampled entries)."""
+    SDPA-mask autograd (sampled entries); both dQ paths."""
     dev = _dev()
     g = load("packed_attn_cfg1.npz")
     seq = _seq_from_lengths(cfg1_segments(0))
     q, k, v, do = cfg1_inputs(0, 2048, 4, 2, 64)
-    got = _run_bwd(seq, q.bfloat16(), k.bfloat16(), v.bfloat16(), do.bfloat16(), dev)
+    got = _run_bwd(seq, q.bfloat16(), k.bfloat16(), v.bfloat16(), do.bfloat16(), dev, stored)
     for gname, arr in zip(("dq", "dk", "dv"), got):
         ref = g[f"{gname}_val"]
         scale = max(1.0, float(np.abs(ref).max()))
