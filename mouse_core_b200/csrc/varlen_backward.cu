@@ -95,27 +95,32 @@ __global__ void __launch_bounds__(256) bwd_delta_kernel(const __nv_bfloat16* __r
   // The row groups of one warp advance together (the stride is a multiple of
   // the groups per warp), so the loop test on the warp's first row keeps the
   // shuffles below convergent; rows past the end are masked per group.
+  // Four rows per thread per pass: eight 16-byte loads in flight.
+  constexpr int R = 4;
   const long long gw = (tid & 31) / tpr;
-  for (long long r0 = tid / tpr; r0 - gw < rows; r0 += 2 * stride) {
-    const long long r1 = r0 + stride;
-    const bool has0 = r0 < rows, has1 = r1 < rows;
-    uint4 a0 = make_uint4(0, 0, 0, 0), b0 = a0, a1 = a0, b1 = a0;
-    if (has0) {
-      a0 = __ldg(reinterpret_cast<const uint4*>(out + r0 * hd) + part);
-      b0 = __ldg(reinterpret_cast<const uint4*>(dout + r0 * hd) + part);
+  for (long long r0 = tid / tpr; r0 - gw < rows; r0 += R * stride) {
+    uint4 a[R], b[R];
+#pragma unroll
+    for (int i = 0; i < R; ++i) {
+      const long long r = r0 + i * stride;
+      a[i] = b[i] = make_uint4(0, 0, 0, 0);
+      if (r < rows) {
+        a[i] = __ldg(reinterpret_cast<const uint4*>(out + r * hd) + part);
+        b[i] = __ldg(reinterpret_cast<const uint4*>(dout + r * hd) + part);
+      }
     }
-    if (has1) {
-      a1 = __ldg(reinterpret_cast<const uint4*>(out + r1 * hd) + part);
-      b1 = __ldg(reinterpret_cast<const uint4*>(dout + r1 * hd) + part);
-    }
-    float s0 = dot8_bf16(a0, b0), s1 = dot8_bf16(a1, b1);
-    for (int o = tpr >> 1; o > 0; o >>= 1) {
-      s0 += __shfl_xor_sync(0xffffffffu, s0, o);
-      s1 += __shfl_xor_sync(0xffffffffu, s1, o);
-    }
+    float s[R];
+#pragma unroll
+    for (int i = 0; i < R; ++i) s[i] = dot8_bf16(a[i], b[i]);
+    for (int o = tpr >> 1; o > 0; o >>= 1)
+#pragma unroll
+      for (int i = 0; i < R; ++i) s[i] += __shfl_xor_sync(0xffffffffu, s[i], o);
     if (part == 0) {
-      if (has0) delta[(r0 % Hq) * (long long)L + r0 / Hq] = s0;
-      if (has1) delta[(r1 % Hq) * (long long)L + r1 / Hq] = s1;
+#pragma unroll
+      for (int i = 0; i < R; ++i) {
+        const long long r = r0 + i * stride;
+        if (r < rows) delta[(r % Hq) * (long long)L + r / Hq] = s[i];
+      }
     }
   }
 }
