@@ -219,6 +219,34 @@ int mb_varlen_attention_bwd_stored(const void* q, const void* k, const void* v, 
                                    float* delta, void* ds_scratch, size_t ds_bytes, mb_stream_t stream);
 
 /* ---------------------------------------------------------------------
+ * Decode-step layout glue (K9), byte-for-byte the index maps of
+ * models/base.py:1163-1201 (_flat_to_batched_left_pad) and
+ * models/embedding/packing.py:8-28 (left_align_content).
+ * mb_flat_rank: rank int32 [L] = position of token i among the tokens of its
+ *   id (stable; -1 for ids outside [0, batch)); stats int32 [batch + 2] =
+ *   tokens per id, their maximum, and a flag (1: a prediction index outside
+ *   [-L, L) or past n_pred, written as -1; negative indices count from the
+ *   end, as Python indexing does); local_indices int64 [batch, steps]
+ *   = rank of row b's prediction tokens in columns steps - n_b .. steps - 1
+ *   (n_b = step_counts[b], read from prediction_indices[step_offsets[b] ..]),
+ *   0 elsewhere. batch <= MB_FLAT_RANK_MAX_BATCH (one CTA, shared counters).
+ * mb_flat_scatter: out [batch, max_len, row_bytes] zeroed, then flat row i
+ *   copied to (sequence_ids[i], rank[i]).
+ * mb_left_align: with rl = prediction_indices[b, steps-1] + 1 > 0, row b's
+ *   first rl columns move to columns L - rl .. L - 1 (the rest zero) and its
+ *   indices shift by L - rl; with rl <= 0 the row is zero and the indices
+ *   are unchanged.
+ * ------------------------------------------------------------------- */
+#define MB_FLAT_RANK_MAX_BATCH 49152
+int mb_flat_rank(const int64_t* sequence_ids, int L, int batch, const int64_t* prediction_indices, int n_pred,
+                 const int32_t* step_counts, const int32_t* step_offsets, int steps, int32_t* rank, int32_t* stats,
+                 int64_t* local_indices, mb_stream_t stream);
+int mb_flat_scatter(const void* embeds, int L, int row_bytes, const int64_t* sequence_ids, const int32_t* rank,
+                    int batch, int max_len, void* out, mb_stream_t stream);
+int mb_left_align(const void* embeds, int batch, int L, int row_bytes, const int64_t* prediction_indices, int steps,
+                  void* aligned, int64_t* aligned_indices, mb_stream_t stream);
+
+/* ---------------------------------------------------------------------
  * Segment metadata of a packed stream (K7).
  * Replaces the position ids of models/backbone/flex_train.py:84-92 (and
  * models/base.py:1226-1236) and the BlockMask build of flex_train.py:116-125.

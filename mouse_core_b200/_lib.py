@@ -37,6 +37,9 @@ PROTOTYPES = {
                                          _c_float, _vp, _vp, _vp, _vp, _vp]),
     "mb_segment_meta": (_c_int, [_vp, _c_int, _c_int, _vp, _vp, _vp, _vp, _vp, _vp]),
     "mb_varlen_bwd_pair_offsets": (_c_int, [_vp, _c_int, _vp, _vp]),
+    "mb_flat_rank": (_c_int, [_vp, _c_int, _c_int, _vp, _c_int, _vp, _vp, _c_int, _vp, _vp, _vp, _vp]),
+    "mb_flat_scatter": (_c_int, [_vp, _c_int, _c_int, _vp, _vp, _c_int, _c_int, _vp, _vp]),
+    "mb_left_align": (_c_int, [_vp, _c_int, _c_int, _c_int, _vp, _c_int, _vp, _vp, _vp]),
     "mb_varlen_attention_bwd_stored": (_c_int, [_vp, _vp, _vp, _vp, _vp, _vp, _c_int, _c_int, _c_int, _c_int, _vp,
                                                 _vp, _vp, _vp, _c_int, _c_float, _vp, _vp, _vp, _vp, _vp, _c_size,
                                                 _vp]),

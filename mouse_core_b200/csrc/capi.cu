@@ -388,6 +388,47 @@ int mb_varlen_attention_bwd_stored(const void* q, const void* k, const void* v, 
                     n_pairs, scale, dq, dk, dv, delta, ds_scratch, ds_bytes, stream);
 }
 
+// ---------------------------------------------------------------- decode-step layout glue (K9)
+
+int mb_flat_rank(const int64_t* sequence_ids, int L, int batch, const int64_t* prediction_indices, int n_pred,
+                 const int32_t* step_counts, const int32_t* step_offsets, int steps, int32_t* rank, int32_t* stats,
+                 int64_t* local_indices, mb_stream_t stream) {
+  if (L < 0 || batch < 0 || n_pred < 0 || steps < 0) return fail(MB_ERR_INVALID_ARG, "sizes must be >= 0");
+  if (batch > MB_FLAT_RANK_MAX_BATCH) return fail(MB_ERR_UNSUPPORTED, "batch above MB_FLAT_RANK_MAX_BATCH");
+  if (!stats || (L > 0 && (!sequence_ids || !rank)) || (batch > 0 && steps > 0 && (!step_counts || !step_offsets ||
+                                                                                    !local_indices)) ||
+      (n_pred > 0 && !prediction_indices))
+    return fail(MB_ERR_INVALID_ARG, "a required pointer is NULL");
+  cudaError_t e = mb::launch_flat_rank(sequence_ids, L, batch, prediction_indices, n_pred, step_counts, step_offsets,
+                                       steps, rank, stats, local_indices, (cudaStream_t)stream);
+  return e == cudaSuccess ? MB_OK : cuda_fail(e, "flat rank launch");
+}
+
+int mb_flat_scatter(const void* embeds, int L, int row_bytes, const int64_t* sequence_ids, const int32_t* rank,
+                    int batch, int max_len, void* out, mb_stream_t stream) {
+  if (L < 0 || row_bytes <= 0 || batch < 0 || max_len < 0) return fail(MB_ERR_INVALID_ARG, "bad sizes");
+  const size_t out_bytes = (size_t)batch * (size_t)max_len * (size_t)row_bytes;
+  if (out_bytes == 0) return MB_OK;
+  if (!out || (L > 0 && (!embeds || !sequence_ids || !rank))) return fail(MB_ERR_INVALID_ARG, "a required pointer is NULL");
+  cudaError_t e = cudaMemsetAsync(out, 0, out_bytes, (cudaStream_t)stream);
+  if (e != cudaSuccess) return cuda_fail(e, "flat scatter zero fill");
+  if (L == 0) return MB_OK;
+  e = mb::launch_flat_scatter(embeds, L, row_bytes, sequence_ids, rank, max_len, out, (cudaStream_t)stream);
+  return e == cudaSuccess ? MB_OK : cuda_fail(e, "flat scatter launch");
+}
+
+int mb_left_align(const void* embeds, int batch, int L, int row_bytes, const int64_t* prediction_indices, int steps,
+                  void* aligned, int64_t* aligned_indices, mb_stream_t stream) {
+  if (batch < 0 || L < 0 || row_bytes <= 0 || steps <= 0)
+    return fail(MB_ERR_INVALID_ARG, "batch, L >= 0, row_bytes > 0 and steps >= 1 required");
+  if (batch == 0) return MB_OK;
+  if (!prediction_indices || !aligned_indices || (L > 0 && (!embeds || !aligned)))
+    return fail(MB_ERR_INVALID_ARG, "a required pointer is NULL");
+  cudaError_t e = mb::launch_left_align(embeds, batch, L, row_bytes, prediction_indices, steps, aligned,
+                                        aligned_indices, (cudaStream_t)stream);
+  return e == cudaSuccess ? MB_OK : cuda_fail(e, "left align launch");
+}
+
 int mb_segment_meta(const int64_t* sequence_ids, int L, int tile, int64_t* position, int32_t* run_start,
                     int32_t* run_end, int32_t* tile_lo, int32_t* flags, mb_stream_t stream) {
   if (L < 0 || tile <= 0) return fail(MB_ERR_INVALID_ARG, "L must be >= 0 and tile > 0");

@@ -110,6 +110,15 @@ cudaError_t launch_varlen_bwd(const CUtensorMap& qm, const CUtensorMap& km, cons
                               VarlenBwdParams p, cudaStream_t stream);
 cudaError_t launch_varlen_pair_offsets(const int32_t* tile_lo, int L, int32_t* pair_off, cudaStream_t stream);
 
+// Decode-step layout glue (packing.cu).
+cudaError_t launch_flat_rank(const int64_t* seq, int L, int B, const int64_t* pred, int N, const int32_t* steps,
+                             const int32_t* step_off, int S, int32_t* rank, int32_t* stats, int64_t* local,
+                             cudaStream_t stream);
+cudaError_t launch_flat_scatter(const void* emb, int L, int row_bytes, const int64_t* seq, const int32_t* rank,
+                                int Lmax, void* out, cudaStream_t stream);
+cudaError_t launch_left_align(const void* emb, int B, int L, int row_bytes, const int64_t* pi, int S, void* out,
+                              int64_t* out_idx, cudaStream_t stream);
+
 // Training element-wise kernels (train_elementwise.cu).
 cudaError_t launch_rmsnorm_fwd(const __nv_bfloat16* x, const __nv_bfloat16* w, float eps, int rows, int D,
                                __nv_bfloat16* y, float* rstd, cudaStream_t stream);

@@ -7,5 +7,6 @@
 #include "segment_meta.cu"
 #include "varlen_attention.cu"
 #include "varlen_backward.cu"
+#include "packing.cu"
 #include "capi.cu"
 #include "decode_noalloc.cu"

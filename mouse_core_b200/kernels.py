@@ -289,6 +289,55 @@ def varlen_attention_bwd(q, k, v, out, dout, lse, run_start, run_end, scale, til
     return dq, dk, dv
 
 
+# ---------------------------------------------------------------- decode-step layout glue (K9)
+
+
+def flat_rank(sequence_ids: torch.Tensor, prediction_indices: torch.Tensor, steps_and_offsets: torch.Tensor,
+              B: int, S: int):
+    """``(rank int32 [L], stats int32 [B + 2], local int64 [B, S])`` of
+    ``mb_flat_rank``; ``steps_and_offsets`` is int32 ``[2, B]`` (step counts,
+    then their exclusive prefix sums)."""
+    _need(sequence_ids, "sequence_ids", torch.int64)
+    _need(prediction_indices, "prediction_indices", torch.int64)
+    _need(steps_and_offsets, "steps_and_offsets", torch.int32)
+    L, dev = sequence_ids.numel(), sequence_ids.device
+    rank = torch.empty(L, dtype=torch.int32, device=dev)
+    stats = torch.empty(B + 2, dtype=torch.int32, device=dev)
+    local = torch.empty(B, S, dtype=torch.int64, device=dev)
+    _lib.call("mb_flat_rank", _p(sequence_ids), L, int(B), _p(prediction_indices), prediction_indices.numel(),
+              _p(steps_and_offsets[0]), _p(steps_and_offsets[1]), int(S), _p(rank), _p(stats), _p(local),
+              _stream(sequence_ids))
+    _count()
+    return rank, stats, local
+
+
+def flat_scatter(embeds: torch.Tensor, sequence_ids: torch.Tensor, rank: torch.Tensor, B: int, max_len: int):
+    """Right-padded ``[B, max_len, D]`` copy of flat ``embeds [L, D]`` at
+    ``(sequence_ids[i], rank[i])`` (``mb_flat_scatter``)."""
+    _need(embeds, "embeds")
+    _need(sequence_ids, "sequence_ids", torch.int64)
+    _need(rank, "rank", torch.int32)
+    L, D = embeds.shape
+    out = torch.empty(B, max_len, D, dtype=embeds.dtype, device=embeds.device)
+    _lib.call("mb_flat_scatter", _p(embeds), L, D * embeds.element_size(), _p(sequence_ids), _p(rank), int(B),
+              int(max_len), _p(out), _stream(embeds))
+    _count()
+    return out
+
+
+def left_align(embeds: torch.Tensor, prediction_indices: torch.Tensor):
+    """``(aligned [B, L, D], aligned_indices int64 [B, S])`` of ``mb_left_align``."""
+    _need(embeds, "embeds")
+    _need(prediction_indices, "prediction_indices", torch.int64)
+    B, L, D = embeds.shape
+    out = torch.empty_like(embeds)
+    idx = torch.empty_like(prediction_indices)
+    _lib.call("mb_left_align", _p(embeds), B, L, D * embeds.element_size(), _p(prediction_indices),
+              prediction_indices.shape[1], _p(out), _p(idx), _stream(embeds))
+    _count()
+    return out, idx
+
+
 def silu_mul(gate_up: torch.Tensor) -> torch.Tensor:
     """``silu(gate) * up`` for ``gate_up [..., 2I]``; returns ``[..., I]``."""
     _need(gate_up, "gate_up", BF16)

@@ -9,13 +9,18 @@ reference's per-row Python loops with ``.item()`` host syncs:
 * ``flat_sequence_position_ids``     models/base.py:1226-1236
 * ``flat_sequence_causal_mask``      models/base.py:1204-1223
 
-They run on whatever device their inputs are on (they are index plumbing,
-not kernels); the CUDA training path computes position ids with the K7
-segment kernel instead (``mouse_core_b200.packed``).
+On CPU tensors they are whole-tensor torch ops (the reference's CPU path).
+On CUDA tensors the two decode-step maps run as the K9 kernels
+(``mb_flat_rank`` + ``mb_flat_scatter``, ``mb_left_align``): one rank/count
+pass in a single CTA, one read-back of the counts (``token_lengths`` is a
+host list and sets the output width), one scatter, one shift. The CUDA
+training path computes position ids with the K7 segment kernel instead
+(``mouse_core_b200.packed``).
 """
 
 from __future__ import annotations
 
+import numpy as np
 import torch
 
 
@@ -26,6 +31,8 @@ def left_align_content(embeds: torch.Tensor, prediction_indices: torch.Tensor):
     content move it to columns ``L - row_len ..`` and shift their indices by
     ``L - row_len``. Returns ``(aligned_embeds, aligned_indices)``.
     """
+    if embeds.is_cuda:
+        return _left_align_content_cuda(embeds, prediction_indices)
     B, L = embeds.shape[0], embeds.shape[1]
     row_len = prediction_indices[:, -1] + 1
     has = row_len > 0
@@ -63,6 +70,8 @@ def flat_to_batched_left_pad(embeds: torch.Tensor, sequence_ids: torch.Tensor, p
     and ``local_indices[b, S - n + s]`` the in-row index of row ``b``'s
     ``s``-th prediction token (``n = step_counts[b]``).
     """
+    if embeds.is_cuda:
+        return _flat_to_batched_left_pad_cuda(embeds, sequence_ids, prediction_indices, B, S, step_counts)
     L, D = embeds.shape
     dev = embeds.device
     seq = sequence_ids.to(dev).long()
@@ -83,6 +92,46 @@ def flat_to_batched_left_pad(embeds: torch.Tensor, sequence_ids: torch.Tensor, p
         within = torch.arange(total, device=dev) - torch.repeat_interleave(torch.cumsum(n, 0) - n, n)
         cols = S - n[rows] + within
         local[rows, cols] = rank[prediction_indices[:total].to(dev).long()]
+    return out, token_lengths, local
+
+
+def _left_align_content_cuda(embeds: torch.Tensor, prediction_indices: torch.Tensor):
+    """K9 ``mb_left_align``: one pass over the rows, no host sync."""
+    from mouse_core_b200 import kernels as K
+
+    if prediction_indices.dim() != 2 or prediction_indices.shape[1] == 0:
+        raise IndexError("prediction_indices needs at least one column (its last column gives the row length)")
+    if embeds.shape[0] != prediction_indices.shape[0]:
+        raise ValueError("embeds and prediction_indices disagree on the batch size")
+    pi = prediction_indices.to(embeds.device, torch.long).contiguous()
+    aligned, idx = K.left_align(embeds.contiguous(), pi)
+    return aligned, idx.to(prediction_indices.dtype)
+
+
+def _flat_to_batched_left_pad_cuda(embeds, sequence_ids, prediction_indices, B, S, step_counts):
+    """K9 ``mb_flat_rank`` + ``mb_flat_scatter``: ranks, counts and local
+    indices in one kernel, one read-back of the counts (the result's row
+    width and ``token_lengths`` are host values), then one scatter."""
+    from mouse_core_b200 import kernels as K
+
+    L, D = embeds.shape
+    dev = embeds.device
+    B, S = int(B), int(S)
+    steps = np.full(B, S, dtype=np.int64)
+    k = min(len(step_counts), B)
+    if k:
+        steps[:k] = np.asarray(list(step_counts[:k]), dtype=np.int64)
+    offs = np.cumsum(steps) - steps
+    host = torch.from_numpy(np.stack([steps, offs]).astype(np.int32))
+    meta = host.to(dev, non_blocking=False)
+    seq = sequence_ids.to(dev, torch.long).reshape(-1).contiguous()
+    pred = prediction_indices.to(dev, torch.long).reshape(-1).contiguous()
+    rank, stats, local = K.flat_rank(seq, pred, meta, B, S)
+    st = stats.cpu().numpy()
+    if st[B + 1]:
+        raise IndexError("a prediction index is out of range for the flat tokens")
+    token_lengths = [int(c) for c in st[:B]]
+    out = K.flat_scatter(embeds.contiguous(), seq, rank, B, int(st[B]) if B else 0)
     return out, token_lengths, local
 
 

@@ -120,3 +120,14 @@ def test_stored_ds_backward_argument_rules(lib):
     assert lib.mb_varlen_attention_bwd_stored(*a, 36, 0.1, p, p, p, p, p, 1 << 30, None) == 1
     assert lib.mb_varlen_bwd_pair_offsets(None, -1, p, None) == 1
     assert lib.mb_varlen_bwd_pair_offsets(None, 5, p, None) == 1
+
+
+def test_glue_argument_rules(lib):
+    p = ctypes.c_void_p(4096)
+    assert lib.mb_flat_rank(p, 4, 49153, p, 1, p, p, 1, p, p, p, None) == 2  # batch above the shared counters
+    assert lib.mb_flat_rank(p, -1, 4, p, 1, p, p, 1, p, p, p, None) == 1
+    assert lib.mb_flat_rank(p, 4, 2, None, 3, p, p, 1, p, p, p, None) == 1 and b"NULL" in lib.mb_last_error()
+    assert lib.mb_flat_scatter(p, 4, 0, p, p, 2, 2, p, None) == 1
+    assert lib.mb_flat_scatter(None, 0, 16, None, None, 0, 0, None, None) == 0  # nothing to write
+    assert lib.mb_left_align(p, 2, 3, 16, p, 0, p, p, None) == 1  # needs a last index column
+    assert lib.mb_left_align(None, 0, 3, 16, None, 1, None, None, None) == 0
