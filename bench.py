@@ -581,6 +581,202 @@ def run_large_batch(args):
     return out
 
 
+# GRPO branch rollout: Qwen3-0.6B architecture cut to 8 layers; per GPU 64
+# roots with contexts U[1024, 8192], each forked into 16 branches at a point
+# U[1, root length] (the branch shares the root's full pages; only a partial
+# last page is copied), a 256-token prefill per branch, then one-token decode
+# steps of every branch (the roots sit out). 128-token pages.
+GR = {"layers": 8, "roots": 64, "branches": 16, "root_len": (1024, 8192), "prefill": 256, "page": 128}
+
+
+def grpo_config(n_gpus, roots):
+    return {"workload": f"GRPO branch rollout, Qwen3-0.6B arch cut to 8 layers, {roots} roots/GPU with contexts "
+                        f"U[1024,8192], {GR['branches']} branches per root forked at U[1, root length] sharing "
+                        f"the root's pages, {GR['prefill']}-token branch prefill, then branch decode; "
+                        "128-token pages",
+            "roots_per_gpu": roots, "branches_per_root": GR["branches"], "layers": GR["layers"],
+            "hidden": HIDDEN, "q_heads": HEADS, "kv_heads": KV_HEADS, "head_dim": HEAD_DIM,
+            "page_size": GR["page"], "parallelism": f"roots sharded x{n_gpus} (no collective)",
+            "l2": "inputs larger than L2: each decode step reads ~90 GB of KV per GPU"}
+
+
+def run_grpo(args):
+    import torch
+    import torch.distributed as dist
+    import torch.nn.functional as F
+
+    from mouse_core_b200 import _lib
+    from mouse_core_b200 import kernels as K
+    from mouse_core_b200.backbone import Qwen3Backbone
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    R, G, P, D = args.grpo_roots, GR["branches"], GR["page"], HIDDEN
+    NB = R * G
+    B = R + NB
+    torch.manual_seed(0)
+    bb = Qwen3Backbone(hidden_dim=D, num_layers=GR["layers"], num_heads=HEADS, num_key_value_heads=KV_HEADS,
+                       head_dim=HEAD_DIM, intermediate_size=INTER,
+                       rope_parameters={"rope_type": "default", "rope_theta": ROPE_THETA})
+    bb = bb.to(device=dev, dtype=torch.bfloat16).eval()
+    g = torch.Generator().manual_seed(2)
+    table = torch.randn(VOCAB, D, generator=g).to(device=dev, dtype=torch.bfloat16)
+    head = ActionHead(dev, 1)
+
+    rng = np.random.default_rng(5000 + rank)
+    lo, hi = GR["root_len"]
+    root_len = rng.integers(lo, hi + 1, size=R)
+    fork_at = rng.integers(1, np.repeat(root_len, G) + 1)  # per branch, U[1, root length]
+    W, K_steps = args.warmup, args.steps
+    n_step_calls = W + 2 * K_steps + W + K_steps
+    pages = int(((root_len + P - 1) // P).sum() + ((fork_at % P) > 0).sum()
+                + NB * ((GR["prefill"] + n_step_calls + 2 * P - 1) // P) + 8)
+    sess = bb.decode_session(batch_size=B, capacity=P, page_size=P, num_pages=pages)
+    lengths = np.concatenate([root_len, np.zeros(NB, dtype=np.int64)])
+    ctx_ids = [transition_ids(rng, rng.integers(0, 4, size=int(L)), int(L)) for L in lengths]
+    prefill(sess, table, ctx_ids, lengths)
+    root_pages = sess.pages.num_pages - sess.pages.free_pages
+    sess.fork(np.repeat(np.arange(R), G), R + np.arange(NB), fork_at)
+    fork_pages = sess.pages.num_pages - sess.pages.free_pages - root_pages
+    unshared_pages = int(((fork_at + P - 1) // P).sum())  # the same prefixes copied per branch
+    page_bytes = GR["layers"] * 2 * KV_HEADS * P * HEAD_DIM * 2
+
+    # Branch prefill (timed on its own): 256 tokens per branch, roots sit out.
+    S = GR["prefill"]
+    pre_ids = torch.from_numpy(rng.integers(0, VOCAB, size=(B, S))).to(dev)
+    pre_len = [0] * R + [S] * NB
+    torch.cuda.synchronize()
+    p0, p1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    p0.record()
+    sess.forward(embeds=table[pre_ids], lengths=pre_len)
+    p1.record()
+    torch.cuda.synchronize()
+    prefill_ms = p0.elapsed_time(p1)
+
+    step_len = [0] * R + [1] * NB
+    ids_dev = torch.from_numpy(np.stack([transition_ids(rng, rng.integers(0, 4, size=B), B)
+                                         for _ in range(n_step_calls)])).to(dev)
+    call = [0]
+
+    def device_step():
+        i = call[0]
+        call[0] += 1
+        h = sess.forward(embeds=table[ids_dev[i].long()].view(B, 1, D), lengths=step_len)
+        return head(h[R:, -1]).argmax(-1)
+
+    for _ in range(W):
+        device_step()
+    torch.cuda.synchronize()
+    barrier()
+    torch.cuda.synchronize()
+    clocks = Clocks(local)
+    launches0 = K.launch_count[0]
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(K_steps):
+        device_step()
+    e1.record()
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    launches = K.launch_count[0] - launches0
+    ms = e0.elapsed_time(e1)
+    sess.attn_events = []
+    kv_sum = 0
+    for _ in range(K_steps):
+        kv_sum += int(sess._len.sum()) + NB
+        device_step()
+    torch.cuda.synchronize()
+    attn_ms = [a.elapsed_time(b) for a, b in sess.attn_events]
+    sess.attn_events = None
+
+    h_ids = torch.empty(B, dtype=torch.int32, pin_memory=True)
+    h_act = torch.empty(NB, dtype=torch.int64, pin_memory=True)
+    d_ids = torch.empty(B, dtype=torch.int32, device=dev)
+    act = rng.integers(0, 4, size=B)
+
+    def e2e_step():  # through the public API: ids from pinned host memory, actions read back
+        nonlocal act
+        call[0] += 1
+        h_ids.numpy()[:] = transition_ids(rng, act, B)
+        d_ids.copy_(h_ids, non_blocking=True)
+        h = sess.forward(embeds=table[d_ids.long()].view(B, 1, D), lengths=step_len)
+        h_act.copy_(head(h[R:, -1]).argmax(-1), non_blocking=True)
+        torch.cuda.current_stream().synchronize()
+        act[R:] = h_act.numpy()
+
+    for _ in range(W):
+        e2e_step()
+    torch.cuda.synchronize()
+    barrier()
+    torch.cuda.synchronize()
+    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    f0.record()
+    for _ in range(K_steps):
+        e2e_step()
+    f1.record()
+    torch.cuda.synchronize()
+    e2e_ms = f0.elapsed_time(f1)
+    t = torch.tensor([ms, e2e_ms, prefill_ms], device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_max, e2e_max, pre_max = (float(x) for x in t.tolist())
+    status = _lib.device_status()
+    attn_bytes = kv_sum / K_steps * 2 * KV_HEADS * HEAD_DIM * 2 + 2 * B * HEADS * HEAD_DIM * 2
+    attn_avg_ms = statistics.mean(attn_ms) if attn_ms else float("nan")
+    achieved = attn_bytes / (attn_avg_ms * 1e-3) / 1e9
+    peaks = {}
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            peaks = json.load(f)
+    except (OSError, ValueError):
+        pass
+    peak = float(peaks.get("hbm_gbs", 6650.0))
+    out = None
+    if rank == 0:
+        out = {"metric": "branch env-steps/s in GRPO rollout decode", "unit": "env-steps/s",
+               "value": round(NB * world * K_steps / (ms_max * 1e-3), 1), "n_gpus": world, "steps": K_steps,
+               "warmup": W, "ms_per_step": round(ms_max / K_steps, 4), "higher_is_better": True, "scaling": "weak",
+               "vs_baseline": None, "dtype": "bf16",
+               "data": "synthetic (seeded transition tokens; random-init weights)",
+               "config": grpo_config(world, R),
+               "e2e": {"value": round(NB * world * K_steps / (e2e_max * 1e-3), 1), "unit": "env-steps/s",
+                       "h2d_bytes_per_step": int(B * 4 * world), "d2h_bytes_per_step": int(NB * 8 * world),
+                       "ms_per_step": round(e2e_max / K_steps, 4)},
+               "branch_prefill": {"tokens_per_s": round(NB * S * world / (pre_max * 1e-3), 1),
+                                  "ms": round(pre_max, 3)},
+               "prefix_sharing": {"root_kv_gb": round(root_pages * page_bytes / 1e9, 2),
+                                  "branch_prefix_kv_gb_if_copied": round(unshared_pages * page_bytes / 1e9, 2),
+                                  "branch_prefix_kv_gb_with_sharing": round(fork_pages * page_bytes / 1e9, 2)},
+               "roofline": {"kernel": "split_decode_kernel (K1)", "bound": "hbm", "achieved": round(achieved, 1),
+                            "peak": peak, "peak_source": "measured" if "hbm_gbs" in peaks else "fallback",
+                            "unit": "GB/s", "frac": round(achieved / peak, 4), "traffic": None,
+                            "algorithmic_bytes_per_launch": int(attn_bytes), "avg_launch_ms": round(attn_avg_ms, 5),
+                            "launches_timed": len(attn_ms),
+                            "note": "algorithmic bytes count every branch's whole context; the 16 branches of a "
+                                    "root read the same shared prefix pages back to back and L2 serves the "
+                                    "repeats, so the fraction can exceed 1"},
+               "cpu_baseline": None,
+               "cpu_baseline_note": "not run: one step reads ~90 GB of KV; the decode line's CPU port covers the "
+                                    "same per-token arithmetic",
+               "gpu_launches": int(launches), "clocks": clk, "device_status": status}
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return out
+
+
 def packed_segments(seed, rows=8, row_len=16384, lo=256, hi=4096):
     """Segment lengths of the packed-training workload: per row, lengths
     U[lo, hi] until the row is full, the last one truncated."""
@@ -977,12 +1173,17 @@ def main():
     ap.add_argument("--large-batch", action="store_true",
                     help="time large-batch decode (Llama-3.2-1B arch, 512 envs/GPU, hd 64) instead")
     ap.add_argument("--lb-envs", type=int, default=LB["envs"], help="envs per GPU for --large-batch")
+    ap.add_argument("--grpo", action="store_true",
+                    help="time GRPO branch decode (8-layer Qwen3-0.6B arch, 64 roots x 16 forked branches)")
+    ap.add_argument("--grpo-roots", type=int, default=GR["roots"], help="roots per GPU for --grpo")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
     globals()["ENVS"] = args.envs
     if args.large_batch and args.impl == "ours":
         out = run_large_batch(args)
+    elif args.grpo and args.impl == "ours":
+        out = run_grpo(args)
     elif args.train and args.impl == "ours":
         out = run_train(args)
     elif args.packed_only:
