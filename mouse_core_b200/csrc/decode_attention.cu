@@ -599,7 +599,11 @@ __global__ void __launch_bounds__(160) block_decode_kernel(const __grid_constant
 
 // ------------------------------------------------------------------ host side
 
-size_t decode_chunk_tokens(int head_dim) { return head_dim == 128 ? 1024 : 2048; }
+// Tokens per split-mode work item. Measured on B200 (K1 share of the copy
+// bandwidth): hd 128 decode of 256 rows with U[64,4096] contexts 0.82 at 1024,
+// 0.87 at 2048, 0.86 at 4096; hd 64 with 512 rows log-uniform in [128,16384]
+// 0.76 at 2048, 0.73 at 4096, 0.65 at 8192.
+size_t decode_chunk_tokens(int) { return 2048; }
 
 size_t decode_workspace_layout(int B, int Hkv, int R, int head_dim, int max_kv_len, WorkspaceLayout* lay) {
   const size_t chunk = decode_chunk_tokens(head_dim);

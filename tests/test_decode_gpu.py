@@ -113,8 +113,8 @@ def test_decode_attention_long_rows_split_combine():
     dev = _dev()
     from mouse_core_b200 import kernels as K
 
-    B, Hq, Hkv, hd, page, S = 6, 16, 8, 128, 128, 1
-    lens_after = [4096, 3001, 1, 5000, 2048, 777]
+    B, Hq, Hkv, hd, page, S = 7, 16, 8, 128, 128, 1
+    lens_after = [4096, 3001, 1, 5000, 2048, 777, 9000]
     n_new = [1] * B
     q, kp, vp, bt, q_pos, k_rows, v_rows = _paged_case(B, Hq, Hkv, hd, page, S, lens_after, n_new, 9)
     out = K.decode_attention(q.to(dev), kp.to(dev), vp.to(dev), torch.from_numpy(bt).to(dev),
