@@ -855,8 +855,13 @@ def packed_attention_metric(device, reps=10, rows=8):
             "workload": f"{L} tokens ({rows} x 16384), {len(segs)} segments U[256,4096], 16/8 heads, hd 128, bf16",
             "value": round(tf_all, 1), "unit": "TFLOP/s", "algorithmic_flops_fwd": flops,
             "flops_note": "algorithmic = 4*Hq*hd*sum s(s+1)/2 (unmasked pairs only); bwd counted as 2.5x fwd",
-            "fwd": {"ms": round(ms, 4), "tflops": round(tf, 1), "frac": round(tf / peak, 4)},
+            "peak_note": "frac: of the measured burst bf16 peak; frac_of_sustained: of the cuBLAS rate measured "
+                         "under the same power cap a seconds-long tensor loop meets (the clocks below say which "
+                         "regime this run was in)",
+            "fwd": {"ms": round(ms, 4), "tflops": round(tf, 1), "frac": round(tf / peak, 4),
+                    "frac_of_sustained": round(tf / float(peak_sus), 4) if peak_sus else None},
             "bwd": {"ms": round(ms_bwd, 4), "tflops": round(tf_bwd, 1), "frac": round(tf_bwd / peak, 4),
+                    "frac_of_sustained": round(tf_bwd / float(peak_sus), 4) if peak_sus else None,
                     "path": f"stored dS ({n_pairs} pairs x {Hq} heads x 32 KB = {Hq * n_pairs * 32768 / 2**30:.2f} GiB)"},
             "bwd_recompute": {"ms": round(ms_recompute, 4), "tflops": round(tf_rec, 1),
                               "frac": round(tf_rec / peak, 4)},

@@ -442,3 +442,24 @@ def test_device_step_matches_host_step():
         both(1, [1] * B)
     assert taken[0] >= 140, taken[0]
     assert fast.pages.num_pages > 8 and fast.pages.max_pages > 2  # grew and widened on the way
+
+
+def test_decode_step_meta_reports_rows_past_the_table():
+    """K8 on a row whose next token would land past the block table's width
+    records kDevBadPage and writes no table entry; other rows step normally."""
+    dev = _dev()
+    from mouse_core_b200 import _lib
+    from mouse_core_b200 import kernels as K
+
+    page, width = 64, 2
+    bt = torch.tensor([[5, 6], [7, -1], [8, 9]], dtype=torch.int32, device=dev)
+    kv_len = torch.tensor([70, 64, 128], dtype=torch.int32, device=dev)  # row 2 is full
+    new_page = torch.tensor([-1, 11, 12], dtype=torch.int32, device=dev)
+    q_pos, slot = torch.empty_like(kv_len), torch.empty_like(kv_len)
+    _lib.device_status()  # clear
+    K.decode_step_meta(bt, q_pos, kv_len, slot, page, new_page)
+    assert _lib.device_status() == 3  # kDevBadPage
+    assert bt.cpu().tolist() == [[5, 6], [7, 11], [8, 9]]
+    assert q_pos.cpu().tolist() == [70, 64, 128]
+    assert slot.cpu().tolist() == [6 * page + 6, 11 * page + 0, -1]
+    assert kv_len.cpu().tolist() == [71, 65, 129]

@@ -139,6 +139,9 @@ def _run_bwd(seq, q, k, v, do, dev, stored=False):
     if stored:
         pair_off = K.varlen_pair_offsets(tl, seq.shape[0])
         n_pairs = pair_count(seq)
+        T = (seq.shape[0] + 127) // 128
+        per_tile = np.arange(T) - tl.cpu().numpy() // 128 + 1
+        assert np.array_equal(pair_off.cpu().numpy(), np.concatenate([[0], np.cumsum(per_tile)]))
         assert int(pair_off[-1].item()) == n_pairs
         extra = dict(tile_lo=tl, pair_off=pair_off, n_pairs=n_pairs)
     dq, dk, dv = K.varlen_attention_bwd(qd, kd, vd, out, dod, lse, rs, re, scale, **extra)
