@@ -173,3 +173,59 @@ def test_pair_count_matches_brute_force():
                 brute += bool(((ids[q][:, None] == ids[k][None, :]) & (k[None, :] <= q[:, None])).any())
         assert pair_count(ids) == brute, lens
     assert pair_count(np.zeros(0, dtype=np.int64)) == 0
+
+
+def test_install_patches_and_restores_the_reference_hot_path(monkeypatch):
+    """``install()`` swaps exactly the hot-path functions of an importable
+    ``mouse_core`` (here stand-in modules with the same names) for ours, and
+    ``uninstall()`` puts every original back."""
+    import sys
+    import types
+
+    from mouse_core_b200 import integration, kv_policy, packing
+    from mouse_core_b200.decode import PagedDecodeSession
+
+    def orig(*a, **k):
+        raise AssertionError("original called")
+
+    mods = {}
+    for name in ("mouse_core", "mouse_core.models", "mouse_core.models.backbone", "mouse_core.models.backbone.base",
+                 "mouse_core.models.backbone.flex_train", "mouse_core.models.embedding",
+                 "mouse_core.models.embedding.packing", "mouse_core.models.base", "mouse_core.models.kv_policy"):
+        mods[name] = types.ModuleType(name)
+        monkeypatch.setitem(sys.modules, name, mods[name])
+
+    class Backbone:
+        decode_session = orig
+
+    mods["mouse_core.models.backbone.base"].Backbone = Backbone
+    mods["mouse_core.models.backbone.flex_train"].flex_packed_forward = orig
+    mods["mouse_core.models.embedding.packing"].left_align_content = orig
+    mods["mouse_core.models.base"]._flat_to_batched_left_pad = orig
+    for fn in ("resolve_cache_bounds", "rebuild_starts", "cache_needs_rebuild"):
+        setattr(mods["mouse_core.models.kv_policy"], fn, orig)
+
+    integration.install()
+    try:
+        assert mods["mouse_core.models.embedding.packing"].left_align_content is packing.left_align_content
+        assert mods["mouse_core.models.base"]._flat_to_batched_left_pad is packing.flat_to_batched_left_pad
+        assert mods["mouse_core.models.kv_policy"].cache_needs_rebuild is kv_policy.cache_needs_rebuild
+        from mouse_core_b200.packed import flex_packed_forward
+
+        assert mods["mouse_core.models.backbone.flex_train"].flex_packed_forward is flex_packed_forward
+        assert Backbone.decode_session is not orig
+        try:
+            Backbone().decode_session(batch_size=2, capacity=8)  # no ``model``: the reference's error
+        except NotImplementedError:
+            pass
+        else:
+            raise AssertionError("a backbone without a model must not get a session")
+        assert PagedDecodeSession is not None
+    finally:
+        integration.uninstall()
+    assert Backbone.decode_session is orig
+    assert mods["mouse_core.models.embedding.packing"].left_align_content is orig
+    assert mods["mouse_core.models.base"]._flat_to_batched_left_pad is orig
+    assert mods["mouse_core.models.backbone.flex_train"].flex_packed_forward is orig
+    for fn in ("resolve_cache_bounds", "rebuild_starts", "cache_needs_rebuild"):
+        assert getattr(mods["mouse_core.models.kv_policy"], fn) is orig
