@@ -133,16 +133,21 @@ int mb_page_copy(const void* src_pool, void* dst_pool, const int32_t* src_pages,
                  long long page_elems, mb_stream_t stream);
 
 /* ---------------------------------------------------------------------
- * One decode step's metadata on the device (every row appends one token).
- * Replaces the host-side position and slot bookkeeping of
- * FlexDecodeSession.forward (models/backbone/flex_decode.py:180-195) for the
- * one-token-per-row step: reads each row's current length from kv_len
+ * One decode step's metadata on the device (each row appends at most one
+ * token). Replaces the host-side position and slot bookkeeping of
+ * FlexDecodeSession.forward (models/backbone/flex_decode.py:180-195) for
+ * steps of lengths 0 or 1: reads each row's current length from kv_len
  * [batch] (left there by the previous step), writes q_pos = length, the new
  * token's cache slot (page * page_size + offset, looked up in block_table
- * [batch, max_pages]) and kv_len = length + 1. new_page [batch] (or NULL)
- * holds the id of a page a row's token opens (else -1); it is written into
- * the block table first. All int32, device memory.
+ * [batch, max_pages]) and kv_len = length + 1. new_page [batch] (or NULL:
+ * every row -1) holds a code per row: -1 append; a page id >= 0 that the
+ * row's token opens (written into the block table first), with
+ * MB_STEP_RESTART set when the row was emptied (it restarts at length 0 and
+ * the page goes to column 0); -2 the row appends nothing (q_pos =
+ * max(length - 1, 0), slot -1, length kept); -3 the row was emptied and
+ * appends nothing (q_pos 0, slot -1, length 0). All int32, device memory.
  * ------------------------------------------------------------------- */
+#define MB_STEP_RESTART (1 << 30)
 int mb_decode_step_meta(int batch, int max_pages, int page_size, const int32_t* new_page, int32_t* block_table,
                         int32_t* q_pos, int32_t* kv_len, int32_t* slot, mb_stream_t stream);
 

@@ -123,26 +123,42 @@ cudaError_t launch_page_copy(const __nv_bfloat16* src_pool, __nv_bfloat16* dst_p
   return cudaGetLastError();
 }
 
-// One decode step's metadata on the device (every row appends one token):
-// the current length L = kv_len[b] (left there by the previous step), the
-// new token's position L, its cache slot from the block table, and the new
-// length L + 1. A row whose token opens a page gets that page's id in
-// new_page[b] (else -1), which is written into the block table first. A
-// column past the table's width is reported (kDevBadPage) and the token is
+constexpr int kStepRestart = 1 << 30;  // decode_step_meta code flag: the row restarts at length 0
+
+// One decode step's metadata on the device (each row appends at most one
+// token): the current length L = kv_len[b] (left there by the previous step),
+// the new token's position L, its cache slot from the block table, and the
+// new length L + 1. code[b] (or -1 for every row when code is NULL):
+//   -1  append; the token's page is already in the table;
+//   >=0 append; the token opens page code[b], written into the table first;
+//       with bit 30 set the row was emptied: it restarts at length 0 and the
+//       page (the low bits) goes to column 0;
+//   -2  append nothing (position max(L - 1, 0), no slot, length kept);
+//   -3  the row was emptied and appends nothing (position 0, length 0).
+// A column past the table's width is reported (kDevBadPage) and the token is
 // not cached (slot -1).
-__global__ void decode_step_meta_kernel(int B, int width, int page_size, const int32_t* __restrict__ new_page,
+__global__ void decode_step_meta_kernel(int B, int width, int page_size, const int32_t* __restrict__ code,
                                         int32_t* __restrict__ block_table, int32_t* __restrict__ q_pos,
                                         int32_t* __restrict__ kv_len, int32_t* __restrict__ slot) {
   const int b = blockIdx.x * blockDim.x + threadIdx.x;
   if (b >= B) return;
-  const int L = kv_len[b];
+  const int c = code ? code[b] : -1;
+  int L = kv_len[b];
+  if (c == -2 || c == -3) {
+    if (c == -3) L = 0;
+    q_pos[b] = max(L - 1, 0);
+    slot[b] = -1;
+    kv_len[b] = L;
+    return;
+  }
+  if (c >= 0 && (c & kStepRestart)) L = 0;
+  const int np = c >= 0 ? (c & ~kStepRestart) : -1;
   const int col = L / page_size;
   int s = -1;
   if (L < 0 || col >= width) {
     report(kDevBadPage);
   } else {
     int32_t* entry = block_table + (size_t)b * width + col;
-    const int np = new_page ? new_page[b] : -1;
     if (np >= 0) *entry = np;
     s = (np >= 0 ? np : *entry) * page_size + L % page_size;
   }

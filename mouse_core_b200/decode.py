@@ -46,6 +46,11 @@ def _round_up(value: int, multiple: int) -> int:
     return -(-value // multiple) * multiple
 
 
+# mb_decode_step_meta code flag (MB_STEP_RESTART): the row was emptied and its
+# token restarts it at length 0, opening the page in the low bits at column 0.
+_STEP_RESTART = 1 << 30
+
+
 class _LayerWeights:
     """Per-layer weights; QKV and gate/up are concatenated once per weight
     version so each runs as one GEMM."""
@@ -142,12 +147,17 @@ class PagedDecodeSession:
         # Single-token steps (S = 1, the steady state of env stepping) replay a
         # CUDA graph of the whole layer stack after one eager warm-up call.
         self.use_graphs = True
-        # One-token steps between replays: positions, slots and lengths are
-        # made on the device from the previous step's lengths (K8,
-        # mb_decode_step_meta), fed only with the pages the step opens; the
-        # host keeps its page table and lengths in step with it.
+        # Steps of at most one token per row between replays: positions,
+        # slots and lengths are made on the device from the previous step's
+        # lengths (K8, mb_decode_step_meta), fed only with one code per row
+        # (pages opened, rows sitting out, rows emptied since); the host keeps
+        # its page table and lengths in step with it.
         self.use_device_step = True
         self._device_step_ok = False  # device metadata is the one-token layout of the host's state
+        # Rows emptied by reset_rows while the device path stays valid: their
+        # device table rows and lengths are stale until a step restarts them
+        # (or a host-path call re-sends the whole table).
+        self._pending_reset = np.zeros(self.B, dtype=bool)
         self._new_page_dev = torch.full((self.B,), -1, dtype=torch.int32, device=self.device)
         self._step_args: tuple | None = None  # pointers of the captured graph's metadata views
         self._graph = None
@@ -181,9 +191,15 @@ class PagedDecodeSession:
     def reset_rows(self, rows) -> None:
         """Empty ``rows`` (their pages return to the pool); the next call
         decodes them from position 0, as a fresh session would."""
-        self._device_step_ok = False
-        self.pages.release_rows(rows)
-        self._len[np.atleast_1d(np.asarray(rows, dtype=np.int64))] = 0
+        r = np.atleast_1d(np.asarray(rows, dtype=np.int64))
+        table_synced = not self.pages.dirty
+        self.pages.release_rows(r)
+        self._len[r] = 0
+        if self._device_step_ok and table_synced:
+            self.pages.dirty = False  # only these rows differ; the next step restarts them
+            self._pending_reset[r] = True
+        else:
+            self._device_step_ok = False
 
     def fork(self, src_rows, dst_rows, prefix_lengths=None) -> None:
         """Start rows ``dst_rows`` as branches of ``src_rows``: branch ``i``
@@ -296,7 +312,7 @@ class PagedDecodeSession:
             if real.any():
                 slot[real] = self.pages.slots(rows[real], pos[real])
 
-        bt_changed = self.pages.dirty
+        bt_changed = self.pages.dirty or bool(self._pending_reset.any())
         width = self.pages.max_pages
         n_meta = 2 * B * S + B + (B * width if bt_changed else 0)
         buf, i = self._stage(n_meta)
@@ -328,35 +344,57 @@ class PagedDecodeSession:
                 self._bt_dev = torch.empty((B, width), dtype=torch.int32, device=self.device)
             self._bt_dev.copy_(dev[2 * B * S + B:n_meta].view(B, width))
             self.pages.dirty = False
+            self._pending_reset[:] = False
         self._len = new_len
         self._device_step_ok = S == 1
         return q_pos_d, kv_len_d, slot_d, int(new_len.max()) if B else 0
 
     def _device_step(self, lengths) -> bool:
-        """A one-token step whose metadata the device makes (K8): the host
-        only opens the pages this step's tokens start and uploads their ids.
-        False (nothing changed) when the host path must run instead: not every
-        row appends one token, the device metadata is stale, or the new pages
+        """A step of at most one token per row whose metadata the device makes
+        (K8): the host only opens the pages this step's tokens start and, when
+        anything but a plain append happens, uploads one code per row. False
+        (nothing changed) when the host path must run instead: a row appends
+        more than one token, the device metadata is stale, or the new pages
         would not fit the pool or the block table's width."""
         B, P, pages = self.B, self.page_size, self.pages
         if not self._device_step_ok or pages.dirty:
             return False
+        n = None  # every row appends one token
         if isinstance(lengths, list):
-            if len(lengths) != B or lengths.count(1) != B:
+            if len(lengths) != B:
                 return False
+            if lengths.count(1) != B:
+                if lengths.count(1) + lengths.count(0) != B:
+                    return False
+                n = np.asarray(lengths, dtype=np.int64)
         else:
-            n = np.asarray(lengths).reshape(-1)
-            if n.shape[0] != B or not bool((n == 1).all()):
+            a = np.asarray(lengths).reshape(-1)
+            if a.shape[0] != B or not bool(((a == 0) | (a == 1)).all()):
                 return False
-        opening = np.flatnonzero(pages.npages * P <= self._len)
+            if not bool((a == 1).all()):
+                n = a.astype(np.int64)
+        grows = pages.npages * P <= self._len
+        opening = np.flatnonzero(grows if n is None else grows & (n == 1))
         if opening.size:
             if opening.size > pages.free_pages or int(pages.npages[opening].max()) >= pages.max_pages:
                 return False
-            ids = pages.open_pages(opening)
+        pend = self._pending_reset
+        any_pend = bool(pend.any())
+        coded = opening.size > 0 or n is not None or any_pend
+        if coded:
             buf, i = self._stage(B)
             host = buf.numpy()[:B]
             host.fill(-1)
-            host[opening] = ids
+            if n is not None:
+                host[n == 0] = -2
+                if any_pend:
+                    host[pend & (n == 0)] = -3
+            if opening.size:
+                ids = pages.open_pages(opening)
+                if any_pend:
+                    ids = np.where(pend[opening], ids | _STEP_RESTART, ids)
+                host[opening] = ids
+            pend[:] = False
             self._new_page_dev.copy_(buf[:B], non_blocking=True)
             ev = self._staging_ev[i]
             if ev is None:
@@ -366,8 +404,8 @@ class PagedDecodeSession:
             dev = self._meta_dev
             self._step_args = K.decode_step_meta_args(self._bt_dev, dev[:B], dev[B:2 * B], dev[2 * B:3 * B], P,
                                                       self._new_page_dev)
-        K.decode_step_meta_launch(self._step_args, opening.size > 0, torch.cuda.current_stream().cuda_stream)
-        self._len = self._len + 1
+        K.decode_step_meta_launch(self._step_args, coded, torch.cuda.current_stream().cuda_stream)
+        self._len = self._len + (1 if n is None else n)
         return True
 
     @torch.no_grad()

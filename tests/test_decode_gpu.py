@@ -392,10 +392,12 @@ def test_fork_shares_prefix_pages_and_matches_independent_rows():
 
 
 def test_device_step_matches_host_step():
-    """One-token steps whose positions, slots and lengths the device derives
-    (K8) equal the host-prepared steps bit for bit, across page openings, a
-    pool growth, a block-table widening, row resets, a fork and multi-token
-    chunks in between; the page tables stay identical on host and device."""
+    """Steps of at most one token per row whose positions, slots and lengths
+    the device derives (K8) equal the host-prepared steps bit for bit, across
+    page openings, a pool growth, a block-table widening, rows sitting out,
+    rows emptied between steps (restarted by the device step, sitting out,
+    or re-sent by a multi-token chunk), a fork and multi-token chunks; the
+    page tables agree on host and device wherever a row holds pages."""
     dev = _dev()
     from mouse_core_b200.backbone import Qwen3Backbone
 
@@ -426,11 +428,12 @@ def test_device_step_matches_host_step():
         assert fast._len.tolist() == host._len.tolist()
         assert np.array_equal(fast.pages.table, host.pages.table)
         w = fast.pages.max_pages
-        assert np.array_equal(fast._bt_dev[:, :w].cpu().numpy(), fast.pages.table)
+        held = np.arange(w)[None, :] < fast.pages.npages[:, None]  # emptied rows keep stale device entries
+        assert np.array_equal(fast._bt_dev[:, :w].cpu().numpy()[held], fast.pages.table[held])
 
     both(60, rng.integers(1, 61, size=B).tolist())
     for step in range(160):
-        if step == 30:
+        if step == 30:  # emptied, then refilled by a multi-token chunk (host path re-sends the table)
             fast.reset_rows([1, 3])
             host.reset_rows([1, 3])
             both(9, [0, 9, 0, 4, 0, 0])
@@ -438,9 +441,16 @@ def test_device_step_matches_host_step():
             fast.fork([0, 2], [4, 5], [17, 64])
             host.fork([0, 2], [4, 5], [17, 64])
         elif step == 100:
-            both(1, [1, 0, 1, 1, 0, 1])  # a row sitting out goes through the host path
+            both(1, [1, 0, 1, 1, 0, 1])  # rows sitting out
+        elif step in (110, 130):  # emptied between steps: the device step restarts them
+            fast.reset_rows([2, 5])
+            host.reset_rows([2, 5])
+        elif step == 120:  # one emptied row sits out its first step, the other restarts
+            fast.reset_rows([0, 4])
+            host.reset_rows([0, 4])
+            both(1, [0, 1, 1, 1, 1, 1])
         both(1, [1] * B)
-    assert taken[0] >= 140, taken[0]
+    assert taken[0] >= 145, taken[0]
     assert fast.pages.num_pages > 8 and fast.pages.max_pages > 2  # grew and widened on the way
 
 
