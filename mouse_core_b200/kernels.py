@@ -150,9 +150,11 @@ def page_copy(src_pool: torch.Tensor, dst_pool: torch.Tensor, src_pages: torch.T
 def decode_step_meta(block_table: torch.Tensor, q_pos: torch.Tensor, kv_len: torch.Tensor, slot: torch.Tensor,
                      page_size: int, new_page: torch.Tensor | None = None) -> None:
     """In place: one decode step's ``q_pos``, ``slot`` and ``kv_len`` (int32
-    ``[B]``) from the current ``kv_len`` and ``block_table [B, max_pages]``,
-    after writing ``new_page[b] >= 0`` (pages the step's tokens open) into
-    the table."""
+    ``[B]``) from the current ``kv_len`` and ``block_table [B, max_pages]``.
+    ``new_page`` holds one code per row (``None``: every row appends): -1
+    append; a page id the row's token opens (written into the table first),
+    with bit 30 set for a row emptied since (it restarts at length 0); -2 the
+    row sits out; -3 the row was emptied and sits out."""
     for name, t in (("block_table", block_table), ("q_pos", q_pos), ("kv_len", kv_len), ("slot", slot)):
         _need(t, name, torch.int32)
     if new_page is not None:
