@@ -290,9 +290,20 @@ int mb_segment_meta(const int64_t* sequence_ids, int L, int tile, int64_t* posit
  *   mb_qkv_heads_bwd_scratch_floats(L, head_dim) floats.
  * mb_silu_mul_bwd: gradient of h = silu(gate) * up over gate_up [rows, 2I]:
  *   dgate_up[:, :I] = dh * up * silu'(gate), dgate_up[:, I:] = dh * silu(gate).
+ * mb_add_rmsnorm_fwd: the decoder layer's residual add fused in front of the
+ *   norm: sum_out = bf16(x + residual) (the module's add), then y and rstd of
+ *   mb_rmsnorm_fwd over sum_out.
+ * mb_rmsnorm_bwd_add: mb_rmsnorm_bwd with dsum, the gradient that reaches
+ *   the normalised input along the residual path, added into dx before its
+ *   one rounding (dx is then the gradient of both x and residual).
  * ------------------------------------------------------------------- */
 int mb_rmsnorm_fwd(const void* x, const void* weight, float eps, int rows, int dim, void* y, float* rstd,
                    mb_stream_t stream);
+int mb_add_rmsnorm_fwd(const void* x, const void* residual, const void* weight, float eps, int rows, int dim,
+                       void* sum_out, void* y, float* rstd, mb_stream_t stream);
+int mb_rmsnorm_bwd_add(const void* dy, const void* x, const void* weight, const float* rstd, const void* dsum,
+                       int rows, int dim, void* dx, float* dweight, float* scratch, size_t scratch_floats,
+                       mb_stream_t stream);
 size_t mb_rmsnorm_bwd_scratch_floats(int rows, int dim);
 int mb_rmsnorm_bwd(const void* dy, const void* x, const void* weight, const float* rstd, int rows, int dim, void* dx,
                    float* dweight, float* scratch, size_t scratch_floats, mb_stream_t stream);

@@ -44,6 +44,8 @@ PROTOTYPES = {
                                                 _vp, _vp, _vp, _c_int, _c_float, _vp, _vp, _vp, _vp, _vp, _c_size,
                                                 _vp]),
     "mb_rmsnorm_fwd": (_c_int, [_vp, _vp, _c_float, _c_int, _c_int, _vp, _vp, _vp]),
+    "mb_add_rmsnorm_fwd": (_c_int, [_vp, _vp, _vp, _c_float, _c_int, _c_int, _vp, _vp, _vp, _vp]),
+    "mb_rmsnorm_bwd_add": (_c_int, [_vp, _vp, _vp, _vp, _vp, _c_int, _c_int, _vp, _vp, _vp, _c_size, _vp]),
     "mb_rmsnorm_bwd_scratch_floats": (_c_size, [_c_int, _c_int]),
     "mb_rmsnorm_bwd": (_c_int, [_vp, _vp, _vp, _vp, _c_int, _c_int, _vp, _vp, _vp, _c_size, _vp]),
     "mb_qkv_heads_fwd": (_c_int, [_vp, _c_ll, _c_int, _c_int, _c_int, _c_int, _vp, _vp, _c_float, _c_float,

@@ -464,9 +464,24 @@ int mb_rmsnorm_fwd(const void* x, const void* weight, float eps, int rows, int d
   if (!x || !weight || !y || !rstd) return fail(MB_ERR_INVALID_ARG, "a required pointer is NULL");
   if (!aligned(x, 16) || !aligned(weight, 16) || !aligned(y, 16))
     return fail(MB_ERR_INVALID_ARG, "x, weight and y must be 16-byte aligned");
-  cudaError_t e = mb::launch_rmsnorm_fwd(static_cast<const __nv_bfloat16*>(x), static_cast<const __nv_bfloat16*>(weight),
-                                         eps, rows, dim, static_cast<__nv_bfloat16*>(y), rstd, (cudaStream_t)stream);
+  cudaError_t e = mb::launch_rmsnorm_fwd(static_cast<const __nv_bfloat16*>(x), nullptr,
+                                         static_cast<const __nv_bfloat16*>(weight), eps, rows, dim, nullptr,
+                                         static_cast<__nv_bfloat16*>(y), rstd, (cudaStream_t)stream);
   return e == cudaSuccess ? MB_OK : cuda_fail(e, "rmsnorm fwd launch");
+}
+
+int mb_add_rmsnorm_fwd(const void* x, const void* residual, const void* weight, float eps, int rows, int dim,
+                       void* sum_out, void* y, float* rstd, mb_stream_t stream) {
+  if (int rc = check_norm_dim(rows, dim)) return rc;
+  if (rows == 0) return MB_OK;
+  if (!x || !residual || !weight || !sum_out || !y || !rstd) return fail(MB_ERR_INVALID_ARG, "a required pointer is NULL");
+  if (!aligned(x, 16) || !aligned(residual, 16) || !aligned(weight, 16) || !aligned(sum_out, 16) || !aligned(y, 16))
+    return fail(MB_ERR_INVALID_ARG, "x, residual, weight, sum_out and y must be 16-byte aligned");
+  cudaError_t e = mb::launch_rmsnorm_fwd(static_cast<const __nv_bfloat16*>(x), static_cast<const __nv_bfloat16*>(residual),
+                                         static_cast<const __nv_bfloat16*>(weight), eps, rows, dim,
+                                         static_cast<__nv_bfloat16*>(sum_out), static_cast<__nv_bfloat16*>(y), rstd,
+                                         (cudaStream_t)stream);
+  return e == cudaSuccess ? MB_OK : cuda_fail(e, "add rmsnorm fwd launch");
 }
 
 size_t mb_rmsnorm_bwd_scratch_floats(int rows, int dim) {
@@ -475,8 +490,11 @@ size_t mb_rmsnorm_bwd_scratch_floats(int rows, int dim) {
   return (size_t)mb::rmsnorm_bwd_partials(rows, dim) * (size_t)dim;
 }
 
-int mb_rmsnorm_bwd(const void* dy, const void* x, const void* weight, const float* rstd, int rows, int dim, void* dx,
-                   float* dweight, float* scratch, size_t scratch_floats, mb_stream_t stream) {
+namespace {
+
+int rmsnorm_bwd_common(const void* dy, const void* x, const void* weight, const float* rstd, const void* dsum,
+                       int rows, int dim, void* dx, float* dweight, float* scratch, size_t scratch_floats,
+                       mb_stream_t stream) {
   if (int rc = check_norm_dim(rows, dim)) return rc;
   if (!dweight) return fail(MB_ERR_INVALID_ARG, "dweight is NULL");
   if (rows > 0) {
@@ -486,10 +504,26 @@ int mb_rmsnorm_bwd(const void* dy, const void* x, const void* weight, const floa
     if (!aligned(dy, 16) || !aligned(x, 16) || !aligned(weight, 16) || !aligned(dx, 16))
       return fail(MB_ERR_INVALID_ARG, "dy, x, weight and dx must be 16-byte aligned");
   }
+  if (dsum && !aligned(dsum, 16)) return fail(MB_ERR_INVALID_ARG, "dsum must be 16-byte aligned");
   cudaError_t e = mb::launch_rmsnorm_bwd(static_cast<const __nv_bfloat16*>(dy), static_cast<const __nv_bfloat16*>(x),
-                                         static_cast<const __nv_bfloat16*>(weight), rstd, rows, dim,
+                                         static_cast<const __nv_bfloat16*>(weight), rstd,
+                                         static_cast<const __nv_bfloat16*>(dsum), rows, dim,
                                          static_cast<__nv_bfloat16*>(dx), scratch, dweight, (cudaStream_t)stream);
   return e == cudaSuccess ? MB_OK : cuda_fail(e, "rmsnorm bwd launch");
+}
+
+}  // namespace
+
+int mb_rmsnorm_bwd(const void* dy, const void* x, const void* weight, const float* rstd, int rows, int dim, void* dx,
+                   float* dweight, float* scratch, size_t scratch_floats, mb_stream_t stream) {
+  return rmsnorm_bwd_common(dy, x, weight, rstd, nullptr, rows, dim, dx, dweight, scratch, scratch_floats, stream);
+}
+
+int mb_rmsnorm_bwd_add(const void* dy, const void* x, const void* weight, const float* rstd, const void* dsum,
+                       int rows, int dim, void* dx, float* dweight, float* scratch, size_t scratch_floats,
+                       mb_stream_t stream) {
+  if (rows > 0 && !dsum) return fail(MB_ERR_INVALID_ARG, "dsum is NULL");
+  return rmsnorm_bwd_common(dy, x, weight, rstd, dsum, rows, dim, dx, dweight, scratch, scratch_floats, stream);
 }
 
 int mb_qkv_heads_fwd(const void* qkv, long long qkv_row_stride, int L, int q_heads, int kv_heads, int head_dim,

@@ -120,12 +120,13 @@ cudaError_t launch_left_align(const void* emb, int B, int L, int row_bytes, cons
                               int64_t* out_idx, cudaStream_t stream);
 
 // Training element-wise kernels (train_elementwise.cu).
-cudaError_t launch_rmsnorm_fwd(const __nv_bfloat16* x, const __nv_bfloat16* w, float eps, int rows, int D,
-                               __nv_bfloat16* y, float* rstd, cudaStream_t stream);
+cudaError_t launch_rmsnorm_fwd(const __nv_bfloat16* x, const __nv_bfloat16* res, const __nv_bfloat16* w, float eps,
+                               int rows, int D, __nv_bfloat16* sum, __nv_bfloat16* y, float* rstd,
+                               cudaStream_t stream);
 int rmsnorm_bwd_partials(int rows, int D);
 cudaError_t launch_rmsnorm_bwd(const __nv_bfloat16* dy, const __nv_bfloat16* x, const __nv_bfloat16* w,
-                               const float* rstd, int rows, int D, __nv_bfloat16* dx, float* partial, float* dw,
-                               cudaStream_t stream);
+                               const float* rstd, const __nv_bfloat16* dsum, int rows, int D, __nv_bfloat16* dx,
+                               float* partial, float* dw, cudaStream_t stream);
 int qkv_heads_bwd_partials(int L, int HD);
 cudaError_t launch_qkv_heads_fwd(const __nv_bfloat16* qkv, long long xs, int L, int Hq, int Hkv, int HD,
                                  const __nv_bfloat16* qw, const __nv_bfloat16* kw, float q_eps, float k_eps,

@@ -47,7 +47,9 @@ static int resident_blocks(K kernel, int threads, int smem) {
 // 8 contiguous elements (D a multiple of 256, at most 2048).
 template <int NCH>
 __global__ void __launch_bounds__(256) rmsnorm_fwd_kernel(const __nv_bfloat16* __restrict__ x,
+                                                          const __nv_bfloat16* __restrict__ res,
                                                           const __nv_bfloat16* __restrict__ w, float eps, int rows,
+                                                          __nv_bfloat16* __restrict__ sum,
                                                           __nv_bfloat16* __restrict__ y, float* __restrict__ rstd) {
   constexpr int D = NCH * 256;
   const int lane = threadIdx.x & 31;
@@ -58,7 +60,19 @@ __global__ void __launch_bounds__(256) rmsnorm_fwd_kernel(const __nv_bfloat16* _
     float ss = 0.f;
 #pragma unroll
     for (int c = 0; c < NCH; ++c) {
+      const size_t off = (size_t)row * D + c * 256 + lane * 8;
       xv[c] = *reinterpret_cast<const uint4*>(xr + c * 256 + lane * 8);
+      if (res != nullptr) {  // the residual add, rounded to bf16 as the module's add is
+        const uint4 rv = *reinterpret_cast<const uint4*>(res + off);
+        uint32_t* a = reinterpret_cast<uint32_t*>(&xv[c]);
+        const uint32_t* b = reinterpret_cast<const uint32_t*>(&rv);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const float2 fa = unpack_bf16x2(a[i]), fb = unpack_bf16x2(b[i]);
+          a[i] = pack_bf16x2(fa.x + fb.x, fa.y + fb.y);
+        }
+        *reinterpret_cast<uint4*>(sum + off) = xv[c];
+      }
       const uint32_t* u = reinterpret_cast<const uint32_t*>(&xv[c]);
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
@@ -97,7 +111,8 @@ template <int NCH>
 __global__ void __launch_bounds__(kNormBwdWarps * 32) rmsnorm_bwd_kernel(const __nv_bfloat16* __restrict__ dy,
                                                           const __nv_bfloat16* __restrict__ x,
                                                           const __nv_bfloat16* __restrict__ w,
-                                                          const float* __restrict__ rstd, int rows,
+                                                          const float* __restrict__ rstd,
+                                                          const __nv_bfloat16* __restrict__ dsum, int rows,
                                                           __nv_bfloat16* __restrict__ dx,
                                                           float* __restrict__ partial) {
   constexpr int D = NCH * 256;
@@ -155,10 +170,13 @@ __global__ void __launch_bounds__(kNormBwdWarps * 32) rmsnorm_bwd_kernel(const _
       const float2* wf = reinterpret_cast<const float2*>(wsm + c * 256 + lane * 8);
       uint4 o;
       uint32_t* ou = reinterpret_cast<uint32_t*>(&o);
+      uint4 sv = make_uint4(0, 0, 0, 0);  // gradient reaching the normalised input directly (residual path)
+      if (dsum != nullptr) sv = *reinterpret_cast<const uint4*>(dsum + (size_t)row * D + c * 256 + lane * 8);
+      const uint32_t* su = reinterpret_cast<const uint32_t*>(&sv);
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
-        const float2 d2 = unpack_bf16x2(du[i]), x2 = unpack_bf16x2(xu[i]), w2 = wf[i];
-        ou[i] = pack_bf16x2(r * (d2.x * w2.x - x2.x * r * dot), r * (d2.y * w2.y - x2.y * r * dot));
+        const float2 d2 = unpack_bf16x2(du[i]), x2 = unpack_bf16x2(xu[i]), w2 = wf[i], s2 = unpack_bf16x2(su[i]);
+        ou[i] = pack_bf16x2(r * (d2.x * w2.x - x2.x * r * dot) + s2.x, r * (d2.y * w2.y - x2.y * r * dot) + s2.y);
       }
       *reinterpret_cast<uint4*>(dx + (size_t)row * D + c * 256 + lane * 8) = o;
     }
@@ -237,11 +255,12 @@ static int norm_bwd_blocks(int rows, int D) {
     default: return cudaErrorInvalidValue; \
   }
 
-cudaError_t launch_rmsnorm_fwd(const __nv_bfloat16* x, const __nv_bfloat16* w, float eps, int rows, int D,
-                               __nv_bfloat16* y, float* rstd, cudaStream_t stream) {
+cudaError_t launch_rmsnorm_fwd(const __nv_bfloat16* x, const __nv_bfloat16* res, const __nv_bfloat16* w, float eps,
+                               int rows, int D, __nv_bfloat16* sum, __nv_bfloat16* y, float* rstd,
+                               cudaStream_t stream) {
   if (rows <= 0) return cudaSuccess;
   const int blocks = norm_blocks(rows);
-#define MB_FWD(N) rmsnorm_fwd_kernel<N><<<blocks, 256, 0, stream>>>(x, w, eps, rows, y, rstd)
+#define MB_FWD(N) rmsnorm_fwd_kernel<N><<<blocks, 256, 0, stream>>>(x, res, w, eps, rows, sum, y, rstd)
   MB_NORM_DISPATCH(D / 256, MB_FWD)
 #undef MB_FWD
   return cudaGetLastError();
@@ -250,8 +269,8 @@ cudaError_t launch_rmsnorm_fwd(const __nv_bfloat16* x, const __nv_bfloat16* w, f
 int rmsnorm_bwd_partials(int rows, int D) { return norm_bwd_blocks(rows, D); }
 
 cudaError_t launch_rmsnorm_bwd(const __nv_bfloat16* dy, const __nv_bfloat16* x, const __nv_bfloat16* w,
-                               const float* rstd, int rows, int D, __nv_bfloat16* dx, float* partial, float* dw,
-                               cudaStream_t stream) {
+                               const float* rstd, const __nv_bfloat16* dsum, int rows, int D, __nv_bfloat16* dx,
+                               float* partial, float* dw, cudaStream_t stream) {
   if (rows <= 0) {
     cudaMemsetAsync(dw, 0, sizeof(float) * D, stream);
     return cudaGetLastError();
@@ -262,7 +281,7 @@ cudaError_t launch_rmsnorm_bwd(const __nv_bfloat16* dy, const __nv_bfloat16* x, 
 #define MB_BWD(N)                                                                                          \
   do {                                                                                                     \
     e = cudaFuncSetAttribute(rmsnorm_bwd_kernel<N>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);  \
-    if (e == cudaSuccess) rmsnorm_bwd_kernel<N><<<blocks, kNormBwdWarps * 32, smem, stream>>>(dy, x, w, rstd, rows, dx, partial); \
+    if (e == cudaSuccess) rmsnorm_bwd_kernel<N><<<blocks, kNormBwdWarps * 32, smem, stream>>>(dy, x, w, rstd, dsum, rows, dx, partial); \
   } while (0)
   MB_NORM_DISPATCH(D / 256, MB_BWD)
 #undef MB_BWD

@@ -374,11 +374,34 @@ def rmsnorm_fwd(x: torch.Tensor, weight: torch.Tensor, eps: float):
     return y, rstd
 
 
-def rmsnorm_bwd(dy: torch.Tensor, x: torch.Tensor, weight: torch.Tensor, rstd: torch.Tensor):
-    """``(dx bf16, dweight f32)`` of ``rmsnorm_fwd``."""
+def add_rmsnorm_fwd(x: torch.Tensor, residual: torch.Tensor, weight: torch.Tensor, eps: float):
+    """``(sum, y, rstd)``: ``sum = bf16(x + residual)``, then ``rmsnorm_fwd(sum)``."""
+    for name, t in (("x", x), ("residual", residual), ("weight", weight)):
+        _need(t, name, BF16)
+    if residual.shape != x.shape:
+        raise ValueError("residual must match x")
+    D = x.shape[-1]
+    rows = x.numel() // D
+    total = torch.empty_like(x)
+    y = torch.empty_like(x)
+    rstd = torch.empty(rows, dtype=torch.float32, device=x.device)
+    _lib.call("mb_add_rmsnorm_fwd", _p(x), _p(residual), _p(weight), float(eps), rows, D, _p(total), _p(y), _p(rstd),
+              _stream(x))
+    _count()
+    return total, y, rstd
+
+
+def rmsnorm_bwd(dy: torch.Tensor, x: torch.Tensor, weight: torch.Tensor, rstd: torch.Tensor,
+                dsum: torch.Tensor | None = None):
+    """``(dx bf16, dweight f32)`` of ``rmsnorm_fwd``; with ``dsum`` (the
+    gradient reaching ``x`` along a residual path) added into ``dx``."""
     for name, t in (("dy", dy), ("x", x), ("weight", weight)):
         _need(t, name, BF16)
     _need(rstd, "rstd", torch.float32)
+    if dsum is not None:
+        _need(dsum, "dsum", BF16)
+        if dsum.shape != x.shape:
+            raise ValueError("dsum must match x")
     D = x.shape[-1]
     rows = x.numel() // D
     if dy.shape != x.shape or rstd.numel() != rows:
@@ -387,8 +410,12 @@ def rmsnorm_bwd(dy: torch.Tensor, x: torch.Tensor, weight: torch.Tensor, rstd: t
     dw = torch.empty(D, dtype=torch.float32, device=x.device)
     n = int(_lib.load().mb_rmsnorm_bwd_scratch_floats(rows, D))
     scratch = torch.empty(max(n, 1), dtype=torch.float32, device=x.device)
-    _lib.call("mb_rmsnorm_bwd", _p(dy), _p(x), _p(weight), _p(rstd), rows, D, _p(dx), _p(dw), _p(scratch), n,
-              _stream(x))
+    if dsum is None:
+        _lib.call("mb_rmsnorm_bwd", _p(dy), _p(x), _p(weight), _p(rstd), rows, D, _p(dx), _p(dw), _p(scratch), n,
+                  _stream(x))
+    else:
+        _lib.call("mb_rmsnorm_bwd_add", _p(dy), _p(x), _p(weight), _p(rstd), _p(dsum), rows, D, _p(dx), _p(dw),
+                  _p(scratch), n, _stream(x))
     _count(2)
     return dx, dw
 

@@ -144,6 +144,29 @@ class _RMSNorm(torch.autograd.Function):
         return dx, dw.to(weight.dtype), None
 
 
+class _AddRMSNorm(torch.autograd.Function):
+    """``(s, y)``: ``s = bf16(x + residual)`` (the decoder layer's residual
+    add) and ``y = RMSNorm(s)`` in one pass (K4); the backward adds the
+    gradient reaching ``s`` along the residual path into the norm's input
+    gradient in the same pass."""
+
+    @staticmethod
+    def forward(ctx, x, residual, weight, eps):
+        ctx.set_materialize_grads(False)
+        total, y, rstd = K.add_rmsnorm_fwd(x.contiguous(), residual.contiguous(), weight, eps)
+        ctx.save_for_backward(total, weight, rstd)
+        return total, y
+
+    @staticmethod
+    def backward(ctx, dtotal, dy):
+        total, weight, rstd = ctx.saved_tensors
+        if dy is None:
+            return dtotal, dtotal, None, None
+        dx, dw = K.rmsnorm_bwd(dy.contiguous(), total, weight, rstd,
+                               None if dtotal is None else dtotal.contiguous())
+        return dx, dx, dw.to(weight.dtype), None
+
+
 class _QKVHeads(torch.autograd.Function):
     """Split a fused QKV projection ``[L, (Hq + 2 Hkv) hd]`` into attention
     inputs in one pass: q and k through the per-head RMSNorm (when the model
@@ -179,13 +202,26 @@ class _SiluMul(torch.autograd.Function):
         return K.silu_mul_bwd(gate_up, dh.contiguous())
 
 
+def _k4_norm(module, x) -> bool:
+    D = x.shape[-1]
+    return hasattr(module, "variance_epsilon") and D % 256 == 0 and D <= 2048
+
+
 def _norm(module, x):
     """The model's RMSNorm through K4 when its width is supported (an
     ``nn.Identity`` final norm, as the backbones install, stays as is)."""
-    D = x.shape[-1]
-    if hasattr(module, "variance_epsilon") and D % 256 == 0 and D <= 2048:
+    if _k4_norm(module, x):
         return _RMSNorm.apply(x, module.weight, float(module.variance_epsilon))
     return module(x)
+
+
+def _add_norm(module, residual, delta):
+    """``(h, norm(h))`` for ``h = residual + delta``: one K4 pass when the
+    norm is a supported RMSNorm, else the add and the module."""
+    if _k4_norm(module, residual):
+        return _AddRMSNorm.apply(delta, residual, module.weight, float(module.variance_epsilon))
+    h = residual + delta
+    return h, _norm(module, h)
 
 
 def _fused_attention_inputs(attn):
@@ -236,9 +272,13 @@ def flex_packed_forward(*, model: torch.nn.Module, embeds: torch.Tensor, sequenc
 
     h = x
     hiddens = []
+    pending = None  # the last MLP output, not yet added to h (fused into the next norm)
     for layer in hf.layers:
+        if pending is None:
+            hn = _norm(layer.input_layernorm, h)
+        else:
+            h, hn = _add_norm(layer.input_layernorm, h, pending)
         residual = h
-        hn = _norm(layer.input_layernorm, h)
         attn = layer.self_attn
         q_norm = getattr(attn, "q_norm", None)
         if _fused_attention_inputs(attn):
@@ -261,17 +301,21 @@ def flex_packed_forward(*, model: torch.nn.Module, embeds: torch.Tensor, sequenc
             q = q * c + _rotate_half(q) * s_
             k = k * c + _rotate_half(k) * s_
         o = layout.attend(q, k, v, float(attn.scaling))
-        h = residual + attn.o_proj(o.reshape(L, n_heads * hd))
         mlp = layer.mlp
-        hn = _norm(layer.post_attention_layernorm, h)
+        h, hn = _add_norm(layer.post_attention_layernorm, residual, attn.o_proj(o.reshape(L, n_heads * hd)))
         if _fused_mlp(mlp, cfg):
             gate_up = torch.nn.functional.linear(hn, torch.cat((mlp.gate_proj.weight, mlp.up_proj.weight), dim=0))
-            h = h + mlp.down_proj(_SiluMul.apply(gate_up))
+            pending = mlp.down_proj(_SiluMul.apply(gate_up))
         else:
-            h = h + mlp(hn)
+            pending = mlp(hn)
         if output_hidden_states:
+            h = h + pending
+            pending = None
             hiddens.append(h)
-    h = _norm(hf.norm, h)
+    if pending is None:
+        h = _norm(hf.norm, h)
+    else:
+        h = _add_norm(hf.norm, h, pending)[1]
     if output_hidden_states:
         return h, tuple(hiddens)
     return h

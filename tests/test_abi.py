@@ -131,3 +131,12 @@ def test_glue_argument_rules(lib):
     assert lib.mb_flat_scatter(None, 0, 16, None, None, 0, 0, None, None) == 0  # nothing to write
     assert lib.mb_left_align(p, 2, 3, 16, p, 0, p, p, None) == 1  # needs a last index column
     assert lib.mb_left_align(None, 0, 3, 16, None, 1, None, None, None) == 0
+
+
+def test_add_rmsnorm_argument_rules(lib):
+    p = ctypes.c_void_p(4096)
+    assert lib.mb_add_rmsnorm_fwd(p, p, p, 1e-6, 4, 1000, p, p, p, None) == 2  # width
+    assert lib.mb_add_rmsnorm_fwd(p, None, p, 1e-6, 4, 1024, p, p, p, None) == 1
+    assert lib.mb_add_rmsnorm_fwd(None, None, None, 1e-6, 0, 1024, None, None, None, None) == 0
+    assert lib.mb_rmsnorm_bwd_add(p, p, p, p, None, 4, 1024, p, p, p, 1 << 20, None) == 1
+    assert b"dsum" in lib.mb_last_error()

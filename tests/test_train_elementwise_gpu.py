@@ -68,6 +68,39 @@ def test_rmsnorm_fwd_bwd(rows, dim):
     assert _rel(dw, wf.grad) < 1e-2
 
 
+@pytest.mark.parametrize("rows,dim", [(1, 256), (777, 1024), (300, 2048)])
+def test_add_rmsnorm_fwd_bwd(rows, dim):
+    """The residual add fused in front of the norm: the sum equals the bf16
+    add bit for bit, the norm follows the module's rounding; the backward with
+    the residual-path gradient equals fp32 autograd of sum -> (sum, norm)."""
+    dev = _dev()
+    from mouse_core_b200 import kernels as K
+    from transformers.models.qwen3.modeling_qwen3 import Qwen3RMSNorm
+
+    g = torch.Generator(device="cpu").manual_seed(rows * 7 + dim)
+    a = (torch.randn(rows, dim, generator=g) * 2).bfloat16().to(dev)
+    b = (torch.randn(rows, dim, generator=g) * 2).bfloat16().to(dev)
+    w = (1 + 0.2 * torch.randn(dim, generator=g)).bfloat16().to(dev)
+    dy = torch.randn(rows, dim, generator=g).bfloat16().to(dev)
+    ds = torch.randn(rows, dim, generator=g).bfloat16().to(dev)
+    total, y, rstd = K.add_rmsnorm_fwd(a, b, w, 1e-6)
+    assert torch.equal(total, b + a)
+    mod = Qwen3RMSNorm(dim, eps=1e-6).to(dev, torch.bfloat16)
+    with torch.no_grad():
+        mod.weight.copy_(w)
+        y_mod = mod(b + a)
+    ulp = y_mod.float().abs() * 2.0 ** -7 + 1e-30
+    assert bool(((y.float() - y_mod.float()).abs() <= 2 * ulp).all())
+
+    sf = total.float().requires_grad_(True)
+    wf = w.float().requires_grad_(True)
+    yf = _rmsnorm_fp32(sf, wf, 1e-6)
+    ((yf * dy.float()).sum() + (sf * ds.float()).sum()).backward()
+    dx, dw = K.rmsnorm_bwd(dy, total, w, rstd, dsum=ds)
+    assert _maxabs(dx, sf.grad) < 2e-2
+    assert _rel(dw, wf.grad) < 1e-2
+
+
 def test_rmsnorm_rejects_unsupported_width():
     dev = _dev()
     from mouse_core_b200 import _lib
