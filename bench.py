@@ -8,8 +8,10 @@ lengths start uniform in [64, 4096]; paged KV with 128-token pages; policy
 start_cache 1024 / max_cache 8192 (grow-then-rebuild, checked every step).
 Each token embeds one transition id ((obs*4 + action)*2 + reward)*2 + done
 (obs in [0,63], action in [0,3], reward in {0,1}, done ~ Bernoulli(0.02)):
-a single discrete modality of vocab 1024. A 4-way DiscreteActionValueHead
-(fp32 RMSNorm -> SwiGLU -> linear) takes the argmax.
+a single discrete modality of vocab 1024. A token whose done bit is set ends
+its env's task: the context is cleared and the env's next token starts a new
+one (its row restarts at position 0). A 4-way DiscreteActionValueHead (fp32
+RMSNorm -> SwiGLU -> linear) takes the argmax.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
@@ -18,8 +20,10 @@ Multi-GPU: one process per GPU (torchrun); each rank decodes its own 256 envs
 / max-over-ranks device time.
 
 `value` times K steps with inputs resident in HBM; `e2e` times the same steps
-through the public API with the token ids in pinned host memory (H2D copy
-each step) and the actions read back to the host (D2H copy + sync each step).
+through the public API — the grow-then-rebuild caller loop
+(GrowRebuildDecoder: policy check every step, rows re-windowed when they
+need it) — with the token ids in pinned host memory (H2D copy each step) and
+the actions read back to the host (D2H copy + sync each step).
 `--impl reference` times the reference algorithm's CPU restatement (the
 oracle; the reference itself is pure Python and is not installed on the GPU
 box) on the host cores for the same metric.
@@ -58,7 +62,8 @@ def transition_ids(rng, actions, n):
 
 def workload_config(n_gpus):
     return {"workload": "cached batched decode, Qwen3-0.6B arch truncated to 2 layers, 256 envs/GPU, "
-                        "context lengths U[64,4096], 128-token pages, start_cache 1024 / max_cache 8192",
+                        "context lengths U[64,4096], 128-token pages, start_cache 1024 / max_cache 8192, "
+                        "done ~ Bernoulli(0.02) ends the env's task (context cleared, row restarts)",
             "envs_per_gpu": ENVS, "global_envs": ENVS * n_gpus, "layers": LAYERS, "hidden": HIDDEN,
             "q_heads": HEADS, "kv_heads": KV_HEADS, "head_dim": HEAD_DIM, "page_size": PAGE,
             "context_len": [LEN_LO, LEN_HI], "parallelism": f"env-sharded x{n_gpus} (no collective)",
@@ -225,7 +230,7 @@ def run_ours(args):
 
     from mouse_core_b200 import _lib
     from mouse_core_b200 import kernels as K
-    from mouse_core_b200.kv_policy import cache_needs_rebuild, resolve_cache_bounds
+    from mouse_core_b200.kv_policy import resolve_cache_bounds
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -253,25 +258,27 @@ def run_ours(args):
     sess = model.decode_session(batch_size=ENVS, capacity=max_cache, page_size=PAGE)
     prefill(sess, table, ctx_ids, lengths)
     torch.cuda.synchronize()
-    cached_starts = np.zeros(ENVS, dtype=np.int64)
-    ends = lengths.copy()
-    cached_ends = ends.copy()
-    ctx_start = np.zeros(ENVS, dtype=np.int64)
 
     K_steps, W = args.steps, args.warmup
     total = K_steps + W
     # ---------------- device-resident loop (`value`)
+    # A token whose done bit is set ends its env's task: the env's context is
+    # cleared after that step and its next token starts a fresh one (the row
+    # is emptied, and the device step restarts it at position 0).
     actions = rng.integers(0, 4, size=ENVS)
-    ids_dev = torch.from_numpy(np.stack([transition_ids(rng, actions, ENVS)
-                                         for _ in range(total + K_steps)])).to(dev)
+    ids_host = np.stack([transition_ids(rng, actions, ENVS) for _ in range(total + K_steps)])
+    ids_dev = torch.from_numpy(ids_host).to(dev)
+    task_end = (ids_host & 1).astype(bool)
     ones = [1] * ENVS
 
     def device_step(i):
+        if i > 0:
+            gone = np.flatnonzero(task_end[i - 1])
+            if gone.size:
+                sess.reset_rows(gone)
         emb = table[ids_dev[i].long()].view(ENVS, 1, HIDDEN)
         h = sess.forward(embeds=emb, lengths=ones)
         return head(h[:, -1]).argmax(-1)
-
-    bytes_per_layer = []
 
     for i in range(W):
         device_step(i)
@@ -282,58 +289,75 @@ def run_ours(args):
     launches0 = K.launch_count[0]
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
+    t_host = time.perf_counter()
     e0.record()
     for i in range(W, total):
         device_step(i)
     e1.record()
+    host_us = (time.perf_counter() - t_host) * 1e6 / K_steps  # host time to issue one step
     torch.cuda.synchronize()
     clk = clocks.stop()
     launches = K.launch_count[0] - launches0
     ms = e0.elapsed_time(e1)
+    resets_timed = int(task_end[W - 1:total - 1].sum())
     # Roofline pass: K more steps run eagerly with CUDA events around every
     # attention launch (on the launching stream); same kernel, same data.
     sess.attn_events = []
     kv_sum = 0
     for i in range(total, total + K_steps):
-        kv_sum += int(sess._len.sum()) + ENVS  # kv_len after this step's append
+        gone = task_end[i - 1]
+        kv_sum += int(sess._len[~gone].sum()) + ENVS  # kv_len after this step's append
         device_step(i)
     torch.cuda.synchronize()
     attn_ms = [a.elapsed_time(b) for a, b in sess.attn_events]
     sess.attn_events = None
     barrier()
-    ms_t = torch.tensor([ms], device=dev)
-    if world > 1:
-        dist.all_reduce(ms_t, op=dist.ReduceOp.MAX)
-    ms_max = float(ms_t.item())
-    ends = ends + total + K_steps
-    cached_ends = ends.copy()
 
     # ---------------- end-to-end loop through the public API (`e2e`)
-    h_ids = torch.empty(ENVS, dtype=torch.int32, pin_memory=True)
+    # The grow-then-rebuild caller loop (GrowRebuildDecoder, per-row): every
+    # step appends each env's token to its host context, checks the policy
+    # (rows_needing_rebuild against max_cache, task ends), re-windows the rows
+    # that need it, and decodes; token ids go host -> device from pinned
+    # memory and the actions come back to the host.
+    from mouse_core_b200.grow_rebuild import GrowRebuildDecoder
+
+    cap = int(lengths.max()) + 2 * (total + K_steps) + 8
+    history = np.zeros((ENVS, cap), dtype=np.int32)
+    ends = lengths.copy()
+    for b in range(ENVS):
+        history[b, :lengths[b]] = ctx_ids[b]
+    rows = np.arange(ENVS)
+    for i in range(total + K_steps):  # the host contexts of what the session now holds
+        if i > 0:
+            ends[task_end[i - 1]] = 0
+        history[rows, ends] = ids_host[i]
+        ends += 1
+    dec = GrowRebuildDecoder(model, ENVS, lambda ids: table[ids], max_cache=max_cache, start_cache=start_cache,
+                             per_row=True)
+    dec.adopt(sess, np.zeros(ENVS, dtype=np.int64), ends)
+    pending = task_end[total + K_steps - 1].copy()
+    ends[pending] = 0
     h_act = torch.empty(ENVS, dtype=torch.int64, pin_memory=True)
-    d_ids = torch.empty(ENVS, dtype=torch.int32, device=dev)
     act = rng.integers(0, 4, size=ENVS)
 
     def e2e_step():
-        nonlocal act, ends, cached_ends, sess
-        ends = ends + 1
-        if cache_needs_rebuild(has_cache=True, cached_starts=cached_starts, cached_ends=cached_ends, ends=ends,
-                               context_start=ctx_start, max_cache=max_cache, batch_complete=True):
-            raise RuntimeError("rebuild inside the timed horizon (lengths are chosen so it cannot happen)")
-        h_ids.numpy()[:] = transition_ids(rng, act, ENVS)
-        d_ids.copy_(h_ids, non_blocking=True)
-        emb = table[d_ids.long()].view(ENVS, 1, HIDDEN)
-        h = sess.forward(embeds=emb, lengths=ones)
+        nonlocal act, pending
+        tok = transition_ids(rng, act, ENVS)
+        history[rows, ends] = tok
+        ends[:] += 1
+        h, _ = dec.step(history, ends, 0, rebuild=pending)
         h_act.copy_(head(h[:, -1]).argmax(-1), non_blocking=True)
         torch.cuda.current_stream().synchronize()
         act = h_act.numpy().copy()
-        cached_ends = ends.copy()
+        pending = (tok & 1).astype(bool)
+        ends[pending] = 0
 
     for _ in range(W):
         e2e_step()
     torch.cuda.synchronize()
     barrier()
     torch.cuda.synchronize()
+    rebuilt0 = dec.rows_rebuilt
     f0 = torch.cuda.Event(enable_timing=True)
     f1 = torch.cuda.Event(enable_timing=True)
     f0.record()
@@ -342,10 +366,16 @@ def run_ours(args):
     f1.record()
     torch.cuda.synchronize()
     e2e_ms = f0.elapsed_time(f1)
-    et = torch.tensor([e2e_ms], device=dev)
+    e2e_rebuilt = dec.rows_rebuilt - rebuilt0
+    per_rank = torch.tensor([ms / K_steps, host_us, e2e_ms / K_steps], device=dev)
     if world > 1:
-        dist.all_reduce(et, op=dist.ReduceOp.MAX)
-    e2e_max = float(et.item())
+        gathered = [torch.zeros_like(per_rank) for _ in range(world)]
+        dist.all_gather(gathered, per_rank)
+    else:
+        gathered = [per_rank]
+    per_rank_rows = [[round(float(x), 4) for x in t.tolist()] for t in gathered]
+    ms_max = max(r[0] for r in per_rank_rows) * K_steps
+    e2e_max = max(r[2] for r in per_rank_rows) * K_steps
     status = _lib.device_status()
 
     # Algorithmic bytes of one attention launch: K+V of every cached slot of
@@ -390,6 +420,13 @@ def run_ours(args):
             "gpu_launches": int(launches),
             "clocks": clk,
             "device_status": status,
+            "task_ends": {"rows_reset_in_timed_steps": resets_timed,
+                          "rows_rebuilt_in_e2e_steps": int(e2e_rebuilt),
+                          "rule": "a token with its done bit set (p = 0.02) ends the env's task: the context is "
+                                  "cleared and the next token starts a fresh one (the row restarts at position 0); "
+                                  "the e2e loop also checks max_cache every step (rows_needing_rebuild)"},
+            "per_rank": {"fields": ["device_ms_per_step", "host_us_to_issue_step", "e2e_ms_per_step"],
+                         "ranks": per_rank_rows},
         }
     if rank == 0 and not args.no_packed:
         out["packed_attention"] = packed_attention_metric(dev)

@@ -169,3 +169,83 @@ def config_from_hf(hf_config, inv_freq, attention_scaling=1.0):
         inv_freq=np.asarray(inv_freq, dtype=np.float64),
         attention_scaling=float(attention_scaling),
     )
+
+
+class GrowRebuildOracle:
+    """Restates the caller loop that drives the grow-then-rebuild policy:
+    ``_act_from_contexts`` in ``run_eval`` (examples/02_train_offline.ipynb,
+    cell 11) over ``DecodeSessionOracle``, with the policy functions of
+    ``oracle.policy`` (kv_policy.py:14-72).
+
+    Batch mode (``per_row=False``) is the reference's loop: when
+    ``cache_needs_rebuild`` (or a forced rebuild) fires, the session is dropped
+    and a new one prefills ``history[b, rebuild_starts[b]:ends[b]]`` for every
+    row (models/base.py:932-934 makes the new session); otherwise each row
+    appends ``history[b, cached_ends[b]:ends[b]]``. Per-row mode runs that same
+    loop independently for every row (a batch of one env each).
+
+    ``step`` returns ``(out [B, S, D], fed [B])`` laid out like the session's
+    left-padded output: row ``b``'s ``fed[b]`` new tokens in its last columns.
+    """
+
+    def __init__(self, decoder: DecoderOracle, batch_size: int, table, max_cache: int, start_cache=None,
+                 per_row: bool = False):
+        from oracle.policy import resolve_cache_bounds
+
+        self.dec = decoder
+        self.B = batch_size
+        self.table = np.asarray(table, dtype=np.float64)
+        self.max_cache, self.start_cache = resolve_cache_bounds(max_cache, start_cache)
+        self.per_row = per_row
+        if per_row:
+            self.rows = [GrowRebuildOracle(decoder, 1, table, max_cache, start_cache) for _ in range(batch_size)]
+        self.session = None
+        self.cached_starts = np.zeros(batch_size, dtype=np.int64)
+        self.cached_ends = np.zeros(batch_size, dtype=np.int64)
+
+    def step(self, history, ends, context_start=0, rebuild=False):
+        from oracle.policy import cache_needs_rebuild, rebuild_starts
+
+        hist = np.asarray(history)
+        ends = np.asarray(ends, dtype=np.int64)
+        ctx = np.broadcast_to(np.asarray(context_start, dtype=np.int64), ends.shape)
+        if self.per_row:
+            forced = np.zeros(self.B, dtype=bool)
+            if rebuild is True:
+                forced[:] = True
+            elif rebuild is not False and rebuild is not None:
+                r = np.asarray(rebuild)
+                if r.dtype == bool:
+                    forced |= r
+                else:
+                    forced[r] = True
+            parts = [row.step(hist[b:b + 1], ends[b:b + 1], ctx[b:b + 1], bool(forced[b]))
+                     for b, row in enumerate(self.rows)]
+            fed = np.array([int(p[1][0]) for p in parts], dtype=np.int64)
+            S = max(int(fed.max()), 1)
+            out = np.zeros((self.B, S, self.table.shape[1]))
+            for b, (o, n) in enumerate(parts):
+                if n[0]:
+                    out[b, S - n[0]:] = o[0, o.shape[1] - n[0]:]
+            return out, fed
+        need = (rebuild is True or (rebuild is not False and rebuild is not None and np.asarray(rebuild).any())
+                or cache_needs_rebuild(has_cache=self.session is not None, cached_starts=self.cached_starts,
+                                       cached_ends=self.cached_ends, ends=ends, context_start=ctx,
+                                       max_cache=self.max_cache, batch_complete=True))
+        if need:
+            starts = rebuild_starts(ends=ends, context_start=ctx, start_cache=self.start_cache,
+                                    max_cache=self.max_cache)
+            self.session = DecodeSessionOracle(self.dec, self.B)
+            self.cached_starts = starts
+        else:
+            starts = self.cached_ends
+        fed = ends - starts
+        S = max(int(fed.max()), 1)
+        emb = np.zeros((self.B, S, self.table.shape[1]))
+        for b in range(self.B):
+            n = int(fed[b])
+            if n:
+                emb[b, S - n:] = self.table[hist[b, starts[b]:ends[b]]]
+        out = self.session.forward(emb, fed)
+        self.cached_ends = ends.copy()
+        return out, fed

@@ -2,7 +2,7 @@
 
 Run in a container where the reference source tree is available::
 
-    python tests/golden/make_golden.py --reference /root/reference/src
+    python tests/golden/make_golden.py --reference <reference checkout>/src [--only grow_rebuild ...]
 
 It imports micahr234/mouse-core v0.4.0 from that tree (with a stand-in
 ``tensordict`` module and package metadata written to a temp dir, because the
@@ -27,6 +27,11 @@ return:
                        fp16-representable so they store exactly).
 * ``packed_fwd_qwen3.npz`` ``flex_packed_forward``'s CPU twin (the HF stack
                        with the dense mask + per-run position ids).
+* ``grow_rebuild_qwen3.npz`` the caller loop that drives the grow-then-rebuild
+                       policy (kv_policy.py + ``FlexDecodeSession``) over a
+                       40-call ragged schedule with task ends and a small
+                       ``max_cache``: whole-batch rebuilds, and each env
+                       run alone (the per-row semantics).
 
 The fixtures are small; nothing at test time reads the reference.
 """
@@ -43,6 +48,9 @@ from pathlib import Path
 import numpy as np
 
 HERE = Path(__file__).resolve().parent
+sys.path.insert(0, str(HERE.parent.parent))
+
+from tests.golden_io import grow_rebuild_schedule  # noqa: E402  (the schedule the GPU tests replay)
 
 
 def _install_shims(tmp: Path) -> None:
@@ -296,6 +304,87 @@ def make_decode(arch: str) -> None:
     np.savez_compressed(HERE / f"decode_{arch}.npz", **rec)
 
 
+class _RefGrowRebuildLoop:
+    """The reference's caller loop (``_act_from_contexts`` in ``run_eval``,
+    examples/02_train_offline.ipynb cell 11) with its own kv_policy functions
+    and ``FlexDecodeSession``; the session is dropped and re-made on every
+    rebuild, as ``Model.forward`` does with ``cache=None`` (base.py:932-934)."""
+
+    def __init__(self, model, B, table, max_cache, start_cache):
+        from mouse_core.models.kv_policy import resolve_cache_bounds
+
+        self.model, self.B, self.table = model, B, table
+        self.max_cache, self.start_cache = resolve_cache_bounds(max_cache, start_cache)
+        self.session = None
+        self.cached_starts = np.zeros(B, dtype=np.int64)
+        self.cached_ends = np.zeros(B, dtype=np.int64)
+
+    def step(self, hist, ends, ctx, rebuild):
+        import torch
+        from mouse_core.models.backbone.flex_decode import FlexDecodeSession
+        from mouse_core.models.kv_policy import cache_needs_rebuild, rebuild_starts
+
+        need = rebuild or cache_needs_rebuild(
+            has_cache=self.session is not None, cached_starts=self.cached_starts, cached_ends=self.cached_ends,
+            ends=ends, context_start=ctx, max_cache=self.max_cache, batch_complete=True)
+        if need:
+            starts = rebuild_starts(ends=ends, context_start=ctx, start_cache=self.start_cache,
+                                    max_cache=self.max_cache)
+            self.cached_starts = starts
+        else:
+            starts = self.cached_ends
+        fed = ends - starts
+        S = max(int(fed.max()), 1)
+        emb = torch.zeros(self.B, S, self.table.shape[1])
+        for b in range(self.B):
+            n = int(fed[b])
+            if n:
+                emb[b, S - n:] = self.table[torch.from_numpy(hist[b, starts[b]:ends[b]])]
+        if need:
+            self.session = FlexDecodeSession(self.model, batch_size=self.B, capacity=S)
+        with torch.no_grad():
+            out = self.session.forward(embeds=emb, lengths=fed.tolist())
+        self.cached_ends = ends.copy()
+        return out.numpy(), fed
+
+
+def make_grow_rebuild() -> None:
+    """The reference's caller loop over a 40-call schedule with a tiny
+    ``max_cache`` so rebuilds are frequent: batch mode (every rebuild
+    re-windows the whole batch) and, for the per-row semantics, the same loop
+    run on each env alone (a batch of one)."""
+    import torch
+    from mouse_core.models.backbone import Qwen3Backbone
+
+    torch.manual_seed(31)
+    bb = Qwen3Backbone(hidden_dim=64, num_layers=2, num_heads=2, num_key_value_heads=1, head_dim=64)
+    model = bb.model.eval()
+    _round_fp16_(model)
+    with torch.no_grad():
+        for name, p in model.named_parameters():
+            if "norm" in name:
+                p.copy_((1.0 + 0.25 * torch.randn_like(p)).half().float())
+    B, calls, vocab, max_cache, start_cache = 4, 40, 48, 24, 10
+    g = torch.Generator().manual_seed(9)
+    table = torch.randn(vocab, 64, generator=g).half().float()
+    rec = {"inv_freq": model.rotary_emb.inv_freq.numpy(), "eps": np.array(float(model.config.rms_norm_eps)),
+           "n_heads": np.array(2), "n_kv_heads": np.array(1), "head_dim": np.array(64), "num_layers": np.array(2),
+           "qk_norm": np.array(True), "table": table.numpy(), "max_cache": np.array(max_cache),
+           "start_cache": np.array(start_cache), "calls": np.array(calls), "B": np.array(B)}
+    for key, val in _weights(model).items():
+        rec["w:" + key] = val
+    batch = _RefGrowRebuildLoop(model, B, table, max_cache, start_cache)
+    alone = [_RefGrowRebuildLoop(model, 1, table, max_cache, start_cache) for _ in range(B)]
+    for ci, (hist, ends, ctx, ended) in enumerate(grow_rebuild_schedule(4, B, calls, vocab)):
+        out, fed = batch.step(hist, ends, ctx, bool(ended.any()))
+        rec[f"c{ci}_hist"], rec[f"c{ci}_ends"], rec[f"c{ci}_ctx"], rec[f"c{ci}_ended"] = hist, ends, ctx, ended
+        rec[f"c{ci}_out"], rec[f"c{ci}_fed"] = out, fed
+        for b in range(B):
+            o, f = alone[b].step(hist[b:b + 1], ends[b:b + 1], ctx[b:b + 1], bool(ended[b]))
+            rec[f"c{ci}_row{b}_out"], rec[f"c{ci}_row{b}_fed"] = o, f
+    np.savez_compressed(HERE / "grow_rebuild_qwen3.npz", **rec)
+
+
 def make_packed_forward() -> None:
     import torch
     from mouse_core.models.backbone import Qwen3Backbone
@@ -321,24 +410,39 @@ def make_packed_forward() -> None:
     np.savez_compressed(HERE / "packed_fwd_qwen3.npz", **rec)
 
 
+FIXTURES = ("index_maps", "kv_policy", "packed_attention", "decode", "packed_forward", "grow_rebuild")
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference/src")
+    ap.add_argument("--reference", default=os.environ.get("MOUSE_CORE_REFERENCE_SRC"),
+                    help="the reference's src/ directory (or set MOUSE_CORE_REFERENCE_SRC)")
+    ap.add_argument("--only", nargs="*", choices=FIXTURES, default=list(FIXTURES),
+                    help="regenerate only these fixtures")
     args = ap.parse_args()
+    if not args.reference:
+        ap.error("give --reference <reference src dir> or set MOUSE_CORE_REFERENCE_SRC")
     tmp = Path(tempfile.mkdtemp(prefix="mouse_ref_shim_"))
     _install_shims(tmp)
     sys.path.insert(0, os.path.abspath(args.reference))
     import torch
 
     torch.set_num_threads(min(8, os.cpu_count() or 1))
-    maps: dict = {}
-    make_index_maps(maps)
-    np.savez_compressed(HERE / "index_maps.npz", **maps)
-    (HERE / "kv_policy.json").write_text(json.dumps(make_kv_policy()))
-    make_packed_attention()
-    make_decode("qwen3")
-    make_decode("llama")
-    make_packed_forward()
+    if "index_maps" in args.only:
+        maps: dict = {}
+        make_index_maps(maps)
+        np.savez_compressed(HERE / "index_maps.npz", **maps)
+    if "kv_policy" in args.only:
+        (HERE / "kv_policy.json").write_text(json.dumps(make_kv_policy()))
+    if "packed_attention" in args.only:
+        make_packed_attention()
+    if "decode" in args.only:
+        make_decode("qwen3")
+        make_decode("llama")
+    if "packed_forward" in args.only:
+        make_packed_forward()
+    if "grow_rebuild" in args.only:
+        make_grow_rebuild()
     print("golden fixtures written to", HERE)
 
 

@@ -58,3 +58,33 @@ def decoder_from_fixture(rec):
         attention_scaling=float(rec["attention_scaling"]) if "attention_scaling" in rec else 1.0,
     )
     return DecoderOracle(weights, cfg), weights
+
+
+def grow_rebuild_schedule(seed: int, B: int, calls: int, vocab: int, max_append: int = 3):
+    """A caller-loop schedule for the grow-then-rebuild fixtures: before each
+    call every env either ends its task (context cleared, ``context_start``
+    back to 0, a forced rebuild as the reference's loop does on a task end),
+    moves its ``context_start`` forward, or appends 0..``max_append`` new
+    tokens. Yields
+    ``(history [B, T], ends [B], context_start [B], task_ended [B])`` per call."""
+    rng = np.random.default_rng(seed)
+    hist = [[] for _ in range(B)]
+    ctx = np.zeros(B, dtype=np.int64)
+    for _ in range(calls):
+        ended = np.zeros(B, dtype=bool)
+        for b in range(B):
+            u = rng.random()
+            if hist[b] and u < 0.06:
+                hist[b] = []
+                ctx[b] = 0
+                ended[b] = True
+            elif len(hist[b]) > 4 and u < 0.09:
+                ctx[b] = max(int(ctx[b]), len(hist[b]) - 3)
+            else:
+                hist[b].extend(int(t) for t in rng.integers(0, vocab, size=int(rng.integers(0, max_append + 1))))
+        ends = np.array([len(h) for h in hist], dtype=np.int64)
+        T = max(int(ends.max()), 1)
+        arr = np.zeros((B, T), dtype=np.int64)
+        for b in range(B):
+            arr[b, :ends[b]] = hist[b]
+        yield arr, ends, ctx.copy(), ended

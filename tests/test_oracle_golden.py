@@ -146,3 +146,32 @@ def test_packed_forward_oracle_matches_reference():
     dec, _ = decoder_from_fixture(rec)
     h = odec.packed_forward(dec, rec["emb"], rec["seq"])
     assert np.abs(h - rec["out"]).max() < 1e-4
+
+
+@pytest.mark.parametrize("per_row", [False, True])
+def test_grow_rebuild_oracle_matches_reference(per_row):
+    """The oracle's restatement of the caller loop that drives the
+    grow-then-rebuild policy equals the reference's own loop (its kv_policy
+    functions and FlexDecodeSession) call for call: batch rebuilds, and each
+    env run alone for the per-row semantics."""
+    rec = load("grow_rebuild_qwen3.npz")
+    dec, _ = decoder_from_fixture(rec)
+    B = int(rec["B"])
+    loop = odec.GrowRebuildOracle(dec, B, rec["table"].astype(np.float64), int(rec["max_cache"]),
+                                  int(rec["start_cache"]), per_row=per_row)
+    rebuilt = 0
+    for ci in range(int(rec["calls"])):
+        ended = rec[f"c{ci}_ended"]
+        out, fed = loop.step(rec[f"c{ci}_hist"], rec[f"c{ci}_ends"], rec[f"c{ci}_ctx"],
+                             ended if per_row else bool(ended.any()))
+        S = out.shape[1]
+        for b in range(B):
+            if per_row:
+                ref, n = rec[f"c{ci}_row{b}_out"][0], int(rec[f"c{ci}_row{b}_fed"][0])
+            else:
+                ref, n = rec[f"c{ci}_out"][b], int(rec[f"c{ci}_fed"][b])
+            assert int(fed[b]) == n, (ci, b)
+            if n:
+                assert np.abs(out[b, S - n:] - ref[ref.shape[0] - n:]).max() < 1e-5, (ci, b)
+        rebuilt += int((fed > 3).sum())  # a window longer than any append is a rebuild
+    assert rebuilt >= 5
