@@ -48,8 +48,21 @@ int mb_version(void);
 
 /* Read (and optionally clear) the device status word the kernels report
  * bounded-wait timeouts and out-of-pool page ids through. Synchronizes the
- * device. 0 = healthy. */
+ * device. 0 = healthy; 1 / 2 = a consumer / producer wait ran out; 3 = a page
+ * id outside the pool (or a token past the block table); 4 = misaligned
+ * dynamic shared memory; 5 = a stored-dS pair index outside the scratch;
+ * 6 = a CTA's own copies did not land before it exited. */
 int mb_device_status(int* status_out, int clear);
+
+/* Diagnostics, no counterpart in the reference (whose kernels come from
+ * Inductor and never wait on one another): set how many clock cycles every
+ * bounded wait of the kernels on the current device spins after its first
+ * failed test before it gives up, records 1 or 2 in the status word and lets
+ * its CTA stop cleanly; < 0 restores the default (4e9 cycles, about two
+ * seconds). A small value makes a healthy pipeline's waits run out, which is
+ * how the timeout path is tested; it applies to kernels launched after the
+ * call returns (the call synchronizes the device). */
+int mb_set_wait_limit(long long cycles);
 
 /* ---------------------------------------------------------------------
  * Cached decode attention (K1).
@@ -94,7 +107,8 @@ int mb_decode_attention(const void* q, const void* k_pool, const void* v_pool, i
  * whose workspace (mb_decode_workspace_bytes) exceeds that is rejected with
  * MB_ERR_WORKSPACE. It calls no allocator. The first call on a device looks
  * up the array's device address (cudaGetSymbolAddress) with that device
- * current; make it before capturing any stream. Every call shares the one
+ * current; make it before capturing any stream. `stream` must belong to the
+ * current device (MB_ERR_INVALID_ARG otherwise). Every call shares the one
  * array and rebuilds its work list and merge counters from scratch, so calls
  * that overlap on the GPU (several streams or host threads at once) race and
  * must be serialised by the caller. */

@@ -19,6 +19,7 @@ PROTOTYPES = {
     "mb_last_error": (ctypes.c_char_p, []),
     "mb_version": (_c_int, []),
     "mb_device_status": (_c_int, [ctypes.POINTER(_c_int), _c_int]),
+    "mb_set_wait_limit": (_c_int, [ctypes.c_longlong]),
     "mb_decode_workspace_bytes": (_c_size, [_c_int, _c_int, _c_int, _c_int, _c_int]),
     "mb_decode_plan": (_c_int, [_vp, _c_int, _c_int, _c_int, _c_int, _c_int, _vp, _c_size, _vp]),
     "mb_decode_attention": (_c_int, [_vp, _vp, _vp, _c_int, _vp, _c_int, _vp, _vp, _c_int, _c_int, _c_int,
@@ -97,3 +98,9 @@ def device_status(clear: bool = True) -> int:
     out = ctypes.c_int(0)
     check(load().mb_device_status(ctypes.byref(out), int(clear)), "mb_device_status")
     return out.value
+
+
+def set_wait_limit(cycles: int | None) -> None:
+    """Cycles every bounded wait of the kernels spins before it gives up
+    (``None`` restores the default of about two seconds); synchronizes."""
+    check(load().mb_set_wait_limit(-1 if cycles is None else int(cycles)), "mb_set_wait_limit")

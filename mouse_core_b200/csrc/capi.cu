@@ -100,6 +100,15 @@ int mb_device_status(int* status_out, int clear) {
   return MB_OK;
 }
 
+int mb_set_wait_limit(long long cycles) {
+  const long long v = cycles < 0 ? mb::kWaitCycles : cycles;
+  cudaError_t e = cudaMemcpyToSymbol(mb::g_wait_limit, &v, sizeof(v));
+  if (e != cudaSuccess) return cuda_fail(e, "set wait limit");
+  e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceSynchronize");
+  return MB_OK;
+}
+
 size_t mb_decode_workspace_bytes(int batch, int kv_heads, int q_rows, int head_dim, int max_kv_len) {
   if (batch <= 0 || kv_heads <= 0 || q_rows <= 0 || q_rows > 16) return 0;
   if (head_dim != 64 && head_dim != 128) return 0;

@@ -25,6 +25,7 @@ enum DeviceStatus : int {
   kDevBadPage = 3,       // block-table entry outside the page pool
   kDevBadSmem = 4,       // dynamic shared memory base not 1024-byte aligned
   kDevBadPair = 5,       // stored-dS pair index outside the scratch (inconsistent pair offsets)
+  kDevTimeoutDrain = 6,  // a CTA's own copies did not land before it exited
 };
 
 // The library is one translation unit (mouse_b200.cu), so the status word is
@@ -36,6 +37,14 @@ __device__ __forceinline__ void report(int code) { atomicCAS(&g_device_status, 0
 // About two seconds at B200 clocks: long enough never to fire on a healthy
 // pipeline, short enough that a broken one ends and the host sees a status.
 constexpr long long kWaitCycles = 4000000000ll;
+
+// Cycles a wait spins after its first failed test before it gives up; the
+// host can change it (mb_set_wait_limit) to make a wait run out on purpose.
+__device__ long long g_wait_limit = kWaitCycles;
+
+// Limit of the waits that drain a CTA's own in-flight copies before it exits:
+// those copies always complete, so this never depends on g_wait_limit.
+constexpr long long kDrainCycles = kWaitCycles;
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -71,16 +80,56 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
+__device__ __forceinline__ long long wait_limit() {
+  return *reinterpret_cast<volatile long long*>(&g_wait_limit);
+}
+
 // Wait for the phase with the given parity to complete; false on timeout
-// (after recording `code` in the device status word).
+// (after recording `code` in the device status word). The limit is checked
+// before every retry, so a limit of 0 gives up right after the first failed
+// test.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int code) {
   if (mbar_try_wait(bar, parity)) return true;
+  const long long limit = wait_limit();
   const long long t0 = clock64();
   while (true) {
-    if (mbar_try_wait(bar, parity)) return true;
-    if (clock64() - t0 > kWaitCycles) {
+    if (clock64() - t0 > limit) {
       report(code);
       return false;
+    }
+    if (mbar_try_wait(bar, parity)) return true;
+  }
+}
+
+// As mbar_wait, but also gives up (without a new code) once `*abort` is set,
+// and sets `*abort` itself when it times out, so the other warps of the CTA
+// stop waiting too.
+__device__ __forceinline__ bool mbar_wait_abortable(uint64_t* bar, uint32_t parity, int code, int* abort) {
+  volatile int* ab = abort;
+  if (mbar_try_wait(bar, parity)) return true;
+  const long long limit = wait_limit();
+  const long long t0 = clock64();
+  while (true) {
+    if (*ab) return false;
+    if (clock64() - t0 > limit) {
+      report(code);
+      *ab = 1;
+      return false;
+    }
+    if (mbar_try_wait(bar, parity)) return true;
+  }
+}
+
+// Wait for a phase that this CTA's own in-flight copies complete (a TMA load
+// it issued) before the CTA exits; bounded by kDrainCycles, not by the
+// host-set limit.
+__device__ __forceinline__ void mbar_drain(uint64_t* bar, uint32_t parity) {
+  if (mbar_try_wait(bar, parity)) return;
+  const long long t0 = clock64();
+  while (!mbar_try_wait(bar, parity)) {
+    if (clock64() - t0 > kDrainCycles) {
+      report(kDevTimeoutDrain);
+      return;
     }
   }
 }
@@ -152,6 +201,21 @@ __device__ __forceinline__ uint32_t swz128(uint32_t row, uint32_t chunk) {
 // Named barrier over `nthreads` threads (id 0 is __syncthreads).
 __device__ __forceinline__ void named_barrier(int id, int nthreads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+
+// Named barrier that also ORs a predicate over its `nthreads` threads: every
+// thread gets the same answer, so a decision taken on it keeps them together.
+__device__ __forceinline__ bool named_barrier_or(int id, int nthreads, bool pred) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 p, %1, 0;\n\t"
+      "bar.red.or.pred q, %2, %3, p;\n\t"
+      "selp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(r)
+      : "r"((uint32_t)pred), "r"(id), "r"(nthreads)
+      : "memory");
+  return r != 0;
 }
 
 __device__ __forceinline__ float warp_sum(float v) {

@@ -25,6 +25,7 @@
 //    the four warps split the query rows and walk the causal KV range.
 //
 // Every wait is bounded (common.cuh); TMA loads never use multicast.
+#include <atomic>
 #include "common.cuh"
 #include "kernels.h"
 
@@ -232,6 +233,10 @@ __global__ void __launch_bounds__(160, 2) split_decode_kernel(const __grid_const
   uint64_t* item_full = empty + C::STAGES;
   uint64_t* item_empty = item_full + SM::NSLOT;
   int* flag = reinterpret_cast<int*>(item_empty + SM::NSLOT);
+  // Set by the first wait of this CTA that runs out: every role then stops
+  // (consumers together, at a barrier), the producer lets its issued copies
+  // land, and no output of an incomplete item is written.
+  int* abort = flag + 1;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
@@ -243,6 +248,7 @@ __global__ void __launch_bounds__(160, 2) split_decode_kernel(const __grid_const
       mbar_init(&item_full[s], 1);
       mbar_init(&item_empty[s], 1);
     }
+    *abort = 0;
     fence_barrier_init();
   }
   __syncthreads();
@@ -257,12 +263,15 @@ __global__ void __launch_bounds__(160, 2) split_decode_kernel(const __grid_const
       prefetch_tensormap(&kmap);
       prefetch_tensormap(&vmap);
     }
-    uint32_t it = 0;
+    uint32_t it = 0;  // tiles issued (lane 0)
     int k = 0;
     for (int item = blockIdx.x; item < n_items; item += gridDim.x, ++k) {
       const int slot = k & 1;
       bool ok = true;
-      if (lane == 0) ok = mbar_wait(&item_empty[slot], ((k >> 1) & 1) ^ 1, kDevTimeoutEmpty);
+      if (lane == 0) {
+        ok = mbar_wait_abortable(&item_empty[slot], ((k >> 1) & 1) ^ 1, kDevTimeoutEmpty, abort) &&
+             !*reinterpret_cast<volatile int*>(abort);
+      }
       if (!__shfl_sync(0xffffffffu, ok, 0)) break;
       const int2 ent = p.entries[item / p.Hkv];
       const int h = item % p.Hkv, b = ent.x;
@@ -298,7 +307,10 @@ __global__ void __launch_bounds__(160, 2) split_decode_kernel(const __grid_const
         mbar_arrive(&item_full[slot]);
         for (int t0 = t_begin; t0 < t_end; t0 += C::T, ++it) {
           const int st = it % C::STAGES;
-          if (!mbar_wait(&empty[st], ((it / C::STAGES) & 1) ^ 1, kDevTimeoutEmpty)) {
+          // A consumer that gave up sets `abort` before releasing its stage,
+          // so a stage whose load may still be in flight is never reused.
+          if (!mbar_wait_abortable(&empty[st], ((it / C::STAGES) & 1) ^ 1, kDevTimeoutEmpty, abort) ||
+              *reinterpret_cast<volatile int*>(abort)) {
             ok = false;
             break;
           }
@@ -308,6 +320,12 @@ __global__ void __launch_bounds__(160, 2) split_decode_kernel(const __grid_const
       }
       if (!__shfl_sync(0xffffffffu, ok, 0)) break;
     }
+    // Every load this CTA issued lands before the CTA may exit (only the last
+    // STAGES can still be in flight).
+    if (lane == 0) {
+      for (uint32_t j = it > (uint32_t)C::STAGES ? it - C::STAGES : 0u; j < it; ++j)
+        mbar_drain(&full[j % C::STAGES], (j / C::STAGES) & 1);
+    }
     return;
   }
 
@@ -315,15 +333,17 @@ __global__ void __launch_bounds__(160, 2) split_decode_kernel(const __grid_const
   const int tid = threadIdx.x;  // 0..127
   const int gid = lane >> 2, tig = lane & 3;
   uint32_t it = 0;
-  bool alive = true;
   int k = 0;
   for (int item = blockIdx.x; item < n_items; item += gridDim.x, ++k) {
     const int slot = k & 1;
-    if (alive && !mbar_wait(&item_full[slot], (k >> 1) & 1, kDevTimeoutFull)) alive = false;
+    bool alive = mbar_wait_abortable(&item_full[slot], (k >> 1) & 1, kDevTimeoutFull, abort);
+    // All four consumer warps leave together (the barrier's OR) when any of
+    // them found no staged item: its metadata would be garbage.
+    if (named_barrier_or(1, 128, !alive)) break;
     const uint8_t* sq = slots + slot * SM::SLOT;
     const int* meta = reinterpret_cast<const int*>(sq + 16 * SM::QROW);
     const int b = meta[kMetaB], h = meta[kMetaH];
-    const int t_begin = meta[kMetaBegin], t_end = alive ? meta[kMetaEnd] : meta[kMetaBegin];
+    const int t_begin = meta[kMetaBegin], t_end = meta[kMetaEnd];
     const int nchunks = meta[kMetaChunks];
     const int kv_end[2] = {meta[kMetaKvEnd + gid], meta[kMetaKvEnd + gid + 8]};
     uint32_t qa[HD / 16][4];
@@ -344,7 +364,7 @@ __global__ void __launch_bounds__(160, 2) split_decode_kernel(const __grid_const
 
     for (int t0 = t_begin; t0 < t_end; t0 += C::T, ++it) {
       const int st = it % C::STAGES;
-      if (alive && !mbar_wait(&full[st], (it / C::STAGES) & 1, kDevTimeoutFull)) alive = false;
+      if (alive && !mbar_wait_abortable(&full[st], (it / C::STAGES) & 1, kDevTimeoutFull, abort)) alive = false;
       if (alive) {
         const uint32_t kb = smem_u32(kring + st * C::TILE_BYTES);
         const uint32_t vb = smem_u32(vring + st * C::TILE_BYTES);
@@ -359,6 +379,8 @@ __global__ void __launch_bounds__(160, 2) split_decode_kernel(const __grid_const
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty[st]);
     }
+    // An item with a tile that never arrived is not written (the CTA stops).
+    if (named_barrier_or(1, 128, !alive)) break;
 
     // ---- merge the four warps' (m, l, o) for the R real rows
 #pragma unroll
@@ -507,6 +529,7 @@ __global__ void __launch_bounds__(160) block_decode_kernel(const __grid_constant
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + 2 * C::STAGES * C::TILE_BYTES);
   uint64_t* empty = full + C::STAGES;
   __shared__ int kv_hi_s;
+  __shared__ int abort_s;  // as in the split kernel: the first wait that runs out stops the CTA
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int qb = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
@@ -517,6 +540,7 @@ __global__ void __launch_bounds__(160) block_decode_kernel(const __grid_constant
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 4);
     }
+    abort_s = 0;
     fence_barrier_init();
     // KV range this block needs: up to the largest q_pos of its rows.
     const int r_lo = qb * 64, r_hi = min(r_lo + 64, R);
@@ -531,13 +555,18 @@ __global__ void __launch_bounds__(160) block_decode_kernel(const __grid_constant
     if (lane == 0) {
       prefetch_tensormap(&kmap);
       prefetch_tensormap(&vmap);
-      uint32_t it = 0;
+      uint32_t it = 0;  // tiles issued
       for (int t0 = 0; t0 < kv_hi; t0 += C::T, ++it) {
         const int st = it % C::STAGES;
-        if (!mbar_wait(&empty[st], ((it / C::STAGES) & 1) ^ 1, kDevTimeoutEmpty)) return;
+        if (!mbar_wait_abortable(&empty[st], ((it / C::STAGES) & 1) ^ 1, kDevTimeoutEmpty, &abort_s) ||
+            *reinterpret_cast<volatile int*>(&abort_s))
+          break;
         issue_tile<HD>(&kmap, &vmap, kring + st * C::TILE_BYTES, vring + st * C::TILE_BYTES, &full[st], p, b, h,
                        t0, len);
       }
+      // The issued loads land before the CTA may exit.
+      for (uint32_t j = it > (uint32_t)C::STAGES ? it - C::STAGES : 0u; j < it; ++j)
+        mbar_drain(&full[j % C::STAGES], (j / C::STAGES) & 1);
     }
     return;
   }
@@ -566,7 +595,7 @@ __global__ void __launch_bounds__(160) block_decode_kernel(const __grid_constant
   uint32_t it = 0;
   for (int t0 = 0; t0 < kv_hi; t0 += C::T, ++it) {
     const int st = it % C::STAGES;
-    if (alive && !mbar_wait(&full[st], (it / C::STAGES) & 1, kDevTimeoutFull)) alive = false;
+    if (alive && !mbar_wait_abortable(&full[st], (it / C::STAGES) & 1, kDevTimeoutFull, &abort_s)) alive = false;
     if (alive && t0 < warp_hi) {
       const uint32_t kb = smem_u32(kring + st * C::TILE_BYTES);
       const uint32_t vb = smem_u32(vring + st * C::TILE_BYTES);
@@ -578,6 +607,8 @@ __global__ void __launch_bounds__(160) block_decode_kernel(const __grid_constant
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[st]);
   }
+  // Rows whose keys did not all arrive are not written.
+  if (named_barrier_or(1, 128, !alive)) return;
 
 #pragma unroll
   for (int half = 0; half < 2; ++half) {
@@ -623,16 +654,19 @@ size_t decode_workspace_layout(int B, int Hkv, int R, int head_dim, int max_kv_l
   return off;
 }
 
-static int g_num_sms = 0;
-
+// SM count of the current device, cached per device ordinal (several host
+// threads may launch at once: the cache entries are atomics).
 static int num_sms() {
-  if (g_num_sms == 0) {
-    int dev = 0;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&g_num_sms, cudaDevAttrMultiProcessorCount, dev);
-    if (g_num_sms <= 0) g_num_sms = 148;
+  constexpr int kMaxDevices = 64;
+  static std::atomic<int> cache[kMaxDevices];
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return 148;
+  int n = cache[dev].load(std::memory_order_relaxed);
+  if (n <= 0) {
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+    cache[dev].store(n, std::memory_order_relaxed);
   }
-  return g_num_sms;
+  return n;
 }
 
 template <int HD>

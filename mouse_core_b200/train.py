@@ -6,8 +6,9 @@ heads produce per-step Q values and ``DqnObjective`` (objectives/dqn.py:
 116-213) computes the TD loss, followed by ``loss.backward()`` and
 ``optimizer.step()``. Here the packed rows of a step are split across ranks
 (one process per GPU); each rank runs forward/backward on its rows through
-the tcgen05 attention, the summed gradients cross NVLink in ONE all-reduce
-of a flat fp32 buffer (NCCL), and every rank applies the same optimizer
+the tcgen05 attention, the summed gradients cross NVLink in ONE logical
+all-reduce (NCCL, fp32), cut into buckets launched from backward hooks so it
+overlaps the last row's backward, and every rank applies the same optimizer
 update. Nothing else is communicated.
 
 ``td_loss`` restates the reference's TD loss for the synthetic workload, with
@@ -43,55 +44,124 @@ def td_loss(q: torch.Tensor, q_target: torch.Tensor, action: torch.Tensor, rewar
 
 
 class GradientAllReduce:
-    """Sum the gradients of ``params`` across ranks with one collective.
+    """Sum the gradients of ``params`` across ranks: one logical all-reduce
+    per step, cut into buckets that go out while the backward still runs.
 
-    Gradients are packed into one persistent fp32 buffer, all-reduced once
-    (sum), scaled by ``scale`` and written back. With a single rank it only
-    applies the scale, in place, and never allocates the buffer.
+    Parameters are grouped into fp32 buckets of about ``bucket_bytes``, last
+    registered first (the order the backward finishes them). A hook on every
+    parameter (``register_post_accumulate_grad_hook``) counts its bucket's
+    final gradients once the reducer is armed; a full bucket is copied into its
+    buffer and all-reduced asynchronously (NCCL on its own stream, after the
+    gradient kernels of the current stream). Buckets always launch in index
+    order, so every rank issues the same collectives in the same order even
+    if its hooks fire in another one; ``__call__`` launches whatever the hooks
+    did not (parameters without a gradient count as zeros), waits, scales and
+    writes the sums back into ``.grad``.
+
+    Use: ``arm()`` right before a step's last backward (earlier backwards of
+    the step only accumulate), then ``__call__(scale)`` after it. Without
+    ``arm()`` the call reduces every bucket itself (no overlap). With one rank
+    nothing is exchanged or allocated: the call only scales.
     """
 
-    def __init__(self, params, group=None):
+    def __init__(self, params, group=None, bucket_bytes: int = 64 << 20):
         self.params = [p for p in params if p.requires_grad]
         self.group = group
         self.device = self.params[0].device if self.params else torch.device("cpu")
-        self._flat = None
+        self.world = dist.get_world_size(group) if dist.is_available() and dist.is_initialized() else 1
+        self.buckets: list[list[int]] = []
+        cur, size = [], 0
+        for i in reversed(range(len(self.params))):
+            cur.append(i)
+            size += self.params[i].numel() * 4
+            if size >= bucket_bytes:
+                self.buckets.append(cur)
+                cur, size = [], 0
+        if cur:
+            self.buckets.append(cur)
+        self._bucket_of = {i: b for b, idx in enumerate(self.buckets) for i in idx}
+        self._flat: list[torch.Tensor | None] = [None] * len(self.buckets)
+        self._works: list = [None] * len(self.buckets)
+        self._pending = [len(b) for b in self.buckets]
+        self._next = 0
+        self._armed = False
+        self._hooks = []
+        if self.world > 1:
+            for i, p in enumerate(self.params):
+                self._hooks.append(p.register_post_accumulate_grad_hook(self._hook(i)))
+
+    def _hook(self, i: int):
+        def on_grad(_param):
+            if not self._armed:
+                return
+            b = self._bucket_of[i]
+            self._pending[b] -= 1
+            while self._next < len(self.buckets) and self._pending[self._next] == 0:
+                self._launch(self._next)
+                self._next += 1
+        return on_grad
+
+    def _buffer(self, b: int) -> torch.Tensor:
+        if self._flat[b] is None:
+            n = sum(self.params[i].numel() for i in self.buckets[b])
+            self._flat[b] = torch.zeros(n, dtype=torch.float32, device=self.device)
+        return self._flat[b]
+
+    def _launch(self, b: int) -> None:
+        flat = self._buffer(b)
+        grads = [self.params[i].grad for i in self.buckets[b]]
+        if all(g is not None for g in grads):
+            torch.cat([g.reshape(-1) for g in grads], out=flat)
+        else:
+            o = 0
+            for i, g in zip(self.buckets[b], grads):
+                n = self.params[i].numel()
+                if g is None:
+                    flat[o:o + n].zero_()
+                else:
+                    flat[o:o + n].copy_(g.reshape(-1))
+                o += n
+        self._works[b] = dist.all_reduce(flat, op=dist.ReduceOp.SUM, group=self.group, async_op=True)
 
     @property
     def flat(self) -> torch.Tensor:
-        """The fp32 exchange buffer, allocated on first use (multi-rank only)."""
-        if self._flat is None:
-            n = sum(p.numel() for p in self.params)
-            self._flat = torch.zeros(n, dtype=torch.float32, device=self.device)
-        return self._flat
+        """All buckets' exchange buffers as one tensor (a copy; for inspection)."""
+        return torch.cat([self._buffer(b) for b in range(len(self.buckets))]) if self.buckets else torch.zeros(0)
+
+    def arm(self) -> None:
+        """The next backward is the step's last: launch buckets as they fill."""
+        if self.world > 1:
+            self._pending = [len(b) for b in self.buckets]
+            self._next = 0
+            self._armed = True
 
     def __call__(self, scale: float = 1.0) -> None:
-        world = dist.get_world_size(self.group) if dist.is_available() and dist.is_initialized() else 1
-        if world == 1:
-            # nothing to exchange: scale in place, no round trip through the buffer
+        if self.world == 1:
+            # nothing to exchange: scale in place, no round trip through a buffer
             if scale != 1.0:
                 grads = [p.grad for p in self.params if p.grad is not None]
                 if grads:
                     torch._foreach_mul_(grads, scale)
             return
-        o = 0
-        for p in self.params:
-            n = p.numel()
-            if p.grad is None:
-                self.flat[o:o + n].zero_()
-            else:
-                self.flat[o:o + n].copy_(p.grad.reshape(-1))
-            o += n
-        if world > 1:
-            dist.all_reduce(self.flat, op=dist.ReduceOp.SUM, group=self.group)
-        if scale != 1.0:
-            self.flat.mul_(scale)
-        o = 0
-        for p in self.params:
-            n = p.numel()
-            if p.grad is None:
-                p.grad = torch.empty_like(p)
-            p.grad.copy_(self.flat[o:o + n].view_as(p.grad))
-            o += n
+        self._armed = False
+        while self._next < len(self.buckets):  # the buckets the hooks did not launch
+            self._launch(self._next)
+            self._next += 1
+        for b, work in enumerate(self._works):
+            work.wait()
+            flat = self._flat[b]
+            if scale != 1.0:
+                flat.mul_(scale)
+            idx = self.buckets[b]
+            for i in idx:
+                if self.params[i].grad is None:
+                    self.params[i].grad = torch.empty_like(self.params[i])
+            sizes = [self.params[i].numel() for i in idx]
+            grads = [self.params[i].grad for i in idx]
+            torch._foreach_copy_(grads, [t.view_as(g) for t, g in zip(flat.split(sizes), grads)])
+        self._works = [None] * len(self.buckets)
+        self._next = 0
+        self._pending = [len(b) for b in self.buckets]
 
 
 class ActionValueHead(torch.nn.Module):
@@ -147,11 +217,13 @@ class PackedDQNTrainer:
         device scalar (no host sync)."""
         self.opt.zero_grad(set_to_none=True)
         loss_sum = torch.zeros((), device=self.reduce.device)
-        for row in rows:
+        for r, row in enumerate(rows):
             emb = self.embedding(row.token_ids)
             h = self._forward(model=self.model, embeds=emb, sequence_ids=row.sequence_ids)
             q = self.head(h.float())
             loss = td_loss(q, row.q_target, row.action, row.reward, row.done, row.sequence_ids)
+            if r == len(rows) - 1:
+                self.reduce.arm()  # gradients become final during this backward
             (loss / total_rows).backward()
             loss_sum = loss_sum + loss.detach()
         self.reduce()

@@ -34,22 +34,31 @@ def _free_port():
     return port
 
 
-def _worker(rank, world, port, out):
+def _worker(rank, world, port, out, armed, bucket_bytes):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
         model = _tiny()
         rows = _batches()
         mine = rows[rank::world]
-        for x in mine:
-            (model(x).pow(2).mean() / len(rows)).backward()
-        GradientAllReduce(model.parameters())()
+        reduce = GradientAllReduce(model.parameters(), bucket_bytes=bucket_bytes)
+        for step in range(2):  # the reducer is reused across steps
+            model.zero_grad(set_to_none=True)
+            for i, x in enumerate(mine):
+                if armed and i == len(mine) - 1:
+                    reduce.arm()  # buckets go out from the last backward's hooks
+                (model(x).pow(2).mean() / len(rows)).backward()
+            reduce()
         out[rank] = [p.grad.clone() for p in model.parameters()]
+        out[f"buckets{rank}"] = len(reduce.buckets)
     finally:
         dist.destroy_process_group()
 
 
-def test_one_allreduce_matches_single_process_gradient():
+@pytest.mark.parametrize("armed,bucket_bytes", [(False, 64 << 20), (True, 64 << 20), (True, 100)])
+def test_one_allreduce_matches_single_process_gradient(armed, bucket_bytes):
+    """One logical all-reduce per step, in one bucket or (100-byte buckets)
+    two, launched by __call__ or from the backward hooks."""
     model = _tiny()
     rows = _batches()
     for x in rows:
@@ -59,7 +68,7 @@ def test_one_allreduce_matches_single_process_gradient():
     out = manager.dict()
     ctx = mp.get_context("spawn")
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, out)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, out, armed, bucket_bytes)) for r in range(2)]
     for p in procs:
         p.start()
     for p in procs:
@@ -68,6 +77,51 @@ def test_one_allreduce_matches_single_process_gradient():
     for rank in range(2):
         for a, b in zip(out[rank], ref):
             assert torch.allclose(a, b, atol=1e-6)
+    assert out["buckets0"] == (2 if bucket_bytes == 100 else 1)
+
+
+def _dead_peer_worker(rank, port, out):
+    """Rank 1 stops before the step's all-reduce (it never joins it and exits
+    later); rank 0 must get an error from the process group's timeout instead
+    of waiting forever."""
+    import time
+    from datetime import timedelta
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=2, timeout=timedelta(seconds=3))
+    model = _tiny()
+    (model(_batches()[rank]).pow(2).mean()).backward()
+    if rank == 1:
+        time.sleep(8)  # gone from the step: no collective
+        out[rank] = "left"
+        return
+    t0 = time.monotonic()
+    try:
+        GradientAllReduce(model.parameters())()
+        out[rank] = "no error"
+    except Exception as e:  # the process group reports the missing peer
+        out[rank] = f"error after {time.monotonic() - t0:.1f}s: {type(e).__name__}"
+
+
+def test_dead_peer_ends_the_allreduce_with_an_error():
+    manager = mp.Manager()
+    out = manager.dict()
+    ctx = mp.get_context("spawn")
+    port = _free_port()
+    procs = [ctx.Process(target=_dead_peer_worker, args=(r, port, out)) for r in range(2)]
+    for p in procs:
+        p.start()
+    try:
+        for p in procs:
+            p.join(timeout=90)
+    finally:
+        for p in procs:
+            if p.is_alive():
+                p.kill()
+    assert out.get(1) == "left"
+    msg = out.get(0, "no result (hung)")
+    assert msg.startswith("error after"), msg
+    assert float(msg.split()[2].rstrip("s:")) < 30, msg
 
 
 def test_single_rank_reduce_only_scales():
