@@ -32,12 +32,20 @@ std::mutex g_noalloc_mutex;
 uint8_t* g_noalloc_base[kNoAllocMaxDevices] = {};
 
 // Device address of the scratch array on the current device (looked up once
-// per device, with that device current).
-int noalloc_scratch_address(uint8_t** out) {
+// per device, with that device current). The kernels run on `stream`, so the
+// stream must belong to that same device: the address is only valid there.
+int noalloc_scratch_address(cudaStream_t stream, uint8_t** out) {
   int dev = -1;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
   if (dev < 0 || dev >= kNoAllocMaxDevices) return fail(MB_ERR_UNSUPPORTED, "device ordinal out of range");
+  int stream_dev = -1;
+  e = cudaStreamGetDevice(stream, &stream_dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaStreamGetDevice");
+  if (stream_dev != dev)
+    return fail(MB_ERR_INVALID_ARG, "the stream belongs to device " + std::to_string(stream_dev) +
+                                        " but device " + std::to_string(dev) +
+                                        " is current; make the stream's device current first");
   std::lock_guard<std::mutex> lock(g_noalloc_mutex);
   if (!g_noalloc_base[dev]) {
     void* p = nullptr;
@@ -67,7 +75,7 @@ extern "C" int mb_decode_attention_noalloc(const void* q, const void* k_pool, co
                                       std::to_string((size_t)MB_NOALLOC_SCRATCH_BYTES) +
                                       "); use mb_decode_attention with a caller-provided workspace");
   uint8_t* scratch = nullptr;
-  if ((rc = noalloc_scratch_address(&scratch))) return rc;
+  if ((rc = noalloc_scratch_address((cudaStream_t)stream, &scratch))) return rc;
   // plan_ready = 0: the work list is rebuilt and the merge counters cleared on
   // every call, so nothing depends on what the previous call left behind.
   return mb_decode_attention(q, k_pool, v_pool, num_pages, block_table, max_pages, q_pos, kv_len, batch, q_len,

@@ -5,9 +5,12 @@ the pointers its framework handed it, or a process whose device memory
 belongs to another framework's allocator — so they cannot pass the workspace
 mb_decode_attention needs. mb_decode_attention_noalloc runs the same kernels
 out of a scratch array compiled into the library. Here it is called through
-the C ABI twice in a row (the second call finds the first call's leftovers in
-the shared scratch) and each result must match the workspace entry point
-within the 2e-2 max-abs tolerance of the other attention tests.
+the C ABI twice in a row, first on a shape with many long rows (many split
+work items, so partial results fill much of the scratch), then on a smaller
+one that reuses the scratch the first call left behind; each result must
+match the workspace entry point within the 2e-2 max-abs tolerance of the
+other attention tests, and neither call may change the device memory in use
+(torch's allocator or the driver's free-memory count).
 
 This file sorts last so that a run stopping at the first failure has already
 run every other test.
@@ -25,11 +28,11 @@ import torch
 ATOL = 2e-2
 
 
-def _case(B, Hq, Hkv, hd, page, S, seed, dev):
+def _case(B, Hq, Hkv, hd, page, S, seed, dev, max_before=3000):
     rng = np.random.default_rng(seed)
     n_new = rng.integers(0, S + 1, size=B)
     n_new[0] = S
-    before = rng.integers(0, 3000, size=B)
+    before = rng.integers(0, max_before, size=B)
     before[-1] = 0
     lens = (before + n_new).astype(np.int64)
     npg = [math.ceil(int(L) / page) for L in lens]
@@ -62,17 +65,33 @@ def test_noalloc_matches_workspace_entry_point_twice():
     build.build()
     lib = _lib.load()
     dev = torch.device("cuda")
-    # Two calls in a row with different shapes, split mode (the scratch is used).
-    for B, Hq, Hkv, hd, page, S, seed in ((9, 16, 8, 128, 128, 1, 1), (6, 32, 8, 64, 64, 2, 2)):
-        q, kp, vp, bt, q_pos, kv_len, max_kv = _case(B, Hq, Hkv, hd, page, S, seed, dev)
+    # Split mode both times (the scratch is used): the first shape has many
+    # long rows, so it lays out more work items and partials than the second.
+    shapes = ((96, 16, 8, 128, 128, 1, 1, 12000), (6, 32, 8, 64, 64, 2, 2, 3000))
+    cases = []
+    for B, Hq, Hkv, hd, page, S, seed, max_before in shapes:
+        q, kp, vp, bt, q_pos, kv_len, max_kv = _case(B, Hq, Hkv, hd, page, S, seed, dev, max_before)
         ref = K.decode_attention(q, kp, vp, bt, q_pos, kv_len, hd ** -0.5, max_kv)
-        out = torch.full_like(q, float("nan"))
-        stream = torch.cuda.current_stream().cuda_stream
+        cases.append((B, Hq, Hkv, hd, page, S, q, kp, vp, bt, q_pos, kv_len, max_kv, ref,
+                      torch.full_like(q, float("nan"))))
+    need = [lib.mb_decode_workspace_bytes(c[0], c[2], (c[1] // c[2]) * c[5], c[3], c[12]) for c in cases]
+    assert need[0] > 4 * need[1] and need[0] <= 32 * 1024 * 1024, need
+    torch.cuda.synchronize()
+    used_before = torch.cuda.memory_allocated()
+    free_before, _ = torch.cuda.mem_get_info()
+    stream = torch.cuda.current_stream().cuda_stream
+    for B, Hq, Hkv, hd, page, S, q, kp, vp, bt, q_pos, kv_len, max_kv, ref, out in cases:
         rc = lib.mb_decode_attention_noalloc(q.data_ptr(), kp.data_ptr(), vp.data_ptr(), kp.shape[0], bt.data_ptr(),
                                              bt.shape[1], q_pos.data_ptr(), kv_len.data_ptr(), B, S, Hq, Hkv, hd,
                                              page, ctypes.c_float(hd ** -0.5), max_kv, out.data_ptr(), stream)
         assert rc == 0, lib.mb_last_error()
-        torch.cuda.synchronize()
+    torch.cuda.synchronize()
+    free_after, _ = torch.cuda.mem_get_info()
+    assert torch.cuda.memory_allocated() == used_before
+    # The workspace the first shape would need (several MiB) was never allocated.
+    assert free_before - free_after < need[0] // 2, (free_before, free_after, need[0])
+    for c in cases:
+        ref, out = c[13], c[14]
         assert torch.isfinite(out.float()).all()
         err = (out.float() - ref.float()).abs().max().item()
         assert err <= ATOL, f"noalloc differs from the workspace entry point by {err}"
