@@ -271,14 +271,20 @@ def run_ours(args):
     task_end = (ids_host & 1).astype(bool)
     ones = [1] * ENVS
 
+    def embed_fn(ids):
+        return table[ids]
+
+    def act_fn(h):
+        return head(h).argmax(-1)
+
     def device_step(i):
+        # One graph per step: embedding gather, both layers, the fp32 head and
+        # the argmax (PagedDecodeSession.decode_step).
         if i > 0:
             gone = np.flatnonzero(task_end[i - 1])
             if gone.size:
                 sess.reset_rows(gone)
-        emb = table[ids_dev[i].long()].view(ENVS, 1, HIDDEN)
-        h = sess.forward(embeds=emb, lengths=ones)
-        return head(h[:, -1]).argmax(-1)
+        return sess.decode_step(ids_dev[i], ones, embed_fn, act_fn)
 
     for i in range(W):
         device_step(i)
@@ -332,8 +338,7 @@ def run_ours(args):
             ends[task_end[i - 1]] = 0
         history[rows, ends] = ids_host[i]
         ends += 1
-    dec = GrowRebuildDecoder(model, ENVS, lambda ids: table[ids], max_cache=max_cache, start_cache=start_cache,
-                             per_row=True)
+    dec = GrowRebuildDecoder(model, ENVS, embed_fn, max_cache=max_cache, start_cache=start_cache, per_row=True)
     dec.adopt(sess, np.zeros(ENVS, dtype=np.int64), ends)
     pending = task_end[total + K_steps - 1].copy()
     ends[pending] = 0
@@ -345,8 +350,8 @@ def run_ours(args):
         tok = transition_ids(rng, act, ENVS)
         history[rows, ends] = tok
         ends[:] += 1
-        h, _ = dec.step(history, ends, 0, rebuild=pending)
-        h_act.copy_(head(h[:, -1]).argmax(-1), non_blocking=True)
+        a, _ = dec.step(history, ends, 0, rebuild=pending, head=act_fn)
+        h_act.copy_(a, non_blocking=True)
         torch.cuda.current_stream().synchronize()
         act = h_act.numpy().copy()
         pending = (tok & 1).astype(bool)
@@ -509,14 +514,19 @@ def run_large_batch(args):
     ones = [1] * envs
     call = [0]
 
+    def embed_fn(ids):
+        return table[ids]
+
+    def act_fn(h):
+        return head(h).argmax(-1)
+
     def device_step():
         i = call[0]
         call[0] += 1
         gone = np.flatnonzero(retire[i])
         if gone.size:
             sess.reset_rows(gone)
-        h = sess.forward(embeds=table[ids_dev[i].long()].view(envs, 1, D), lengths=ones)
-        return head(h[:, -1]).argmax(-1)
+        return sess.decode_step(ids_dev[i], ones, embed_fn, act_fn)
 
     def barrier():
         if world > 1:
@@ -540,8 +550,7 @@ def run_large_batch(args):
             sess.reset_rows(gone)
         h_ids.numpy()[:] = transition_ids(rng, act, envs)
         d_ids.copy_(h_ids, non_blocking=True)
-        h = sess.forward(embeds=table[d_ids.long()].view(envs, 1, D), lengths=ones)
-        h_act.copy_(head(h[:, -1]).argmax(-1), non_blocking=True)
+        h_act.copy_(sess.decode_step(d_ids, ones, embed_fn, act_fn), non_blocking=True)
         torch.cuda.current_stream().synchronize()
         act = h_act.numpy().copy()
 
@@ -574,7 +583,7 @@ def run_large_batch(args):
     sess.attn_events = []
     kv_sum = 0
     for _ in range(K_steps):
-        kv_sum += int(sess._len.sum()) + envs
+        kv_sum += int(sess._len[~retire[call[0]]].sum()) + envs  # after this step's retirements
         device_step()
     torch.cuda.synchronize()
     attn_ms = [a.elapsed_time(b) for a, b in sess.attn_events]
@@ -635,6 +644,25 @@ def grpo_config(n_gpus, roots):
             "hidden": HIDDEN, "q_heads": HEADS, "kv_heads": KV_HEADS, "head_dim": HEAD_DIM,
             "page_size": GR["page"], "parallelism": f"roots sharded x{n_gpus} (no collective)",
             "l2": "inputs larger than L2: each decode step reads ~90 GB of KV per GPU"}
+
+
+def unique_kv_tokens(sess, rows):
+    """Distinct cached tokens that ``rows`` of a paged session read: a page
+    several rows share (a forked prefix) counts once, with the most tokens
+    any of them reads from it."""
+    P = sess.page_size
+    L = sess._len[rows]
+    npg = (L + P - 1) // P
+    width = int(npg.max()) if len(rows) else 0
+    if width == 0:
+        return 0
+    cols = np.arange(width)
+    held = cols[None, :] < npg[:, None]
+    ids = sess.pages.table[rows][:, :width][held]
+    tok = np.minimum(P, L[:, None] - cols[None, :] * P)[held]
+    best = np.zeros(sess.pages.num_pages, dtype=np.int64)
+    np.maximum.at(best, ids, tok)
+    return int(best.sum())
 
 
 def run_grpo(args):
@@ -707,11 +735,16 @@ def run_grpo(args):
                                          for _ in range(n_step_calls)])).to(dev)
     call = [0]
 
+    def embed_fn(ids):
+        return table[ids]
+
+    def act_fn(h):  # the branches' actions (the roots sit out)
+        return head(h[R:]).argmax(-1)
+
     def device_step():
         i = call[0]
         call[0] += 1
-        h = sess.forward(embeds=table[ids_dev[i].long()].view(B, 1, D), lengths=step_len)
-        return head(h[R:, -1]).argmax(-1)
+        return sess.decode_step(ids_dev[i], step_len, embed_fn, act_fn)
 
     for _ in range(W):
         device_step()
@@ -732,7 +765,8 @@ def run_grpo(args):
     sess.attn_events = []
     kv_sum = 0
     for _ in range(K_steps):
-        kv_sum += int(sess._len.sum()) + NB
+        # Shared prefix pages are read by every branch of a root but count once.
+        kv_sum += unique_kv_tokens(sess, np.arange(R, B)) + NB
         device_step()
     torch.cuda.synchronize()
     attn_ms = [a.elapsed_time(b) for a, b in sess.attn_events]
@@ -748,8 +782,7 @@ def run_grpo(args):
         call[0] += 1
         h_ids.numpy()[:] = transition_ids(rng, act, B)
         d_ids.copy_(h_ids, non_blocking=True)
-        h = sess.forward(embeds=table[d_ids.long()].view(B, 1, D), lengths=step_len)
-        h_act.copy_(head(h[R:, -1]).argmax(-1), non_blocking=True)
+        h_act.copy_(sess.decode_step(d_ids, step_len, embed_fn, act_fn), non_blocking=True)
         torch.cuda.current_stream().synchronize()
         act[R:] = h_act.numpy()
 
@@ -801,9 +834,8 @@ def run_grpo(args):
                             "unit": "GB/s", "frac": round(achieved / peak, 4), "traffic": None,
                             "algorithmic_bytes_per_launch": int(attn_bytes), "avg_launch_ms": round(attn_avg_ms, 5),
                             "launches_timed": len(attn_ms),
-                            "note": "algorithmic bytes count every branch's whole context; the 16 branches of a "
-                                    "root read the same shared prefix pages back to back and L2 serves the "
-                                    "repeats, so the fraction can exceed 1"},
+                            "note": "algorithmic bytes count each distinct cached token once per launch: a "
+                                    "prefix page the 16 branches of a root share is counted once"},
                "cpu_baseline": None,
                "cpu_baseline_note": "not run: one step reads ~90 GB of KV; the decode line's CPU port covers the "
                                     "same per-token arithmetic",
@@ -1103,15 +1135,26 @@ def _oracle_decoder(seed):
     return odec.DecoderOracle(sd, cfg)
 
 
+def _host_threads():
+    """Give numpy's BLAS and torch every host core (torchrun sets
+    OMP_NUM_THREADS=1 for its ranks) and return the thread count in use."""
+    import torch
+    from threadpoolctl import threadpool_info, threadpool_limits
+
+    n = os.cpu_count() or 1
+    threadpool_limits(limits=n)
+    torch.set_num_threads(n)
+    blas = [i.get("num_threads", 1) for i in threadpool_info() if i.get("user_api") == "blas"]
+    return max(blas) if blas else torch.get_num_threads()
+
+
 def cpu_baseline(seconds=15.0, sample_envs=16):
     """Oracle port of the reference decode step on the host cores: one S=1
     step of ``sample_envs`` envs whose caches hold U[64,4096] random slots,
     repeated for about ``seconds``."""
-    import torch
-
     from oracle import decoder as odec
 
-    torch.set_num_threads(os.cpu_count() or 1)
+    threads = _host_threads()
     dec = _oracle_decoder(0)
     rng = np.random.default_rng(7)
     lens = rng.integers(LEN_LO, LEN_HI + 1, size=sample_envs)
@@ -1128,7 +1171,7 @@ def cpu_baseline(seconds=15.0, sample_envs=16):
         el = time.perf_counter() - t0
         if el >= seconds:
             break
-    return {"value": round(sample_envs * steps / el, 3), "unit": "env-steps/s", "cores": os.cpu_count() or 1,
+    return {"value": round(sample_envs * steps / el, 3), "unit": "env-steps/s", "cores": threads,
             "kind": "port",
             "sample": f"{steps} decode steps of {sample_envs} envs (2 layers, float64 numpy oracle restating "
                       f"FlexDecodeSession.forward), cache lengths U[64,4096], {el:.1f} s"}
@@ -1147,7 +1190,7 @@ def train_cpu_baseline(seconds=15.0, row_len=2048, layers=1):
     from mouse_core_b200.packing import flat_sequence_causal_mask, flat_sequence_position_ids
     from mouse_core_b200.train import ActionValueHead, td_loss
 
-    torch.set_num_threads(os.cpu_count() or 1)
+    threads = _host_threads()
     torch.manual_seed(0)
     bb = Qwen3Backbone(hidden_dim=HIDDEN, num_layers=layers, num_heads=HEADS, num_key_value_heads=KV_HEADS,
                        head_dim=HEAD_DIM, intermediate_size=INTER,
@@ -1168,7 +1211,7 @@ def train_cpu_baseline(seconds=15.0, row_len=2048, layers=1):
         if el >= seconds:
             break
     per_layer = row_len * steps / el * layers
-    return {"value": round(per_layer / TRAIN_LAYERS, 3), "unit": "tokens/s", "cores": os.cpu_count() or 1,
+    return {"value": round(per_layer / TRAIN_LAYERS, 3), "unit": "tokens/s", "cores": threads,
             "kind": "port", "per_layer_tokens_per_s": round(per_layer, 1),
             "sample": f"{steps} fwd+bwd passes of one {row_len}-token row (segments {segs}) through {layers} "
                       f"layer(s), fp32 dense-mask SDPA path, {el:.1f} s; value extrapolated to 28 layers"}

@@ -163,6 +163,13 @@ class PagedDecodeSession:
         self._graph = None
         self._graph_key = None
         self._graph_warm = False
+        # decode_step's graph: embedding gather + layer stack + norm + head.
+        self._step_graph = None
+        self._step_graph_key = None
+        self._step_graph_warm = False
+        self._step_ids = None
+        self._step_out = None
+        self._step_launches = 0
         self._staging = [None, None]
         self._staging_ev = [None, None]
         self._turn = 0
@@ -330,6 +337,7 @@ class PagedDecodeSession:
             self._meta_dev = torch.empty(max(n_meta, 2 * self._meta_dev.numel()), dtype=torch.int32,
                                          device=self.device)
             self._graph = None  # its captured views point at the old buffer
+            self._step_graph = None
         dev = self._meta_dev
         dev[:n_meta].copy_(buf[:n_meta], non_blocking=True)
         ev = self._staging_ev[i]
@@ -468,6 +476,86 @@ class PagedDecodeSession:
         K._count(self._graph_launches)
         return self.model.norm(self._graph_out.view(B, S, D).clone())
 
+    def _graph_key_now(self):
+        for lw in self._layers:
+            lw.refresh()
+        return (self.k_pool.data_ptr(), self._bt_dev.data_ptr(), self._meta_dev.data_ptr(), self.cap,
+                tuple(lw.version for lw in self._layers))
+
+    @torch.no_grad()
+    def decode_step(self, ids: torch.Tensor, lengths, embed, head):
+        """One step of at most one token per row, from token ids to the
+        head's output, replayed as ONE CUDA graph.
+
+        The reference's caller runs this step as separate pieces: the encoder's
+        embedding gather, ``FlexDecodeSession.forward`` with S = 1, the fp32
+        head (models/heads/swiglu.py:71-74) and ``get_action``'s argmax
+        (models/base.py:1065-1106). Here the gather, the layer stack (K1/K2
+        and the GEMMs), the final norm and ``head`` are captured together, so
+        a step costs the host one device-step metadata launch (K8) and one
+        graph launch.
+
+        Args:
+            ids: ``[B]`` token ids on the device (any value for rows that sit
+                out); copied into the graph's input buffer.
+            lengths: ``[B]`` 0/1 tokens per row (list or array).
+            embed: ``embed(ids [B]) -> [B, D]`` in the backbone's dtype.
+            head: ``head(h [B, D]) -> tensor`` (e.g. action values' argmax).
+            Both must be device-only work (no host syncs) and the same
+            callables from step to step (a new one is captured anew).
+
+        Returns the head's output: a buffer of the graph, overwritten by the
+        next step (copy it out before then). A step whose metadata the device
+        cannot make (after a multi-token call, a fork or pool growth) is
+        prepared on the host and replays the same graph; the first step runs
+        eagerly and the second captures the graph, with the same results.
+        """
+        B = self.B
+        if ids.shape[0] != B:
+            raise ValueError(f"Session was created for batch_size={B}, got {ids.shape[0]} ids.")
+        use_graph = (B > 0 and self.use_graphs and self.use_device_step and self.attn_events is None
+                     and not torch.cuda.is_current_stream_capturing())
+        if use_graph and self._step_graph is not None:
+            key = (self._graph_key_now(), id(embed), id(head))
+            if key == self._step_graph_key and self._device_step(lengths):
+                self._step_ids.copy_(ids, non_blocking=True)
+                self._step_graph.replay()
+                K._count(self._step_launches)
+                return self._step_out
+        if not use_graph:
+            h = self.forward(embeds=embed(ids).view(B, 1, -1), lengths=lengths)
+            return head(h[:, -1])
+        q_pos, kv_len, slot, _ = self.prepare(lengths, 1)
+        if self._step_graph is not None and (self._graph_key_now(), id(embed), id(head)) == self._step_graph_key:
+            # Host-prepared metadata landed in the buffers the graph reads.
+            self._step_ids.copy_(ids, non_blocking=True)
+            self._step_graph.replay()
+            K._count(self._step_launches)
+            return self._step_out
+        if not self._step_graph_warm:
+            # Eager warm-up: allocates the workspace and initialises cuBLAS.
+            self._step_graph_warm = True
+            x = embed(ids).to(self.device, self.dtype).reshape(B, -1).contiguous()
+            h = self._body(x, q_pos, kv_len, slot, 1, False)
+            return head(self.model.norm(h.view(B, 1, -1))[:, -1])
+        self._step_graph = None
+        self._step_ids = torch.empty_like(ids, device=self.device)
+        self._step_ids.copy_(ids)
+        graph = torch.cuda.CUDAGraph()
+        n0 = K.launch_count[0]
+        with torch.cuda.graph(graph):
+            xs = embed(self._step_ids).to(self.dtype).reshape(B, -1)
+            h = self._body(xs, q_pos, kv_len, slot, 1, False)
+            self._step_out = head(self.model.norm(h.view(B, 1, -1))[:, -1])
+        self._step_launches = K.launch_count[0] - n0
+        K.launch_count[0] = n0
+        self._step_graph = graph
+        self._step_graph_key = (self._graph_key_now(), id(embed), id(head))
+        self._step_args = None
+        graph.replay()  # capturing ran nothing: this step runs now
+        K._count(self._step_launches)
+        return self._step_out
+
     def _body(self, x, q_pos, kv_len, slot, S, output_hidden_states):
         """The layer stack for flattened ``x [B*S, D]``; returns the last hidden
         state (before the final norm) and, if asked, every layer's."""
@@ -481,6 +569,7 @@ class PagedDecodeSession:
             if self._workspace.numel() < need:
                 self._workspace = torch.empty(need, dtype=torch.uint8, device=self.device)
                 self._graph = None
+                self._step_graph = None
             K.decode_plan(kv_len, Hkv, R, hd, self.cap, self._workspace)
         q_pos_flat = q_pos.reshape(-1)
 

@@ -138,7 +138,7 @@ class GrowRebuildDecoder:
         return dev.view(ids.shape)
 
     @torch.no_grad()
-    def step(self, history: np.ndarray, ends, context_start=0, *, rebuild=False,
+    def step(self, history: np.ndarray, ends, context_start=0, *, rebuild=False, head=None,
              output_hidden_states: bool = False):
         """Run one call of the caller loop.
 
@@ -151,6 +151,12 @@ class GrowRebuildDecoder:
             rebuild: ``True`` forces a rebuild of every row (the reference
                 passes it when a task ended); a ``[B]`` mask or row indices
                 name the rows whose task ended (see ``rows_to_rebuild``).
+            head: Optional ``head(h [B, D]) -> tensor`` applied to each row's
+                latest hidden state (e.g. the action head and its argmax);
+                one-token calls then run gather, layers and head as one CUDA
+                graph (``PagedDecodeSession.decode_step``) and return
+                ``(head output, fed)`` — a graph buffer, valid until the next
+                call.
 
         Returns:
             ``(h, fed)``: the session output ``[B, S, D]`` (left-padded: row
@@ -189,8 +195,15 @@ class GrowRebuildDecoder:
             col = np.arange(S, dtype=np.int64)[None, :]
             src = starts[:, None] + col - (S - fed)[:, None]  # left-padded: real tokens are the last fed[b]
             ids = hist[np.arange(B)[:, None], np.clip(src, 0, max(hist.shape[1] - 1, 0))]
-        emb = self.embed(self._stage_ids(np.ascontiguousarray(ids, dtype=np.int32)))
-        out = self.session.forward(embeds=emb, lengths=fed, output_hidden_states=output_hidden_states)
+        ids_dev = self._stage_ids(np.ascontiguousarray(ids, dtype=np.int32))
+        if head is not None and not output_hidden_states:
+            if S == 1:  # gather + layers + head as one graph replay
+                out = self.session.decode_step(ids_dev[:, 0], fed, self.embed, head)
+            else:
+                out = head(self.session.forward(embeds=self.embed(ids_dev), lengths=fed)[:, -1])
+            self.cached_ends = ends.copy()
+            return out, fed
+        out = self.session.forward(embeds=self.embed(ids_dev), lengths=fed, output_hidden_states=output_hidden_states)
         self.cached_ends = ends.copy()
         if output_hidden_states:
             h, hiddens = out

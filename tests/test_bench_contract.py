@@ -28,3 +28,37 @@ def test_reference_arm_prints_one_contract_line():
     assert d["e2e"]["h2d_bytes_per_step"] == 0 and d["e2e"]["d2h_bytes_per_step"] == 0
     assert d["cpu_baseline"]["kind"] in ("port", "reference") and d["cpu_baseline"]["cores"] >= 1
     assert d["config"]["workload"].startswith("cached batched decode")
+
+
+def test_reference_arm_under_torchrun_uses_every_core():
+    """torchrun sets OMP_NUM_THREADS=1 for its ranks; the CPU arm lifts it
+    and reports the threads it ran with."""
+    env = dict(os.environ, OMP_NUM_THREADS="1")
+    proc = subprocess.run([sys.executable, os.path.join(ROOT, "bench.py"), "--impl", "reference", "--steps", "1",
+                           "--warmup", "3", "--cpu-seconds", "1"], capture_output=True, text=True, timeout=600,
+                          cwd=ROOT, env=env)
+    assert proc.returncode == 0, proc.stderr[-2000:]
+    d = json.loads([ln for ln in proc.stdout.splitlines() if ln.startswith("{")][0])
+    assert d["cpu_baseline"]["cores"] == (os.cpu_count() or 1)
+
+
+def test_unique_kv_tokens_counts_shared_pages_once():
+    import numpy as np
+
+    sys.path.insert(0, ROOT)
+    import bench
+    from mouse_core_b200.pages import PageTable
+
+    class Sess:  # the attributes the helper reads
+        page_size = 4
+
+    s = Sess()
+    s.pages = PageTable(3, 16, 4, 4)
+    s.pages.allocate(np.array([3, 0, 0]))   # root: 10 tokens in 3 pages
+    s.pages.share(1, 0, 2)                  # branch 1 shares the root's 2 full pages
+    s.pages.share(2, 0, 2)                  # branch 2 as well
+    s.pages.allocate(np.array([0, 1, 1]))   # each branch's own third page
+    s._len = np.array([10, 11, 9])
+    # branches: 8 shared tokens once + 3 + 1 private
+    assert bench.unique_kv_tokens(s, np.array([1, 2])) == 8 + 3 + 1
+    assert bench.unique_kv_tokens(s, np.array([0, 1, 2])) == 8 + 2 + 3 + 1

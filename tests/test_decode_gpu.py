@@ -473,3 +473,61 @@ def test_decode_step_meta_reports_rows_past_the_table():
     assert q_pos.cpu().tolist() == [70, 64, 128]
     assert slot.cpu().tolist() == [6 * page + 6, 11 * page + 0, -1]
     assert kv_len.cpu().tolist() == [71, 65, 129]
+
+
+def test_decode_step_graph_matches_forward_and_head():
+    """decode_step runs the embedding gather, the layer stack, the final norm
+    and the caller's head as one CUDA graph; step for step it must give what
+    forward + the head give, across page openings, rows sitting out, rows
+    emptied between steps (K8 restarts) and a multi-token chunk between."""
+    dev = _dev()
+    from mouse_core_b200.backbone import Qwen3Backbone
+
+    torch.manual_seed(13)
+    bb = Qwen3Backbone(hidden_dim=256, num_layers=2, num_heads=4, num_key_value_heads=2, head_dim=128)
+    bb = bb.to(device=dev, dtype=torch.bfloat16).eval()
+    B, page, V = 5, 64, 50
+    g = torch.Generator().manual_seed(1)
+    table = torch.randn(V, 256, generator=g).bfloat16().to(dev)
+    w = (torch.randn(4, 256, generator=g) / 16).to(dev)
+
+    def embed(ids):
+        return table[ids]
+
+    def head(h):
+        return torch.nn.functional.linear(torch.nn.functional.rms_norm(h.float(), (256,), None, 1e-5), w)
+
+    fast = bb.decode_session(batch_size=B, capacity=64, page_size=page)
+    ref = bb.decode_session(batch_size=B, capacity=64, page_size=page)
+    ref.use_graphs = False
+    rng = np.random.default_rng(3)
+    pre = rng.integers(0, V, size=(B, 40))
+    lens = [40, 7, 0, 33, 12]
+    x = table[torch.from_numpy(pre).to(dev)]
+    fast.forward(embeds=x, lengths=lens)
+    ref.forward(embeds=x, lengths=lens)
+    replays = 0
+    for step in range(90):
+        if step in (20, 50):
+            fast.reset_rows([1, 4])
+            ref.reset_rows([1, 4])
+        if step == 35:  # a multi-token chunk: the host path, then graph steps again
+            ids2 = torch.from_numpy(rng.integers(0, V, size=(B, 3))).to(dev)
+            a = fast.forward(embeds=table[ids2], lengths=[3, 0, 2, 1, 3])
+            b = ref.forward(embeds=table[ids2], lengths=[3, 0, 2, 1, 3])
+            assert (a.float() - b.float()).abs().max().item() <= 1e-2
+        ids = torch.from_numpy(rng.integers(0, V, size=B)).to(dev)
+        n = [1] * B if step % 7 else [1, 0, 1, 1, 0]
+        before = fast._step_graph
+        out = fast.decode_step(ids, n, embed, head).clone()
+        replays += before is not None and fast._step_graph is before
+        h = ref.forward(embeds=table[ids].view(B, 1, 256), lengths=n)
+        want = head(h[:, -1])
+        live = torch.tensor(n, device=dev).bool()
+        err = (out[live] - want[live]).abs().max().item()
+        assert err <= 1e-3 * max(1.0, want.abs().max().item()), (step, err)
+        assert fast._len.tolist() == ref._len.tolist()
+    assert replays >= 70, replays
+    from mouse_core_b200 import _lib
+
+    assert _lib.device_status() == 0
