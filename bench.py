@@ -398,6 +398,16 @@ def run_ours(args):
     peak = float(peaks.get("hbm_gbs", 6650.0))
     peak_src = "measured" if "hbm_gbs" in peaks else "fallback"
 
+    # The packed training step on the same ranks (strong scaling of the
+    # 8-row step: rows split across ranks, one gradient all-reduce per step).
+    del dec, sess
+    torch.cuda.empty_cache()
+    train = None
+    if not args.no_train:
+        train = train_measure(dev, world, rank, local, TRAIN_ROWS, max(1, min(K_steps, args.train_steps)),
+                              W)
+        torch.cuda.empty_cache()
+
     out = None
     if rank == 0:
         value = ENVS * world * K_steps / (ms_max * 1e-3)
@@ -433,6 +443,8 @@ def run_ours(args):
             "per_rank": {"fields": ["device_ms_per_step", "host_us_to_issue_step", "e2e_ms_per_step"],
                          "ranks": per_rank_rows},
         }
+    if rank == 0 and train is not None:
+        out["train"] = train
     if rank == 0 and not args.no_packed:
         out["packed_attention"] = packed_attention_metric(dev)
     if rank == 0 and not args.no_cpu_baseline:
@@ -997,11 +1009,6 @@ def run_train(args):
     import torch
     import torch.distributed as dist
 
-    from mouse_core_b200 import _lib
-    from mouse_core_b200 import kernels as K
-    from mouse_core_b200.backbone import Qwen3Backbone
-    from mouse_core_b200.train import ActionValueHead, PackedDQNTrainer, PackedRow
-
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
@@ -1011,12 +1018,27 @@ def run_train(args):
         from datetime import timedelta
 
         dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
+    out = train_measure(dev, world, rank, local, args.train_rows, args.steps, args.warmup)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return out
+
+
+def train_measure(dev, world, rank, local, rows_total, K_steps, W):
+    """Time the packed DQN training step on this process group (every rank
+    calls it; rank 0 gets the result line, the others None)."""
+    import torch
+    import torch.distributed as dist
+
+    from mouse_core_b200 import _lib
+    from mouse_core_b200 import kernels as K
+    from mouse_core_b200.backbone import Qwen3Backbone
+    from mouse_core_b200.train import ActionValueHead, PackedDQNTrainer, PackedRow
 
     def barrier():
         if world > 1:
             dist.barrier()
-
-    rows_total = args.train_rows
     torch.manual_seed(0)
     bb = Qwen3Backbone(hidden_dim=HIDDEN, num_layers=TRAIN_LAYERS, num_heads=HEADS, num_key_value_heads=KV_HEADS,
                        head_dim=HEAD_DIM, intermediate_size=INTER,
@@ -1041,7 +1063,6 @@ def run_train(args):
     pinned = [{k: torch.from_numpy(v).pin_memory() for k, v in r.items()} for r in host]
     h2d_bytes = sum(t.numel() * t.element_size() for p in pinned for t in p.values()) * world
 
-    W, K_steps = args.warmup, args.steps
     for _ in range(W):
         trainer.step(resident, rows_total)
     torch.cuda.synchronize()
@@ -1110,10 +1131,9 @@ def run_train(args):
                             "flops_note": "per GPU: (6 * 440.4M params * tokens + 3.5 x algorithmic attention "
                                           "forward) / n_gpus"},
                "attention_fwd_flops_per_step": attn_fwd, "loss": float(loss.item()),
-               "gpu_launches": int(launches), "clocks": clk, "device_status": status}
-    if world > 1:
-        dist.barrier()
-        dist.destroy_process_group()
+               "gpu_launches": int(launches), "clocks": clk, "device_status": status,
+               "all_reduce": "one logical fp32 all-reduce per step in 64 MB buckets launched from backward "
+                             "hooks during the last row's backward (none with one GPU)"}
     return out
 
 
@@ -1255,6 +1275,9 @@ def main():
                     "smaller values only for profiling captures)")
     ap.add_argument("--train", action="store_true", help="time the packed DQN training step instead of decode")
     ap.add_argument("--train-rows", type=int, default=TRAIN_ROWS, help="16384-token rows per training step")
+    ap.add_argument("--no-train", action="store_true", help="leave the training object out of the decode line")
+    ap.add_argument("--train-steps", type=int, default=5,
+                    help="timed steps of the training object in the decode line (its warm-up is --warmup)")
     ap.add_argument("--large-batch", action="store_true",
                     help="time large-batch decode (Llama-3.2-1B arch, 512 envs/GPU, hd 64) instead")
     ap.add_argument("--lb-envs", type=int, default=LB["envs"], help="envs per GPU for --large-batch")

@@ -209,7 +209,10 @@ struct SplitSmem {
 };
 
 // Item metadata slot layout (ints after the Q rows).
-enum : int { kMetaB = 0, kMetaH, kMetaBegin, kMetaEnd, kMetaChunks, kMetaKvEnd = 8 };
+// kMetaB < 0 marks the end of the CTA's work; kMetaItem is the item's index
+// in the row-ordered work list (entry * Hkv + kv-head), where its partial
+// result goes.
+enum : int { kMetaB = 0, kMetaH, kMetaBegin, kMetaEnd, kMetaChunks, kMetaItem, kMetaKvEnd = 8 };
 
 template <int HD>
 __global__ void __launch_bounds__(160, 2) split_decode_kernel(const __grid_constant__ CUtensorMap kmap,
@@ -263,23 +266,36 @@ __global__ void __launch_bounds__(160, 2) split_decode_kernel(const __grid_const
       prefetch_tensormap(&kmap);
       prefetch_tensormap(&vmap);
     }
+    // Items are taken one at a time from a counter over the longest-first
+    // order, so CTAs that drew short items simply take more of them.
     uint32_t it = 0;  // tiles issued (lane 0)
-    int k = 0;
-    for (int item = blockIdx.x; item < n_items; item += gridDim.x, ++k) {
+    for (int k = 0;; ++k) {
       const int slot = k & 1;
       bool ok = true;
+      int next = -1;
       if (lane == 0) {
         ok = mbar_wait_abortable(&item_empty[slot], ((k >> 1) & 1) ^ 1, kDevTimeoutEmpty, abort) &&
              !*reinterpret_cast<volatile int*>(abort);
+        if (ok) next = atomicAdd(&p.work[0], 1);
       }
       if (!__shfl_sync(0xffffffffu, ok, 0)) break;
-      const int2 ent = p.entries[item / p.Hkv];
+      next = __shfl_sync(0xffffffffu, next, 0);
+      uint8_t* sq = slots + slot * SM::SLOT;
+      int* meta = reinterpret_cast<int*>(sq + 16 * SM::QROW);
+      if (next >= n_items) {  // no work left: tell the consumers
+        if (lane == 0) {
+          meta[kMetaB] = -1;
+          mbar_arrive(&item_full[slot]);
+        }
+        break;
+      }
+      const int e = p.order[next / p.Hkv];
+      const int item = e * p.Hkv + next % p.Hkv;
+      const int2 ent = p.entries[e];
       const int h = item % p.Hkv, b = ent.x;
       const int len = p.kv_len[b];
       const int t_begin = ent.y * p.chunk_tokens;
       const int t_end = min(t_begin + p.chunk_tokens, len);
-      uint8_t* sq = slots + slot * SM::SLOT;
-      int* meta = reinterpret_cast<int*>(sq + 16 * SM::QROW);
       if (lane < 16) {
         int ke = len;
         if (lane < R) ke = min(p.q_pos[(size_t)b * p.S + lane / p.G] + 1, len);
@@ -291,6 +307,7 @@ __global__ void __launch_bounds__(160, 2) split_decode_kernel(const __grid_const
         meta[kMetaBegin] = t_begin;
         meta[kMetaEnd] = t_end;
         meta[kMetaChunks] = p.row_chunks[b];
+        meta[kMetaItem] = item;
       }
       for (int c = lane; c < 16 * (HD / 8); c += 32) {
         const int r = c / (HD / 8), ch = c % (HD / 8);
@@ -325,6 +342,13 @@ __global__ void __launch_bounds__(160, 2) split_decode_kernel(const __grid_const
     if (lane == 0) {
       for (uint32_t j = it > (uint32_t)C::STAGES ? it - C::STAGES : 0u; j < it; ++j)
         mbar_drain(&full[j % C::STAGES], (j / C::STAGES) & 1);
+      // The last CTA to finish taking work resets the counter for the next
+      // launch (the next layer replays this kernel without a new plan).
+      __threadfence();
+      if (atomicAdd(&p.work[1], 1) == (int)gridDim.x - 1) {
+        p.work[0] = 0;
+        p.work[1] = 0;
+      }
     }
     return;
   }
@@ -333,8 +357,7 @@ __global__ void __launch_bounds__(160, 2) split_decode_kernel(const __grid_const
   const int tid = threadIdx.x;  // 0..127
   const int gid = lane >> 2, tig = lane & 3;
   uint32_t it = 0;
-  int k = 0;
-  for (int item = blockIdx.x; item < n_items; item += gridDim.x, ++k) {
+  for (int k = 0;; ++k) {
     const int slot = k & 1;
     bool alive = mbar_wait_abortable(&item_full[slot], (k >> 1) & 1, kDevTimeoutFull, abort);
     // All four consumer warps leave together (the barrier's OR) when any of
@@ -343,6 +366,8 @@ __global__ void __launch_bounds__(160, 2) split_decode_kernel(const __grid_const
     const uint8_t* sq = slots + slot * SM::SLOT;
     const int* meta = reinterpret_cast<const int*>(sq + 16 * SM::QROW);
     const int b = meta[kMetaB], h = meta[kMetaH];
+    if (b < 0) break;  // the producer found no work left (the same value for every consumer)
+    const int item = meta[kMetaItem];
     const int t_begin = meta[kMetaBegin], t_end = meta[kMetaEnd];
     const int nchunks = meta[kMetaChunks];
     const int kv_end[2] = {meta[kMetaKvEnd + gid], meta[kMetaKvEnd + gid + 8]};
@@ -462,18 +487,34 @@ __global__ void __launch_bounds__(160, 2) split_decode_kernel(const __grid_const
 }
 
 // Work list of (row, chunk) entries: max(1, ceil(kv_len / chunk)) per row,
-// in row order, plus each row's first entry and chunk count. Also clears the
-// per-(row, kv-head) tickets. One CTA of 1024 threads.
+// in row order, plus each row's first entry and chunk count, and the order
+// the split kernel's CTAs take the entries in: longest chunk first (a
+// counting sort on the chunk length in 64-token units), so the short chunks
+// of short rows fill in at the end instead of leaving a tail of long ones.
+// Also clears the per-(row, kv-head) tickets and the work counters. One CTA
+// of 1024 threads.
+constexpr int kPlanBuckets = 33;  // chunk lengths 0 .. 2048 in 64-token units
+
 __global__ void __launch_bounds__(1024) decode_plan_kernel(const int32_t* kv_len, int B, int Hkv, int chunk,
                                                            int max_entries, int2* entries, int* n_entries,
-                                                           int* row_start, int* row_chunks, int* counters) {
+                                                           int* row_start, int* row_chunks, int* counters,
+                                                           int* order, int* work) {
   __shared__ int warp_tot[32];
   __shared__ int total_s;
+  __shared__ int hist[kPlanBuckets];
+  __shared__ int cursor[kPlanBuckets];
   const int tid = threadIdx.x;
+  if (tid < kPlanBuckets) hist[tid] = 0;
   const int per = (B + 1023) / 1024;
   const int r0 = min(tid * per, B), r1 = min(r0 + per, B);
+  const int unit = max(chunk / (kPlanBuckets - 1), 1);
+  auto bucket = [&](int len, int j) {  // descending rank of chunk j of a row of `len` tokens
+    const int sz = min(chunk, max(len - j * chunk, 0));
+    return (kPlanBuckets - 1) - min((sz + unit - 1) / unit, kPlanBuckets - 1);
+  };
   int cnt = 0;
   for (int r = r0; r < r1; ++r) cnt += max(1, (max(kv_len[r], 0) + chunk - 1) / chunk);
+  __syncthreads();
   // block exclusive scan of cnt
   const int lane = tid & 31, w = tid >> 5;
   int x = cnt;
@@ -500,19 +541,43 @@ __global__ void __launch_bounds__(1024) decode_plan_kernel(const int32_t* kv_len
   if (total > max_entries) {
     if (tid == 0) {
       *n_entries = 0;
+      work[0] = 0;
+      work[1] = 0;
       report(kDevBadPage);
     }
     return;
   }
   for (int r = r0; r < r1; ++r) {
-    const int c = max(1, (max(kv_len[r], 0) + chunk - 1) / chunk);
+    const int len = max(kv_len[r], 0);
+    const int c = max(1, (len + chunk - 1) / chunk);
     row_start[r] = base;
     row_chunks[r] = c;
-    for (int j = 0; j < c; ++j) entries[base + j] = make_int2(r, j);
+    for (int j = 0; j < c; ++j) {
+      entries[base + j] = make_int2(r, j);
+      atomicAdd(&hist[bucket(len, j)], 1);
+    }
     base += c;
   }
   for (int i = tid; i < B * Hkv; i += 1024) counters[i] = 0;
-  if (tid == 0) *n_entries = total;
+  __syncthreads();
+  if (tid == 0) {
+    int acc = 0;
+    for (int k = 0; k < kPlanBuckets; ++k) {
+      cursor[k] = acc;
+      acc += hist[k];
+    }
+    *n_entries = total;
+    work[0] = 0;
+    work[1] = 0;
+  }
+  __syncthreads();
+  base = x - cnt + (w > 0 ? warp_tot[w - 1] : 0);
+  for (int r = r0; r < r1; ++r) {
+    const int len = max(kv_len[r], 0);
+    const int c = max(1, (len + chunk - 1) / chunk);
+    for (int j = 0; j < c; ++j) order[atomicAdd(&cursor[bucket(len, j)], 1)] = base + j;
+    base += c;
+  }
 }
 
 // Block mode: one CTA per (64-row query block, kv-head, row).
@@ -648,6 +713,8 @@ size_t decode_workspace_layout(int B, int Hkv, int R, int head_dim, int max_kv_l
   lay->row_start = off;  off = up(off + (size_t)B * sizeof(int));
   lay->row_chunks = off; off = up(off + (size_t)B * sizeof(int));
   lay->counters = off;   off = up(off + (size_t)B * Hkv * sizeof(int));
+  lay->order = off;      off = up(off + max_entries * sizeof(int));
+  lay->work = off;       off = up(off + 2 * sizeof(int));
   lay->part_lse = off;   off = up(off + max_entries * Hkv * R * sizeof(float));
   lay->part_o = off;     off = up(off + max_entries * Hkv * R * head_dim * sizeof(float));
   lay->total = off;
@@ -703,7 +770,8 @@ cudaError_t launch_decode_plan(const int32_t* kv_len, int B, int Hkv, int head_d
       kv_len, B, Hkv, (int)decode_chunk_tokens(head_dim), (int)lay.max_entries,
       reinterpret_cast<int2*>(ws + lay.entries), reinterpret_cast<int*>(ws + lay.n_entries),
       reinterpret_cast<int*>(ws + lay.row_start), reinterpret_cast<int*>(ws + lay.row_chunks),
-      reinterpret_cast<int*>(ws + lay.counters));
+      reinterpret_cast<int*>(ws + lay.counters), reinterpret_cast<int*>(ws + lay.order),
+      reinterpret_cast<int*>(ws + lay.work));
   return cudaGetLastError();
 }
 
@@ -716,6 +784,8 @@ cudaError_t launch_decode_attention(const CUtensorMap& km, const CUtensorMap& vm
     p.row_start = reinterpret_cast<const int*>(ws + lay.row_start);
     p.row_chunks = reinterpret_cast<const int*>(ws + lay.row_chunks);
     p.counters = reinterpret_cast<int*>(ws + lay.counters);
+    p.order = reinterpret_cast<const int*>(ws + lay.order);
+    p.work = reinterpret_cast<int*>(ws + lay.work);
     p.part_lse = reinterpret_cast<float*>(ws + lay.part_lse);
     p.part_o = reinterpret_cast<float*>(ws + lay.part_o);
     const size_t max_items = lay.max_entries * p.Hkv;

@@ -27,13 +27,15 @@ struct AttnParams {
   const int* row_start;
   const int* row_chunks;
   int* counters;
+  const int* order;            // entries, longest chunk first (the order CTAs take work in)
+  int* work;                   // [2]: next work item, CTAs finished (zeroed by the plan and the last CTA)
   float* part_lse;
   float* part_o;
 };
 
 struct WorkspaceLayout {
   size_t max_entries;
-  size_t entries, n_entries, row_start, row_chunks, counters, part_lse, part_o;
+  size_t entries, n_entries, row_start, row_chunks, counters, order, work, part_lse, part_o;
   size_t total;
 };
 

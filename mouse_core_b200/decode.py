@@ -38,6 +38,7 @@ import torch.nn.functional as F
 
 from mouse_core_b200 import kernels as K
 from mouse_core_b200.pages import PageTable
+from mouse_core_b200.trace import nvtx_range
 
 DEFAULT_PAGE_SIZE = 128
 
@@ -422,6 +423,10 @@ class PagedDecodeSession:
         ``lengths[b]`` real trailing tokens per row). Returns hidden states
         ``[B, S, D]`` (pad positions meaningless) and, with
         ``output_hidden_states=True``, the tuple of per-layer hidden states."""
+        with nvtx_range("decode_step" if embeds.shape[1] == 1 else "prefill"):
+            return self._forward(embeds, lengths, output_hidden_states)
+
+    def _forward(self, embeds, lengths, output_hidden_states):
         B, S, D = embeds.shape
         if B != self.B:
             raise ValueError(f"Session was created for batch_size={self.B}, got {B}.")
@@ -510,6 +515,10 @@ class PagedDecodeSession:
         prepared on the host and replays the same graph; the first step runs
         eagerly and the second captures the graph, with the same results.
         """
+        with nvtx_range("decode_step_graph"):
+            return self._decode_step(ids, lengths, embed, head)
+
+    def _decode_step(self, ids, lengths, embed, head):
         B = self.B
         if ids.shape[0] != B:
             raise ValueError(f"Session was created for batch_size={B}, got {ids.shape[0]} ids.")

@@ -39,6 +39,7 @@ import numpy as np
 import torch
 
 from mouse_core_b200 import kernels as K
+from mouse_core_b200.trace import nvtx_range
 
 
 class _SegmentAttention(torch.autograd.Function):
@@ -47,7 +48,8 @@ class _SegmentAttention(torch.autograd.Function):
     @staticmethod
     def forward(ctx, q, k, v, run_start, run_end, tile_lo, scale, pair_off, n_pairs):
         q, k, v = q.contiguous(), k.contiguous(), v.contiguous()
-        out, lse = K.varlen_attention_fwd(q, k, v, run_start, tile_lo, scale)
+        with nvtx_range("packed_attention_fwd"):
+            out, lse = K.varlen_attention_fwd(q, k, v, run_start, tile_lo, scale)
         ctx.save_for_backward(q, k, v, out, lse, run_start, run_end, tile_lo)
         ctx.scale = scale
         ctx.pair_off, ctx.n_pairs = pair_off, n_pairs
@@ -56,8 +58,9 @@ class _SegmentAttention(torch.autograd.Function):
     @staticmethod
     def backward(ctx, dout):
         q, k, v, out, lse, run_start, run_end, tile_lo = ctx.saved_tensors
-        dq, dk, dv = K.varlen_attention_bwd(q, k, v, out, dout.contiguous(), lse, run_start, run_end, ctx.scale,
-                                            tile_lo=tile_lo, pair_off=ctx.pair_off, n_pairs=ctx.n_pairs)
+        with nvtx_range("packed_attention_bwd"):
+            dq, dk, dv = K.varlen_attention_bwd(q, k, v, out, dout.contiguous(), lse, run_start, run_end, ctx.scale,
+                                                tile_lo=tile_lo, pair_off=ctx.pair_off, n_pairs=ctx.n_pairs)
         return dq, dk, dv, None, None, None, None, None, None
 
 

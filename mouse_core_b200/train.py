@@ -22,6 +22,8 @@ from dataclasses import dataclass
 import torch
 import torch.distributed as dist
 
+from mouse_core_b200.trace import nvtx_range
+
 
 def td_loss(q: torch.Tensor, q_target: torch.Tensor, action: torch.Tensor, reward: torch.Tensor,
             done: torch.Tensor, sequence_id: torch.Tensor, gammas=(0.99, 0.0, 0.99, 0.0, 0.0)) -> torch.Tensor:
@@ -121,7 +123,8 @@ class GradientAllReduce:
                 else:
                     flat[o:o + n].copy_(g.reshape(-1))
                 o += n
-        self._works[b] = dist.all_reduce(flat, op=dist.ReduceOp.SUM, group=self.group, async_op=True)
+        with nvtx_range(f"grad_allreduce_bucket{b}"):
+            self._works[b] = dist.all_reduce(flat, op=dist.ReduceOp.SUM, group=self.group, async_op=True)
 
     @property
     def flat(self) -> torch.Tensor:
@@ -143,6 +146,10 @@ class GradientAllReduce:
                 if grads:
                     torch._foreach_mul_(grads, scale)
             return
+        with nvtx_range("grad_allreduce_wait"):
+            self._finish(scale)
+
+    def _finish(self, scale: float) -> None:
         self._armed = False
         while self._next < len(self.buckets):  # the buckets the hooks did not launch
             self._launch(self._next)
