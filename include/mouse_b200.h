@@ -135,6 +135,13 @@ int mb_kv_append(const void* qkv, int tokens, int qkv_stride, const int32_t* pos
                  float attention_scaling, int q_heads, int kv_heads, int head_dim, int page_size,
                  long long num_pages, void* q_out, void* k_out, void* v_out, void* k_pool, void* v_pool,
                  mb_stream_t stream);
+/* The same with an fp32 qkv (the fp32 output of the QKV projection when the
+ * decode session keeps its residual stream in fp32); outputs stay bf16. */
+int mb_kv_append_f32(const float* qkv, int tokens, int qkv_stride, const int32_t* pos, const int32_t* slot,
+                     const void* q_norm_w, const void* k_norm_w, float eps, const float* inv_freq,
+                     float attention_scaling, int q_heads, int kv_heads, int head_dim, int page_size,
+                     long long num_pages, void* q_out, void* k_out, void* v_out, void* k_pool, void* v_pool,
+                     mb_stream_t stream);
 
 /* ---------------------------------------------------------------------
  * Page copy (K3): dst_pool[dst_pages[i]] = src_pool[src_pages[i]] for one
@@ -177,6 +184,17 @@ int mb_decode_step_meta(int batch, int max_pages, int page_size, const int32_t* 
 int mb_rmsnorm(const void* x, const void* residual, const void* weight, float eps, int rows, int dim, void* sum_out,
                void* norm_out, mb_stream_t stream);
 int mb_silu_mul(const void* gate_up, int rows, int inter, void* out, mb_stream_t stream);
+/* The same glue for a residual stream kept in fp32 (the decode session's
+ * default): the reference rounds the stream to bf16 at every residual add
+ * (flex_decode.py:231, 233); here only the GEMM inputs are rounded, once.
+ * mb_rmsnorm_f32: sum_out = x + delta in fp32 (x fp32, or x_bf16 for the
+ *   bf16 embeddings entering the first layer; delta fp32 or NULL; sum_out may
+ *   be x or NULL), norm_out = bf16(RMSNorm(sum) * w).
+ * mb_silu_mul_f32: out = bf16(silu(gate) * up) for an fp32 gate_up [rows, 2I],
+ *   I a multiple of 4, gate_up 16-byte aligned. */
+int mb_rmsnorm_f32(const float* x, const void* x_bf16, const float* delta, const void* weight, float eps, int rows,
+                   int dim, float* sum_out, void* norm_out, mb_stream_t stream);
+int mb_silu_mul_f32(const float* gate_up, int rows, int inter, void* out, mb_stream_t stream);
 
 /* ---------------------------------------------------------------------
  * Packed varlen segment-causal attention forward (K5, tcgen05).

@@ -190,11 +190,14 @@ int mb_decode_attention(const void* q, const void* k_pool, const void* v_pool, i
   return e == cudaSuccess ? MB_OK : cuda_fail(e, "decode attention launch");
 }
 
-int mb_kv_append(const void* qkv, int tokens, int qkv_stride, const int32_t* pos, const int32_t* slot,
-                 const void* q_norm_w, const void* k_norm_w, float eps, const float* inv_freq,
-                 float attention_scaling, int q_heads, int kv_heads, int head_dim, int page_size,
-                 long long num_pages, void* q_out, void* k_out, void* v_out, void* k_pool, void* v_pool,
-                 mb_stream_t stream) {
+}  // extern "C"
+
+namespace {
+int kv_append_impl(const void* qkv, bool qkv_f32, int tokens, int qkv_stride, const int32_t* pos,
+                   const int32_t* slot, const void* q_norm_w, const void* k_norm_w, float eps, const float* inv_freq,
+                   float attention_scaling, int q_heads, int kv_heads, int head_dim, int page_size,
+                   long long num_pages, void* q_out, void* k_out, void* v_out, void* k_pool, void* v_pool,
+                   mb_stream_t stream) {
   if (tokens < 0) return fail(MB_ERR_INVALID_ARG, "tokens must be >= 0");
   if (tokens == 0) return MB_OK;
   if (head_dim != 64 && head_dim != 128) return fail(MB_ERR_UNSUPPORTED, "head_dim must be 64 or 128");
@@ -202,13 +205,16 @@ int mb_kv_append(const void* qkv, int tokens, int qkv_stride, const int32_t* pos
   if (!qkv || !pos || !inv_freq || !q_out) return fail(MB_ERR_INVALID_ARG, "a required pointer is NULL");
   if (qkv_stride < (q_heads + 2 * kv_heads) * head_dim)
     return fail(MB_ERR_INVALID_ARG, "qkv_stride smaller than (q_heads + 2 * kv_heads) * head_dim");
-  if (qkv_stride % 2 || !aligned(qkv, 4) || !aligned(q_out, 4))
-    return fail(MB_ERR_INVALID_ARG, "qkv/q_out must be 4-byte aligned with an even stride");
+  if (qkv_stride % 2 || !aligned(qkv, qkv_f32 ? 8 : 4) || !aligned(q_out, 4))
+    return fail(MB_ERR_INVALID_ARG, "qkv (4-byte, 8 for fp32) / q_out (4-byte) must be aligned with an even stride");
   if ((k_pool == nullptr) != (v_pool == nullptr)) return fail(MB_ERR_INVALID_ARG, "pass both pools or neither");
   if (k_pool && (!slot || page_size <= 0 || num_pages <= 0))
     return fail(MB_ERR_INVALID_ARG, "paged append needs slot, page_size and num_pages");
   mb::AppendParams p{};
-  p.qkv = static_cast<const __nv_bfloat16*>(qkv);
+  if (qkv_f32)
+    p.qkv_f32 = static_cast<const float*>(qkv);
+  else
+    p.qkv = static_cast<const __nv_bfloat16*>(qkv);
   p.T = tokens;
   p.qkv_stride = qkv_stride;
   p.pos = pos;
@@ -230,6 +236,29 @@ int mb_kv_append(const void* qkv, int tokens, int qkv_stride, const int32_t* pos
   p.num_slots = k_pool ? num_pages * (long long)page_size : 0;
   cudaError_t e = mb::launch_append(p, (cudaStream_t)stream);
   return e == cudaSuccess ? MB_OK : cuda_fail(e, "kv append launch");
+}
+}  // namespace
+
+extern "C" {
+
+int mb_kv_append(const void* qkv, int tokens, int qkv_stride, const int32_t* pos, const int32_t* slot,
+                 const void* q_norm_w, const void* k_norm_w, float eps, const float* inv_freq,
+                 float attention_scaling, int q_heads, int kv_heads, int head_dim, int page_size,
+                 long long num_pages, void* q_out, void* k_out, void* v_out, void* k_pool, void* v_pool,
+                 mb_stream_t stream) {
+  return kv_append_impl(qkv, false, tokens, qkv_stride, pos, slot, q_norm_w, k_norm_w, eps, inv_freq,
+                        attention_scaling, q_heads, kv_heads, head_dim, page_size, num_pages, q_out, k_out, v_out,
+                        k_pool, v_pool, stream);
+}
+
+int mb_kv_append_f32(const float* qkv, int tokens, int qkv_stride, const int32_t* pos, const int32_t* slot,
+                     const void* q_norm_w, const void* k_norm_w, float eps, const float* inv_freq,
+                     float attention_scaling, int q_heads, int kv_heads, int head_dim, int page_size,
+                     long long num_pages, void* q_out, void* k_out, void* v_out, void* k_pool, void* v_pool,
+                     mb_stream_t stream) {
+  return kv_append_impl(qkv, true, tokens, qkv_stride, pos, slot, q_norm_w, k_norm_w, eps, inv_freq,
+                        attention_scaling, q_heads, kv_heads, head_dim, page_size, num_pages, q_out, k_out, v_out,
+                        k_pool, v_pool, stream);
 }
 
 int mb_page_copy(const void* src_pool, void* dst_pool, const int32_t* src_pages, const int32_t* dst_pages, int n,
@@ -269,6 +298,31 @@ int mb_rmsnorm(const void* x, const void* residual, const void* weight, float ep
                                      static_cast<__nv_bfloat16*>(sum_out), static_cast<__nv_bfloat16*>(norm_out),
                                      (cudaStream_t)stream);
   return e == cudaSuccess ? MB_OK : cuda_fail(e, "rmsnorm launch");
+}
+
+int mb_rmsnorm_f32(const float* x, const void* x_bf16, const float* delta, const void* weight, float eps, int rows,
+                   int dim, float* sum_out, void* norm_out, mb_stream_t stream) {
+  if (rows < 0 || dim <= 0 || dim % 2) return fail(MB_ERR_INVALID_ARG, "rows >= 0 and an even dim > 0 required");
+  if (rows == 0) return MB_OK;
+  if ((x == nullptr) == (x_bf16 == nullptr)) return fail(MB_ERR_INVALID_ARG, "pass exactly one of x and x_bf16");
+  if (!weight || !norm_out) return fail(MB_ERR_INVALID_ARG, "NULL pointer");
+  if ((x && !aligned(x, 8)) || (x_bf16 && !aligned(x_bf16, 4)) || (delta && !aligned(delta, 8)) ||
+      (sum_out && !aligned(sum_out, 8)) || !aligned(norm_out, 4) || !aligned(weight, 4))
+    return fail(MB_ERR_INVALID_ARG, "misaligned buffer (fp32 buffers 8-byte, bf16 4-byte)");
+  cudaError_t e = mb::launch_rmsnorm_f32(x, static_cast<const __nv_bfloat16*>(x_bf16), delta,
+                                         static_cast<const __nv_bfloat16*>(weight), eps, rows, dim, sum_out,
+                                         static_cast<__nv_bfloat16*>(norm_out), (cudaStream_t)stream);
+  return e == cudaSuccess ? MB_OK : cuda_fail(e, "rmsnorm_f32 launch");
+}
+
+int mb_silu_mul_f32(const float* gate_up, int rows, int inter, void* out, mb_stream_t stream) {
+  if (rows < 0 || inter <= 0 || inter % 4) return fail(MB_ERR_INVALID_ARG, "rows >= 0 and inter % 4 == 0 required");
+  if (rows == 0) return MB_OK;
+  if (!gate_up || !out || !aligned(gate_up, 16) || !aligned(out, 8))
+    return fail(MB_ERR_INVALID_ARG, "NULL or misaligned pointer (gate_up 16-byte, out 8-byte)");
+  cudaError_t e = mb::launch_silu_mul_f32(gate_up, rows, inter, static_cast<__nv_bfloat16*>(out),
+                                          (cudaStream_t)stream);
+  return e == cudaSuccess ? MB_OK : cuda_fail(e, "silu_mul_f32 launch");
 }
 
 int mb_silu_mul(const void* gate_up, int rows, int inter, void* out, mb_stream_t stream) {

@@ -113,4 +113,88 @@ cudaError_t launch_silu_mul(const __nv_bfloat16* gate_up, int rows, int I, __nv_
   return cudaGetLastError();
 }
 
+// ---------------------------------------------------------------- fp32 residual stream
+// The same layer glue for decoding with an fp32 residual stream: the sum of
+// the residual and the sublayer output stays fp32 (no bf16 rounding at the
+// adds), and only the GEMM inputs are rounded to bf16, once each. One CTA per
+// row; `x` is the fp32 stream (or `x_bf16`, the bf16 embeddings entering the
+// first layer), `delta` the fp32 sublayer output or null; `sum_out` may alias
+// `x` (every element is read and written by the same thread).
+__global__ void __launch_bounds__(256) rmsnorm_f32_kernel(const float* x, const __nv_bfloat16* x_bf16,
+                                                          const float* delta, const __nv_bfloat16* w, float eps,
+                                                          int D, float* sum_out, __nv_bfloat16* norm_out) {
+  const size_t row = blockIdx.x;
+  __shared__ float red[8];
+  float ss = 0.f;
+  for (int i = threadIdx.x * 2; i < D; i += blockDim.x * 2) {
+    float2 v = x ? *reinterpret_cast<const float2*>(x + row * D + i)
+                 : __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(x_bf16 + row * D + i));
+    if (delta) {
+      const float2 d = *reinterpret_cast<const float2*>(delta + row * D + i);
+      v.x += d.x;
+      v.y += d.y;
+    }
+    if (sum_out) *reinterpret_cast<float2*>(sum_out + row * D + i) = v;
+    ss += v.x * v.x + v.y * v.y;
+  }
+  ss = warp_sum(ss);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float t = (threadIdx.x < blockDim.x / 32) ? red[threadIdx.x] : 0.f;
+    t = warp_sum(t);
+    if (threadIdx.x == 0) red[0] = t;
+  }
+  __syncthreads();
+  const float r = rsqrtf(red[0] / (float)D + eps);
+  for (int i = threadIdx.x * 2; i < D; i += blockDim.x * 2) {
+    float2 v;
+    if (sum_out) {
+      v = *reinterpret_cast<const float2*>(sum_out + row * D + i);
+    } else {
+      v = x ? *reinterpret_cast<const float2*>(x + row * D + i)
+            : __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(x_bf16 + row * D + i));
+      if (delta) {
+        const float2 d = *reinterpret_cast<const float2*>(delta + row * D + i);
+        v.x += d.x;
+        v.y += d.y;
+      }
+    }
+    const float2 w2 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(w + i));
+    *reinterpret_cast<__nv_bfloat162*>(norm_out + row * D + i) = __floats2bfloat162_rn(v.x * r * w2.x, v.y * r * w2.y);
+  }
+}
+
+cudaError_t launch_rmsnorm_f32(const float* x, const __nv_bfloat16* x_bf16, const float* delta,
+                               const __nv_bfloat16* w, float eps, int rows, int D, float* sum_out,
+                               __nv_bfloat16* norm_out, cudaStream_t stream) {
+  if (rows <= 0) return cudaSuccess;
+  const int threads = std::min(256, std::max(32, ((D / 2 + 31) / 32) * 32));
+  rmsnorm_f32_kernel<<<rows, threads, 0, stream>>>(x, x_bf16, delta, w, eps, D, sum_out, norm_out);
+  return cudaGetLastError();
+}
+
+// out = bf16(silu(g) * u) for an fp32 [rows, 2I] = gate | up, 4 elements per thread.
+__global__ void __launch_bounds__(128) silu_mul_f32_kernel(const float* __restrict__ gu, int rows, int I,
+                                                           __nv_bfloat16* __restrict__ out) {
+  const int c = blockIdx.x * blockDim.x + threadIdx.x;
+  if (c >= (I >> 2)) return;
+  for (int row = blockIdx.y; row < rows; row += gridDim.y) {
+    const size_t gbase = (size_t)row * 2 * I + (size_t)c * 4;
+    const float4 g = *reinterpret_cast<const float4*>(gu + gbase);
+    const float4 u = *reinterpret_cast<const float4*>(gu + gbase + I);
+    uint2 o;
+    o.x = pack_bf16x2(g.x / (1.f + expf(-g.x)) * u.x, g.y / (1.f + expf(-g.y)) * u.y);
+    o.y = pack_bf16x2(g.z / (1.f + expf(-g.z)) * u.z, g.w / (1.f + expf(-g.w)) * u.w);
+    *reinterpret_cast<uint2*>(out + (size_t)row * I + (size_t)c * 4) = o;
+  }
+}
+
+cudaError_t launch_silu_mul_f32(const float* gate_up, int rows, int I, __nv_bfloat16* out, cudaStream_t stream) {
+  if (rows <= 0 || I <= 0) return cudaSuccess;
+  const int by = std::min(rows, 65535);
+  silu_mul_f32_kernel<<<dim3((unsigned)((I / 4 + 127) / 128), (unsigned)by), 128, 0, stream>>>(gate_up, rows, I, out);
+  return cudaGetLastError();
+}
+
 }  // namespace mb

@@ -47,7 +47,8 @@ cudaError_t launch_decode_attention(const CUtensorMap& km, const CUtensorMap& vm
                                     const WorkspaceLayout& lay, uint8_t* ws, bool split, cudaStream_t stream);
 
 struct AppendParams {
-  const __nv_bfloat16* qkv;  // [T, qkv_stride]: q | k | v
+  const __nv_bfloat16* qkv;  // [T, qkv_stride]: q | k | v (bf16), or
+  const float* qkv_f32;      // the same in fp32 (exactly one of the two is set)
   int T, qkv_stride;
   const int32_t* pos;        // [T] RoPE position
   const int32_t* slot;       // [T] page * page_size + offset, or -1 (not cached)
@@ -73,6 +74,12 @@ cudaError_t launch_rmsnorm(const __nv_bfloat16* x, const __nv_bfloat16* residual
                            float eps, int rows, int D, __nv_bfloat16* sum_out, __nv_bfloat16* norm_out,
                            cudaStream_t stream);
 cudaError_t launch_silu_mul(const __nv_bfloat16* gate_up, int rows, int I, __nv_bfloat16* out, cudaStream_t stream);
+// fp32 residual stream variants: sum = x (+ delta) kept in fp32, norm rounded
+// once to bf16; SiLU product of an fp32 gate|up rounded once to bf16.
+cudaError_t launch_rmsnorm_f32(const float* x, const __nv_bfloat16* x_bf16, const float* delta,
+                               const __nv_bfloat16* w, float eps, int rows, int D, float* sum_out,
+                               __nv_bfloat16* norm_out, cudaStream_t stream);
+cudaError_t launch_silu_mul_f32(const float* gate_up, int rows, int I, __nv_bfloat16* out, cudaStream_t stream);
 
 struct VarlenParams {
   int L, Hq, Hkv, G, heads_per_cta, head_dim;

@@ -41,13 +41,22 @@ __global__ void __launch_bounds__(256) append_kernel(const AppendParams p) {
   }
 
   for (int hh = warp; hh < nheads; hh += blockDim.x / 32) {
-    const __nv_bfloat16* src = p.qkv + (size_t)t * p.qkv_stride + (size_t)hh * HD + lane * E;
+    const size_t src_off = (size_t)t * p.qkv_stride + (size_t)hh * HD + lane * E;
     float x[E];
+    if (p.qkv_f32) {  // fp32 projection output (fp32 residual-stream decoding)
 #pragma unroll
-    for (int e = 0; e < E; e += 2) {
-      const __nv_bfloat162 v2 = *reinterpret_cast<const __nv_bfloat162*>(src + e);
-      x[e] = __low2float(v2);
-      x[e + 1] = __high2float(v2);
+      for (int e = 0; e < E; e += 2) {
+        const float2 v2 = *reinterpret_cast<const float2*>(p.qkv_f32 + src_off + e);
+        x[e] = v2.x;
+        x[e + 1] = v2.y;
+      }
+    } else {
+#pragma unroll
+      for (int e = 0; e < E; e += 2) {
+        const __nv_bfloat162 v2 = *reinterpret_cast<const __nv_bfloat162*>(p.qkv + src_off + e);
+        x[e] = __low2float(v2);
+        x[e + 1] = __high2float(v2);
+      }
     }
     const bool is_q = hh < p.Hq;
     const bool is_k = !is_q && hh < p.Hq + p.Hkv;

@@ -52,6 +52,38 @@ def _round_up(value: int, multiple: int) -> int:
 _STEP_RESTART = 1 << 30
 
 
+def rope_frequencies(rotary, config, device) -> tuple[torch.Tensor, float]:
+    """RoPE inverse frequencies in fp32 as the model config defines them, and
+    the cos/sin scaling.
+
+    A transformers rotary module keeps its frequencies in an ``inv_freq``
+    buffer, and casting the model to bf16 casts that buffer too: the
+    frequencies keep 8 mantissa bits, so the rotation angle ``pos * f`` of a
+    token at position 500 is off by up to ~1 radian at the highest frequency.
+    The reference's bf16 decode inherits that (flex_decode.py:204 calls the
+    module). The frequencies are a function of the config, so they are
+    recomputed here in fp32 with transformers' own initialiser for the
+    config's rope type (Llama-3 scaling included); rope types whose module
+    updates the buffer at run time fall back to the buffer."""
+    rope_type = getattr(rotary, "rope_type", "default")
+    try:
+        if rope_type == "default":
+            fn = type(rotary).compute_default_rope_parameters
+        elif rope_type in ("dynamic", "longrope"):
+            fn = None
+        else:
+            from transformers.modeling_rope_utils import ROPE_INIT_FUNCTIONS
+
+            fn = ROPE_INIT_FUNCTIONS[rope_type]
+        if fn is not None:
+            inv, scaling = fn(config, device)
+            return inv.to(device=device, dtype=torch.float32), float(scaling)
+    except Exception:  # an unknown rotary module: use what it holds
+        pass
+    return (rotary.inv_freq.to(device=device, dtype=torch.float32),
+            float(getattr(rotary, "attention_scaling", 1.0)))
+
+
 class _LayerWeights:
     """Per-layer weights; QKV and gate/up are concatenated once per weight
     version so each runs as one GEMM."""
@@ -168,6 +200,10 @@ class PagedDecodeSession:
         self._step_graph = None
         self._step_graph_key = None
         self._step_graph_warm = False
+        # Keep the residual stream in fp32 between the layers (only GEMM
+        # inputs, q/k/v and the pool are bf16); False restores the modules'
+        # bf16 rounding at every add.
+        self.residual_fp32 = True
         self._step_ids = None
         self._step_out = None
         self._step_launches = 0
@@ -175,8 +211,7 @@ class PagedDecodeSession:
         self._staging_ev = [None, None]
         self._turn = 0
         self._layers = [_LayerWeights(layer, self.n_heads, self.n_kv_heads, self.head_dim) for layer in hf.layers]
-        self.inv_freq = hf.rotary_emb.inv_freq.to(device=self.device, dtype=torch.float32)
-        self.attention_scaling = float(getattr(hf.rotary_emb, "attention_scaling", 1.0))
+        self.inv_freq, self.attention_scaling = rope_frequencies(hf.rotary_emb, cfg, self.device)
         # When a list, each attention launch appends its (start, end) CUDA
         # events recorded on the launching stream (used for roofline timing).
         self.attn_events: list | None = None
@@ -442,7 +477,7 @@ class PagedDecodeSession:
                 self._graph_x.copy_(x)
                 self._graph.replay()
                 K._count(self._graph_launches)
-                return self.model.norm(self._graph_out.view(B, S, D).clone())
+                return self._final(self._graph_out.view(B, S, D), copy=True)
         q_pos, kv_len, slot, max_kv = self.prepare(lengths, S)
         if B == 0 or S == 0:
             h = x.view(B, S, D)
@@ -453,8 +488,8 @@ class PagedDecodeSession:
             out = self._body(x, q_pos, kv_len, slot, S, output_hidden_states)
             if output_hidden_states:
                 h, hiddens = out
-                return self.model.norm(h.view(B, S, D)), tuple(t.view(B, S, D) for t in hiddens)
-            return self.model.norm(out.view(B, S, D))
+                return self._final(h.view(B, S, D)), tuple(t.view(B, S, D).to(self.dtype) for t in hiddens)
+            return self._final(out.view(B, S, D))
         for lw in self._layers:
             lw.refresh()
         key = (self.k_pool.data_ptr(), self._bt_dev.data_ptr(), self._meta_dev.data_ptr(), self.cap,
@@ -463,7 +498,7 @@ class PagedDecodeSession:
             if not self._graph_warm:
                 # Eager warm-up: allocates the workspace and initialises cuBLAS.
                 self._graph_warm = True
-                return self.model.norm(self._body(x, q_pos, kv_len, slot, 1, False).view(B, S, D))
+                return self._final(self._body(x, q_pos, kv_len, slot, 1, False).view(B, S, D))
             self._graph = None
             self._graph_x = torch.empty_like(x)
             self._graph_x.copy_(x)
@@ -479,7 +514,15 @@ class PagedDecodeSession:
             self._graph_x.copy_(x)
         self._graph.replay()
         K._count(self._graph_launches)
-        return self.model.norm(self._graph_out.view(B, S, D).clone())
+        return self._final(self._graph_out.view(B, S, D), copy=True)
+
+    def _final(self, h: torch.Tensor, copy: bool = False) -> torch.Tensor:
+        """The model's final norm, in the model's dtype (a fresh tensor when
+        ``h`` is a graph buffer)."""
+        h = self.model.norm(h)
+        if h.dtype != self.dtype:
+            return h.to(self.dtype)
+        return h.clone() if copy else h
 
     def _graph_key_now(self):
         for lw in self._layers:
@@ -568,6 +611,8 @@ class PagedDecodeSession:
     def _body(self, x, q_pos, kv_len, slot, S, output_hidden_states):
         """The layer stack for flattened ``x [B*S, D]``; returns the last hidden
         state (before the final norm) and, if asked, every layer's."""
+        if self.residual_fp32:
+            return self._body_f32(x, q_pos, kv_len, slot, S, output_hidden_states)
         B = self.B
         D = x.shape[-1]
         Hq, Hkv, hd = self.n_heads, self.n_kv_heads, self.head_dim
@@ -613,6 +658,73 @@ class PagedDecodeSession:
         if output_hidden_states:
             return h, hiddens
         return h
+
+    def _plan(self, kv_len, S):
+        """Split-KV work list for this call (once, shared by every layer)."""
+        B, Hkv, hd = self.B, self.n_kv_heads, self.head_dim
+        R = (self.n_heads // Hkv) * S
+        split = R <= 16
+        if split:
+            need = K.decode_workspace_bytes(B, Hkv, R, hd, self.cap)
+            if self._workspace.numel() < need:
+                self._workspace = torch.empty(need, dtype=torch.uint8, device=self.device)
+                self._graph = None
+                self._step_graph = None
+            K.decode_plan(kv_len, Hkv, R, hd, self.cap, self._workspace)
+        return split
+
+    def _body_f32(self, x, q_pos, kv_len, slot, S, output_hidden_states):
+        """The layer stack with an fp32 residual stream: the embeddings enter
+        it exactly, every residual add and every projection output stays
+        fp32 (cuBLAS bf16 GEMMs with fp32 outputs), and only the GEMM inputs
+        are rounded to bf16 (the normalised activations, the attention output,
+        the SiLU product) together with the q/k/v the attention kernel and the
+        bf16 page pool take. The reference's bf16 modules round the stream at
+        every add and every op output instead; against the fp32 forward this
+        path's greedy actions agree more often (measured on the decode
+        benchmark's model shape). Returns fp32 hidden states."""
+        B = self.B
+        Hq, Hkv, hd = self.n_heads, self.n_kv_heads, self.head_dim
+        split = self._plan(kv_len, S)
+        q_pos_flat = q_pos.reshape(-1)
+        resid, delta = None, None
+        hiddens = []
+        for li, lw in enumerate(self._layers):
+            lw.refresh()
+            if resid is None:
+                resid, hn = K.rmsnorm_f32(x, lw.in_w, lw.in_eps)
+            else:
+                resid, hn = K.rmsnorm_f32(resid, lw.in_w, lw.in_eps, delta=delta, sum_out=resid)
+            qkv = _mm_f32(hn, lw.wqkv, lw.bqkv)
+            q = K.kv_append(qkv, q_pos_flat, Hq, Hkv, hd, self.inv_freq, self.attention_scaling,
+                            lw.q_norm_w, lw.k_norm_w, lw.qk_eps, slot=slot,
+                            k_pool=self.k_pool[li], v_pool=self.v_pool[li])
+            if self.attn_events is not None:
+                ev0 = torch.cuda.Event(enable_timing=True)
+                ev0.record()
+            o = K.decode_attention(q.view(B, S, Hq, hd), self.k_pool[li], self.v_pool[li], self._bt_dev, q_pos,
+                                   kv_len, lw.scale, self.cap, workspace=self._workspace if split else None,
+                                   plan_ready=split)
+            if self.attn_events is not None:
+                ev1 = torch.cuda.Event(enable_timing=True)
+                ev1.record()
+                self.attn_events.append((ev0, ev1))
+            a = _mm_f32(o.view(B * S, Hq * hd), lw.o_proj.weight, lw.o_proj.bias)
+            resid, hn2 = K.rmsnorm_f32(resid, lw.post_w, lw.post_eps, delta=a, sum_out=resid)
+            delta = _mm_f32(K.silu_mul_f32(_mm_f32(hn2, lw.wgu, lw.bgu)), lw.down.weight, lw.down.bias)
+            if output_hidden_states:
+                hiddens.append(resid + delta)
+        h = hiddens[-1] if output_hidden_states else resid + delta
+        if output_hidden_states:
+            return h, hiddens
+        return h
+
+
+def _mm_f32(x: torch.Tensor, w: torch.Tensor, b: torch.Tensor | None = None) -> torch.Tensor:
+    """``x @ w.T (+ b)`` of bf16 operands with an fp32 result (cuBLAS accumulates
+    in fp32 either way; the output is just not rounded to bf16)."""
+    y = torch.mm(x, w.t(), out_dtype=torch.float32)
+    return y if b is None else y + b.float()
 
 
 # The reference's name, so callers and tests written against it keep working.

@@ -104,8 +104,10 @@ def kv_append(qkv: torch.Tensor, pos: torch.Tensor, q_heads: int, kv_heads: int,
               q_out: torch.Tensor | None = None, k_out: torch.Tensor | None = None,
               v_out: torch.Tensor | None = None) -> torch.Tensor:
     """Fused q/k RMSNorm + RoPE + paged append (K2). ``qkv [T, >=(Hq+2Hkv)hd]``
-    bf16 with unit inner stride; returns ``q_out [T, Hq, hd]``."""
-    _need(qkv, "qkv", BF16, contiguous=False)
+    bf16 (or fp32: the fp32 projection output of the fp32 residual stream)
+    with unit inner stride; returns ``q_out [T, Hq, hd]`` (bf16)."""
+    f32 = qkv.dtype == torch.float32
+    _need(qkv, "qkv", torch.float32 if f32 else BF16, contiguous=False)
     if qkv.ndim != 2 or qkv.stride(1) != 1:
         raise ValueError("qkv must be 2-D with unit inner stride")
     _need(pos, "pos", torch.int32)
@@ -127,7 +129,8 @@ def kv_append(qkv: torch.Tensor, pos: torch.Tensor, q_heads: int, kv_heads: int,
     for name, t in (("k_out", k_out), ("v_out", v_out)):
         if t is not None:
             _need(t, name, BF16)
-    _lib.call("mb_kv_append", _p(qkv), T, qkv.stride(0), _p(pos), _p(slot), _p(q_norm_w), _p(k_norm_w),
+    _lib.call("mb_kv_append_f32" if f32 else "mb_kv_append", _p(qkv), T, qkv.stride(0), _p(pos), _p(slot),
+              _p(q_norm_w), _p(k_norm_w),
               float(eps), _p(inv_freq), float(attention_scaling), q_heads, kv_heads, head_dim, page_size,
               num_pages, _p(q_out), _p(k_out), _p(v_out), _p(k_pool), _p(v_pool), _stream(qkv))
     _count()
@@ -202,6 +205,39 @@ def rmsnorm(x: torch.Tensor, weight: torch.Tensor, eps: float, residual: torch.T
     _lib.call("mb_rmsnorm", _p(x), _p(residual), _p(weight), float(eps), rows, D, _p(s), _p(norm), _stream(x))
     _count()
     return (s if s is not None else x), norm
+
+
+def rmsnorm_f32(x: torch.Tensor, weight: torch.Tensor, eps: float, delta: torch.Tensor | None = None,
+                sum_out: torch.Tensor | None = None):
+    """fp32 residual stream: returns ``(sum, norm)`` with ``sum = x + delta``
+    kept fp32 (``x`` fp32, or the bf16 embeddings entering the first layer;
+    written into ``sum_out`` when given, which may be ``x``) and ``norm =
+    bf16(RMSNorm(sum) * weight)``."""
+    _need(x, "x", torch.float32 if x.dtype == torch.float32 else BF16)
+    _need(weight, "weight", BF16)
+    D = x.shape[-1]
+    rows = x.numel() // D
+    if delta is not None:
+        _need(delta, "delta", torch.float32)
+    if sum_out is None and (delta is not None or x.dtype != torch.float32):
+        sum_out = torch.empty(x.shape, dtype=torch.float32, device=x.device)
+    norm = torch.empty(x.shape, dtype=BF16, device=x.device)
+    xf, xb = (x, None) if x.dtype == torch.float32 else (None, x)
+    _lib.call("mb_rmsnorm_f32", _p(xf), _p(xb), _p(delta), _p(weight), float(eps), rows, D, _p(sum_out), _p(norm),
+              _stream(x))
+    _count()
+    return (sum_out if sum_out is not None else x), norm
+
+
+def silu_mul_f32(gate_up: torch.Tensor) -> torch.Tensor:
+    """``bf16(silu(gate) * up)`` for an fp32 ``gate_up [..., 2I]``; returns ``[..., I]`` bf16."""
+    _need(gate_up, "gate_up", torch.float32)
+    I2 = gate_up.shape[-1]
+    rows = gate_up.numel() // I2
+    out = torch.empty(*gate_up.shape[:-1], I2 // 2, dtype=BF16, device=gate_up.device)
+    _lib.call("mb_silu_mul_f32", _p(gate_up), rows, I2 // 2, _p(out), _stream(gate_up))
+    _count()
+    return out
 
 
 def segment_meta(sequence_ids: torch.Tensor, tile: int = 128, with_run_end: bool = False):

@@ -1,18 +1,21 @@
-"""Greedy action agreement of the cached decode path.
+"""Greedy action agreement of the cached decode path with the fp32 forward.
 
-256 envs with prefixes U[16, 512] then 8 single-token decode steps on the
-decode benchmark's model shape (Qwen3-0.6B dimensions, 2 layers, random init,
-bf16-rounded weights shared by every path); each env's action at every step
-is argmax of the fp32 DiscreteActionValueHead over the last hidden state.
-Paths: ours (paged session, bf16 kernels), the stock transformers modules'
-dense causal forward over the whole sequence in fp32, and the same in bf16.
+The bar (>= 99.9% of greedy actions equal) is asserted against the fp32
+forward of the same weights: that is the reference computation the bf16
+paths approximate. 512 envs with prefixes U[16, 512] then 39 single-token
+decode steps, 20,480 decisions, on the decode benchmark's model shape
+(Qwen3-0.6B dimensions, 2 layers, random init, bf16-rounded weights shared by
+every path); each action is argmax of the fp32 DiscreteActionValueHead over
+the last hidden state. Paths:
 
-With random-init weights many decisions are near-ties that bf16 rounding
-flips whichever code computes it: the stock modules in bf16 agree with fp32
-on ~99.8% of decisions. The bar here is that our path agrees with fp32 at
-least as well as the stock bf16 path does (within 0.25 percentage points of
-sampling noise) and on >= 99.5% of decisions, and that their top-2 margins
-agree.
+* ours: the paged session's one-graph decode step, whose residual stream stays
+  fp32 between layers (only GEMM inputs, q/k/v and the page pool are bf16) and
+  whose head reads the fp32 stream;
+* the stock transformers modules' dense causal forward in fp32 (the target);
+* the same in bf16 (for context: the reference's own bf16 arithmetic, which
+  rounds the stream at every add, falls short of the bar on these weights —
+  with random init, a few tenths of a percent of decisions sit closer to a
+  tie than bf16 rounding noise).
 """
 
 from __future__ import annotations
@@ -26,6 +29,7 @@ import torch
 pytestmark = pytest.mark.gpu
 
 HIDDEN, LAYERS, HEADS, KV_HEADS, HEAD_DIM, INTER, VOCAB = 1024, 2, 16, 8, 128, 3072, 1024
+BAR = 0.999
 
 
 def _dev():
@@ -77,40 +81,45 @@ def test_greedy_action_agreement_with_fp32():
     with torch.no_grad():
         emb.weight.copy_(emb.weight.bfloat16().float())
     emb = emb.to(dev)
+    table = emb.weight.detach().bfloat16()
     head = _Head(dev)
 
-    B, steps = 256, 8
+    def embed(ids):
+        return table[ids]
+
+    B, steps = 512, 39
     rng = np.random.default_rng(0)
     plen = rng.integers(16, 513, size=B)
     toks = [list(rng.integers(0, VOCAB, size=int(n))) for n in plen]
     sess = bb16.decode_session(batch_size=B, capacity=1024)
-    S = int(plen.max())
+    assert sess.residual_fp32
+    S = int(plen.max()) - 1
     x = torch.zeros(B, S, HIDDEN, dtype=torch.bfloat16, device=dev)
     with torch.no_grad():
-        for b in range(B):
-            x[b, S - plen[b]:] = emb(torch.tensor(toks[b], device=dev)).bfloat16()
-        h = sess.forward(embeds=x, lengths=plen.tolist())[:, -1]
+        for b in range(B):  # every prefix but its last token, as one ragged prefill
+            x[b, S - plen[b] + 1:] = table[torch.tensor(toks[b][:-1], device=dev)]
+        sess.forward(embeds=x, lengths=(plen - 1).tolist())
     q_ours, q32, q16 = [], [], []
+    last = torch.tensor([t[-1] for t in toks], device=dev)
     for k in range(steps + 1):
         if k > 0:
             new = rng.integers(0, VOCAB, size=B)
             for b in range(B):
                 toks[b].append(int(new[b]))
-            with torch.no_grad():
-                step = emb(torch.from_numpy(new).to(dev)).bfloat16()[:, None]
-                h = sess.forward(embeds=step, lengths=[1] * B)[:, -1]
-        q_ours.append(head(h))
+            last = torch.from_numpy(new).to(dev)
+        q_ours.append(sess.decode_step(last, [1] * B, embed, head).clone())
         q32.append(head(_dense_last(bb32, emb, toks, torch.float32, dev)))
         q16.append(head(_dense_last(bb16, emb, toks, torch.bfloat16, dev)))
     q_ours, q32, q16 = (torch.cat(q) for q in (q_ours, q32, q16))
+    n = q32.shape[0]
     a_ours = float((q_ours.argmax(-1) == q32.argmax(-1)).float().mean())
     a_stock = float((q16.argmax(-1) == q32.argmax(-1)).float().mean())
-    print(f"greedy agreement with fp32 over {q32.shape[0]} decisions: ours {a_ours:.4f}, stock bf16 {a_stock:.4f}")
-    assert a_ours >= 0.995
-    assert a_ours >= a_stock - 0.0025
-    # where ours disagrees, fp32 itself barely separates the two actions
+    print(f"greedy agreement with fp32 over {n} decisions: ours {a_ours:.5f}, stock bf16 modules {a_stock:.5f}")
+    assert n == B * (steps + 1)
+    assert a_ours >= BAR, f"ours agrees with fp32 on {a_ours:.5f} of {n} decisions (bar {BAR})"
+    # Where ours disagrees, fp32 itself barely separates the two actions.
     top2 = q32.topk(2, dim=-1).values
     margin = top2[:, 0] - top2[:, 1]
     flips = q_ours.argmax(-1) != q32.argmax(-1)
     if flips.any():
-        assert float(margin[flips].max()) < float(margin.median())
+        assert float(margin[flips].max()) < float(margin.quantile(0.05))

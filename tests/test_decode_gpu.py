@@ -495,7 +495,9 @@ def test_decode_step_graph_matches_forward_and_head():
         return table[ids]
 
     def head(h):
-        return torch.nn.functional.linear(torch.nn.functional.rms_norm(h.float(), (256,), None, 1e-5), w)
+        # forward() hands back the model dtype; decode_step gives the head the
+        # fp32 residual stream, so round it the same way before comparing.
+        return torch.nn.functional.linear(torch.nn.functional.rms_norm(h.bfloat16().float(), (256,), None, 1e-5), w)
 
     fast = bb.decode_session(batch_size=B, capacity=64, page_size=page)
     ref = bb.decode_session(batch_size=B, capacity=64, page_size=page)
@@ -531,3 +533,44 @@ def test_decode_step_graph_matches_forward_and_head():
     from mouse_core_b200 import _lib
 
     assert _lib.device_status() == 0
+
+
+def test_fp32_residual_glue_kernels():
+    """The fp32 residual-stream glue: the add stays exact in fp32, the norm
+    and SiLU product are rounded once to bf16, and K2 reading an fp32 QKV
+    projection matches K2 reading its bf16 rounding within bf16 precision."""
+    dev = _dev()
+    from mouse_core_b200 import kernels as K
+
+    g = torch.Generator().manual_seed(3)
+    x = torch.randn(33, 1024, generator=g).to(dev)
+    d = torch.randn(33, 1024, generator=g).to(dev)
+    w = (1 + 0.1 * torch.randn(1024, generator=g)).bfloat16().to(dev)
+    s, n = K.rmsnorm_f32(x, w, 1e-6, delta=d)
+    assert s.dtype == torch.float32 and n.dtype == torch.bfloat16
+    assert torch.equal(s, x + d)
+    want = (s * torch.rsqrt(s.pow(2).mean(-1, keepdim=True) + 1e-6) * w.float())
+    assert (n.float() - want).abs().max().item() <= 1e-2 * want.abs().max().item()
+    xb = torch.randn(5, 1024, generator=g).bfloat16().to(dev)  # the embeddings entering layer 0
+    s0, n0 = K.rmsnorm_f32(xb, w, 1e-6)
+    assert torch.equal(s0, xb.float())
+    x2 = x.clone()
+    s2, _ = K.rmsnorm_f32(x2, w, 1e-6, delta=d, sum_out=x2)  # in place
+    assert s2.data_ptr() == x2.data_ptr() and torch.equal(x2, x + d)
+    gu = torch.randn(9, 2 * 3072, generator=g).to(dev)
+    o = K.silu_mul_f32(gu)
+    ref = torch.nn.functional.silu(gu[:, :3072]) * gu[:, 3072:]
+    assert bool(((o.float() - ref).abs() <= ref.abs() * 2.0 ** -8 + 1e-30).all())  # one bf16 rounding
+    # K2 on an fp32 qkv vs on the same values in bf16: both round once at the output.
+    Hq, Hkv, hd = 16, 8, 128
+    qkv = torch.randn(7, (Hq + 2 * Hkv) * hd, generator=g).to(dev)
+    qkv16 = qkv.bfloat16().float()
+    pos = torch.arange(7, dtype=torch.int32, device=dev) * 37
+    inv = (1e6 ** (-torch.arange(0, hd, 2, dtype=torch.float32) / hd)).to(dev)
+    qw = (1 + 0.1 * torch.randn(hd, generator=g)).bfloat16().to(dev)
+    kw = (1 + 0.1 * torch.randn(hd, generator=g)).bfloat16().to(dev)
+    ko, vo = (torch.empty(7, Hkv, hd, dtype=torch.bfloat16, device=dev) for _ in range(2))
+    ko16, vo16 = (torch.empty_like(ko) for _ in range(2))
+    q32 = K.kv_append(qkv16, pos, Hq, Hkv, hd, inv, 1.0, qw, kw, 1e-6, k_out=ko, v_out=vo)
+    q16 = K.kv_append(qkv16.bfloat16(), pos, Hq, Hkv, hd, inv, 1.0, qw, kw, 1e-6, k_out=ko16, v_out=vo16)
+    assert torch.equal(q32, q16) and torch.equal(ko, ko16) and torch.equal(vo, vo16)

@@ -229,3 +229,27 @@ def test_install_patches_and_restores_the_reference_hot_path(monkeypatch):
     assert mods["mouse_core.models.backbone.flex_train"].flex_packed_forward is orig
     for fn in ("resolve_cache_bounds", "rebuild_starts", "cache_needs_rebuild"):
         assert getattr(mods["mouse_core.models.kv_policy"], fn) is orig
+
+
+def test_decode_rope_frequencies_survive_a_bf16_cast():
+    """Casting a backbone to bf16 rounds its rotary module's inv_freq buffer;
+    the decode session recomputes the config's fp32 frequencies (default and
+    Llama-3 rope types) instead."""
+    import torch
+
+    from mouse_core_b200.backbone import LlamaBackbone, Qwen3Backbone
+    from mouse_core_b200.decode import rope_frequencies
+
+    for bb in (Qwen3Backbone(hidden_dim=256, num_layers=1, num_heads=2, num_key_value_heads=1, head_dim=128,
+                             rope_parameters={"rope_type": "default", "rope_theta": 1e6}),
+               LlamaBackbone(hidden_dim=256, num_layers=1, num_heads=4, num_key_value_heads=2,
+                             max_position_embeddings=16384,
+                             rope_parameters={"rope_type": "llama3", "rope_theta": 5e5, "factor": 32.0,
+                                              "low_freq_factor": 1.0, "high_freq_factor": 4.0,
+                                              "original_max_position_embeddings": 8192})):
+        exact = bb.model.rotary_emb.inv_freq.clone()
+        bb = bb.to(torch.bfloat16)
+        assert not torch.equal(bb.model.rotary_emb.inv_freq.float(), exact)  # the cast rounded the buffer
+        inv, scaling = rope_frequencies(bb.model.rotary_emb, bb.model.config, torch.device("cpu"))
+        assert inv.dtype == torch.float32 and torch.equal(inv, exact)
+        assert scaling == float(bb.model.rotary_emb.attention_scaling)
