@@ -266,7 +266,8 @@ def run_ours(args):
     # cleared after that step and its next token starts a fresh one (the row
     # is emptied, and the device step restarts it at position 0).
     actions = rng.integers(0, 4, size=ENVS)
-    ids_host = np.stack([transition_ids(rng, actions, ENVS) for _ in range(total + K_steps)])
+    n_calls = total + 2 * K_steps  # warm-up + timed, host-cost pass, roofline pass
+    ids_host = np.stack([transition_ids(rng, actions, ENVS) for _ in range(n_calls)])
     ids_dev = torch.from_numpy(ids_host).to(dev)
     task_end = (ids_host & 1).astype(bool)
     ones = [1] * ENVS
@@ -295,22 +296,30 @@ def run_ours(args):
     launches0 = K.launch_count[0]
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
-    t_host = time.perf_counter()
     e0.record()
     for i in range(W, total):
         device_step(i)
     e1.record()
-    host_us = (time.perf_counter() - t_host) * 1e6 / K_steps  # host time to issue one step
     torch.cuda.synchronize()
     clk = clocks.stop()
     launches = K.launch_count[0] - launches0
     ms = e0.elapsed_time(e1)
     resets_timed = int(task_end[W - 1:total - 1].sum())
+    # Host cost of a step: the same steps issued one at a time onto an idle
+    # GPU (synchronised before each), so no wait for the device is counted.
+    host_t = []
+    for i in range(total, total + K_steps):
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        device_step(i)
+        host_t.append(time.perf_counter() - t0)
+    torch.cuda.synchronize()
+    host_us = statistics.median(host_t) * 1e6
     # Roofline pass: K more steps run eagerly with CUDA events around every
     # attention launch (on the launching stream); same kernel, same data.
     sess.attn_events = []
     kv_sum = 0
-    for i in range(total, total + K_steps):
+    for i in range(total + K_steps, n_calls):
         gone = task_end[i - 1]
         kv_sum += int(sess._len[~gone].sum()) + ENVS  # kv_len after this step's append
         device_step(i)
@@ -327,20 +336,20 @@ def run_ours(args):
     # memory and the actions come back to the host.
     from mouse_core_b200.grow_rebuild import GrowRebuildDecoder
 
-    cap = int(lengths.max()) + 2 * (total + K_steps) + 8
+    cap = int(lengths.max()) + n_calls + total + 8
     history = np.zeros((ENVS, cap), dtype=np.int32)
     ends = lengths.copy()
     for b in range(ENVS):
         history[b, :lengths[b]] = ctx_ids[b]
     rows = np.arange(ENVS)
-    for i in range(total + K_steps):  # the host contexts of what the session now holds
+    for i in range(n_calls):  # the host contexts of what the session now holds
         if i > 0:
             ends[task_end[i - 1]] = 0
         history[rows, ends] = ids_host[i]
         ends += 1
     dec = GrowRebuildDecoder(model, ENVS, embed_fn, max_cache=max_cache, start_cache=start_cache, per_row=True)
     dec.adopt(sess, np.zeros(ENVS, dtype=np.int64), ends)
-    pending = task_end[total + K_steps - 1].copy()
+    pending = task_end[n_calls - 1].copy()
     ends[pending] = 0
     h_act = torch.empty(ENVS, dtype=torch.int64, pin_memory=True)
     act = rng.integers(0, 4, size=ENVS)
@@ -440,11 +449,13 @@ def run_ours(args):
                           "rule": "a token with its done bit set (p = 0.02) ends the env's task: the context is "
                                   "cleared and the next token starts a fresh one (the row restarts at position 0); "
                                   "the e2e loop also checks max_cache every step (rows_needing_rebuild)"},
-            "per_rank": {"fields": ["device_ms_per_step", "host_us_to_issue_step", "e2e_ms_per_step"],
+            "per_rank": {"fields": ["device_ms_per_step", "host_us_per_step_on_idle_gpu", "e2e_ms_per_step"],
                          "ranks": per_rank_rows},
         }
     if rank == 0 and train is not None:
         out["train"] = train
+    if rank == 0 and not args.no_packed:
+        out["prefill_attention"] = prefill_attention_metric(dev)
     if rank == 0 and not args.no_packed:
         out["packed_attention"] = packed_attention_metric(dev)
     if rank == 0 and not args.no_cpu_baseline:
@@ -953,6 +964,75 @@ def packed_attention_metric(device, reps=10, rows=8):
                          "frac_of_sustained": round(tf_all / float(peak_sus), 4) if peak_sus else None}}
 
 
+def prefill_attention_metric(device, reps=5):
+    """TFLOP/s of the tcgen05 paged prefill attention (one layer's K/V pool):
+    the GRPO branch prefill shape (256 rows each prefilling 256 tokens over a
+    cached context U[1024, 8192]) and the grow-then-rebuild prefill (256 rows
+    each re-prefilling a 1024-token window from an empty cache). Qwen3-0.6B
+    heads (16 q / 8 kv, hd 128), 128-token pages scattered through the pool.
+    Algorithmic FLOPs = 4 * Hq * hd * sum over real queries of the keys each
+    one sees."""
+    import torch
+
+    from mouse_core_b200 import kernels as K
+
+    peaks = {}
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            peaks = json.load(f)
+    except (OSError, ValueError):
+        pass
+    peak = float(peaks.get("bf16_tflops", 1590.0))
+    rng = np.random.default_rng(11)
+    Hq, Hkv, hd, page = HEADS, KV_HEADS, HEAD_DIM, PAGE
+    res = {}
+    for name, B, S, ctx in (("branch_prefill", 256, 256, rng.integers(1024, 8193, size=256)),
+                            ("rebuild_prefill", 256, 1024, np.zeros(256, dtype=np.int64))):
+        lens = (ctx + S).astype(np.int64)
+        npg = (lens + page - 1) // page
+        P = int(npg.sum())
+        perm = rng.permutation(P).astype(np.int32)
+        bt = np.full((B, int(npg.max())), -1, dtype=np.int32)
+        o = 0
+        for b in range(B):
+            bt[b, :npg[b]] = perm[o:o + npg[b]]
+            o += npg[b]
+        g = torch.Generator(device=device).manual_seed(3)
+        kp = torch.randn(P, Hkv, page, hd, generator=g, device=device).bfloat16()
+        vp = torch.randn(P, Hkv, page, hd, generator=g, device=device).bfloat16()
+        q = torch.randn(B, S, Hq, hd, generator=g, device=device).bfloat16()
+        q_pos = torch.from_numpy((ctx[:, None] + np.arange(S)[None, :]).astype(np.int32)).to(device)
+        kv_len = torch.from_numpy(lens.astype(np.int32)).to(device)
+        btd = torch.from_numpy(bt).to(device)
+        out = torch.empty_like(q)
+        flops = 4 * Hq * hd * int(sum(S * int(c) + S * (S + 1) // 2 for c in ctx))
+
+        ws = torch.empty(256, dtype=torch.uint8, device=device)  # the persistent CTAs' tile counter
+
+        def run():
+            K.decode_attention(q, kp, vp, btd, q_pos, kv_len, hd ** -0.5, int(lens.max()), out=out, workspace=ws)
+
+        for _ in range(2):
+            run()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            run()
+        e1.record()
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / reps
+        tf = flops / (ms * 1e-3) / 1e12
+        res[name] = {"rows": B, "queries_per_row": S, "context": "U[1024,8192]" if ctx.any() else "empty",
+                     "ms": round(ms, 4), "tflops": round(tf, 1), "frac": round(tf / peak, 4),
+                     "algorithmic_flops": flops}
+        del kp, vp, q, out
+        torch.cuda.empty_cache()
+    return {"kernel": "varlen_fwd_kernel<PAGED> (tcgen05 paged prefill, one layer)", "bound": "tensor",
+            "peak": peak, "peak_source": "measured" if "bf16_tflops" in peaks else "fallback", "unit": "TFLOP/s",
+            **res}
+
+
 # ------------------------------------------------------- packed training
 TRAIN_LAYERS, TRAIN_ROWS, TRAIN_ROW_LEN = 28, 8, 16384
 
@@ -1271,6 +1351,7 @@ def main():
     ap.add_argument("--no-packed", action="store_true", help="skip the packed-attention secondary metric")
     ap.add_argument("--packed-only", action="store_true", help="only time the packed-attention kernels")
     ap.add_argument("--packed-rows", type=int, default=8, help="16384-token rows in the packed stream")
+    ap.add_argument("--prefill-only", action="store_true", help="only time the paged prefill attention")
     ap.add_argument("--envs", type=int, default=ENVS, help="envs per GPU (256 is the benchmark workload; "
                     "smaller values only for profiling captures)")
     ap.add_argument("--train", action="store_true", help="time the packed DQN training step instead of decode")
@@ -1294,6 +1375,11 @@ def main():
         out = run_grpo(args)
     elif args.train and args.impl == "ours":
         out = run_train(args)
+    elif args.prefill_only:
+        import torch
+
+        out = prefill_attention_metric(torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0"))),
+                                       reps=args.steps)
     elif args.packed_only:
         import torch
 

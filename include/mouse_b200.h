@@ -86,7 +86,12 @@ int mb_decode_plan(const int32_t* kv_len, int batch, int kv_heads, int q_rows, i
 /* out = softmax(scale * q k^T, masked to slots <= q_pos) v, per row and
  * q-head (q-head h reads kv-head h / (q_heads / kv_heads)). head_dim 64 or
  * 128; page_size a multiple of 64. plan_ready = 1 reuses the plan already
- * in `workspace` (built by mb_decode_plan for the same kv_len); 0 builds it. */
+ * in `workspace` (built by mb_decode_plan for the same kv_len); 0 builds it.
+ * Three schedules: split mode (q_rows <= 16: one-token decode; workspace
+ * required); the tcgen05 prefill (q_len >= 64 with q and out 16-byte
+ * aligned: 128-query tiles over TMEM accumulators, K/V pages gathered by TMA;
+ * a workspace, if given, holds the persistent CTAs' tile counter in its first
+ * 4 bytes, otherwise one CTA runs per tile); warp-MMA block mode otherwise. */
 int mb_decode_attention(const void* q, const void* k_pool, const void* v_pool, int num_pages,
                         const int32_t* block_table, int max_pages, const int32_t* q_pos, const int32_t* kv_len,
                         int batch, int q_len, int q_heads, int kv_heads, int head_dim, int page_size, float scale,

@@ -175,6 +175,39 @@ int mb_decode_attention(const void* q, const void* k_pool, const void* v_pool, i
   p.num_pages = num_pages;
   p.scale_log2 = scale * 1.4426950408889634f;
 
+  // Prefill chunks of at least kPrefillMinRows queries per row run on the
+  // tcgen05 kernel (128-query tiles, TMEM accumulators, page-gathering TMA);
+  // shorter multi-row chunks keep the warp-MMA block mode.
+  constexpr int kPrefillMinRows = 64;
+  if (!split && q_len >= kPrefillMinRows && aligned(q, 16) && aligned(out, 16) &&
+      (long long)batch * q_len < (1ll << 31)) {
+    CUtensorMap qm;
+    if ((rc = encode_token_map(&qm, q, batch * q_len, q_heads, head_dim))) return rc;
+    mb::VarlenParams vp{};
+    vp.L = batch * q_len;
+    vp.Hq = q_heads;
+    vp.Hkv = kv_heads;
+    vp.G = G;
+    vp.heads_per_cta = (G % 2 == 0) ? 2 : 1;
+    vp.head_dim = head_dim;
+    vp.scale_log2 = p.scale_log2;
+    vp.out = static_cast<__nv_bfloat16*>(out);
+    vp.block_table = block_table;
+    vp.q_pos = q_pos;
+    vp.kv_len = kv_len;
+    vp.B = batch;
+    vp.S = q_len;
+    vp.max_pages = max_pages;
+    vp.page_size = page_size;
+    vp.num_pages = num_pages;
+    // With any workspace the kernel runs persistent CTAs over a tile counter
+    // kept in its first 4 bytes.
+    if (workspace && workspace_bytes >= sizeof(int) && aligned(workspace, 4))
+      vp.tile_counter = static_cast<int*>(workspace);
+    cudaError_t e = mb::launch_paged_prefill(qm, km, vm, vp, (cudaStream_t)stream);
+    return e == cudaSuccess ? MB_OK : cuda_fail(e, "paged prefill launch");
+  }
+
   mb::WorkspaceLayout lay{};
   uint8_t* ws = static_cast<uint8_t*>(workspace);
   if (split) {

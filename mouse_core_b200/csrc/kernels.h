@@ -89,9 +89,21 @@ struct VarlenParams {
   __nv_bfloat16* out;        // [L, Hq, HD]
   float* lse;                // [Hq, L], log2 units
   int* tile_counter;         // [1] scratch: the persistent kernel's tile counter
+  // Paged prefill (the same kernel over a decode session's page pool):
+  // queries [B * S, Hq, HD] (row b * S + s), query (b, s) sees the cached
+  // keys 0 .. q_pos[b, s] of row b through block_table; out [B * S, Hq, HD];
+  // no lse. One CTA per work tile (tile_counter unused).
+  const int32_t* block_table;  // [B, max_pages]
+  const int32_t* q_pos;        // [B, S]
+  const int32_t* kv_len;       // [B]
+  int B, S, max_pages, page_size, num_pages;
 };
 cudaError_t launch_varlen_fwd(const CUtensorMap& qm, const CUtensorMap& km, const CUtensorMap& vm,
                               const VarlenParams& p, cudaStream_t stream);
+// qm: 3-D token map over the B * S query rows; km / vm: 2-D 64 x 64-box maps
+// of one layer's K / V pool (the decode kernel's maps).
+cudaError_t launch_paged_prefill(const CUtensorMap& qm, const CUtensorMap& km, const CUtensorMap& vm,
+                                 const VarlenParams& p, cudaStream_t stream);
 
 struct VarlenBwdParams {
   int L, Hq, Hkv, G, head_dim;

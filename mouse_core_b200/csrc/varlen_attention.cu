@@ -58,24 +58,73 @@ struct FwdBarriers {
   int tile[2];
 };
 
+// One work tile: 128 query rows starting at flat row q0 (rows up to row_end
+// belong to it), q-heads h0 .. h0 + heads_per_cta - 1 over kv-head kvh, and
+// its key tiles t_lo .. t_lo + n - 1. Paged prefill: row b of the batch,
+// key tiles of that row's cache.
 struct FwdWork {
-  int q0, h0, kvh, qt, t_lo, n;
+  int q0, row_end, h0, kvh, qt, t_lo, n, b;
 };
 
+template <bool PAGED>
 __device__ __forceinline__ FwdWork fwd_work(int tile, const VarlenParams& p) {
-  const int n_qt = (p.L + 127) / 128;
   const int groups = p.Hq / p.heads_per_cta;
   FwdWork w;
-  w.qt = n_qt - 1 - tile / groups;  // longest-history tiles of a stream first
   w.h0 = (tile % groups) * p.heads_per_cta;
   w.kvh = w.h0 / p.G;
-  w.q0 = w.qt * 128;
-  w.t_lo = p.tile_lo[w.qt] / 128;
-  w.n = min(w.q0 + 127, p.L - 1) / 128 - w.t_lo + 1;
+  if constexpr (PAGED) {
+    // Tiles of later query rows (more keys) first, all rows alike.
+    const int n_qt = (p.S + 127) / 128;
+    const int rest = tile / groups;
+    w.qt = n_qt - 1 - rest / p.B;
+    w.b = rest % p.B;
+    w.q0 = w.b * p.S + w.qt * 128;
+    w.row_end = w.b * p.S + p.S;
+    // q_pos grows along a row (left pads sit at 0), so the tile's last row
+    // bounds the keys it needs; a tile with no key still runs one masked one.
+    const int last = min(w.qt * 128 + 127, p.S - 1);
+    const int hi = min(p.q_pos[(size_t)w.b * p.S + last] + 1, p.kv_len[w.b]);
+    w.t_lo = 0;
+    w.n = max(1, (hi + 127) / 128);
+  } else {
+    const int n_qt = (p.L + 127) / 128;
+    w.qt = n_qt - 1 - tile / groups;  // longest-history tiles of a stream first
+    w.b = 0;
+    w.q0 = w.qt * 128;
+    w.row_end = p.L;
+    w.t_lo = p.tile_lo[w.qt] / 128;
+    w.n = min(w.q0 + 127, p.L - 1) / 128 - w.t_lo + 1;
+  }
   return w;
 }
 
+// K or V key tile [kv0, kv0 + 128) of row b, kv-head kvh from the page pool:
+// two 64-row boxes per 64-column block (a 64- or 128-token page holds whole
+// boxes), written where the contiguous kernel's 128-row box would put them.
+// Boxes past the row's keys or the block table read zeros (y = -64).
 template <int HD>
+__device__ __forceinline__ void load_paged_kv(uint8_t* dst, const CUtensorMap* map, uint64_t* bar,
+                                              const VarlenParams& p, int b, int kvh, int kv0) {
+  using C = FwdTile<HD>;
+  const int len = p.kv_len[b];
+#pragma unroll
+  for (int g = 0; g < 2; ++g) {
+    const int tok = kv0 + 64 * g;
+    int y = -64;
+    if (tok < len) {
+      const int pidx = tok / p.page_size;
+      const int pg = pidx < p.max_pages ? p.block_table[(size_t)b * p.max_pages + pidx] : -1;
+      if (pg >= 0 && pg < p.num_pages)
+        y = (pg * p.Hkv + kvh) * p.page_size + tok % p.page_size;
+      else
+        report(kDevBadPage);
+    }
+#pragma unroll
+    for (int cb = 0; cb < C::NCB; ++cb) tma_load_2d(dst + cb * C::BOX + g * (C::BOX / 2), map, bar, cb * 64, y);
+  }
+}
+
+template <int HD, bool PAGED>
 __global__ void __launch_bounds__(320, 1) varlen_fwd_kernel(const __grid_constant__ CUtensorMap qmap,
                                                            const __grid_constant__ CUtensorMap kmap,
                                                            const __grid_constant__ CUtensorMap vmap,
@@ -90,7 +139,8 @@ __global__ void __launch_bounds__(320, 1) varlen_fwd_kernel(const __grid_constan
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int hpc = p.heads_per_cta;
-  const int n_work = ((p.L + C::BM - 1) / C::BM) * (p.Hq / hpc);
+  const int n_work = PAGED ? p.B * ((p.S + C::BM - 1) / C::BM) * (p.Hq / hpc)
+                           : ((p.L + C::BM - 1) / C::BM) * (p.Hq / hpc);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < 2; ++s) {
@@ -139,7 +189,10 @@ __global__ void __launch_bounds__(320, 1) varlen_fwd_kernel(const __grid_constan
     for (int k = 0; ok; ++k) {
       int tile = -1;
       if (lane == 0) {
-        tile = k == 0 ? (int)blockIdx.x : (int)gridDim.x + atomicAdd(p.tile_counter, 1);
+        if (PAGED && p.tile_counter == nullptr)  // one tile per CTA
+          tile = k == 0 ? (int)blockIdx.x : -1;
+        else
+          tile = k == 0 ? (int)blockIdx.x : (int)gridDim.x + atomicAdd(p.tile_counter, 1);
         if (tile >= n_work) tile = -1;
         ok = mbar_wait(&bars->tile_empty[k & 1], ((k >> 1) & 1) ^ 1, kDevTimeoutEmpty);
         if (ok) {
@@ -150,7 +203,7 @@ __global__ void __launch_bounds__(320, 1) varlen_fwd_kernel(const __grid_constan
       tile = __shfl_sync(0xffffffffu, tile, 0);
       ok = __shfl_sync(0xffffffffu, ok, 0);
       if (!ok || tile < 0) break;
-      const FwdWork w = fwd_work(tile, p);
+      const FwdWork w = fwd_work<PAGED>(tile, p);
       if (lane == 0) {
         // The Q slots are free once the previous tile's last Q K^T completed.
         if (k > 0) ok = mbar_wait(&bars->q_empty, (k - 1) & 1, kDevTimeoutEmpty);
@@ -166,11 +219,19 @@ __global__ void __launch_bounds__(320, 1) varlen_fwd_kernel(const __grid_constan
           if (!(ok = mbar_wait(&bars->kv_empty[st], ((jj / C::STAGES) & 1) ^ 1, kDevTimeoutEmpty))) break;
           const int kv0 = (w.t_lo + j) * C::BN;
           mbar_arrive_expect_tx(&bars->k_full[st], C::KVTILE);
-          for (int cb = 0; cb < C::NCB; ++cb)
-            tma_load_3d(ks + st * C::KVTILE + cb * C::BOX, &kmap, &bars->k_full[st], cb * 64, w.kvh, kv0);
+          if constexpr (PAGED) {
+            load_paged_kv<HD>(ks + st * C::KVTILE, &kmap, &bars->k_full[st], p, w.b, w.kvh, kv0);
+          } else {
+            for (int cb = 0; cb < C::NCB; ++cb)
+              tma_load_3d(ks + st * C::KVTILE + cb * C::BOX, &kmap, &bars->k_full[st], cb * 64, w.kvh, kv0);
+          }
           mbar_arrive_expect_tx(&bars->v_full[st], C::KVTILE);
-          for (int cb = 0; cb < C::NCB; ++cb)
-            tma_load_3d(vs + st * C::KVTILE + cb * C::BOX, &vmap, &bars->v_full[st], cb * 64, w.kvh, kv0);
+          if constexpr (PAGED) {
+            load_paged_kv<HD>(vs + st * C::KVTILE, &vmap, &bars->v_full[st], p, w.b, w.kvh, kv0);
+          } else {
+            for (int cb = 0; cb < C::NCB; ++cb)
+              tma_load_3d(vs + st * C::KVTILE + cb * C::BOX, &vmap, &bars->v_full[st], cb * 64, w.kvh, kv0);
+          }
         }
       }
       ok = __shfl_sync(0xffffffffu, ok, 0);
@@ -196,7 +257,7 @@ __global__ void __launch_bounds__(320, 1) varlen_fwd_kernel(const __grid_constan
     for (int k = 0; ok; ++k) {
       const int tile = take_tile(k, ok);
       if (!ok || tile < 0) break;
-      const int n = fwd_work(tile, p).n;
+      const int n = fwd_work<PAGED>(tile, p).n;
       if (!(ok = mbar_wait_warp(&bars->q_full, k & 1, kDevTimeoutFull))) break;
       if (!(ok = mbar_wait_warp(&bars->k_full[J % C::STAGES], (J / C::STAGES) & 1, kDevTimeoutFull))) break;
       for (int hh = 0; hh < hpc; ++hh) issue_qk(hh, J % C::STAGES);
@@ -246,11 +307,17 @@ __global__ void __launch_bounds__(320, 1) varlen_fwd_kernel(const __grid_constan
     for (int k = 0; ok; ++k) {
       const int tile = take_tile(k, ok);
       if (!ok || tile < 0) break;
-      const FwdWork w = fwd_work(tile, p);
-      const int q_tok = w.q0 + r;
-      const bool row_ok = q_tok < p.L;
-      const int lo = row_ok ? p.run_start[q_tok] : 0x7fffffff;
-      const int hi = q_tok;
+      const FwdWork w = fwd_work<PAGED>(tile, p);
+      const int q_tok = w.q0 + r;  // flat query row
+      const bool row_ok = q_tok < w.row_end;
+      int lo, hi;
+      if constexpr (PAGED) {  // cached keys 0 .. q_pos of the row (none past its length)
+        lo = 0;
+        hi = row_ok ? min(p.q_pos[q_tok], p.kv_len[w.b] - 1) : -1;
+      } else {  // same segment, causal
+        lo = row_ok ? p.run_start[q_tok] : 0x7fffffff;
+        hi = q_tok;
+      }
       float m_used = -INFINITY, l = 0.f;
       for (int j = 0; active && j < w.n; ++j) {
         const int jj = J + j;
@@ -357,7 +424,7 @@ __global__ void __launch_bounds__(320, 1) varlen_fwd_kernel(const __grid_constan
             }
           }
         }
-        if (row_ok) p.lse[(size_t)h * p.L + q_tok] = (l > 0.f) ? m_used + log2f(l) : -INFINITY;
+        if (row_ok && !PAGED) p.lse[(size_t)h * p.L + q_tok] = (l > 0.f) ? m_used + log2f(l) : -INFINITY;
       } else {
         tc_fence_before();
         __syncwarp();
@@ -385,14 +452,44 @@ cudaError_t launch_varlen_fwd(const CUtensorMap& qm, const CUtensorMap& km, cons
   if (e != cudaSuccess) return e;
   if (p.head_dim == 128) {
     const int smem = FwdTile<128>::SMEM;
-    e = cudaFuncSetAttribute(varlen_fwd_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    e = cudaFuncSetAttribute(varlen_fwd_kernel<128, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
-    varlen_fwd_kernel<128><<<grid, 320, smem, stream>>>(qm, km, vm, p);
+    varlen_fwd_kernel<128, false><<<grid, 320, smem, stream>>>(qm, km, vm, p);
   } else {
     const int smem = FwdTile<64>::SMEM;
-    e = cudaFuncSetAttribute(varlen_fwd_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    e = cudaFuncSetAttribute(varlen_fwd_kernel<64, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
-    varlen_fwd_kernel<64><<<grid, 320, smem, stream>>>(qm, km, vm, p);
+    varlen_fwd_kernel<64, false><<<grid, 320, smem, stream>>>(qm, km, vm, p);
+  }
+  return cudaGetLastError();
+}
+
+// Paged prefill: persistent CTAs (one per SM) taking (row, 128-query tile,
+// q-head pair) tiles from p.tile_counter when the caller gave scratch for it,
+// else one CTA per tile.
+cudaError_t launch_paged_prefill(const CUtensorMap& qm, const CUtensorMap& km, const CUtensorMap& vm,
+                                 const VarlenParams& p, cudaStream_t stream) {
+  long long n_work = (long long)p.B * ((p.S + 127) / 128) * (p.Hq / p.heads_per_cta);
+  if (n_work <= 0) return cudaSuccess;
+  if (n_work >= (1ll << 31)) return cudaErrorInvalidValue;
+  cudaError_t e;
+  if (p.tile_counter) {
+    int dev = 0, sms = 148;
+    if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    n_work = std::min<long long>(n_work, sms);
+    e = cudaMemsetAsync(p.tile_counter, 0, sizeof(int), stream);
+    if (e != cudaSuccess) return e;
+  }
+  if (p.head_dim == 128) {
+    const int smem = FwdTile<128>::SMEM;
+    e = cudaFuncSetAttribute(varlen_fwd_kernel<128, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return e;
+    varlen_fwd_kernel<128, true><<<(unsigned)n_work, 320, smem, stream>>>(qm, km, vm, p);
+  } else {
+    const int smem = FwdTile<64>::SMEM;
+    e = cudaFuncSetAttribute(varlen_fwd_kernel<64, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return e;
+    varlen_fwd_kernel<64, true><<<(unsigned)n_work, 320, smem, stream>>>(qm, km, vm, p);
   }
   return cudaGetLastError();
 }

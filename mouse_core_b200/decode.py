@@ -614,17 +614,8 @@ class PagedDecodeSession:
         if self.residual_fp32:
             return self._body_f32(x, q_pos, kv_len, slot, S, output_hidden_states)
         B = self.B
-        D = x.shape[-1]
         Hq, Hkv, hd = self.n_heads, self.n_kv_heads, self.head_dim
-        R = (Hq // Hkv) * S
-        split = R <= 16
-        if split:
-            need = K.decode_workspace_bytes(B, Hkv, R, hd, self.cap)
-            if self._workspace.numel() < need:
-                self._workspace = torch.empty(need, dtype=torch.uint8, device=self.device)
-                self._graph = None
-                self._step_graph = None
-            K.decode_plan(kv_len, Hkv, R, hd, self.cap, self._workspace)
+        split = self._plan(kv_len, S)
         q_pos_flat = q_pos.reshape(-1)
 
         resid, delta = x, None
@@ -643,8 +634,7 @@ class PagedDecodeSession:
                 ev0 = torch.cuda.Event(enable_timing=True)
                 ev0.record()
             o = K.decode_attention(q.view(B, S, Hq, hd), self.k_pool[li], self.v_pool[li], self._bt_dev, q_pos,
-                                   kv_len, lw.scale, self.cap, workspace=self._workspace if split else None,
-                                   plan_ready=split)
+                                   kv_len, lw.scale, self.cap, workspace=self._workspace, plan_ready=split)
             if self.attn_events is not None:
                 ev1 = torch.cuda.Event(enable_timing=True)
                 ev1.record()
@@ -671,6 +661,10 @@ class PagedDecodeSession:
                 self._graph = None
                 self._step_graph = None
             K.decode_plan(kv_len, Hkv, R, hd, self.cap, self._workspace)
+        elif self._workspace.numel() < 256:  # prefill chunks keep a tile counter in it
+            self._workspace = torch.empty(256, dtype=torch.uint8, device=self.device)
+            self._graph = None
+            self._step_graph = None
         return split
 
     def _body_f32(self, x, q_pos, kv_len, slot, S, output_hidden_states):
@@ -703,8 +697,7 @@ class PagedDecodeSession:
                 ev0 = torch.cuda.Event(enable_timing=True)
                 ev0.record()
             o = K.decode_attention(q.view(B, S, Hq, hd), self.k_pool[li], self.v_pool[li], self._bt_dev, q_pos,
-                                   kv_len, lw.scale, self.cap, workspace=self._workspace if split else None,
-                                   plan_ready=split)
+                                   kv_len, lw.scale, self.cap, workspace=self._workspace, plan_ready=split)
             if self.attn_events is not None:
                 ev1 = torch.cuda.Event(enable_timing=True)
                 ev1.record()

@@ -84,16 +84,18 @@ def decode_attention(q: torch.Tensor, k_pool: torch.Tensor, v_pool: torch.Tensor
         _need(out, "out", BF16)
     G = Hq // Hkv
     ws_ptr, ws_n = None, 0
-    if G * S <= 16:
+    split = G * S <= 16
+    if split:
         need = decode_workspace_bytes(B, Hkv, G * S, hd, max_kv_len)
         if workspace is None or workspace.numel() < need:
             workspace = torch.empty(need, dtype=torch.uint8, device=q.device)
+    if workspace is not None:  # prefill chunks use 4 bytes of it as a tile counter
         _need(workspace, "workspace", torch.uint8)
         ws_ptr, ws_n = _p(workspace), workspace.numel()
     _lib.call("mb_decode_attention", _p(q), _p(k_pool), _p(v_pool), P, _p(block_table), block_table.shape[1],
               _p(q_pos), _p(kv_len), B, S, Hq, Hkv, hd, page, float(scale), int(max_kv_len), int(plan_ready),
               _p(out), ws_ptr, ws_n, _stream(q))
-    _count(2 if (ws_ptr is not None and not plan_ready) else 1)
+    _count(2 if (split and not plan_ready) else 1)
     return out
 
 

@@ -73,7 +73,11 @@ CASES = [
     (4, 32, 8, 64, 128, 5, 3),      # R = 20: block mode
     (3, 16, 8, 128, 128, 40, 4),    # ragged prefill chunk, 2 query blocks
     (3, 4, 4, 128, 64, 3, 5),       # no GQA sharing
-    (2, 8, 2, 64, 64, 70, 6),       # G=4 prefill, 280 rows
+    (2, 8, 2, 64, 64, 70, 6),       # G=4 prefill, 280 rows: tcgen05 prefill (S >= 64), partial tile
+    (3, 16, 8, 128, 128, 256, 7),   # tcgen05 prefill: two query tiles per row over a cached history
+    (2, 16, 8, 128, 64, 1024, 8),   # a 1024-token window (the rebuild prefill), 64-token pages
+    (3, 4, 4, 128, 128, 130, 9),    # no GQA pairing (one q-head per CTA), a 2-row second tile
+    (4, 32, 8, 64, 64, 96, 10),     # hd 64, G = 4
 ]
 
 
@@ -103,6 +107,13 @@ def test_decode_attention_matches_oracle(B, Hq, Hkv, hd, page, S, seed):
     assert np.isfinite(got).all()
     err = np.abs(got - ref).max()
     assert err < ATOL, f"max abs err {err}"
+    if S >= 64:  # the tcgen05 prefill again, persistent over a tile counter in a workspace
+        ws = torch.full((256,), 7, dtype=torch.uint8, device=dev)
+        out2 = K.decode_attention(q.to(dev), kp.to(dev), vp.to(dev), torch.from_numpy(bt).to(dev),
+                                  torch.from_numpy(q_pos).to(dev),
+                                  torch.tensor(lens_after, dtype=torch.int32, device=dev), scale, max(lens_after),
+                                  workspace=ws)
+        assert np.abs(out2.float().cpu().numpy() - ref).max() < ATOL
     from mouse_core_b200 import _lib
 
     assert _lib.device_status() == 0
