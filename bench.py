@@ -416,6 +416,15 @@ def run_ours(args):
         train = train_measure(dev, world, rank, local, TRAIN_ROWS, max(1, min(K_steps, args.train_steps)),
                               W)
         torch.cuda.empty_cache()
+    # The large-batch decode and the GRPO branch rollout on the same ranks
+    # (each rank owns its slice of envs / roots; no collective).
+    large_batch = grpo = None
+    if not args.no_extra:
+        large_batch = large_batch_measure(dev, world, rank, local, LB["envs"], max(1, min(K_steps, args.extra_steps)),
+                                          W)
+        torch.cuda.empty_cache()
+        grpo = grpo_measure(dev, world, rank, local, GR["roots"], max(1, min(K_steps, args.extra_steps)), W)
+        torch.cuda.empty_cache()
 
     out = None
     if rank == 0:
@@ -454,6 +463,10 @@ def run_ours(args):
         }
     if rank == 0 and train is not None:
         out["train"] = train
+    if rank == 0 and large_batch is not None:
+        out["large_batch"] = large_batch
+    if rank == 0 and grpo is not None:
+        out["grpo"] = grpo
     if rank == 0 and not args.no_packed:
         out["prefill_attention"] = prefill_attention_metric(dev)
     if rank == 0 and not args.no_packed:
@@ -485,14 +498,9 @@ def large_batch_config(n_gpus, envs):
             "l2": "inputs larger than L2: each step reads ~54 GB of KV per GPU"}
 
 
-def run_large_batch(args):
+def _setup_ranks():
     import torch
     import torch.distributed as dist
-    import torch.nn.functional as F
-
-    from mouse_core_b200 import _lib
-    from mouse_core_b200 import kernels as K
-    from mouse_core_b200.backbone import LlamaBackbone
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -503,7 +511,35 @@ def run_large_batch(args):
         from datetime import timedelta
 
         dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
-    envs = args.lb_envs
+    return dev, world, rank, local
+
+
+def _teardown_ranks(world):
+    import torch.distributed as dist
+
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def run_large_batch(args):
+    dev, world, rank, local = _setup_ranks()
+    out = large_batch_measure(dev, world, rank, local, args.lb_envs, args.steps, args.warmup)
+    _teardown_ranks(world)
+    return out
+
+
+def large_batch_measure(dev, world, rank, local, envs, K_steps, W):
+    """Time the large-batch decode on this process group (every rank calls
+    it; rank 0 gets the result line)."""
+    import torch
+    import torch.distributed as dist
+    import torch.nn.functional as F
+
+    from mouse_core_b200 import _lib
+    from mouse_core_b200 import kernels as K
+    from mouse_core_b200.backbone import LlamaBackbone
+
     D, hd, Hkv, Hq, P = LB["hidden"], LB["head_dim"], LB["kv_heads"], LB["heads"], LB["page"]
     torch.manual_seed(0)
     bb = LlamaBackbone(hidden_dim=D, num_layers=LB["layers"], num_heads=Hq, num_key_value_heads=Hkv,
@@ -522,7 +558,6 @@ def run_large_batch(args):
     rng = np.random.default_rng(3000 + rank)
     lo, hi = LB["len"]
     lengths = np.exp(rng.uniform(np.log(lo), np.log(hi), size=envs)).astype(np.int64)
-    W, K_steps = args.warmup, args.steps
     n_step_calls = 2 * W + 3 * K_steps  # alternating device / e2e steps, then the roofline pass
     # Exactly the pages the contexts and every timed step can need (the pool
     # never grows): each row's longest possible length plus one page of slack.
@@ -644,9 +679,6 @@ def run_large_batch(args):
                             "launches_timed": len(attn_ms)},
                "kv_pool_gb": round(pages * LB["layers"] * 2 * Hkv * P * hd * 2 / 1e9, 1),
                "gpu_launches": int(launches), "clocks": clk, "device_status": status}
-    if world > 1:
-        dist.barrier()
-        dist.destroy_process_group()
     return out
 
 
@@ -689,6 +721,15 @@ def unique_kv_tokens(sess, rows):
 
 
 def run_grpo(args):
+    dev, world, rank, local = _setup_ranks()
+    out = grpo_measure(dev, world, rank, local, args.grpo_roots, args.steps, args.warmup)
+    _teardown_ranks(world)
+    return out
+
+
+def grpo_measure(dev, world, rank, local, roots, K_steps, W):
+    """Time the GRPO branch rollout on this process group (every rank calls
+    it; rank 0 gets the result line)."""
     import torch
     import torch.distributed as dist
     import torch.nn.functional as F
@@ -697,21 +738,11 @@ def run_grpo(args):
     from mouse_core_b200 import kernels as K
     from mouse_core_b200.backbone import Qwen3Backbone
 
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
-    if world > 1:
-        from datetime import timedelta
-
-        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
-
     def barrier():
         if world > 1:
             dist.barrier()
 
-    R, G, P, D = args.grpo_roots, GR["branches"], GR["page"], HIDDEN
+    R, G, P, D = roots, GR["branches"], GR["page"], HIDDEN
     NB = R * G
     B = R + NB
     torch.manual_seed(0)
@@ -727,7 +758,6 @@ def run_grpo(args):
     lo, hi = GR["root_len"]
     root_len = rng.integers(lo, hi + 1, size=R)
     fork_at = rng.integers(1, np.repeat(root_len, G) + 1)  # per branch, U[1, root length]
-    W, K_steps = args.warmup, args.steps
     n_step_calls = W + 2 * K_steps + W + K_steps
     pages = int(((root_len + P - 1) // P).sum() + ((fork_at % P) > 0).sum()
                 + NB * ((GR["prefill"] + n_step_calls + 2 * P - 1) // P) + 8)
@@ -863,9 +893,6 @@ def run_grpo(args):
                "cpu_baseline_note": "not run: one step reads ~90 GB of KV; the decode line's CPU port covers the "
                                     "same per-token arithmetic",
                "gpu_launches": int(launches), "clocks": clk, "device_status": status}
-    if world > 1:
-        dist.barrier()
-        dist.destroy_process_group()
     return out
 
 
@@ -1357,6 +1384,10 @@ def main():
     ap.add_argument("--train", action="store_true", help="time the packed DQN training step instead of decode")
     ap.add_argument("--train-rows", type=int, default=TRAIN_ROWS, help="16384-token rows per training step")
     ap.add_argument("--no-train", action="store_true", help="leave the training object out of the decode line")
+    ap.add_argument("--no-extra", action="store_true",
+                    help="leave the large-batch and GRPO objects out of the decode line")
+    ap.add_argument("--extra-steps", type=int, default=5,
+                    help="timed steps of the large-batch and GRPO objects in the decode line")
     ap.add_argument("--train-steps", type=int, default=5,
                     help="timed steps of the training object in the decode line (its warm-up is --warmup)")
     ap.add_argument("--large-batch", action="store_true",
