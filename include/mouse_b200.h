@@ -51,7 +51,8 @@ int mb_version(void);
  * device. 0 = healthy; 1 / 2 = a consumer / producer wait ran out; 3 = a page
  * id outside the pool (or a token past the block table); 4 = misaligned
  * dynamic shared memory; 5 = a stored-dS pair index outside the scratch;
- * 6 = a CTA's own copies did not land before it exited. */
+ * 6 = a CTA's own copies did not land before it exited; 7 = an embedding id
+ * outside its table. */
 int mb_device_status(int* status_out, int clear);
 
 /* Diagnostics, no counterpart in the reference (whose kernels come from
@@ -200,6 +201,22 @@ int mb_silu_mul(const void* gate_up, int rows, int inter, void* out, mb_stream_t
 int mb_rmsnorm_f32(const float* x, const void* x_bf16, const float* delta, const void* weight, float eps, int rows,
                    int dim, float* sum_out, void* norm_out, mb_stream_t stream);
 int mb_silu_mul_f32(const float* gate_up, int rows, int inter, void* out, mb_stream_t stream);
+
+/* ---------------------------------------------------------------------
+ * Token embedding of a flat TokenBatch (K11). Replaces NumericEmbedder.forward
+ * (models/embedding/embedding.py:293-326): embeds[t] = the row ids[t] of the
+ * table of type types[t] (kinds[type] = 1), or, for Fourier types (kind 2),
+ * fourier_scale * cos(scalars[t] * freqs[ids[t]] + phases[ids[t]])
+ * (models/embedding/encoding.py:67-86), else zero. tables is a device array
+ * of n_types device pointers to [vocab[type], dim] rows in out's dtype (bf16,
+ * or fp32 when out_f32); freqs / phases fp32 [freq_sets, dim]. An id outside
+ * its table or bank leaves the token zero and sets status 7. All index arrays
+ * int32, device memory; dim * element size a multiple of 16 bytes.
+ * ------------------------------------------------------------------- */
+int mb_embed_tokens(const int32_t* types, const int32_t* ids, const float* scalars, long long tokens, int dim,
+                    const int32_t* kinds, const void* const* tables, const int32_t* vocab, int n_types,
+                    const float* fourier_freqs, const float* fourier_phases, int freq_sets, float fourier_scale,
+                    void* out, int out_f32, mb_stream_t stream);
 
 /* ---------------------------------------------------------------------
  * Packed varlen segment-causal attention forward (K5, tcgen05).

@@ -33,6 +33,8 @@ PROTOTYPES = {
     "mb_page_copy": (_c_int, [_vp, _vp, _vp, _vp, _c_int, _c_ll, _vp]),
     "mb_decode_step_meta": (_c_int, [_c_int, _c_int, _c_int, _vp, _vp, _vp, _vp, _vp, _vp]),
     "mb_rmsnorm": (_c_int, [_vp, _vp, _vp, _c_float, _c_int, _c_int, _vp, _vp, _vp]),
+    "mb_embed_tokens": (_c_int, [_vp, _vp, _vp, _c_ll, _c_int, _vp, _vp, _vp, _c_int, _vp, _vp, _c_int,
+                                 _c_float, _vp, _c_int, _vp]),
     "mb_silu_mul": (_c_int, [_vp, _c_int, _c_int, _vp, _vp]),
     "mb_rmsnorm_f32": (_c_int, [_vp, _vp, _vp, _vp, _c_float, _c_int, _c_int, _vp, _vp, _vp]),
     "mb_silu_mul_f32": (_c_int, [_vp, _c_int, _c_int, _vp, _vp]),

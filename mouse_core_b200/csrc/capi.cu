@@ -358,6 +358,38 @@ int mb_silu_mul_f32(const float* gate_up, int rows, int inter, void* out, mb_str
   return e == cudaSuccess ? MB_OK : cuda_fail(e, "silu_mul_f32 launch");
 }
 
+int mb_embed_tokens(const int32_t* types, const int32_t* ids, const float* scalars, long long tokens, int dim,
+                    const int32_t* kinds, const void* const* tables, const int32_t* vocab, int n_types,
+                    const float* fourier_freqs, const float* fourier_phases, int freq_sets, float fourier_scale,
+                    void* out, int out_f32, mb_stream_t stream) {
+  if (tokens < 0 || dim <= 0 || n_types < 0 || freq_sets < 0)
+    return fail(MB_ERR_INVALID_ARG, "tokens >= 0, dim > 0, n_types >= 0 and freq_sets >= 0 required");
+  if (tokens == 0) return MB_OK;
+  if (dim % (out_f32 ? 4 : 8)) return fail(MB_ERR_UNSUPPORTED, "dim must be a multiple of 16 bytes of elements");
+  if (!types || !ids || !scalars || !out || (n_types > 0 && (!kinds || !tables || !vocab)))
+    return fail(MB_ERR_INVALID_ARG, "a required pointer is NULL");
+  if (freq_sets > 0 && (!fourier_freqs || !fourier_phases))
+    return fail(MB_ERR_INVALID_ARG, "Fourier banks need freqs and phases");
+  if (!aligned(out, 16)) return fail(MB_ERR_INVALID_ARG, "out must be 16-byte aligned");
+  mb::EmbedParams p{};
+  p.types = types;
+  p.ids = ids;
+  p.scalars = scalars;
+  p.L = tokens;
+  p.D = dim;
+  p.n_types = n_types;
+  p.kinds = kinds;
+  p.tables = tables;
+  p.vocab = vocab;
+  p.freqs = fourier_freqs;
+  p.phases = fourier_phases;
+  p.freq_sets = freq_sets;
+  p.fourier_scale = fourier_scale;
+  p.out = out;
+  cudaError_t e = mb::launch_embed_tokens(p, out_f32 != 0, (cudaStream_t)stream);
+  return e == cudaSuccess ? MB_OK : cuda_fail(e, "embed tokens launch");
+}
+
 int mb_silu_mul(const void* gate_up, int rows, int inter, void* out, mb_stream_t stream) {
   if (rows < 0 || inter <= 0 || inter % 2) return fail(MB_ERR_INVALID_ARG, "rows >= 0 and an even inter required");
   if (rows == 0) return MB_OK;

@@ -26,6 +26,7 @@ enum DeviceStatus : int {
   kDevBadSmem = 4,       // dynamic shared memory base not 1024-byte aligned
   kDevBadPair = 5,       // stored-dS pair index outside the scratch (inconsistent pair offsets)
   kDevTimeoutDrain = 6,  // a CTA's own copies did not land before it exited
+  kDevBadIndex = 7,      // an embedding id outside its table (the token is left zero)
 };
 
 // The library is one translation unit (mouse_b200.cu), so the status word is

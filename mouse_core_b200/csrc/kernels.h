@@ -169,4 +169,22 @@ cudaError_t launch_decode_step_meta(int B, int width, int page_size, const int32
 cudaError_t launch_segment_meta(const int64_t* seq, int L, int tile, int64_t* pos_out, int32_t* run_start,
                                 int32_t* run_end, int32_t* tile_lo, int32_t* flags, cudaStream_t stream);
 
+// Token embedding (embed.cu).
+struct EmbedParams {
+  const int32_t* types;        // [L] token type (modality) id
+  const int32_t* ids;          // [L] table row, or Fourier bank for Fourier types
+  const float* scalars;        // [L] Fourier input
+  long long L;
+  int D, n_types;
+  const int32_t* kinds;        // [n_types]: 0 none, 1 table, 2 Fourier
+  const void* const* tables;   // [n_types] device pointers to [vocab, D] rows (table kinds)
+  const int32_t* vocab;        // [n_types]
+  const float* freqs;          // [freq_sets, D]
+  const float* phases;         // [freq_sets, D]
+  int freq_sets;
+  float fourier_scale;
+  void* out;                   // [L, D], the tables' dtype (bf16 or fp32)
+};
+cudaError_t launch_embed_tokens(const EmbedParams& p, bool out_f32, cudaStream_t stream);
+
 }  // namespace mb

@@ -8,5 +8,6 @@
 #include "varlen_attention.cu"
 #include "varlen_backward.cu"
 #include "packing.cu"
+#include "embed.cu"
 #include "capi.cu"
 #include "decode_noalloc.cu"

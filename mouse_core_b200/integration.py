@@ -60,6 +60,26 @@ def install(mouse_core_module=None) -> None:
     if flex_packed_forward is not None:
         flex_train = importlib.import_module("mouse_core.models.backbone.flex_train")
         _patch(flex_train, "flex_packed_forward", flex_packed_forward)
+    try:
+        embedding = importlib.import_module("mouse_core.models.embedding.embedding")
+    except ImportError:
+        embedding = None
+    if embedding is not None and hasattr(embedding, "NumericEmbedder"):
+        from mouse_core_b200.encoder import fused_forward
+
+        cls = embedding.NumericEmbedder
+        reference_forward = cls.forward
+
+        def forward(self, token_batch):
+            # CUDA embedders take the one-kernel path; a CPU embedder is the
+            # caller's own CPU model and keeps the reference's code.
+            try:
+                on_cuda = next(self.parameters()).device.type == "cuda"
+            except StopIteration:
+                on_cuda = self.fourier.freqs.device.type == "cuda"
+            return fused_forward(self, token_batch) if on_cuda else reference_forward(self, token_batch)
+
+        _patch(cls, "forward", forward)
 
 
 def uninstall() -> None:

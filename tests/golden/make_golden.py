@@ -32,6 +32,10 @@ return:
                        40-call ragged schedule with task ends and a small
                        ``max_cache``: whole-batch rebuilds, and each env
                        run alone (the per-row semantics).
+* ``embedding.npz``    ``NumericEmbedder`` (models/embedding/embedding.py):
+                       ``prepare`` and ``forward`` on ragged transition rows
+                       with discrete, rff, continuous (optional) and learnable
+                       modalities.
 
 The fixtures are small; nothing at test time reads the reference.
 """
@@ -385,6 +389,52 @@ def make_grow_rebuild() -> None:
     np.savez_compressed(HERE / "grow_rebuild_qwen3.npz", **rec)
 
 
+EMBED_MODALITIES = [
+    {"type": "discrete", "field": "obs", "vocab_size": 16},
+    {"type": "discrete", "field": "action", "vocab_size": 4},
+    {"type": "rff", "field": "reward"},
+    {"type": "continuous", "field": "pos", "dim": 3, "required": False},
+    {"type": "learnable", "tokens": 2},
+]
+
+
+def make_embedding() -> None:
+    """The reference's NumericEmbedder (prepare + forward, fp32) on ragged
+    batches of transition rows, one of them with an optional field missing."""
+    import torch
+    from mouse_core.models.embedding.embedding import NumericEmbedder
+
+    torch.manual_seed(41)
+    emb = NumericEmbedder(hidden_dim=64, modalities=EMBED_MODALITIES, fourier_min=0.01, fourier_max=10.0)
+    rng = np.random.default_rng(42)
+    rec = {"hidden_dim": np.array(64)}
+    for key, val in emb.state_dict().items():
+        rec["w:" + key] = val.numpy()
+    rec["meta_type_id"] = np.array([m.type_id for m in emb._meta])
+    rec["meta_kind"] = np.array([m.kind for m in emb._meta])
+    for ci, steps in enumerate([[4, 0, 2], [1, 3, 5, 2]]):
+        batch = []
+        for n in steps:
+            rows = []
+            for _ in range(n):
+                row = {"obs": int(rng.integers(0, 16)), "action": int(rng.integers(0, 4)),
+                       "reward": float(rng.normal())}
+                if rng.random() < 0.7:
+                    row["pos"] = rng.normal(size=3).astype(np.float32) * 3.0
+                rows.append(row)
+            batch.append(rows)
+        tb = emb.prepare(batch)
+        with torch.no_grad():
+            embeds, _, pred = emb(tb)
+        for name in ("token_types", "token_ids", "scalars", "sequence_ids", "step_ids", "prediction_indices"):
+            rec[f"c{ci}_{name}"] = np.asarray(getattr(tb, name))
+        rec[f"c{ci}_B"] = np.array(tb.B)
+        rec[f"c{ci}_sequence_id"] = np.asarray(tb.col_values["sequence_id"])
+        rec[f"c{ci}_embeds"] = embeds.numpy()
+        rec[f"c{ci}_pred"] = pred.numpy()
+    np.savez_compressed(HERE / "embedding.npz", **rec)
+
+
 def make_packed_forward() -> None:
     import torch
     from mouse_core.models.backbone import Qwen3Backbone
@@ -410,7 +460,7 @@ def make_packed_forward() -> None:
     np.savez_compressed(HERE / "packed_fwd_qwen3.npz", **rec)
 
 
-FIXTURES = ("index_maps", "kv_policy", "packed_attention", "decode", "packed_forward", "grow_rebuild")
+FIXTURES = ("index_maps", "kv_policy", "packed_attention", "decode", "packed_forward", "grow_rebuild", "embedding")
 
 
 def main() -> None:
@@ -443,6 +493,8 @@ def main() -> None:
         make_packed_forward()
     if "grow_rebuild" in args.only:
         make_grow_rebuild()
+    if "embedding" in args.only:
+        make_embedding()
     print("golden fixtures written to", HERE)
 
 

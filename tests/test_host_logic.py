@@ -191,7 +191,8 @@ def test_install_patches_and_restores_the_reference_hot_path(monkeypatch):
     mods = {}
     for name in ("mouse_core", "mouse_core.models", "mouse_core.models.backbone", "mouse_core.models.backbone.base",
                  "mouse_core.models.backbone.flex_train", "mouse_core.models.embedding",
-                 "mouse_core.models.embedding.packing", "mouse_core.models.base", "mouse_core.models.kv_policy"):
+                 "mouse_core.models.embedding.packing", "mouse_core.models.base", "mouse_core.models.kv_policy",
+                 "mouse_core.models.embedding.embedding"):
         mods[name] = types.ModuleType(name)
         monkeypatch.setitem(sys.modules, name, mods[name])
 
@@ -199,6 +200,11 @@ def test_install_patches_and_restores_the_reference_hot_path(monkeypatch):
         decode_session = orig
 
     mods["mouse_core.models.backbone.base"].Backbone = Backbone
+
+    class NumericEmbedder:
+        forward = orig
+
+    mods["mouse_core.models.embedding.embedding"].NumericEmbedder = NumericEmbedder
     mods["mouse_core.models.backbone.flex_train"].flex_packed_forward = orig
     mods["mouse_core.models.embedding.packing"].left_align_content = orig
     mods["mouse_core.models.base"]._flat_to_batched_left_pad = orig
@@ -214,6 +220,7 @@ def test_install_patches_and_restores_the_reference_hot_path(monkeypatch):
 
         assert mods["mouse_core.models.backbone.flex_train"].flex_packed_forward is flex_packed_forward
         assert Backbone.decode_session is not orig
+        assert NumericEmbedder.forward is not orig
         try:
             Backbone().decode_session(batch_size=2, capacity=8)  # no ``model``: the reference's error
         except NotImplementedError:
@@ -224,6 +231,7 @@ def test_install_patches_and_restores_the_reference_hot_path(monkeypatch):
     finally:
         integration.uninstall()
     assert Backbone.decode_session is orig
+    assert NumericEmbedder.forward is orig
     assert mods["mouse_core.models.embedding.packing"].left_align_content is orig
     assert mods["mouse_core.models.base"]._flat_to_batched_left_pad is orig
     assert mods["mouse_core.models.backbone.flex_train"].flex_packed_forward is orig

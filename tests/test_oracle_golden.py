@@ -175,3 +175,19 @@ def test_grow_rebuild_oracle_matches_reference(per_row):
                 assert np.abs(out[b, S - n:] - ref[ref.shape[0] - n:]).max() < 1e-5, (ci, b)
         rebuilt += int((fed > 3).sum())  # a window longer than any append is a rebuild
     assert rebuilt >= 5
+
+
+def test_embedding_oracle_matches_reference():
+    """NumericEmbedder.forward restated: table rows for discrete and learnable
+    tokens, static Fourier features for rff / continuous ones."""
+    from oracle import encoder as oenc
+
+    rec = load("embedding.npz")
+    tables = {int(t): rec[f"w:_tables.{t}.weight"] for t, k in zip(rec["meta_type_id"], rec["meta_kind"])
+              if str(k) != "fourier"}
+    fourier = [int(t) for t, k in zip(rec["meta_type_id"], rec["meta_kind"]) if str(k) == "fourier"]
+    for ci in range(2):
+        got = oenc.embed_tokens(rec[f"c{ci}_token_types"], rec[f"c{ci}_token_ids"], rec[f"c{ci}_scalars"], tables,
+                                fourier, rec["w:fourier.freqs"], rec["w:fourier.phases"],
+                                float(rec["w:fourier.output_scale"]), int(rec["hidden_dim"]))
+        assert np.abs(got - rec[f"c{ci}_embeds"]).max() < 1e-5
