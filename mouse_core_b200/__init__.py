@@ -4,6 +4,7 @@ Drop-in pieces for ``mouse_core.models``:
 
 * ``PagedDecodeSession`` (alias ``FlexDecodeSession``) — cached batched
   decode over ragged env batches with a paged KV cache.
+* ``GrowRebuildDecoder`` — the grow-then-rebuild caller loop on that session.
 * ``flex_packed_forward`` — packed segment-causal training forward whose
   attention (and its backward) run on tcgen05 kernels.
 * ``Qwen3Backbone`` / ``LlamaBackbone`` / ``IdentityBackbone`` /
@@ -33,6 +34,7 @@ from mouse_core_b200.packing import (
 
 __all__ = [
     "PagedDecodeSession",
+    "GrowRebuildDecoder",
     "FlexDecodeSession",
     "flex_packed_forward",
     "Backbone",
@@ -57,6 +59,10 @@ def __getattr__(name):
         from mouse_core_b200 import decode
 
         return getattr(decode, name)
+    if name == "GrowRebuildDecoder":
+        from mouse_core_b200.grow_rebuild import GrowRebuildDecoder
+
+        return GrowRebuildDecoder
     if name == "flex_packed_forward":
         from mouse_core_b200.packed import flex_packed_forward
 
