@@ -52,7 +52,7 @@ int mb_version(void);
  * id outside the pool (or a token past the block table); 4 = misaligned
  * dynamic shared memory; 5 = a stored-dS pair index outside the scratch;
  * 6 = a CTA's own copies did not land before it exited; 7 = an embedding id
- * outside its table. */
+ * outside its table, or a TD action / done code out of range. */
 int mb_device_status(int* status_out, int clear);
 
 /* Diagnostics, no counterpart in the reference (whose kernels come from
@@ -217,6 +217,31 @@ int mb_embed_tokens(const int32_t* types, const int32_t* ids, const float* scala
                     const int32_t* kinds, const void* const* tables, const int32_t* vocab, int n_types,
                     const float* fourier_freqs, const float* fourier_phases, int freq_sets, float fourier_scale,
                     void* out, int out_f32, mb_stream_t stream);
+
+/* ---------------------------------------------------------------------
+ * One-step TD loss (K12). Replaces DqnObjective.__call__
+ * (objectives/dqn.py:116-213) and _valid_transitions (dqn.py:12-39): over
+ * the pairs (i, i + 1) with equal sequence_id (all pairs when it is NULL),
+ * target = reward[i+1] + gammas[done[i+1]] * max_a q_target[i+1],
+ * loss = mean (q[i, action[i+1]] - target)^2 (+ cql_weight * (|target| +
+ * cql_eps) * (logsumexp(q[i]) - q[i, action[i+1]])). out (device, 6 floats):
+ * loss, valid pairs, then mean / std / min / max over valid pairs of
+ * max_a q[i] (the reference's metrics) — no host sync; loss is NaN when no
+ * pair is valid. q, q_target f32 [n, actions]; action, done, sequence_id
+ * int64 [n]; reward f32 [n]; gammas: host array of 5 (done codes 0..4);
+ * scratch of mb_td_loss_scratch_bytes(n), zero-filled once before its first
+ * use (calls leave it ready for the next). mb_td_loss_bwd writes
+ * dq = grad_out[0] * d loss / d q (grad_out a device scalar or NULL for 1)
+ * from the forward's scratch and out. A pair whose action or done code is out
+ * of range is left out and sets status 7.
+ * ------------------------------------------------------------------- */
+size_t mb_td_loss_scratch_bytes(int n);
+int mb_td_loss_fwd(const float* q, const float* q_target, const int64_t* action, const float* reward,
+                   const int64_t* done, const int64_t* sequence_id, int n, int actions, const float* gammas,
+                   float cql_weight, float cql_eps, void* scratch, size_t scratch_bytes, float* out,
+                   mb_stream_t stream);
+int mb_td_loss_bwd(const float* q, const int64_t* action, int n, int actions, float cql_weight, void* scratch,
+                   size_t scratch_bytes, const float* out, const float* grad_out, float* dq, mb_stream_t stream);
 
 /* ---------------------------------------------------------------------
  * Packed varlen segment-causal attention forward (K5, tcgen05).

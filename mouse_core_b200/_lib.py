@@ -35,6 +35,10 @@ PROTOTYPES = {
     "mb_rmsnorm": (_c_int, [_vp, _vp, _vp, _c_float, _c_int, _c_int, _vp, _vp, _vp]),
     "mb_embed_tokens": (_c_int, [_vp, _vp, _vp, _c_ll, _c_int, _vp, _vp, _vp, _c_int, _vp, _vp, _c_int,
                                  _c_float, _vp, _c_int, _vp]),
+    "mb_td_loss_scratch_bytes": (_c_size, [_c_int]),
+    "mb_td_loss_fwd": (_c_int, [_vp, _vp, _vp, _vp, _vp, _vp, _c_int, _c_int, _vp, _c_float, _c_float, _vp,
+                                _c_size, _vp, _vp]),
+    "mb_td_loss_bwd": (_c_int, [_vp, _vp, _c_int, _c_int, _c_float, _vp, _c_size, _vp, _vp, _vp, _vp]),
     "mb_silu_mul": (_c_int, [_vp, _c_int, _c_int, _vp, _vp]),
     "mb_rmsnorm_f32": (_c_int, [_vp, _vp, _vp, _vp, _c_float, _c_int, _c_int, _vp, _vp, _vp]),
     "mb_silu_mul_f32": (_c_int, [_vp, _c_int, _c_int, _vp, _vp]),

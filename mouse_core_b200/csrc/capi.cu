@@ -390,6 +390,71 @@ int mb_embed_tokens(const int32_t* types, const int32_t* ids, const float* scala
   return e == cudaSuccess ? MB_OK : cuda_fail(e, "embed tokens launch");
 }
 
+size_t mb_td_loss_scratch_bytes(int n) {
+  if (n <= 0) return 0;
+  auto up = [](size_t x) { return (x + 255) & ~size_t(255); };
+  return up((size_t)n * 4) * 2 + up((size_t)mb::td_blocks(n) * 6 * 4) + 256 + up((size_t)n);
+}
+
+namespace {
+int td_params(const float* q, const float* q_target, const int64_t* action, const float* reward, const int64_t* done,
+              const int64_t* seq, int n, int actions, const float* gammas, float cql_weight, float cql_eps,
+              void* scratch, size_t scratch_bytes, float* out, mb::TdParams* p) {
+  if (n < 2) return fail(MB_ERR_INVALID_ARG, "Not enough valid q values in data.");
+  if (actions <= 0) return fail(MB_ERR_INVALID_ARG, "actions must be > 0");
+  if (!q || !action || !out || !scratch) return fail(MB_ERR_INVALID_ARG, "a required pointer is NULL");
+  const size_t need = mb_td_loss_scratch_bytes(n);
+  if (scratch_bytes < need || !aligned(scratch, 256))
+    return fail(MB_ERR_WORKSPACE, "TD loss scratch needs " + std::to_string(need) + " bytes, 256-byte aligned");
+  auto up = [](size_t x) { return (x + 255) & ~size_t(255); };
+  uint8_t* base = static_cast<uint8_t*>(scratch);
+  size_t o = 0;
+  p->err = reinterpret_cast<float*>(base + o);       o += up((size_t)n * 4);
+  p->cql_scale = reinterpret_cast<float*>(base + o); o += up((size_t)n * 4);
+  p->partials = reinterpret_cast<float*>(base + o);  o += up((size_t)mb::td_blocks(n) * 6 * 4);
+  p->ticket = reinterpret_cast<int*>(base + o);      o += 256;
+  p->valid = base + o;
+  p->q = q;
+  p->q_target = q_target;
+  p->action = action;
+  p->reward = reward;
+  p->done = done;
+  p->seq = seq;
+  p->N = n;
+  p->A = actions;
+  for (int k = 0; k < 5; ++k) p->gamma[k] = gammas ? gammas[k] : 0.f;
+  p->cql_weight = cql_weight;
+  p->cql_eps = cql_eps;
+  p->out = out;
+  return MB_OK;
+}
+}  // namespace
+
+int mb_td_loss_fwd(const float* q, const float* q_target, const int64_t* action, const float* reward,
+                   const int64_t* done, const int64_t* sequence_id, int n, int actions, const float* gammas,
+                   float cql_weight, float cql_eps, void* scratch, size_t scratch_bytes, float* out,
+                   mb_stream_t stream) {
+  mb::TdParams p{};
+  int rc = td_params(q, q_target, action, reward, done, sequence_id, n, actions, gammas, cql_weight, cql_eps,
+                     scratch, scratch_bytes, out, &p);
+  if (rc) return rc;
+  if (!q_target || !reward || !done || !gammas) return fail(MB_ERR_INVALID_ARG, "a required pointer is NULL");
+  cudaError_t e = mb::launch_td_loss_fwd(p, (cudaStream_t)stream);
+  return e == cudaSuccess ? MB_OK : cuda_fail(e, "td loss forward launch");
+}
+
+int mb_td_loss_bwd(const float* q, const int64_t* action, int n, int actions, float cql_weight, void* scratch,
+                   size_t scratch_bytes, const float* out, const float* grad_out, float* dq, mb_stream_t stream) {
+  mb::TdParams p{};
+  int rc = td_params(q, nullptr, action, nullptr, nullptr, nullptr, n, actions, nullptr, cql_weight, 0.f, scratch,
+                     scratch_bytes, const_cast<float*>(out), &p);
+  if (rc) return rc;
+  if (!dq) return fail(MB_ERR_INVALID_ARG, "dq is NULL");
+  p.dq = dq;
+  cudaError_t e = mb::launch_td_loss_bwd(p, grad_out, (cudaStream_t)stream);
+  return e == cudaSuccess ? MB_OK : cuda_fail(e, "td loss backward launch");
+}
+
 int mb_silu_mul(const void* gate_up, int rows, int inter, void* out, mb_stream_t stream) {
   if (rows < 0 || inter <= 0 || inter % 2) return fail(MB_ERR_INVALID_ARG, "rows >= 0 and an even inter required");
   if (rows == 0) return MB_OK;

@@ -187,4 +187,27 @@ struct EmbedParams {
 };
 cudaError_t launch_embed_tokens(const EmbedParams& p, bool out_f32, cudaStream_t stream);
 
+// TD loss (td_loss.cu).
+struct TdParams {
+  const float* q;         // [N, A] online action values (fp32)
+  const float* q_target;  // [N, A] target action values
+  const int64_t* action;  // [N]
+  const float* reward;    // [N]
+  const int64_t* done;    // [N] done codes 0..4
+  const int64_t* seq;     // [N] sequence ids, or null (every pair valid)
+  int N, A;
+  float gamma[5];
+  float cql_weight, cql_eps;
+  float* err;             // [N] scratch: per-pair TD error
+  uint8_t* valid;         // [N] scratch
+  float* cql_scale;       // [N] scratch (CQL only)
+  float* partials;        // [blocks * 6] scratch
+  int* ticket;            // [1] scratch, zero before the first call (left zero)
+  float* out;             // [6]: loss, valid pairs, q mean, std, min, max
+  float* dq;              // [N, A] gradient (backward)
+};
+int td_blocks(int N);
+cudaError_t launch_td_loss_fwd(const TdParams& p, cudaStream_t stream);
+cudaError_t launch_td_loss_bwd(const TdParams& p, const float* grad_out, cudaStream_t stream);
+
 }  // namespace mb

@@ -9,5 +9,6 @@
 #include "varlen_backward.cu"
 #include "packing.cu"
 #include "embed.cu"
+#include "td_loss.cu"
 #include "capi.cu"
 #include "decode_noalloc.cu"

@@ -158,3 +158,72 @@ def flat_sequence_causal_mask(*, sequence_ids: torch.Tensor, dtype: torch.dtype)
     out = torch.full((L, L), torch.finfo(dtype).min, dtype=dtype, device=sequence_ids.device)
     out.masked_fill_(allow, 0.0)
     return out.view(1, 1, L, L)
+
+
+# ---------------------------------------------------------------------------
+# Loader-side packing of training windows into fixed-length rows.
+# ---------------------------------------------------------------------------
+
+def pack_windows(lengths, row_len: int):
+    """Assign windows of ``lengths[w]`` tokens to rows of at most ``row_len``
+    tokens, first fit in decreasing length order (windows stay whole).
+
+    The reference's loader puts a whole batch of windows into ONE flat stream
+    (data/dataloader.py:314-339); the packed kernels work best on rows of a
+    fixed token budget (stable shapes for the attention work lists and the
+    activations). Returns ``(row [W], offset [W], row_tokens [R])``: window
+    ``w`` occupies tokens ``offset[w] .. offset[w] + lengths[w]`` of row
+    ``row[w]``; inside a row windows keep their original relative order.
+    """
+    lengths = np.asarray(lengths, dtype=np.int64).reshape(-1)
+    if (lengths < 0).any():
+        raise ValueError("window lengths must be >= 0")
+    if lengths.size and int(lengths.max()) > row_len:
+        raise ValueError(f"a window of {int(lengths.max())} tokens does not fit a row of {row_len}")
+    order = np.argsort(-lengths, kind="stable")
+    row = np.zeros(lengths.size, dtype=np.int64)
+    free: list[int] = []
+    for w in order:
+        n = int(lengths[w])
+        for r, f in enumerate(free):
+            if f >= n:
+                row[w] = r
+                free[r] = f - n
+                break
+        else:
+            row[w] = len(free)
+            free.append(row_len - n)
+    offset = np.zeros(lengths.size, dtype=np.int64)
+    row_tokens = np.zeros(len(free), dtype=np.int64)
+    for w in range(lengths.size):  # original order inside each row
+        offset[w] = row_tokens[row[w]]
+        row_tokens[row[w]] += lengths[w]
+    return row, offset, row_tokens
+
+
+def pack_rows(windows, row_len: int):
+    """Pack windows (dicts of equally long per-token arrays, e.g. token ids,
+    actions, rewards, done codes, targets) into rows of at most ``row_len``
+    tokens. Each row is a dict of the concatenated arrays plus
+    ``sequence_ids`` (the window's index inside the row, so the segment mask
+    keeps windows apart and positions restart per window), ``cu_seqlens``
+    (int32 ``[windows in row + 1]``) and ``window_ids`` (the windows it holds,
+    in order)."""
+    if not windows:
+        return []
+    keys = list(windows[0].keys())
+    lengths = np.array([len(next(iter(w.values()))) for w in windows], dtype=np.int64)
+    for w in windows:
+        if list(w.keys()) != keys or any(len(v) != len(next(iter(w.values()))) for v in w.values()):
+            raise ValueError("every window must hold the same keys, each with one entry per token")
+    row, _, _ = pack_windows(lengths, row_len)
+    rows = []
+    for r in range(int(row.max()) + 1):
+        ids = np.flatnonzero(row == r)
+        out = {k: np.concatenate([np.asarray(windows[w][k]) for w in ids]) for k in keys}
+        seg = lengths[ids]
+        out["sequence_ids"] = np.repeat(np.arange(ids.size, dtype=np.int64), seg)
+        out["cu_seqlens"] = np.concatenate([[0], np.cumsum(seg)]).astype(np.int32)
+        out["window_ids"] = ids
+        rows.append(out)
+    return rows

@@ -17,6 +17,7 @@ the target network's output supplied as an input tensor.
 
 from __future__ import annotations
 
+import ctypes
 from dataclasses import dataclass
 
 import torch
@@ -43,6 +44,62 @@ def td_loss(q: torch.Tensor, q_target: torch.Tensor, action: torch.Tensor, rewar
     target = (reward[1:] + g * q_target[1:].amax(-1)).detach()
     err = (q_sa - target) ** 2
     return err[valid].mean()
+
+
+class _FusedTDLoss(torch.autograd.Function):
+    """K12 forward (loss + metrics, no host sync) and backward (d loss / d q)."""
+
+    @staticmethod
+    def forward(ctx, q, q_target, action, reward, done, sequence_id, gammas, cql_weight, cql_eps):
+        from mouse_core_b200 import _lib
+
+        q = q.contiguous().float()
+        N, A = q.shape
+        lib = _lib.load()
+        scratch = torch.zeros(int(lib.mb_td_loss_scratch_bytes(N)), dtype=torch.uint8, device=q.device)
+        out = torch.empty(6, dtype=torch.float32, device=q.device)
+        g = (ctypes.c_float * 5)(*[float(x) for x in gammas])  # host array, alive through the call
+        _lib.call("mb_td_loss_fwd", q.data_ptr(), q_target.contiguous().float().data_ptr(),
+                  action.contiguous().data_ptr(), reward.contiguous().float().data_ptr(), done.contiguous().data_ptr(),
+                  None if sequence_id is None else sequence_id.contiguous().data_ptr(), N, A,
+                  ctypes.cast(g, ctypes.c_void_p), float(cql_weight),
+                  float(cql_eps), scratch.data_ptr(), scratch.numel(), out.data_ptr(),
+                  torch.cuda.current_stream(q.device).cuda_stream)
+        ctx.save_for_backward(q, action.contiguous(), out)
+        ctx.scratch, ctx.cql_weight = scratch, float(cql_weight)
+        return out
+
+    @staticmethod
+    def backward(ctx, grad_out):
+        from mouse_core_b200 import _lib
+
+        q, action, out = ctx.saved_tensors
+        N, A = q.shape
+        dq = torch.empty_like(q)
+        g = grad_out.contiguous().float()
+        _lib.call("mb_td_loss_bwd", q.data_ptr(), action.data_ptr(), N, A, ctx.cql_weight, ctx.scratch.data_ptr(),
+                  ctx.scratch.numel(), out.data_ptr(), g.data_ptr(), dq.data_ptr(),
+                  torch.cuda.current_stream(q.device).cuda_stream)
+        return dq, None, None, None, None, None, None, None, None
+
+
+def td_loss_fused(q: torch.Tensor, q_target: torch.Tensor, action: torch.Tensor, reward: torch.Tensor,
+                  done: torch.Tensor, sequence_id: torch.Tensor | None, gammas=(0.99, 0.0, 0.99, 0.0, 0.0),
+                  cql_weight: float = 0.0, cql_eps: float = 1.0):
+    """``td_loss`` (plus ``DqnObjective``'s optional CQL term and its metrics)
+    as one CUDA kernel forward and one backward: returns ``(loss, metrics)``
+    with ``metrics`` a device tensor ``[valid pairs, q_values_mean,
+    q_values_std, q_values_min, q_values_max]`` read back only if the caller
+    asks (the reference syncs to build its dict). Gradients flow to ``q``."""
+    if q.ndim != 2:
+        raise ValueError(f"DQN expects action_value shape [N, A], got {tuple(q.shape)}.")
+    if q.shape[0] < 2:
+        raise ValueError("Not enough valid q values in data.")
+    if q.device.type != "cuda":
+        raise RuntimeError("the fused TD loss runs on a CUDA device (B200, sm_100a) only")
+    out = _FusedTDLoss.apply(q, q_target.detach(), action, reward, done, sequence_id, tuple(gammas), cql_weight,
+                             cql_eps)
+    return out[0], out[1:].detach()
 
 
 class GradientAllReduce:
@@ -228,7 +285,7 @@ class PackedDQNTrainer:
             emb = self.embedding(row.token_ids)
             h = self._forward(model=self.model, embeds=emb, sequence_ids=row.sequence_ids)
             q = self.head(h.float())
-            loss = td_loss(q, row.q_target, row.action, row.reward, row.done, row.sequence_ids)
+            loss, _ = td_loss_fused(q, row.q_target, row.action, row.reward, row.done, row.sequence_ids)
             if r == len(rows) - 1:
                 self.reduce.arm()  # gradients become final during this backward
             (loss / total_rows).backward()

@@ -6,6 +6,7 @@ FMA-pipe exp2 of the attention backward must meet its error bound."""
 from __future__ import annotations
 
 import numpy as np
+import pytest
 import torch
 
 import mouse_core_b200 as mb
@@ -261,3 +262,35 @@ def test_decode_rope_frequencies_survive_a_bf16_cast():
         inv, scaling = rope_frequencies(bb.model.rotary_emb, bb.model.config, torch.device("cpu"))
         assert inv.dtype == torch.float32 and torch.equal(inv, exact)
         assert scaling == float(bb.model.rotary_emb.attention_scaling)
+
+
+def test_pack_windows_into_fixed_rows():
+    """Windows stay whole, every window lands once, rows respect the token
+    budget, offsets tile each row in the windows' original order, and
+    sequence ids / cu_seqlens describe the same segments."""
+    import numpy as np
+    import torch
+
+    from mouse_core_b200.packing import flat_sequence_position_ids, pack_rows, pack_windows
+
+    rng = np.random.default_rng(3)
+    lengths = rng.integers(256, 4097, size=37)
+    row, off, tokens = pack_windows(lengths, 16384)
+    assert tokens.max() <= 16384 and tokens.sum() == lengths.sum()
+    assert tokens.size <= int(np.ceil(lengths.sum() / 16384)) + 2  # first fit decreasing is near the bound
+    for r in range(tokens.size):
+        ids = np.flatnonzero(row == r)
+        assert np.array_equal(off[ids], np.concatenate([[0], np.cumsum(lengths[ids])[:-1]]))
+    with pytest.raises(ValueError):
+        pack_windows([5, 20000], 16384)
+    windows = [{"token_ids": rng.integers(0, 1024, size=n), "reward": rng.random(n)} for n in lengths]
+    rows = pack_rows(windows, 16384)
+    seen = np.concatenate([r["window_ids"] for r in rows])
+    assert np.array_equal(np.sort(seen), np.arange(lengths.size))
+    for r in rows:
+        n = r["token_ids"].shape[0]
+        assert n <= 16384 and r["sequence_ids"].shape == (n,) and r["cu_seqlens"][-1] == n
+        assert np.array_equal(np.diff(r["cu_seqlens"]), lengths[r["window_ids"]])
+        assert np.array_equal(r["token_ids"][:lengths[r["window_ids"][0]]], windows[r["window_ids"][0]]["token_ids"])
+        pos = flat_sequence_position_ids(torch.from_numpy(r["sequence_ids"])).numpy().reshape(-1)
+        assert np.array_equal(pos[r["cu_seqlens"][:-1]], np.zeros(len(r["window_ids"])))

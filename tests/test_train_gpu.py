@@ -119,3 +119,48 @@ def test_trainer_step_updates_and_reduces_loss():
     losses = [float(trainer.step(rows, total_rows=1)) for _ in range(8)]
     assert not torch.equal(before, head.out.weight)
     assert losses[-1] < losses[0]
+
+
+def _reference_td(q, q_target, action, reward, done, seq, gammas, cql_weight, cql_eps):
+    """DqnObjective.__call__ (objectives/dqn.py:116-213) restated in torch fp64."""
+    valid = seq[1:] == seq[:-1]
+    curr = q[:-1]
+    a = action[1:]
+    g = torch.tensor(gammas, dtype=q.dtype, device=q.device)[done[1:]]
+    qv = curr.gather(-1, a.unsqueeze(-1)).squeeze(-1)
+    target = reward[1:].to(q.dtype) + g * q_target[1:].amax(-1)
+    loss = (qv - target.detach()) ** 2
+    if cql_weight > 0:
+        scale = (target.abs() + cql_eps).detach()
+        loss = loss + cql_weight * scale * (torch.logsumexp(curr, -1) - qv)
+    m = curr.amax(-1).detach()[valid]
+    return loss[valid].mean(), torch.stack([valid.sum().to(q.dtype), m.mean(), m.std(), m.min(), m.max()])
+
+
+@pytest.mark.parametrize("cql_weight", [0.0, 0.5])
+def test_fused_td_loss_matches_the_objective(cql_weight):
+    """K12's loss, metrics and gradient against DqnObjective's formulas (fp64),
+    over a packed stream with several sequences and every done code."""
+    dev = _dev()
+    from mouse_core_b200.train import td_loss_fused
+
+    g = torch.Generator().manual_seed(4)
+    N, A = 5000, 4
+    q = torch.randn(N, A, generator=g).to(dev).requires_grad_(True)
+    qt = torch.rand(N, A, generator=g).to(dev)
+    action = torch.randint(0, A, (N,), generator=g).to(dev)
+    reward = torch.randn(N, generator=g).to(dev)
+    done = torch.randint(0, 5, (N,), generator=g).to(dev)
+    seq = torch.sort(torch.randint(0, 37, (N,), generator=g)).values.to(dev)
+    gammas = (0.99, 0.5, 0.9, 0.0, 0.25)
+    loss, metrics = td_loss_fused(q, qt, action, reward, done, seq, gammas, cql_weight, 1.0)
+    loss.backward()
+    q64 = q.detach().double().requires_grad_(True)
+    ref_loss, ref_metrics = _reference_td(q64, qt.double(), action, reward, done, seq, gammas, cql_weight, 1.0)
+    ref_loss.backward()
+    assert abs(loss.item() - ref_loss.item()) <= 1e-5 * max(1.0, abs(ref_loss.item()))
+    assert torch.allclose(metrics.double(), ref_metrics, rtol=1e-5, atol=1e-5)
+    assert torch.allclose(q.grad.double(), q64.grad, rtol=1e-4, atol=1e-8)
+    from mouse_core_b200 import _lib
+
+    assert _lib.device_status() == 0
