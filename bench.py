@@ -212,15 +212,18 @@ def prefill(sess, table, ctx_ids, lengths, chunk=512):
         done += n
 
 
-def roofline_traffic_per_launch():
-    """Per-launch DRAM bytes of the split decode kernel from the committed ncu
-    summary (profiles/decode_attention_cfg2.json), or None."""
+def roofline_traffic_per_launch(algorithmic_bytes):
+    """Per-launch DRAM bytes of the split decode kernel: the DRAM / algorithmic
+    byte ratio of the committed ncu capture (profiles/decode_attention_cfg2.json,
+    a smaller launch of the same kernel; traffic grows with the KV bytes read)
+    times this run's algorithmic bytes per launch, or None."""
     path = os.path.join(ROOT, "profiles", "decode_attention_cfg2.json")
     try:
         with open(path) as f:
             rec = json.load(f)
-        return rec.get("dram_bytes_per_launch_scaled")
-    except (OSError, ValueError):
+        ratio = rec["capture_dram_bytes_per_launch"] / rec["capture_algorithmic_bytes_per_launch"]
+        return int(ratio * algorithmic_bytes)
+    except (OSError, ValueError, KeyError, ZeroDivisionError):
         return None
 
 
@@ -448,7 +451,7 @@ def run_ours(args):
                     "ms_per_step": round(e2e_max / K_steps, 4)},
             "roofline": {"kernel": "split_decode_kernel (K1)", "bound": "hbm", "achieved": round(achieved, 1),
                          "peak": peak, "peak_source": peak_src, "unit": "GB/s", "frac": round(achieved / peak, 4),
-                         "traffic": roofline_traffic_per_launch(), "algorithmic_bytes_per_launch": int(attn_bytes),
+                         "traffic": roofline_traffic_per_launch(attn_bytes), "algorithmic_bytes_per_launch": int(attn_bytes),
                          "avg_launch_ms": round(attn_avg_ms, 5), "launches_timed": len(attn_ms)},
             "gpu_launches": int(launches),
             "clocks": clk,

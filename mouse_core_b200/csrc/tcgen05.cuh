@@ -320,6 +320,47 @@ __device__ __forceinline__ float exp2_fma(float x) {
   return __int_as_float(__float_as_int(p) + (__float_as_int(t) << 23));
 }
 
+// Three-input f32 maximum (one instruction on sm_100).
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
+// Packed fp32 pairs (one instruction for two lanes of arithmetic on sm_100):
+// (d0, d1) = (a0, a1) * (b0, b1) + (c0, c1) and (d0, d1) = (a0, a1) + (b0, b1),
+// each rounded to nearest like fmaf / a + b.
+__device__ __forceinline__ void ffma2(float& d0, float& d1, float a0, float a1, float b0, float b1, float c0,
+                                      float c1) {
+  asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\tmov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+      "mov.b64 rc, {%6, %7};\n\tfma.rn.f32x2 rd, ra, rb, rc;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d0), "=f"(d1)
+      : "f"(a0), "f"(a1), "f"(b0), "f"(b1), "f"(c0), "f"(c1));
+}
+__device__ __forceinline__ void fadd2(float& d0, float& d1, float a0, float a1, float b0, float b1) {
+  asm("{\n\t.reg .b64 ra, rb, rd;\n\tmov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+      "add.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d0), "=f"(d1)
+      : "f"(a0), "f"(a1), "f"(b0), "f"(b1));
+}
+
+// exp2_fma on a pair, its range reduction and cubic in packed fp32 pairs:
+// the same arithmetic (and results) as two exp2_fma calls in fewer
+// instructions.
+__device__ __forceinline__ void exp2_fma2(float& y0, float& y1, float x0, float x1) {
+  x0 = fmaxf(x0, -126.f);
+  x1 = fmaxf(x1, -126.f);
+  float t0, t1, n0, n1, f0, f1, q0, q1;
+  fadd2(t0, t1, x0, x1, 12582912.f, 12582912.f);
+  fadd2(n0, n1, t0, t1, -12582912.f, -12582912.f);
+  ffma2(f0, f1, n0, n1, -1.f, -1.f, x0, x1);  // x - n, exact
+  ffma2(q0, q1, 0.0550089821f, 0.0550089821f, f0, f1, 0.242210975f, 0.242210975f);
+  ffma2(q0, q1, q0, q1, f0, f1, 0.693282916f, 0.693282916f);
+  ffma2(q0, q1, q0, q1, f0, f1, 1.f, 1.f);
+  y0 = __int_as_float(__float_as_int(q0) + (__float_as_int(t0) << 23));
+  y1 = __int_as_float(__float_as_int(q1) + (__float_as_int(t1) << 23));
+}
+
 // Warpgroup register re-balancing (all four warps of a warpgroup execute it).
 // The block's register budget is fixed at launch; a kernel's decreases and
 // increases must sum to no more than that budget.

@@ -342,13 +342,15 @@ __global__ void __launch_bounds__(320, 1) varlen_fwd_kernel(const __grid_constan
           }
           // Row max and (below) row sum as 8 independent chains: one long
           // dependent chain per thread would serialise the softmax warp.
+          // Three-input maxima halve the max instructions.
           float mp[8];
 #pragma unroll
-          for (int q = 0; q < 8; ++q) mp[q] = __uint_as_float(v[q]);
+          for (int q = 0; q < 8; ++q) mp[q] = fmaxf(__uint_as_float(v[q]), __uint_as_float(v[8 + q]));
 #pragma unroll
-          for (int e = 8; e < 128; ++e) mp[e & 7] = fmaxf(mp[e & 7], __uint_as_float(v[e]));
-          const float mx = fmaxf(fmaxf(fmaxf(mp[0], mp[1]), fmaxf(mp[2], mp[3])),
-                                 fmaxf(fmaxf(mp[4], mp[5]), fmaxf(mp[6], mp[7])));
+          for (int e = 16; e < 128; e += 16)
+#pragma unroll
+            for (int q = 0; q < 8; ++q) mp[q] = fmax3(mp[q], __uint_as_float(v[e + q]), __uint_as_float(v[e + 8 + q]));
+          const float mx = fmax3(fmax3(mp[0], mp[1], mp[2]), fmax3(mp[3], mp[4], mp[5]), fmaxf(mp[6], mp[7]));
           // The scale is positive, so the max of raw scores gives the max of scaled ones.
           const float m_tile = mx * p.scale_log2;
           const float m_new = fmaxf(m_used, m_tile);
@@ -361,14 +363,25 @@ __global__ void __launch_bounds__(320, 1) varlen_fwd_kernel(const __grid_constan
           float ls[8];
 #pragma unroll
           for (int q = 0; q < 8; ++q) ls[q] = 0.f;
+          // Scale and shift, exponentials and row sums on packed fp32 pairs;
+          // one pair in four takes its 2^x on the FMA pipe (exp2_fma2), which
+          // unloads the SFU, the bound of this loop.
 #pragma unroll
           for (int c = 0; c < 4; ++c) {
             uint32_t pk[16];
 #pragma unroll
             for (int e = 0; e < 32; e += 2) {
-              const float p0 = fast_exp2(fmaf(__uint_as_float(v[32 * c + e]), p.scale_log2, neg_mu));
-              const float p1 = fast_exp2(fmaf(__uint_as_float(v[32 * c + e + 1]), p.scale_log2, neg_mu));
-              ls[(e >> 1) & 7] += p0 + p1;
+              float x0, x1, p0, p1;
+              ffma2(x0, x1, __uint_as_float(v[32 * c + e]), __uint_as_float(v[32 * c + e + 1]), p.scale_log2,
+                    p.scale_log2, neg_mu, neg_mu);
+              if (((e >> 1) & 7) >= 6) {
+                exp2_fma2(p0, p1, x0, x1);
+              } else {
+                p0 = fast_exp2(x0);
+                p1 = fast_exp2(x1);
+              }
+              const int q = 2 * ((e >> 1) & 3);
+              fadd2(ls[q], ls[q + 1], ls[q], ls[q + 1], p0, p1);
               pk[e >> 1] = pack_bf16x2(p0, p1);
             }
             tmem_st16(t_s + 16 * c, pk);

@@ -132,7 +132,8 @@ def _fma32(a, b, c):
 
 
 def test_exp2_fma_error_bound():
-    """The FMA-pipe 2^x of the attention backward (`exp2_fma`, tcgen05.cuh),
+    """The FMA-pipe 2^x of the attention kernels (`exp2_fma`, and its packed
+    pair form `exp2_fma2`, whose steps round the same way; tcgen05.cuh),
     restated step by step in float32: magic-number rounding to n, a cubic in
     f = x - n on [-0.5, 0.5], n added to the exponent field. Its relative
     error stays below 1.1e-4 (under bf16's half-ulp of 2^-9) over the softmax
