@@ -269,7 +269,7 @@ def run_ours(args):
     # cleared after that step and its next token starts a fresh one (the row
     # is emptied, and the device step restarts it at position 0).
     actions = rng.integers(0, 4, size=ENVS)
-    n_calls = total + 2 * K_steps  # warm-up + timed, host-cost pass, roofline pass
+    n_calls = total + K_steps  # warm-up + timed, host-cost pass
     ids_host = np.stack([transition_ids(rng, actions, ENVS) for _ in range(n_calls)])
     ids_dev = torch.from_numpy(ids_host).to(dev)
     task_end = (ids_host & 1).astype(bool)
@@ -281,18 +281,20 @@ def run_ours(args):
     def act_fn(h):
         return head(h).argmax(-1)
 
-    def device_step(i):
+    def device_step(i, s=sess):
         # One graph per step: embedding gather, both layers, the fp32 head and
         # the argmax (PagedDecodeSession.decode_step).
         if i > 0:
             gone = np.flatnonzero(task_end[i - 1])
             if gone.size:
-                sess.reset_rows(gone)
-        return sess.decode_step(ids_dev[i], ones, embed_fn, act_fn)
+                s.reset_rows(gone)
+        return s.decode_step(ids_dev[i], ones, embed_fn, act_fn)
 
     for i in range(W):
         device_step(i)
     torch.cuda.synchronize()
+    # The roofline pass below replays the timed steps on a copy of this state.
+    twin = sess.clone()
     barrier()
     torch.cuda.synchronize()
     clocks = Clocks(local)
@@ -318,17 +320,24 @@ def run_ours(args):
         host_t.append(time.perf_counter() - t0)
     torch.cuda.synchronize()
     host_us = statistics.median(host_t) * 1e6
-    # Roofline pass: K more steps run eagerly with CUDA events around every
-    # attention launch (on the launching stream); same kernel, same data.
-    sess.attn_events = []
+    # Roofline pass: the timed steps again, eagerly, on the copy of the cache
+    # taken before them (same tokens, same task ends, so the same KV bytes per
+    # launch); each attention launch is repeated (attn_reps) between CUDA
+    # events on the launching stream, the repeats queued back to back, so the
+    # events time the kernel alone. The KV read per launch is larger than L2.
+    twin.attn_events = []
     kv_sum = 0
-    for i in range(total + K_steps, n_calls):
+    ctx_mean = []
+    for i in range(W, total):
         gone = task_end[i - 1]
-        kv_sum += int(sess._len[~gone].sum()) + ENVS  # kv_len after this step's append
-        device_step(i)
+        kv_now = int(twin._len[~gone].sum()) + ENVS  # kv_len after this step's append
+        kv_sum += kv_now
+        ctx_mean.append(kv_now / ENVS)
+        device_step(i, twin)
     torch.cuda.synchronize()
-    attn_ms = [a.elapsed_time(b) for a, b in sess.attn_events]
-    sess.attn_events = None
+    attn_ms = [a.elapsed_time(b) / r for a, b, r in twin.attn_events]
+    del twin
+    torch.cuda.empty_cache()
     barrier()
 
     # ---------------- end-to-end loop through the public API (`e2e`)
@@ -458,6 +467,8 @@ def run_ours(args):
             "device_status": status,
             "task_ends": {"rows_reset_in_timed_steps": resets_timed,
                           "rows_rebuilt_in_e2e_steps": int(e2e_rebuilt),
+                          "mean_cached_tokens_per_row": {"first_timed_step": round(ctx_mean[0], 1),
+                                                         "last_timed_step": round(ctx_mean[-1], 1)},
                           "rule": "a token with its done bit set (p = 0.02) ends the env's task: the context is "
                                   "cleared and the next token starts a fresh one (the row restarts at position 0); "
                                   "the e2e loop also checks max_cache every step (rows_needing_rebuild)"},
@@ -647,7 +658,7 @@ def large_batch_measure(dev, world, rank, local, envs, K_steps, W):
         kv_sum += int(sess._len[~retire[call[0]]].sum()) + envs  # after this step's retirements
         device_step()
     torch.cuda.synchronize()
-    attn_ms = [a.elapsed_time(b) for a, b in sess.attn_events]
+    attn_ms = [a.elapsed_time(b) / r for a, b, r in sess.attn_events]
     sess.attn_events = None
     t = torch.tensor([ms, e2e_ms], device=dev)
     if world > 1:
@@ -825,7 +836,7 @@ def grpo_measure(dev, world, rank, local, roots, K_steps, W):
         kv_sum += unique_kv_tokens(sess, np.arange(R, B)) + NB
         device_step()
     torch.cuda.synchronize()
-    attn_ms = [a.elapsed_time(b) for a, b in sess.attn_events]
+    attn_ms = [a.elapsed_time(b) / r for a, b, r in sess.attn_events]
     sess.attn_events = None
 
     h_ids = torch.empty(B, dtype=torch.int32, pin_memory=True)

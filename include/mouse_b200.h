@@ -84,6 +84,22 @@ size_t mb_decode_workspace_bytes(int batch, int kv_heads, int q_rows, int head_d
 int mb_decode_plan(const int32_t* kv_len, int batch, int kv_heads, int q_rows, int head_dim, int max_kv_len,
                    void* workspace, size_t workspace_bytes, mb_stream_t stream);
 
+/* mb_decode_plan for rows that may share cached pages (forked prefixes,
+ * e.g. GRPO branches of one root): rows are grouped in aligned blocks of
+ * 16 / q_rows; where rows of a block hold a whole 2048-token chunk on the
+ * very same pages as the block's first row that has that chunk, one work
+ * item reads the chunk's K/V once for all of their queries (the other rows'
+ * entries get no item of their own). Results are identical to
+ * mb_decode_plan's. Requires
+ * every query to see every cached slot of its row (q_pos[b, s] >= kv_len[b]
+ * - q_rows, as in one-token decode: q_pos = kv_len - 1), and q_rows <= 8 for
+ * any sharing to happen. Replaces nothing in the reference, whose decode
+ * session copies a forked prefix per row (flex_decode.py:226-229 reads it
+ * per row). */
+int mb_decode_plan_shared(const int32_t* kv_len, const int32_t* block_table, int max_pages, int page_size,
+                          int batch, int kv_heads, int q_rows, int head_dim, int max_kv_len, void* workspace,
+                          size_t workspace_bytes, mb_stream_t stream);
+
 /* out = softmax(scale * q k^T, masked to slots <= q_pos) v, per row and
  * q-head (q-head h reads kv-head h / (q_heads / kv_heads)). head_dim 64 or
  * 128; page_size a multiple of 64. plan_ready = 1 reuses the plan already

@@ -22,6 +22,8 @@ PROTOTYPES = {
     "mb_set_wait_limit": (_c_int, [ctypes.c_longlong]),
     "mb_decode_workspace_bytes": (_c_size, [_c_int, _c_int, _c_int, _c_int, _c_int]),
     "mb_decode_plan": (_c_int, [_vp, _c_int, _c_int, _c_int, _c_int, _c_int, _vp, _c_size, _vp]),
+    "mb_decode_plan_shared": (_c_int, [_vp, _vp, _c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _vp,
+                                       _c_size, _vp]),
     "mb_decode_attention": (_c_int, [_vp, _vp, _vp, _c_int, _vp, _c_int, _vp, _vp, _c_int, _c_int, _c_int,
                                      _c_int, _c_int, _c_int, _c_float, _c_int, _c_int, _vp, _vp, _c_size, _vp]),
     "mb_decode_attention_noalloc": (_c_int, [_vp, _vp, _vp, _c_int, _vp, _c_int, _vp, _vp, _c_int, _c_int,

@@ -126,8 +126,25 @@ int mb_decode_plan(const int32_t* kv_len, int batch, int kv_heads, int q_rows, i
   const size_t need = mb::decode_workspace_layout(batch, kv_heads, q_rows, head_dim, max_kv_len, &lay);
   if (!workspace || workspace_bytes < need || !aligned(workspace, 256))
     return fail(MB_ERR_WORKSPACE, "workspace needs " + std::to_string(need) + " bytes, 256-byte aligned");
-  cudaError_t e = mb::launch_decode_plan(kv_len, batch, kv_heads, head_dim, lay,
+  cudaError_t e = mb::launch_decode_plan(kv_len, nullptr, 0, 0, batch, kv_heads, q_rows, head_dim, lay,
                                          static_cast<uint8_t*>(workspace), (cudaStream_t)stream);
+  return e == cudaSuccess ? MB_OK : cuda_fail(e, "decode plan launch");
+}
+
+int mb_decode_plan_shared(const int32_t* kv_len, const int32_t* block_table, int max_pages, int page_size,
+                          int batch, int kv_heads, int q_rows, int head_dim, int max_kv_len, void* workspace,
+                          size_t workspace_bytes, mb_stream_t stream) {
+  if (batch <= 0) return MB_OK;
+  if (!kv_len || !block_table) return fail(MB_ERR_INVALID_ARG, "kv_len or block_table is NULL");
+  if (q_rows <= 0 || q_rows > 16) return fail(MB_ERR_INVALID_ARG, "a plan exists only for 1..16 query rows");
+  if (head_dim != 64 && head_dim != 128) return fail(MB_ERR_UNSUPPORTED, "head_dim must be 64 or 128");
+  if (max_pages <= 0 || page_size <= 0) return fail(MB_ERR_INVALID_ARG, "max_pages and page_size must be positive");
+  mb::WorkspaceLayout lay;
+  const size_t need = mb::decode_workspace_layout(batch, kv_heads, q_rows, head_dim, max_kv_len, &lay);
+  if (!workspace || workspace_bytes < need || !aligned(workspace, 256))
+    return fail(MB_ERR_WORKSPACE, "workspace needs " + std::to_string(need) + " bytes, 256-byte aligned");
+  cudaError_t e = mb::launch_decode_plan(kv_len, block_table, max_pages, page_size, batch, kv_heads, q_rows,
+                                         head_dim, lay, static_cast<uint8_t*>(workspace), (cudaStream_t)stream);
   return e == cudaSuccess ? MB_OK : cuda_fail(e, "decode plan launch");
 }
 
@@ -215,7 +232,8 @@ int mb_decode_attention(const void* q, const void* k_pool, const void* v_pool, i
     if (!workspace || workspace_bytes < need || !aligned(workspace, 256))
       return fail(MB_ERR_WORKSPACE, "workspace needs " + std::to_string(need) + " bytes, 256-byte aligned");
     if (!plan_ready) {
-      cudaError_t e = mb::launch_decode_plan(kv_len, batch, kv_heads, head_dim, lay, ws, (cudaStream_t)stream);
+      cudaError_t e =
+          mb::launch_decode_plan(kv_len, nullptr, 0, 0, batch, kv_heads, R, head_dim, lay, ws, (cudaStream_t)stream);
       if (e != cudaSuccess) return cuda_fail(e, "decode plan launch");
     }
   }

@@ -208,11 +208,20 @@ struct SplitSmem {
   }
 };
 
+// Position of the n-th (0-based) set bit of `mask`.
+__device__ __forceinline__ int nth_bit(int mask, int n) {
+  for (int i = 0; i < n; ++i) mask &= mask - 1;
+  return __ffs(mask) - 1;
+}
+
 // Item metadata slot layout (ints after the Q rows).
 // kMetaB < 0 marks the end of the CTA's work; kMetaItem is the item's index
 // in the row-ordered work list (entry * Hkv + kv-head), where its partial
 // result goes.
-enum : int { kMetaB = 0, kMetaH, kMetaBegin, kMetaEnd, kMetaChunks, kMetaItem, kMetaKvEnd = 8 };
+// kMetaWidth is the item's member mask (bit k: batch row b + k; more than one
+// bit for a chunk several rows share, whose queries are R rows per member)
+// and kMetaChunk the chunk's index in each row.
+enum : int { kMetaB = 0, kMetaH, kMetaBegin, kMetaEnd, kMetaChunks, kMetaItem, kMetaWidth, kMetaChunk, kMetaKvEnd = 8 };
 
 template <int HD>
 __global__ void __launch_bounds__(160, 2) split_decode_kernel(const __grid_constant__ CUtensorMap kmap,
@@ -256,7 +265,7 @@ __global__ void __launch_bounds__(160, 2) split_decode_kernel(const __grid_const
   }
   __syncthreads();
 
-  const int n_items = *p.n_entries * p.Hkv;
+  const int n_items = *p.n_order * p.Hkv;
 
   if (warp == 4) {
     // ---------------------------------------------------------- producer warp
@@ -296,9 +305,14 @@ __global__ void __launch_bounds__(160, 2) split_decode_kernel(const __grid_const
       const int len = p.kv_len[b];
       const int t_begin = ent.y * p.chunk_tokens;
       const int t_end = min(t_begin + p.chunk_tokens, len);
+      const int members = p.width[e];  // nonzero for an entry in the order
+      const int width = __popc(members);
       if (lane < 16) {
         int ke = len;
-        if (lane < R) ke = min(p.q_pos[(size_t)b * p.S + lane / p.G] + 1, len);
+        if (width > 1)
+          ke = t_end;  // a shared chunk lies wholly below every query of its rows
+        else if (lane < R)
+          ke = min(p.q_pos[(size_t)b * p.S + lane / p.G] + 1, len);
         meta[kMetaKvEnd + lane] = ke;
       }
       if (lane == 0) {
@@ -308,13 +322,18 @@ __global__ void __launch_bounds__(160, 2) split_decode_kernel(const __grid_const
         meta[kMetaEnd] = t_end;
         meta[kMetaChunks] = p.row_chunks[b];
         meta[kMetaItem] = item;
+        meta[kMetaWidth] = members;
+        meta[kMetaChunk] = ent.y;
       }
+      // Query row r of the item: query row r % R (= s * G + g) of the item's
+      // (r / R)-th member row.
       for (int c = lane; c < 16 * (HD / 8); c += 32) {
         const int r = c / (HD / 8), ch = c % (HD / 8);
         uint4 val = make_uint4(0, 0, 0, 0);
-        if (r < R) {
-          const int s_ = r / p.G, g = r % p.G;
-          val = *reinterpret_cast<const uint4*>(p.q + (((size_t)b * p.S + s_) * p.Hq + (size_t)h * p.G + g) * HD +
+        if (r < width * R) {
+          const int bb = b + nth_bit(members, r / R), rr = r % R;
+          const int s_ = rr / p.G, g = rr % p.G;
+          val = *reinterpret_cast<const uint4*>(p.q + (((size_t)bb * p.S + s_) * p.Hq + (size_t)h * p.G + g) * HD +
                                                 ch * 8);
         }
         *reinterpret_cast<uint4*>(sq + r * SM::QROW + ch * 16) = val;
@@ -367,9 +386,10 @@ __global__ void __launch_bounds__(160, 2) split_decode_kernel(const __grid_const
     const int* meta = reinterpret_cast<const int*>(sq + 16 * SM::QROW);
     const int b = meta[kMetaB], h = meta[kMetaH];
     if (b < 0) break;  // the producer found no work left (the same value for every consumer)
-    const int item = meta[kMetaItem];
     const int t_begin = meta[kMetaBegin], t_end = meta[kMetaEnd];
-    const int nchunks = meta[kMetaChunks];
+    const int nchunks = meta[kMetaChunks];  // of row b (a shared chunk's rows all have more than one)
+    const int members = meta[kMetaWidth], chunk = meta[kMetaChunk];
+    const int width = __popc(members);
     const int kv_end[2] = {meta[kMetaKvEnd + gid], meta[kMetaKvEnd + gid + 8]};
     uint32_t qa[HD / 16][4];
 #pragma unroll
@@ -407,78 +427,90 @@ __global__ void __launch_bounds__(160, 2) split_decode_kernel(const __grid_const
     // An item with a tile that never arrived is not written (the CTA stops).
     if (named_barrier_or(1, 128, !alive)) break;
 
-    // ---- merge the four warps' (m, l, o) for the R real rows
+    // ---- merge the four warps' (m, l, o), R query rows at a time (one member
+    // row of the item per round; a shared chunk has `width` of them)
+    for (int bi = 0; bi < width; ++bi) {
+      const int r0 = bi * R;
+      if (bi > 0) named_barrier(1, 128);  // the previous round has read comb_*
 #pragma unroll
-    for (int half = 0; half < 2; ++half) {
-      l[half] += __shfl_xor_sync(0xffffffffu, l[half], 1);
-      l[half] += __shfl_xor_sync(0xffffffffu, l[half], 2);
-      const int r = gid + 8 * half;
-      if (r < R) {
-        if (tig == 0) {
-          comb_m[warp * R + r] = m[half];
-          comb_l[warp * R + r] = l[half];
-        }
+      for (int half = 0; half < 2; ++half) {
+        float lh = l[half];
+        lh += __shfl_xor_sync(0xffffffffu, lh, 1);
+        lh += __shfl_xor_sync(0xffffffffu, lh, 2);
+        const int r = gid + 8 * half - r0;
+        if (r >= 0 && r < R) {
+          if (tig == 0) {
+            comb_m[warp * R + r] = m[half];
+            comb_l[warp * R + r] = lh;
+          }
 #pragma unroll
-        for (int d = 0; d < HD / 8; ++d) {
-          float2 v = make_float2(o[d][2 * half], o[d][2 * half + 1]);
-          *reinterpret_cast<float2*>(&comb_o[((size_t)warp * R + r) * HD + d * 8 + tig * 2]) = v;
+          for (int d = 0; d < HD / 8; ++d) {
+            float2 v = make_float2(o[d][2 * half], o[d][2 * half + 1]);
+            *reinterpret_cast<float2*>(&comb_o[((size_t)warp * R + r) * HD + d * 8 + tig * 2]) = v;
+          }
         }
       }
-    }
-    named_barrier(1, 128);
-    for (int idx = tid; idx < R * HD; idx += 128) {
-      const int r = idx / HD, col = idx % HD;
-      float M = -INFINITY;
+      named_barrier(1, 128);
+      const int bb = b + nth_bit(members, bi);
+      const size_t pit = ((size_t)p.row_start[bb] + chunk) * p.Hkv + h;  // = item when width == 1
+      for (int idx = tid; idx < R * HD; idx += 128) {
+        const int r = idx / HD, col = idx % HD;
+        float M = -INFINITY;
 #pragma unroll
-      for (int w = 0; w < 4; ++w) M = fmaxf(M, comb_m[w * R + r]);
-      const float Mu = (M == -INFINITY) ? 0.f : M;
-      float L = 0.f, O = 0.f;
+        for (int w = 0; w < 4; ++w) M = fmaxf(M, comb_m[w * R + r]);
+        const float Mu = (M == -INFINITY) ? 0.f : M;
+        float L = 0.f, O = 0.f;
 #pragma unroll
-      for (int w = 0; w < 4; ++w) {
-        const float f = exp2f(comb_m[w * R + r] - Mu);
-        L += comb_l[w * R + r] * f;
-        O += comb_o[((size_t)w * R + r) * HD + col] * f;
-      }
-      const float val = (L > 0.f) ? O / L : 0.f;
-      if (nchunks == 1) {
-        const int s_ = r / p.G, g = r % p.G;
-        p.out[(((size_t)b * p.S + s_) * p.Hq + (size_t)h * p.G + g) * HD + col] = __float2bfloat16_rn(val);
-      } else {
-        p.part_o[((size_t)item * R + r) * HD + col] = val;
-        if (col == 0) p.part_lse[(size_t)item * R + r] = (L > 0.f) ? M + log2f(L) : -INFINITY;
+        for (int w = 0; w < 4; ++w) {
+          const float f = exp2f(comb_m[w * R + r] - Mu);
+          L += comb_l[w * R + r] * f;
+          O += comb_o[((size_t)w * R + r) * HD + col] * f;
+        }
+        const float val = (L > 0.f) ? O / L : 0.f;
+        if (nchunks == 1) {  // (width 1 only: a shared chunk's rows have later chunks)
+          const int s_ = r / p.G, g = r % p.G;
+          p.out[(((size_t)b * p.S + s_) * p.Hq + (size_t)h * p.G + g) * HD + col] = __float2bfloat16_rn(val);
+        } else {
+          p.part_o[(pit * R + r) * HD + col] = val;
+          if (col == 0) p.part_lse[pit * R + r] = (L > 0.f) ? M + log2f(L) : -INFINITY;
+        }
       }
     }
     if (nchunks > 1) {
-      // Release this CTA's partials, take a ticket; the last CTA of the
-      // (row, kv-head) acquires every partial and merges them.
-      named_barrier(1, 128);
-      if (tid == 0) {
-        __threadfence();
-        const int ticket = atomicAdd(&p.counters[b * p.Hkv + h], 1);
-        *flag = (ticket == nchunks - 1);
-        if (*flag) __threadfence();
-      }
-      named_barrier(1, 128);
-      if (*flag) {
-        const int first = p.row_start[b];
-        for (int idx = tid; idx < R * HD; idx += 128) {
-          const int r = idx / HD, col = idx % HD;
-          float M = -INFINITY;
-          for (int c = 0; c < nchunks; ++c)
-            M = fmaxf(M, __ldcg(&p.part_lse[((size_t)(first + c) * p.Hkv + h) * R + r]));
-          const float Mu = (M == -INFINITY) ? 0.f : M;
-          float den = 0.f, num = 0.f;
-          for (int c = 0; c < nchunks; ++c) {
-            const size_t pit = (size_t)(first + c) * p.Hkv + h;
-            const float f = exp2f(__ldcg(&p.part_lse[pit * R + r]) - Mu);
-            den += f;
-            num += f * __ldcg(&p.part_o[(pit * R + r) * HD + col]);
-          }
-          const int s_ = r / p.G, g = r % p.G;
-          p.out[(((size_t)b * p.S + s_) * p.Hq + (size_t)h * p.G + g) * HD + col] =
-              __float2bfloat16_rn(den > 0.f ? num / den : 0.f);
+      // Release this CTA's partials, take a ticket per covered row; the last
+      // CTA of a (row, kv-head) acquires every partial and merges them.
+      for (int bi = 0; bi < width; ++bi) {
+        const int bb = b + nth_bit(members, bi);
+        const int nch = p.row_chunks[bb];
+        named_barrier(1, 128);
+        if (tid == 0) {
+          __threadfence();
+          const int ticket = atomicAdd(&p.counters[bb * p.Hkv + h], 1);
+          *flag = (ticket == nch - 1);
+          if (*flag) __threadfence();
         }
-        if (tid == 0) p.counters[b * p.Hkv + h] = 0;
+        named_barrier(1, 128);
+        if (*flag) {
+          const int first = p.row_start[bb];
+          for (int idx = tid; idx < R * HD; idx += 128) {
+            const int r = idx / HD, col = idx % HD;
+            float M = -INFINITY;
+            for (int c = 0; c < nch; ++c)
+              M = fmaxf(M, __ldcg(&p.part_lse[((size_t)(first + c) * p.Hkv + h) * R + r]));
+            const float Mu = (M == -INFINITY) ? 0.f : M;
+            float den = 0.f, num = 0.f;
+            for (int c = 0; c < nch; ++c) {
+              const size_t pc = (size_t)(first + c) * p.Hkv + h;
+              const float f = exp2f(__ldcg(&p.part_lse[pc * R + r]) - Mu);
+              den += f;
+              num += f * __ldcg(&p.part_o[(pc * R + r) * HD + col]);
+            }
+            const int s_ = r / p.G, g = r % p.G;
+            p.out[(((size_t)bb * p.S + s_) * p.Hq + (size_t)h * p.G + g) * HD + col] =
+                __float2bfloat16_rn(den > 0.f ? num / den : 0.f);
+          }
+          if (tid == 0) p.counters[bb * p.Hkv + h] = 0;
+        }
       }
     }
     named_barrier(1, 128);
@@ -493,24 +525,67 @@ __global__ void __launch_bounds__(160, 2) split_decode_kernel(const __grid_const
 // of short rows fill in at the end instead of leaving a tail of long ones.
 // Also clears the per-(row, kv-head) tickets and the work counters. One CTA
 // of 1024 threads.
+//
+// Shared chunks (block_table given): rows are taken in aligned blocks of
+// NG = 16 / q_rows. In each block, the first row whose chunk j qualifies
+// leads, and every row of the block whose chunk j lies on the very same pages
+// (forked prefixes) joins its item: the K/V tiles are read once for all of
+// their queries (at most 16 MMA rows). The item's entry holds the member
+// rows as a bit mask (bit k: leader + k); the members' own entries get 0 and
+// no item, their partials are written by the shared item. A chunk qualifies
+// when it is whole and wholly below every query (end <= kv_len - q_rows).
 constexpr int kPlanBuckets = 33;  // chunk lengths 0 .. 2048 in 64-token units
 
-__global__ void __launch_bounds__(1024) decode_plan_kernel(const int32_t* kv_len, int B, int Hkv, int chunk,
-                                                           int max_entries, int2* entries, int* n_entries,
-                                                           int* row_start, int* row_chunks, int* counters,
-                                                           int* order, int* work) {
+__global__ void __launch_bounds__(1024) decode_plan_kernel(const int32_t* kv_len, const int32_t* block_table,
+                                                           int max_pages, int page_size, int B, int Hkv,
+                                                           int q_rows, int chunk, int max_entries, int2* entries,
+                                                           int* n_entries, int* row_start, int* row_chunks,
+                                                           int* counters, int* order, int* n_order, int* width,
+                                                           int* work) {
   __shared__ int warp_tot[32];
-  __shared__ int total_s;
+  __shared__ int total_s, n_order_s;
   __shared__ int hist[kPlanBuckets];
   __shared__ int cursor[kPlanBuckets];
   const int tid = threadIdx.x;
   if (tid < kPlanBuckets) hist[tid] = 0;
+  if (tid == 0) n_order_s = 0;
   const int per = (B + 1023) / 1024;
   const int r0 = min(tid * per, B), r1 = min(r0 + per, B);
   const int unit = max(chunk / (kPlanBuckets - 1), 1);
   auto bucket = [&](int len, int j) {  // descending rank of chunk j of a row of `len` tokens
     const int sz = min(chunk, max(len - j * chunk, 0));
     return (kPlanBuckets - 1) - min((sz + unit - 1) / unit, kPlanBuckets - 1);
+  };
+  const bool share = block_table != nullptr && page_size > 0 && chunk % page_size == 0 && q_rows > 0 &&
+                     q_rows <= 8;
+  const int NG = share ? 16 / q_rows : 1;
+  const int ppc = share ? chunk / page_size : 0;  // pages per chunk
+  auto eligible = [&](int r, int j) {
+    return (j + 1) * chunk <= max(kv_len[r], 0) - q_rows && (j + 1) * ppc <= max_pages;
+  };
+  auto same_pages = [&](int ra, int rb, int j) {
+    const int32_t* ta = block_table + (size_t)ra * max_pages + (size_t)j * ppc;
+    const int32_t* tb = block_table + (size_t)rb * max_pages + (size_t)j * ppc;
+    for (int q = 0; q < ppc; ++q)
+      if (ta[q] < 0 || ta[q] != tb[q]) return false;
+    return true;
+  };
+  // Rows whose item is entry (r, j)'s, as a mask over rows r .. r + NG - 1
+  // (bit 0: r itself); 0 when another row's item covers the entry.
+  auto members_of = [&](int r, int j) {
+    if (NG == 1 || !eligible(r, j)) return 1;
+    const int blk0 = r - r % NG, blk1 = min(blk0 + NG, B);
+    int lead = r;
+    for (int x = blk0; x < r; ++x)
+      if (eligible(x, j)) {
+        lead = x;
+        break;
+      }
+    if (lead != r) return same_pages(lead, r, j) ? 0 : 1;
+    int mask = 1;
+    for (int x = r + 1; x < blk1; ++x)
+      if (eligible(x, j) && same_pages(r, x, j)) mask |= 1 << (x - r);
+    return mask;
   };
   int cnt = 0;
   for (int r = r0; r < r1; ++r) cnt += max(1, (max(kv_len[r], 0) + chunk - 1) / chunk);
@@ -541,12 +616,14 @@ __global__ void __launch_bounds__(1024) decode_plan_kernel(const int32_t* kv_len
   if (total > max_entries) {
     if (tid == 0) {
       *n_entries = 0;
+      *n_order = 0;
       work[0] = 0;
       work[1] = 0;
       report(kDevBadPage);
     }
     return;
   }
+  int mine = 0;  // entries of this thread's rows that get an item
   for (int r = r0; r < r1; ++r) {
     const int len = max(kv_len[r], 0);
     const int c = max(1, (len + chunk - 1) / chunk);
@@ -554,10 +631,16 @@ __global__ void __launch_bounds__(1024) decode_plan_kernel(const int32_t* kv_len
     row_chunks[r] = c;
     for (int j = 0; j < c; ++j) {
       entries[base + j] = make_int2(r, j);
-      atomicAdd(&hist[bucket(len, j)], 1);
+      const int wd = members_of(r, j);
+      width[base + j] = wd;
+      if (wd > 0) {
+        atomicAdd(&hist[bucket(len, j)], 1);
+        ++mine;
+      }
     }
     base += c;
   }
+  atomicAdd(&n_order_s, mine);
   for (int i = tid; i < B * Hkv; i += 1024) counters[i] = 0;
   __syncthreads();
   if (tid == 0) {
@@ -567,6 +650,7 @@ __global__ void __launch_bounds__(1024) decode_plan_kernel(const int32_t* kv_len
       acc += hist[k];
     }
     *n_entries = total;
+    *n_order = n_order_s;
     work[0] = 0;
     work[1] = 0;
   }
@@ -575,7 +659,8 @@ __global__ void __launch_bounds__(1024) decode_plan_kernel(const int32_t* kv_len
   for (int r = r0; r < r1; ++r) {
     const int len = max(kv_len[r], 0);
     const int c = max(1, (len + chunk - 1) / chunk);
-    for (int j = 0; j < c; ++j) order[atomicAdd(&cursor[bucket(len, j)], 1)] = base + j;
+    for (int j = 0; j < c; ++j)
+      if (width[base + j] > 0) order[atomicAdd(&cursor[bucket(len, j)], 1)] = base + j;
     base += c;
   }
 }
@@ -714,6 +799,8 @@ size_t decode_workspace_layout(int B, int Hkv, int R, int head_dim, int max_kv_l
   lay->row_chunks = off; off = up(off + (size_t)B * sizeof(int));
   lay->counters = off;   off = up(off + (size_t)B * Hkv * sizeof(int));
   lay->order = off;      off = up(off + max_entries * sizeof(int));
+  lay->n_order = off;    off = up(off + sizeof(int));
+  lay->width = off;      off = up(off + max_entries * sizeof(int));
   lay->work = off;       off = up(off + 2 * sizeof(int));
   lay->part_lse = off;   off = up(off + max_entries * Hkv * R * sizeof(float));
   lay->part_o = off;     off = up(off + max_entries * Hkv * R * head_dim * sizeof(float));
@@ -764,13 +851,15 @@ static cudaError_t launch_block(const CUtensorMap& km, const CUtensorMap& vm, co
   return cudaGetLastError();
 }
 
-cudaError_t launch_decode_plan(const int32_t* kv_len, int B, int Hkv, int head_dim, const WorkspaceLayout& lay,
-                               uint8_t* ws, cudaStream_t stream) {
+cudaError_t launch_decode_plan(const int32_t* kv_len, const int32_t* block_table, int max_pages, int page_size,
+                               int B, int Hkv, int q_rows, int head_dim, const WorkspaceLayout& lay, uint8_t* ws,
+                               cudaStream_t stream) {
   decode_plan_kernel<<<1, 1024, 0, stream>>>(
-      kv_len, B, Hkv, (int)decode_chunk_tokens(head_dim), (int)lay.max_entries,
-      reinterpret_cast<int2*>(ws + lay.entries), reinterpret_cast<int*>(ws + lay.n_entries),
+      kv_len, block_table, max_pages, page_size, B, Hkv, q_rows, (int)decode_chunk_tokens(head_dim),
+      (int)lay.max_entries, reinterpret_cast<int2*>(ws + lay.entries), reinterpret_cast<int*>(ws + lay.n_entries),
       reinterpret_cast<int*>(ws + lay.row_start), reinterpret_cast<int*>(ws + lay.row_chunks),
       reinterpret_cast<int*>(ws + lay.counters), reinterpret_cast<int*>(ws + lay.order),
+      reinterpret_cast<int*>(ws + lay.n_order), reinterpret_cast<int*>(ws + lay.width),
       reinterpret_cast<int*>(ws + lay.work));
   return cudaGetLastError();
 }
@@ -785,6 +874,8 @@ cudaError_t launch_decode_attention(const CUtensorMap& km, const CUtensorMap& vm
     p.row_chunks = reinterpret_cast<const int*>(ws + lay.row_chunks);
     p.counters = reinterpret_cast<int*>(ws + lay.counters);
     p.order = reinterpret_cast<const int*>(ws + lay.order);
+    p.n_order = reinterpret_cast<const int*>(ws + lay.n_order);
+    p.width = reinterpret_cast<const int*>(ws + lay.width);
     p.work = reinterpret_cast<int*>(ws + lay.work);
     p.part_lse = reinterpret_cast<float*>(ws + lay.part_lse);
     p.part_o = reinterpret_cast<float*>(ws + lay.part_o);

@@ -28,6 +28,8 @@ struct AttnParams {
   const int* row_chunks;
   int* counters;
   const int* order;            // entries, longest chunk first (the order CTAs take work in)
+  const int* n_order;          // entries in `order`
+  const int* width;            // per entry: member mask of its item (bit k: row + k; 1 alone; 0 covered)
   int* work;                   // [2]: next work item, CTAs finished (zeroed by the plan and the last CTA)
   float* part_lse;
   float* part_o;
@@ -35,14 +37,19 @@ struct AttnParams {
 
 struct WorkspaceLayout {
   size_t max_entries;
-  size_t entries, n_entries, row_start, row_chunks, counters, order, work, part_lse, part_o;
+  size_t entries, n_entries, row_start, row_chunks, counters, order, n_order, width, work, part_lse, part_o;
   size_t total;
 };
 
 size_t decode_chunk_tokens(int head_dim);
 size_t decode_workspace_layout(int B, int Hkv, int R, int head_dim, int max_kv_len, WorkspaceLayout* lay);
-cudaError_t launch_decode_plan(const int32_t* kv_len, int B, int Hkv, int head_dim, const WorkspaceLayout& lay,
-                               uint8_t* ws, cudaStream_t stream);
+// block_table == nullptr: every (row, chunk) is its own item. Otherwise the
+// plan also finds chunks whose pages consecutive rows share (see the plan
+// kernel) and gives each run one item; the caller's queries must see every
+// cached slot (q_pos[b, s] >= kv_len[b] - q_rows).
+cudaError_t launch_decode_plan(const int32_t* kv_len, const int32_t* block_table, int max_pages, int page_size,
+                               int B, int Hkv, int q_rows, int head_dim, const WorkspaceLayout& lay, uint8_t* ws,
+                               cudaStream_t stream);
 cudaError_t launch_decode_attention(const CUtensorMap& km, const CUtensorMap& vm, AttnParams p,
                                     const WorkspaceLayout& lay, uint8_t* ws, bool split, cudaStream_t stream);
 

@@ -66,6 +66,8 @@ struct FwdWork {
   int q0, row_end, h0, kvh, qt, t_lo, n, b;
 };
 
+constexpr int kPrefillRowBlock = 4;
+
 template <bool PAGED>
 __device__ __forceinline__ FwdWork fwd_work(int tile, const VarlenParams& p) {
   const int groups = p.Hq / p.heads_per_cta;
@@ -73,11 +75,16 @@ __device__ __forceinline__ FwdWork fwd_work(int tile, const VarlenParams& p) {
   w.h0 = (tile % groups) * p.heads_per_cta;
   w.kvh = w.h0 / p.G;
   if constexpr (PAGED) {
-    // Tiles of later query rows (more keys) first, all rows alike.
+    // Rows in blocks of kPrefillRowBlock; inside a block, later query tiles
+    // (more keys) first, then row, then head group. The query tiles that read
+    // the same row's K/V run close together, so the re-reads hit L2.
     const int n_qt = (p.S + 127) / 128;
     const int rest = tile / groups;
-    w.qt = n_qt - 1 - rest / p.B;
-    w.b = rest % p.B;
+    const int blk = rest / (kPrefillRowBlock * n_qt);
+    const int r_in = rest - blk * kPrefillRowBlock * n_qt;
+    const int nb = min(kPrefillRowBlock, p.B - blk * kPrefillRowBlock);  // rows in this block
+    w.qt = n_qt - 1 - r_in / nb;
+    w.b = blk * kPrefillRowBlock + r_in % nb;
     w.q0 = w.b * p.S + w.qt * 128;
     w.row_end = w.b * p.S + p.S;
     // q_pos grows along a row (left pads sit at 0), so the tile's last row
@@ -363,9 +370,11 @@ __global__ void __launch_bounds__(320, 1) varlen_fwd_kernel(const __grid_constan
           float ls[8];
 #pragma unroll
           for (int q = 0; q < 8; ++q) ls[q] = 0.f;
-          // Scale and shift, exponentials and row sums on packed fp32 pairs;
-          // one pair in four takes its 2^x on the FMA pipe (exp2_fma2), which
-          // unloads the SFU, the bound of this loop.
+          // Scale and shift, exponentials and row sums on packed fp32 pairs.
+          // In the training forward one pair in four takes its 2^x on the FMA
+          // pipe (exp2_fma2, relative error 1e-4), which unloads the SFU, the
+          // bound of this loop; the paged prefill, whose outputs feed the
+          // decode cache, keeps every exponential on the SFU.
 #pragma unroll
           for (int c = 0; c < 4; ++c) {
             uint32_t pk[16];
@@ -374,7 +383,7 @@ __global__ void __launch_bounds__(320, 1) varlen_fwd_kernel(const __grid_constan
               float x0, x1, p0, p1;
               ffma2(x0, x1, __uint_as_float(v[32 * c + e]), __uint_as_float(v[32 * c + e + 1]), p.scale_log2,
                     p.scale_log2, neg_mu, neg_mu);
-              if (((e >> 1) & 7) >= 6) {
+              if (!PAGED && ((e >> 1) & 7) >= 6) {
                 exp2_fma2(p0, p1, x0, x1);
               } else {
                 p0 = fast_exp2(x0);

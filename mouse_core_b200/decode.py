@@ -30,6 +30,7 @@ raises — there is no CPU or eager fallback.
 
 from __future__ import annotations
 
+import copy
 from typing import Any, cast
 
 import numpy as np
@@ -212,9 +213,52 @@ class PagedDecodeSession:
         self._turn = 0
         self._layers = [_LayerWeights(layer, self.n_heads, self.n_kv_heads, self.head_dim) for layer in hf.layers]
         self.inv_freq, self.attention_scaling = rope_frequencies(hf.rotary_emb, cfg, self.device)
-        # When a list, each attention launch appends its (start, end) CUDA
-        # events recorded on the launching stream (used for roofline timing).
+        # When a list, each attention launch appends (start, end, reps): CUDA
+        # events on the launching stream around `attn_reps` repeats of the
+        # launch (used for roofline timing; see _attend).
         self.attn_events: list | None = None
+        self.attn_reps = 4
+
+    def clone(self) -> "PagedDecodeSession":
+        """An independent copy of this session's cache (page pools, page
+        table, lengths, pending resets) that shares the model weights and
+        holds no captured graph: stepping either one leaves the other as it
+        was. Costs one device copy of the pools."""
+        c = copy.copy(self)
+        c.k_pool, c.v_pool = self.k_pool.clone(), self.v_pool.clone()
+        c.pages = copy.deepcopy(self.pages)
+        c._len = self._len.copy()
+        c._pending_reset = self._pending_reset.copy()
+        c._bt_dev = self._bt_dev.clone()
+        c._meta_dev = self._meta_dev.clone()
+        c._new_page_dev = self._new_page_dev.clone()
+        c._workspace = torch.empty_like(self._workspace)
+        c._graph = c._graph_key = c._step_graph = c._step_graph_key = c._step_args = None
+        c._graph_warm = c._step_graph_warm = False
+        c._step_ids = c._step_out = None
+        c._staging, c._staging_ev = [None, None], [None, None]
+        c.attn_events = None
+        return c
+
+    def _attend(self, q, li, scale, q_pos, kv_len, split):
+        """Attention of layer ``li`` over the page pool (K1 split/block decode
+        or the tcgen05 paged prefill). With ``attn_events`` set, the launch is
+        then repeated ``attn_reps`` times between two CUDA events on the
+        launching stream: each repeat is queued behind the previous launch,
+        so the events time the kernel and not a gap while the host submits it
+        (the launch reads the pools and writes a fresh output: repeats are
+        idempotent)."""
+        args = (q, self.k_pool[li], self.v_pool[li], self._bt_dev, q_pos, kv_len, scale, self.cap)
+        o = K.decode_attention(*args, workspace=self._workspace, plan_ready=split)
+        if self.attn_events is not None:
+            reps = max(1, int(self.attn_reps))
+            ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            ev0.record()
+            for _ in range(reps):
+                o = K.decode_attention(*args, workspace=self._workspace, plan_ready=split)
+            ev1.record()
+            self.attn_events.append((ev0, ev1, reps))
+        return o
 
     # ------------------------------------------------------------------ state
     @property
@@ -630,15 +674,7 @@ class PagedDecodeSession:
             q = K.kv_append(qkv, q_pos_flat, Hq, Hkv, hd, self.inv_freq, self.attention_scaling,
                             lw.q_norm_w, lw.k_norm_w, lw.qk_eps, slot=slot,
                             k_pool=self.k_pool[li], v_pool=self.v_pool[li])
-            if self.attn_events is not None:
-                ev0 = torch.cuda.Event(enable_timing=True)
-                ev0.record()
-            o = K.decode_attention(q.view(B, S, Hq, hd), self.k_pool[li], self.v_pool[li], self._bt_dev, q_pos,
-                                   kv_len, lw.scale, self.cap, workspace=self._workspace, plan_ready=split)
-            if self.attn_events is not None:
-                ev1 = torch.cuda.Event(enable_timing=True)
-                ev1.record()
-                self.attn_events.append((ev0, ev1))
+            o = self._attend(q.view(B, S, Hq, hd), li, lw.scale, q_pos, kv_len, split)
             a = lw.o_proj(o.view(B * S, Hq * hd))
             resid, hn2 = K.rmsnorm(a, lw.post_w, lw.post_eps, residual=resid)
             delta = lw.down(K.silu_mul(F.linear(hn2, lw.wgu, lw.bgu)))
@@ -660,7 +696,10 @@ class PagedDecodeSession:
                 self._workspace = torch.empty(need, dtype=torch.uint8, device=self.device)
                 self._graph = None
                 self._step_graph = None
-            K.decode_plan(kv_len, Hkv, R, hd, self.cap, self._workspace)
+            # One-token steps see every cached slot, so chunks that forked
+            # rows hold on the same pages can share one work item.
+            K.decode_plan(kv_len, Hkv, R, hd, self.cap, self._workspace,
+                          block_table=self._bt_dev if S == 1 else None, page_size=self.page_size)
         elif self._workspace.numel() < 256:  # prefill chunks keep a tile counter in it
             self._workspace = torch.empty(256, dtype=torch.uint8, device=self.device)
             self._graph = None
@@ -693,15 +732,7 @@ class PagedDecodeSession:
             q = K.kv_append(qkv, q_pos_flat, Hq, Hkv, hd, self.inv_freq, self.attention_scaling,
                             lw.q_norm_w, lw.k_norm_w, lw.qk_eps, slot=slot,
                             k_pool=self.k_pool[li], v_pool=self.v_pool[li])
-            if self.attn_events is not None:
-                ev0 = torch.cuda.Event(enable_timing=True)
-                ev0.record()
-            o = K.decode_attention(q.view(B, S, Hq, hd), self.k_pool[li], self.v_pool[li], self._bt_dev, q_pos,
-                                   kv_len, lw.scale, self.cap, workspace=self._workspace, plan_ready=split)
-            if self.attn_events is not None:
-                ev1 = torch.cuda.Event(enable_timing=True)
-                ev1.record()
-                self.attn_events.append((ev0, ev1))
+            o = self._attend(q.view(B, S, Hq, hd), li, lw.scale, q_pos, kv_len, split)
             a = _mm_f32(o.view(B * S, Hq * hd), lw.o_proj.weight, lw.o_proj.bias)
             resid, hn2 = K.rmsnorm_f32(resid, lw.post_w, lw.post_eps, delta=a, sum_out=resid)
             delta = _mm_f32(K.silu_mul_f32(_mm_f32(hn2, lw.wgu, lw.bgu)), lw.down.weight, lw.down.bias)

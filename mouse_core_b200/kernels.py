@@ -46,11 +46,21 @@ def decode_workspace_bytes(batch: int, kv_heads: int, q_rows: int, head_dim: int
 
 
 def decode_plan(kv_len: torch.Tensor, kv_heads: int, q_rows: int, head_dim: int, max_kv_len: int,
-                workspace: torch.Tensor) -> None:
+                workspace: torch.Tensor, block_table: torch.Tensor | None = None, page_size: int = 0) -> None:
+    """The split-mode work list for ``kv_len``. With ``block_table`` (and the
+    pool's ``page_size``) whole chunks that consecutive rows hold on the same
+    pages get one shared work item (``mb_decode_plan_shared``); the queries
+    must then see every cached slot (one-token decode)."""
     _need(kv_len, "kv_len", torch.int32)
     _need(workspace, "workspace", torch.uint8)
-    _lib.call("mb_decode_plan", _p(kv_len), kv_len.numel(), kv_heads, q_rows, head_dim, max_kv_len,
-              _p(workspace), workspace.numel(), _stream(kv_len))
+    if block_table is None:
+        _lib.call("mb_decode_plan", _p(kv_len), kv_len.numel(), kv_heads, q_rows, head_dim, max_kv_len,
+                  _p(workspace), workspace.numel(), _stream(kv_len))
+    else:
+        _need(block_table, "block_table", torch.int32)
+        _lib.call("mb_decode_plan_shared", _p(kv_len), _p(block_table), block_table.shape[1], int(page_size),
+                  kv_len.numel(), kv_heads, q_rows, head_dim, max_kv_len, _p(workspace), workspace.numel(),
+                  _stream(kv_len))
     _count()
 
 

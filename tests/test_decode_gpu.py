@@ -346,6 +346,88 @@ def test_session_graph_replay_matches_eager():
     assert graph_sess.lengths.tolist() == eager_sess.lengths.tolist()
 
 
+@pytest.mark.parametrize("hd,page,Hq,Hkv", [(128, 128, 16, 8), (64, 64, 32, 16), (128, 64, 16, 8)])
+def test_shared_chunk_plan_matches_plain_plan(hd, page, Hq, Hkv):
+    """One-token decode over rows that hold forked prefixes on the same pages:
+    the plan that gives a shared 2048-token chunk one work item for a block of
+    rows (mb_decode_plan_shared) yields bit-for-bit the outputs of the plan
+    that reads the chunk once per row (mb_decode_plan), and both match the
+    oracle. Rows: a root's branches filling an aligned block and spilling into
+    the next one, a second group that does not start a block, lone rows, a
+    branch forked inside a chunk, and rows shorter than one chunk."""
+    dev = _dev()
+    from mouse_core_b200 import kernels as K
+
+    G = Hq // Hkv
+    NG = 16 // G
+    rng = np.random.default_rng(hd + page)
+    gen = torch.Generator().manual_seed(hd + page)
+    chunk = 2048
+    ppc = chunk // page
+    # Per row: (root id or None, pages shared with that root). Root 0's
+    # branches fill the first aligned block and spill into the next one;
+    # root 1's branches sit after the second block's start, behind rows of
+    # root 0; in the third block two short rows come first and root 2's
+    # branches alternate with lone rows (a member mask with gaps); one of
+    # root 1's branches forks inside its second chunk.
+    layout = [(0, 3 * ppc)] * (NG + 2) + [(None, 0), (1, 2 * ppc), (1, 2 * ppc), (1, ppc + ppc // 2)]
+    layout += [(None, 0)] * (2 * NG - len(layout))
+    layout += [("short", 0), ("short", 0)] + [(2, 2 * ppc), (None, 0)] * 3 + [(2, 2 * ppc)]
+    B = len(layout)
+    lens = []
+    for root, ns in layout:
+        if root == "short":
+            lens.append(int(rng.integers(1, chunk)))
+        elif root is None:
+            lens.append(int(rng.integers(1, 3 * chunk)))
+        else:
+            lens.append(ns * page + int(rng.integers(1, 3 * page)))
+    npg = [math.ceil(L / page) for L in lens]
+    maxp = max(npg)
+    bt = np.full((B, maxp), -1, dtype=np.int32)
+    nxt = 0
+    root_pages = {}
+    for r, (root, ns) in enumerate(layout):
+        start = 0
+        if isinstance(root, int):
+            if root not in root_pages:
+                root_pages[root] = list(range(nxt, nxt + 3 * ppc))
+                nxt += 3 * ppc
+            bt[r, :ns] = root_pages[root][:ns]
+            start = ns
+        for i in range(start, npg[r]):
+            bt[r, i] = nxt
+            nxt += 1
+    P = nxt + 1
+    kp = torch.randn(P, Hkv, page, hd, generator=gen).bfloat16()
+    vp = torch.randn(P, Hkv, page, hd, generator=gen).bfloat16()
+    q = torch.randn(B, 1, Hq, hd, generator=gen).bfloat16()
+    kv_len = torch.tensor(lens, dtype=torch.int32)
+    q_pos = (kv_len - 1).view(B, 1).to(torch.int32)
+    d = lambda t: t.to(dev)  # noqa: E731
+    kp_d, vp_d, bt_d, q_d, kvl_d, qp_d = map(d, (kp, vp, torch.from_numpy(bt), q, kv_len, q_pos))
+    scale = hd ** -0.5
+    cap = max(lens)
+    ws = torch.empty(K.decode_workspace_bytes(B, Hkv, G, hd, cap), dtype=torch.uint8, device=dev)
+    K.decode_plan(kvl_d, Hkv, G, hd, cap, ws)
+    plain = K.decode_attention(q_d, kp_d, vp_d, bt_d, qp_d, kvl_d, scale, cap, workspace=ws, plan_ready=True)
+    K.decode_plan(kvl_d, Hkv, G, hd, cap, ws, block_table=bt_d, page_size=page)
+    shared = K.decode_attention(q_d, kp_d, vp_d, bt_d, qp_d, kvl_d, scale, cap, workspace=ws, plan_ready=True)
+    torch.cuda.synchronize()
+    from mouse_core_b200 import _lib
+
+    assert _lib.device_status() == 0
+    assert torch.equal(plain, shared)
+    # Oracle on every row (float64, same bf16 inputs).
+    k_rows = [torch.cat([kp[bt[b, i]].transpose(0, 1) for i in range(npg[b])])[:lens[b]].float().numpy()
+              for b in range(B)]
+    v_rows = [torch.cat([vp[bt[b, i]].transpose(0, 1) for i in range(npg[b])])[:lens[b]].float().numpy()
+              for b in range(B)]
+    ref = oatt.cached_decode_attention(q.float().numpy(), k_rows, v_rows, q_pos.numpy(), scale)
+    err = np.abs(shared.float().cpu().numpy() - ref).max()
+    assert err < ATOL, f"max abs err {err}"
+
+
 def test_fork_shares_prefix_pages_and_matches_independent_rows():
     """Branches forked at arbitrary points share the root's full pages, copy
     only the partial last page, and decode exactly like rows that computed
