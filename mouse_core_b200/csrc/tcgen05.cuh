@@ -327,6 +327,13 @@ __device__ __forceinline__ float fmax3(float a, float b, float c) {
   return d;
 }
 
+// Three-input f32 minimum.
+__device__ __forceinline__ float fmin3(float a, float b, float c) {
+  float d;
+  asm("min.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
 // Packed fp32 pairs (one instruction for two lanes of arithmetic on sm_100):
 // (d0, d1) = (a0, a1) * (b0, b1) + (c0, c1) and (d0, d1) = (a0, a1) + (b0, b1),
 // each rounded to nearest like fmaf / a + b.

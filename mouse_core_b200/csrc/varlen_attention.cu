@@ -67,6 +67,9 @@ struct FwdWork {
 };
 
 constexpr int kPrefillRowBlock = 4;
+// Score of a masked key (-2^90): its exponential is 0 (or, on the FMA-pipe
+// path, 2^-126), and a row max equal to it means no visible key.
+constexpr float kMaskedScore = -1.2379401e27f;
 
 template <bool PAGED>
 __device__ __forceinline__ FwdWork fwd_work(int tile, const VarlenParams& p) {
@@ -341,10 +344,18 @@ __global__ void __launch_bounds__(320, 1) varlen_fwd_kernel(const __grid_constan
           for (int c = 0; c < 4; ++c) tmem_ld32(t_s + 32 * c, *reinterpret_cast<uint32_t(*)[32]>(v + 32 * c));
           tmem_wait_ld();
           if (!full) {
+            // Keys outside [lo, hi] go to kMaskedScore by arithmetic alone:
+            // the minimum with two linear bounds, huge inside the row's key
+            // range and hugely negative past either end of it, then the
+            // maximum with kMaskedScore (a score no real one comes near).
+            const float big = 1.2676506e30f;  // 2^100
+            const float lo_e = row_ok ? (float)max(lo - kv0, 0) - 0.5f : 1000.f;
+            const float hi_e = row_ok ? (float)min(hi - kv0, C::BN - 1) + 0.5f : -1000.f;
+            const float hb = hi_e * big, lb = -lo_e * big;
 #pragma unroll
             for (int e = 0; e < 128; ++e) {
-              const int kv = kv0 + e;
-              if (!row_ok || kv < lo || kv > hi) v[e] = 0xff800000u;  // -inf
+              const float m = fmin3(__uint_as_float(v[e]), fmaf(-(float)e, big, hb), fmaf((float)e, big, lb));
+              v[e] = __float_as_uint(fmaxf(m, kMaskedScore));
             }
           }
           // Row max and (below) row sum as 8 independent chains: one long
@@ -357,7 +368,8 @@ __global__ void __launch_bounds__(320, 1) varlen_fwd_kernel(const __grid_constan
           for (int e = 16; e < 128; e += 16)
 #pragma unroll
             for (int q = 0; q < 8; ++q) mp[q] = fmax3(mp[q], __uint_as_float(v[e + q]), __uint_as_float(v[e + 8 + q]));
-          const float mx = fmax3(fmax3(mp[0], mp[1], mp[2]), fmax3(mp[3], mp[4], mp[5]), fmaxf(mp[6], mp[7]));
+          float mx = fmax3(fmax3(mp[0], mp[1], mp[2]), fmax3(mp[3], mp[4], mp[5]), fmaxf(mp[6], mp[7]));
+          if (mx <= kMaskedScore) mx = -INFINITY;  // no key of this tile is visible to the row
           // The scale is positive, so the max of raw scores gives the max of scaled ones.
           const float m_tile = mx * p.scale_log2;
           const float m_new = fmaxf(m_used, m_tile);
