@@ -1288,13 +1288,30 @@ def _oracle_decoder(seed):
     return odec.DecoderOracle(sd, cfg)
 
 
+def _usable_cores():
+    """Cores this process may run on: its CPU affinity, capped by a cgroup
+    CPU quota when one is set (a container's share of a larger host)."""
+    try:
+        n = len(os.sched_getaffinity(0))
+    except (AttributeError, OSError):
+        n = os.cpu_count() or 1
+    try:
+        with open("/sys/fs/cgroup/cpu.max") as f:
+            quota, period = f.read().split()[:2]
+        if quota != "max" and int(period) > 0:
+            n = min(n, max(1, -(-int(quota) // int(period))))
+    except (OSError, ValueError):
+        pass
+    return max(1, n)
+
+
 def _host_threads():
-    """Give numpy's BLAS and torch every host core (torchrun sets
+    """Give numpy's BLAS and torch every usable host core (torchrun sets
     OMP_NUM_THREADS=1 for its ranks) and return the thread count in use."""
     import torch
     from threadpoolctl import threadpool_info, threadpool_limits
 
-    n = os.cpu_count() or 1
+    n = _usable_cores()
     threadpool_limits(limits=n)
     torch.set_num_threads(n)
     blas = [i.get("num_threads", 1) for i in threadpool_info() if i.get("user_api") == "blas"]
