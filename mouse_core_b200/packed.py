@@ -205,6 +205,40 @@ class _SiluMul(torch.autograd.Function):
         return K.silu_mul_bwd(gate_up, dh.contiguous())
 
 
+class _CatLinear(torch.autograd.Function):
+    """``x @ cat(weights)^T`` with the concatenated weight built once per
+    weight version (the rows of one step share it) instead of on every
+    forward; the backward splits dW back onto the separate weights."""
+
+    @staticmethod
+    def forward(ctx, x, w_cat, *weights):
+        ctx.save_for_backward(x, w_cat)
+        ctx.rows = [w.shape[0] for w in weights]
+        return torch.nn.functional.linear(x, w_cat)
+
+    @staticmethod
+    def backward(ctx, dy):
+        x, w_cat = ctx.saved_tensors
+        dy2 = dy.reshape(-1, dy.shape[-1])
+        dx = (dy2 @ w_cat).view(x.shape) if ctx.needs_input_grad[0] else None
+        dw = dy2.t() @ x.reshape(-1, x.shape[-1])
+        return (dx, None, *torch.split(dw, ctx.rows, dim=0))
+
+
+def _cat_linear(owner, key, x, weights):
+    """``linear(x, cat(weights))`` through _CatLinear, the concatenation
+    cached on ``owner`` under ``key`` and rebuilt when a weight's storage or
+    version changes (an optimizer step updates them in place)."""
+    cache = owner.__dict__.setdefault("_mb_cat_cache", {})
+    tag = tuple((w.data_ptr(), w._version, w.dtype, tuple(w.shape)) for w in weights)
+    hit = cache.get(key)
+    if hit is None or hit[0] != tag:
+        with torch.no_grad():
+            hit = (tag, torch.cat([w.detach() for w in weights], dim=0))
+        cache[key] = hit
+    return _CatLinear.apply(x, hit[1], *weights)
+
+
 def _k4_norm(module, x) -> bool:
     D = x.shape[-1]
     return hasattr(module, "variance_epsilon") and D % 256 == 0 and D <= 2048
@@ -285,8 +319,7 @@ def flex_packed_forward(*, model: torch.nn.Module, embeds: torch.Tensor, sequenc
         attn = layer.self_attn
         q_norm = getattr(attn, "q_norm", None)
         if _fused_attention_inputs(attn):
-            w_qkv = torch.cat((attn.q_proj.weight, attn.k_proj.weight, attn.v_proj.weight), dim=0)
-            qkv = torch.nn.functional.linear(hn, w_qkv)
+            qkv = _cat_linear(attn, "qkv", hn, (attn.q_proj.weight, attn.k_proj.weight, attn.v_proj.weight))
             if q_norm is not None:
                 q, k, v = _QKVHeads.apply(qkv, q_norm.weight, attn.k_norm.weight, cos, sin,
                                           float(q_norm.variance_epsilon), float(attn.k_norm.variance_epsilon),
@@ -307,7 +340,7 @@ def flex_packed_forward(*, model: torch.nn.Module, embeds: torch.Tensor, sequenc
         mlp = layer.mlp
         h, hn = _add_norm(layer.post_attention_layernorm, residual, attn.o_proj(o.reshape(L, n_heads * hd)))
         if _fused_mlp(mlp, cfg):
-            gate_up = torch.nn.functional.linear(hn, torch.cat((mlp.gate_proj.weight, mlp.up_proj.weight), dim=0))
+            gate_up = _cat_linear(mlp, "gate_up", hn, (mlp.gate_proj.weight, mlp.up_proj.weight))
             pending = mlp.down_proj(_SiluMul.apply(gate_up))
         else:
             pending = mlp(hn)
