@@ -495,7 +495,10 @@ def run_ours(args):
         out["prefill_attention"] = prefill_obj
     if rank == 0 and packed_obj is not None:
         out["packed_attention"] = packed_obj
-    if rank == 0 and not args.no_cpu_baseline:
+    # The CPU baseline is timed at N = 1 only: under torchrun the other ranks'
+    # processes share the host, and the per-N comparison is the driver's
+    # reference arm (rank 0 alone, the other ranks exit).
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
         out["cpu_baseline"] = cpu_baseline(args.cpu_seconds)
     if world > 1:
         dist.barrier()

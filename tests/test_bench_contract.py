@@ -31,15 +31,19 @@ def test_reference_arm_prints_one_contract_line():
 
 
 def test_reference_arm_under_torchrun_uses_every_core():
-    """torchrun sets OMP_NUM_THREADS=1 for its ranks; the CPU arm lifts it
-    and reports the threads it ran with."""
+    """torchrun sets OMP_NUM_THREADS=1 for its ranks; the CPU arm lifts it to
+    every usable core (affinity, capped by a CPU quota) and reports the
+    threads it ran with."""
     env = dict(os.environ, OMP_NUM_THREADS="1")
     proc = subprocess.run([sys.executable, os.path.join(ROOT, "bench.py"), "--impl", "reference", "--steps", "1",
                            "--warmup", "3", "--cpu-seconds", "1"], capture_output=True, text=True, timeout=600,
                           cwd=ROOT, env=env)
     assert proc.returncode == 0, proc.stderr[-2000:]
     d = json.loads([ln for ln in proc.stdout.splitlines() if ln.startswith("{")][0])
-    assert d["cpu_baseline"]["cores"] == (os.cpu_count() or 1)
+    sys.path.insert(0, ROOT)
+    import bench
+
+    assert d["cpu_baseline"]["cores"] == bench._usable_cores()
 
 
 def test_unique_kv_tokens_counts_shared_pages_once():
