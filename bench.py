@@ -701,7 +701,8 @@ def large_batch_measure(dev, world, rank, local, envs, K_steps, W):
                        "ms_per_step": round(e2e_max / K_steps, 4)},
                "roofline": {"kernel": "split_decode_kernel (K1), hd 64", "bound": "hbm", "achieved": round(achieved, 1),
                             "peak": peak, "peak_source": "measured" if "hbm_gbs" in peaks else "fallback",
-                            "unit": "GB/s", "frac": round(achieved / peak, 4), "traffic": None,
+                            "unit": "GB/s", "frac": round(achieved / peak, 4),
+                            "traffic": roofline_traffic_per_launch(attn_bytes, "large_batch_split_decode_64envs.json"),
                             "algorithmic_bytes_per_launch": int(attn_bytes), "avg_launch_ms": round(attn_avg_ms, 5),
                             "launches_timed": len(attn_ms)},
                "kv_pool_gb": round(pages * LB["layers"] * 2 * Hkv * P * hd * 2 / 1e9, 1),
