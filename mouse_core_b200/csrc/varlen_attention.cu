@@ -16,11 +16,16 @@
 // through a two-slot ring, and barrier phases follow a running key-tile count
 // across tiles. Q is released after a tile's last Q K^T MMA, so the next
 // tile's Q loads during the last softmax, P V and epilogue; O is released
-// once the epilogue has read it. Warp roles (320 threads):
+// once the epilogue has read it. Warp roles (512 threads, four warpgroups):
 //   warp 0      TMA producer: Q once per tile, K/V tiles through a 2-3 stage ring
 //   warp 1      TMEM allocator; the whole warp issues every tcgen05.mma
-//   warps 2-5   softmax of head 0 (thread = query row = TMEM lane)
-//   warps 6-9   softmax of head 1
+//   warps 2-3   idle (they complete the control warpgroup)
+//   warps 4-7   softmax of head 0 (thread = query row = TMEM lane)
+//   warps 8-11  softmax of head 1
+//   warps 12-15 epilogue: a tile's O out of TMEM, normalised and stored,
+//               while the softmax warps already work on the next tile
+// The block is launched with 128 registers a thread; setmaxnreg gives the
+// softmax warpgroups 184 and the control and epilogue ones 56 and 80.
 // Tensor memory (512 columns): S_h = Q_h K^T at columns 128h, O_h at 256 + HD h.
 // Softmax reads S, writes P (bf16 pairs) back over the first 64 columns of
 // S_h, and the MMA O_h += P V takes P straight from TMEM. The two heads
@@ -33,7 +38,18 @@
 #include "kernels.h"
 #include "tcgen05.cuh"
 
+#include <atomic>
+
 namespace mb {
+
+// Block: 16 warps in four warpgroups (see the role table above). The block is
+// launched with 128 registers a thread; setmaxnreg then moves them from the
+// control and epilogue warpgroups to the two softmax warpgroups.
+constexpr int kFwdThreads = 512;
+constexpr int kFwdLaunchRegs = 128;  // 65536 / 512
+constexpr int kFwdCtrlRegs = 56, kFwdEpiRegs = 80, kFwdSoftmaxRegs = 184;
+static_assert(128 * kFwdCtrlRegs + 128 * kFwdEpiRegs + 256 * kFwdSoftmaxRegs <= kFwdThreads * kFwdLaunchRegs,
+              "the register split must fit the launch allocation");
 
 template <int HD>
 struct FwdTile {
@@ -44,7 +60,7 @@ struct FwdTile {
   static constexpr int KVTILE = NCB * BOX;            // one K (or V) tile
   static constexpr int STAGES = HD == 128 ? 2 : 3;
   static constexpr int RING = 2 * STAGES * KVTILE;
-  static constexpr int SMEM = 1024 + 2 * QTILE + RING + 256;
+  static constexpr int SMEM = 1024 + 2 * QTILE + RING + 4352;
   static constexpr uint32_t TMEM_COLS = 512;
 };
 
@@ -54,9 +70,12 @@ struct FwdBarriers {
   uint64_t k_full[3], v_full[3], kv_empty[3];
   uint64_t s_full[2], p_full[2];
   uint64_t o_full, o_empty;
+  uint64_t stats_full[2];  // a tile's row max / row sum handed from the softmax to the epilogue warps
   uint32_t tmem_base;
   int tile[2];
+  float stats[2][2][2][128];  // [tile parity][head][max, sum][row]
 };
+static_assert(sizeof(FwdBarriers) <= 4352, "barrier / stats block outgrew its shared memory share");
 
 // One work tile: 128 query rows starting at flat row q0 (rows up to row_end
 // belong to it), q-heads h0 .. h0 + heads_per_cta - 1 over kv-head kvh, and
@@ -135,7 +154,7 @@ __device__ __forceinline__ void load_paged_kv(uint8_t* dst, const CUtensorMap* m
 }
 
 template <int HD, bool PAGED>
-__global__ void __launch_bounds__(320, 1) varlen_fwd_kernel(const __grid_constant__ CUtensorMap qmap,
+__global__ void __launch_bounds__(kFwdThreads, 1) varlen_fwd_kernel(const __grid_constant__ CUtensorMap qmap,
                                                            const __grid_constant__ CUtensorMap kmap,
                                                            const __grid_constant__ CUtensorMap vmap,
                                                            const VarlenParams p) {
@@ -155,7 +174,8 @@ __global__ void __launch_bounds__(320, 1) varlen_fwd_kernel(const __grid_constan
   if (threadIdx.x == 0) {
     for (int s = 0; s < 2; ++s) {
       mbar_init(&bars->tile_full[s], 1);
-      mbar_init(&bars->tile_empty[s], 9);  // MMA warp + 8 softmax warps
+      mbar_init(&bars->tile_empty[s], 13);  // MMA warp + 8 softmax warps + 4 epilogue warps
+      mbar_init(&bars->stats_full[s], 8);
     }
     mbar_init(&bars->q_full, 1);
     mbar_init(&bars->q_empty, 1);
@@ -169,7 +189,7 @@ __global__ void __launch_bounds__(320, 1) varlen_fwd_kernel(const __grid_constan
       mbar_init(&bars->p_full[h], 4);
     }
     mbar_init(&bars->o_full, 1);
-    mbar_init(&bars->o_empty, 8);
+    mbar_init(&bars->o_empty, 4);
     fence_barrier_init();
   }
   if (warp == 1) tmem_alloc(&bars->tmem_base, C::TMEM_COLS);
@@ -187,6 +207,8 @@ __global__ void __launch_bounds__(320, 1) varlen_fwd_kernel(const __grid_constan
     return tile;
   };
 
+  if (warp < 4) {
+  regs_dec<kFwdCtrlRegs>();
   if (warp == 0) {
     // ------------------------------------------------------------ producer
     bool ok = true;
@@ -303,9 +325,11 @@ __global__ void __launch_bounds__(320, 1) varlen_fwd_kernel(const __grid_constan
       umma_commit_warp(&bars->o_full);
       J += n;
     }
-  } else {
+  }
+  } else if (warp < 12) {
+    regs_inc<kFwdSoftmaxRegs>();
     // ------------------------------------------------------------ softmax
-    const int hh = (warp - 2) >> 2;
+    const int hh = (warp - 4) >> 2;
     const int sub = warp & 3;  // TMEM lane quarter this warp may access
     const int r = sub * 32 + lane;
     const uint32_t lane_bits = (uint32_t)(sub * 32) << 16;
@@ -427,25 +451,47 @@ __global__ void __launch_bounds__(320, 1) varlen_fwd_kernel(const __grid_constan
         __syncwarp();
         if (lane == 0) mbar_arrive(&bars->p_full[hh]);
       }
-      // Epilogue: O out of TMEM in 32-column chunks, normalised and stored
-      // with lse; the accumulator is released after its last chunk. A warp
-      // without a head (odd GQA group) only keeps the o_empty count.
-      if (!(ok = ok && mbar_wait_warp(&bars->o_full, k & 1, kDevTimeoutFull))) break;
+      // Hand the rows' max and sum to the epilogue warps and go straight on
+      // to the next tile: its first S is usually waiting already. (Every
+      // softmax warp arrives, a warp without a head included.)
+      bars->stats[k & 1][hh][0][r] = m_used;
+      bars->stats[k & 1][hh][1][r] = l;
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bars->stats_full[k & 1]);
+      J += w.n;
+    }
+  } else {
+    regs_dec<kFwdEpiRegs>();
+    // ------------------------------------------------------------ epilogue
+    // O of both heads out of TMEM in 32-column chunks, normalised with the
+    // softmax warps' row sums and stored with lse; the accumulator is
+    // released after the last chunk, so the next tile's first P V may
+    // overwrite it. Runs under the next tile's first softmax phase.
+    const int sub = warp & 3;  // TMEM lane quarter this warp may access
+    const int r = sub * 32 + lane;
+    const uint32_t lane_bits = (uint32_t)(sub * 32) << 16;
+    bool ok = true;
+    for (int k = 0; ok; ++k) {
+      const int tile = take_tile(k, ok);
+      if (!ok || tile < 0) break;
+      const FwdWork w = fwd_work<PAGED>(tile, p);
+      const int q_tok = w.q0 + r;
+      const bool row_ok = q_tok < w.row_end;
+      if (!(ok = mbar_wait_warp(&bars->o_full, k & 1, kDevTimeoutFull))) break;
+      if (!(ok = mbar_wait_warp(&bars->stats_full[k & 1], (k >> 1) & 1, kDevTimeoutFull))) break;
       tc_fence_after();
-      if (active) {
+      for (int hh = 0; hh < hpc; ++hh) {
         const int h = w.h0 + hh;
+        const float m_used = bars->stats[k & 1][hh][0][r];
+        const float l = bars->stats[k & 1][hh][1][r];
         const float inv = (l > 0.f) ? 1.f / l : 0.f;
+        const uint32_t t_o = tbase + 256 + HD * hh + lane_bits;
         uint4* d4 = reinterpret_cast<uint4*>(p.out + ((size_t)q_tok * p.Hq + h) * HD);
 #pragma unroll
         for (int c = 0; c < HD / 32; ++c) {
           uint32_t o[32];
           tmem_ld32(t_o + 32 * c, o);
           tmem_wait_ld();
-          if (c == HD / 32 - 1) {
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&bars->o_empty);
-          }
           if (row_ok) {
 #pragma unroll
             for (int q4 = 0; q4 < 4; ++q4) {
@@ -459,12 +505,10 @@ __global__ void __launch_bounds__(320, 1) varlen_fwd_kernel(const __grid_constan
           }
         }
         if (row_ok && !PAGED) p.lse[(size_t)h * p.L + q_tok] = (l > 0.f) ? m_used + log2f(l) : -INFINITY;
-      } else {
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&bars->o_empty);
       }
-      J += w.n;
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bars->o_empty);
     }
   }
   tc_fence_before();
@@ -474,6 +518,22 @@ __global__ void __launch_bounds__(320, 1) varlen_fwd_kernel(const __grid_constan
     __syncwarp();
     tmem_dealloc(tbase, C::TMEM_COLS);
   }
+}
+
+// Prepare one instantiation for launch: its dynamic shared memory, and a
+// check that the kernel is launched with the registers the setmaxnreg split
+// draws on (an increase beyond the launch allocation would never complete).
+template <int HD, bool PAGED>
+cudaError_t fwd_prepare(int smem) {
+  static std::atomic<int> ready{0};
+  if (ready.load(std::memory_order_acquire)) return cudaSuccess;
+  cudaFuncAttributes a{};
+  cudaError_t e = cudaFuncGetAttributes(&a, varlen_fwd_kernel<HD, PAGED>);
+  if (e != cudaSuccess) return e;
+  if (a.numRegs < kFwdLaunchRegs) return cudaErrorInvalidConfiguration;
+  e = cudaFuncSetAttribute(varlen_fwd_kernel<HD, PAGED>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e == cudaSuccess) ready.store(1, std::memory_order_release);
+  return e;
 }
 
 cudaError_t launch_varlen_fwd(const CUtensorMap& qm, const CUtensorMap& km, const CUtensorMap& vm,
@@ -486,14 +546,14 @@ cudaError_t launch_varlen_fwd(const CUtensorMap& qm, const CUtensorMap& km, cons
   if (e != cudaSuccess) return e;
   if (p.head_dim == 128) {
     const int smem = FwdTile<128>::SMEM;
-    e = cudaFuncSetAttribute(varlen_fwd_kernel<128, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    e = fwd_prepare<128, false>(smem);
     if (e != cudaSuccess) return e;
-    varlen_fwd_kernel<128, false><<<grid, 320, smem, stream>>>(qm, km, vm, p);
+    varlen_fwd_kernel<128, false><<<grid, kFwdThreads, smem, stream>>>(qm, km, vm, p);
   } else {
     const int smem = FwdTile<64>::SMEM;
-    e = cudaFuncSetAttribute(varlen_fwd_kernel<64, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    e = fwd_prepare<64, false>(smem);
     if (e != cudaSuccess) return e;
-    varlen_fwd_kernel<64, false><<<grid, 320, smem, stream>>>(qm, km, vm, p);
+    varlen_fwd_kernel<64, false><<<grid, kFwdThreads, smem, stream>>>(qm, km, vm, p);
   }
   return cudaGetLastError();
 }
@@ -516,14 +576,14 @@ cudaError_t launch_paged_prefill(const CUtensorMap& qm, const CUtensorMap& km, c
   }
   if (p.head_dim == 128) {
     const int smem = FwdTile<128>::SMEM;
-    e = cudaFuncSetAttribute(varlen_fwd_kernel<128, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    e = fwd_prepare<128, true>(smem);
     if (e != cudaSuccess) return e;
-    varlen_fwd_kernel<128, true><<<(unsigned)n_work, 320, smem, stream>>>(qm, km, vm, p);
+    varlen_fwd_kernel<128, true><<<(unsigned)n_work, kFwdThreads, smem, stream>>>(qm, km, vm, p);
   } else {
     const int smem = FwdTile<64>::SMEM;
-    e = cudaFuncSetAttribute(varlen_fwd_kernel<64, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    e = fwd_prepare<64, true>(smem);
     if (e != cudaSuccess) return e;
-    varlen_fwd_kernel<64, true><<<(unsigned)n_work, 320, smem, stream>>>(qm, km, vm, p);
+    varlen_fwd_kernel<64, true><<<(unsigned)n_work, kFwdThreads, smem, stream>>>(qm, km, vm, p);
   }
   return cudaGetLastError();
 }
