@@ -102,6 +102,23 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int co
   }
 }
 
+// As mbar_wait, for a wait off the critical path: the warp sleeps between
+// polls, so it takes no issue slots or barrier-unit cycles from the warps
+// doing the work it waits for.
+__device__ __forceinline__ bool mbar_wait_sleepy(uint64_t* bar, uint32_t parity, int code) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const long long limit = wait_limit();
+  const long long t0 = clock64();
+  while (true) {
+    if (clock64() - t0 > limit) {
+      report(code);
+      return false;
+    }
+    __nanosleep(256);
+    if (mbar_try_wait(bar, parity)) return true;
+  }
+}
+
 // As mbar_wait, but also gives up (without a new code) once `*abort` is set,
 // and sets `*abort` itself when it times out, so the other warps of the CTA
 // stop waiting too.

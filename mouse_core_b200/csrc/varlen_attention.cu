@@ -24,8 +24,8 @@
 //   warps 8-11  softmax of head 1
 //   warps 12-15 epilogue: a tile's O out of TMEM, normalised and stored,
 //               while the softmax warps already work on the next tile
-// The block is launched with 128 registers a thread; setmaxnreg gives the
-// softmax warpgroups 184 and the control and epilogue ones 56 and 80.
+// The block is launched with 128 registers a thread; setmaxnreg moves them
+// from the control and epilogue warpgroups to the softmax ones (FwdRegs).
 // Tensor memory (512 columns): S_h = Q_h K^T at columns 128h, O_h at 256 + HD h.
 // Softmax reads S, writes P (bf16 pairs) back over the first 64 columns of
 // S_h, and the MMA O_h += P V takes P straight from TMEM. The two heads
@@ -47,9 +47,16 @@ namespace mb {
 // control and epilogue warpgroups to the two softmax warpgroups.
 constexpr int kFwdThreads = 512;
 constexpr int kFwdLaunchRegs = 128;  // 65536 / 512
-constexpr int kFwdCtrlRegs = 56, kFwdEpiRegs = 80, kFwdSoftmaxRegs = 184;
-static_assert(128 * kFwdCtrlRegs + 128 * kFwdEpiRegs + 256 * kFwdSoftmaxRegs <= kFwdThreads * kFwdLaunchRegs,
-              "the register split must fit the launch allocation");
+// Registers per thread of the control, epilogue and softmax warpgroups. The
+// split was measured per instantiation: the paged prefill runs best with 184
+// for the softmax, the training forward with 168 (its FMA-pipe exponentials
+// schedule worse with more).
+template <bool PAGED>
+struct FwdRegs {
+  static constexpr int ctrl = 56, epi = PAGED ? 80 : 112, softmax = PAGED ? 184 : 168;
+  static_assert(128 * ctrl + 128 * epi + 256 * softmax <= kFwdThreads * kFwdLaunchRegs,
+                "the register split must fit the launch allocation");
+};
 
 template <int HD>
 struct FwdTile {
@@ -208,7 +215,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1) varlen_fwd_kernel(const __grid
   };
 
   if (warp < 4) {
-  regs_dec<kFwdCtrlRegs>();
+  regs_dec<FwdRegs<PAGED>::ctrl>();
   if (warp == 0) {
     // ------------------------------------------------------------ producer
     bool ok = true;
@@ -327,7 +334,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1) varlen_fwd_kernel(const __grid
     }
   }
   } else if (warp < 12) {
-    regs_inc<kFwdSoftmaxRegs>();
+    regs_inc<FwdRegs<PAGED>::softmax>();
     // ------------------------------------------------------------ softmax
     const int hh = (warp - 4) >> 2;
     const int sub = warp & 3;  // TMEM lane quarter this warp may access
@@ -461,7 +468,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1) varlen_fwd_kernel(const __grid
       J += w.n;
     }
   } else {
-    regs_dec<kFwdEpiRegs>();
+    regs_dec<FwdRegs<PAGED>::epi>();
     // ------------------------------------------------------------ epilogue
     // O of both heads out of TMEM in 32-column chunks, normalised with the
     // softmax warps' row sums and stored with lse; the accumulator is
@@ -470,15 +477,24 @@ __global__ void __launch_bounds__(kFwdThreads, 1) varlen_fwd_kernel(const __grid
     const int sub = warp & 3;  // TMEM lane quarter this warp may access
     const int r = sub * 32 + lane;
     const uint32_t lane_bits = (uint32_t)(sub * 32) << 16;
+    // Its waits sleep between polls: a tile's O is ready only at the tile's
+    // end, and polling all along would take issue slots and barrier-unit
+    // cycles from the softmax warps on the same sub-partitions.
+    auto wait = [&](uint64_t* bar, uint32_t parity) {
+      return __all_sync(0xffffffffu, mbar_wait_sleepy(bar, parity, kDevTimeoutFull));
+    };
     bool ok = true;
     for (int k = 0; ok; ++k) {
-      const int tile = take_tile(k, ok);
+      ok = wait(&bars->tile_full[k & 1], (k >> 1) & 1);
+      const int tile = ok ? *reinterpret_cast<volatile int*>(&bars->tile[k & 1]) : -1;
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bars->tile_empty[k & 1]);
       if (!ok || tile < 0) break;
       const FwdWork w = fwd_work<PAGED>(tile, p);
       const int q_tok = w.q0 + r;
       const bool row_ok = q_tok < w.row_end;
-      if (!(ok = mbar_wait_warp(&bars->o_full, k & 1, kDevTimeoutFull))) break;
-      if (!(ok = mbar_wait_warp(&bars->stats_full[k & 1], (k >> 1) & 1, kDevTimeoutFull))) break;
+      if (!(ok = wait(&bars->o_full, k & 1))) break;
+      if (!(ok = wait(&bars->stats_full[k & 1], (k >> 1) & 1))) break;
       tc_fence_after();
       for (int hh = 0; hh < hpc; ++hh) {
         const int h = w.h0 + hh;
