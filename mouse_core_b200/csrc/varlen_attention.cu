@@ -45,16 +45,20 @@ namespace mb {
 // Block: 16 warps in four warpgroups (see the role table above). The block is
 // launched with 128 registers a thread; setmaxnreg then moves them from the
 // control and epilogue warpgroups to the two softmax warpgroups.
-constexpr int kFwdThreads = 512;
-constexpr int kFwdLaunchRegs = 128;  // 65536 / 512
-// Registers per thread of the control, epilogue and softmax warpgroups. The
-// split was measured per instantiation: the paged prefill runs best with 184
-// for the softmax, the training forward with 168 (its FMA-pipe exponentials
-// schedule worse with more).
+// The paged prefill's work tiles are short (1-8 key tiles for a rebuild
+// window), so a dedicated epilogue warpgroup drains O there while the softmax
+// warps start the next tile (512 threads, setmaxnreg split below). The
+// training forward's tiles are longer and ran ~4% slower that way (the extra
+// warps share the sub-partitions), so it keeps the softmax warps draining O
+// themselves (320 threads, 168 registers each).
 template <bool PAGED>
-struct FwdRegs {
-  static constexpr int ctrl = 56, epi = PAGED ? 80 : 112, softmax = PAGED ? 184 : 168;
-  static_assert(128 * ctrl + 128 * epi + 256 * softmax <= kFwdThreads * kFwdLaunchRegs,
+constexpr int fwd_threads() {
+  return PAGED ? 512 : 320;
+}
+constexpr int kFwdLaunchRegs = 128;  // 65536 / 512: the paged prefill's launch allocation
+struct FwdRegs {  // paged prefill: control, epilogue and softmax warpgroups
+  static constexpr int ctrl = 56, epi = 80, softmax = 184;
+  static_assert(128 * ctrl + 128 * epi + 256 * softmax <= 512 * kFwdLaunchRegs,
                 "the register split must fit the launch allocation");
 };
 
@@ -161,7 +165,7 @@ __device__ __forceinline__ void load_paged_kv(uint8_t* dst, const CUtensorMap* m
 }
 
 template <int HD, bool PAGED>
-__global__ void __launch_bounds__(kFwdThreads, 1) varlen_fwd_kernel(const __grid_constant__ CUtensorMap qmap,
+__global__ void __launch_bounds__(fwd_threads<PAGED>(), 1) varlen_fwd_kernel(const __grid_constant__ CUtensorMap qmap,
                                                            const __grid_constant__ CUtensorMap kmap,
                                                            const __grid_constant__ CUtensorMap vmap,
                                                            const VarlenParams p) {
@@ -181,7 +185,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1) varlen_fwd_kernel(const __grid
   if (threadIdx.x == 0) {
     for (int s = 0; s < 2; ++s) {
       mbar_init(&bars->tile_full[s], 1);
-      mbar_init(&bars->tile_empty[s], 13);  // MMA warp + 8 softmax warps + 4 epilogue warps
+      mbar_init(&bars->tile_empty[s], PAGED ? 13 : 9);  // MMA warp + 8 softmax warps (+ 4 epilogue warps)
       mbar_init(&bars->stats_full[s], 8);
     }
     mbar_init(&bars->q_full, 1);
@@ -196,7 +200,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1) varlen_fwd_kernel(const __grid
       mbar_init(&bars->p_full[h], 4);
     }
     mbar_init(&bars->o_full, 1);
-    mbar_init(&bars->o_empty, 4);
+    mbar_init(&bars->o_empty, PAGED ? 4 : 8);  // whoever drains O
     fence_barrier_init();
   }
   if (warp == 1) tmem_alloc(&bars->tmem_base, C::TMEM_COLS);
@@ -214,8 +218,9 @@ __global__ void __launch_bounds__(kFwdThreads, 1) varlen_fwd_kernel(const __grid
     return tile;
   };
 
-  if (warp < 4) {
-  regs_dec<FwdRegs<PAGED>::ctrl>();
+  constexpr int kSoftmaxWarp0 = PAGED ? 4 : 2;
+  if (warp < kSoftmaxWarp0) {
+  if constexpr (PAGED) regs_dec<FwdRegs::ctrl>();
   if (warp == 0) {
     // ------------------------------------------------------------ producer
     bool ok = true;
@@ -333,10 +338,10 @@ __global__ void __launch_bounds__(kFwdThreads, 1) varlen_fwd_kernel(const __grid
       J += n;
     }
   }
-  } else if (warp < 12) {
-    regs_inc<FwdRegs<PAGED>::softmax>();
+  } else if (warp < kSoftmaxWarp0 + 8) {
+    if constexpr (PAGED) regs_inc<FwdRegs::softmax>();
     // ------------------------------------------------------------ softmax
-    const int hh = (warp - 4) >> 2;
+    const int hh = (warp - kSoftmaxWarp0) >> 2;
     const int sub = warp & 3;  // TMEM lane quarter this warp may access
     const int r = sub * 32 + lane;
     const uint32_t lane_bits = (uint32_t)(sub * 32) << 16;
@@ -458,17 +463,58 @@ __global__ void __launch_bounds__(kFwdThreads, 1) varlen_fwd_kernel(const __grid
         __syncwarp();
         if (lane == 0) mbar_arrive(&bars->p_full[hh]);
       }
-      // Hand the rows' max and sum to the epilogue warps and go straight on
-      // to the next tile: its first S is usually waiting already. (Every
-      // softmax warp arrives, a warp without a head included.)
-      bars->stats[k & 1][hh][0][r] = m_used;
-      bars->stats[k & 1][hh][1][r] = l;
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&bars->stats_full[k & 1]);
+      if constexpr (PAGED) {
+        // Hand the rows' max and sum to the epilogue warps and go straight
+        // on to the next tile: its first S is usually waiting already.
+        // (Every softmax warp arrives, a warp without a head included.)
+        bars->stats[k & 1][hh][0][r] = m_used;
+        bars->stats[k & 1][hh][1][r] = l;
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bars->stats_full[k & 1]);
+      } else {
+        // Epilogue: O out of TMEM in 32-column chunks, normalised and
+        // stored with lse; the accumulator is released after its last
+        // chunk. A warp without a head (odd GQA group) only keeps the
+        // o_empty count.
+        if (!(ok = ok && mbar_wait_warp(&bars->o_full, k & 1, kDevTimeoutFull))) break;
+        tc_fence_after();
+        if (active) {
+          const int h = w.h0 + hh;
+          const float inv = (l > 0.f) ? 1.f / l : 0.f;
+          uint4* d4 = reinterpret_cast<uint4*>(p.out + ((size_t)q_tok * p.Hq + h) * HD);
+#pragma unroll
+          for (int c = 0; c < HD / 32; ++c) {
+            uint32_t o[32];
+            tmem_ld32(t_o + 32 * c, o);
+            tmem_wait_ld();
+            if (c == HD / 32 - 1) {
+              tc_fence_before();
+              __syncwarp();
+              if (lane == 0) mbar_arrive(&bars->o_empty);
+            }
+            if (row_ok) {
+#pragma unroll
+              for (int q4 = 0; q4 < 4; ++q4) {
+                uint4 u;
+                u.x = pack_bf16x2(__uint_as_float(o[8 * q4 + 0]) * inv, __uint_as_float(o[8 * q4 + 1]) * inv);
+                u.y = pack_bf16x2(__uint_as_float(o[8 * q4 + 2]) * inv, __uint_as_float(o[8 * q4 + 3]) * inv);
+                u.z = pack_bf16x2(__uint_as_float(o[8 * q4 + 4]) * inv, __uint_as_float(o[8 * q4 + 5]) * inv);
+                u.w = pack_bf16x2(__uint_as_float(o[8 * q4 + 6]) * inv, __uint_as_float(o[8 * q4 + 7]) * inv);
+                d4[4 * c + q4] = u;
+              }
+            }
+          }
+          if (row_ok) p.lse[(size_t)h * p.L + q_tok] = (l > 0.f) ? m_used + log2f(l) : -INFINITY;
+        } else {
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&bars->o_empty);
+        }
+      }
       J += w.n;
     }
-  } else {
-    regs_dec<FwdRegs<PAGED>::epi>();
+  } else if constexpr (PAGED) {
+    regs_dec<FwdRegs::epi>();
     // ------------------------------------------------------------ epilogue
     // O of both heads out of TMEM in 32-column chunks, normalised with the
     // softmax warps' row sums and stored with lse; the accumulator is
@@ -536,9 +582,10 @@ __global__ void __launch_bounds__(kFwdThreads, 1) varlen_fwd_kernel(const __grid
   }
 }
 
-// Prepare one instantiation for launch: its dynamic shared memory, and a
-// check that the kernel is launched with the registers the setmaxnreg split
-// draws on (an increase beyond the launch allocation would never complete).
+// Prepare one instantiation for launch: its dynamic shared memory, and for
+// the paged prefill a check that the kernel is launched with the registers
+// the setmaxnreg split draws on (an increase beyond the launch allocation
+// would never complete).
 template <int HD, bool PAGED>
 cudaError_t fwd_prepare(int smem) {
   static std::atomic<int> ready{0};
@@ -546,7 +593,7 @@ cudaError_t fwd_prepare(int smem) {
   cudaFuncAttributes a{};
   cudaError_t e = cudaFuncGetAttributes(&a, varlen_fwd_kernel<HD, PAGED>);
   if (e != cudaSuccess) return e;
-  if (a.numRegs < kFwdLaunchRegs) return cudaErrorInvalidConfiguration;
+  if (PAGED && a.numRegs < kFwdLaunchRegs) return cudaErrorInvalidConfiguration;
   e = cudaFuncSetAttribute(varlen_fwd_kernel<HD, PAGED>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e == cudaSuccess) ready.store(1, std::memory_order_release);
   return e;
@@ -564,12 +611,12 @@ cudaError_t launch_varlen_fwd(const CUtensorMap& qm, const CUtensorMap& km, cons
     const int smem = FwdTile<128>::SMEM;
     e = fwd_prepare<128, false>(smem);
     if (e != cudaSuccess) return e;
-    varlen_fwd_kernel<128, false><<<grid, kFwdThreads, smem, stream>>>(qm, km, vm, p);
+    varlen_fwd_kernel<128, false><<<grid, fwd_threads<false>(), smem, stream>>>(qm, km, vm, p);
   } else {
     const int smem = FwdTile<64>::SMEM;
     e = fwd_prepare<64, false>(smem);
     if (e != cudaSuccess) return e;
-    varlen_fwd_kernel<64, false><<<grid, kFwdThreads, smem, stream>>>(qm, km, vm, p);
+    varlen_fwd_kernel<64, false><<<grid, fwd_threads<false>(), smem, stream>>>(qm, km, vm, p);
   }
   return cudaGetLastError();
 }
@@ -594,12 +641,12 @@ cudaError_t launch_paged_prefill(const CUtensorMap& qm, const CUtensorMap& km, c
     const int smem = FwdTile<128>::SMEM;
     e = fwd_prepare<128, true>(smem);
     if (e != cudaSuccess) return e;
-    varlen_fwd_kernel<128, true><<<(unsigned)n_work, kFwdThreads, smem, stream>>>(qm, km, vm, p);
+    varlen_fwd_kernel<128, true><<<(unsigned)n_work, fwd_threads<true>(), smem, stream>>>(qm, km, vm, p);
   } else {
     const int smem = FwdTile<64>::SMEM;
     e = fwd_prepare<64, true>(smem);
     if (e != cudaSuccess) return e;
-    varlen_fwd_kernel<64, true><<<(unsigned)n_work, kFwdThreads, smem, stream>>>(qm, km, vm, p);
+    varlen_fwd_kernel<64, true><<<(unsigned)n_work, fwd_threads<true>(), smem, stream>>>(qm, km, vm, p);
   }
   return cudaGetLastError();
 }
