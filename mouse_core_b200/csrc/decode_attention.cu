@@ -303,16 +303,24 @@ __global__ void __launch_bounds__(160, 2) split_decode_kernel(const __grid_const
       const int2 ent = p.entries[e];
       const int h = item % p.Hkv, b = ent.x;
       const int len = p.kv_len[b];
-      const int t_begin = ent.y * p.chunk_tokens;
-      const int t_end = min(t_begin + p.chunk_tokens, len);
+      const int tf = p.t_from[e];  // a row's tail item starts inside the chunk
+      const int t_begin = tf >= 0 ? tf : ent.y * p.chunk_tokens;
+      const int t_end = min(ent.y * p.chunk_tokens + p.chunk_tokens, len);
       const int members = p.width[e];  // nonzero for an entry in the order
       const int width = __popc(members);
       if (lane < 16) {
         int ke = len;
-        if (width > 1)
-          ke = t_end;  // a shared chunk lies wholly below every query of its rows
-        else if (lane < R)
+        if (width > 1) {
+          // A shared chunk lies wholly below every query of its rows; a
+          // member holding only its head sees keys up to its own pages.
+          ke = t_end;
+          if (lane < width * R) {
+            const int kb = p.kv_bound[p.row_start[b + nth_bit(members, lane / R)] + ent.y];
+            if (kb > 0) ke = kb;
+          }
+        } else if (lane < R) {
           ke = min(p.q_pos[(size_t)b * p.S + lane / p.G] + 1, len);
+        }
         meta[kMetaKvEnd + lane] = ke;
       }
       if (lane == 0) {
@@ -390,6 +398,7 @@ __global__ void __launch_bounds__(160, 2) split_decode_kernel(const __grid_const
     const int nchunks = meta[kMetaChunks];  // of row b (a shared chunk's rows all have more than one)
     const int members = meta[kMetaWidth], chunk = meta[kMetaChunk];
     const int width = __popc(members);
+    const int item = meta[kMetaItem];
     const int kv_end[2] = {meta[kMetaKvEnd + gid], meta[kMetaKvEnd + gid + 8]};
     uint32_t qa[HD / 16][4];
 #pragma unroll
@@ -452,7 +461,9 @@ __global__ void __launch_bounds__(160, 2) split_decode_kernel(const __grid_const
       }
       named_barrier(1, 128);
       const int bb = b + nth_bit(members, bi);
-      const size_t pit = ((size_t)p.row_start[bb] + chunk) * p.Hkv + h;  // = item when width == 1
+      // A lone item's partial goes to its own entry (a row's chunk or its
+      // tail); a shared item's to each member's entry for the chunk.
+      const size_t pit = width == 1 ? (size_t)item : ((size_t)p.row_start[bb] + chunk) * p.Hkv + h;
       for (int idx = tid; idx < R * HD; idx += 128) {
         const int r = idx / HD, col = idx % HD;
         float M = -INFINITY;
@@ -541,7 +552,7 @@ __global__ void __launch_bounds__(1024) decode_plan_kernel(const int32_t* kv_len
                                                            int q_rows, int chunk, int max_entries, int2* entries,
                                                            int* n_entries, int* row_start, int* row_chunks,
                                                            int* counters, int* order, int* n_order, int* width,
-                                                           int* work) {
+                                                           int* kv_bound, int* t_from, int* work) {
   __shared__ int warp_tot[32];
   __shared__ int total_s, n_order_s;
   __shared__ int hist[kPlanBuckets];
@@ -552,43 +563,82 @@ __global__ void __launch_bounds__(1024) decode_plan_kernel(const int32_t* kv_len
   const int per = (B + 1023) / 1024;
   const int r0 = min(tid * per, B), r1 = min(r0 + per, B);
   const int unit = max(chunk / (kPlanBuckets - 1), 1);
-  auto bucket = [&](int len, int j) {  // descending rank of chunk j of a row of `len` tokens
-    const int sz = min(chunk, max(len - j * chunk, 0));
-    return (kPlanBuckets - 1) - min((sz + unit - 1) / unit, kPlanBuckets - 1);
+  auto bucket_of = [&](int sz) {  // descending rank of an item of `sz` tokens
+    return (kPlanBuckets - 1) - min((max(sz, 0) + unit - 1) / unit, kPlanBuckets - 1);
   };
+  auto len_of = [&](int r) { return max(kv_len[r], 0); };
+  auto chunks_of = [&](int r) { return max(1, (len_of(r) + chunk - 1) / chunk); };
   const bool share = block_table != nullptr && page_size > 0 && chunk % page_size == 0 && q_rows > 0 &&
                      q_rows <= 8;
   const int NG = share ? 16 / q_rows : 1;
   const int ppc = share ? chunk / page_size : 0;  // pages per chunk
   auto eligible = [&](int r, int j) {
-    return (j + 1) * chunk <= max(kv_len[r], 0) - q_rows && (j + 1) * ppc <= max_pages;
+    return (j + 1) * chunk <= len_of(r) - q_rows && (j + 1) * ppc <= max_pages;
   };
-  auto same_pages = [&](int ra, int rb, int j) {
+  // Leading pages of chunk j that rows ra and rb hold on the same page ids.
+  auto common_pages = [&](int ra, int rb, int j) {
+    const int lim = min(ppc, max_pages - j * ppc);
     const int32_t* ta = block_table + (size_t)ra * max_pages + (size_t)j * ppc;
     const int32_t* tb = block_table + (size_t)rb * max_pages + (size_t)j * ppc;
-    for (int q = 0; q < ppc; ++q)
-      if (ta[q] < 0 || ta[q] != tb[q]) return false;
-    return true;
+    int q = 0;
+    while (q < lim && ta[q] >= 0 && ta[q] == tb[q]) ++q;
+    return q;
+  };
+  // The row that leads chunk j in r's block: its first row whose chunk j is
+  // whole and below every query; -1 when there is none.
+  auto leader = [&](int r, int j) {
+    const int blk0 = r - r % NG, blk1 = min(blk0 + NG, B);
+    for (int x = blk0; x < blk1; ++x)
+      if (eligible(x, j)) return x;
+    return -1;
+  };
+  // Where row r's own pages start inside chunk j when it shares only the
+  // chunk's head with the leader (a branch forked inside the chunk): that
+  // token, or 0.
+  auto head_bound = [&](int r, int j, int lead) {
+    if (lead < 0 || lead == r) return 0;
+    const int sp = common_pages(lead, r, j);
+    if (sp == 0 || sp == ppc) return 0;
+    const int bnd = j * chunk + sp * page_size;
+    return bnd <= len_of(r) - q_rows ? bnd : 0;
+  };
+  auto joins = [&](int lead, int x, int j) {  // row x's chunk j (or its head) rides on lead's item
+    return (eligible(x, j) && common_pages(lead, x, j) == ppc) || head_bound(x, j, lead) > 0;
   };
   // Rows whose item is entry (r, j)'s, as a mask over rows r .. r + NG - 1
-  // (bit 0: r itself); 0 when another row's item covers the entry.
+  // (bit 0: r itself); 0 when the block leader's item covers the entry.
   auto members_of = [&](int r, int j) {
-    if (NG == 1 || !eligible(r, j)) return 1;
-    const int blk0 = r - r % NG, blk1 = min(blk0 + NG, B);
-    int lead = r;
-    for (int x = blk0; x < r; ++x)
-      if (eligible(x, j)) {
-        lead = x;
-        break;
-      }
-    if (lead != r) return same_pages(lead, r, j) ? 0 : 1;
+    if (NG == 1) return 1;
+    const int lead = leader(r, j);
+    if (lead < 0) return 1;
+    if (lead != r) return joins(lead, r, j) ? 0 : 1;
     int mask = 1;
+    const int blk1 = min(r - r % NG + NG, B);
     for (int x = r + 1; x < blk1; ++x)
-      if (eligible(x, j) && same_pages(r, x, j)) mask |= 1 << (x - r);
+      if (joins(r, x, j)) mask |= 1 << (x - r);
     return mask;
   };
+  // The chunk whose head row r shares with its leader, so that the chunk's
+  // rest is an extra item of the row (its "tail"), and where the tail
+  // starts; -1 when the row has none.
+  auto tail_of = [&](int r, int& bnd) {
+    bnd = 0;
+    if (NG == 1) return -1;
+    const int c = chunks_of(r);
+    for (int j = 0; j < c; ++j) {
+      const int b_ = head_bound(r, j, leader(r, j));
+      if (b_ > 0) {
+        bnd = b_;
+        return j;
+      }
+    }
+    return -1;
+  };
   int cnt = 0;
-  for (int r = r0; r < r1; ++r) cnt += max(1, (max(kv_len[r], 0) + chunk - 1) / chunk);
+  for (int r = r0; r < r1; ++r) {
+    int bnd;
+    cnt += chunks_of(r) + (tail_of(r, bnd) >= 0 ? 1 : 0);
+  }
   __syncthreads();
   // block exclusive scan of cnt
   const int lane = tid & 31, w = tid >> 5;
@@ -625,20 +675,32 @@ __global__ void __launch_bounds__(1024) decode_plan_kernel(const int32_t* kv_len
   }
   int mine = 0;  // entries of this thread's rows that get an item
   for (int r = r0; r < r1; ++r) {
-    const int len = max(kv_len[r], 0);
-    const int c = max(1, (len + chunk - 1) / chunk);
+    const int len = len_of(r);
+    const int c = chunks_of(r);
+    int bnd;
+    const int jt = tail_of(r, bnd);
     row_start[r] = base;
-    row_chunks[r] = c;
+    row_chunks[r] = c + (jt >= 0 ? 1 : 0);
     for (int j = 0; j < c; ++j) {
       entries[base + j] = make_int2(r, j);
       const int wd = members_of(r, j);
       width[base + j] = wd;
+      kv_bound[base + j] = j == jt ? bnd : 0;  // read by the leader's item for this row's queries
+      t_from[base + j] = -1;
       if (wd > 0) {
-        atomicAdd(&hist[bucket(len, j)], 1);
+        atomicAdd(&hist[bucket_of(min(chunk, len - j * chunk))], 1);
         ++mine;
       }
     }
-    base += c;
+    if (jt >= 0) {  // the tail: tokens bnd .. of chunk jt, an item of this row alone
+      entries[base + c] = make_int2(r, jt);
+      width[base + c] = 1;
+      kv_bound[base + c] = 0;
+      t_from[base + c] = bnd;
+      atomicAdd(&hist[bucket_of(min(len, (jt + 1) * chunk) - bnd)], 1);
+      ++mine;
+    }
+    base += c + (jt >= 0 ? 1 : 0);
   }
   atomicAdd(&n_order_s, mine);
   for (int i = tid; i < B * Hkv; i += 1024) counters[i] = 0;
@@ -657,11 +719,15 @@ __global__ void __launch_bounds__(1024) decode_plan_kernel(const int32_t* kv_len
   __syncthreads();
   base = x - cnt + (w > 0 ? warp_tot[w - 1] : 0);
   for (int r = r0; r < r1; ++r) {
-    const int len = max(kv_len[r], 0);
-    const int c = max(1, (len + chunk - 1) / chunk);
+    const int len = len_of(r);
+    const int c = chunks_of(r);
     for (int j = 0; j < c; ++j)
-      if (width[base + j] > 0) order[atomicAdd(&cursor[bucket(len, j)], 1)] = base + j;
-    base += c;
+      if (width[base + j] > 0) order[atomicAdd(&cursor[bucket_of(min(chunk, len - j * chunk))], 1)] = base + j;
+    if (row_chunks[r] > c) {
+      const int jt = entries[base + c].y;
+      order[atomicAdd(&cursor[bucket_of(min(len, (jt + 1) * chunk) - t_from[base + c])], 1)] = base + c;
+    }
+    base += row_chunks[r];
   }
 }
 
@@ -789,7 +855,7 @@ size_t decode_chunk_tokens(int) { return 2048; }
 size_t decode_workspace_layout(int B, int Hkv, int R, int head_dim, int max_kv_len, WorkspaceLayout* lay) {
   const size_t chunk = decode_chunk_tokens(head_dim);
   const size_t per_row = std::max<size_t>(1, ((size_t)std::max(max_kv_len, 0) + chunk - 1) / chunk);
-  const size_t max_entries = (size_t)B * per_row;
+  const size_t max_entries = (size_t)B * (per_row + 1);  // + one tail entry per row (shared plans)
   auto up = [](size_t x) { return (x + 255) & ~size_t(255); };
   size_t off = 0;
   lay->max_entries = max_entries;
@@ -801,6 +867,8 @@ size_t decode_workspace_layout(int B, int Hkv, int R, int head_dim, int max_kv_l
   lay->order = off;      off = up(off + max_entries * sizeof(int));
   lay->n_order = off;    off = up(off + sizeof(int));
   lay->width = off;      off = up(off + max_entries * sizeof(int));
+  lay->kv_bound = off;   off = up(off + max_entries * sizeof(int));
+  lay->t_from = off;     off = up(off + max_entries * sizeof(int));
   lay->work = off;       off = up(off + 2 * sizeof(int));
   lay->part_lse = off;   off = up(off + max_entries * Hkv * R * sizeof(float));
   lay->part_o = off;     off = up(off + max_entries * Hkv * R * head_dim * sizeof(float));
@@ -860,6 +928,7 @@ cudaError_t launch_decode_plan(const int32_t* kv_len, const int32_t* block_table
       reinterpret_cast<int*>(ws + lay.row_start), reinterpret_cast<int*>(ws + lay.row_chunks),
       reinterpret_cast<int*>(ws + lay.counters), reinterpret_cast<int*>(ws + lay.order),
       reinterpret_cast<int*>(ws + lay.n_order), reinterpret_cast<int*>(ws + lay.width),
+      reinterpret_cast<int*>(ws + lay.kv_bound), reinterpret_cast<int*>(ws + lay.t_from),
       reinterpret_cast<int*>(ws + lay.work));
   return cudaGetLastError();
 }
@@ -876,6 +945,8 @@ cudaError_t launch_decode_attention(const CUtensorMap& km, const CUtensorMap& vm
     p.order = reinterpret_cast<const int*>(ws + lay.order);
     p.n_order = reinterpret_cast<const int*>(ws + lay.n_order);
     p.width = reinterpret_cast<const int*>(ws + lay.width);
+    p.kv_bound = reinterpret_cast<const int*>(ws + lay.kv_bound);
+    p.t_from = reinterpret_cast<const int*>(ws + lay.t_from);
     p.work = reinterpret_cast<int*>(ws + lay.work);
     p.part_lse = reinterpret_cast<float*>(ws + lay.part_lse);
     p.part_o = reinterpret_cast<float*>(ws + lay.part_o);

@@ -30,6 +30,8 @@ struct AttnParams {
   const int* order;            // entries, longest chunk first (the order CTAs take work in)
   const int* n_order;          // entries in `order`
   const int* width;            // per entry: member mask of its item (bit k: row + k; 1 alone; 0 covered)
+  const int* kv_bound;         // per entry: a member's key end inside a shared chunk (0: the whole chunk)
+  const int* t_from;           // per entry: a tail item's first token (-1: the chunk's start)
   int* work;                   // [2]: next work item, CTAs finished (zeroed by the plan and the last CTA)
   float* part_lse;
   float* part_o;
@@ -37,7 +39,8 @@ struct AttnParams {
 
 struct WorkspaceLayout {
   size_t max_entries;
-  size_t entries, n_entries, row_start, row_chunks, counters, order, n_order, width, work, part_lse, part_o;
+  size_t entries, n_entries, row_start, row_chunks, counters, order, n_order, width, kv_bound, t_from, work,
+      part_lse, part_o;
   size_t total;
 };
 

@@ -350,9 +350,11 @@ def test_session_graph_replay_matches_eager():
 def test_shared_chunk_plan_matches_plain_plan(hd, page, Hq, Hkv):
     """One-token decode over rows that hold forked prefixes on the same pages:
     the plan that gives a shared 2048-token chunk one work item for a block of
-    rows (mb_decode_plan_shared) yields bit-for-bit the outputs of the plan
-    that reads the chunk once per row (mb_decode_plan), and both match the
-    oracle. Rows: a root's branches filling an aligned block and spilling into
+    rows (mb_decode_plan_shared) matches the plan that reads the chunk once
+    per row (mb_decode_plan) — bit for bit on every row that holds whole
+    chunks only, within one bf16 rounding where a row's chunk is split into a
+    shared head and its own tail (two partials instead of one) — and both
+    match the oracle. Rows: a root's branches filling an aligned block and spilling into
     the next one, a second group that does not start a block, lone rows, a
     branch forked inside a chunk, and rows shorter than one chunk."""
     dev = _dev()
@@ -368,11 +370,14 @@ def test_shared_chunk_plan_matches_plain_plan(hd, page, Hq, Hkv):
     # branches fill the first aligned block and spill into the next one;
     # root 1's branches sit after the second block's start, behind rows of
     # root 0; in the third block two short rows come first and root 2's
-    # branches alternate with lone rows (a member mask with gaps); one of
-    # root 1's branches forks inside its second chunk.
+    # branches alternate with lone rows (a member mask with gaps), one of
+    # them forked inside its second chunk (it shares that chunk's head and
+    # has the rest as a tail item); one of root 1's branches forks inside
+    # its second chunk too.
     layout = [(0, 3 * ppc)] * (NG + 2) + [(None, 0), (1, 2 * ppc), (1, 2 * ppc), (1, ppc + ppc // 2)]
     layout += [(None, 0)] * (2 * NG - len(layout))
-    layout += [("short", 0), ("short", 0)] + [(2, 2 * ppc), (None, 0)] * 3 + [(2, 2 * ppc)]
+    layout += [("short", 0), ("short", 0)] + [(2, 2 * ppc), (None, 0)] * 2 + [(2, ppc + ppc // 2), (None, 0)]
+    layout += [(2, 2 * ppc)]
     B = len(layout)
     lens = []
     for root, ns in layout:
@@ -417,7 +422,11 @@ def test_shared_chunk_plan_matches_plain_plan(hd, page, Hq, Hkv):
     from mouse_core_b200 import _lib
 
     assert _lib.device_status() == 0
-    assert torch.equal(plain, shared)
+    split_rows = [r for r, (root, ns) in enumerate(layout) if isinstance(root, int) and ns % ppc]
+    whole = [r for r in range(B) if r not in split_rows]
+    assert torch.equal(plain[whole], shared[whole])
+    d = (plain.float() - shared.float()).abs()
+    assert float(d.max()) <= 2 ** -8 * max(1.0, float(plain.float().abs().max())), float(d.max())
     # Oracle on every row (float64, same bf16 inputs).
     k_rows = [torch.cat([kp[bt[b, i]].transpose(0, 1) for i in range(npg[b])])[:lens[b]].float().numpy()
               for b in range(B)]
