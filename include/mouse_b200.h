@@ -89,8 +89,12 @@ int mb_decode_plan(const int32_t* kv_len, int batch, int kv_heads, int q_rows, i
  * 16 / q_rows; where rows of a block hold a whole 2048-token chunk on the
  * very same pages as the block's first row that has that chunk, one work
  * item reads the chunk's K/V once for all of their queries (the other rows'
- * entries get no item of their own). Results are identical to
- * mb_decode_plan's. Requires
+ * entries get no item of their own); a row that holds only the chunk's head
+ * on those pages (forked inside the chunk) joins the item for the head and
+ * reads the rest of the chunk as an extra item of its own. Outputs equal
+ * mb_decode_plan's bit for bit for rows holding whole chunks, and within
+ * bf16 rounding for a row whose chunk is split (two partials merged instead
+ * of one). Requires
  * every query to see every cached slot of its row (q_pos[b, s] >= kv_len[b]
  * - q_rows, as in one-token decode: q_pos = kv_len - 1), and q_rows <= 8 for
  * any sharing to happen. Replaces nothing in the reference, whose decode
