@@ -408,7 +408,7 @@ def run_ours(args):
     # every row and kv-head (2 * Hkv * hd * 2 B per token) + q/out.
     mean_kv = kv_sum / K_steps
     attn_bytes = mean_kv * 2 * KV_HEADS * HEAD_DIM * 2 + 2 * ENVS * HEADS * HEAD_DIM * 2
-    attn_avg_ms = statistics.mean(attn_ms) if attn_ms else float("nan")
+    attn_avg_ms = statistics.median(attn_ms) if attn_ms else float("nan")  # a host hiccup can idle one bracket
     achieved = attn_bytes / (attn_avg_ms * 1e-3) / 1e9
     peaks = {}
     try:
@@ -471,7 +471,7 @@ def run_ours(args):
             "roofline": {"kernel": "split_decode_kernel (K1)", "bound": "hbm", "achieved": round(achieved, 1),
                          "peak": peak, "peak_source": peak_src, "unit": "GB/s", "frac": round(achieved / peak, 4),
                          "traffic": roofline_traffic_per_launch(attn_bytes), "algorithmic_bytes_per_launch": int(attn_bytes),
-                         "avg_launch_ms": round(attn_avg_ms, 5), "launches_timed": len(attn_ms)},
+                         "median_launch_ms": round(attn_avg_ms, 5), "launches_timed": len(attn_ms)},
             "gpu_launches": int(launches),
             "clocks": clk,
             "device_status": status,
@@ -679,7 +679,7 @@ def large_batch_measure(dev, world, rank, local, envs, K_steps, W):
     ms_max, e2e_max = (float(x) for x in t.tolist())
     status = _lib.device_status()
     attn_bytes = kv_sum / K_steps * 2 * Hkv * hd * 2 + 2 * envs * Hq * hd * 2
-    attn_avg_ms = statistics.mean(attn_ms) if attn_ms else float("nan")
+    attn_avg_ms = statistics.median(attn_ms) if attn_ms else float("nan")  # a host hiccup can idle one bracket
     achieved = attn_bytes / (attn_avg_ms * 1e-3) / 1e9
     peaks = {}
     try:
@@ -703,7 +703,7 @@ def large_batch_measure(dev, world, rank, local, envs, K_steps, W):
                             "peak": peak, "peak_source": "measured" if "hbm_gbs" in peaks else "fallback",
                             "unit": "GB/s", "frac": round(achieved / peak, 4),
                             "traffic": roofline_traffic_per_launch(attn_bytes, "large_batch_split_decode_64envs.json"),
-                            "algorithmic_bytes_per_launch": int(attn_bytes), "avg_launch_ms": round(attn_avg_ms, 5),
+                            "algorithmic_bytes_per_launch": int(attn_bytes), "median_launch_ms": round(attn_avg_ms, 5),
                             "launches_timed": len(attn_ms)},
                "kv_pool_gb": round(pages * LB["layers"] * 2 * Hkv * P * hd * 2 / 1e9, 1),
                "gpu_launches": int(launches), "clocks": clk, "device_status": status}
@@ -885,7 +885,7 @@ def grpo_measure(dev, world, rank, local, roots, K_steps, W):
     ms_max, e2e_max, pre_max = (float(x) for x in t.tolist())
     status = _lib.device_status()
     attn_bytes = kv_sum / K_steps * 2 * KV_HEADS * HEAD_DIM * 2 + 2 * B * HEADS * HEAD_DIM * 2
-    attn_avg_ms = statistics.mean(attn_ms) if attn_ms else float("nan")
+    attn_avg_ms = statistics.median(attn_ms) if attn_ms else float("nan")  # a host hiccup can idle one bracket
     achieved = attn_bytes / (attn_avg_ms * 1e-3) / 1e9
     peaks = {}
     try:
@@ -914,7 +914,7 @@ def grpo_measure(dev, world, rank, local, roots, K_steps, W):
                             "peak": peak, "peak_source": "measured" if "hbm_gbs" in peaks else "fallback",
                             "unit": "GB/s", "frac": round(achieved / peak, 4),
                             "traffic": roofline_traffic_per_launch(attn_bytes, "grpo_split_decode_8roots.json"),
-                            "algorithmic_bytes_per_launch": int(attn_bytes), "avg_launch_ms": round(attn_avg_ms, 5),
+                            "algorithmic_bytes_per_launch": int(attn_bytes), "median_launch_ms": round(attn_avg_ms, 5),
                             "launches_timed": len(attn_ms),
                             "note": "algorithmic bytes count each distinct cached token once per launch: a "
                                     "prefix page the 16 branches of a root share is counted once"},
