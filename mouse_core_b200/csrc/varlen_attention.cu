@@ -16,16 +16,19 @@
 // through a two-slot ring, and barrier phases follow a running key-tile count
 // across tiles. Q is released after a tile's last Q K^T MMA, so the next
 // tile's Q loads during the last softmax, P V and epilogue; O is released
-// once the epilogue has read it. Warp roles (512 threads, four warpgroups):
+// once the epilogue has read it. Warp roles of the training forward (320
+// threads):
 //   warp 0      TMA producer: Q once per tile, K/V tiles through a 2-3 stage ring
 //   warp 1      TMEM allocator; the whole warp issues every tcgen05.mma
-//   warps 2-3   idle (they complete the control warpgroup)
-//   warps 4-7   softmax of head 0 (thread = query row = TMEM lane)
-//   warps 8-11  softmax of head 1
-//   warps 12-15 epilogue: a tile's O out of TMEM, normalised and stored,
-//               while the softmax warps already work on the next tile
-// The block is launched with 128 registers a thread; setmaxnreg moves them
-// from the control and epilogue warpgroups to the softmax ones (FwdRegs).
+//   warps 2-5   softmax of head 0 (thread = query row = TMEM lane), then
+//               the tile's epilogue for it
+//   warps 6-9   softmax of head 1, then its epilogue
+// The paged prefill (512 threads, four warpgroups) moves the epilogue to its
+// own warps: warps 0-1 as above, 2-3 idle (they complete the control
+// warpgroup), 4-7 and 8-11 softmax, 12-15 the epilogue of both heads, which
+// drains a tile's O while the softmax warps already work on the next tile;
+// it is launched with 128 registers a thread and setmaxnreg moves them from
+// the control and epilogue warpgroups to the softmax ones (FwdRegs).
 // Tensor memory (512 columns): S_h = Q_h K^T at columns 128h, O_h at 256 + HD h.
 // Softmax reads S, writes P (bf16 pairs) back over the first 64 columns of
 // S_h, and the MMA O_h += P V takes P straight from TMEM. The two heads
