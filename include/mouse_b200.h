@@ -51,7 +51,7 @@ int mb_version(void);
  * device. 0 = healthy; 1 / 2 = a consumer / producer wait ran out; 3 = a page
  * id outside the pool (or a token past the block table); 4 = misaligned
  * dynamic shared memory; 5 = a stored-dS pair index outside the scratch;
- * 6 = a CTA's own copies did not land before it exited; 7 = an embedding id
+ * 6 = a CTA's own copies or MMAs did not complete before it exited; 7 = an embedding id
  * outside its table, or a TD action / done code out of range. */
 int mb_device_status(int* status_out, int clear);
 

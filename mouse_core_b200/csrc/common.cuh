@@ -25,7 +25,7 @@ enum DeviceStatus : int {
   kDevBadPage = 3,       // block-table entry outside the page pool
   kDevBadSmem = 4,       // dynamic shared memory base not 1024-byte aligned
   kDevBadPair = 5,       // stored-dS pair index outside the scratch (inconsistent pair offsets)
-  kDevTimeoutDrain = 6,  // a CTA's own copies did not land before it exited
+  kDevTimeoutDrain = 6,  // a CTA's own copies or MMAs did not complete before it exited
   kDevBadIndex = 7,      // an embedding id outside its table (the token is left zero)
 };
 
@@ -150,6 +150,17 @@ __device__ __forceinline__ void mbar_drain(uint64_t* bar, uint32_t parity) {
       return;
     }
   }
+}
+
+// Every load a CTA issued into a ring of `stages` barriers lands before the
+// CTA exits: load i of the `issued` went to barrier i % stages in phase
+// (i / stages) & 1, and only the last `stages` can still be in flight (a slot
+// is reloaded only after its previous phase completed). Each barrier's last
+// phase is also the newest it will ever reach, so the wait is exact whether
+// the pipeline finished or a wait of it ran out.
+__device__ __forceinline__ void drain_ring(uint64_t* ring, int stages, int issued) {
+  for (int i = issued > stages ? issued - stages : 0; i < issued; ++i)
+    mbar_drain(&ring[i % stages], (uint32_t)(i / stages) & 1);
 }
 
 // ---------------------------------------------------------------- TMA

@@ -217,6 +217,16 @@ __device__ __forceinline__ void umma_commit_warp(uint64_t* bar) {
       : "memory");
 }
 
+// Every MMA the calling warp issued completes before its CTA frees TMEM and
+// exits: one commit of all of them to `bar` (a barrier of count 1 used for
+// nothing else) and a wait on its first phase, bounded by kDrainCycles. An
+// issued MMA always completes (its operands were complete when it was
+// issued), so this holds on a timed-out pipeline too.
+__device__ __forceinline__ void umma_drain_warp(uint64_t* bar) {
+  umma_commit_warp(bar);
+  mbar_drain(bar, 0);
+}
+
 // Arrive on `bar` once every tcgen05 operation this thread issued so far is done.
 __device__ __forceinline__ void umma_commit(uint64_t* bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))

@@ -85,8 +85,10 @@ struct FwdBarriers {
   uint64_t s_full[2], p_full[2];
   uint64_t o_full, o_empty;
   uint64_t stats_full[2];  // a tile's row max / row sum handed from the softmax to the epilogue warps
+  uint64_t mma_drain;      // every MMA of the CTA complete, before TMEM is freed
   uint32_t tmem_base;
   int tile[2];
+  int q_armed;  // Q tiles whose loads the producer issued (kept here: its registers are few)
   float stats[2][2][2][128];  // [tile parity][head][max, sum][row]
 };
 static_assert(sizeof(FwdBarriers) <= 4352, "barrier / stats block outgrew its shared memory share");
@@ -204,6 +206,8 @@ __global__ void __launch_bounds__(fwd_threads<PAGED>(), 1) varlen_fwd_kernel(con
     }
     mbar_init(&bars->o_full, 1);
     mbar_init(&bars->o_empty, PAGED ? 4 : 8);  // whoever drains O
+    mbar_init(&bars->mma_drain, 1);
+    bars->q_armed = 0;
     fence_barrier_init();
   }
   if (warp == 1) tmem_alloc(&bars->tmem_base, C::TMEM_COLS);
@@ -232,7 +236,7 @@ __global__ void __launch_bounds__(fwd_threads<PAGED>(), 1) varlen_fwd_kernel(con
       prefetch_tensormap(&kmap);
       prefetch_tensormap(&vmap);
     }
-    int J = 0;  // key tiles of earlier work tiles: ring slots and phases continue
+    int J = 0;  // K/V tile pairs issued so far (lane 0): ring slots and phases continue
     for (int k = 0; ok; ++k) {
       int tile = -1;
       if (lane == 0) {
@@ -259,8 +263,10 @@ __global__ void __launch_bounds__(fwd_threads<PAGED>(), 1) varlen_fwd_kernel(con
           for (int hh = 0; hh < hpc; ++hh)
             for (int cb = 0; cb < C::NCB; ++cb)
               tma_load_3d(qs + hh * C::QTILE + cb * C::BOX, &qmap, &bars->q_full, cb * 64, w.h0 + hh, w.q0);
+          *reinterpret_cast<volatile int*>(&bars->q_armed) = k + 1;
         }
-        for (int j = 0; ok && j < w.n; ++j) {
+        int j = 0;
+        for (; ok && j < w.n; ++j) {
           const int jj = J + j;
           const int st = jj % C::STAGES;
           if (!(ok = mbar_wait(&bars->kv_empty[st], ((jj / C::STAGES) & 1) ^ 1, kDevTimeoutEmpty))) break;
@@ -280,9 +286,15 @@ __global__ void __launch_bounds__(fwd_threads<PAGED>(), 1) varlen_fwd_kernel(con
               tma_load_3d(vs + st * C::KVTILE + cb * C::BOX, &vmap, &bars->v_full[st], cb * 64, w.kvh, kv0);
           }
         }
+        J += j;  // w.n, or the pairs issued before a wait ran out
       }
       ok = __shfl_sync(0xffffffffu, ok, 0);
-      J += w.n;
+    }
+    // Every load issued lands before the CTA exits, also when a wait ran out.
+    if (lane == 0) {
+      drain_ring(&bars->q_full, 1, *reinterpret_cast<volatile int*>(&bars->q_armed));
+      drain_ring(bars->k_full, C::STAGES, J);
+      drain_ring(bars->v_full, C::STAGES, J);
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issue
@@ -340,6 +352,7 @@ __global__ void __launch_bounds__(fwd_threads<PAGED>(), 1) varlen_fwd_kernel(con
       umma_commit_warp(&bars->o_full);
       J += n;
     }
+    umma_drain_warp(&bars->mma_drain);  // before TMEM is freed, also when a wait ran out
   }
   } else if (warp < kSoftmaxWarp0 + 8) {
     if constexpr (PAGED) regs_inc<FwdRegs::softmax>();

@@ -188,6 +188,7 @@ struct DqBars {
   uint64_t ds_done[2];  // bf16 dS of item j in TMEM (set j & 1)
   uint64_t acc_full;    // dQ of the tile complete in TMEM
   uint64_t acc_empty;   // the element-wise warps have read it out
+  uint64_t mma_drain;   // every MMA of the CTA complete, before TMEM is freed
   uint32_t tmem_base;
   int tile[2];
 };
@@ -250,6 +251,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1) varlen_bwd_dq_kernel(const __g
     mbar_init(&bars->dp_loaded, kEwWarps);
     mbar_init(&bars->acc_full, 1);
     mbar_init(&bars->acc_empty, kEwWarps);
+    mbar_init(&bars->mma_drain, 1);
     fence_barrier_init();
   }
   if (warp == 1) tmem_alloc(&bars->tmem_base, 512);
@@ -277,6 +279,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1) varlen_bwd_dq_kernel(const __g
       prefetch_tensormap(&dom);
     }
     int J = 0;  // items of earlier tiles: ring slots and phases continue across tiles
+    int n_fixed = 0, n_k = 0, n_v = 0;  // loads issued into each ring (lane 0)
     for (int k = 0; ok; ++k) {
       int tile = -1;
       if (lane == 0) {
@@ -301,6 +304,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1) varlen_bwd_dq_kernel(const __g
             tma_load_3d(qs + cb * C::BOX, &qmap, &bars->fixed_full, cb * 64, d.h, d.q0);
             tma_load_3d(dos + cb * C::BOX, &dom, &bars->fixed_full, cb * 64, d.h, d.q0);
           }
+          ++n_fixed;
         }
         for (int j = 0; ok && j < d.n; ++j) {
           const int jj = J + j;
@@ -310,14 +314,22 @@ __global__ void __launch_bounds__(kBwdThreads, 1) varlen_bwd_dq_kernel(const __g
           mbar_arrive_expect_tx(&bars->k_full[ks], C::TILE);
           for (int cb = 0; cb < C::NCB; ++cb)
             tma_load_3d(kring + ks * C::TILE + cb * C::BOX, &kmap, &bars->k_full[ks], cb * 64, d.kvh, kv0);
+          ++n_k;
           if (!(ok = mbar_wait(&bars->v_empty[vsl], ((jj >> 1) & 1) ^ 1, kDevTimeoutEmpty))) break;
           mbar_arrive_expect_tx(&bars->v_full[vsl], C::TILE);
           for (int cb = 0; cb < C::NCB; ++cb)
             tma_load_3d(vring + vsl * C::TILE + cb * C::BOX, &vmap, &bars->v_full[vsl], cb * 64, d.kvh, kv0);
+          ++n_v;
         }
       }
       ok = __shfl_sync(0xffffffffu, ok, 0);
       J += d.n;
+    }
+    // Every load issued lands before the CTA exits, also when a wait ran out.
+    if (lane == 0) {
+      drain_ring(&bars->fixed_full, 1, n_fixed);
+      drain_ring(bars->k_full, 3, n_k);
+      drain_ring(bars->v_full, 2, n_v);
     }
   } else if (warp == 1) {
     constexpr uint32_t ID_S = umma_idesc_bf16(128, 128, 0, 0);
@@ -366,6 +378,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1) varlen_bwd_dq_kernel(const __g
       umma_commit_warp(&bars->fixed_empty);
       J += n;
     }
+    umma_drain_warp(&bars->mma_drain);  // before TMEM is freed, also when a wait ran out
   } else {
     const int cq = (warp - 2) >> 2;  // column quarter of every 128-column tile
     const int sub = warp & 3;         // TMEM lane quarter
@@ -487,6 +500,7 @@ struct DkdvBars {
   uint64_t ds_done;          // bf16 dS^T of the current item in TMEM
   uint64_t acc_full;         // dV, dK of the tile complete in TMEM
   uint64_t acc_empty;        // the element-wise warps have read them out
+  uint64_t mma_drain;        // every MMA of the CTA complete, before TMEM is freed
   uint32_t tmem_base;
   int tile[2];
 };
@@ -553,6 +567,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1) varlen_bwd_dkdv_kernel(const _
     mbar_init(&bars->ds_done, kDsWarps);
     mbar_init(&bars->acc_full, 1);
     mbar_init(&bars->acc_empty, kPWarps + kDsWarps);
+    mbar_init(&bars->mma_drain, 1);
     fence_barrier_init();
   }
   if (warp == 1) tmem_alloc(&bars->tmem_base, 512);
@@ -581,6 +596,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1) varlen_bwd_dkdv_kernel(const _
     }
     bool ok = true;
     int J = 0;  // items of earlier tiles: ring slots and phases continue across tiles
+    int n_fixed = 0, n_q = 0, n_d = 0;  // loads issued into each ring (lane 0)
     for (int k = 0; ok; ++k) {
       int tile = -1;
       if (lane == 0) {
@@ -605,6 +621,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1) varlen_bwd_dkdv_kernel(const _
             tma_load_3d(ks + cb * C::BOX, &kmap, &bars->fixed_full, cb * 64, d.kvh, d.kv0);
             tma_load_3d(vs + cb * C::BOX, &vmap, &bars->fixed_full, cb * 64, d.kvh, d.kv0);
           }
+          ++n_fixed;
         }
       }
       ok = __shfl_sync(0xffffffffu, ok, 0);
@@ -638,7 +655,10 @@ __global__ void __launch_bounds__(kBwdThreads, 1) varlen_bwd_dkdv_kernel(const _
 #pragma unroll
         for (int i = 0; i < 4; ++i) lse_ring[qs * 128 + lane + 32 * i] = lpre[i];
         __syncwarp();
-        if (lane == 0) mbar_arrive(&bars->q_full[qs]);
+        if (lane == 0) {
+          mbar_arrive(&bars->q_full[qs]);
+          ++n_q;
+        }
         if (lane == 0) ok = mbar_wait(&bars->d_empty[dsl], ((tt >> 1) & 1) ^ 1, kDevTimeoutEmpty);
         ok = __shfl_sync(0xffffffffu, ok, 0);
         if (!ok) break;
@@ -650,10 +670,20 @@ __global__ void __launch_bounds__(kBwdThreads, 1) varlen_bwd_dkdv_kernel(const _
 #pragma unroll
         for (int i = 0; i < 4; ++i) dlt_ring[dsl * 128 + lane + 32 * i] = dpre[i];
         __syncwarp();
-        if (lane == 0) mbar_arrive(&bars->d_full[dsl]);
+        if (lane == 0) {
+          mbar_arrive(&bars->d_full[dsl]);
+          ++n_d;
+        }
         if (t + 1 < d.n) prefetch(t + 1);
       }
       J += d.n;
+    }
+    // Every load issued lands before the CTA exits, also when a wait ran out
+    // (a Q or dO slot's phase also takes its staging arrive, made just above).
+    if (lane == 0) {
+      drain_ring(&bars->fixed_full, 1, n_fixed);
+      drain_ring(bars->q_full, 3, n_q);
+      drain_ring(bars->d_full, 2, n_d);
     }
   } else if (warp == 1) {
     constexpr uint32_t ID_S = umma_idesc_bf16(128, 128, 0, 0);
@@ -714,6 +744,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1) varlen_bwd_dkdv_kernel(const _
       umma_commit_warp(&bars->acc_full);
       J += n;
     }
+    umma_drain_warp(&bars->mma_drain);  // before TMEM is freed, also when a wait ran out
   } else {
     const bool p_warp = warp < 2 + kPWarps;
     const int ch = (warp - (p_warp ? 2 : 2 + kPWarps)) >> 2;  // column half of every 128-column tile
@@ -915,6 +946,7 @@ struct DqsBars {
   uint64_t tile_full[2], tile_empty[2];              // tile-id ring
   uint64_t full[kDqsStages], empty[kDqsStages];      // dS block + K tile per stage
   uint64_t acc_full[2], acc_empty[2];                // the two dQ accumulators
+  uint64_t mma_drain;                                // every MMA of the CTA complete, before TMEM is freed
   uint32_t tmem_base;
   int tile[2];
 };
@@ -962,6 +994,7 @@ __global__ void __launch_bounds__(kDqsThreads, 1)
       mbar_init(&bars->full[s], 1);
       mbar_init(&bars->empty[s], 1);
     }
+    mbar_init(&bars->mma_drain, 1);
     fence_barrier_init();
   }
   if (warp == 1) tmem_alloc(&bars->tmem_base, 2 * HD);
@@ -982,6 +1015,7 @@ __global__ void __launch_bounds__(kDqsThreads, 1)
     if (lane == 0) prefetch_tensormap(&kmap);
     bool ok = true;
     int J = 0;  // items of earlier tiles: stage slots and phases continue across tiles
+    int n_full = 0;  // stages loaded (lane 0)
     for (int k = 0; ok; ++k) {
       int tile = -1;
       if (lane == 0) {
@@ -1010,11 +1044,14 @@ __global__ void __launch_bounds__(kDqsThreads, 1)
             bulk_load(st, p.ds + ((size_t)d.h * p.n_pairs + d.pair0 + t) * (128 * 128), A_BYTES, &bars->full[s]);
           for (int cb = 0; cb < C::NCB; ++cb)
             tma_load_3d(st + A_BYTES + cb * C::BOX, &kmap, &bars->full[s], cb * 64, d.kvh, (d.t_lo + t) * 128);
+          ++n_full;
         }
       }
       ok = __shfl_sync(0xffffffffu, ok, 0);
       J += d.n;
     }
+    // Every load issued lands before the CTA exits, also when a wait ran out.
+    if (lane == 0) drain_ring(bars->full, kDqsStages, n_full);
   } else if (warp == 1) {
     constexpr uint32_t ID = umma_idesc_bf16(128, HD, 1, 1);
     bool ok = true;
@@ -1040,6 +1077,7 @@ __global__ void __launch_bounds__(kDqsThreads, 1)
       umma_commit_warp(&bars->acc_full[k & 1]);
       J += n;
     }
+    umma_drain_warp(&bars->mma_drain);  // before TMEM is freed, also when a wait ran out
   } else {
     const int sub = warp & 3, half = (warp - 2) >> 2;
     const uint32_t lane_bits = (uint32_t)(sub * 32) << 16;
