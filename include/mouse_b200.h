@@ -170,6 +170,32 @@ int mb_kv_append_f32(const float* qkv, int tokens, int qkv_stride, const int32_t
                      mb_stream_t stream);
 
 /* ---------------------------------------------------------------------
+ * QKV projection with the K2 epilogue (K13, tcgen05).
+ * Replaces, per layer of a decode step, the q/k/v projections of
+ * models/backbone/flex_decode.py:204-224 together with mb_kv_append_f32:
+ * y = x w_qkv^T (+ bias) accumulates in fp32 in tensor memory and goes
+ * straight into K2's arithmetic (q/k RMSNorm, RoPE, one rounding to bf16),
+ * q to q_out and k/v to their page slots; the fp32 projection is never
+ * written. Same outputs as the fp32 GEMM followed by mb_kv_append_f32, up to
+ * the GEMM's order of summation.
+ *   x [tokens, hidden] bf16 (row-major, 16-byte aligned; hidden % 8 == 0);
+ *   w_qkv [(q_heads + 2 kv_heads) * head_dim, hidden] bf16 (q | k | v rows),
+ *   a multiple of 128 rows; bias bf16 of that length or NULL;
+ *   rope_table [tokens, head_dim / 2] (cos, sin) float pairs from
+ *   mb_rope_table for the tokens' positions (one table serves every layer);
+ *   q/k norm weights bf16 [head_dim] or NULL; slot [tokens] as for
+ *   mb_kv_append (k_pool, v_pool and slot NULL together: q only).
+ * mb_rope_table writes (cos, sin)(pos[t] * inv_freq[j]) * attention_scaling,
+ * j < head_dim / 2: tokens * head_dim floats, 16-byte aligned.
+ * ------------------------------------------------------------------- */
+int mb_rope_table(const int32_t* pos, int tokens, const float* inv_freq, int head_dim, float attention_scaling,
+                  float* table, mb_stream_t stream);
+int mb_qkv_append(const void* x, int tokens, int hidden, const void* w_qkv, const void* bias, const float* rope_table,
+                  const void* q_norm_w, const void* k_norm_w, float eps, const int32_t* slot, int q_heads,
+                  int kv_heads, int head_dim, int page_size, long long num_pages, void* q_out, void* k_pool,
+                  void* v_pool, mb_stream_t stream);
+
+/* ---------------------------------------------------------------------
  * Page copy (K3): dst_pool[dst_pages[i]] = src_pool[src_pages[i]] for one
  * layer's pool, page_elems = kv_heads * page_size * head_dim elements.
  * Replaces the whole-cache copy of FlexDecodeSession._grow

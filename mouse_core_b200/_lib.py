@@ -32,6 +32,9 @@ PROTOTYPES = {
                               _c_int, _c_int, _c_ll, _vp, _vp, _vp, _vp, _vp, _vp]),
     "mb_kv_append_f32": (_c_int, [_vp, _c_int, _c_int, _vp, _vp, _vp, _vp, _c_float, _vp, _c_float, _c_int,
                                   _c_int, _c_int, _c_int, _c_ll, _vp, _vp, _vp, _vp, _vp, _vp]),
+    "mb_rope_table": (_c_int, [_vp, _c_int, _vp, _c_int, _c_float, _vp, _vp]),
+    "mb_qkv_append": (_c_int, [_vp, _c_int, _c_int, _vp, _vp, _vp, _vp, _vp, _c_float, _vp, _c_int, _c_int, _c_int,
+                               _c_int, _c_ll, _vp, _vp, _vp, _vp]),
     "mb_page_copy": (_c_int, [_vp, _vp, _vp, _vp, _c_int, _c_ll, _vp]),
     "mb_decode_step_meta": (_c_int, [_c_int, _c_int, _c_int, _vp, _vp, _vp, _vp, _vp, _vp]),
     "mb_rmsnorm": (_c_int, [_vp, _vp, _vp, _c_float, _c_int, _c_int, _vp, _vp, _vp]),

@@ -69,6 +69,22 @@ int encode_token_map(CUtensorMap* map, const void* base, int L, int heads, int h
   return MB_OK;
 }
 
+// A row-major bf16 matrix [rows, cols] read in boxes of 64 columns x 128
+// rows with the 128-byte swizzle (the K-major operand layout of tcgen05).
+int encode_matrix_map(CUtensorMap* map, const void* base, long long rows, int cols) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return fail(MB_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)cols * 2};
+  cuuint32_t box[2] = {64, 128};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(MB_ERR_CUDA, "cuTensorMapEncodeTiled failed (" + std::to_string((int)r) + ")");
+  return MB_OK;
+}
+
 int check_decode_shape(int batch, int q_len, int q_heads, int kv_heads, int head_dim, int page_size) {
   if (batch < 0 || q_len < 0 || q_heads <= 0 || kv_heads <= 0)
     return fail(MB_ERR_INVALID_ARG, "batch/q_len must be >= 0 and head counts > 0");
@@ -310,6 +326,64 @@ int mb_kv_append_f32(const float* qkv, int tokens, int qkv_stride, const int32_t
   return kv_append_impl(qkv, true, tokens, qkv_stride, pos, slot, q_norm_w, k_norm_w, eps, inv_freq,
                         attention_scaling, q_heads, kv_heads, head_dim, page_size, num_pages, q_out, k_out, v_out,
                         k_pool, v_pool, stream);
+}
+
+int mb_rope_table(const int32_t* pos, int tokens, const float* inv_freq, int head_dim, float attention_scaling,
+                  float* table, mb_stream_t stream) {
+  if (tokens < 0) return fail(MB_ERR_INVALID_ARG, "tokens must be >= 0");
+  if (head_dim != 64 && head_dim != 128) return fail(MB_ERR_UNSUPPORTED, "head_dim must be 64 or 128");
+  if (tokens == 0) return MB_OK;
+  if (!pos || !inv_freq || !table) return fail(MB_ERR_INVALID_ARG, "a required pointer is NULL");
+  if (!aligned(table, 16)) return fail(MB_ERR_INVALID_ARG, "table must be 16-byte aligned");
+  cudaError_t e = mb::launch_rope_table(pos, tokens, inv_freq, head_dim, attention_scaling, table,
+                                        (cudaStream_t)stream);
+  return e == cudaSuccess ? MB_OK : cuda_fail(e, "rope table launch");
+}
+
+int mb_qkv_append(const void* x, int tokens, int hidden, const void* w_qkv, const void* bias, const float* rope_table,
+                  const void* q_norm_w, const void* k_norm_w, float eps, const int32_t* slot, int q_heads,
+                  int kv_heads, int head_dim, int page_size, long long num_pages, void* q_out, void* k_pool,
+                  void* v_pool, mb_stream_t stream) {
+  if (tokens < 0 || hidden <= 0 || q_heads <= 0 || kv_heads <= 0)
+    return fail(MB_ERR_INVALID_ARG, "tokens >= 0, hidden > 0 and head counts > 0 required");
+  if (q_heads % kv_heads) return fail(MB_ERR_INVALID_ARG, "q_heads must be a multiple of kv_heads");
+  if (head_dim != 64 && head_dim != 128) return fail(MB_ERR_UNSUPPORTED, "head_dim must be 64 or 128");
+  const long long n = (long long)(q_heads + 2 * kv_heads) * head_dim;
+  if (n % 128) return fail(MB_ERR_UNSUPPORTED, "(q_heads + 2 kv_heads) * head_dim must be a multiple of 128");
+  if (hidden % 8) return fail(MB_ERR_UNSUPPORTED, "hidden must be a multiple of 8");
+  if (tokens == 0) return MB_OK;
+  if (!x || !w_qkv || !rope_table || !q_out) return fail(MB_ERR_INVALID_ARG, "a required pointer is NULL");
+  if (!aligned(x, 16) || !aligned(w_qkv, 16) || !aligned(rope_table, 16) || !aligned(q_out, 16))
+    return fail(MB_ERR_INVALID_ARG, "x, w_qkv, rope_table and q_out must be 16-byte aligned");
+  if (k_pool || v_pool) {
+    if (!k_pool || !v_pool || !slot) return fail(MB_ERR_INVALID_ARG, "k_pool, v_pool and slot go together");
+    if (page_size <= 0 || num_pages <= 0) return fail(MB_ERR_INVALID_ARG, "page_size and num_pages must be > 0");
+    if (!aligned(k_pool, 16) || !aligned(v_pool, 16)) return fail(MB_ERR_INVALID_ARG, "pools must be 16-byte aligned");
+  }
+  CUtensorMap xm, wm;
+  int rc;
+  if ((rc = encode_matrix_map(&xm, x, tokens, hidden))) return rc;
+  if ((rc = encode_matrix_map(&wm, w_qkv, n, hidden))) return rc;
+  mb::QkvAppendParams p{};
+  p.T = tokens;
+  p.K = hidden;
+  p.N = (int)n;
+  p.Hq = q_heads;
+  p.Hkv = kv_heads;
+  p.head_dim = head_dim;
+  p.page_size = page_size;
+  p.bias = static_cast<const __nv_bfloat16*>(bias);
+  p.rope = reinterpret_cast<const float2*>(rope_table);
+  p.q_norm_w = static_cast<const __nv_bfloat16*>(q_norm_w);
+  p.k_norm_w = static_cast<const __nv_bfloat16*>(k_norm_w);
+  p.eps = eps;
+  p.slot = k_pool ? slot : nullptr;
+  p.num_slots = k_pool ? num_pages * page_size : 0;
+  p.q_out = static_cast<__nv_bfloat16*>(q_out);
+  p.k_pool = static_cast<__nv_bfloat16*>(k_pool);
+  p.v_pool = static_cast<__nv_bfloat16*>(v_pool);
+  cudaError_t e = mb::launch_qkv_append(xm, wm, p, (cudaStream_t)stream);
+  return e == cudaSuccess ? MB_OK : cuda_fail(e, "qkv append launch");
 }
 
 int mb_page_copy(const void* src_pool, void* dst_pool, const int32_t* src_pages, const int32_t* dst_pages, int n,

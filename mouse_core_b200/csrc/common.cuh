@@ -51,6 +51,11 @@ __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
 
+// Dynamic shared memory is used from its base without padding (the kernels
+// need nearly all 227 KB); the 128-byte-swizzled TMA boxes need the base
+// 1024-byte aligned, which is checked before anything else runs.
+__device__ __forceinline__ bool smem_base_aligned(const void* p) { return (smem_u32(p) & 1023u) == 0; }
+
 // ---------------------------------------------------------------- mbarrier
 __device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
   asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");

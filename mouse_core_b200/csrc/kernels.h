@@ -77,6 +77,27 @@ struct AppendParams {
 };
 cudaError_t launch_append(const AppendParams& p, cudaStream_t stream);
 
+// K13 (qkv_append.cu): the QKV GEMM of the decode layer with K2 as its
+// epilogue. x [T, K] and W [N, K] bf16 come through the tensor maps.
+struct QkvAppendParams {
+  int T, K, N;                    // tokens, hidden size, (Hq + 2 Hkv) * HD (a multiple of 128)
+  int Hq, Hkv, head_dim, page_size;
+  const __nv_bfloat16* bias;      // [N] or null
+  const float2* rope;             // [T, HD/2] (cos, sin) * attention scaling, from launch_rope_table
+  const __nv_bfloat16* q_norm_w;  // [HD] or null
+  const __nv_bfloat16* k_norm_w;  // [HD] or null
+  float eps;
+  const int32_t* slot;            // [T] page * page_size + offset, or -1 (not cached); null: none cached
+  long long num_slots;            // P * page_size (slot bound check), 0 without pools
+  __nv_bfloat16* q_out;           // [T, Hq, HD]
+  __nv_bfloat16* k_pool;          // [P, Hkv, page, HD] or null
+  __nv_bfloat16* v_pool;
+};
+cudaError_t launch_qkv_append(const CUtensorMap& xm, const CUtensorMap& wm, const QkvAppendParams& p,
+                              cudaStream_t stream);
+cudaError_t launch_rope_table(const int32_t* pos, int T, const float* inv_freq, int head_dim, float attn_scaling,
+                              float* table, cudaStream_t stream);
+
 cudaError_t launch_page_copy(const __nv_bfloat16* src_pool, __nv_bfloat16* dst_pool, const int32_t* src_pages,
                              const int32_t* dst_pages, int n, long long page_elems, cudaStream_t stream);
 

@@ -167,11 +167,6 @@ constexpr int kPWarps = 8, kDsWarps = 8;
 // (exp2_fma) instead of the SFU, whose throughput bounds the P phase.
 constexpr int kFmaExp = 4;
 
-// Dynamic shared memory is used from its base without padding (the kernels
-// need nearly all 227 KB); the 128-byte-swizzled TMA boxes need the base
-// 1024-byte aligned, which is checked before anything else runs.
-__device__ __forceinline__ bool smem_base_aligned(const void* p) { return (smem_u32(p) & 1023u) == 0; }
-
 // ---------------------------------------------------------------- dq kernel
 // Persistent: one CTA per SM takes (query tile, q-head) tiles from a global
 // counter, heaviest query tiles first. The producer hands each tile id to

@@ -205,6 +205,12 @@ class PagedDecodeSession:
         # inputs, q/k/v and the pool are bf16); False restores the modules'
         # bf16 rounding at every add.
         self.residual_fp32 = True
+        # Run each layer's QKV projection as K13 (the tcgen05 GEMM with K2 as
+        # its epilogue, no fp32 projection written) instead of cuBLAS
+        # followed by K2. Off by default: at decode sizes (256-1024 tokens,
+        # hidden 1024-2048) cuBLAS + K2 measured 9.6 against 11.3 us per
+        # layer, K13's 64-256 CTAs each streaming its whole K extent.
+        self.fused_qkv = False
         self._step_ids = None
         self._step_out = None
         self._step_launches = 0
@@ -706,6 +712,17 @@ class PagedDecodeSession:
             self._step_graph = None
         return split
 
+    def _fused_qkv(self, lw, tokens: int) -> bool:
+        """Whether this layer's QKV projection runs as K13: asked for
+        (``fused_qkv``), bf16 weights (and norms and bias), heads filling whole
+        128-column tiles, at most FUSED_QKV_MAX_TOKENS tokens."""
+        if not self.fused_qkv:
+            return False
+        n = lw.wqkv.shape[0]
+        if tokens > FUSED_QKV_MAX_TOKENS or n % 128 or lw.wqkv.shape[1] % 8 or lw.wqkv.dtype != torch.bfloat16:
+            return False
+        return all(t is None or t.dtype == torch.bfloat16 for t in (lw.bqkv, lw.q_norm_w, lw.k_norm_w))
+
     def _body_f32(self, x, q_pos, kv_len, slot, S, output_hidden_states):
         """The layer stack with an fp32 residual stream: the embeddings enter
         it exactly, every residual add and every projection output stays
@@ -722,16 +739,25 @@ class PagedDecodeSession:
         q_pos_flat = q_pos.reshape(-1)
         resid, delta = None, None
         hiddens = []
+        rope = None
         for li, lw in enumerate(self._layers):
             lw.refresh()
             if resid is None:
                 resid, hn = K.rmsnorm_f32(x, lw.in_w, lw.in_eps)
             else:
                 resid, hn = K.rmsnorm_f32(resid, lw.in_w, lw.in_eps, delta=delta, sum_out=resid)
-            qkv = _mm_f32(hn, lw.wqkv, lw.bqkv)
-            q = K.kv_append(qkv, q_pos_flat, Hq, Hkv, hd, self.inv_freq, self.attention_scaling,
-                            lw.q_norm_w, lw.k_norm_w, lw.qk_eps, slot=slot,
-                            k_pool=self.k_pool[li], v_pool=self.v_pool[li])
+            if self._fused_qkv(lw, B * S):
+                # K13: the QKV GEMM with K2 as its epilogue; one RoPE table
+                # for the step's tokens serves every layer.
+                if rope is None:
+                    rope = K.rope_table(q_pos_flat, self.inv_freq, hd, self.attention_scaling)
+                q = K.qkv_append(hn, lw.wqkv, lw.bqkv, rope, Hq, Hkv, hd, lw.q_norm_w, lw.k_norm_w, lw.qk_eps,
+                                 slot=slot, k_pool=self.k_pool[li], v_pool=self.v_pool[li])
+            else:
+                qkv = _mm_f32(hn, lw.wqkv, lw.bqkv)
+                q = K.kv_append(qkv, q_pos_flat, Hq, Hkv, hd, self.inv_freq, self.attention_scaling,
+                                lw.q_norm_w, lw.k_norm_w, lw.qk_eps, slot=slot,
+                                k_pool=self.k_pool[li], v_pool=self.v_pool[li])
             o = self._attend(q.view(B, S, Hq, hd), li, lw.scale, q_pos, kv_len, split)
             a = _mm_f32(o.view(B * S, Hq * hd), lw.o_proj.weight, lw.o_proj.bias)
             resid, hn2 = K.rmsnorm_f32(resid, lw.post_w, lw.post_eps, delta=a, sum_out=resid)
@@ -742,6 +768,12 @@ class PagedDecodeSession:
         if output_hidden_states:
             return h, hiddens
         return h
+
+
+# Largest token count of one forward whose QKV projection runs as K13 (the
+# GEMM with K2 as its epilogue) when the session asks for it: every decode
+# step and short chunk; longer prefill chunks keep cuBLAS followed by K2.
+FUSED_QKV_MAX_TOKENS = 8192
 
 
 def _mm_f32(x: torch.Tensor, w: torch.Tensor, b: torch.Tensor | None = None) -> torch.Tensor:

@@ -149,6 +149,55 @@ def kv_append(qkv: torch.Tensor, pos: torch.Tensor, q_heads: int, kv_heads: int,
     return q_out
 
 
+def rope_table(pos: torch.Tensor, inv_freq: torch.Tensor, head_dim: int, attention_scaling: float = 1.0,
+               out: torch.Tensor | None = None) -> torch.Tensor:
+    """``[T, head_dim / 2, 2]`` f32: (cos, sin)(pos[t] * inv_freq[j]) *
+    attention_scaling, the rotation factors of K2, for ``qkv_append``."""
+    _need(pos, "pos", torch.int32)
+    _need(inv_freq, "inv_freq", torch.float32)
+    T = pos.numel()
+    if out is None:
+        out = torch.empty(T, head_dim // 2, 2, dtype=torch.float32, device=pos.device)
+    _lib.call("mb_rope_table", _p(pos), T, _p(inv_freq), head_dim, float(attention_scaling), _p(out), _stream(pos))
+    _count()
+    return out
+
+
+def qkv_append(x: torch.Tensor, w_qkv: torch.Tensor, bias: torch.Tensor | None, rope: torch.Tensor, q_heads: int,
+               kv_heads: int, head_dim: int, q_norm_w: torch.Tensor | None = None,
+               k_norm_w: torch.Tensor | None = None, eps: float = 1e-6, slot: torch.Tensor | None = None,
+               k_pool: torch.Tensor | None = None, v_pool: torch.Tensor | None = None) -> torch.Tensor:
+    """K13: ``x [T, hidden] @ w_qkv.T (+ bias)`` on tcgen05 with K2 as the
+    epilogue (q/k RMSNorm, RoPE from ``rope``, bf16 q returned, k/v stored at
+    ``slot`` in the pools); the same outputs as the fp32 GEMM followed by
+    ``kv_append`` up to the GEMM's order of summation."""
+    _need(x, "x", BF16)
+    _need(w_qkv, "w_qkv", BF16)
+    _need(rope, "rope", torch.float32)
+    T, hidden = x.shape
+    if w_qkv.shape != ((q_heads + 2 * kv_heads) * head_dim, hidden):
+        raise ValueError("w_qkv must be [(q_heads + 2 kv_heads) * head_dim, hidden]")
+    if rope.numel() != T * head_dim:
+        raise ValueError("rope must hold head_dim / 2 (cos, sin) pairs per token")
+    if bias is not None:
+        _need(bias, "bias", BF16)
+    for name, t in (("q_norm_w", q_norm_w), ("k_norm_w", k_norm_w)):
+        if t is not None:
+            _need(t, name, BF16)
+    page_size, num_pages = 0, 0
+    if k_pool is not None:
+        _need(k_pool, "k_pool", BF16)
+        _need(v_pool, "v_pool", BF16)
+        _need(slot, "slot", torch.int32)
+        num_pages, _, page_size, _ = k_pool.shape
+    q_out = torch.empty(T, q_heads, head_dim, dtype=BF16, device=x.device)
+    _lib.call("mb_qkv_append", _p(x), T, hidden, _p(w_qkv), _p(bias), _p(rope), _p(q_norm_w), _p(k_norm_w),
+              float(eps), _p(slot), q_heads, kv_heads, head_dim, page_size, num_pages, _p(q_out), _p(k_pool),
+              _p(v_pool), _stream(x))
+    _count()
+    return q_out
+
+
 def page_copy(src_pool: torch.Tensor, dst_pool: torch.Tensor, src_pages: torch.Tensor,
               dst_pages: torch.Tensor) -> None:
     """``dst_pool[dst_pages[i]] = src_pool[src_pages[i]]`` (K3), one layer."""

@@ -246,9 +246,10 @@ def test_session_matches_reference_golden(arch):
     assert sess.pages.num_pages >= 3, "the pool should have grown"
 
 
-def test_session_random_schedule_fuzz():
+@pytest.mark.parametrize("fused_qkv", [False, True])  # cuBLAS QKV + K2, or K13 (the GEMM with K2 as epilogue)
+def test_session_random_schedule_fuzz(fused_qkv):
     """Randomised ragged schedules on a Qwen3-shaped model (hd 128, GQA 2):
-    every real step equals the oracle session."""
+    every real step equals the oracle session, with either QKV projection."""
     dev = _dev()
     from mouse_core_b200.backbone import Qwen3Backbone
 
@@ -269,6 +270,7 @@ def test_session_random_schedule_fuzz():
     rng = np.random.default_rng(3)
     B = 5
     sess = bb.decode_session(batch_size=B, capacity=16)
+    sess.fused_qkv = fused_qkv
     osess = odec.DecodeSessionOracle(dec, B)
     for call in range(6):
         lens = rng.integers(0, 9, size=B)

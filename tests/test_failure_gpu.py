@@ -132,3 +132,27 @@ def test_packed_attention_wait_timeout_is_reported_and_recovers(stored):
     for name, g, r in zip(("dq", "dk", "dv"), grads, ref_g):
         bound = ATOL * max(1.0, float(np.abs(r).max()))
         assert np.abs(g.float().cpu().numpy() - r).max() <= bound, name
+
+
+def test_qkv_projection_wait_timeout_is_reported_and_recovers():
+    """K13 (the QKV GEMM with the K2 epilogue) with a wait limit of 0: each
+    launch finishes and reports a timeout; with the default limit back the
+    same call gives the GEMM-then-K2 outputs on the same context."""
+    dev = _dev()
+    from mouse_core_b200 import _lib
+    from mouse_core_b200 import kernels as K
+
+    T, hidden, Hq, Hkv, hd = 200, 1024, 16, 8, 128
+    g = torch.Generator(device=dev).manual_seed(5)
+    x = torch.randn(T, hidden, generator=g, device=dev).bfloat16()
+    w = (torch.randn((Hq + 2 * Hkv) * hd, hidden, generator=g, device=dev) * hidden ** -0.5).bfloat16()
+    pos = torch.arange(T, dtype=torch.int32, device=dev) * 7
+    inv_freq = (1e6 ** (-torch.arange(0, hd, 2, device=dev, dtype=torch.float32) / hd)).contiguous()
+    rope = K.rope_table(pos, inv_freq, hd)
+    _timed_out_launches(lambda: K.qkv_append(x, w, None, rope, Hq, Hkv, hd))
+    q = K.qkv_append(x, w, None, rope, Hq, Hkv, hd)
+    q_ref = K.kv_append(torch.mm(x, w.t(), out_dtype=torch.float32), pos, Hq, Hkv, hd, inv_freq)
+    torch.cuda.synchronize()
+    assert _lib.device_status() == 0
+    diff = (q.float() - q_ref.float()).abs()
+    assert bool((diff <= 2 ** -7 * torch.maximum(q.float().abs(), q_ref.float().abs()) + 1e-6).all())
