@@ -140,3 +140,28 @@ def test_add_rmsnorm_argument_rules(lib):
     assert lib.mb_add_rmsnorm_fwd(None, None, None, 1e-6, 0, 1024, None, None, None, None) == 0
     assert lib.mb_rmsnorm_bwd_add(p, p, p, p, None, 4, 1024, p, p, p, 1 << 20, None) == 1
     assert b"dsum" in lib.mb_last_error()
+
+
+def test_qkv_append_argument_rules(lib):
+    """K13 and its RoPE table reject bad shapes and pointers before any CUDA
+    call; zero tokens is a no-op that needs no pointers."""
+    p = ctypes.c_void_p(4096)  # aligned, never dereferenced
+    odd = ctypes.c_void_p(4098)
+
+    def qa(tokens=8, hidden=1024, hq=16, hkv=8, hd=128, x=p, w=p, rope=p, q=p, kp=None, vp=None, slot=None,
+           page=0, pages=0):
+        return lib.mb_qkv_append(x, tokens, hidden, w, None, rope, None, None, 1e-6, slot, hq, hkv, hd, page,
+                                 pages, q, kp, vp, None)
+
+    assert qa(tokens=0, x=None, w=None, rope=None, q=None) == 0
+    assert qa(hd=96) == 2 and b"head_dim" in lib.mb_last_error()
+    assert qa(hq=1, hkv=1, hd=64) == 2 and b"multiple of 128" in lib.mb_last_error()  # 3 heads of 64
+    assert qa(hidden=1020) == 2 and b"hidden" in lib.mb_last_error()
+    assert qa(hq=3, hkv=2) == 1 and b"multiple of kv_heads" in lib.mb_last_error()
+    assert qa(rope=None) == 1 and b"NULL" in lib.mb_last_error()
+    assert qa(x=odd) == 1 and b"aligned" in lib.mb_last_error()
+    assert qa(kp=p, vp=p) == 1 and b"go together" in lib.mb_last_error()  # pools without slots
+    assert qa(kp=p, vp=p, slot=p) == 1 and b"page_size" in lib.mb_last_error()
+    assert lib.mb_rope_table(p, 4, p, 96, 1.0, p, None) == 2
+    assert lib.mb_rope_table(p, 4, p, 128, 1.0, odd, None) == 1
+    assert lib.mb_rope_table(None, 0, None, 128, 1.0, None, None) == 0
