@@ -47,6 +47,15 @@ __device__ long long g_wait_limit = kWaitCycles;
 // those copies always complete, so this never depends on g_wait_limit.
 constexpr long long kDrainCycles = kWaitCycles;
 
+// Host side: launch set-up (a kernel's shared-memory attribute, an
+// occupancy figure) is per device, so one-time caches of it are indexed by
+// the current device's ordinal; -1 (no caching) outside [0, kMaxDevices).
+constexpr int kMaxDevices = 64;
+inline int device_slot() {
+  int d = -1;
+  return (cudaGetDevice(&d) == cudaSuccess && d >= 0 && d < kMaxDevices) ? d : -1;
+}
+
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }

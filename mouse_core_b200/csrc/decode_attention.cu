@@ -879,10 +879,9 @@ size_t decode_workspace_layout(int B, int Hkv, int R, int head_dim, int max_kv_l
 // SM count of the current device, cached per device ordinal (several host
 // threads may launch at once: the cache entries are atomics).
 static int num_sms() {
-  constexpr int kMaxDevices = 64;
   static std::atomic<int> cache[kMaxDevices];
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return 148;
+  const int dev = device_slot();
+  if (dev < 0) return 148;
   int n = cache[dev].load(std::memory_order_relaxed);
   if (n <= 0) {
     if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;

@@ -227,11 +227,12 @@ template <int HD>
 static cudaError_t launch_qkv_append_hd(const CUtensorMap& xm, const CUtensorMap& wm, const QkvAppendParams& p,
                                         cudaStream_t stream) {
   constexpr int smem = 2 * kQaStages * kQaBox + (int)sizeof(QaBars);
-  static std::atomic<int> ready{0};
-  if (!ready.load(std::memory_order_acquire)) {
+  static std::atomic<int> ready[kMaxDevices];  // the attribute is set once per device
+  const int dev = device_slot();
+  if (dev < 0 || !ready[dev].load(std::memory_order_acquire)) {
     cudaError_t e = cudaFuncSetAttribute(qkv_append_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
-    ready.store(1, std::memory_order_release);
+    if (dev >= 0) ready[dev].store(1, std::memory_order_release);
   }
   const dim3 grid((unsigned)((p.T + 127) / 128), (unsigned)(p.N / 128));
   qkv_append_kernel<HD><<<grid, kQaThreads, smem, stream>>>(xm, wm, p);

@@ -222,11 +222,14 @@ static void launch_colsum(const float* partial, int P, int D, int split, float* 
 static int norm_blocks(int rows) { return std::max(1, std::min((rows + 7) / 8, 148 * 4)); }
 
 // One full wave of the backward kernel for dim D (its shared memory holds
-// the per-warp weight-gradient rows and the weight).
+// the per-warp weight-gradient rows and the weight), cached per device.
 static int norm_bwd_blocks(int rows, int D) {
-  static int cap[9] = {0};
+  static std::atomic<int> cache[kMaxDevices][9];
   const int nch = D / 256;
   if (nch < 1 || nch > 8) return 1;
+  const int dev = device_slot();
+  int cap[9] = {0};
+  if (dev >= 0) cap[nch] = cache[dev][nch].load(std::memory_order_relaxed);
   if (!cap[nch]) {
     const int smem = (kNormBwdWarps + 1) * D * (int)sizeof(float);
     switch (nch) {
@@ -238,6 +241,7 @@ static int norm_bwd_blocks(int rows, int D) {
       MB_CAP(1) MB_CAP(2) MB_CAP(3) MB_CAP(4) MB_CAP(5) MB_CAP(6) MB_CAP(7) MB_CAP(8)
 #undef MB_CAP
     }
+    if (dev >= 0) cache[dev][nch].store(cap[nch], std::memory_order_relaxed);
   }
   return std::max(1, std::min((rows + kNormBwdWarps - 1) / kNormBwdWarps, cap[nch]));
 }

@@ -598,20 +598,21 @@ __global__ void __launch_bounds__(fwd_threads<PAGED>(), 1) varlen_fwd_kernel(con
   }
 }
 
-// Prepare one instantiation for launch: its dynamic shared memory, and for
-// the paged prefill a check that the kernel is launched with the registers
-// the setmaxnreg split draws on (an increase beyond the launch allocation
-// would never complete).
+// Prepare one instantiation for launch on the current device (once per
+// device): its dynamic shared memory, and for the paged prefill a check that
+// the kernel is launched with the registers the setmaxnreg split draws on
+// (an increase beyond the launch allocation would never complete).
 template <int HD, bool PAGED>
 cudaError_t fwd_prepare(int smem) {
-  static std::atomic<int> ready{0};
-  if (ready.load(std::memory_order_acquire)) return cudaSuccess;
+  static std::atomic<int> ready[kMaxDevices];
+  const int dev = device_slot();
+  if (dev >= 0 && ready[dev].load(std::memory_order_acquire)) return cudaSuccess;
   cudaFuncAttributes a{};
   cudaError_t e = cudaFuncGetAttributes(&a, varlen_fwd_kernel<HD, PAGED>);
   if (e != cudaSuccess) return e;
   if (PAGED && a.numRegs < kFwdLaunchRegs) return cudaErrorInvalidConfiguration;
   e = cudaFuncSetAttribute(varlen_fwd_kernel<HD, PAGED>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-  if (e == cudaSuccess) ready.store(1, std::memory_order_release);
+  if (e == cudaSuccess && dev >= 0) ready[dev].store(1, std::memory_order_release);
   return e;
 }
 
